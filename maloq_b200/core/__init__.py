@@ -1,0 +1,1 @@
+"""maloq_b200 subpackage."""

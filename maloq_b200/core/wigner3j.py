@@ -1,0 +1,127 @@
+"""Real-basis Wigner 3j tensors and the coupled <-> uncoupled basis transform.
+
+``wigner_3j(l1, l2, l3)`` is the unit-Frobenius-norm tensor ``C[i, j, k]`` that is invariant
+under simultaneous rotation, ``C = (D1 (x) D2 (x) D3) C`` for every rotation, with the D
+matrices of :mod:`maloq_b200.core.sph`.  Because ``l3`` appears at most once in
+``l1 (x) l2``, the invariant subspace is one-dimensional; for the sorted triple it is computed as the null space
+of ``sum_R (D1(R) (x) D2(R) (x) D3(R) - I)`` over two generic rotations, in float64.  The
+overall sign of the sorted triple is fixed by making its first non-zero entry (C order)
+positive; other orders follow from the permutation symmetry of 3j symbols.
+
+The coupled<->uncoupled transform follows the reference's ``e3TensorDecomp``
+(``fock_utils/utils_tensor_decomp.py:51-169``): an orbital block ``H[l1, l2]`` of shape
+``(2l1+1) x (2l2+1)`` maps to coefficients ``c_l3 = (2 l3 + 1) sum_ij C(l3, l1, l2)_{k,i,j} H_ij``
+(``get_net_out``) and back by ``H_ij = sum_k C(l1, l2, l3)_{i,j,k} c_k`` (``get_H``).
+"""
+
+from __future__ import annotations
+
+from functools import lru_cache
+
+import numpy as np
+import torch
+
+from . import sph
+
+
+@lru_cache(maxsize=None)
+def _wigner_3j_np(l1: int, l2: int, l3: int) -> np.ndarray:
+    """Tensor for any order of (l1, l2, l3), derived from the sorted triple so that the
+    permutation symmetry of 3j symbols holds: cyclic permutations leave it unchanged, odd
+    permutations multiply it by (-1)^(l1+l2+l3)."""
+    ls = (l1, l2, l3)
+    order = sorted(range(3), key=lambda i: (ls[i], i))
+    base = _wigner_3j_sorted(*(ls[i] for i in order))
+    # base axes correspond to ls[order[0]], ls[order[1]], ls[order[2]]; move them back
+    inv = [order.index(i) for i in range(3)]
+    out = np.transpose(base, inv)
+    odd = sum(1 for a in range(3) for b in range(a + 1, 3) if order[a] > order[b]) % 2
+    if odd and (l1 + l2 + l3) % 2:
+        out = -out
+    return np.ascontiguousarray(out)
+
+
+@lru_cache(maxsize=None)
+def _wigner_3j_sorted(l1: int, l2: int, l3: int) -> np.ndarray:
+    if not (abs(l1 - l2) <= l3 <= l1 + l2):
+        raise ValueError(f"l3={l3} not in |l1-l2|..l1+l2 for l1={l1}, l2={l2}")
+    d1, d2, d3 = 2 * l1 + 1, 2 * l2 + 1, 2 * l3 + 1
+    rots = [sph.euler_matrix(0.7, 1.3, -0.4), sph.euler_matrix(-1.9, 0.5, 2.2)]
+    A = []
+    for R in rots:
+        D = np.kron(np.kron(sph.wigner_D_from_matrix(l1, R), sph.wigner_D_from_matrix(l2, R)),
+                    sph.wigner_D_from_matrix(l3, R))
+        A.append(D - np.eye(d1 * d2 * d3))
+    A = np.concatenate(A, axis=0)
+    _, s, vt = np.linalg.svd(A)
+    v = vt[-1]
+    assert s[-1] < 1e-8 and (len(s) < 2 or s[-2] > 1e-4), "invariant subspace must be 1-D"
+    v = v / np.linalg.norm(v)
+    v[np.abs(v) < 1e-13] = 0.0
+    nz = np.flatnonzero(np.abs(v) > 1e-10)
+    if v[nz[0]] < 0:
+        v = -v
+    return v.reshape(d1, d2, d3)
+
+
+def wigner_3j(l1: int, l2: int, l3: int, dtype=torch.float32, device=None) -> torch.Tensor:
+    return torch.tensor(_wigner_3j_np(l1, l2, l3), dtype=dtype, device=device)
+
+
+def l1l2_to_l3s(l1: int, l2: int) -> list[int]:
+    """Coupled degrees for an l1 x l2 orbital block (diffuse shells are tagged l + 10)."""
+    l1, l2 = l1 % 10, l2 % 10
+    return list(range(abs(l1 - l2), l1 + l2 + 1))
+
+
+class BasisTransform:
+    """Dense block-diagonal coupled<->uncoupled transform for a list of (l1, l2) blocks.
+
+    ``W`` [D, D]: coupled label row -> uncoupled block row (``get_H``);
+    ``W_inv`` [D, D]: the inverse (``get_net_out``).  ``blocks`` lists, per orbital block,
+    ``(l1, l2, coupled_start, uncoupled_start)`` for kernels that exploit the block
+    structure instead of the dense matrix.
+    Reference: ``fock_utils/utils_tensor_decomp.py:51-169``.
+    """
+
+    def __init__(self, out_js_list, dtype=torch.float32, device="cpu"):
+        self.out_js_list = [(int(a), int(b)) for a, b in out_js_list]
+        in_slices, h_slices = [0], [0]
+        blocks = []
+        wms, wms_H = [], []
+        for l1, l2 in self.out_js_list:
+            a, b = l1 % 10, l2 % 10
+            l3s = l1l2_to_l3s(a, b)
+            wm = np.concatenate([_wigner_3j_np(a, b, l3) for l3 in l3s], axis=-1)  # [d1, d2, sum d3]
+            wmH = np.concatenate([_wigner_3j_np(l3, a, b) * (2 * l3 + 1) for l3 in l3s], axis=0)  # [sum d3, d1, d2]
+            blocks.append((a, b, in_slices[-1], h_slices[-1]))
+            in_slices.append(in_slices[-1] + sum(2 * l + 1 for l in l3s))
+            h_slices.append(h_slices[-1] + (2 * a + 1) * (2 * b + 1))
+            wms.append(wm)
+            wms_H.append(wmH)
+        self.in_slices, self.H_slices, self.blocks = in_slices, h_slices, blocks
+        D_in, D_h = in_slices[-1], h_slices[-1]
+        W = np.zeros((D_in, D_h))
+        W_inv = np.zeros((D_h, D_in))
+        for i in range(len(self.out_js_list)):
+            i0, i1, h0, h1 = in_slices[i], in_slices[i + 1], h_slices[i], h_slices[i + 1]
+            W[i0:i1, h0:h1] = wms[i].reshape(h1 - h0, i1 - i0).T
+            W_inv[h0:h1, i0:i1] = wms_H[i].reshape(i1 - i0, h1 - h0).T
+        self.W_global = torch.tensor(W, dtype=dtype, device=device)
+        self.W_global_inv = torch.tensor(W_inv, dtype=dtype, device=device)
+        self.dim = D_in
+
+    def to(self, device=None, dtype=None):
+        self.W_global = self.W_global.to(device=device, dtype=dtype)
+        self.W_global_inv = self.W_global_inv.to(device=device, dtype=dtype)
+        return self
+
+    def get_H(self, net_out: torch.Tensor) -> torch.Tensor:
+        from ..ops import basis_transform as bt
+
+        return bt.apply_transform(net_out, self.W_global.to(net_out.device, net_out.dtype))
+
+    def get_net_out(self, H: torch.Tensor) -> torch.Tensor:
+        from ..ops import basis_transform as bt
+
+        return bt.apply_transform(H, self.W_global_inv.to(H.device, H.dtype))

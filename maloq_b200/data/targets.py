@@ -1,0 +1,177 @@
+"""Fock targets: Hamiltonian blocks -> coupled-basis labels per node and edge.
+
+Mirrors the reference's ``Fock_Targets`` pipeline (``fock_utils/fock_targets_batched.py``):
+matrix -> label rows (``matrix2label``) -> coupled basis (``get_net_out``) -> optional
+per-element l=0 shift.  Synthetic Hamiltonians come from a frozen random-init teacher
+model (:class:`Teacher`): its coupled outputs are mapped to blocks (``get_H`` +
+``label2matrix``), symmetrised (H_ij <- (H_ij + H_ji^T) / 2), and then sent through the
+forward pipeline, so targets are exactly equivariant and learnable.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from ..core.irreps import make_label_layout
+from ..core.wigner3j import BasisTransform
+from .batch import GraphSample, collate
+from .labels import BlockSparseMatrix, PairTable, block_pointers, labels_to_matrix, matrix_to_labels, orbital_offsets
+
+
+class FockLabeler:
+    def __init__(self, orbital_basis, device="cpu", dtype=torch.float32):
+        self.orbital_basis = {int(k): list(v) for k, v in orbital_basis.items()}
+        self.layout = make_label_layout(self.orbital_basis)
+        self.table = PairTable(self.layout)
+        self.transform = BasisTransform(self.layout.out_js_list, dtype=dtype, device=device)
+        self.device, self.dtype = torch.device(device), dtype
+        self.pos_t, self.mask_t = self.table.torch_tables(self.device)
+
+    @property
+    def irreps(self):
+        return self.layout.irreps_out
+
+    @property
+    def target_len(self):
+        return self.layout.target_len
+
+    def pairs(self, s: GraphSample):
+        n = s.num_nodes
+        rows = np.concatenate([s.src, np.arange(n)])
+        cols = np.concatenate([s.dst, np.arange(n)])
+        return rows, cols
+
+    def _pt(self, s, rows, cols):
+        return torch.as_tensor(self.table.pair_type(s.z[rows], s.z[cols]), device=self.device)
+
+    def labels_from_blocks(self, s: GraphSample, bsm: BlockSparseMatrix):
+        """Coupled labels (node_y [N, D], y [E, D]) of a block-sparse Hamiltonian whose
+        blocks are ordered as ``pairs(s)``."""
+        rows, cols = self.pairs(s)
+        data = torch.as_tensor(bsm.data, device=self.device, dtype=self.dtype)
+        ptr = torch.as_tensor(bsm.block_ptr, device=self.device)
+        lab = matrix_to_labels(data, ptr, self._pt(s, rows, cols), self.pos_t)
+        coupled = self.transform.get_net_out(lab)
+        E = s.num_edges
+        return coupled[E:], coupled[:E]
+
+    def blocks_from_labels(self, s: GraphSample, node_lab, edge_lab) -> BlockSparseMatrix:
+        rows, cols = self.pairs(s)
+        coupled = torch.cat([edge_lab, node_lab], 0).to(self.device, self.dtype)
+        unc = self.transform.get_H(coupled)
+        ptr_np = block_pointers(s.z, rows, cols, self.table)
+        ptr = torch.as_tensor(ptr_np, device=self.device)
+        data = labels_to_matrix(unc, ptr, self._pt(s, rows, cols), self.pos_t, int(ptr_np[-1]))
+        return BlockSparseMatrix(rows, cols, ptr_np, data.cpu().numpy(), orbital_offsets(s.z, self.table))
+
+    def symmetrize(self, s: GraphSample, bsm: BlockSparseMatrix) -> BlockSparseMatrix:
+        """H_ij <- (H_ij + H_ji^T)/2 for every stored pair (the reverse pair must be stored)."""
+        rows, cols = bsm.rows, bsm.cols
+        n = s.num_nodes
+        key = rows * n + cols
+        rkey = cols * n + rows
+        order = np.argsort(key)
+        rev = order[np.searchsorted(key[order], rkey)]
+        nz = self.table.norb[self.table.z_to_type[s.z]]
+        out = bsm.data.copy()
+        for b in range(len(rows)):
+            a = bsm.data[bsm.block_ptr[b]:bsm.block_ptr[b + 1]].reshape(nz[rows[b]], nz[cols[b]])
+            rb = rev[b]
+            t = bsm.data[bsm.block_ptr[rb]:bsm.block_ptr[rb + 1]].reshape(nz[rows[rb]], nz[cols[rb]]).T
+            out[bsm.block_ptr[b]:bsm.block_ptr[b + 1]] = (0.5 * (a + t)).ravel()
+        return BlockSparseMatrix(rows, cols, bsm.block_ptr, out, bsm.orb_ptr)
+
+
+class Teacher:
+    """Frozen random-init backbone + Fock head producing coupled labels."""
+
+    def __init__(self, model_kwargs, labeler: FockLabeler, seed=1234, device="cpu"):
+        from ..models.backbone import eSEN_Backbone
+        from ..models.heads import Fock_Irreps_Head
+
+        g = torch.random.get_rng_state()
+        torch.manual_seed(seed)
+        kw = dict(model_kwargs)
+        self.backbone = eSEN_Backbone(labeler.irreps, include_edges=True, **kw).to(device).eval()
+        self.head = Fock_Irreps_Head(None, labeler.irreps, lmax=kw["lmax"], sphere_channels=kw["sphere_channels"],
+                                     ls_list=labeler.layout.ls_list, reduce_node=False).to(device).eval()
+        torch.random.set_rng_state(g)
+        for p in list(self.backbone.parameters()) + list(self.head.parameters()):
+            p.requires_grad_(False)
+        self.labeler, self.device = labeler, torch.device(device)
+
+    @torch.no_grad()
+    def hamiltonians(self, samples, chunk=16):
+        """Symmetrised block-sparse Hamiltonians for ``samples``."""
+        out = []
+        for i in range(0, len(samples), chunk):
+            part = samples[i:i + chunk]
+            b = collate(part, self.labeler.table).to(self.device)
+            emb = self.backbone(b)
+            n_out, e_out = self.head(emb, b)
+            n_out, e_out = n_out[0], e_out[0]
+            no, eo = 0, 0
+            for s in part:
+                nl = n_out[no:no + s.num_nodes]
+                el = e_out[eo:eo + s.num_edges]
+                no += s.num_nodes
+                eo += s.num_edges
+                bsm = self.labeler.blocks_from_labels(s, nl, el)
+                out.append(self.labeler.symmetrize(s, bsm))
+        return out
+
+
+def attach_targets(samples, hamiltonians, labeler: FockLabeler, scale_shift=None):
+    """Fill ``node_y``/``y`` ([1, rows, D] float32, CPU) of every sample."""
+    for s, h in zip(samples, hamiltonians):
+        ny, y = labeler.labels_from_blocks(s, h)
+        if scale_shift is not None:
+            ny = scale_shift.shift(ny, s.z)
+        s.node_y = ny.unsqueeze(0).cpu()
+        s.y = y.unsqueeze(0).cpu()
+    return samples
+
+
+class ScaleShift:
+    """Per-element mean of the l=0 node label entries, subtracted from targets (shift only,
+    as the reference applies it: ``fock_targets_batched.py:1093-1194``)."""
+
+    def __init__(self, labeler: FockLabeler, samples=None, means=None):
+        irr = labeler.irreps
+        idx, s = [], 0
+        for it in irr:
+            if it.l == 0:
+                idx.append(s)
+            s += it.dim
+        self.scalar_idx = torch.tensor(idx, dtype=torch.long)
+        self.means = means if means is not None else {}
+        if samples is not None and means is None:
+            acc, cnt = {}, {}
+            for smp in samples:
+                for z, row in zip(smp.z, smp.node_y[0]):
+                    acc.setdefault(int(z), torch.zeros(len(idx)))
+                    acc[int(z)] += row[self.scalar_idx].float()
+                    cnt[int(z)] = cnt.get(int(z), 0) + 1
+            self.means = {z: (acc[z] / cnt[z]) for z in acc}
+
+    def _table(self, device, dtype):
+        zmax = max(self.means) if self.means else 0
+        t = torch.zeros(zmax + 1, len(self.scalar_idx), device=device, dtype=dtype)
+        for z, v in self.means.items():
+            t[z] = v.to(device, dtype)
+        return t
+
+    def shift(self, node_y, z):
+        t = self._table(node_y.device, node_y.dtype)
+        zt = torch.as_tensor(np.asarray(z), device=node_y.device)
+        out = node_y.clone()
+        out[:, self.scalar_idx.to(node_y.device)] -= t[zt]
+        return out
+
+    def unshift(self, node_y, z):
+        t = self._table(node_y.device, node_y.dtype)
+        zt = torch.as_tensor(np.asarray(z), device=node_y.device)
+        out = node_y.clone()
+        out[:, self.scalar_idx.to(node_y.device)] += t[zt]
+        return out

@@ -1,0 +1,249 @@
+"""SO(2)-equivariant eSEN backbone (HELM) with m-truncated edge-frame rotations.
+
+Reference: ``helm/esen_osh.py:57-517`` (backbone), ``helm/esen_block.py`` (blocks),
+``helm/nn/embedding.py`` (edge-degree embedding).  Differences by design:
+
+* the per-edge rotation is built once per forward as a compact m-truncated
+  matrix ``rot`` [E, R, (L+1)^2] (R = m-major rows with |m| <= mmax), which also performs
+  the l->m reordering; the reverse rotation is its transpose.  This makes ``mmax < lmax``
+  work (the reference needs ``mmax == lmax``);
+* the roll angle gamma is 0 instead of random: the SO(2) layers commute with rolls about
+  the edge axis, so the output does not depend on it;
+* in graph-partitioned mode the source-node features of an edge may live on another
+  GPU; the edge kernels read them through a :class:`maloq_b200.parallel.halo.HaloPlan`.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from ..core import sph
+from .layers import (
+    EnvelopedBesselBasis,
+    GateActivation,
+    GaussianSmearing,
+    RadialMLP,
+    SO2_Convolution,
+    SO3_Linear,
+    get_normalization_layer,
+)
+from .so3 import CoefficientMapping
+
+
+class Edgewise(nn.Module):
+    """Message passing: gather, rotate into the edge frame, SO(2) conv, gate, SO(2) conv,
+    rotate back, then sum over incoming edges (node path) or keep per edge (edge path).
+
+    Reference ``helm/esen_block.py:34-258``.
+    """
+
+    def __init__(self, sphere_channels, hidden_channels, lmax, mmax, edge_channels_list, mapping,
+                 message_type="source-target"):
+        super().__init__()
+        self.sphere_channels, self.hidden_channels = sphere_channels, hidden_channels
+        self.lmax, self.mmax = lmax, mmax
+        self.mapping = mapping
+        self.act = GateActivation(lmax, mmax, hidden_channels, outer_dim="m", mapping=mapping)
+        if message_type == "source-target-message":
+            self.concat_size = 3
+        elif message_type == "source-target":
+            self.concat_size = 2
+        else:
+            raise ValueError(f"unknown message_type {message_type!r}")
+        self.so2_conv_1 = SO2_Convolution(self.concat_size * sphere_channels, hidden_channels, lmax, mmax, mapping,
+                                          internal_weights=False, edge_channels_list=edge_channels_list,
+                                          extra_m0_output_channels=lmax * hidden_channels)
+        self.so2_conv_2 = SO2_Convolution(hidden_channels, sphere_channels, lmax, mmax, mapping,
+                                          internal_weights=True)
+
+    def forward(self, x_node, x_message_edge, x_edge, graph, node_or_edge):
+        return ops.edgewise(self, x_node, x_message_edge if self.concat_size == 3 else None, x_edge, graph,
+                            node_or_edge)
+
+
+class SpectralAtomwise(nn.Module):
+    """Gate scalars from l=0, SO3_Linear, gate, SO3_Linear (``esen_block.py:261-298``)."""
+
+    def __init__(self, sphere_channels, hidden_channels, lmax, mmax):
+        super().__init__()
+        self.lmax = lmax
+        self.hidden_channels = hidden_channels
+        self.scalar_mlp = nn.Sequential(nn.Linear(sphere_channels, lmax * hidden_channels, bias=True), nn.SiLU())
+        self.so3_linear_1 = SO3_Linear(sphere_channels, hidden_channels, lmax)
+        self.act = GateActivation(lmax, lmax, hidden_channels, outer_dim="l")
+        self.so3_linear_2 = SO3_Linear(hidden_channels, sphere_channels, lmax)
+
+    def forward(self, x):
+        lin = self.scalar_mlp[0]
+        g = ops.linear(x[:, 0], lin.weight, lin.bias, act="silu")
+        h = self.so3_linear_1(x)
+        h = self.act(g, h)
+        return self.so3_linear_2(h)
+
+
+class eSEN_Block(nn.Module):
+    """Node path: norm -> Edgewise -> +res -> norm -> atomwise -> +res.
+    Edge path: Edgewise -> norm -> +res -> norm -> atomwise -> +res (``esen_block.py:301-419``)."""
+
+    def __init__(self, sphere_channels, hidden_channels, lmax, mmax, mapping, edge_channels_list,
+                 norm_type="rms_norm_sh", message_type="source-target", node_or_edge="node"):
+        super().__init__()
+        self.node_or_edge = node_or_edge
+        self.norm_1 = get_normalization_layer(norm_type, lmax, sphere_channels)
+        self.norm_2 = get_normalization_layer(norm_type, lmax, sphere_channels)
+        self.edge_wise = Edgewise(sphere_channels, hidden_channels, lmax, mmax, edge_channels_list, mapping, message_type)
+        self.atom_wise = SpectralAtomwise(sphere_channels, hidden_channels, lmax, mmax)
+
+    def forward(self, x_node, x_edge_emb, x_edge, graph):
+        if self.node_or_edge == "node":
+            h = self.norm_1(x_node)
+            h = self.edge_wise(h, x_edge_emb, x_edge, graph, "node")
+            h, res = self.norm_2(h, residual=x_node)  # res = h + x_node
+            return self.atom_wise(h) + res
+        h = self.edge_wise(x_node, x_edge_emb, x_edge, graph, "edge")
+        h = self.norm_1(h)
+        h, res = self.norm_2(h, residual=x_edge_emb)
+        return self.atom_wise(h) + res
+
+
+class EdgeDegreeEmbedding(nn.Module):
+    """Radial MLP -> m = 0 coefficients -> rotate back -> sum/rescale into nodes, or per edge.
+
+    Reference ``helm/nn/embedding.py:17-141``.
+    """
+
+    def __init__(self, sphere_channels, lmax, mmax, edge_channels_list, rescale_factor, mapping):
+        super().__init__()
+        self.sphere_channels, self.lmax = sphere_channels, lmax
+        self.m0 = mapping.m_size[0]
+        self.rad_func = RadialMLP(list(edge_channels_list) + [self.m0 * sphere_channels])
+        self.rescale_factor = rescale_factor
+
+    def forward(self, x_node, x_edge, graph, node_or_edge="node"):
+        e = self.rad_func(x_edge).view(-1, self.m0, self.sphere_channels)
+        if node_or_edge == "node":
+            return ops.rotate_back_m0_scatter(e, graph, x_node, 1.0 / self.rescale_factor)
+        return ops.rotate_back_m0(e, graph)
+
+
+class Graph:
+    """Per-forward graph data shared by all layers.
+
+    ``src``/``dst``: edge endpoints (local node ids; with a partition, ``src`` may index the
+    halo); ``rot``: m-truncated rotation; ``dst_ptr``: CSR offsets of edges sorted by
+    ``dst`` (edges must be dst-sorted); ``num_nodes``; ``halo``: optional HaloPlan.
+    """
+
+    def __init__(self, src, dst, rot, dst_ptr, num_nodes, lmax, mmax, halo=None):
+        self.src, self.dst, self.rot, self.dst_ptr = src, dst, rot, dst_ptr
+        self.num_nodes, self.lmax, self.mmax, self.halo = num_nodes, lmax, mmax, halo
+        self.cache = {}
+
+
+class eSEN_Backbone(nn.Module):
+    """Atom embedding, edge-degree embedding, N x (node block [+ edge block]), final norm.
+
+    Reference ``helm/esen_osh.py:57-485``.  ``forward`` takes a :class:`GraphBatch`
+    (``maloq_b200.data.batch``) and returns the dict of the reference.
+    """
+
+    def __init__(self, irreps_out=None, max_num_elements=100, sphere_channels=128, lmax=2, mmax=2, cutoff=10.0,
+                 edge_channels=128, distance_function="gaussian", num_distance_basis=512, num_layers=2,
+                 hidden_channels=128, norm_type="rms_norm_sh", act_type="gate", mlp_type="spectral",
+                 gaussian_width=1.0, include_edges=True, open_shell=False, wigner_backend="cuda",
+                 distributed_graph_training=False, message_type="source-target", **unused):
+        super().__init__()
+        if act_type != "gate" or mlp_type != "spectral":
+            raise ValueError("only act_type='gate' and mlp_type='spectral' are implemented (as in the reference)")
+        self.max_num_elements, self.lmax, self.mmax = max_num_elements, lmax, mmax
+        self.sphere_channels, self.hidden_channels = sphere_channels, hidden_channels
+        self.include_edges, self.num_layers = include_edges, num_layers
+        self.num_spins = 2 if open_shell else 1
+        self.message_type = message_type
+        for l, J in enumerate(sph.J_matrices(lmax, dtype=torch.float64)):
+            self.register_buffer(f"Jd_{l}", J)
+        self.sph_feature_size = (lmax + 1) ** 2
+        self.mappingReduced = CoefficientMapping(lmax, mmax)
+        self.sphere_embedding = nn.Embedding(max_num_elements, sphere_channels)
+        self.abs_max_charge = 10
+        self.charge_embedding = nn.Embedding(2 * self.abs_max_charge + 1, sphere_channels)
+        self.max_spin_multiplicity = 11
+        self.spin_embedding = nn.Embedding(self.max_spin_multiplicity, sphere_channels)
+        self.scalar_node_embedding = nn.Linear(3 * sphere_channels, sphere_channels)
+        self.cutoff, self.edge_channels, self.num_distance_basis = cutoff, edge_channels, num_distance_basis
+        if distance_function == "gaussian":
+            self.distance_expansion = GaussianSmearing(0.0, cutoff, num_distance_basis, gaussian_width)
+        elif distance_function == "bessel":
+            self.distance_expansion = EnvelopedBesselBasis(num_distance_basis, cutoff)
+        else:
+            raise ValueError("unknown distance function")
+        self.source_embedding = nn.Embedding(max_num_elements, edge_channels)
+        self.target_embedding = nn.Embedding(max_num_elements, edge_channels)
+        nn.init.uniform_(self.source_embedding.weight.data, -0.001, 0.001)
+        nn.init.uniform_(self.target_embedding.weight.data, -0.001, 0.001)
+        self.edge_channels_list = [num_distance_basis + 2 * edge_channels, edge_channels, edge_channels]
+        self.edge_degree_embedding = EdgeDegreeEmbedding(sphere_channels, lmax, mmax, self.edge_channels_list, 5.0,
+                                                         self.mappingReduced)
+        self.node_blocks = nn.ModuleList()
+        if include_edges:
+            self.edge_blocks = nn.ModuleList()
+        for _ in range(num_layers):
+            self.node_blocks.append(eSEN_Block(sphere_channels, hidden_channels, lmax, mmax, self.mappingReduced,
+                                               self.edge_channels_list, norm_type, message_type, "node"))
+            if include_edges:
+                self.edge_blocks.append(eSEN_Block(sphere_channels, hidden_channels, lmax, mmax, self.mappingReduced,
+                                                   self.edge_channels_list, norm_type, message_type, "edge"))
+        self.norm = get_normalization_layer(norm_type, lmax, sphere_channels)
+
+    # ---------------------------------------------------------------------------------
+    def build_graph(self, batch) -> Graph:
+        edge_attr = batch.edge_attr
+        vec = edge_attr[:, [2, 3, 1]]  # (x, y, z) -> model frame (y, z, x): polar axis = input z
+        rot = ops.edge_rotation(vec, self.lmax, self.mmax, [getattr(self, f"Jd_{l}") for l in range(self.lmax + 1)],
+                                self.mappingReduced)
+        return Graph(batch.edge_index[0], batch.edge_index[1], rot, batch.dst_ptr, batch.num_nodes,
+                     self.lmax, self.mmax, getattr(batch, "halo", None))
+
+    def forward(self, batch):
+        graph = self.build_graph(batch)
+        dist = batch.edge_attr[:, 0]
+        z = batch.atomic_numbers
+        n_local = graph.num_nodes
+        z_local = z if getattr(batch, "local_node_ids", None) is None else z[batch.local_node_ids]
+        charge = batch.atom_charge + self.abs_max_charge
+        spin = batch.atom_spin
+        emb = torch.cat([self.sphere_embedding(z_local), self.charge_embedding(charge), self.spin_embedding(spin)], -1)
+        l0 = ops.linear(emb, self.scalar_node_embedding.weight, self.scalar_node_embedding.bias)
+        x_node = l0.new_zeros(n_local, self.sph_feature_size, self.sphere_channels)
+        x_node[:, 0] = l0
+        gauss = self.distance_expansion(dist)
+        x_edge = torch.cat([self.source_embedding(batch.src_z), gauss, self.target_embedding(batch.dst_z)], dim=1)
+        x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
+        x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
+        for i in range(self.num_layers):
+            x_node = self.node_blocks[i](x_node, x_edge_emb, x_edge, graph)
+            if self.include_edges:
+                x_edge_emb = self.edge_blocks[i](x_node, x_edge_emb, x_edge, graph)
+        x_node = self.norm(x_node)
+        out = {"node_embeddings": x_node, "edge_index": batch.edge_index, "edge_distance": dist,
+               "edge_distance_vec": batch.edge_attr[:, [2, 3, 1]], "partition": getattr(batch, "halo", None)}
+        if self.include_edges:
+            out["edge_embeddings"] = self.norm(x_edge_emb)
+        else:
+            out.update({"x_edge": x_edge, "graph": graph})
+        return out
+
+    @property
+    def num_params(self):
+        return sum(p.numel() for p in self.parameters())
+
+    def no_weight_decay(self) -> set:
+        """Biases, norm affine parameters and LayerNorm parameters (``esen_osh.py:492-517``)."""
+        out = set()
+        for name, _ in self.named_parameters():
+            leaf = name.rsplit(".", 1)[-1]
+            if leaf in ("bias", "affine_weight", "affine_bias") or ".net.1." in name or ".net.4." in name:
+                out.add(name)
+        return out

@@ -1,0 +1,111 @@
+"""Op layer: every hot op of the model, with one CUDA implementation (sm_100a kernels in
+``ops/csrc``) used for CUDA tensors and the PyTorch definition (``ops/reference.py``) used
+for CPU tensors.  On a CUDA tensor an op whose kernel library is not built raises
+instead of falling back.
+"""
+
+from __future__ import annotations
+
+from . import reference as _ref
+from . import native as _native
+
+__all__ = [
+    "linear", "layernorm_silu", "so3_linear", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
+    "rotate_back_m0_scatter", "rotate_back_m0", "fock_loss",
+]
+
+
+_FORCE_TORCH = False
+
+
+def use_torch_ops(flag: bool = True) -> None:
+    """Run the PyTorch definitions on CUDA tensors too (the NCCL/PyTorch baseline arm and
+    the oracle side of kernel tests)."""
+    global _FORCE_TORCH
+    _FORCE_TORCH = bool(flag)
+
+
+def _cuda(*tensors) -> bool:
+    if _FORCE_TORCH:
+        return False
+    for t in tensors:
+        if t is not None and hasattr(t, "is_cuda"):
+            return bool(t.is_cuda)
+    return False
+
+
+def linear(x, weight, bias=None, act=None):
+    if _cuda(x):
+        return _native.linear(x, weight, bias, act)
+    return _ref.linear(x, weight, bias, act)
+
+
+def layernorm_silu(x, weight, bias, eps=1e-5):
+    if _cuda(x):
+        return _native.layernorm_silu(x, weight, bias, eps)
+    return _ref.layernorm_silu(x, weight, bias, eps)
+
+
+def so3_linear(x, weight, bias, lmax):
+    if _cuda(x):
+        return _native.so3_linear(x, weight, bias, lmax)
+    return _ref.so3_linear(x, weight, bias, lmax)
+
+
+def gate(gating_scalars, x, expand_index, lmax):
+    if _cuda(x):
+        return _native.gate(gating_scalars, x, expand_index, lmax)
+    return _ref.gate(gating_scalars, x, expand_index, lmax)
+
+
+def rms_norm_sh(x, affine_weight, affine_bias, balance_degree_weight, eps, residual=None):
+    if _cuda(x):
+        return _native.rms_norm_sh(x, affine_weight, affine_bias, eps, residual)
+    return _ref.rms_norm_sh(x, affine_weight, affine_bias, balance_degree_weight, eps, residual)
+
+
+def edge_rotation(vec_yzx, lmax, mmax, Js, mapping):
+    if _cuda(vec_yzx):
+        return _native.edge_rotation(vec_yzx, lmax, mmax, Js, mapping)
+    return _ref.edge_rotation(vec_yzx, lmax, mmax, Js, mapping)
+
+
+def _src_feats(x_node, graph):
+    if graph.halo is not None:
+        return graph.halo.gather_source(x_node, graph)
+    return None
+
+
+def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
+    if _cuda(x_node):
+        return _native.edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge)
+    return _ref.edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge, _src_feats(x_node, graph))
+
+
+def rotate_back_m0_scatter(e, graph, x_node, scale):
+    if _cuda(e):
+        return _native.rotate_back_m0_scatter(e, graph, x_node, scale)
+    y = _ref.rotate_back_m0(e, graph.rot)
+    return x_node + _ref.scatter_sum(y * scale, graph.dst, graph.num_nodes).to(x_node.dtype)
+
+
+def rotate_back_m0(e, graph):
+    if _cuda(e):
+        return _native.rotate_back_m0(e, graph)
+    return _ref.rotate_back_m0(e, graph.rot)
+
+
+def fock_loss(node_out, edge_out, node_target, edge_target, node_mask, edge_mask, loss_fn):
+    return _ref.fock_loss(node_out, edge_out, node_target, edge_target, node_mask, edge_mask, loss_fn)
+
+
+def fock_head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):
+    if _cuda(x):
+        return _native.fock_head_process(x, ws, bs, layer_params, act, act_scale, abs_gates)
+    return _ref.fock_head_process(x, ws, bs, layer_params, act, act_scale, abs_gates)
+
+
+def gather_scale(x, idx, mult=None):
+    if _cuda(x):
+        return _native.gather_scale(x, idx, mult)
+    return _ref.gather_scale(x, idx, mult)
