@@ -1,0 +1,233 @@
+"""Headline benchmark: training graphs/s on the drug-like data-parallel config.
+
+Config (BASELINE "Drug-like molecules, data-parallel bf16 on 1/2/4/8 B200"): 30-50 atom
+molecules from {H,C,N,O,F,S,Cl}, def2-SVP-like basis (H 5, 2nd row 14, S/Cl 18 orbitals,
+labels of 324 entries, lmax 4), eSEN backbone lmax=4, mmax=2, 128 channels, 6 layers,
+6 A graph cutoff, 32 molecules per GPU, Fock head with node reductions, rmse+mse loss,
+Adam.  Weak scaling: every rank trains on its own 32 molecules per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|torch|reference]
+
+``native`` runs this framework's kernels; ``torch`` the same model on PyTorch ops with an
+NCCL bucketed all-reduce (the reference-math baseline); ``reference`` the unmodified
+reference package from ``baseline/_ref`` (prints an ``unavailable`` line when it cannot
+be imported).  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+BASELINE_VALUE = None  # BASELINE.json publishes no number for this metric
+METRIC = "train graphs/s (drug-like DP, device-timed, max over ranks)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="native", choices=["native", "torch", "reference"])
+    ap.add_argument("--batch", type=int, default=32, help="molecules per GPU")
+    ap.add_argument("--layers", type=int, default=6)
+    ap.add_argument("--channels", type=int, default=128)
+    ap.add_argument("--n-batches", type=int, default=4, help="distinct batches cycled per rank")
+    ap.add_argument("--grad-sync", default=None)
+    return ap.parse_args()
+
+
+def reference_arm(args):
+    """Run the unmodified reference through its public API, if it imports."""
+    ref = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(ref):
+        return {"impl": "reference", "unavailable": "baseline/_ref not installed"}
+    code = ("import sys; sys.path.insert(0, %r); import maloq.helm.esen_osh, maloq.train_utils.training_workflow" % ref)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd="/tmp")
+    if r.returncode != 0:
+        last = (r.stderr.strip().splitlines() or ["import failed"])[-1]
+        return {"impl": "reference",
+                "unavailable": f"reference package cannot import offline (its dependencies e3nn, cupy, mpi4py, "
+                               f"fairchem, torch_geometric, ase are not installable here): {last}"}
+    return {"impl": "reference", "unavailable": "reference imports but its data pipeline needs cupy/mpi4py at run time"}
+
+
+class ClockSampler:
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, f"/tmp/maloq_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps(reference_arm(args)))
+        return
+    sys.path.insert(0, HERE)
+    import torch
+    import torch.distributed as dist
+
+    from maloq_b200 import ops
+    from maloq_b200.data import batch as B
+    from maloq_b200.data import datasets
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.parallel import dist as pdist
+    from maloq_b200.parallel.dp import GradSync
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        device = pdist.setup_env(backend="nccl")
+    else:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+    rank = pdist.rank()
+    if args.impl == "torch":
+        ops.use_torch_ops(True)
+    torch.manual_seed(0)
+
+    kind = "druglike"
+    labeler = datasets.labeler_for(kind, device)
+    lmax = labeler.layout.lmax
+    kw = dict(sphere_channels=args.channels, hidden_channels=args.channels, lmax=lmax, mmax=2, cutoff=6.0,
+              edge_channels=args.channels, num_layers=args.layers, num_distance_basis=128)
+    t0 = time.time()
+    samples, _ = datasets.build_dataset(kind, args.batch * args.n_batches, kw, seed=1000 + rank, device=device,
+                                        labeler=labeler)
+    host_batches = [B.collate(g, labeler.table).pin_memory() for g in B.batches_by_count(samples, args.batch)]
+    dev_batches = [b.to(device) for b in host_batches]
+    n_edges = sum(b.num_edges for b in host_batches) / len(host_batches)
+    n_nodes = sum(b.num_nodes for b in host_batches) / len(host_batches)
+    t_data = time.time() - t0
+
+    torch.manual_seed(1)
+    backbone = eSEN_Backbone(labeler.irreps, include_edges=True, **kw).to(device)
+    head = Fock_Irreps_Head(None, labeler.irreps, lmax=lmax, sphere_channels=args.channels,
+                            ls_list=labeler.layout.ls_list, reduce_node=True, reduce_node_intra=True).to(device)
+    params = list(backbone.parameters()) + list(head.parameters())
+    opt = torch.optim.Adam(params, lr=1e-4, fused=True)
+    sync = None
+    if world > 1:
+        mode = args.grad_sync or ("nccl" if args.impl == "torch" else "fused")
+        sync = GradSync(params, mode=mode)
+    trainer = SplitTrainer(backbone, head, labeler.irreps, mask_table=torch.as_tensor(labeler.table.mask),
+                           grad_sync=sync)
+    loss_fn = L.rmse_mse_padded_loss
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt)
+    barrier()
+
+    # ---------------- device-timed steps (inputs resident, L2 flushed between steps)
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    launches0 = ops.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record()
+        trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt)
+        ev[i][1].record()
+    barrier()
+    launches = ops.launch_count() - launches0
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+
+    # ---------------- end to end through the public API: H2D from pinned memory + loss D2H
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e2e_start.record()
+    loss_vals = []
+    for i in range(args.steps):
+        hb = host_batches[i % len(host_batches)]
+        db = hb.to(device, non_blocking=True)
+        _, _, loss = trainer.train_step(db, loss_fn, opt)
+        loss_vals.append(loss.item())
+    e2e_end.record()
+    barrier()
+    clk = clocks.stop()
+    e2e_ms = e2e_start.elapsed_time(e2e_end)
+    h2d = sum(v.numel() * v.element_size() for v in host_batches[0].tensors().values())
+
+    t = torch.tensor([ms, e2e_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    ms_step = ms / args.steps
+    graphs = args.batch * world
+    value = graphs / (ms_step / 1e3)
+    e2e_value = graphs / (e2e_ms / args.steps / 1e3)
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 2), "unit": "graphs/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "dtype": "bf16" if args.impl == "native" else "fp32",
+            "data": "synthetic (random drug-like molecules, frozen random-init teacher targets; random-init weights)",
+            "config": {"model": f"eSEN lmax={lmax} mmax=2 C={args.channels} layers={args.layers} + Fock head "
+                                f"(def2-SVP-like, D={labeler.target_len})",
+                       "global_batch": graphs, "seq_len": None, "parallelism": f"dp{world}",
+                       "edges_per_gpu_step": round(n_edges), "atoms_per_gpu_step": round(n_nodes),
+                       "l2": "256 MiB buffer written between timed steps, outside the step events",
+                       "impl": args.impl, "grad_sync": None if sync is None else sync.mode},
+            "e2e": {"value": round(e2e_value, 2), "unit": "graphs/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "final_loss": loss_vals[-1],
+            "setup_s": round(t_data, 1),
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        pdist.cleanup_process_group()
+
+
+if __name__ == "__main__":
+    main()

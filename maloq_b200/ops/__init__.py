@@ -18,6 +18,11 @@ __all__ = [
 _FORCE_TORCH = False
 
 
+def launch_count() -> int:
+    """Number of this library's CUDA kernels launched so far in this process."""
+    return _native.launch_count()
+
+
 def use_torch_ops(flag: bool = True) -> None:
     """Run the PyTorch definitions on CUDA tensors too (the NCCL/PyTorch baseline arm and
     the oracle side of kernel tests)."""

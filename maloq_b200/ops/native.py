@@ -21,7 +21,19 @@ def _get(name):
     return fn
 
 
-def __getattr__(name):
+def __getattr__(name):  # noqa: D401 - module-level op lookup
     if name.startswith("_"):
         raise AttributeError(name)
     return _get(name)
+
+
+_LAUNCHES = [0]
+
+
+def count_launches(n: int = 1) -> None:
+    """Called by every kernel wrapper with the number of kernels it launched."""
+    _LAUNCHES[0] += n
+
+
+def launch_count() -> int:
+    return _LAUNCHES[0]

@@ -1,0 +1,235 @@
+"""Train / evaluate / infer loops (reference ``train_utils/splittrainer.py``).
+
+:class:`SplitTrainer` keeps the reference's constructor and method names.  What differs:
+
+* the step is device-timed with CUDA events (no host ``perf_counter`` around async work);
+* data-parallel gradients go through :class:`maloq_b200.parallel.dp.GradSync`, which
+  reduces bucket by bucket while backward still runs (the reference all-reduces every
+  parameter after backward, ``splittrainer.py:204-218``);
+* the Fock loss is one fused masked kernel that also writes its gradient;
+* batches are prefetched to the device on a side stream from pinned host memory;
+* checkpoints carry the epoch, scheduler and RNG state in addition to the reference's
+  ``{backbone|head}.pt`` files, so resume continues where it stopped.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..ops import loss as loss_ops
+from . import checkpoint as ckpt
+
+
+def _rank():
+    return dist.get_rank() if dist.is_available() and dist.is_initialized() else 0
+
+
+def _world():
+    return dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+
+
+class Prefetcher:
+    """Copies host batches to the device on a side stream, one batch ahead."""
+
+    def __init__(self, batches, device):
+        self.batches, self.device = batches, torch.device(device)
+        self.stream = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
+
+    def __iter__(self):
+        if self.stream is None:
+            for b in self.batches:
+                yield b.to(self.device)
+            return
+        it = iter(self.batches)
+        nxt = None
+        try:
+            nxt = self._issue(next(it))
+        except StopIteration:
+            return
+        for b in it:
+            cur, ev = nxt
+            torch.cuda.current_stream(self.device).wait_event(ev)
+            nxt = self._issue(b)
+            yield cur
+        cur, ev = nxt
+        torch.cuda.current_stream(self.device).wait_event(ev)
+        yield cur
+
+    def _issue(self, b):
+        with torch.cuda.stream(self.stream):
+            d = b.to(self.device, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        return d, ev
+
+
+class SplitTrainer:
+    def __init__(self, backbone, head, head_irreps, save_frequency=10, run_id=None, run_name="noname",
+                 mask_table=None, grad_sync=None):
+        self.backbone, self.head, self.head_irreps = backbone, head, head_irreps
+        self.save_frequency, self.run_name = save_frequency, run_name
+        self.mask_table = mask_table
+        self.grad_sync = grad_sync
+        self.open_shell = getattr(head, "num_spins", 1) > 1
+        self.history = {"train_node": [], "train_edge": [], "val_node": [], "val_edge": []}
+        self.start_epoch = 0
+
+    # ------------------------------------------------------------------ one step
+    def masks(self, batch):
+        mt = self.mask_table.to(batch.node_pair_type.device)
+        return mt, batch.node_pair_type, batch.edge_pair_type
+
+    def forward_loss(self, batch, loss_fxn):
+        emb = self.backbone(batch)
+        node_out, edge_out = self.head(emb, batch)
+        mt, npt, ept = self.masks(batch)
+        spins = node_out.shape[0]
+        lns, les, lts = [], [], []
+        for s in range(spins):
+            ln, le, lt = loss_ops.fock_loss(node_out[s], edge_out[s], batch.node_y[s], batch.y[s], mt, npt, ept,
+                                            loss_fxn)
+            lns.append(ln)
+            les.append(le)
+            lts.append(lt)
+        return sum(lns) / spins, sum(les) / spins, sum(lts) / spins
+
+    def train_step(self, batch, loss_fxn, optimizer, scheduler=None):
+        ln, le, loss = self.forward_loss(batch, loss_fxn)
+        if self.grad_sync is not None:
+            self.grad_sync.begin_step()
+        loss.backward()
+        if self.grad_sync is not None:
+            self.grad_sync.finish()
+        optimizer.step()
+        optimizer.zero_grad(set_to_none=True)
+        if scheduler is not None and not hasattr(scheduler, "patience"):
+            scheduler.step()
+        return ln.detach(), le.detach(), loss.detach()
+
+    # ------------------------------------------------------------------ loops
+    def train(self, num_epochs, loss_fxn, optimizer, scheduler, device, train_loader, loss_target_string="fock_matrix",
+              node_target_name="node_y", val_loader=None, edge_target_name="y", output_folder="outputs",
+              step_every_epoch=False, min_lr=1e-10, log_every=1, **unused):
+        rank = _rank()
+        val_loader = val_loader or train_loader
+        self.check_batch_consistency(len(train_loader), len(val_loader), device)
+        os.makedirs(output_folder, exist_ok=True)
+        for epoch in range(self.start_epoch, num_epochs):
+            self.backbone.train()
+            self.head.train()
+            t0 = time.perf_counter()
+            sn = torch.zeros((), device=device)
+            se = torch.zeros((), device=device)
+            for bi, batch in enumerate(Prefetcher(train_loader, device)):
+                ln, le, loss = self.train_step(batch, loss_fxn, optimizer, scheduler)
+                sn += ln
+                se += le
+                if rank == 0 and log_every and bi % log_every == 0:
+                    print(f"--> Rank {rank} epoch {epoch + 1} batch {bi} loss: {loss.item():.6g}", flush=True)
+            nb = max(1, len(train_loader))
+            self.history["train_node"].append(sn.item() / nb)
+            self.history["train_edge"].append(se.item() / nb)
+            vn, ve, vt = self.validate(val_loader, loss_fxn, device)
+            self.history["val_node"].append(vn)
+            self.history["val_edge"].append(ve)
+            if hasattr(scheduler, "patience"):
+                scheduler.step(vt)
+            elif step_every_epoch and scheduler is not None:
+                scheduler.step()
+            lr = optimizer.param_groups[0]["lr"]
+            if rank == 0:
+                print(f"Epoch {epoch + 1}, Train Loss: [node] {self.history['train_node'][-1]:.6g} "
+                      f"[edge] {self.history['train_edge'][-1]:.6g}  Val: [node] {vn:.6g} [edge] {ve:.6g}  "
+                      f"lr {lr:.3g}  time {time.perf_counter() - t0:.2f}s", flush=True)
+            done = lr <= min_lr
+            if rank == 0 and ((epoch + 1) % self.save_frequency == 0 or done or epoch + 1 == num_epochs):
+                self.save_training_state(epoch, optimizer, scheduler, output_folder)
+            if done:
+                print("Reached minimum learning rate, finished training.", flush=True)
+                return
+        return self.history
+
+    @torch.no_grad()
+    def validate(self, loader, loss_fxn, device):
+        self.backbone.eval()
+        self.head.eval()
+        tot = torch.zeros(3, device=device, dtype=torch.float64)
+        for batch in Prefetcher(loader, device):
+            ln, le, lt = self.forward_loss(batch, loss_fxn)
+            tot += torch.stack([ln, le, lt]).double()
+        tot /= max(1, len(loader))
+        if _world() > 1:
+            dist.all_reduce(tot)
+            tot /= _world()
+        return tuple(tot.tolist())
+
+    def check_batch_consistency(self, num_train_batches, num_val_batches, device):
+        """All ranks must see the same number of batches (``splittrainer.py:1152-1170``)."""
+        if _world() == 1:
+            return
+        t = torch.tensor([num_train_batches, num_val_batches], device=device if dist.get_backend() == "nccl" else "cpu")
+        lst = [torch.zeros_like(t) for _ in range(_world())]
+        dist.all_gather(lst, t)
+        if not all(torch.equal(lst[0], x) for x in lst):
+            raise ValueError(f"Mismatch in number of batches across ranks: {[x.tolist() for x in lst]}")
+
+    def save_training_state(self, epoch, optimizer, scheduler, output_folder):
+        ckpt.save_training_state(output_folder, self.backbone, self.head, optimizer, scheduler, epoch, self.history)
+
+    # ------------------------------------------------------------------ eval / infer
+    @torch.no_grad()
+    def evaluate(self, loss_fxn, device, loader, labeler, output_folder="outputs", samples=None, scale_shift=None,
+                 **unused):
+        """Per structure: label MAE, Hamiltonian MAE and eigenvalue MAE (generalised with S
+        when an overlap is given), written to ``model_fock_eval_{rank}.txt``
+        (reference ``splittrainer.py:378-822``)."""
+        import scipy.linalg
+
+        from ..data.batch import collate
+
+        self.backbone.eval()
+        self.head.eval()
+        rank = _rank()
+        rows = []
+        for k, s in enumerate(samples):
+            b = collate([s], labeler.table).to(device)
+            emb = self.backbone(b)
+            no, eo = self.head(emb, b)
+            no, eo = no[0], eo[0]
+            if scale_shift is not None:
+                no = scale_shift.unshift(no, s.z)
+                ty = scale_shift.unshift(b.node_y[0], s.z)
+            else:
+                ty = b.node_y[0]
+            bp = labeler.blocks_from_labels(s, no, eo)
+            bt = labeler.blocks_from_labels(s, ty, b.y[0])
+            Hp, Ht = bp.to_dense(), bt.to_dense()
+            Hp = 0.5 * (Hp + Hp.T)
+            ep = scipy.linalg.eigvalsh(Hp)
+            et = scipy.linalg.eigvalsh(Ht)
+            rows.append((k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), s.num_nodes))
+        os.makedirs(output_folder, exist_ok=True)
+        with open(os.path.join(output_folder, f"model_fock_eval_{rank}.txt"), "w") as f:
+            f.write("Index\tTotal_MAE\tEigenvalue_MAE\tNum_Atoms\n")
+            for r in rows:
+                f.write("\t".join(str(x) for x in r) + "\n")
+        return rows
+
+    @torch.no_grad()
+    def infer(self, device, batch, labeler, output_folder="outputs", partition=None, **unused):
+        """Forward + label -> block-sparse Hamiltonian; every rank writes its own blocks
+        (``hamiltonian_rank{r}.npz``) instead of gathering to rank 0."""
+        from ..parallel.infer import write_partition_hamiltonian
+
+        self.backbone.eval()
+        self.head.eval()
+        emb = self.backbone(batch)
+        no, eo = self.head(emb, batch)
+        return write_partition_hamiltonian(output_folder, batch, no[0], eo[0], labeler, partition)

@@ -1,0 +1,231 @@
+"""TrainingWorkflow: config -> data -> model -> train / eval / infer (reference
+``train_utils/training_workflow.py``).
+
+Same public API as the reference: ``TrainingWorkflow(config).run()`` with the reference's
+config keys (plus ``mmax``, ``grad_sync``, ``num_structures``).  Datasets:
+
+* ``synthetic_small`` / ``synthetic_druglike`` / ``synthetic_large`` / ``synthetic_sio2`` -
+  generated structures with teacher targets (:mod:`maloq_b200.data.datasets`);
+* ``nablaDFT`` - the nablaDFT SQLite Hamiltonian database (:mod:`maloq_b200.data.readers`).
+
+``rcut_orbitals`` is a per-atom radius, so graphs connect pairs closer than
+``2 * rcut_orbitals`` (reference ``fock_targets_batched.py:208``); ``rcut_gaussian`` is the
+Gaussian-smearing range.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import random
+
+import numpy as np
+import torch
+
+from ..core.irreps import Irreps
+from ..data import batch as B
+from ..data import datasets
+from ..models.backbone import eSEN_Backbone
+from ..models.heads import Fock_Irreps_Head, HELM_Energy_Head, HELM_Force_Head
+from ..parallel import dist as pdist
+from . import checkpoint as ckpt
+from . import loss as L
+from .trainer import SplitTrainer
+
+
+class TrainingWorkflow:
+    DEFAULTS = {
+        "run_name": "run", "output_folder": "outputs", "open_shell": False,
+        "device": "cuda" if torch.cuda.is_available() else "cpu", "wigner_backend": "cuda",
+        "distribute_graphs": False, "partition_type": None, "tiling_dims": None, "lr_init": 1e-4,
+        "optimizer_type": "adam", "compute_total_energy": False,
+        "dist_backend": "nccl" if torch.cuda.is_available() else "gloo",
+        "dtype": torch.float32, "train_or_eval": "train", "train_backbone": True, "train_head": True,
+        "restart_backbone": False, "restart_head": False, "restart_optimizer": False,
+        "backbone_checkpoint": "backbone.pt", "head_checkpoint": "head.pt", "reduce_edge": False,
+        "reduce_node": True, "reduce_node_intra": True, "loss_target": "fock_matrix", "num_epochs": 1,
+        "batch_size": 1, "scheduler_type": "cosine", "eta_min": 1e-8, "patience": 100, "threshold": 1e-8,
+        "save_frequency": 10, "num_distance_basis": 128, "num_mp_layers": 3, "l_embedding_dim": 128,
+        "rcut_orbitals": 3.0, "rcut_gaussian": 6.0, "gaussian_width": 1.0,
+        "train_loss_fxn": L.rmse_mse_padded_loss, "test_loss_fxn": L.l1_unpadded_loss,
+        "dataset_name": "synthetic_small", "num_structures": 16, "num_train": 0, "num_val": 0,
+        "grad_sync": None, "seed": 42,
+    }
+
+    def __init__(self, config):
+        self.config = self.DEFAULTS | dict(config)
+        for k in ("train_loss_fxn", "test_loss_fxn"):
+            self.config[k] = L.get_loss(self.config[k])
+        self.setup_environment()
+        self.check_input_config()
+
+    def setup_environment(self):
+        seed = self.config["seed"]
+        torch.manual_seed(seed)
+        np.random.seed(seed)
+        random.seed(seed)
+        torch.set_default_dtype(self.config["dtype"] if self.config["dtype"] != torch.bfloat16 else torch.float32)
+        self.rank, self.world_size, _ = pdist.env_rank_world()
+        if self.config["device"] == "cpu":
+            self.config["dist_backend"] = "gloo"
+        if self.world_size > 1 or self.config["distribute_graphs"]:
+            self.device = pdist.setup_env(backend=self.config["dist_backend"])
+            if self.config["device"] == "cpu":
+                self.device = torch.device("cpu")
+        else:
+            self.device = torch.device(self.config["device"])
+            if self.device.type == "cuda":
+                torch.cuda.set_device(self.device)
+        if self.rank == 0:
+            os.makedirs(self.config["output_folder"], exist_ok=True)
+
+    def check_input_config(self):
+        c = self.config
+        c["include_edges"] = "matrix" in c["loss_target"]
+        if c.get("hidden_dim") is None:
+            c["hidden_dim"] = c["l_embedding_dim"]
+        c.setdefault("message_type", "source-target")
+        c.setdefault("basis_transform_backend", "cuda")
+        if c["distribute_graphs"] and c["partition_type"] is None:
+            c["partition_type"] = "slab"
+        if c["reduce_edge"] and c["distribute_graphs"]:
+            raise ValueError("reduce_edge and distribute_graphs cannot both be True")
+        if c["distribute_graphs"] and "matrix" not in c["loss_target"]:
+            raise ValueError("distributed graph training needs a matrix-valued loss target")
+        for name, key in (("backbone", "restart_backbone"), ("head", "restart_head")):
+            if c[key]:
+                path = os.path.join(c["output_folder"], c[f"{name}_checkpoint"])
+                if not os.path.exists(path):
+                    raise FileNotFoundError(f"{name} checkpoint not found at {path}")
+                try:
+                    torch.load(path, map_location="cpu", weights_only=False)
+                except Exception as e:  # noqa: BLE001 - report which file is corrupt
+                    raise ValueError(f"Error loading {name} checkpoint from {path}: {e}") from e
+        if self.rank == 0 and c["train_or_eval"] == "train":
+            path = os.path.join(c["output_folder"], f"config_{c['run_name']}.json")
+            with open(path, "w") as f:
+                json.dump({k: (v.__name__ if hasattr(v, "__name__") else str(v)) for k, v in c.items()}, f, indent=4)
+
+    # ------------------------------------------------------------------ data
+    def model_kwargs(self, lmax):
+        c = self.config
+        mmax = c.get("mmax") or lmax
+        return dict(sphere_channels=c["l_embedding_dim"], hidden_channels=c["hidden_dim"], lmax=lmax,
+                    mmax=min(mmax, lmax), cutoff=c["rcut_gaussian"], edge_channels=c["l_embedding_dim"],
+                    num_layers=c["num_mp_layers"], num_distance_basis=c["num_distance_basis"],
+                    gaussian_width=c["gaussian_width"], message_type=c["message_type"], open_shell=c["open_shell"])
+
+    def prepare_data(self):
+        c = self.config
+        name = c["dataset_name"]
+        if name.startswith("synthetic_"):
+            kind = name[len("synthetic_"):]
+            labeler = datasets.labeler_for(kind, self.device)
+            kw = self.model_kwargs(labeler.layout.lmax)
+            n = c["num_structures"]
+            samples, labeler = datasets.build_dataset(kind, n, kw, seed=c["seed"], device=self.device,
+                                                      cutoff=2 * c["rcut_orbitals"], labeler=labeler)
+        elif name == "nablaDFT":
+            from ..data.readers import load_nabladft
+
+            samples, labeler = load_nabladft(c["dbpath"], c, self.device)
+        else:
+            raise ValueError(f"Unknown dataset name: {name}")
+        n_val = c["num_val"] or max(1, len(samples) // 8)
+        n_train = c["num_train"] or (len(samples) - n_val)
+        train, val = samples[:n_train], samples[n_train:n_train + n_val]
+        if self.world_size > 1 and not c["distribute_graphs"]:
+            train = [train[i] for i in pdist.split_indices(len(train), self.rank, self.world_size)]
+            val = [val[i] for i in pdist.split_indices(len(val), self.rank, self.world_size, drop_remainder=False)] or val[:1]
+        bs = c["batch_size"]
+        mk = lambda xs: [B.collate(g, labeler.table).pin_memory() if self.device.type == "cuda"
+                         else B.collate(g, labeler.table) for g in B.batches_by_count(xs, bs, drop_last=False)]
+        self.labeler = labeler
+        self.val_samples = val
+        return mk(train), mk(val), labeler
+
+    # ------------------------------------------------------------------ model
+    def build_model(self, labeler):
+        c = self.config
+        irreps = labeler.irreps
+        lmax = irreps.lmax
+        backbone = eSEN_Backbone(irreps, include_edges=c["include_edges"], **self.model_kwargs(lmax)).to(self.device)
+        if c["loss_target"] in ("fock_matrix", "density_matrix"):
+            head = Fock_Irreps_Head(None, irreps, lmax=lmax, sphere_channels=c["l_embedding_dim"],
+                                    reduce_edge=c["reduce_edge"], open_shell=c["open_shell"],
+                                    ls_list=labeler.layout.ls_list, reduce_node=c["reduce_node"],
+                                    reduce_node_intra=c["reduce_node_intra"])
+        elif c["loss_target"] == "forces":
+            head = HELM_Force_Head(backbone)
+        else:
+            head = HELM_Energy_Head(backbone)
+        head = head.to(self.device)
+        params = []
+        for m, flag in ((backbone, c["train_backbone"]), (head, c["train_head"])):
+            if flag:
+                params += list(m.parameters())
+            else:
+                for p in m.parameters():
+                    p.requires_grad_(False)
+        if c["optimizer_type"] == "adamw":
+            opt = torch.optim.AdamW(params, lr=c["lr_init"], weight_decay=c.get("weight_decay", 0.0))
+        elif c["optimizer_type"] == "muon":
+            opt = L.HybridMuon(params, muon_lr=c.get("muon_lr", 0.02), adamw_lr=c["lr_init"],
+                               weight_decay=c.get("weight_decay", 0.0))
+        else:
+            opt = torch.optim.Adam(params, lr=c["lr_init"], **({"fused": True} if self.device.type == "cuda" else {}))
+        folder = c["output_folder"]
+        if c["restart_backbone"]:
+            ckpt.load_model(backbone, os.path.join(folder, c["backbone_checkpoint"]), self.device)
+        if c["restart_head"]:
+            ckpt.load_model(head, os.path.join(folder, c["head_checkpoint"]), self.device,
+                            opt if c["restart_optimizer"] else None)
+        return backbone, head, opt
+
+    def get_scheduler(self, optimizer, n_batches):
+        c = self.config
+        if c["scheduler_type"] == "plateau":
+            return torch.optim.lr_scheduler.ReduceLROnPlateau(optimizer, mode="min", factor=0.5,
+                                                              patience=c["patience"], threshold=c["threshold"])
+        return torch.optim.lr_scheduler.CosineAnnealingLR(optimizer, T_max=max(1, c["num_epochs"] * n_batches),
+                                                          eta_min=c["eta_min"])
+
+    def grad_sync(self, backbone, head):
+        if self.world_size <= 1:
+            return None
+        from ..parallel.dp import GradSync
+
+        mode = self.config["grad_sync"] or ("fused" if self.device.type == "cuda" else "nccl")
+        params = [p for p in list(backbone.parameters()) + list(head.parameters()) if p.requires_grad]
+        return GradSync(params, mode=mode)
+
+    # ------------------------------------------------------------------ run
+    def run(self):
+        try:
+            c = self.config
+            train, val, labeler = self.prepare_data()
+            backbone, head, opt = self.build_model(labeler)
+            sched = self.get_scheduler(opt, len(train))
+            mask_table = torch.as_tensor(labeler.table.mask)
+            trainer = SplitTrainer(backbone, head, labeler.irreps, save_frequency=c["save_frequency"],
+                                   run_name=c["run_name"], mask_table=mask_table,
+                                   grad_sync=self.grad_sync(backbone, head))
+            if c["train_or_eval"] == "train":
+                if c["restart_backbone"] or c["restart_head"]:
+                    st = ckpt.load_resume(c["output_folder"], sched)
+                    if st is not None:
+                        trainer.start_epoch = st["epoch"] + 1
+                        trainer.history = st["history"]
+                return trainer.train(c["num_epochs"], c["train_loss_fxn"], opt, sched, self.device, train,
+                                     val_loader=val, output_folder=c["output_folder"],
+                                     step_every_epoch=c["step_every_epoch"] if "step_every_epoch" in c else False,
+                                     log_every=c.get("log_every", 1))
+            if c["train_or_eval"] == "eval":
+                return trainer.evaluate(c["test_loss_fxn"], self.device, val, labeler,
+                                        output_folder=c["output_folder"], samples=self.val_samples)
+            return trainer.infer(self.device, val[0].to(self.device), labeler, output_folder=c["output_folder"])
+        finally:
+            self.close()
+
+    def close(self):
+        pdist.cleanup_process_group(sync_barrier=self.world_size > 1)
