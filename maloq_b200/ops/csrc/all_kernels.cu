@@ -1,0 +1,5 @@
+// Unity translation unit of the kernel library: every kernel source is included here so
+// that device globals (the error word) have exactly one definition without relocatable
+// device code.
+#include "runtime.cu"
+#include "gemm.cu"
