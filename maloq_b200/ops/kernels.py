@@ -95,7 +95,7 @@ class _Linear(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             gx = gemm_nt(g2, weight.t().contiguous()).to(ctx.in_dtype).reshape(ctx.in_shape)
         if ctx.needs_input_grad[1]:
-            gw = gemm_tn_weight_grad(g2, x2)[:, : weight.shape[1]]
+            gw = gemm_tn_weight_grad(g2, x2)[: weight.shape[0], : weight.shape[1]]
         if ctx.has_bias and ctx.needs_input_grad[2]:
             gb = gy.reshape(-1, gy.shape[-1]).float().sum(0)
         return gx, gw, gb

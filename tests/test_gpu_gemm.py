@@ -84,3 +84,14 @@ def test_linear_autograd_matches_torch(cuda_device):
     _close(x.grad, x2.grad, 1e-2)
     _close(w.grad, w2.grad, 1e-2)
     _close(b.grad, b2.grad, 1e-3)
+
+
+def test_linear_odd_sizes(cuda_device):
+    from maloq_b200 import ops
+
+    x = torch.randn(50, 13, device=cuda_device, requires_grad=True)
+    w = torch.randn(7, 13, device=cuda_device, requires_grad=True)
+    y = ops.linear(x, w)
+    y.sum().backward()
+    assert w.grad.shape == w.shape and x.grad.shape == x.shape
+    _close(y, _ref(x.detach(), w.detach()), 1e-2)
