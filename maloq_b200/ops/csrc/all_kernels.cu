@@ -3,3 +3,4 @@
 // device code.
 #include "runtime.cu"
 #include "gemm.cu"
+#include "noalloc.cu"
