@@ -4,3 +4,4 @@
 #include "runtime.cu"
 #include "gemm.cu"
 #include "noalloc.cu"
+#include "edge.cu"

@@ -4,6 +4,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "edge.h"
 #include "gemm.h"
 #include "runtime.h"
 
@@ -20,7 +21,7 @@ void gemm(std::vector<at::Tensor> As, std::vector<at::Tensor> Bs, std::vector<at
           std::vector<c10::optional<at::Tensor>> biases, bool mn_major, int64_t act, double alpha, int64_t splits,
           int64_t bn) {
   const size_t np = As.size();
-  TORCH_CHECK(np >= 1 && np <= 4 && Bs.size() == np && Cs.size() == np, "gemm: 1..4 problems");
+  TORCH_CHECK(np >= 1 && np <= 8 && Bs.size() == np && Cs.size() == np, "gemm: 1..8 problems");
   std::vector<maloq::GemmProblem> P(np);
   const bool out_fp32 = Cs[0].scalar_type() == at::kFloat;
   for (size_t i = 0; i < np; ++i) {
@@ -71,6 +72,106 @@ void splitk_reduce(at::Tensor part, at::Tensor out, double beta) {
                                   part.stride(0), (float)beta, stream()));
 }
 
+
+template <class T>
+T* ptr(const c10::optional<at::Tensor>& t) {
+  return t.has_value() ? t->data_ptr<T>() : nullptr;
+}
+
+void chk(const at::Tensor& t, at::ScalarType dt, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.scalar_type() == dt, what,
+              ": expected a contiguous CUDA tensor of ", dt);
+}
+
+__nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+const long long* ll(const at::Tensor& t) { return reinterpret_cast<const long long*>(t.data_ptr<int64_t>()); }
+const long long* ll(const c10::optional<at::Tensor>& t) { return t.has_value() ? ll(*t) : nullptr; }
+
+// A [E, R*Cin] = rad * rot . [X[src] | X[dst] | XE]
+void gather_rotate_fwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
+                       at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor A, int64_t Cin) {
+  chk(X, at::kFloat, "X");
+  chk(rot, at::kFloat, "rot");
+  chk(A, at::kBFloat16, "A");
+  chk(src, at::kLong, "src");
+  chk(dst, at::kLong, "dst");
+  if (XE.has_value()) chk(*XE, at::kFloat, "XE");
+  if (rad.has_value()) chk(*rad, at::kFloat, "rad");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::edge_gather_rotate_fwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), ll(src), ll(dst),
+                                      rot.data_ptr<float>(), ptr<float>(rad), bf(A), (int)src.size(0),
+                                      (int)X.size(2), (int)Cin, stream()));
+}
+
+void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
+                       at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor dA, at::Tensor DSRC,
+                       at::Tensor DDST, c10::optional<at::Tensor> DXE, c10::optional<at::Tensor> DRAD, int64_t Cin) {
+  chk(X, at::kFloat, "X");
+  chk(dA, at::kBFloat16, "dA");
+  chk(DSRC, at::kFloat, "DSRC");
+  chk(DDST, at::kFloat, "DDST");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::edge_gather_rotate_bwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), ll(src), ll(dst),
+                                      rot.data_ptr<float>(), ptr<float>(rad), bf(dA), DSRC.data_ptr<float>(),
+                                      DDST.data_ptr<float>(), ptr<float>(DXE), ptr<float>(DRAD), (int)src.size(0),
+                                      (int)X.size(2), (int)Cin, stream()));
+}
+
+// DX[n] = sum over dst-CSR of DDST + sum over src-CSR of DSRC (either may be absent)
+void node_reduce(at::Tensor DDST, at::Tensor dst_ptr, c10::optional<at::Tensor> DSRC,
+                 c10::optional<at::Tensor> src_perm, c10::optional<at::Tensor> src_ptr, at::Tensor DX) {
+  chk(DDST, at::kFloat, "DDST");
+  chk(DX, at::kFloat, "DX");
+  const int N = (int)DX.size(0);
+  const int SC = (int)(DX.numel() / std::max<int64_t>(1, N));
+  const at::cuda::CUDAGuard guard(DX.device());
+  check(maloq::edge_node_reduce(DDST.data_ptr<float>(), ll(dst_ptr), ptr<float>(DSRC), ll(src_perm), ll(src_ptr),
+                                DX.data_ptr<float>(), N, SC, stream()));
+}
+
+void rotate_back_scatter(int64_t L, int64_t MM, at::Tensor Y, int64_t koff, int64_t Rk, at::Tensor rot,
+                         at::Tensor dst_ptr, c10::optional<at::Tensor> base, at::Tensor out, double scale) {
+  chk(Y, at::kBFloat16, "Y");
+  chk(out, at::kFloat, "out");
+  if (base.has_value()) chk(*base, at::kFloat, "base");
+  const at::cuda::CUDAGuard guard(Y.device());
+  check(maloq::edge_rotate_back_scatter((int)L, (int)MM, bf(Y), (int)Y.size(1), (int)koff, rot.data_ptr<float>(),
+                                        ll(dst_ptr), ptr<float>(base), out.data_ptr<float>(), (int)out.size(0),
+                                        (int)out.size(2), (int)Rk, (float)scale, stream()));
+}
+
+void rotate_back_edge(int64_t L, int64_t MM, at::Tensor Y, int64_t koff, int64_t Rk, at::Tensor rot, at::Tensor out) {
+  chk(Y, at::kBFloat16, "Y");
+  chk(out, at::kFloat, "out");
+  const at::cuda::CUDAGuard guard(Y.device());
+  check(maloq::edge_rotate_back((int)L, (int)MM, bf(Y), (int)Y.size(1), (int)koff, rot.data_ptr<float>(),
+                                out.data_ptr<float>(), (int)out.size(0), (int)out.size(2), (int)Rk, stream()));
+}
+
+void rotate_grad(int64_t L, int64_t MM, at::Tensor G, c10::optional<at::Tensor> rows, at::Tensor rot,
+                 c10::optional<at::Tensor> DY, c10::optional<at::Tensor> DYf, int64_t Rk, double scale) {
+  chk(G, at::kFloat, "G");
+  const at::cuda::CUDAGuard guard(G.device());
+  check(maloq::edge_rotate_grad((int)L, (int)MM, G.data_ptr<float>(), ll(rows), rot.data_ptr<float>(),
+                                DY.has_value() ? bf(*DY) : nullptr, ptr<float>(DYf), (int)rot.size(0),
+                                (int)G.size(2), (int)Rk, (float)scale, stream()));
+}
+
+void gate_fwd(int64_t L, int64_t MM, at::Tensor Y1, at::Tensor H1, int64_t H) {
+  chk(Y1, at::kBFloat16, "Y1");
+  chk(H1, at::kBFloat16, "H1");
+  const at::cuda::CUDAGuard guard(Y1.device());
+  check(maloq::edge_gate_fwd((int)L, (int)MM, bf(Y1), bf(H1), (int)Y1.size(0), (int)H, stream()));
+}
+
+void gate_bwd(int64_t L, int64_t MM, at::Tensor Y1, at::Tensor dH1, at::Tensor dY1, int64_t H) {
+  chk(Y1, at::kBFloat16, "Y1");
+  chk(dH1, at::kBFloat16, "dH1");
+  chk(dY1, at::kBFloat16, "dY1");
+  const at::cuda::CUDAGuard guard(Y1.device());
+  check(maloq::edge_gate_bwd((int)L, (int)MM, bf(Y1), bf(dH1), bf(dY1), (int)Y1.size(0), (int)H, stream()));
+}
+
 int64_t error_status(bool clear) { return maloq::error_status(clear); }
 
 }  // namespace
@@ -78,5 +179,13 @@ int64_t error_status(bool clear) { return maloq::error_status(clear); }
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "grouped tcgen05 bf16 GEMM");
   m.def("splitk_reduce", &splitk_reduce, "sum split-K partials");
+  m.def("gather_rotate_fwd", &gather_rotate_fwd);
+  m.def("gather_rotate_bwd", &gather_rotate_bwd);
+  m.def("rotate_back_scatter", &rotate_back_scatter);
+  m.def("rotate_back_edge", &rotate_back_edge);
+  m.def("rotate_grad", &rotate_grad);
+  m.def("gate_fwd", &gate_fwd);
+  m.def("gate_bwd", &gate_bwd);
+  m.def("node_reduce", &node_reduce);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
 }

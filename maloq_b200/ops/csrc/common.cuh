@@ -9,6 +9,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 
 #ifndef MALOQ_SPIN_LIMIT
 #define MALOQ_SPIN_LIMIT (1u << 26)

@@ -1,0 +1,369 @@
+// Edge-frame kernels of the Edgewise message pass (CUDA cores; memory-bound).
+//
+// Layouts: node features X [N, S, C] fp32 (S = (L+1)^2 l-major coefficients), edge
+// embeddings XE [E, S, C] fp32, rotation ROT [E, R, S] fp32 (R m-major rows, |m| <= mmax;
+// row k only has entries in the 2l+1 columns of its degree), messages A / H / Y
+// [E, R*Cm] bf16 (row k of edge e at columns k*Cm .. k*Cm+Cm-1), radial modulation
+// RAD [E, NS*Cin] fp32 (NS slots, see edge_frame.cuh).
+// Edges are sorted by destination; dst_ptr [N+1] gives each node's incoming-edge range and
+// src_perm/src_ptr the same for sources, so every reduction over edges is a fixed-order
+// segmented sum (deterministic, no atomics).
+// Kernels are templated on the frame (L, MM) so the row/degree structure is compile-time.
+#include "common.cuh"
+#include "edge.h"
+#include "edge_frame.cuh"
+
+namespace maloq {
+
+__device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// ---------------------------------------------------------------- gather + rotate + modulate
+// A[e, k, c'] = rad[e, slot(k)*Cin + c'] * sum_{j in degree l_k} rot[e,k,j] * in[e, j, c']
+// in = [X[src] | X[dst] | XE[e]] along channels (Cin = 2C or 3C).
+template <int L, int MM>
+__global__ void __launch_bounds__(128) gather_rotate_fwd_kernel(
+    const float* __restrict__ X, const float* __restrict__ XE, const long long* __restrict__ src,
+    const long long* __restrict__ dst, const float* __restrict__ rot, const float* __restrict__ rad,
+    __nv_bfloat16* __restrict__ A, int E, int C, int Cin) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R;
+  const int e = blockIdx.x;
+  const int cp = blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= E || cp >= Cin) return;
+  const float* base;
+  if (cp < C) base = X + (size_t)src[e] * S * C + cp;
+  else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
+  else base = XE + (size_t)e * S * C + (cp - 2 * C);
+  float in[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) in[j] = __ldg(base + (size_t)j * C);
+  const float* re = rot + (size_t)e * R * S;
+  const float* rd = rad ? rad + (size_t)e * F::NS * Cin + cp : nullptr;
+  __nv_bfloat16* out = A + (size_t)e * R * Cin + cp;
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const int l = F::row_l(k);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = l * l; j < (l + 1) * (l + 1); ++j) acc += __ldg(re + k * S + j) * in[j];
+    if (rd) acc *= __ldg(rd + (size_t)F::slot(k) * Cin);
+    out[(size_t)k * Cin] = __float2bfloat16_rn(acc);
+  }
+}
+
+// Backward of gather_rotate, one thread per (edge, channel): u = rot . in (recomputed),
+// dU = dA * rad, dRAD[slot] = sum over the slot's rows of dA * u, d_in = rot^T dU.
+// d_in goes to DSRC[e] (channels of x[src]), DDST[e] (x[dst]) or DXE[e] (edge embedding).
+template <int L, int MM>
+__global__ void __launch_bounds__(128) gather_rotate_bwd_kernel(
+    const float* __restrict__ X, const float* __restrict__ XE, const long long* __restrict__ src,
+    const long long* __restrict__ dst, const float* __restrict__ rot, const float* __restrict__ rad,
+    const __nv_bfloat16* __restrict__ dA, float* __restrict__ DSRC, float* __restrict__ DDST,
+    float* __restrict__ DXE, float* __restrict__ DRAD, int E, int C, int Cin) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R;
+  const int e = blockIdx.x;
+  const int cp = blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= E || cp >= Cin) return;
+  float in[S];
+  if (rad) {
+    const float* base;
+    if (cp < C) base = X + (size_t)src[e] * S * C + cp;
+    else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
+    else base = XE + (size_t)e * S * C + (cp - 2 * C);
+#pragma unroll
+    for (int j = 0; j < S; ++j) in[j] = __ldg(base + (size_t)j * C);
+  }
+  const float* re = rot + (size_t)e * R * S;
+  const float* rd = rad ? rad + (size_t)e * F::NS * Cin + cp : nullptr;
+  const __nv_bfloat16* ga = dA + (size_t)e * R * Cin + cp;
+  float din[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) din[j] = 0.f;
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    if (!F::leads(k)) continue;
+    const int kp = F::pair(k);
+    const int l = F::row_l(k);
+    const float r = rd ? __ldg(rd + (size_t)F::slot(k) * Cin) : 1.f;
+    float dr = 0.f;
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (q == 1 && kp < 0) continue;
+      const int kk = q == 0 ? k : kp;
+      const float g = bf2f(ga[(size_t)kk * Cin]);
+      if (rd) {
+        float u = 0.f;
+#pragma unroll
+        for (int j = l * l; j < (l + 1) * (l + 1); ++j) u += __ldg(re + kk * S + j) * in[j];
+        dr += g * u;
+      }
+      const float du = g * r;
+#pragma unroll
+      for (int j = l * l; j < (l + 1) * (l + 1); ++j) din[j] += __ldg(re + kk * S + j) * du;
+    }
+    if (rd) DRAD[(size_t)e * F::NS * Cin + (size_t)F::slot(k) * Cin + cp] = dr;
+  }
+  float* o;
+  if (cp < C) o = DSRC + (size_t)e * S * C + cp;
+  else if (cp < 2 * C) o = DDST + (size_t)e * S * C + (cp - C);
+  else o = DXE + (size_t)e * S * C + (cp - 2 * C);
+#pragma unroll
+  for (int j = 0; j < S; ++j) o[(size_t)j * C] = din[j];
+}
+
+// DX[n] = sum_{e: dst=n} DDST[e] + sum_{e: src=n} DSRC[e], both in fixed (CSR) order.
+__global__ void node_reduce_kernel(const float* __restrict__ DDST, const long long* __restrict__ dst_ptr,
+                                   const float* __restrict__ DSRC, const long long* __restrict__ src_perm,
+                                   const long long* __restrict__ src_ptr, float* __restrict__ DX, int N, int SC) {
+  const int n = blockIdx.x;
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;
+  if (n >= N || i >= SC) return;
+  float s = 0.f;
+  for (long long e = dst_ptr[n]; e < dst_ptr[n + 1]; ++e) s += DDST[(size_t)e * SC + i];
+  if (DSRC)
+    for (long long q = src_ptr[n]; q < src_ptr[n + 1]; ++q) s += DSRC[(size_t)src_perm[q] * SC + i];
+  DX[(size_t)n * SC + i] = s;
+}
+
+// ---------------------------------------------------------------- rotate back
+// Node path: OUT[n, j, c] = scale * sum_{e: dst=n} sum_{k<Rk} rot[e,k,j] Y[e, koff + k*C + c] (+ BASE)
+template <int L, int MM>
+__global__ void __launch_bounds__(128) rotate_back_scatter_kernel(
+    const __nv_bfloat16* __restrict__ Y, int ldy, int koff, const float* __restrict__ rot,
+    const long long* __restrict__ dst_ptr, const float* __restrict__ base, float* __restrict__ out, int N, int C,
+    int Rk, float scale) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R;
+  const int n = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (n >= N || c >= C) return;
+  float acc[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) acc[j] = 0.f;
+#pragma unroll 1
+  for (long long e = dst_ptr[n]; e < dst_ptr[n + 1]; ++e) {
+    const float* re = rot + (size_t)e * R * S;
+    const __nv_bfloat16* ye = Y + (size_t)e * ldy + koff + c;
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (k >= Rk) break;
+      const int l = F::row_l(k);
+      const float y = bf2f(ye[(size_t)k * C]);
+#pragma unroll
+      for (int j = l * l; j < (l + 1) * (l + 1); ++j) acc[j] += __ldg(re + k * S + j) * y;
+    }
+  }
+  float* o = out + (size_t)n * S * C + c;
+  const float* b = base ? base + (size_t)n * S * C + c : nullptr;
+#pragma unroll
+  for (int j = 0; j < S; ++j) o[(size_t)j * C] = acc[j] * scale + (b ? b[(size_t)j * C] : 0.f);
+}
+
+// Edge path: OUT[e, j, c] = sum_{k<Rk} rot[e,k,j] Y[e, koff + k*C + c]
+template <int L, int MM>
+__global__ void __launch_bounds__(128) rotate_back_edge_kernel(const __nv_bfloat16* __restrict__ Y, int ldy, int koff,
+                                                               const float* __restrict__ rot, float* __restrict__ out,
+                                                               int E, int C, int Rk) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R;
+  const int e = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= E || c >= C) return;
+  float acc[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) acc[j] = 0.f;
+  const float* re = rot + (size_t)e * R * S;
+  const __nv_bfloat16* ye = Y + (size_t)e * ldy + koff + c;
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    if (k >= Rk) break;
+    const int l = F::row_l(k);
+    const float y = bf2f(ye[(size_t)k * C]);
+#pragma unroll
+    for (int j = l * l; j < (l + 1) * (l + 1); ++j) acc[j] += __ldg(re + k * S + j) * y;
+  }
+  float* o = out + (size_t)e * S * C + c;
+#pragma unroll
+  for (int j = 0; j < S; ++j) o[(size_t)j * C] = acc[j];
+}
+
+// Backward of both rotate-back kernels: DY[e, k*C + c] = scale * sum_j rot[e,k,j] G[row(e), j, c],
+// row(e) = dst[e] (node path) or e (edge path); bf16 (DY) and/or fp32 (DYf) output.
+template <int L, int MM>
+__global__ void __launch_bounds__(128) rotate_grad_kernel(const float* __restrict__ G,
+                                                          const long long* __restrict__ rows,
+                                                          const float* __restrict__ rot, __nv_bfloat16* __restrict__ DY,
+                                                          float* __restrict__ DYf, int E, int C, int Rk, float scale) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R;
+  const int e = blockIdx.x;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= E || c >= C) return;
+  const long long r = rows ? rows[e] : e;
+  float g[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) g[j] = __ldg(G + ((size_t)r * S + j) * C + c);
+  const float* re = rot + (size_t)e * R * S;
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    if (k >= Rk) break;
+    const int l = F::row_l(k);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = l * l; j < (l + 1) * (l + 1); ++j) acc += __ldg(re + k * S + j) * g[j];
+    acc *= scale;
+    if (DY) DY[((size_t)e * Rk + k) * C + c] = __float2bfloat16_rn(acc);
+    if (DYf) DYf[((size_t)e * Rk + k) * C + c] = acc;
+  }
+}
+
+// ---------------------------------------------------------------- gate (m-major)
+// Y1 [E, G + R*H] with G = L*H gate pre-activations; H1 [E, R*H]:
+// H1[e,0,h] = silu(Y1[e, G+h]); H1[e,k,h] = Y1[e, G+k*H+h] * tanh(Y1[e, (l_k-1)*H + h])
+template <int L, int MM>
+__global__ void gate_fwd_kernel(const __nv_bfloat16* __restrict__ Y1, __nv_bfloat16* __restrict__ H1, int E, int H) {
+  using F = Frame<L, MM>;
+  constexpr int R = F::R;
+  const int e = blockIdx.x;
+  const int h = blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= E || h >= H) return;
+  const int G = L * H;
+  const __nv_bfloat16* y = Y1 + (size_t)e * (G + R * H) + h;
+  __nv_bfloat16* o = H1 + (size_t)e * R * H + h;
+  float t[L];
+#pragma unroll
+  for (int l = 1; l <= L; ++l) t[l - 1] = tanhf(bf2f(y[(size_t)(l - 1) * H]));
+  o[0] = __float2bfloat16_rn(silu(bf2f(y[G])));
+#pragma unroll
+  for (int k = 1; k < R; ++k) o[(size_t)k * H] = __float2bfloat16_rn(bf2f(y[G + (size_t)k * H]) * t[F::row_l(k) - 1]);
+}
+
+template <int L, int MM>
+__global__ void gate_bwd_kernel(const __nv_bfloat16* __restrict__ Y1, const __nv_bfloat16* __restrict__ dH1,
+                                __nv_bfloat16* __restrict__ dY1, int E, int H) {
+  using F = Frame<L, MM>;
+  constexpr int R = F::R;
+  const int e = blockIdx.x;
+  const int h = blockIdx.y * blockDim.x + threadIdx.x;
+  if (e >= E || h >= H) return;
+  const int G = L * H;
+  const __nv_bfloat16* y = Y1 + (size_t)e * (G + R * H) + h;
+  const __nv_bfloat16* dh = dH1 + (size_t)e * R * H + h;
+  __nv_bfloat16* dy = dY1 + (size_t)e * (G + R * H) + h;
+  float t[L], dg[L];
+#pragma unroll
+  for (int l = 1; l <= L; ++l) {
+    t[l - 1] = tanhf(bf2f(y[(size_t)(l - 1) * H]));
+    dg[l - 1] = 0.f;
+  }
+  dy[G] = __float2bfloat16_rn(bf2f(dh[0]) * dsilu(bf2f(y[G])));
+#pragma unroll
+  for (int k = 1; k < R; ++k) {
+    const int l = F::row_l(k);
+    const float d = bf2f(dh[(size_t)k * H]);
+    dy[G + (size_t)k * H] = __float2bfloat16_rn(d * t[l - 1]);
+    dg[l - 1] += d * bf2f(y[G + (size_t)k * H]);
+  }
+#pragma unroll
+  for (int l = 1; l <= L; ++l) dy[(size_t)(l - 1) * H] = __float2bfloat16_rn(dg[l - 1] * (1.f - t[l - 1] * t[l - 1]));
+}
+
+}  // namespace maloq
+
+// ======================================================================= host launchers
+namespace maloq {
+
+static const char* last_error() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+// Instantiated frames: lmax 1..6 with mmax in {1, 2, lmax}.
+#define MALOQ_FRAME_CASE(L_, M_, ...) \
+  if (L == L_ && MM == M_) {          \
+    constexpr int FL = L_, FM = M_;   \
+    __VA_ARGS__;                      \
+    return last_error();              \
+  }
+#define MALOQ_DISPATCH_FRAME(...)                                                                               \
+  MALOQ_FRAME_CASE(1, 1, __VA_ARGS__)                                                                           \
+  MALOQ_FRAME_CASE(2, 1, __VA_ARGS__) MALOQ_FRAME_CASE(2, 2, __VA_ARGS__)                                       \
+  MALOQ_FRAME_CASE(3, 1, __VA_ARGS__) MALOQ_FRAME_CASE(3, 2, __VA_ARGS__) MALOQ_FRAME_CASE(3, 3, __VA_ARGS__)   \
+  MALOQ_FRAME_CASE(4, 1, __VA_ARGS__) MALOQ_FRAME_CASE(4, 2, __VA_ARGS__) MALOQ_FRAME_CASE(4, 4, __VA_ARGS__)   \
+  MALOQ_FRAME_CASE(5, 1, __VA_ARGS__) MALOQ_FRAME_CASE(5, 2, __VA_ARGS__) MALOQ_FRAME_CASE(5, 5, __VA_ARGS__)   \
+  MALOQ_FRAME_CASE(6, 1, __VA_ARGS__) MALOQ_FRAME_CASE(6, 2, __VA_ARGS__) MALOQ_FRAME_CASE(6, 6, __VA_ARGS__)   \
+  return "edge kernels: (lmax, mmax) frame not instantiated (lmax 1..6, mmax in {1, 2, lmax})";
+
+static inline int clampm(int L, int MM) { return MM > L ? L : MM; }
+
+const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
+                                   const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
+                                   int C, int Cin, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (E == 0) return nullptr;
+  dim3 grid(E, (Cin + 127) / 128);
+  MALOQ_DISPATCH_FRAME((gather_rotate_fwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, A, E, C, Cin)))
+}
+
+const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const long long* src,
+                                   const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
+                                   float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
+                                   cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (E == 0) return nullptr;
+  dim3 grid(E, (Cin + 127) / 128);
+  MALOQ_DISPATCH_FRAME((gather_rotate_bwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, dA, DSRC,
+                                                                                DDST, DXE, DRAD, E, C, Cin)))
+}
+
+const char* edge_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,
+                             const long long* src_ptr, float* DX, int N, int SC, cudaStream_t st) {
+  if (N == 0) return nullptr;
+  dim3 grid(N, (SC + 255) / 256);
+  node_reduce_kernel<<<grid, 256, 0, st>>>(DDST, dst_ptr, DSRC, src_perm, src_ptr, DX, N, SC);
+  return last_error();
+}
+
+const char* edge_rotate_back_scatter(int L, int MM, const __nv_bfloat16* Y, int ldy, int koff, const float* rot,
+                                     const long long* dst_ptr, const float* base, float* out, int N, int C, int Rk,
+                                     float scale, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (N == 0) return nullptr;
+  dim3 grid(N, (C + 127) / 128);
+  MALOQ_DISPATCH_FRAME((rotate_back_scatter_kernel<FL, FM><<<grid, 128, 0, st>>>(Y, ldy, koff, rot, dst_ptr, base,
+                                                                                  out, N, C, Rk, scale)))
+}
+
+const char* edge_rotate_back(int L, int MM, const __nv_bfloat16* Y, int ldy, int koff, const float* rot, float* out,
+                             int E, int C, int Rk, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (E == 0) return nullptr;
+  dim3 grid(E, (C + 127) / 128);
+  MALOQ_DISPATCH_FRAME((rotate_back_edge_kernel<FL, FM><<<grid, 128, 0, st>>>(Y, ldy, koff, rot, out, E, C, Rk)))
+}
+
+const char* edge_rotate_grad(int L, int MM, const float* G, const long long* rows, const float* rot,
+                             __nv_bfloat16* DY, float* DYf, int E, int C, int Rk, float scale, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (E == 0) return nullptr;
+  dim3 grid(E, (C + 127) / 128);
+  MALOQ_DISPATCH_FRAME((rotate_grad_kernel<FL, FM><<<grid, 128, 0, st>>>(G, rows, rot, DY, DYf, E, C, Rk, scale)))
+}
+
+const char* edge_gate_fwd(int L, int MM, const __nv_bfloat16* Y1, __nv_bfloat16* H1, int E, int H, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (E == 0) return nullptr;
+  dim3 grid(E, (H + 127) / 128);
+  MALOQ_DISPATCH_FRAME((gate_fwd_kernel<FL, FM><<<grid, 128, 0, st>>>(Y1, H1, E, H)))
+}
+
+const char* edge_gate_bwd(int L, int MM, const __nv_bfloat16* Y1, const __nv_bfloat16* dH1, __nv_bfloat16* dY1, int E,
+                          int H, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (E == 0) return nullptr;
+  dim3 grid(E, (H + 127) / 128);
+  MALOQ_DISPATCH_FRAME((gate_bwd_kernel<FL, FM><<<grid, 128, 0, st>>>(Y1, dH1, dY1, E, H)))
+}
+
+}  // namespace maloq

@@ -1,0 +1,28 @@
+// Host API of the edge-frame kernels (edge.cu).  Plain CUDA types.  L = lmax, MM = mmax.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace maloq {
+
+const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
+                                   const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
+                                   int C, int Cin, cudaStream_t st);
+const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const long long* src,
+                                   const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
+                                   float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
+                                   cudaStream_t st);
+const char* edge_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,
+                             const long long* src_ptr, float* DX, int N, int SC, cudaStream_t st);
+const char* edge_rotate_back_scatter(int L, int MM, const __nv_bfloat16* Y, int ldy, int koff, const float* rot,
+                                     const long long* dst_ptr, const float* base, float* out, int N, int C, int Rk,
+                                     float scale, cudaStream_t st);
+const char* edge_rotate_back(int L, int MM, const __nv_bfloat16* Y, int ldy, int koff, const float* rot, float* out,
+                             int E, int C, int Rk, cudaStream_t st);
+const char* edge_rotate_grad(int L, int MM, const float* G, const long long* rows, const float* rot,
+                             __nv_bfloat16* DY, float* DYf, int E, int C, int Rk, float scale, cudaStream_t st);
+const char* edge_gate_fwd(int L, int MM, const __nv_bfloat16* Y1, __nv_bfloat16* H1, int E, int H, cudaStream_t st);
+const char* edge_gate_bwd(int L, int MM, const __nv_bfloat16* Y1, const __nv_bfloat16* dH1, __nv_bfloat16* dY1, int E,
+                          int H, cudaStream_t st);
+
+}  // namespace maloq

@@ -3,7 +3,7 @@
 //   C[p] (M x N) = alpha * A[p] (M x K) * B[p]^T (K x N) (+ bias[N]) (act)
 //
 // A and B are bf16 and either K-major (row-major [M,K] / [N,K]) or MN-major (row-major
-// [K,M] / [K,N], used for weight gradients where K is the edge dimension).  Up to four
+// [K,M] / [K,N], used for weight gradients where K is the edge dimension).  Up to eight
 // problems run in one launch (the per-|m| SO(2) GEMMs of a layer).  Optional split-K
 // writes fp32 partials [split][M][N]; gemm_splitk_reduce sums them in a fixed order, so
 // weight gradients are deterministic.
@@ -40,7 +40,7 @@ struct alignas(64) GemmProblemDev {
 };
 
 struct GemmParamsDev {
-  GemmProblemDev p[4];
+  GemmProblemDev p[8];
   int nprob;
   int out_fp32;
   int act;
@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(128, 1) gemm_tc_kernel(const __grid_constant__
       if (full_chunk) {
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
-          __nv_bfloat162 h[4];
+          __nv_bfloat162 h[8];
 #pragma unroll
           for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j + 2 * q], v[j + 2 * q + 1]);
           *reinterpret_cast<uint4*>(o + j) = *reinterpret_cast<uint4*>(h);
@@ -266,7 +266,7 @@ static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaS
 
 const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_mn, bool out_fp32, int act,
                         float alpha, int splits, int bn, cudaStream_t stream) {
-  if (nprob < 1 || nprob > 4) return "gemm: 1..4 problems per launch";
+  if (nprob < 1 || nprob > 8) return "gemm: 1..8 problems per launch";
   if (bn != 64 && bn != 128 && bn != 256) return "gemm: bn must be 64, 128 or 256";
   if (a_mn != b_mn) return "gemm: mixed operand majors are not instantiated";
   if (splits < 1) return "gemm: splits must be >= 1";

@@ -16,7 +16,7 @@ struct GemmProblem {
   int M, N, K;
 };
 
-// Launch up to four problems in one kernel.  Returns an error string or nullptr.
+// Launch up to eight problems in one kernel.  Returns an error string or nullptr.
 const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_mn, bool out_fp32, int act,
                         float alpha, int splits, int bn, cudaStream_t stream);
 

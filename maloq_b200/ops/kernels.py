@@ -112,8 +112,7 @@ def linear(x, weight, bias=None, act=None):
 # ------------------------------------------------------------------ ops still on PyTorch glue
 # These run PyTorch on the CUDA tensors until their fused kernels land; each is listed so the
 # set of non-kernel ops is explicit.
-TORCH_GLUE = ("layernorm_silu", "so3_linear", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
-              "rotate_back_m0_scatter", "rotate_back_m0", "fock_head_process", "gather_scale",
+TORCH_GLUE = ("layernorm_silu", "gate", "rms_norm_sh", "edge_rotation", "fock_head_process", "gather_scale",
               "matrix_to_labels", "labels_to_matrix", "basis_transform", "fock_loss")
 
 
@@ -166,21 +165,9 @@ def _head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):
 
 @register("edgewise")
 def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
-    """Edgewise with the SO(2) GEMMs, radial MLP and atomwise linears on tcgen05; gather /
-    rotation / scatter glue on PyTorch until the fused edge kernels land."""
-    c1, c2 = mod.so2_conv_1, mod.so2_conv_2
-    rad = c1.rad_func(x_edge)
-    src = x_node.index_select(0, graph.src) if graph.halo is None else graph.halo.gather_source(x_node, graph)
-    msg = _ref.gather_message(x_node, src, graph.dst, x_msg_edge)
-    msg = torch.bmm(graph.rot, msg)
-    h, g = _so2_conv(msg, rad, c1.gemm_weights(), c1.fc_m0.bias, c1.m_size, c1.extra_m0_output_channels,
-                     c1.m_output_channels)
-    h = _ref.gate(g, h, mod.act.expand_index, mod.lmax)
-    y, _ = _so2_conv(h, None, c2.gemm_weights(), c2.fc_m0.bias, c2.m_size, 0, c2.m_output_channels)
-    y = _ref.rotate_back(y, graph.rot)
-    if node_or_edge == "node":
-        return _ref.scatter_sum(y, graph.dst, graph.num_nodes)
-    return y
+    from . import edge_native
+
+    return edge_native.edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge)
 
 
 def _so2_conv(x, rad, weights, bias0, m_size, extra, cout):
@@ -205,13 +192,18 @@ def _so2_conv(x, rad, weights, bias0, m_size, extra, cout):
     return torch.cat(outs, dim=1), g
 
 
-register("rotate_back_m0")(lambda e, graph: _ref.rotate_back_m0(e, graph.rot))
+@register("rotate_back_m0")
+def rotate_back_m0(e, graph):
+    from . import edge_native
+
+    return edge_native.rotate_back_m0(e, graph)
 
 
 @register("rotate_back_m0_scatter")
 def rotate_back_m0_scatter(e, graph, x_node, scale):
-    y = _ref.rotate_back_m0(e, graph.rot)
-    return x_node + _ref.scatter_sum(y * scale, graph.dst, graph.num_nodes).to(x_node.dtype)
+    from . import edge_native
+
+    return edge_native.rotate_back_m0(e, graph, base=x_node, scale=scale)
 
 
 @register("fock_loss")
