@@ -5,3 +5,4 @@
 #include "gemm.cu"
 #include "noalloc.cu"
 #include "edge.cu"
+#include "norm.cu"

@@ -6,6 +6,7 @@
 
 #include "edge.h"
 #include "gemm.h"
+#include "norm.h"
 #include "runtime.h"
 
 namespace {
@@ -42,7 +43,7 @@ void gemm(std::vector<at::Tensor> As, std::vector<at::Tensor> Bs, std::vector<at
     g.K = (int)(mn_major ? A.size(0) : A.size(1));
     g.N = (int)(mn_major ? B.size(1) : B.size(0));
     TORCH_CHECK((mn_major ? B.size(0) : B.size(1)) == g.K, "gemm: K mismatch");
-    if (splits > 1) {
+    if (splits > 1 || C.dim() == 3) {
       TORCH_CHECK(C.dim() == 3 && out_fp32 && C.size(0) == splits && C.size(1) == g.M && C.size(2) == g.N,
                   "gemm: split-K output must be fp32 [splits, M, N]");
       g.ldc = C.stride(1);
@@ -172,6 +173,68 @@ void gate_bwd(int64_t L, int64_t MM, at::Tensor Y1, at::Tensor dH1, at::Tensor d
   check(maloq::edge_gate_bwd((int)L, (int)MM, bf(Y1), bf(dH1), bf(dY1), (int)Y1.size(0), (int)H, stream()));
 }
 
+
+void rms_norm_fwd(int64_t L, at::Tensor X, c10::optional<at::Tensor> RES, at::Tensor aw, at::Tensor ab,
+                  at::Tensor OUT, c10::optional<at::Tensor> SUM, double eps) {
+  chk(X, at::kFloat, "X");
+  chk(OUT, at::kFloat, "OUT");
+  chk(aw, at::kFloat, "affine_weight");
+  chk(ab, at::kFloat, "affine_bias");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::rms_norm_fwd((int)L, X.data_ptr<float>(), ptr<float>(RES), aw.data_ptr<float>(), ab.data_ptr<float>(),
+                            OUT.data_ptr<float>(), ptr<float>(SUM), (int)X.size(0), (int)X.size(2), (float)eps,
+                            stream()));
+}
+
+void rms_norm_bwd(int64_t L, at::Tensor Sx, at::Tensor G, c10::optional<at::Tensor> GS, at::Tensor aw, at::Tensor DX,
+                  at::Tensor PART, double eps) {
+  chk(Sx, at::kFloat, "S");
+  chk(G, at::kFloat, "G");
+  chk(DX, at::kFloat, "DX");
+  chk(PART, at::kFloat, "PART");
+  const at::cuda::CUDAGuard guard(Sx.device());
+  check(maloq::rms_norm_bwd((int)L, Sx.data_ptr<float>(), G.data_ptr<float>(), ptr<float>(GS), aw.data_ptr<float>(),
+                            DX.data_ptr<float>(), PART.data_ptr<float>(), (int)Sx.size(0), (int)Sx.size(2), (float)eps,
+                            (int)PART.size(0), stream()));
+}
+
+int64_t norm_grid(int64_t rows) { return maloq::norm_grid(rows); }
+
+void ln_silu_fwd(at::Tensor X, at::Tensor w, at::Tensor b, at::Tensor OUT, double eps) {
+  chk(X, at::kFloat, "X");
+  chk(OUT, at::kBFloat16, "OUT");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::ln_silu_fwd(X.data_ptr<float>(), w.data_ptr<float>(), b.data_ptr<float>(), bf(OUT), (int)X.size(0),
+                           (int)X.size(1), (float)eps, stream()));
+}
+
+void ln_silu_bwd(at::Tensor X, at::Tensor w, at::Tensor b, at::Tensor G, at::Tensor DX, at::Tensor PART, double eps) {
+  chk(X, at::kFloat, "X");
+  chk(G, at::kBFloat16, "G");
+  chk(DX, at::kFloat, "DX");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::ln_silu_bwd(X.data_ptr<float>(), w.data_ptr<float>(), b.data_ptr<float>(), bf(G), DX.data_ptr<float>(),
+                           PART.data_ptr<float>(), (int)X.size(0), (int)X.size(1), (float)eps,
+                           (int)(PART.size(0) / 8), stream()));
+}
+
+void gate_l_fwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor OUT) {
+  chk(X, at::kFloat, "X");
+  chk(Gt, at::kFloat, "gates");
+  chk(OUT, at::kFloat, "OUT");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::gate_l_fwd((int)L, X.data_ptr<float>(), Gt.data_ptr<float>(), OUT.data_ptr<float>(), (int)X.size(0),
+                          (int)X.size(2), stream()));
+}
+
+void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tensor DX, at::Tensor DG) {
+  chk(X, at::kFloat, "X");
+  chk(DO, at::kFloat, "DO");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::gate_l_bwd((int)L, X.data_ptr<float>(), Gt.data_ptr<float>(), DO.data_ptr<float>(), DX.data_ptr<float>(),
+                          DG.data_ptr<float>(), (int)X.size(0), (int)X.size(2), stream()));
+}
+
 int64_t error_status(bool clear) { return maloq::error_status(clear); }
 
 }  // namespace
@@ -187,5 +250,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gate_fwd", &gate_fwd);
   m.def("gate_bwd", &gate_bwd);
   m.def("node_reduce", &node_reduce);
+  m.def("rms_norm_fwd", &rms_norm_fwd);
+  m.def("rms_norm_bwd", &rms_norm_bwd);
+  m.def("norm_grid", &norm_grid);
+  m.def("ln_silu_fwd", &ln_silu_fwd);
+  m.def("ln_silu_bwd", &ln_silu_bwd);
+  m.def("gate_l_fwd", &gate_l_fwd);
+  m.def("gate_l_bwd", &gate_l_bwd);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
 }

@@ -1,0 +1,23 @@
+// Host API of norm.cu.  Plain CUDA types.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace maloq {
+
+int norm_grid(long long rows);
+const char* rms_norm_fwd(int L, const float* X, const float* RES, const float* aw, const float* ab, float* OUT,
+                         float* SUM, int B, int C, float eps, cudaStream_t st);
+// PART: [grid, L+2, C] partial (d_affine_weight, d_affine_bias) per CTA
+const char* rms_norm_bwd(int L, const float* Sx, const float* G, const float* GS, const float* aw, float* DX,
+                         float* PART, int B, int C, float eps, int grid, cudaStream_t st);
+const char* ln_silu_fwd(const float* X, const float* w, const float* b, __nv_bfloat16* OUT, int M, int W, float eps,
+                        cudaStream_t st);
+// PART: [grid * 8, 2, W] partial (d_weight, d_bias) per warp (256-thread CTAs)
+const char* ln_silu_bwd(const float* X, const float* w, const float* b, const __nv_bfloat16* G, float* DX, float* PART,
+                        int M, int W, float eps, int grid, cudaStream_t st);
+const char* gate_l_fwd(int L, const float* X, const float* Gt, float* OUT, int B, int H, cudaStream_t st);
+const char* gate_l_bwd(int L, const float* X, const float* Gt, const float* DO, float* DX, float* DG, int B, int H,
+                       cudaStream_t st);
+
+}  // namespace maloq

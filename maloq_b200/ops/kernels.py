@@ -112,35 +112,42 @@ def linear(x, weight, bias=None, act=None):
 # ------------------------------------------------------------------ ops still on PyTorch glue
 # These run PyTorch on the CUDA tensors until their fused kernels land; each is listed so the
 # set of non-kernel ops is explicit.
-TORCH_GLUE = ("layernorm_silu", "gate", "rms_norm_sh", "edge_rotation", "fock_head_process", "gather_scale",
+TORCH_GLUE = ("edge_rotation", "fock_head_process", "gather_scale",
               "matrix_to_labels", "labels_to_matrix", "basis_transform", "fock_loss")
 
 
-register("layernorm_silu")(lambda x, w, b, eps: _ref.layernorm_silu(x, w, b, eps))
-register("gate")(_ref.gate)
-register("rms_norm_sh")(lambda x, aw, ab, eps, residual=None: _ref.rms_norm_sh(
-    x, aw, ab, _balance(aw.shape[0] - 1, x.device), eps, residual))
+@register("layernorm_silu")
+def layernorm_silu(x, w, b, eps):
+    from . import norm_native
+
+    return norm_native.layernorm_silu(x, w, b, eps)
+
+
+@register("gate")
+def gate(gating_scalars, x, expand_index, lmax):
+    from . import norm_native
+
+    return norm_native.gate_l(gating_scalars, x, lmax)
+
+
+@register("rms_norm_sh")
+def rms_norm_sh(x, aw, ab, eps, residual=None):
+    from . import norm_native
+
+    return norm_native.rms_norm_sh(x, aw, ab, eps, residual)
+
+
 register("edge_rotation")(_ref.edge_rotation)
 register("gather_scale")(_ref.gather_scale)
 register("fock_head_process")(lambda x, ws, bs, lp, act, sc, ab: _head_process(x, ws, bs, lp, act, sc, ab))
 register("basis_transform")(lambda x, W: torch.matmul(x, W))
 
 
-def _balance(lmax, device):
-    bw = torch.zeros((lmax + 1) ** 2, 1, device=device)
-    for l in range(lmax + 1):
-        bw[l * l: l * l + 2 * l + 1] = 1.0 / (2 * l + 1)
-    return bw / (lmax + 1)
-
-
 @register("so3_linear")
 def so3_linear(x, weight, bias, lmax):
-    """Per-degree GEMMs: rows of degree l use W[l] (x: [B, (L+1)^2, C])."""
-    outs = []
-    for l in range(lmax + 1):
-        xl = x[:, l * l:(l + 1) ** 2]
-        outs.append(linear(xl, weight[l], bias if l == 0 else None))
-    return torch.cat(outs, dim=1)
+    from . import norm_native
+
+    return norm_native.so3_linear(x, weight, bias, lmax)
 
 
 def _head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):

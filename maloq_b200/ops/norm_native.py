@@ -1,0 +1,184 @@
+"""Autograd wrappers of the norm / gate kernels and the per-degree (SO3) linear.
+
+* :func:`rms_norm_sh` - equivariant RMS norm, optionally fused with the residual add;
+* :func:`layernorm_silu` - silu(LayerNorm(x)) with a bf16 output (the next GEMM's operand);
+* :func:`gate_l` - l-outer gate of the atomwise block;
+* :func:`so3_linear` - per-degree channel mixing as tcgen05 GEMM problems, one per
+  coefficient (strided views of the [B, S, C] layout, no copies), weight gradients as
+  deterministic split-K GEMMs summed per degree.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .native import count_launches
+
+
+def _lib():
+    from .kernels import lib
+
+    return lib()
+
+
+def _partial_grid(rows):
+    return max(1, min(int(rows), 148 * 4))
+
+
+class _RmsNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, res, aw, ab, eps):
+        lib = _lib()
+        L = aw.shape[0] - 1
+        x = x.contiguous().float()
+        res_c = res.contiguous().float() if res is not None else None
+        out = torch.empty_like(x)
+        s = torch.empty_like(x) if res is not None else None
+        lib.rms_norm_fwd(L, x, res_c, aw.contiguous(), ab.contiguous(), out, s, eps)
+        count_launches(1)
+        ctx.save_for_backward(s if s is not None else x, aw)
+        ctx.eps, ctx.has_res = eps, res is not None
+        if res is not None:
+            return out, s
+        return out
+
+    @staticmethod
+    def backward(ctx, g_out, g_s=None):
+        lib = _lib()
+        s, aw = ctx.saved_tensors
+        L = aw.shape[0] - 1
+        B, S, C = s.shape
+        grid = _partial_grid(B)
+        dx = torch.empty_like(s)
+        part = torch.empty(grid, L + 2, C, device=s.device, dtype=torch.float32)
+        gs = g_s.contiguous().float() if (ctx.has_res and g_s is not None) else None
+        if g_out is None:
+            g_out = torch.zeros_like(s)
+        lib.rms_norm_bwd(L, s, g_out.contiguous().float(), gs, aw.contiguous(), dx, part, ctx.eps)
+        count_launches(1)
+        p = part.sum(0)
+        daw, dab = p[: L + 1], p[L + 1]
+        if ctx.has_res:
+            return dx, dx, daw, dab, None
+        return dx, None, daw, dab, None
+
+
+def rms_norm_sh(x, aw, ab, eps, residual=None):
+    if residual is None:
+        return _RmsNorm.apply(x, None, aw, ab, eps)
+    return _RmsNorm.apply(x, residual, aw, ab, eps)
+
+
+class _LnSilu(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, eps):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous().float()
+        out = torch.empty(x2.shape, device=x.device, dtype=torch.bfloat16)
+        _lib().ln_silu_fwd(x2, w.contiguous(), b.contiguous(), out, eps)
+        count_launches(1)
+        ctx.save_for_backward(x2, w, b)
+        ctx.eps, ctx.shape = eps, shape
+        return out.view(shape)
+
+    @staticmethod
+    def backward(ctx, g):
+        x2, w, b = ctx.saved_tensors
+        M, W = x2.shape
+        grid = max(1, min((M + 7) // 8, 148 * 4))
+        dx = torch.empty_like(x2)
+        part = torch.empty(grid * 8, 2, W, device=x2.device, dtype=torch.float32)
+        _lib().ln_silu_bwd(x2, w.contiguous(), b.contiguous(), g.reshape(M, W).to(torch.bfloat16).contiguous(), dx,
+                           part, ctx.eps)
+        count_launches(1)
+        p = part.sum(0)
+        return dx.view(ctx.shape), p[0], p[1], None
+
+
+def layernorm_silu(x, w, b, eps=1e-5):
+    return _LnSilu.apply(x, w, b, eps)
+
+
+class _GateL(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gates, x, lmax):
+        x = x.contiguous().float()
+        gates = gates.contiguous().float()
+        out = torch.empty_like(x)
+        _lib().gate_l_fwd(lmax, x, gates, out)
+        count_launches(1)
+        ctx.save_for_backward(x, gates)
+        ctx.lmax = lmax
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, gates = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        dg = torch.empty_like(gates)
+        _lib().gate_l_bwd(ctx.lmax, x, gates, g.contiguous().float(), dx, dg)
+        count_launches(1)
+        return dg, dx, None
+
+
+def gate_l(gates, x, lmax):
+    return _GateL.apply(gates, x, lmax)
+
+
+def _coef_l(S):
+    out = []
+    l = 0
+    for j in range(S):
+        while (l + 1) * (l + 1) <= j:
+            l += 1
+        out.append(l)
+    return out
+
+
+def _run_problems(As, Ws, Cs, biases, mn=False, splits=1):
+    lib = _lib()
+    for i in range(0, len(As), 8):
+        lib.gemm(As[i:i + 8], Ws[i:i + 8], Cs[i:i + 8], biases[i:i + 8], mn, 0, 1.0, splits, 128)
+        count_launches(1)
+
+
+class _SO3Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        B, S, C = x.shape
+        Co = weight.shape[1]
+        xb = x.to(torch.bfloat16).contiguous().view(B, S * C)
+        wb = weight.to(torch.bfloat16).contiguous()
+        out = torch.empty(B, S * Co, device=x.device, dtype=torch.float32)
+        ls = _coef_l(S)
+        _run_problems([xb[:, j * C:(j + 1) * C] for j in range(S)], [wb[ls[j]] for j in range(S)],
+                      [out[:, j * Co:(j + 1) * Co] for j in range(S)],
+                      [bias.float().contiguous()] + [None] * (S - 1))
+        ctx.save_for_backward(xb, wb)
+        ctx.dims = (B, S, C, Co)
+        ctx.in_dtype = x.dtype
+        return out.view(B, S, Co)
+
+    @staticmethod
+    def backward(ctx, g):
+        xb, wb = ctx.saved_tensors
+        B, S, C, Co = ctx.dims
+        ls = _coef_l(S)
+        L = ls[-1]
+        gb = g.to(torch.bfloat16).contiguous().view(B, S * Co)
+        dx = torch.empty(B, S * C, device=g.device, dtype=torch.float32)
+        wt = [wb[l].t().contiguous() for l in range(L + 1)]
+        _run_problems([gb[:, j * Co:(j + 1) * Co] for j in range(S)], [wt[ls[j]] for j in range(S)],
+                      [dx[:, j * C:(j + 1) * C] for j in range(S)], [None] * S)
+        splits = max(1, min(-(-296 // S), B // 2048, 16))
+        part = torch.empty(S, splits, Co, C, device=g.device, dtype=torch.float32)
+        _run_problems([gb[:, j * Co:(j + 1) * Co] for j in range(S)], [xb[:, j * C:(j + 1) * C] for j in range(S)],
+                      [part[j] for j in range(S)], [None] * S, mn=True, splits=splits)
+        part = part.sum(1)
+        dw = torch.stack([part[l * l:(l + 1) * (l + 1)].sum(0) for l in range(L + 1)])
+        db = g[:, 0].float().sum(0)
+        return dx.view(B, S, C).to(ctx.in_dtype), dw, db
+
+
+def so3_linear(x, weight, bias, lmax):
+    return _SO3Linear.apply(x, weight, bias)
