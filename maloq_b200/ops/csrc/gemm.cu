@@ -8,11 +8,13 @@
 // writes fp32 partials [split][M][N]; gemm_splitk_reduce sums them in a fixed order, so
 // weight gradients are deterministic.
 //
-// CTA = 128 threads, tile 128 x BN x 64, STAGES-deep TMA ring:
+// Persistent CTAs (one per SM) walk a static schedule of 128 x BN output tiles; K in steps of
+// 64 through a STAGES-deep TMA ring:
 //   warp 0 (one elected lane): TMA producer        - waits "empty", loads the A/B tiles
 //   warp 1 (one elected lane): tcgen05.mma issuer  - waits "full", 4 MMAs (K=16), commits "empty"
-//   all 4 warps: epilogue - tcgen05.ld of TMEM lanes 32w..32w+31, bias/activation, store.
-// Accumulators live in TMEM (BN fp32 columns x 128 lanes).  TMA loads use no multicast.
+//   warps 2-5: epilogue - tcgen05.ld of TMEM lanes 32*(w%4).., bias/activation, store.
+// Two TMEM accumulators (2 x BN fp32 columns) let a tile's epilogue overlap the next tile's
+// MMAs.  TMA loads use no multicast.
 #include <cstdio>
 #include <cstring>
 #include <stdexcept>
@@ -29,6 +31,7 @@ constexpr int BK = 64;
 struct alignas(64) GemmProblemDev {
   CUtensorMap ta;
   CUtensorMap tb;
+  CUtensorMap tc;  // output, 3-D {N, M, splits}, box {32, 32, 1}, swizzled
   void* c;
   const float* bias;
   long long ldc;
@@ -47,156 +50,216 @@ struct GemmParamsDev {
   float alpha;
 };
 
+// Decode a linear work index into (problem, m0, n0, split).
+struct TileCoord {
+  int pi, m0, n0, split;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const GemmParamsDev& P, int w, int tiles_per_split, int BN) {
+  TileCoord tc;
+  tc.split = w / tiles_per_split;
+  int t = w - tc.split * tiles_per_split;
+  int pi = 0;
+#pragma unroll 1
+  for (int q = 1; q < P.nprob; ++q)
+    if (t >= P.p[q].tile_begin) pi = q;
+  t -= P.p[pi].tile_begin;
+  tc.pi = pi;
+  tc.m0 = (t / P.p[pi].tiles_n) * BM;
+  tc.n0 = (t % P.p[pi].tiles_n) * BN;
+  return tc;
+}
+
+// Persistent warp-specialised kernel: 6 warps.
+//   warp 0: TMA producer (one lane); warp 1: MMA issuer (one lane);
+//   warps 2-5: epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+// Two TMEM accumulators (2*BN columns): the epilogue of work item i overlaps the MMAs of i+1.
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(128, 1) gemm_tc_kernel(const __grid_constant__ GemmParamsDev P) {
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ GemmParamsDev P, int total_work,
+                                                         int tiles_per_split) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* acc_full = empty + STAGES;  // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (4 arrivals: one per epilogue warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  // epilogue staging: 4 warps x 2 buffers x 32 x 32 x 4 bytes, 1024-aligned
+  uint8_t* stage_out = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
-  int t = blockIdx.x, pi = 0;
-#pragma unroll 1
-  for (int q = 1; q < P.nprob; ++q)
-    if (t >= P.p[q].tile_begin) pi = q;
-  const GemmProblemDev& pr = P.p[pi];
-  t -= pr.tile_begin;
-  const int m0 = (t / pr.tiles_n) * BM;
-  const int n0 = (t % pr.tiles_n) * BN;
-  const int split = blockIdx.y;
-  const int k_begin = split * pr.k_per_split;
-  const int k_end = min(pr.K, k_begin + pr.k_per_split);
-  const int k_tiles = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     fence_barrier_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, BN < 32 ? 32 : BN);
+  if (warp == 0) tmem_alloc(tmem_slot, TMEM_COLS);
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&pr.ta);
-    prefetch_tmap(&pr.tb);
+    for (int q = 0; q < P.nprob; ++q) {
+      prefetch_tmap(&P.p[q].ta);
+      prefetch_tmap(&P.p[q].tb);
+    }
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  bool ok = true;
 
   if (warp == 0) {
+    // ---------------- TMA producer
     if (elect_one()) {
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES && !mbar_wait(&empty[s], ((kt / STAGES) - 1) & 1, ERR_TMA_WAIT)) break;
-        mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
-        const int k = k_begin + kt * BK;
-        uint8_t* a = sA + s * A_BYTES;
-        uint8_t* b = sB + s * B_BYTES;
-        if constexpr (A_MN) {
-          tma_load_2d(a, &pr.ta, &full[s], m0, k);
-          tma_load_2d(a + BK * 128, &pr.ta, &full[s], m0 + 64, k);
-        } else {
-          tma_load_2d(a, &pr.ta, &full[s], k, m0);
-        }
-        if constexpr (B_MN) {
+      int kc = 0;  // k-tile counter across work items (stage ring position)
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x) {
+        const TileCoord tc = decode_tile(P, w, tiles_per_split, BN);
+        const GemmProblemDev& pr = P.p[tc.pi];
+        const int k_begin = tc.split * pr.k_per_split;
+        const int k_end = min(pr.K, k_begin + pr.k_per_split);
+        const int k_tiles = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
+        for (int kt = 0; kt < k_tiles; ++kt, ++kc) {
+          const int s = kc % STAGES;
+          if (kc >= STAGES && !mbar_wait(&empty[s], ((kc / STAGES) - 1) & 1, ERR_TMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+          const int k = k_begin + kt * BK;
+          uint8_t* a = sA + s * A_BYTES;
+          uint8_t* b = sB + s * B_BYTES;
+          if constexpr (A_MN) {
+            tma_load_2d(a, &pr.ta, &full[s], tc.m0, k);
+            tma_load_2d(a + BK * 128, &pr.ta, &full[s], tc.m0 + 64, k);
+          } else {
+            tma_load_2d(a, &pr.ta, &full[s], k, tc.m0);
+          }
+          if constexpr (B_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * BK * 128, &pr.tb, &full[s], n0 + 64 * j, k);
-        } else {
-          tma_load_2d(b, &pr.tb, &full[s], k, n0);
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * BK * 128, &pr.tb, &full[s], tc.n0 + 64 * j, k);
+          } else {
+            tma_load_2d(b, &pr.tb, &full[s], k, tc.n0);
+          }
         }
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
-      bool ok = true;
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        const int s = kt % STAGES;
-        if (!mbar_wait(&full[s], (kt / STAGES) & 1, ERR_MMA_WAIT)) {
+      int kc = 0, it = 0;
+      for (int w = blockIdx.x; w < total_work && ok; w += gridDim.x, ++it) {
+        const TileCoord tc = decode_tile(P, w, tiles_per_split, BN);
+        const GemmProblemDev& pr = P.p[tc.pi];
+        const int k_begin = tc.split * pr.k_per_split;
+        const int k_end = min(pr.K, k_begin + pr.k_per_split);
+        const int k_tiles = k_end > k_begin ? (k_end - k_begin + BK - 1) / BK : 0;
+        const int buf = it & 1;
+        if (it >= 2 && !mbar_wait(&acc_empty[buf], ((it >> 1) - 1) & 1, ERR_MMA_WAIT)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_u32(sA + s * A_BYTES);
-        const uint32_t b = smem_u32(sB + s * B_BYTES);
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kt = 0; kt < k_tiles; ++kt, ++kc) {
+          const int s = kc % STAGES;
+          if (!mbar_wait(&full[s], (kc / STAGES) & 1, ERR_MMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + s * A_BYTES);
+          const uint32_t b = smem_u32(sB + s * B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          uint64_t ad, bd;
-          if constexpr (A_MN) ad = sw128_desc(a + kk * 16 * 128, BK * 128, 1024);
-          else ad = sw128_desc(a + kk * 32, 16, 1024);
-          if constexpr (B_MN) bd = sw128_desc(b + kk * 16 * 128, BK * 128, 1024);
-          else bd = sw128_desc(b + kk * 32, 16, 1024);
-          umma_f16(tmem, ad, bd, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t ad, bd;
+            if constexpr (A_MN) ad = sw128_desc(a + kk * 16 * 128, BK * 128, 1024);
+            else ad = sw128_desc(a + kk * 32, 16, 1024);
+            if constexpr (B_MN) bd = sw128_desc(b + kk * 16 * 128, BK * 128, 1024);
+            else bd = sw128_desc(b + kk * 32, 16, 1024);
+            umma_f16(d, ad, bd, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);  // also fires for k_tiles == 0 (epilogue writes zeros)
       }
-      if (ok) umma_commit(done);
     }
-  }
-  __syncwarp();
-
-  // ---------------- epilogue (all 4 warps; tcgen05.ld is warp-collective)
-  const int row = m0 + warp * 32 + lane;
-  const bool have = k_tiles > 0 && mbar_wait(done, 0, ERR_EPI_WAIT);
-  tc_fence_after();
-  char* cbase = reinterpret_cast<char*>(pr.c);
-  const size_t esz = P.out_fp32 ? 4 : 2;
+  } else {
+    // ---------------- epilogue warps 2..5
+    const int quarter = warp & 3;
+    int it = 0, sbuf = 0;
+    for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++it) {
+      const TileCoord tc = decode_tile(P, w, tiles_per_split, BN);
+      const GemmProblemDev& pr = P.p[tc.pi];
+      const int k_begin = tc.split * pr.k_per_split;
+      const bool have_k = min(pr.K, k_begin + pr.k_per_split) > k_begin;
+      const int buf = it & 1;
+      if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, ERR_EPI_WAIT)) break;
+      tc_fence_after();
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 32) {
-    float v[32];
-    if (have) {
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.f;
-    }
-    const int col0 = n0 + c0;
-    if (row >= pr.M || col0 >= pr.N) continue;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float x = v[j] * P.alpha;
-      if (pr.bias != nullptr && col0 + j < pr.N) x += __ldg(pr.bias + col0 + j);
-      if (P.act == 1) x = silu(x);
-      v[j] = x;
-    }
-    char* rowp = cbase + ((size_t)split * pr.split_stride + (size_t)row * pr.ldc + col0) * esz;
-    const bool full_chunk = col0 + 32 <= pr.N && ((reinterpret_cast<uintptr_t>(rowp) & 15) == 0);
-    if (P.out_fp32) {
-      float* o = reinterpret_cast<float*>(rowp);
-      if (full_chunk) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-      } else {
-        for (int j = 0; j < 32 && col0 + j < pr.N; ++j) o[j] = v[j];
-      }
-    } else {
-      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(rowp);
-      if (full_chunk) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          __nv_bfloat162 h[8];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j + 2 * q], v[j + 2 * q + 1]);
-          *reinterpret_cast<uint4*>(o + j) = *reinterpret_cast<uint4*>(h);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c0), v);
+        if (c0 + 32 >= BN) {
+          // accumulator fully read: hand the buffer back to the MMA warp
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
-      } else {
-        for (int j = 0; j < 32 && col0 + j < pr.N; ++j) o[j] = __float2bfloat16_rn(v[j]);
+        const int col0 = tc.n0 + c0;
+        if (col0 >= pr.N) continue;  // warp-uniform
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float x = have_k ? v[j] * P.alpha : 0.f;
+          if (pr.bias != nullptr && col0 + j < pr.N) x += __ldg(pr.bias + col0 + j);
+          if (P.act == 1) x = silu(x);
+          v[j] = x;
+        }
+        // stage the warp's 32 x 32 chunk (row-major, 32*esz bytes per row) and TMA-store it
+        uint8_t* stg = stage_out + ((quarter * 2 + (sbuf & 1)) * 32 * 32 * 4);
+        if (lane == 0) bulk_wait_read<1>();  // the buffer used two stores ago is free again
+        __syncwarp();
+        if (P.out_fp32) {
+          // 128B-swizzled staging: 16B chunk j of row r lives at chunk j ^ (r & 7)
+          float4* dst = reinterpret_cast<float4*>(stg + lane * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          // 64B-swizzled staging: 16B chunk j of row r lives at chunk j ^ ((r >> 1) & 3)
+          uint4* dst = reinterpret_cast<uint4*>(stg + lane * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
+            dst[j ^ ((lane >> 1) & 3)] = *reinterpret_cast<uint4*>(h);
+          }
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0 && tc.m0 + quarter * 32 < pr.M) {
+          tma_store_3d(&pr.tc, stg, col0, tc.m0 + quarter * 32, tc.split);
+          bulk_commit();
+        }
+        ++sbuf;
       }
     }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, BN < 32 ? 32 : BN);
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
 // Sum split-K partials [S][n] (stride between splits `stride`) into out, fixed order.
@@ -249,9 +312,32 @@ static const char* make_map(CUtensorMap* m, const void* base, long long rows, lo
   return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled failed";
 }
 
+// Output map: 3-D {N, M, splits} over fp32 or bf16, box {32, 32, 1}; 128B swizzle for fp32
+// rows (128 bytes), 64B swizzle for bf16 rows (64 bytes), matching the epilogue staging.
+static const char* make_out_map(CUtensorMap* m, void* base, long long M, long long N, long long ldc, long long sstride,
+                                int splits, bool fp32) {
+  const int es = fp32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return "GEMM output must be 16-byte aligned";
+  if ((ldc * es) % 16 != 0) return "GEMM output row stride must be a multiple of 16 bytes";
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return "cuTensorMapEncodeTiled is not available";
+  long long s2 = splits > 1 ? sstride : M * ldc;
+  if (s2 <= 0) s2 = ldc;
+  if ((s2 * es) % 16 != 0) return "GEMM split stride must be a multiple of 16 bytes";
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)splits};
+  cuuint64_t strides[2] = {(cuuint64_t)(ldc * es), (cuuint64_t)(s2 * es)};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   fp32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? nullptr : "cuTensorMapEncodeTiled (output) failed";
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaStream_t st) {
-  constexpr int smem = STAGES * (BM * BK + BN * BK) * 2 + 1024 + (2 * STAGES + 1) * 8 + 16;
+  constexpr int smem = STAGES * (BM * BK + BN * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 + 4 * 2 * 32 * 32 * 4;
   auto k = gemm_tc_kernel<BN, STAGES, A_MN, B_MN>;
   static bool init = false;  // per process; the attribute applies to every device
   if (!init) {
@@ -259,7 +345,16 @@ static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaS
       return "cudaFuncSetAttribute failed";
     init = true;
   }
-  k<<<dim3(tiles, splits), 128, smem, st>>>(P);
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (num_sms <= 0) num_sms = 148;
+  }
+  const int total = tiles * splits;
+  const int grid = total < num_sms ? total : num_sms;
+  k<<<grid, 192, smem, st>>>(P, total, tiles);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
@@ -284,6 +379,8 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
     if (err) return err;
     err = b_mn ? make_map(&d.tb, g.b, g.K, g.N, g.ldb, BK) : make_map(&d.tb, g.b, g.N, g.K, g.ldb, bn);
     if (err) return err;
+    err = make_out_map(&d.tc, g.c, g.M, g.N, g.ldc, g.split_stride, splits, out_fp32);
+    if (err) return err;
     d.c = g.c;
     d.bias = g.bias;
     d.ldc = g.ldc;
@@ -298,13 +395,13 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
   }
   if (tiles == 0) return nullptr;
   if (!a_mn) {
-    if (bn == 256) return launch_t<256, 3, false, false>(P, tiles, splits, stream);
-    if (bn == 128) return launch_t<128, 5, false, false>(P, tiles, splits, stream);
-    return launch_t<64, 6, false, false>(P, tiles, splits, stream);
+    if (bn == 256) return launch_t<256, 4, false, false>(P, tiles, splits, stream);
+    if (bn == 128) return launch_t<128, 6, false, false>(P, tiles, splits, stream);
+    return launch_t<64, 8, false, false>(P, tiles, splits, stream);
   }
-  if (bn == 256) return launch_t<256, 3, true, true>(P, tiles, splits, stream);
-  if (bn == 128) return launch_t<128, 5, true, true>(P, tiles, splits, stream);
-  return launch_t<64, 6, true, true>(P, tiles, splits, stream);
+  if (bn == 256) return launch_t<256, 4, true, true>(P, tiles, splits, stream);
+  if (bn == 128) return launch_t<128, 6, true, true>(P, tiles, splits, stream);
+  return launch_t<64, 8, true, true>(P, tiles, splits, stream);
 }
 
 const char* gemm_splitk_reduce(const float* part, float* out, long long n, int splits, long long stride, float beta,
