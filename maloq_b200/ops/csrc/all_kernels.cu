@@ -6,3 +6,4 @@
 #include "noalloc.cu"
 #include "edge.cu"
 #include "norm.cu"
+#include "comm.cu"

@@ -4,6 +4,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "comm.h"
 #include "edge.h"
 #include "gemm.h"
 #include "norm.h"
@@ -235,6 +236,22 @@ void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tenso
                           DG.data_ptr<float>(), (int)X.size(0), (int)X.size(2), stream()));
 }
 
+
+// ---- NVLink peer-memory collectives (pointers come from torch symmetric memory handles)
+void peer_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch, int64_t slot_base, int64_t spin_limit) {
+  check(maloq::peer_barrier(reinterpret_cast<uint32_t* const*>(pads_dev), (int)rank, (int)world, (uint32_t)epoch,
+                            (int)slot_base, spin_limit, stream()));
+}
+
+void allreduce_p2p(int64_t bufs_dev, int64_t rank, int64_t world, int64_t off, int64_t n, double scale) {
+  check(maloq::allreduce_p2p(reinterpret_cast<float* const*>(bufs_dev), (int)rank, (int)world, off, n, (float)scale,
+                             stream()));
+}
+
+void allreduce_multimem(int64_t mc, int64_t rank, int64_t world, int64_t off, int64_t n, double scale) {
+  check(maloq::allreduce_multimem(reinterpret_cast<float*>(mc), (int)rank, (int)world, off, n, (float)scale, stream()));
+}
+
 int64_t error_status(bool clear) { return maloq::error_status(clear); }
 
 }  // namespace
@@ -257,5 +274,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ln_silu_bwd", &ln_silu_bwd);
   m.def("gate_l_fwd", &gate_l_fwd);
   m.def("gate_l_bwd", &gate_l_bwd);
+  m.def("peer_barrier", &peer_barrier);
+  m.def("allreduce_p2p", &allreduce_p2p);
+  m.def("allreduce_multimem", &allreduce_multimem);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
 }

@@ -1,0 +1,145 @@
+// Intra-node collectives over NVLink peer memory (symmetric-memory buffers).
+//
+// * peer_barrier: every rank stores `epoch` into slot [rank] of every peer's signal pad
+//   (release, system scope) and then waits until its own pad holds `epoch` from every peer
+//   (acquire, system scope).  The wait is bounded: on timeout it records ERR_PEER_WAIT and
+//   returns, so a missing peer ends the kernel instead of hanging the GPU.
+// * allreduce_p2p: rank r owns chunk r of the bucket.  It reads chunk r from every peer
+//   buffer (plain loads through peer pointers), sums, scales by `scale`, and stores the result
+//   into chunk r of every peer buffer - reduce-scatter and all-gather in one pass, each rank
+//   moving 2 (w-1)/w of the bucket over NVLink.
+// * allreduce_multimem: the same with NVLink SHARP: one multimem.ld_reduce per vector returns
+//   the sum over all ranks (reduced in the switch) and one multimem.st writes it to all ranks.
+// Usage per bucket: barrier(epoch) -> allreduce -> barrier(epoch + 1), all on one stream.
+#include "common.cuh"
+#include "comm.h"
+
+namespace maloq {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void peer_barrier_kernel(uint32_t* const* __restrict__ pads, int rank, int world, uint32_t epoch,
+                                    int slot_base, long long spin_limit) {
+  const int t = threadIdx.x;
+  if (t < world) {
+    __threadfence_system();
+    st_release_sys(pads[t] + slot_base + rank, epoch);
+  }
+  __syncthreads();
+  if (t < world) {
+    const uint32_t* mine = pads[rank] + slot_base + t;
+    long long i = 0;
+    for (; i < spin_limit; ++i) {
+      if ((int)(ld_acquire_sys(mine) - epoch) >= 0) break;
+      __nanosleep(64);
+    }
+    if (i == spin_limit) record_error(ERR_PEER_WAIT);
+  }
+  __syncthreads();
+}
+
+__global__ void allreduce_p2p_kernel(float* const* __restrict__ bufs, int rank, int world, long long off, long long n,
+                                     float scale) {
+  const long long chunk = ((n + world - 1) / world + 3) / 4 * 4;
+  const long long c0 = off + rank * chunk;
+  const long long c1 = off + (rank + 1) * chunk < off + n ? off + (rank + 1) * chunk : off + n;
+  const long long nvec = (c1 - c0) / 4;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < nvec; v += (long long)gridDim.x * blockDim.x) {
+    const long long i = c0 + 4 * v;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < world; ++p) {
+      const float4 x = *reinterpret_cast<const float4*>(bufs[p] + i);
+      s.x += x.x;
+      s.y += x.y;
+      s.z += x.z;
+      s.w += x.w;
+    }
+    s.x *= scale;
+    s.y *= scale;
+    s.z *= scale;
+    s.w *= scale;
+    for (int p = 0; p < world; ++p) *reinterpret_cast<float4*>(bufs[p] + i) = s;
+  }
+  // scalar tail of the chunk
+  const long long tail0 = c0 + 4 * nvec;
+  for (long long i = tail0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < c1;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int p = 0; p < world; ++p) s += bufs[p][i];
+    s *= scale;
+    for (int p = 0; p < world; ++p) bufs[p][i] = s;
+  }
+}
+
+__global__ void allreduce_multimem_kernel(float* mc, int rank, int world, long long off, long long n, float scale) {
+  const long long chunk = ((n + world - 1) / world + 3) / 4 * 4;
+  const long long c0 = off + rank * chunk;
+  const long long c1 = off + (rank + 1) * chunk < off + n ? off + (rank + 1) * chunk : off + n;
+  const long long nvec = (c1 - c0) / 4;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < nvec; v += (long long)gridDim.x * blockDim.x) {
+    float* p = mc + c0 + 4 * v;
+    float a, b, c, d;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(a), "=f"(b), "=f"(c), "=f"(d)
+                 : "l"(p)
+                 : "memory");
+    a *= scale;
+    b *= scale;
+    c *= scale;
+    d *= scale;
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+  }
+  const long long tail0 = c0 + 4 * nvec;
+  for (long long i = tail0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < c1;
+       i += (long long)gridDim.x * blockDim.x) {
+    float a;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(a) : "l"(mc + i) : "memory");
+    a *= scale;
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc + i), "f"(a) : "memory");
+  }
+}
+
+static const char* comm_err() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+const char* peer_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t epoch, int slot_base,
+                         long long spin_limit, cudaStream_t st) {
+  if (world > 1024) return "peer_barrier: world too large";
+  peer_barrier_kernel<<<1, world < 32 ? 32 : world, 0, st>>>(pads_dev, rank, world, epoch, slot_base, spin_limit);
+  return comm_err();
+}
+
+const char* allreduce_p2p(float* const* bufs_dev, int rank, int world, long long off, long long n, float scale,
+                          cudaStream_t st) {
+  if (n == 0) return nullptr;
+  const long long per = (n + world - 1) / world / 4 + 1;
+  int blocks = (int)((per + 255) / 256);
+  if (blocks > 148 * 2) blocks = 148 * 2;
+  if (blocks < 1) blocks = 1;
+  allreduce_p2p_kernel<<<blocks, 256, 0, st>>>(bufs_dev, rank, world, off, n, scale);
+  return comm_err();
+}
+
+const char* allreduce_multimem(float* mc, int rank, int world, long long off, long long n, float scale,
+                               cudaStream_t st) {
+  if (n == 0) return nullptr;
+  const long long per = (n + world - 1) / world / 4 + 1;
+  int blocks = (int)((per + 255) / 256);
+  if (blocks > 148 * 2) blocks = 148 * 2;
+  if (blocks < 1) blocks = 1;
+  allreduce_multimem_kernel<<<blocks, 256, 0, st>>>(mc, rank, world, off, n, scale);
+  return comm_err();
+}
+
+}  // namespace maloq

@@ -24,11 +24,11 @@ import torch.distributed as dist
 
 
 class _Bucket:
-    def __init__(self, params, device, index):
+    def __init__(self, params, device, index, storage=None):
         self.params = params
         self.index = index
         n = sum(p.numel() for p in params)
-        self.buf = torch.zeros(n, dtype=torch.float32, device=device)
+        self.buf = storage if storage is not None else torch.zeros(n, dtype=torch.float32, device=device)
         self.views = []
         off = 0
         for p in params:
@@ -58,17 +58,22 @@ class GradSync:
                 cur, size = [], 0
         if cur:
             buckets.append(cur)
-        self.buckets = [_Bucket(b, self.device, i) for i, b in enumerate(buckets)]
+        self._fused = None
+        if mode == "fused" and self.world > 1:
+            from .symm import PeerAllReduce
+
+            sizes = [(sum(p.numel() for p in b) + 3) // 4 * 4 for b in buckets]
+            self._fused = PeerAllReduce(sum(sizes), self.device, group)
+            offs = [sum(sizes[:i]) for i in range(len(sizes))]
+            self.buckets = [_Bucket(b, self.device, i, self._fused.view(o, sum(p.numel() for p in b)))
+                            for i, (b, o) in enumerate(zip(buckets, offs))]
+        else:
+            self.buckets = [_Bucket(b, self.device, i) for i, b in enumerate(buckets)]
         self._owner = {}
         for b in self.buckets:
             for p, v in zip(b.params, b.views):
                 self._owner[p] = (b, v)
         self.works = []
-        self._fused = None
-        if mode == "fused" and self.world > 1:
-            from .symm import PeerAllReduce
-
-            self._fused = PeerAllReduce(max(b.buf.numel() for b in self.buckets), self.device, group)
         if mode in ("nccl", "fused"):
             for p in self.params:
                 p.register_post_accumulate_grad_hook(self._hook)

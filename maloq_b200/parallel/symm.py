@@ -1,0 +1,91 @@
+"""Fused gradient all-reduce over NVLink peer memory (no NCCL on the hot path).
+
+The data-parallel gradient buckets live in one symmetric-memory allocation
+(``torch.distributed._symmetric_memory``), so every rank can address every peer's buckets.
+Reducing a bucket is three kernels on the reduction stream:
+
+1. ``peer_barrier(epoch)`` - all ranks have finished writing this bucket's gradients;
+2. ``allreduce_multimem`` (NVLink SHARP through NVSwitch, when the group supports multicast)
+   or ``allreduce_p2p`` (peer loads/stores) - rank r reduces chunk r over all ranks, scales
+   by 1/world and writes the result into chunk r of every rank's bucket;
+3. ``peer_barrier(epoch + 1)`` - every chunk has been written everywhere.
+
+The reference reduces every parameter with its own synchronous NCCL all-reduce after
+backward (``train_utils/splittrainer.py:204-218``).  Waits are bounded (see comm.cu); a
+missing peer shows up as a non-zero ``error_status()`` instead of a hang.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..ops.native import count_launches
+
+SPIN_LIMIT = 1 << 28  # polls of ~64 ns back-off: tens of seconds before a barrier gives up
+
+
+class PeerAllReduce:
+    def __init__(self, numel, device, group=None, use_multimem=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from ..ops.kernels import lib
+
+        self.lib = lib()
+        self.group = group or dist.group.WORLD
+        self.device = torch.device(device)
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        self.buf = symm_mem.empty(max(4, (numel + 3) // 4 * 4), dtype=torch.float32, device=self.device)
+        self.buf.zero_()
+        name = self.group.group_name
+        self.hdl = symm_mem.rendezvous(self.buf, name)
+        self.bufs_dev = torch.tensor(self.hdl.buffer_ptrs, dtype=torch.int64, device=self.device)
+        self.pads_dev = torch.tensor(self.hdl.signal_pad_ptrs, dtype=torch.int64, device=self.device)
+        mm = self.hdl.has_multicast_support() if hasattr(self.hdl, "has_multicast_support") else False
+        if use_multimem is None:
+            use_multimem = mm and os.environ.get("MALOQ_NO_MULTIMEM", "0") != "1"
+        self.mc = int(self.hdl.multicast_ptr) if (use_multimem and mm) else 0
+        self.epoch = 0
+        self.events = []
+        self.hdl.barrier()
+
+    @property
+    def transport(self):
+        return "multimem" if self.mc else "p2p"
+
+    def view(self, offset, numel):
+        return self.buf[offset:offset + numel]
+
+    def _barrier(self):
+        self.epoch += 1
+        self.lib.peer_barrier(self.pads_dev.data_ptr(), self.rank, self.world,
+                              self.epoch, 0, SPIN_LIMIT)
+
+    def all_reduce_(self, flat, side_stream=None, scale=1.0):
+        """Reduce ``flat`` (a view of this object's buffer) in place: sum over ranks * scale."""
+        off = flat.data_ptr() - self.buf.data_ptr()
+        assert off % 16 == 0 and 0 <= off and flat.is_contiguous(), "bucket must be an aligned view of the buffer"
+        off //= 4
+        n = flat.numel()
+        stream = side_stream or torch.cuda.current_stream(self.device)
+        if side_stream is not None:
+            side_stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            self._barrier()
+            if self.mc:
+                self.lib.allreduce_multimem(self.mc, self.rank, self.world, off, n, scale)
+            else:
+                self.lib.allreduce_p2p(self.bufs_dev.data_ptr(), self.rank, self.world, off, n, scale)
+            self._barrier()
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            self.events.append(ev)
+        count_launches(3)
+
+    def wait(self, stream):
+        for ev in self.events:
+            stream.wait_event(ev)
+        self.events = []
