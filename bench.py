@@ -216,7 +216,9 @@ def main():
                        "global_batch": graphs, "seq_len": None, "parallelism": f"dp{world}",
                        "edges_per_gpu_step": round(n_edges), "atoms_per_gpu_step": round(n_nodes),
                        "l2": "256 MiB buffer written between timed steps, outside the step events",
-                       "impl": args.impl, "grad_sync": None if sync is None else sync.mode},
+                       "impl": args.impl, "grad_sync": None if sync is None else sync.mode,
+                       "allreduce_transport": (sync._fused.transport if sync is not None and sync._fused is not None
+                                               else ("nccl" if sync is not None else None))},
             "e2e": {"value": round(e2e_value, 2), "unit": "graphs/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": 4},
             "gpu_launches": int(launches),

@@ -44,10 +44,13 @@ class PeerAllReduce:
         self.hdl = symm_mem.rendezvous(self.buf, name)
         self.bufs_dev = torch.tensor(self.hdl.buffer_ptrs, dtype=torch.int64, device=self.device)
         self.pads_dev = torch.tensor(self.hdl.signal_pad_ptrs, dtype=torch.int64, device=self.device)
-        mm = self.hdl.has_multicast_support() if hasattr(self.hdl, "has_multicast_support") else False
+        try:
+            mc = int(self.hdl.multicast_ptr or 0)
+        except Exception:  # noqa: BLE001 - no multicast object for this group
+            mc = 0
         if use_multimem is None:
-            use_multimem = mm and os.environ.get("MALOQ_NO_MULTIMEM", "0") != "1"
-        self.mc = int(self.hdl.multicast_ptr) if (use_multimem and mm) else 0
+            use_multimem = os.environ.get("MALOQ_NO_MULTIMEM", "0") != "1"
+        self.mc = mc if use_multimem else 0
         self.epoch = 0
         self.events = []
         self.hdl.barrier()
