@@ -203,8 +203,10 @@ class eSEN_Backbone(nn.Module):
         vec = edge_attr[:, [2, 3, 1]]  # (x, y, z) -> model frame (y, z, x): polar axis = input z
         rot = ops.edge_rotation(vec, self.lmax, self.mmax, [getattr(self, f"Jd_{l}") for l in range(self.lmax + 1)],
                                 self.mappingReduced)
-        return Graph(batch.edge_index[0], batch.edge_index[1], rot, batch.dst_ptr, batch.num_nodes,
-                     self.lmax, self.mmax, getattr(batch, "halo", None))
+        g = Graph(batch.edge_index[0], batch.edge_index[1], rot, batch.dst_ptr, batch.num_nodes,
+                  self.lmax, self.mmax, getattr(batch, "halo", None))
+        g.num_nodes_ext = getattr(batch, "num_nodes_ext", None) or batch.num_nodes
+        return g
 
     def forward(self, batch):
         graph = self.build_graph(batch)

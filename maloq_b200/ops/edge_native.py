@@ -27,6 +27,18 @@ def _lib():
     return lib()
 
 
+def dst_ptr_ext(graph, n):
+    """Destination CSR offsets over ``n`` rows (halo rows, beyond the owned ones, have no
+    incoming edges)."""
+    if n == graph.dst_ptr.shape[0] - 1:
+        return graph.dst_ptr
+    key = ("dst_ptr_ext", n)
+    if key not in graph.cache:
+        tail = graph.dst_ptr[-1:].expand(n + 1 - graph.dst_ptr.shape[0])
+        graph.cache[key] = torch.cat([graph.dst_ptr, tail]).contiguous()
+    return graph.cache[key]
+
+
 def src_csr(graph):
     """Edges grouped by source node: (perm, ptr), cached on the graph."""
     key = "src_csr"
@@ -164,7 +176,7 @@ class EdgewiseFn(torch.autograd.Function):
         DRAD = torch.empty_like(rad)
         lib.gather_rotate_bwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, dA, DSRC, DDST, DXE, DRAD, Cin)
         DX = torch.empty_like(x_node)
-        lib.node_reduce(DDST, graph.dst_ptr, DSRC, perm, sptr, DX)
+        lib.node_reduce(DDST, dst_ptr_ext(graph, x_node.shape[0]), DSRC, perm, sptr, DX)
         count_launches(6)
         return (DX, DXE, DRAD, db1, db2, None, None, *dw1, *dw2)
 

@@ -1,0 +1,120 @@
+"""Halo (ghost-node) exchange for graph-partitioned message passing.
+
+Every Edgewise layer needs the features of its edges' source nodes; sources owned by other
+ranks form this rank's halo.  :class:`HaloPlan` provides ``extend(x_node, graph)`` ->
+``[owned rows | halo rows]`` with the matching backward (halo gradients are summed back into
+the owners' rows).  Two transports:
+
+* ``"collective"`` - ``all_to_all_single`` of the needed rows inside an autograd function
+  (NCCL on GPUs, gloo on CPU).  This is the reference's design (``helm/nn/communication.py:
+  190-340``) without its per-exchange device synchronise and global barrier.
+* ``"peer"`` - owners publish their rows in a symmetric-memory staging buffer and the edge
+  kernels load halo rows straight from the owner's buffer over NVLink; halo gradients are
+  stored into the owner's receive slots and summed there (see :mod:`maloq_b200.parallel.peer_halo`).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+class _Exchange(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, plan):
+        ctx.plan = plan
+        return plan.fetch(x)
+
+    @staticmethod
+    def backward(ctx, g_halo):
+        return ctx.plan.return_grads(g_halo), None
+
+
+class HaloPlan:
+    def __init__(self, domain, device, group=None, transport="collective"):
+        self.domain = domain
+        self.device = torch.device(device)
+        self.group = group
+        self.transport = transport
+        self.world = domain.world
+        self.n_own = domain.n_own
+        self.n_halo = len(domain.halo)
+        self.send_counts = [len(s) for s in domain.send]
+        self.recv_counts = list(domain.recv_counts)
+        cat = np.concatenate(domain.send) if sum(self.send_counts) else np.zeros(0, dtype=np.int64)
+        self.send_idx = torch.as_tensor(cat, dtype=torch.long, device=self.device)
+        self.peer = None
+
+    # ------------------------------------------------------------------ collective transport
+    def fetch(self, x):
+        rest = tuple(x.shape[1:])
+        send = x.index_select(0, self.send_idx).contiguous()
+        recv = x.new_empty((self.n_halo,) + rest)
+        if self.world > 1:
+            dist.all_to_all_single(recv, send, self.recv_counts, self.send_counts, group=self.group)
+        return recv
+
+    def return_grads(self, g_halo):
+        rest = tuple(g_halo.shape[1:])
+        g_halo = g_halo.contiguous()
+        back = g_halo.new_empty((int(self.send_idx.numel()),) + rest)
+        if self.world > 1:
+            dist.all_to_all_single(back, g_halo, self.send_counts, self.recv_counts, group=self.group)
+        gx = g_halo.new_zeros((self.n_own,) + rest)
+        gx.index_add_(0, self.send_idx, back)
+        return gx
+
+    def gather_halo(self, x):
+        return _Exchange.apply(x, self)
+
+    def extend(self, x_node, graph=None):
+        """[owned | halo] rows, differentiable."""
+        if self.n_halo == 0:
+            return x_node
+        if self.transport == "peer" and self.peer is not None:
+            return self.peer.extend(x_node)
+        return torch.cat([x_node, self.gather_halo(x_node)], dim=0)
+
+    def gather_source(self, x_node, graph):
+        """Features of every local edge's source node (reference-op path)."""
+        return self.extend(x_node, graph).index_select(0, graph.src)
+
+
+def partition_batch(sample, domain, pair_table=None, device="cpu", transport="collective", group=None,
+                    target_dtype=torch.float32):
+    """The GraphBatch of one rank for a partitioned structure ``sample`` (a GraphSample with
+    global numbering).  Targets, if present, are restricted to owned nodes / local edges."""
+    from ..data.batch import GraphBatch
+    from ..data.graph import dst_pointer
+
+    z = sample.z
+    own = domain.owned
+    e = domain.edges
+    src_g, dst_g = sample.src[e], sample.dst[e]
+    kw = dict(
+        atomic_numbers=torch.as_tensor(z[own]),
+        pos=torch.as_tensor(sample.pos[own], dtype=torch.float32),
+        atom_charge=torch.full((len(own),), sample.charge, dtype=torch.long),
+        atom_spin=torch.full((len(own),), sample.spin, dtype=torch.long),
+        batch=torch.zeros(len(own), dtype=torch.long),
+        edge_index=torch.as_tensor(np.stack([domain.src_local, domain.dst_local])),
+        edge_attr=torch.as_tensor(sample.edge_attr[e], dtype=torch.float32),
+        dst_ptr=torch.as_tensor(dst_pointer(domain.dst_local, len(own))),
+        src_z=torch.as_tensor(z[src_g]),
+        dst_z=torch.as_tensor(z[dst_g]),
+        num_atoms_in_molecule=torch.as_tensor([len(own)]),
+        global_node_ids=torch.as_tensor(own),
+        global_edge_ids=torch.as_tensor(e),
+    )
+    b = GraphBatch(**kw)
+    if pair_table is not None:
+        b.node_pair_type = torch.as_tensor(pair_table.pair_type(z[own], z[own]))
+        b.edge_pair_type = torch.as_tensor(pair_table.pair_type(z[src_g], z[dst_g]))
+    if sample.node_y is not None:
+        b.node_y = torch.as_tensor(sample.node_y)[:, own].to(target_dtype)
+        b.y = torch.as_tensor(sample.y)[:, e].to(target_dtype)
+    b = b.to(device)
+    b.halo = HaloPlan(domain, device, group=group, transport=transport)
+    b.num_nodes_ext = domain.n_ext
+    return b

@@ -14,6 +14,18 @@ def free_port():
     return p
 
 
+def _to_numpy(x):
+    import torch
+
+    if isinstance(x, torch.Tensor):
+        return x.detach().cpu().numpy()
+    if isinstance(x, (list, tuple)):
+        return type(x)(_to_numpy(v) for v in x)
+    if isinstance(x, dict):
+        return {k: _to_numpy(v) for k, v in x.items()}
+    return x
+
+
 def _entry(rank, world, port, fn, backend, q, args):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
@@ -27,7 +39,7 @@ def _entry(rank, world, port, fn, backend, q, args):
         else:
             dist.init_process_group("gloo", rank=rank, world_size=world)
         out = fn(rank, world, *args)
-        q.put((rank, "ok", out))
+        q.put((rank, "ok", _to_numpy(out)))
     except Exception:  # noqa: BLE001 - reported to the parent test
         q.put((rank, "err", traceback.format_exc()))
     finally:

@@ -48,7 +48,7 @@ def test_grad_sync_bucketed_matches_average():
     for r in range(2):
         for got_step, exp_step in zip(res[r], exp):
             for g, e in zip(got_step, exp_step):
-                assert torch.allclose(g, e, atol=1e-6)
+                assert torch.allclose(torch.as_tensor(g), e, atol=1e-6)
 
 
 def test_grad_sync_per_param_matches_average():
@@ -56,4 +56,4 @@ def test_grad_sync_per_param_matches_average():
     exp = _expected(2)
     for got_step, exp_step in zip(res[0], exp):
         for g, e in zip(got_step, exp_step):
-            assert torch.allclose(g, e, atol=1e-6)
+            assert torch.allclose(torch.as_tensor(g), e, atol=1e-6)
