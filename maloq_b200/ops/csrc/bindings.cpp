@@ -91,7 +91,9 @@ const long long* ll(const c10::optional<at::Tensor>& t) { return t.has_value() ?
 
 // A [E, R*Cin] = rad * rot . [X[src] | X[dst] | XE]
 void gather_rotate_fwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
-                       at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor A, int64_t Cin) {
+                       at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor A, int64_t Cin,
+                       int64_t peers, c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row,
+                       int64_t n_own) {
   chk(X, at::kFloat, "X");
   chk(rot, at::kFloat, "rot");
   chk(A, at::kBFloat16, "A");
@@ -102,12 +104,16 @@ void gather_rotate_fwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
   const at::cuda::CUDAGuard guard(X.device());
   check(maloq::edge_gather_rotate_fwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), ll(src), ll(dst),
                                       rot.data_ptr<float>(), ptr<float>(rad), bf(A), (int)src.size(0),
-                                      (int)X.size(2), (int)Cin, stream()));
+                                      (int)X.size(2), (int)Cin, reinterpret_cast<const float* const*>(peers),
+                                      halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
+                                      n_own, stream()));
 }
 
 void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
                        at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor dA, at::Tensor DSRC,
-                       at::Tensor DDST, c10::optional<at::Tensor> DXE, c10::optional<at::Tensor> DRAD, int64_t Cin) {
+                       at::Tensor DDST, c10::optional<at::Tensor> DXE, c10::optional<at::Tensor> DRAD, int64_t Cin,
+                       int64_t peers, c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row,
+                       int64_t n_own) {
   chk(X, at::kFloat, "X");
   chk(dA, at::kBFloat16, "dA");
   chk(DSRC, at::kFloat, "DSRC");
@@ -116,18 +122,27 @@ void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
   check(maloq::edge_gather_rotate_bwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), ll(src), ll(dst),
                                       rot.data_ptr<float>(), ptr<float>(rad), bf(dA), DSRC.data_ptr<float>(),
                                       DDST.data_ptr<float>(), ptr<float>(DXE), ptr<float>(DRAD), (int)src.size(0),
-                                      (int)X.size(2), (int)Cin, stream()));
+                                      (int)X.size(2), (int)Cin, reinterpret_cast<const float* const*>(peers),
+                                      halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
+                                      n_own, stream()));
 }
 
 // DX[n] = sum over dst-CSR of DDST + sum over src-CSR of DSRC (either may be absent)
-void node_reduce(at::Tensor DDST, at::Tensor dst_ptr, c10::optional<at::Tensor> DSRC,
+void halo_push(at::Tensor G, int64_t recv, at::Tensor halo_owner, at::Tensor recv_slot) {
+  chk(G, at::kFloat, "G");
+  const int SC = (int)(G.numel() / std::max<int64_t>(1, G.size(0)));
+  const at::cuda::CUDAGuard guard(G.device());
+  check(maloq::edge_halo_push(G.data_ptr<float>(), reinterpret_cast<float* const*>(recv), halo_owner.data_ptr<int>(),
+                              ll(recv_slot), G.size(0), SC, stream()));
+}
+
+void node_reduce(c10::optional<at::Tensor> DDST, at::Tensor dst_ptr, c10::optional<at::Tensor> DSRC,
                  c10::optional<at::Tensor> src_perm, c10::optional<at::Tensor> src_ptr, at::Tensor DX) {
-  chk(DDST, at::kFloat, "DDST");
   chk(DX, at::kFloat, "DX");
   const int N = (int)DX.size(0);
   const int SC = (int)(DX.numel() / std::max<int64_t>(1, N));
   const at::cuda::CUDAGuard guard(DX.device());
-  check(maloq::edge_node_reduce(DDST.data_ptr<float>(), ll(dst_ptr), ptr<float>(DSRC), ll(src_perm), ll(src_ptr),
+  check(maloq::edge_node_reduce(ptr<float>(DDST), ll(dst_ptr), ptr<float>(DSRC), ll(src_perm), ll(src_ptr),
                                 DX.data_ptr<float>(), N, SC, stream()));
 }
 
@@ -267,6 +282,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gate_fwd", &gate_fwd);
   m.def("gate_bwd", &gate_bwd);
   m.def("node_reduce", &node_reduce);
+  m.def("halo_push", &halo_push);
   m.def("rms_norm_fwd", &rms_norm_fwd);
   m.def("rms_norm_bwd", &rms_norm_bwd);
   m.def("norm_grid", &norm_grid);

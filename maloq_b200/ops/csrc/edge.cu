@@ -17,6 +17,22 @@ namespace maloq {
 
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 
+// Source rows of the gather: local rows s < n_own come from X; with a halo (peers != nullptr)
+// rows s >= n_own are halo node h = s - n_own, read from the owner's staging buffer
+// peers[halo_owner[h]] at row halo_row[h] - a load over NVLink.
+struct HaloRef {
+  const float* const* peers;
+  const int* halo_owner;
+  const long long* halo_row;
+  long long n_own;
+};
+
+__device__ __forceinline__ const float* src_row(const float* X, long long s, int S, int C, const HaloRef& H) {
+  if (H.peers == nullptr || s < H.n_own) return X + s * S * C;
+  const long long h = s - H.n_own;
+  return H.peers[H.halo_owner[h]] + H.halo_row[h] * S * C;
+}
+
 // ---------------------------------------------------------------- gather + rotate + modulate
 // A[e, k, c'] = rad[e, slot(k)*Cin + c'] * sum_{j in degree l_k} rot[e,k,j] * in[e, j, c']
 // in = [X[src] | X[dst] | XE[e]] along channels (Cin = 2C or 3C).
@@ -24,14 +40,14 @@ template <int L, int MM>
 __global__ void __launch_bounds__(128) gather_rotate_fwd_kernel(
     const float* __restrict__ X, const float* __restrict__ XE, const long long* __restrict__ src,
     const long long* __restrict__ dst, const float* __restrict__ rot, const float* __restrict__ rad,
-    __nv_bfloat16* __restrict__ A, int E, int C, int Cin) {
+    __nv_bfloat16* __restrict__ A, int E, int C, int Cin, const HaloRef H) {
   using F = Frame<L, MM>;
   constexpr int S = F::S, R = F::R;
   const int e = blockIdx.x;
   const int cp = blockIdx.y * blockDim.x + threadIdx.x;
   if (e >= E || cp >= Cin) return;
   const float* base;
-  if (cp < C) base = X + (size_t)src[e] * S * C + cp;
+  if (cp < C) base = src_row(X, src[e], S, C, H) + cp;
   else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
   else base = XE + (size_t)e * S * C + (cp - 2 * C);
   float in[S];
@@ -59,7 +75,7 @@ __global__ void __launch_bounds__(128) gather_rotate_bwd_kernel(
     const float* __restrict__ X, const float* __restrict__ XE, const long long* __restrict__ src,
     const long long* __restrict__ dst, const float* __restrict__ rot, const float* __restrict__ rad,
     const __nv_bfloat16* __restrict__ dA, float* __restrict__ DSRC, float* __restrict__ DDST,
-    float* __restrict__ DXE, float* __restrict__ DRAD, int E, int C, int Cin) {
+    float* __restrict__ DXE, float* __restrict__ DRAD, int E, int C, int Cin, const HaloRef H) {
   using F = Frame<L, MM>;
   constexpr int S = F::S, R = F::R;
   const int e = blockIdx.x;
@@ -68,7 +84,7 @@ __global__ void __launch_bounds__(128) gather_rotate_bwd_kernel(
   float in[S];
   if (rad) {
     const float* base;
-    if (cp < C) base = X + (size_t)src[e] * S * C + cp;
+    if (cp < C) base = src_row(X, src[e], S, C, H) + cp;
     else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
     else base = XE + (size_t)e * S * C + (cp - 2 * C);
 #pragma unroll
@@ -120,10 +136,23 @@ __global__ void node_reduce_kernel(const float* __restrict__ DDST, const long lo
   const int i = blockIdx.y * blockDim.x + threadIdx.x;
   if (n >= N || i >= SC) return;
   float s = 0.f;
-  for (long long e = dst_ptr[n]; e < dst_ptr[n + 1]; ++e) s += DDST[(size_t)e * SC + i];
+  if (DDST)
+    for (long long e = dst_ptr[n]; e < dst_ptr[n + 1]; ++e) s += DDST[(size_t)e * SC + i];
   if (DSRC)
     for (long long q = src_ptr[n]; q < src_ptr[n + 1]; ++q) s += DSRC[(size_t)src_perm[q] * SC + i];
   DX[(size_t)n * SC + i] = s;
+}
+
+// Halo gradient push: row h of G (halo rows of the extended-space gradient) is stored into
+// slot recv_slot[h] of its owner's receive buffer recv[halo_owner[h]] (a store over NVLink).
+__global__ void halo_push_kernel(const float* __restrict__ G, float* const* __restrict__ recv,
+                                 const int* __restrict__ halo_owner, const long long* __restrict__ recv_slot,
+                                 long long n_halo, int SC) {
+  const long long h = blockIdx.x;
+  if (h >= n_halo) return;
+  const float4* src = reinterpret_cast<const float4*>(G + h * SC);
+  float4* dst = reinterpret_cast<float4*>(recv[halo_owner[h]] + recv_slot[h] * SC);
+  for (int i = threadIdx.x; i < SC / 4; i += blockDim.x) dst[i] = src[i];
 }
 
 // ---------------------------------------------------------------- rotate back
@@ -299,22 +328,35 @@ static inline int clampm(int L, int MM) { return MM > L ? L : MM; }
 
 const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
                                    const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
-                                   int C, int Cin, cudaStream_t st) {
+                                   int C, int Cin, const float* const* peers, const int* halo_owner,
+                                   const long long* halo_row, long long n_own, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
+  const HaloRef H{peers, halo_owner, halo_row, n_own};
   dim3 grid(E, (Cin + 127) / 128);
-  MALOQ_DISPATCH_FRAME((gather_rotate_fwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, A, E, C, Cin)))
+  MALOQ_DISPATCH_FRAME(
+      (gather_rotate_fwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, A, E, C, Cin, H)))
 }
 
 const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const long long* src,
                                    const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
                                    float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
-                                   cudaStream_t st) {
+                                   const float* const* peers, const int* halo_owner, const long long* halo_row,
+                                   long long n_own, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
+  const HaloRef H{peers, halo_owner, halo_row, n_own};
   dim3 grid(E, (Cin + 127) / 128);
   MALOQ_DISPATCH_FRAME((gather_rotate_bwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, dA, DSRC,
-                                                                                DDST, DXE, DRAD, E, C, Cin)))
+                                                                                DDST, DXE, DRAD, E, C, Cin, H)))
+}
+
+const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,
+                           long long n_halo, int SC, cudaStream_t st) {
+  if (n_halo == 0) return nullptr;
+  if (SC % 4) return "halo push: row size must be a multiple of 4 floats";
+  halo_push_kernel<<<(unsigned)n_halo, 128, 0, st>>>(G, recv, halo_owner, recv_slot, n_halo, SC);
+  return last_error();
 }
 
 const char* edge_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,

@@ -95,7 +95,7 @@ def _weight_grads(gys, xs):
 
 class EdgewiseFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_node, x_edge_emb, rad, b1, b2, graph, meta, *weights):
+    def forward(ctx, x_node, x_edge_emb, rad, b1, b2, graph, meta, halo, *weights):
         lib = _lib()
         nw = len(weights) // 2
         w1, w2 = weights[:nw], weights[nw:]
@@ -108,7 +108,7 @@ class EdgewiseFn(torch.autograd.Function):
         xe = x_edge_emb.contiguous() if x_edge_emb is not None else None
         rad = rad.contiguous().float()
         A = torch.empty(E, R * Cin, device=dev, dtype=torch.bfloat16)
-        lib.gather_rotate_fwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, A, Cin)
+        lib.gather_rotate_fwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, A, Cin, *_halo_args(halo))
         w1b = [w.to(torch.bfloat16).contiguous() for w in w1]
         w2b = [w.to(torch.bfloat16).contiguous() for w in w2]
         Y1 = torch.empty(E, G + R * H, device=dev, dtype=torch.bfloat16)
@@ -131,7 +131,7 @@ class EdgewiseFn(torch.autograd.Function):
             lib.rotate_back_edge(*LM, Y2, 0, R, graph.rot, out)
         count_launches(4)
         ctx.save_for_backward(x_node, xe, rad, A, Y1, H1, *w1b, *w2b)
-        ctx.graph, ctx.meta, ctx.nw = graph, meta, nw
+        ctx.graph, ctx.meta, ctx.nw, ctx.halo = graph, meta, nw, halo
         return out
 
     @staticmethod
@@ -174,11 +174,15 @@ class EdgewiseFn(torch.autograd.Function):
         DDST = torch.empty(E, S, C, device=dev, dtype=torch.float32)
         DXE = torch.empty_like(xe) if xe is not None else None
         DRAD = torch.empty_like(rad)
-        lib.gather_rotate_bwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, dA, DSRC, DDST, DXE, DRAD, Cin)
-        DX = torch.empty_like(x_node)
-        lib.node_reduce(DDST, dst_ptr_ext(graph, x_node.shape[0]), DSRC, perm, sptr, DX)
+        lib.gather_rotate_bwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, dA, DSRC, DDST, DXE, DRAD, Cin,
+                              *_halo_args(ctx.halo))
+        n_ext = graph.num_nodes_ext if ctx.halo is not None else x_node.shape[0]
+        DX = torch.empty((n_ext,) + tuple(x_node.shape[1:]), device=dev, dtype=torch.float32)
+        lib.node_reduce(DDST, dst_ptr_ext(graph, n_ext), DSRC, perm, sptr, DX)
+        if ctx.halo is not None:
+            DX = ctx.halo[0].reduce_grads(DX)
         count_launches(6)
-        return (DX, DXE, DRAD, db1, db2, None, None, *dw1, *dw2)
+        return (DX, DXE, DRAD, db1, db2, None, None, None, *dw1, *dw2)
 
 
 def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
@@ -193,9 +197,24 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
                     G=c1.extra_m0_output_channels, m_size=list(mapping.m_size), node=node_or_edge == "node")
         graph.cache[key] = meta
     rad = c1.rad_func(x_edge)
-    x_src_space = graph.halo.extend(x_node, graph) if graph.halo is not None else x_node
+    halo = None
+    x_src_space = x_node
+    if graph.halo is not None:
+        if graph.halo.transport == "peer":
+            peer = graph.halo.peer_for(tuple(x_node.shape[1:]))
+            halo = (peer, peer.publish(x_node))  # rows readable by every rank; slot id
+        else:
+            x_src_space = graph.halo.extend(x_node, graph)
     weights = list(c1.gemm_weights()) + list(c2.gemm_weights())
-    return EdgewiseFn.apply(x_src_space, x_msg_edge, rad, c1.fc_m0.bias, c2.fc_m0.bias, graph, meta, *weights)
+    return EdgewiseFn.apply(x_src_space, x_msg_edge, rad, c1.fc_m0.bias, c2.fc_m0.bias, graph, meta, halo, *weights)
+
+
+def _halo_args(halo):
+    """(peer pointer table, halo owner, halo row, n_own) for the gather kernels."""
+    if halo is None:
+        return 0, None, None, 0
+    peer, slot = halo
+    return peer.table_ptr(slot), peer.halo_owner, peer.halo_row, peer.n_own
 
 
 class RotateBackM0Fn(torch.autograd.Function):

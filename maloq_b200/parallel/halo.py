@@ -69,12 +69,19 @@ class HaloPlan:
         return _Exchange.apply(x, self)
 
     def extend(self, x_node, graph=None):
-        """[owned | halo] rows, differentiable."""
+        """[owned | halo] rows, differentiable (collective transport; the peer transport is used
+        inside the fused edge kernels instead)."""
         if self.n_halo == 0:
             return x_node
-        if self.transport == "peer" and self.peer is not None:
-            return self.peer.extend(x_node)
         return torch.cat([x_node, self.gather_halo(x_node)], dim=0)
+
+    def peer_for(self, row_shape, n_slots=32):
+        """The NVLink halo (created on first use - a collective step on every rank)."""
+        if self.peer is None:
+            from .peer_halo import PeerHalo
+
+            self.peer = PeerHalo(self.domain, self.device, row_shape, n_slots=n_slots, group=self.group)
+        return self.peer
 
     def gather_source(self, x_node, graph):
         """Features of every local edge's source node (reference-op path)."""

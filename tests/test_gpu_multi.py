@@ -88,3 +88,72 @@ def test_fused_grad_sync_matches_nccl_in_training():
     _need(2)
     out = _dist_util.run(_train_worker, world=2, backend="nccl")
     assert max(out.values()) < 1e-5, out
+
+
+def _partition_worker(rank, world, transport):
+    import numpy as np
+    import torch
+
+    from maloq_b200.data import batch as B
+    from maloq_b200.data import basis_sets, structures
+    from maloq_b200.data.targets import FockLabeler
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.ops import kernels
+    from maloq_b200.parallel import partition as P
+    from maloq_b200.parallel.halo import partition_batch
+
+    dev = torch.device("cuda", rank)
+    rng = np.random.default_rng(0)
+    s = structures.Structure(rng.choice([1, 6, 8], size=300), rng.uniform(0, 16, size=(300, 3)))
+    g = B.make_sample(s, 5.0)
+    lab = FockLabeler(basis_sets.get_basis("split_valence_small"))
+    kw = dict(sphere_channels=32, hidden_channels=32, lmax=4, mmax=2, cutoff=5.0, num_layers=2, num_distance_basis=16,
+              edge_channels=32)
+
+    def model():
+        torch.manual_seed(0)
+        bb = eSEN_Backbone(lab.irreps, **kw).to(dev)
+        hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=32, ls_list=lab.layout.ls_list,
+                              reduce_node=True, reduce_node_intra=True).to(dev)
+        return bb, hd
+
+    def run(batch, own, edges):
+        bb, hd = model()
+        no, eo = hd(bb(batch), batch)
+        torch.manual_seed(7)
+        wn = torch.randn(g.num_nodes, no.shape[-1], device=dev)
+        we = torch.randn(len(g.src), eo.shape[-1], device=dev)
+        loss = (no[0] * wn[own]).sum() + (eo[0] * we[edges]).sum()
+        loss.backward()
+        named = [(n, p) for n, p in list(bb.named_parameters()) + [("head." + k, v) for k, v in hd.named_parameters()]]
+        return no[0].detach(), eo[0].detach(), named
+
+    # unpartitioned reference on this GPU
+    full = B.collate([g], lab.table).to(dev)
+    _, _, ref_named = run(full, torch.arange(g.num_nodes, device=dev), torch.arange(len(g.src), device=dev))
+    part = P.partition("rcb", g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+    dom = P.decompose(part, g.src, g.dst, world)[rank]
+    b = partition_batch(g, dom, lab.table, device=dev, transport=transport)
+    no, eo, named = run(b, torch.as_tensor(dom.owned, device=dev), torch.as_tensor(dom.edges, device=dev))
+    errs = {}
+    for (n, p), (_, rp) in zip(named, ref_named):
+        if p.numel() == 0:
+            continue
+        gr = p.grad if p.grad is not None else torch.zeros_like(p)
+        torch.distributed.all_reduce(gr)
+        rg = rp.grad if rp.grad is not None else torch.zeros_like(rp)
+        errs[n] = ((gr - rg).abs().max() / (rg.abs().max() + 1e-6)).item()
+    torch.cuda.synchronize()
+    return no.cpu(), eo.cpu(), errs, kernels.error_status()
+
+
+@pytest.mark.parametrize("transport", ["collective", "peer"])
+def test_partitioned_gpu_matches_unpartitioned(transport):
+    _need(2)
+    out = _dist_util.run(_partition_worker, world=2, backend="nccl", args=(transport,))
+    for r in range(2):
+        _, _, errs, status = out[r]
+        assert status == 0
+        bad = {k: v for k, v in errs.items() if v > 2e-2}
+        assert not bad, (transport, bad)
