@@ -115,8 +115,47 @@ class TrainingWorkflow:
                     num_layers=c["num_mp_layers"], num_distance_basis=c["num_distance_basis"],
                     gaussian_width=c["gaussian_width"], message_type=c["message_type"], open_shell=c["open_shell"])
 
+    def prepare_partitioned(self):
+        """One structure split over the ranks (graph parallel): rank 0 generates it, every rank
+        builds the same partition, keeps its domain, and labels its nodes/edges with the
+        partitioned teacher (reference ``fock_targets_batched.py:231-333``)."""
+        import torch.distributed as dist
+
+        from ..data.targets import Teacher
+        from ..parallel import partition as P
+        from ..parallel.halo import partition_batch
+
+        c = self.config
+        name = c["dataset_name"]
+        kind = name[len("synthetic_"):] if name.startswith("synthetic_") else name
+        labeler = datasets.labeler_for(kind, self.device)
+        obj = [None]
+        if self.rank == 0:
+            obj[0] = datasets.build_samples(kind, 1, seed=c["seed"], cutoff=2 * c["rcut_orbitals"],
+                                            n_atoms=c.get("num_atoms", 20000))[0]
+        if dist.is_initialized():
+            dist.broadcast_object_list(obj, src=0)
+        sample = obj[0]
+        world = self.world_size if dist.is_initialized() else 1
+        part = P.partition(c["partition_type"], sample.num_nodes, world, src=sample.src, dst=sample.dst,
+                           pos=sample.pos, cell=sample.cell)
+        dom = P.decompose(part, sample.src, sample.dst, world)[self.rank if dist.is_initialized() else 0]
+        transport = c.get("halo_transport") or ("peer" if self.device.type == "cuda" and world > 1 else "collective")
+        batch = partition_batch(sample, dom, labeler.table, device=self.device, transport=transport)
+        if c["train_or_eval"] != "infer":
+            teacher = Teacher(self.model_kwargs(labeler.layout.lmax), labeler, device=self.device)
+            with torch.no_grad():
+                no, eo = teacher.head(teacher.backbone(batch), batch)
+            batch.node_y, batch.y = no.detach().clone(), eo.detach().clone()
+        self.labeler = labeler
+        self.val_samples = []
+        self.partition_sample = sample
+        return [batch], [batch], labeler
+
     def prepare_data(self):
         c = self.config
+        if c["distribute_graphs"]:
+            return self.prepare_partitioned()
         name = c["dataset_name"]
         if name.startswith("synthetic_"):
             kind = name[len("synthetic_"):]
@@ -223,6 +262,16 @@ class TrainingWorkflow:
             if c["train_or_eval"] == "eval":
                 return trainer.evaluate(c["test_loss_fxn"], self.device, val, labeler,
                                         output_folder=c["output_folder"], samples=self.val_samples)
+            if c["distribute_graphs"]:
+                b = val[0]
+                s = self.partition_sample
+                e = b.global_edge_ids.cpu().numpy()
+                with torch.no_grad():
+                    no, eo = head(backbone(b), b)
+                from ..parallel.infer import write_partition_hamiltonian
+
+                return write_partition_hamiltonian(c["output_folder"], b, no[0], eo[0], labeler,
+                                                   global_src=s.src[e], global_dst=s.dst[e])
             return trainer.infer(self.device, val[0].to(self.device), labeler, output_folder=c["output_folder"])
         finally:
             self.close()

@@ -105,3 +105,27 @@ def test_partitioned_forward_backward_matches_single_process(pname):
         assert np.allclose(eo, ref_e[edges].numpy(), atol=1e-5, rtol=1e-4)
         for a, b in zip(grads, ref_g):
             assert np.allclose(a, b.numpy(), atol=1e-4, rtol=1e-3)
+
+
+def _workflow_worker(rank, world, folder, mode):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_sio2", num_atoms=150, distribute_graphs=True, partition_type="slab",
+               l_embedding_dim=8, num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.0, rcut_gaussian=4.0,
+               mmax=2, num_epochs=2, lr_init=1e-3, device="cpu", output_folder=folder, train_or_eval=mode,
+               log_every=0, save_frequency=1)
+    return training_workflow.TrainingWorkflow(cfg).run()
+
+
+def test_partitioned_workflow_train_and_infer(tmp_path):
+    out = _dist_util.run(_workflow_worker, world=2, args=(str(tmp_path), "train"))
+    hist = out[0]
+    assert len(hist["train_node"]) == 2 and np.isfinite(hist["train_node"]).all()
+    _dist_util.run(_workflow_worker, world=2, args=(str(tmp_path), "infer"))
+    from maloq_b200.data import datasets
+    from maloq_b200.parallel.infer import load_partitioned_hamiltonian
+
+    H = load_partitioned_hamiltonian(str(tmp_path), datasets.labeler_for("sio2"))
+    dense = H.to_dense()
+    assert dense.shape[0] == 150 * 13
+    assert np.allclose(dense, dense.T, atol=1e-5)
