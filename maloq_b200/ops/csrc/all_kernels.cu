@@ -7,3 +7,4 @@
 #include "edge.cu"
 #include "norm.cu"
 #include "comm.cu"
+#include "misc.cu"

@@ -7,6 +7,7 @@
 #include "comm.h"
 #include "edge.h"
 #include "gemm.h"
+#include "misc.h"
 #include "norm.h"
 #include "runtime.h"
 
@@ -267,6 +268,40 @@ void allreduce_multimem(int64_t mc, int64_t rank, int64_t world, int64_t off, in
   check(maloq::allreduce_multimem(reinterpret_cast<float*>(mc), (int)rank, (int)world, off, n, (float)scale, stream()));
 }
 
+
+void edge_rotation(at::Tensor vec, at::Tensor J, std::vector<int64_t> joff, int64_t L, std::vector<int64_t> row_l,
+                   std::vector<int64_t> row_m, at::Tensor ROT) {
+  TORCH_CHECK(vec.is_cuda() && vec.scalar_type() == at::kFloat && vec.stride(1) == 1, "edge_rotation: fp32 vec [E,3]");
+  chk(J, at::kFloat, "J");
+  chk(ROT, at::kFloat, "ROT");
+  std::vector<int> jo(joff.begin(), joff.end()), rl(row_l.begin(), row_l.end()), rm(row_m.begin(), row_m.end());
+  jo.resize(7, 0);
+  const at::cuda::CUDAGuard guard(vec.device());
+  check(maloq::edge_rotation(vec.data_ptr<float>(), vec.stride(0), J.data_ptr<float>(), jo.data(), (int)L, rl.data(),
+                             rm.data(), (int)rl.size(), ROT.data_ptr<float>(), (int)vec.size(0), stream()));
+}
+
+int64_t fock_loss_grid(int64_t n) { return maloq::fock_loss_grid(n); }
+
+void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, at::Tensor part) {
+  chk(O, at::kFloat, "output");
+  chk(T, at::kFloat, "target");
+  chk(mask, at::kByte, "mask");
+  chk(part, at::kFloat, "part");
+  const at::cuda::CUDAGuard guard(O.device());
+  check(maloq::fock_loss_stats(O.data_ptr<float>(), T.data_ptr<float>(), ll(pt), mask.data_ptr<uint8_t>(),
+                               (int)O.size(1), O.size(0), part.data_ptr<float>(), (int)part.size(0), stream()));
+}
+
+void fock_loss_grad(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, double g_sse, double g_sae,
+                    at::Tensor G) {
+  chk(O, at::kFloat, "output");
+  chk(G, at::kFloat, "grad");
+  const at::cuda::CUDAGuard guard(O.device());
+  check(maloq::fock_loss_grad(O.data_ptr<float>(), T.data_ptr<float>(), ll(pt), mask.data_ptr<uint8_t>(),
+                              (int)O.size(1), O.size(0), (float)g_sse, (float)g_sae, G.data_ptr<float>(), stream()));
+}
+
 int64_t error_status(bool clear) { return maloq::error_status(clear); }
 
 }  // namespace
@@ -293,5 +328,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &peer_barrier);
   m.def("allreduce_p2p", &allreduce_p2p);
   m.def("allreduce_multimem", &allreduce_multimem);
+  m.def("edge_rotation", &edge_rotation);
+  m.def("fock_loss_grid", &fock_loss_grid);
+  m.def("fock_loss_stats", &fock_loss_stats);
+  m.def("fock_loss_grad", &fock_loss_grad);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
 }

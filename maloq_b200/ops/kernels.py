@@ -112,8 +112,7 @@ def linear(x, weight, bias=None, act=None):
 # ------------------------------------------------------------------ ops still on PyTorch glue
 # These run PyTorch on the CUDA tensors until their fused kernels land; each is listed so the
 # set of non-kernel ops is explicit.
-TORCH_GLUE = ("edge_rotation", "fock_head_process", "gather_scale",
-              "matrix_to_labels", "labels_to_matrix", "basis_transform", "fock_loss")
+TORCH_GLUE = ("fock_head_process", "gather_scale", "matrix_to_labels", "labels_to_matrix", "basis_transform")
 
 
 @register("layernorm_silu")
@@ -137,7 +136,6 @@ def rms_norm_sh(x, aw, ab, eps, residual=None):
     return norm_native.rms_norm_sh(x, aw, ab, eps, residual)
 
 
-register("edge_rotation")(_ref.edge_rotation)
 register("gather_scale")(_ref.gather_scale)
 register("fock_head_process")(lambda x, ws, bs, lp, act, sc, ab: _head_process(x, ws, bs, lp, act, sc, ab))
 register("basis_transform")(lambda x, W: torch.matmul(x, W))
@@ -215,11 +213,16 @@ def rotate_back_m0_scatter(e, graph, x_node, scale):
 
 @register("fock_loss")
 def fock_loss(node_out, edge_out, node_t, edge_t, mask_table, node_pt, edge_pt, name):
-    from ..train import loss as L
+    from . import misc_native
 
-    nm = mask_table.index_select(0, node_pt)
-    em = mask_table.index_select(0, edge_pt)
-    return _ref.fock_loss(node_out, edge_out, node_t, edge_t, nm, em, L.get_loss(name))
+    return misc_native.fock_loss(node_out, edge_out, node_t, edge_t, mask_table, node_pt, edge_pt, name)
+
+
+@register("edge_rotation")
+def edge_rotation(vec_yzx, lmax, mmax, Js, mapping):
+    from . import misc_native
+
+    return misc_native.edge_rotation(vec_yzx, lmax, mmax, Js, mapping)
 
 
 def _m2l(data, block_ptr, pair_type, pos_table):
