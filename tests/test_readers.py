@@ -1,0 +1,42 @@
+"""nablaDFT reader (generated mini database), orbital reordering, label round trip."""
+import numpy as np
+import torch
+
+from maloq_b200.data import readers
+from maloq_b200.data.basis_sets import get_basis
+
+
+def test_reorder_is_a_signed_permutation():
+    basis = get_basis("def2_svp_nabla")
+    z = [8, 1, 1]
+    idx, sgn = readers.reorder_indices(z, basis, "aims")
+    assert sorted(idx.tolist()) == list(range(len(idx)))
+    H = np.random.default_rng(0).normal(size=(len(idx), len(idx)))
+    H2 = readers.reorder_orbitals(H, z, basis, "aims")
+    assert np.allclose(np.sort(np.abs(H2).ravel()), np.sort(np.abs(H).ravel()))
+
+
+def test_nabladft_roundtrip(tmp_path):
+    basis = get_basis("def2_svp_nabla")
+    rng = np.random.default_rng(1)
+    mols = []
+    for _ in range(3):
+        z = rng.choice([1, 6, 8], size=5).astype(np.int32)
+        R = rng.uniform(0, 5, size=(5, 3)) / readers.BOHR_TO_ANGSTROM
+        n = sum(sum(2 * l + 1 for l in basis[int(a)]) for a in z)
+        H = rng.normal(size=(n, n))
+        H = H + H.T
+        mols.append((z, R, -1.0, np.zeros((5, 3)), H, np.eye(n), H))
+    path = str(tmp_path / "mini.db")
+    readers.write_nabladft(path, mols)
+    db = readers.NablaDFTDatabase(path)
+    assert len(db) == 3
+    Z, R, E, F, H, S, C = db[1]
+    assert np.allclose(H, mols[1][4].astype(np.float32))
+    samples, lab = readers.load_nabladft(path, {"rcut_orbitals": 10.0, "num_structures": 3})
+    # labels -> blocks reproduces the reordered Hamiltonian on every stored block
+    s = samples[0]
+    bsm = lab.blocks_from_labels(s, s.node_y[0], s.y[0])
+    dense = bsm.to_dense()
+    ref = readers.reorder_orbitals(mols[0][4], mols[0][0], basis, "psi4")
+    assert np.allclose(dense, ref, atol=1e-4)
