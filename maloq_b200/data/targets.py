@@ -63,7 +63,7 @@ class FockLabeler:
         ptr_np = block_pointers(s.z, rows, cols, self.table)
         ptr = torch.as_tensor(ptr_np, device=self.device)
         data = labels_to_matrix(unc, ptr, self._pt(s, rows, cols), self.pos_t, int(ptr_np[-1]))
-        return BlockSparseMatrix(rows, cols, ptr_np, data.cpu().numpy(), orbital_offsets(s.z, self.table))
+        return BlockSparseMatrix(rows, cols, ptr_np, data.detach().cpu().numpy(), orbital_offsets(s.z, self.table))
 
     def symmetrize(self, s: GraphSample, bsm: BlockSparseMatrix) -> BlockSparseMatrix:
         """H_ij <- (H_ij + H_ji^T)/2 for every stored pair (the reverse pair must be stored)."""

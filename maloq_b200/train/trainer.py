@@ -72,11 +72,12 @@ class Prefetcher:
 
 class SplitTrainer:
     def __init__(self, backbone, head, head_irreps, save_frequency=10, run_id=None, run_name="noname",
-                 mask_table=None, grad_sync=None):
+                 mask_table=None, grad_sync=None, nan_guard=False):
         self.backbone, self.head, self.head_irreps = backbone, head, head_irreps
         self.save_frequency, self.run_name = save_frequency, run_name
         self.mask_table = mask_table
         self.grad_sync = grad_sync
+        self.nan_guard = nan_guard
         self.open_shell = getattr(head, "num_spins", 1) > 1
         self.history = {"train_node": [], "train_edge": [], "val_node": [], "val_edge": []}
         self.start_epoch = 0
@@ -102,6 +103,8 @@ class SplitTrainer:
 
     def train_step(self, batch, loss_fxn, optimizer, scheduler=None):
         ln, le, loss = self.forward_loss(batch, loss_fxn)
+        if self.nan_guard and not torch.isfinite(loss).item():
+            raise FloatingPointError(f"non-finite loss {loss.item()} - step skipped (inputs or parameters corrupted)")
         if self.grad_sync is not None:
             self.grad_sync.begin_step()
         loss.backward()

@@ -1,0 +1,81 @@
+"""Failure detection on the host (gloo ranks): a rank that raises, a rank that never joins,
+mismatched batch counts, a non-finite loss.  No GPU is faulted, trapped or hung."""
+import datetime
+import os
+
+import pytest
+import torch
+
+from tests import _dist_util
+
+
+def _raising_worker(rank, world):
+    import torch.distributed as dist
+
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    dist.barrier()
+    return "unreachable"
+
+
+def test_raising_rank_is_reported():
+    with pytest.raises(AssertionError, match="injected failure"):
+        _dist_util.run(_raising_worker, world=2, timeout=60)
+
+
+def test_missing_rank_times_out():
+    import torch.distributed as dist
+
+    store = dist.TCPStore("127.0.0.1", _dist_util.free_port(), 2, True, timeout=datetime.timedelta(seconds=2),
+                          wait_for_workers=False)
+    with pytest.raises(Exception):
+        dist.init_process_group("gloo", store=store, rank=0, world_size=2, timeout=datetime.timedelta(seconds=2))
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def _batch_mismatch_worker(rank, world):
+    from maloq_b200.train.trainer import SplitTrainer
+
+    tr = SplitTrainer(torch.nn.Linear(1, 1), torch.nn.Linear(1, 1), None)
+    try:
+        tr.check_batch_consistency(3 + rank, 2, "cpu")
+    except ValueError as e:
+        return str(e)
+    return "no error"
+
+
+def test_batch_count_mismatch_detected():
+    out = _dist_util.run(_batch_mismatch_worker, world=2)
+    assert all("Mismatch" in v for v in out.values())
+
+
+def test_nan_guard_stops_step():
+    import numpy as np
+
+    from maloq_b200.data import basis_sets, structures
+    from maloq_b200.data.batch import collate, make_sample
+    from maloq_b200.data.targets import FockLabeler
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    lab = FockLabeler(basis_sets.get_basis("split_valence_small"))
+    s = make_sample(structures.random_small_molecule(np.random.default_rng(0)), 5.0)
+    n, e = s.num_nodes, s.num_edges
+    s.node_y = torch.zeros(1, n, lab.target_len)
+    s.y = torch.zeros(1, e, lab.target_len)
+    s.y[0, 0, 0] = float("nan")  # corrupted target
+    b = collate([s], lab.table)
+    kw = dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2, cutoff=5.0, num_layers=1, num_distance_basis=8,
+              edge_channels=8)
+    bb = eSEN_Backbone(lab.irreps, **kw)
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list)
+    tr = SplitTrainer(bb, hd, lab.irreps, mask_table=torch.ones(lab.table.mask.shape, dtype=torch.bool),
+                      nan_guard=True)
+    opt = torch.optim.Adam(list(bb.parameters()) + list(hd.parameters()))
+    before = [p.detach().clone() for p in bb.parameters()]
+    with pytest.raises(FloatingPointError):
+        tr.train_step(b, L.mse_padded_loss, opt)
+    assert all(torch.equal(a, p) for a, p in zip(before, bb.parameters()))

@@ -44,3 +44,20 @@ def test_fused_fock_loss_matches_reference(cuda_device, name):
     gr = torch.autograd.grad(ref[2], [no, eo])
     for a, b in zip(ga, gr):
         assert (a - b).abs().max().item() <= 1e-5 * b.abs().max().item() + 1e-9
+
+
+def test_peer_barrier_timeout_reports_error_and_context_survives(cuda_device):
+    """A peer that never arrives: the bounded wait gives up, records ERR_PEER_WAIT (4), and the
+    CUDA context stays usable.  Both "ranks'" signal pads are local memory of this GPU."""
+    from maloq_b200.ops import kernels
+
+    lib = kernels.lib()
+    kernels.error_status(True)
+    pads = torch.zeros(2, 8, dtype=torch.int32, device=cuda_device)
+    ptrs = torch.tensor([pads[0].data_ptr(), pads[1].data_ptr()], dtype=torch.int64, device=cuda_device)
+    lib.peer_barrier(ptrs.data_ptr(), 0, 2, 1, 0, 2000)  # rank 0 of 2; rank 1 never signals
+    torch.cuda.synchronize()
+    assert kernels.error_status(True) == 4
+    assert pads[1, 0].item() == 1  # rank 0 did signal its peer slot
+    assert torch.ones(3, device=cuda_device).sum().item() == 3
+    assert kernels.error_status() == 0

@@ -1,0 +1,132 @@
+"""Heads (reduce_edge, open shell, energy, forces), checkpoint resume, optimizers."""
+import numpy as np
+import pytest
+import torch
+
+from maloq_b200.core import sph
+from maloq_b200.data import basis_sets, structures
+from maloq_b200.data.batch import collate, make_sample
+from maloq_b200.data.targets import FockLabeler
+from maloq_b200.models.backbone import eSEN_Backbone
+from maloq_b200.models.heads import Fock_Irreps_Head, HELM_Energy_Head, HELM_Force_Head
+
+P = np.array([[0.0, 1.0, 0.0], [0.0, 0.0, 1.0], [1.0, 0.0, 0.0]])
+KW = dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2, cutoff=5.0, num_layers=2, num_distance_basis=8,
+          edge_channels=8)
+
+
+def _batches(R_in, dtype=torch.float64, include_edges=True):
+    rng = np.random.default_rng(3)
+    structs = [structures.random_small_molecule(rng) for _ in range(2)]
+    lab = FockLabeler(basis_sets.get_basis("split_valence_small"), dtype=dtype)
+    out = [make_sample(structures.Structure(s.z, s.pos @ R_in.T), 5.0) for s in structs]
+    return collate(out, lab.table, float_dtype=dtype), lab
+
+
+def test_reduce_edge_head_equivariant_and_symmetric():
+    R_in = sph.euler_matrix(0.3, 1.2, -0.5)
+    Dm = P @ R_in @ P.T
+    b0, lab = _batches(np.eye(3))
+    b1, _ = _batches(R_in)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, **KW).double()
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list, reduce_node=True,
+                          reduce_node_intra=True, reduce_edge=True).double()
+    n0, e0 = hd(bb(b0), b0)
+    n1, e1 = hd(bb(b1), b1)
+    Dl = torch.block_diag(*[torch.tensor(sph.wigner_D_from_matrix(it.l, Dm)) for it in lab.irreps])
+    assert (e0[0] @ Dl.T - e1[0]).abs().max() < 1e-8
+    assert (n0[0] @ Dl.T - n1[0]).abs().max() < 1e-8
+    # the reconstructed (i,j) and (j,i) blocks are transposes of each other
+    s = b0
+    blocks = lab.blocks_from_labels(_sample_of(s, 0, lab), n0[0][: int(s.num_atoms_in_molecule[0])],
+                                    e0[0][: _n_edges(s, 0)])
+    H = blocks.to_dense()
+    assert np.allclose(H, H.T, atol=1e-8)
+
+
+def _n_edges(b, g):
+    nat = b.num_atoms_in_molecule.tolist()
+    dst = b.edge_index[1].numpy()
+    return int((dst < nat[0]).sum()) if g == 0 else None
+
+
+def _sample_of(b, g, lab):
+    from maloq_b200.data.batch import GraphSample
+
+    n = int(b.num_atoms_in_molecule[0])
+    ne = _n_edges(b, 0)
+    ei = b.edge_index[:, :ne].numpy()
+    return GraphSample(b.atomic_numbers[:n].numpy(), b.pos[:n].numpy(), ei[0], ei[1], b.edge_attr[:ne].numpy())
+
+
+def test_open_shell_head_outputs_two_spins():
+    b, lab = _batches(np.eye(3), torch.float32)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, open_shell=True, **KW)
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list, open_shell=True,
+                          reduce_node=True, reduce_node_intra=True)
+    n, e = hd(bb(b), b)
+    assert n.shape[0] == 2 and e.shape[0] == 2 and not torch.allclose(n[0], n[1])
+
+
+def test_energy_invariant_and_forces_equivariant():
+    R_in = sph.euler_matrix(-0.7, 0.4, 2.0)
+    Rm = P @ R_in @ P.T
+    b0, lab = _batches(np.eye(3))
+    b1, _ = _batches(R_in)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, include_edges=False, **KW).double()
+    eh = HELM_Energy_Head(bb).double()
+    fh = HELM_Force_Head(bb).double()
+    e0, e1 = eh(bb(b0), b0)["energies"], eh(bb(b1), b1)["energies"]
+    assert e0.shape == (2,) and torch.allclose(e0, e1, atol=1e-9)
+    f0, f1 = fh(bb(b0), b0)["forces"], fh(bb(b1), b1)["forces"]
+    D1 = torch.tensor(sph.wigner_D_from_matrix(1, Rm))
+    assert torch.allclose(f0 @ D1.T, f1, atol=1e-9)
+
+
+def test_checkpoint_resume_continues(tmp_path):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=12, batch_size=6, num_epochs=2, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               output_folder=str(tmp_path), device="cpu", save_frequency=1, log_every=0)
+    h1 = training_workflow.TrainingWorkflow(cfg).run()
+    sd1 = torch.load(tmp_path / "backbone.pt", weights_only=False)["model_state_dict"]
+    cfg2 = dict(cfg, num_epochs=3, restart_backbone=True, restart_head=True, restart_optimizer=True)
+    h2 = training_workflow.TrainingWorkflow(cfg2).run()
+    assert len(h2["train_node"]) == 3 and h2["train_node"][:2] == h1["train_node"]
+    sd2 = torch.load(tmp_path / "backbone.pt", weights_only=False)["model_state_dict"]
+    assert any(not torch.equal(sd1[k], sd2[k]) for k in sd1 if sd1[k].is_floating_point())
+
+
+@pytest.mark.parametrize("opt", ["adam", "adamw", "muon"])
+def test_optimizers_reduce_loss(tmp_path, opt):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=10, batch_size=5, num_epochs=4, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2, lr_init=3e-3,
+               muon_lr=0.01, optimizer_type=opt, output_folder=str(tmp_path), device="cpu", log_every=0,
+               scheduler_type="plateau")
+    h = training_workflow.TrainingWorkflow(cfg).run()
+    assert h["train_node"][-1] < h["train_node"][0]
+
+
+def test_state_dict_keys_follow_reference_layout():
+    _, lab = _batches(np.eye(3), torch.float32)
+    bb = eSEN_Backbone(lab.irreps, **KW)
+    keys = set(bb.state_dict())
+    for k in ["Jd_0", "Jd_4", "distance_expansion.offset", "sphere_embedding.weight", "scalar_node_embedding.bias",
+              "edge_degree_embedding.rad_func.net.6.weight", "node_blocks.0.norm_1.affine_weight",
+              "node_blocks.0.norm_1.balance_degree_weight", "node_blocks.0.edge_wise.act.expand_index",
+              "node_blocks.0.edge_wise.so2_conv_1.fc_m0.weight", "node_blocks.0.edge_wise.so2_conv_1.so2_m_conv.1.fc.weight",
+              "node_blocks.0.edge_wise.so2_conv_1.rad_func.net.4.bias", "node_blocks.1.atom_wise.so3_linear_2.expand_index",
+              "edge_blocks.1.atom_wise.scalar_mlp.0.weight", "norm.affine_bias"]:
+        assert k in keys, k
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list, reduce_node=True,
+                          reduce_node_intra=True)
+    hk = set(hd.state_dict())
+    for k in ["parity_multiplier", "lin_scalars_learnable.0.weight", "node_lin_out_layers.0.2.weight",
+              "edge_lin_out_layers.0.4.weight"]:
+        assert k in hk, k
