@@ -16,6 +16,7 @@
 // Two TMEM accumulators (2 x BN fp32 columns) let a tile's epilogue overlap the next tile's
 // MMAs.  TMA loads use no multicast.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -27,6 +28,7 @@ namespace maloq {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+constexpr int STAGE_WARP_BYTES = 16384;  // epilogue staging per epilogue warp
 
 struct alignas(64) GemmProblemDev {
   CUtensorMap ta;
@@ -45,6 +47,7 @@ struct alignas(64) GemmProblemDev {
 struct GemmParamsDev {
   GemmProblemDev p[8];
   int nprob;
+  int skip_store;  // diagnostics: epilogue reads TMEM but stores nothing
   int out_fp32;
   int act;
   float alpha;
@@ -55,7 +58,30 @@ struct TileCoord {
   int pi, m0, n0, split;
 };
 
-__device__ __forceinline__ TileCoord decode_tile(const GemmParamsDev& P, int w, int tiles_per_split, int BN) {
+// Epilogue scalars of one work item, copied out of the parameter block into registers once
+// per tile (reading them through a reference into the grid-constant block inside the chunk
+// loop costs a parameter-window load per use).
+struct EpiScalars {
+  const float* bias;
+  float alpha;
+  int act, N, M;
+};
+
+// v[j] (column col0 + j of this lane's row) = act(alpha * v[j] + bias[col0 + j]); lane j loads
+// bias[col0 + j] and the row's 32 values are broadcast by shuffles.
+__device__ __forceinline__ void epilogue_math(float* v, float alpha, const EpiScalars& ep, int col0, int lane) {
+  float b = 0.f;
+  if (ep.bias != nullptr && col0 + lane < ep.N) b = __ldg(ep.bias + col0 + lane);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = v[j] * alpha + __shfl_sync(0xffffffffu, b, j);
+  if (ep.act == 1) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu(v[j]);
+  }
+}
+
+__device__ __forceinline__ TileCoord decode_tile(const GemmParamsDev& P, int w, int tiles_per_split, int BN,
+                                                 int bm = BM) {
   TileCoord tc;
   tc.split = w / tiles_per_split;
   int t = w - tc.split * tiles_per_split;
@@ -65,7 +91,7 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParamsDev& P, int w, 
     if (t >= P.p[q].tile_begin) pi = q;
   t -= P.p[pi].tile_begin;
   tc.pi = pi;
-  tc.m0 = (t / P.p[pi].tiles_n) * BM;
+  tc.m0 = (t / P.p[pi].tiles_n) * bm;
   tc.n0 = (t % P.p[pi].tiles_n) * BN;
   return tc;
 }
@@ -89,7 +115,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   uint64_t* acc_full = empty + STAGES;  // [2] MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (4 arrivals: one per epilogue warp)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  // epilogue staging: 4 warps x 2 buffers x 32 x 32 x 4 bytes, 1024-aligned
+  // epilogue staging: 4 warps x STAGE_WARP_BYTES, 1024-aligned
   uint8_t* stage_out = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 1023) & ~uintptr_t(1023));
 
@@ -197,10 +223,12 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   } else {
     // ---------------- epilogue warps 2..5
     const int quarter = warp & 3;
+    const bool out32 = P.out_fp32 != 0, skip = P.skip_store != 0;
     int it = 0, sbuf = 0;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++it) {
       const TileCoord tc = decode_tile(P, w, tiles_per_split, BN);
       const GemmProblemDev& pr = P.p[tc.pi];
+      const EpiScalars ep{pr.bias, P.alpha, P.act, pr.N, pr.M};
       const int k_begin = tc.split * pr.k_per_split;
       const bool have_k = min(pr.K, k_begin + pr.k_per_split) > k_begin;
       const int buf = it & 1;
@@ -217,19 +245,18 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
         const int col0 = tc.n0 + c0;
-        if (col0 >= pr.N) continue;  // warp-uniform
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float x = have_k ? v[j] * P.alpha : 0.f;
-          if (pr.bias != nullptr && col0 + j < pr.N) x += __ldg(pr.bias + col0 + j);
-          if (P.act == 1) x = silu(x);
-          v[j] = x;
-        }
+        if (col0 >= ep.N || skip) continue;  // warp-uniform
+        epilogue_math(v, have_k ? ep.alpha : 0.f, ep, col0, lane);
         // stage the warp's 32 x 32 chunk (row-major, 32*esz bytes per row) and TMA-store it
-        uint8_t* stg = stage_out + ((quarter * 2 + (sbuf & 1)) * 32 * 32 * 4);
-        if (lane == 0) bulk_wait_read<1>();  // the buffer used two stores ago is free again
+        // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
+        const int ring = out32 ? 4 : 8;
+        uint8_t* stg = stage_out + quarter * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
+        if (lane == 0) {
+          if (out32) bulk_wait_read<3>();  // the chunk stored `ring` chunks ago has been read
+          else bulk_wait_read<7>();
+        }
         __syncwarp();
-        if (P.out_fp32) {
+        if (out32) {
           // 128B-swizzled staging: 16B chunk j of row r lives at chunk j ^ (r & 7)
           float4* dst = reinterpret_cast<float4*>(stg + lane * 128);
 #pragma unroll
@@ -247,7 +274,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         }
         fence_async_shared();
         __syncwarp();
-        if (lane == 0 && tc.m0 + quarter * 32 < pr.M) {
+        if (lane == 0 && tc.m0 + quarter * 32 < ep.M) {
           tma_store_3d(&pr.tc, stg, col0, tc.m0 + quarter * 32, tc.split);
           bulk_commit();
         }
@@ -260,6 +287,186 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ======================================================================= 2-SM variant
+// A CTA pair (cluster of 2) computes a 256 x BN tile with tcgen05.mma.cta_group::2: CTA r
+// loads rows [m0 + 128 r, +128) of A and rows [n0 + r BN/2, +BN/2) of B into its own shared
+// memory; the leader (r = 0) issues the M = 256 MMAs, which read both CTAs' shared memory and
+// write rows 128 r.. of the accumulator into CTA r's TMEM.  Per SM this halves the B bytes per
+// FLOP relative to the 1-SM kernel.  K-major operands only; no split-K.
+// Barriers: full[s] lives in the leader (both CTAs' TMA loads complete on it); empty[s] and
+// acc_full[b] exist in both CTAs and are signalled by two commits from the leader; acc_empty[b]
+// lives in the leader and collects 8 arrivals (4 epilogue warps per CTA).
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant__ GemmParamsDev P, int total_work) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int A_BYTES = 128 * BK * 2;
+  constexpr int B_BYTES = (BN / 2) * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint8_t* stage_out = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t crank = cluster_ctarank();
+  const int cluster = blockIdx.x / 2, nclusters = gridDim.x / 2;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 0) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+  if (warp == 0 && lane == 0) {
+    for (int q = 0; q < P.nprob; ++q) {
+      prefetch_tmap(&P.p[q].ta);
+      prefetch_tmap(&P.p[q].tb);
+    }
+  }
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    if (elect_one()) {
+      int kc = 0;
+      for (int w = cluster; w < total_work && ok; w += nclusters) {
+        const TileCoord tc = decode_tile(P, w, total_work, BN, 256);
+        const GemmProblemDev& pr = P.p[tc.pi];
+        const int k_tiles = (pr.K + BK - 1) / BK;
+        for (int kt = 0; kt < k_tiles; ++kt, ++kc) {
+          const int s = kc % STAGES;
+          if (kc >= STAGES && !mbar_wait(&empty[s], ((kc / STAGES) - 1) & 1, ERR_TMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          const uint32_t leader_full = mapa_shared(smem_u32(&full[s]), 0);
+          if (crank == 0) mbar_arrive_expect_tx(&full[s], 2 * (A_BYTES + B_BYTES));
+          const int k = kt * BK;
+          tma_load_2d_pair(sA + s * A_BYTES, &pr.ta, leader_full, k, tc.m0 + 128 * (int)crank);
+          tma_load_2d_pair(sB + s * B_BYTES, &pr.tb, leader_full, k, tc.n0 + (BN / 2) * (int)crank);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only)
+    if (crank == 0 && elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16(256, BN, 0, 0);
+      const uint32_t empty0 = mapa_shared(smem_u32(&empty[0]), 0), empty1 = mapa_shared(smem_u32(&empty[0]), 1);
+      const uint32_t accf0 = mapa_shared(smem_u32(&acc_full[0]), 0), accf1 = mapa_shared(smem_u32(&acc_full[0]), 1);
+      int kc = 0, it = 0;
+      for (int w = cluster; w < total_work && ok; w += nclusters, ++it) {
+        const TileCoord tc = decode_tile(P, w, total_work, BN, 256);
+        const GemmProblemDev& pr = P.p[tc.pi];
+        const int k_tiles = (pr.K + BK - 1) / BK;
+        const int buf = it & 1;
+        if (it >= 2 && !mbar_wait(&acc_empty[buf], ((it >> 1) - 1) & 1, ERR_MMA_WAIT)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kt = 0; kt < k_tiles; ++kt, ++kc) {
+          const int s = kc % STAGES;
+          if (!mbar_wait(&full[s], (kc / STAGES) & 1, ERR_MMA_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sA + s * A_BYTES);
+          const uint32_t b = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_f16_pair(d, sw128_desc(a + kk * 32, 16, 1024), sw128_desc(b + kk * 32, 16, 1024), idesc,
+                          (kt > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(empty0 + s * 8);
+          umma_commit_pair(empty1 + s * 8);
+        }
+        if (!ok) break;
+        umma_commit_pair(accf0 + buf * 8);
+        umma_commit_pair(accf1 + buf * 8);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 (both CTAs; rows 128 * crank + ...)
+    const int quarter = warp & 3;
+    const bool out32 = P.out_fp32 != 0, skip = P.skip_store != 0;
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int it = 0, sbuf = 0;
+    for (int w = cluster; w < total_work; w += nclusters, ++it) {
+      const TileCoord tc = decode_tile(P, w, total_work, BN, 256);
+      const GemmProblemDev& pr = P.p[tc.pi];
+      const EpiScalars ep{pr.bias, P.alpha, P.act, pr.N, pr.M};
+      const int buf = it & 1;
+      if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, ERR_EPI_WAIT)) break;
+      tc_fence_after();
+      const int row0 = tc.m0 + 128 * (int)crank + quarter * 32;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c0), v);
+        if (c0 + 32 >= BN) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8);
+        }
+        const int col0 = tc.n0 + c0;
+        if (col0 >= ep.N || skip) continue;
+        epilogue_math(v, ep.alpha, ep, col0, lane);
+        // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
+        const int ring = out32 ? 4 : 8;
+        uint8_t* stg = stage_out + quarter * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
+        if (lane == 0) {
+          if (out32) bulk_wait_read<3>();  // the chunk stored `ring` chunks ago has been read
+          else bulk_wait_read<7>();
+        }
+        __syncwarp();
+        if (out32) {
+          float4* dst = reinterpret_cast<float4*>(stg + lane * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[j ^ (lane & 7)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(stg + lane * 64);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 h[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
+            dst[j ^ ((lane >> 1) & 3)] = *reinterpret_cast<uint4*>(h);
+          }
+        }
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0 && row0 < ep.M) {
+          tma_store_3d(&pr.tc, stg, col0, row0, 0);
+          bulk_commit();
+        }
+        ++sbuf;
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 0) tmem_dealloc_pair(tmem, TMEM_COLS);
 }
 
 // Sum split-K partials [S][n] (stride between splits `stride`) into out, fixed order.
@@ -337,7 +544,7 @@ static const char* make_out_map(CUtensorMap* m, void* base, long long M, long lo
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaStream_t st) {
-  constexpr int smem = STAGES * (BM * BK + BN * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 + 4 * 2 * 32 * 32 * 4;
+  constexpr int smem = STAGES * (BM * BK + BN * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 + 4 * STAGE_WARP_BYTES;
   auto k = gemm_tc_kernel<BN, STAGES, A_MN, B_MN>;
   static bool init = false;  // per process; the attribute applies to every device
   if (!init) {
@@ -359,6 +566,46 @@ static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaS
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
 
+template <int BN, int STAGES>
+static const char* launch_2sm(const GemmParamsDev& P, int total, cudaStream_t st) {
+  constexpr int smem = STAGES * (128 * BK + (BN / 2) * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 +
+                       4 * STAGE_WARP_BYTES;
+  auto k = gemm_tc2_kernel<BN, STAGES>;
+  static bool init = false;
+  if (!init) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return "cudaFuncSetAttribute (2-SM) failed";
+    init = true;
+  }
+  static int num_sms = 0;
+  if (num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (num_sms <= 1) num_sms = 148;
+  }
+  int clusters = num_sms / 2;
+  if (total < clusters) clusters = total;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k, P, total);
+  if (e != cudaSuccess) return cudaGetErrorString(e);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
+}
+
+static int g_use_2sm = -1;  // -1: read MALOQ_GEMM_2SM once (default on)
+
 const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_mn, bool out_fp32, int act,
                         float alpha, int splits, int bn, cudaStream_t stream) {
   if (nprob < 1 || nprob > 8) return "gemm: 1..8 problems per launch";
@@ -368,6 +615,7 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
   GemmParamsDev P;
   memset(&P, 0, sizeof(P));
   P.nprob = nprob;
+  P.skip_store = getenv("MALOQ_GEMM_SKIP_STORE") != nullptr;
   P.act = act;
   P.alpha = alpha;
   P.out_fp32 = out_fp32 ? 1 : 0;
@@ -394,14 +642,32 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
     tiles += ((g.M + BM - 1) / BM) * d.tiles_n;
   }
   if (tiles == 0) return nullptr;
-  if (!a_mn) {
-    if (bn == 256) return launch_t<256, 4, false, false>(P, tiles, splits, stream);
-    if (bn == 128) return launch_t<128, 6, false, false>(P, tiles, splits, stream);
-    return launch_t<64, 8, false, false>(P, tiles, splits, stream);
+  if (g_use_2sm < 0) {
+    const char* env = getenv("MALOQ_GEMM_2SM");
+    g_use_2sm = (env && env[0] == '0') ? 0 : 1;
   }
-  if (bn == 256) return launch_t<256, 4, true, true>(P, tiles, splits, stream);
-  if (bn == 128) return launch_t<128, 6, true, true>(P, tiles, splits, stream);
-  return launch_t<64, 8, true, true>(P, tiles, splits, stream);
+  if (!a_mn && splits == 1 && g_use_2sm && (bn == 256 || bn == 128)) {
+    // re-tile with 256-row pair tiles; the B box is BN/2 rows per CTA
+    int total = 0;
+    for (int i = 0; i < nprob; ++i) {
+      GemmProblemDev& d = P.p[i];
+      const GemmProblem& g = probs[i];
+      const char* err = make_map(&d.tb, g.b, g.N, g.K, g.ldb, bn / 2);
+      if (err) return err;
+      d.tile_begin = total;
+      total += ((g.M + 255) / 256) * d.tiles_n;
+    }
+    if (bn == 256) return launch_2sm<256, 4>(P, total, stream);
+    return launch_2sm<128, 6>(P, total, stream);
+  }
+  if (!a_mn) {
+    if (bn == 256) return launch_t<256, 3, false, false>(P, tiles, splits, stream);
+    if (bn == 128) return launch_t<128, 4, false, false>(P, tiles, splits, stream);
+    return launch_t<64, 6, false, false>(P, tiles, splits, stream);
+  }
+  if (bn == 256) return launch_t<256, 3, true, true>(P, tiles, splits, stream);
+  if (bn == 128) return launch_t<128, 4, true, true>(P, tiles, splits, stream);
+  return launch_t<64, 6, true, true>(P, tiles, splits, stream);
 }
 
 const char* gemm_splitk_reduce(const float* part, float* out, long long n, int splits, long long stride, float beta,

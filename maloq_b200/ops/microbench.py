@@ -47,6 +47,18 @@ def bench_gemm(edges, bn):
     print(f"gemm bn={bn}: {ms * 1e3:.1f} us, {fl / ms / 1e9:.1f} TFLOP/s, error_status={kernels.error_status()}")
 
 
+def bench_gemm_shape(M, N, K, bn, out_fp32=False):
+    from . import kernels
+
+    lib = kernels.lib()
+    dev = torch.device("cuda", 0)
+    A = torch.randn(M, K, device=dev).bfloat16()
+    W = torch.randn(N, K, device=dev).bfloat16()
+    C = torch.empty(M, N, device=dev, dtype=torch.float32 if out_fp32 else torch.bfloat16)
+    ms = _timeit(lambda: lib.gemm([A], [W], [C], [None], False, 0, 1.0, 1, bn))
+    print(f"gemm M={M} N={N} K={K} bn={bn}: {ms * 1e3:.1f} us, {2 * M * N * K / ms / 1e9:.1f} TFLOP/s")
+
+
 def bench_edge(edges):
     from . import kernels
 
@@ -74,11 +86,17 @@ def bench_edge(edges):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "edge"])
+    ap.add_argument("what", choices=["gemm", "edge", "shape"])
+    ap.add_argument("--M", type=int, default=32768)
+    ap.add_argument("--N", type=int, default=1024)
+    ap.add_argument("--K", type=int, default=1024)
+    ap.add_argument("--fp32-out", action="store_true")
     ap.add_argument("--bn", type=int, default=128)
     ap.add_argument("--edges", type=int, default=43408)
     a = ap.parse_args(argv)
-    if a.what == "gemm":
+    if a.what == "shape":
+        bench_gemm_shape(a.M, a.N, a.K, a.bn, a.fp32_out)
+    elif a.what == "gemm":
         bench_gemm(a.edges, a.bn)
     else:
         bench_edge(a.edges)
