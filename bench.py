@@ -26,6 +26,11 @@ import time
 HERE = os.path.dirname(os.path.abspath(__file__))
 BASELINE_VALUE = None  # BASELINE.json publishes no number for this metric
 METRIC = "train graphs/s (drug-like DP, device-timed, max over ranks)"
+CONFIGS = {
+    # name: (dataset kind, mmax, default layers, molecules per batch or None, atoms per batch cap)
+    "druglike": ("druglike", 2, 6, 32, None),
+    "large": ("large", 2, 8, None, 4096),
+}
 
 
 def parse():
@@ -39,7 +44,13 @@ def parse():
     ap.add_argument("--channels", type=int, default=128)
     ap.add_argument("--n-batches", type=int, default=4, help="distinct batches cycled per rank")
     ap.add_argument("--grad-sync", default=None)
+    ap.add_argument("--config", default="druglike", choices=list(CONFIGS),
+                    help="druglike (headline) or large (10-150 atoms, lmax 6, 8 layers, <=4096 atoms/GPU)")
     return ap.parse_args()
+
+
+def labeler_name(kind):
+    return {"druglike": "def2-SVP-like", "large": "def2-TZVP-like"}.get(kind, kind)
 
 
 def reference_arm(args):
@@ -127,22 +138,33 @@ def main():
         ops.use_torch_ops(True)
     torch.manual_seed(0)
 
-    kind = "druglike"
+    kind, mmax, def_layers, per_batch, atom_cap = CONFIGS[args.config]
+    if args.config != "druglike" and args.layers == 6:
+        args.layers = def_layers
     labeler = datasets.labeler_for(kind, device)
     lmax = labeler.layout.lmax
-    kw = dict(sphere_channels=args.channels, hidden_channels=args.channels, lmax=lmax, mmax=2, cutoff=6.0,
+    kw = dict(sphere_channels=args.channels, hidden_channels=args.channels, lmax=lmax, mmax=mmax, cutoff=6.0,
               edge_channels=args.channels, num_layers=args.layers, num_distance_basis=128)
     t0 = time.time()
-    samples, _ = datasets.build_dataset(kind, args.batch * args.n_batches, kw, seed=1000 + rank, device=device,
-                                        labeler=labeler)
-    host_batches = [B.collate(g, labeler.table).pin_memory() for g in B.batches_by_count(samples, args.batch)]
+    if per_batch is not None:
+        n_mol = args.batch * args.n_batches
+    else:  # atom-capped batches: enough molecules (mean 80 atoms) for n_batches full batches
+        n_mol = args.n_batches * atom_cap // 80
+    samples, _ = datasets.build_dataset(kind, n_mol, kw, seed=1000 + rank, device=device, labeler=labeler)
+    groups = B.batches_by_count(samples, args.batch) if per_batch is not None else \
+        B.batches_by_atoms(samples, atom_cap)[:args.n_batches]
+    host_batches = [B.collate(g, labeler.table).pin_memory() for g in groups]
+    graphs_per_batch = [len(g) for g in groups]
     dev_batches = [b.to(device) for b in host_batches]
     n_edges = sum(b.num_edges for b in host_batches) / len(host_batches)
     n_nodes = sum(b.num_nodes for b in host_batches) / len(host_batches)
     t_data = time.time() - t0
 
     torch.manual_seed(1)
-    backbone = eSEN_Backbone(labeler.irreps, include_edges=True, **kw).to(device)
+    # the large config's 8 layers of edge activations (~260k edges, lmax 6) exceed device memory
+    # without recompute: each block is recomputed in backward
+    backbone = eSEN_Backbone(labeler.irreps, include_edges=True, activation_checkpointing=args.config == "large",
+                             **kw).to(device)
     head = Fock_Irreps_Head(None, labeler.irreps, lmax=lmax, sphere_channels=args.channels,
                             ls_list=labeler.layout.ls_list, reduce_node=True, reduce_node_intra=True).to(device)
     params = list(backbone.parameters()) + list(head.parameters())
@@ -194,26 +216,29 @@ def main():
     barrier()
     clk = clocks.stop()
     e2e_ms = e2e_start.elapsed_time(e2e_end)
-    h2d = sum(v.numel() * v.element_size() for v in host_batches[0].tensors().values())
+    nbytes = [sum(v.numel() * v.element_size() for v in hb.tensors().values()) for hb in host_batches]
+    h2d = sum(nbytes[i % len(nbytes)] for i in range(args.steps)) / args.steps
 
     t = torch.tensor([ms, e2e_ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
     ms_step = ms / args.steps
-    graphs = args.batch * world
+    # graphs per step on this rank, averaged over the timed steps (batches cycle); weak scaling
+    graphs = world * sum(graphs_per_batch[i % len(graphs_per_batch)] for i in range(args.steps)) / args.steps
     value = graphs / (ms_step / 1e3)
     e2e_value = graphs / (e2e_ms / args.steps / 1e3)
     if rank == 0:
         out = {
-            "metric": METRIC, "value": round(value, 2), "unit": "graphs/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if args.config == "druglike" else
+            "train graphs/s (large molecules DP, device-timed, max over ranks)", "value": round(value, 2), "unit": "graphs/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
             "dtype": "bf16" if args.impl == "native" else "fp32",
-            "data": "synthetic (random drug-like molecules, frozen random-init teacher targets; random-init weights)",
-            "config": {"model": f"eSEN lmax={lmax} mmax=2 C={args.channels} layers={args.layers} + Fock head "
-                                f"(def2-SVP-like, D={labeler.target_len})",
-                       "global_batch": graphs, "seq_len": None, "parallelism": f"dp{world}",
+            "data": f"synthetic (random {kind} molecules, frozen random-init teacher targets; random-init weights)",
+            "config": {"model": f"eSEN lmax={lmax} mmax={mmax} C={args.channels} layers={args.layers} + Fock head "
+                                f"({labeler_name(kind)}, D={labeler.target_len})",
+                       "global_batch": round(graphs, 2), "atoms_cap_per_gpu": atom_cap, "seq_len": None, "parallelism": f"dp{world}",
                        "edges_per_gpu_step": round(n_edges), "atoms_per_gpu_step": round(n_nodes),
                        "l2": "256 MiB buffer written between timed steps, outside the step events",
                        "impl": args.impl, "grad_sync": None if sync is None else sync.mode,
@@ -224,6 +249,8 @@ def main():
             "gpu_launches": int(launches),
             "clocks": clk,
             "final_loss": loss_vals[-1],
+            "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 2**30, 2),
+            "activation_checkpointing": backbone.activation_checkpointing,
             "setup_s": round(t_data, 1),
         }
         print(json.dumps(out), flush=True)

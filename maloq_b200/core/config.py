@@ -56,6 +56,7 @@ class SplitConfig(_Section):
 
 class ModelConfig(_Section):
     wigner_backend: str = "cuda"
+    activation_checkpointing: bool = False
     l_embedding_dim: int = 128
     num_distance_basis: int = 128
     num_mp_layers: int = 3

@@ -153,8 +153,12 @@ class eSEN_Backbone(nn.Module):
                  edge_channels=128, distance_function="gaussian", num_distance_basis=512, num_layers=2,
                  hidden_channels=128, norm_type="rms_norm_sh", act_type="gate", mlp_type="spectral",
                  gaussian_width=1.0, include_edges=True, open_shell=False, wigner_backend="cuda",
-                 distributed_graph_training=False, message_type="source-target", **unused):
+                 distributed_graph_training=False, message_type="source-target", activation_checkpointing=False,
+                 **unused):
         super().__init__()
+        # recompute each block's forward during backward (saves only the block inputs); needed
+        # for graphs whose per-layer edge activations exceed device memory
+        self.activation_checkpointing = bool(activation_checkpointing)
         if act_type != "gate" or mlp_type != "spectral":
             raise ValueError("only act_type='gate' and mlp_type='spectral' are implemented (as in the reference)")
         self.max_num_elements, self.lmax, self.mmax = max_num_elements, lmax, mmax
@@ -224,10 +228,11 @@ class eSEN_Backbone(nn.Module):
         x_edge = torch.cat([self.source_embedding(batch.src_z), gauss, self.target_embedding(batch.dst_z)], dim=1)
         x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
         x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
+        ckpt = self.activation_checkpointing and torch.is_grad_enabled()
         for i in range(self.num_layers):
-            x_node = self.node_blocks[i](x_node, x_edge_emb, x_edge, graph)
+            x_node = self._run_block(self.node_blocks[i], ckpt, x_node, x_edge_emb, x_edge, graph)
             if self.include_edges:
-                x_edge_emb = self.edge_blocks[i](x_node, x_edge_emb, x_edge, graph)
+                x_edge_emb = self._run_block(self.edge_blocks[i], ckpt, x_node, x_edge_emb, x_edge, graph)
         x_node = self.norm(x_node)
         out = {"node_embeddings": x_node, "edge_index": batch.edge_index, "edge_distance": dist,
                "edge_distance_vec": batch.edge_attr[:, [2, 3, 1]], "partition": getattr(batch, "halo", None)}
@@ -236,6 +241,14 @@ class eSEN_Backbone(nn.Module):
         else:
             out.update({"x_edge": x_edge, "graph": graph})
         return out
+
+    @staticmethod
+    def _run_block(block, ckpt, x_node, x_edge_emb, x_edge, graph):
+        if not ckpt:
+            return block(x_node, x_edge_emb, x_edge, graph)
+        from torch.utils.checkpoint import checkpoint
+
+        return checkpoint(block, x_node, x_edge_emb, x_edge, graph, use_reentrant=False)
 
     @property
     def num_params(self):

@@ -85,6 +85,7 @@ class TrainingWorkflow:
         if c.get("hidden_dim") is None:
             c["hidden_dim"] = c["l_embedding_dim"]
         c.setdefault("message_type", "source-target")
+        c.setdefault("activation_checkpointing", False)
         c.setdefault("basis_transform_backend", "cuda")
         if c["distribute_graphs"] and c["partition_type"] is None:
             c["partition_type"] = "slab"
@@ -113,7 +114,8 @@ class TrainingWorkflow:
         return dict(sphere_channels=c["l_embedding_dim"], hidden_channels=c["hidden_dim"], lmax=lmax,
                     mmax=min(mmax, lmax), cutoff=c["rcut_gaussian"], edge_channels=c["l_embedding_dim"],
                     num_layers=c["num_mp_layers"], num_distance_basis=c["num_distance_basis"],
-                    gaussian_width=c["gaussian_width"], message_type=c["message_type"], open_shell=c["open_shell"])
+                    gaussian_width=c["gaussian_width"], message_type=c["message_type"], open_shell=c["open_shell"],
+                    activation_checkpointing=c["activation_checkpointing"])
 
     def prepare_partitioned(self):
         """One structure split over the ranks (graph parallel): rank 0 generates it, every rank

@@ -130,3 +130,17 @@ def test_state_dict_keys_follow_reference_layout():
     for k in ["parity_multiplier", "lin_scalars_learnable.0.weight", "node_lin_out_layers.0.2.weight",
               "edge_lin_out_layers.0.4.weight"]:
         assert k in hk, k
+
+
+def test_activation_checkpointing_matches_plain_backward():
+    b, lab = _batches(np.eye(3))
+    grads = []
+    for ckpt in (False, True):
+        torch.manual_seed(0)
+        bb = eSEN_Backbone(lab.irreps, activation_checkpointing=ckpt, **KW).double()
+        out = bb(b)
+        loss = out["node_embeddings"].pow(2).sum() + out["edge_embeddings"].pow(2).sum()
+        loss.backward()
+        grads.append([p.grad.clone() for p in bb.parameters()])
+    for g0, g1 in zip(*grads):
+        assert torch.allclose(g0, g1, rtol=1e-10, atol=1e-12)
