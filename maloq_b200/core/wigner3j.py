@@ -116,12 +116,36 @@ class BasisTransform:
         self.W_global_inv = self.W_global_inv.to(device=device, dtype=dtype)
         return self
 
+    def column_tables(self, inverse: bool):
+        """Per output column u of the transform (``inverse`` = uncoupled -> coupled):
+        ``meta[u] = (s, n, c, 0)`` and ``coef`` such that
+        ``out[:, u] = sum_{j<n} in[:, s + j] * coef[c + j * n]`` (one square CG block per orbital
+        shell pair; coefficients of adjacent columns of a block are adjacent)."""
+        key = "_tables_inv" if inverse else "_tables_fwd"
+        if getattr(self, key, None) is None:
+            W = (self.W_global_inv if inverse else self.W_global).detach().cpu().double().numpy()
+            src = self.H_slices if inverse else self.in_slices
+            dst = self.in_slices if inverse else self.H_slices
+            meta = np.zeros((self.dim, 4), dtype=np.int32)
+            coef = []
+            base = 0
+            for g in range(len(self.out_js_list)):
+                s0, s1, d0, d1 = src[g], src[g + 1], dst[g], dst[g + 1]
+                n = s1 - s0
+                blk = W[s0:s1, d0:d1]  # [j, k]
+                coef.append(blk.reshape(-1))
+                for k in range(n):
+                    meta[d0 + k] = (s0, n, base + k, 0)
+                base += n * n
+            setattr(self, key, (meta, np.concatenate(coef)))
+        return getattr(self, key)
+
     def get_H(self, net_out: torch.Tensor) -> torch.Tensor:
         from ..ops import basis_transform as bt
 
-        return bt.apply_transform(net_out, self.W_global.to(net_out.device, net_out.dtype))
+        return bt.apply_transform(net_out, self, inverse=False)
 
     def get_net_out(self, H: torch.Tensor) -> torch.Tensor:
         from ..ops import basis_transform as bt
 
-        return bt.apply_transform(H, self.W_global_inv.to(H.device, H.dtype))
+        return bt.apply_transform(H, self, inverse=True)

@@ -16,7 +16,7 @@ import torch
 from ..core.irreps import make_label_layout
 from ..core.wigner3j import BasisTransform
 from .batch import GraphSample, collate
-from .labels import BlockSparseMatrix, PairTable, block_pointers, labels_to_matrix, matrix_to_labels, orbital_offsets
+from .labels import BlockSparseMatrix, PairTable, block_pointers, orbital_offsets
 
 
 class FockLabeler:
@@ -51,18 +51,21 @@ class FockLabeler:
         rows, cols = self.pairs(s)
         data = torch.as_tensor(bsm.data, device=self.device, dtype=self.dtype)
         ptr = torch.as_tensor(bsm.block_ptr, device=self.device)
-        lab = matrix_to_labels(data, ptr, self._pt(s, rows, cols), self.pos_t)
-        coupled = self.transform.get_net_out(lab)
+        from ..ops import labels as lab_ops
+
+        coupled = lab_ops.blocks_to_coupled(data, ptr, self._pt(s, rows, cols), self.pos_t, self.transform)
         E = s.num_edges
         return coupled[E:], coupled[:E]
 
     def blocks_from_labels(self, s: GraphSample, node_lab, edge_lab) -> BlockSparseMatrix:
         rows, cols = self.pairs(s)
         coupled = torch.cat([edge_lab, node_lab], 0).to(self.device, self.dtype)
-        unc = self.transform.get_H(coupled)
+        from ..ops import labels as lab_ops
+
         ptr_np = block_pointers(s.z, rows, cols, self.table)
         ptr = torch.as_tensor(ptr_np, device=self.device)
-        data = labels_to_matrix(unc, ptr, self._pt(s, rows, cols), self.pos_t, int(ptr_np[-1]))
+        data = lab_ops.coupled_to_blocks(coupled, ptr, self._pt(s, rows, cols), self.pos_t, self.transform,
+                                         int(ptr_np[-1]))
         return BlockSparseMatrix(rows, cols, ptr_np, data.detach().cpu().numpy(), orbital_offsets(s.z, self.table))
 
     def symmetrize(self, s: GraphSample, bsm: BlockSparseMatrix) -> BlockSparseMatrix:

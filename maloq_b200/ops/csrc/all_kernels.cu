@@ -8,3 +8,4 @@
 #include "norm.cu"
 #include "comm.cu"
 #include "misc.cu"
+#include "labels.cu"

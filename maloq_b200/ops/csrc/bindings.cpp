@@ -7,6 +7,7 @@
 #include "comm.h"
 #include "edge.h"
 #include "gemm.h"
+#include "labels.h"
 #include "misc.h"
 #include "norm.h"
 #include "runtime.h"
@@ -281,6 +282,49 @@ void edge_rotation(at::Tensor vec, at::Tensor J, std::vector<int64_t> joff, int6
                              rm.data(), (int)rl.size(), ROT.data_ptr<float>(), (int)vec.size(0), stream()));
 }
 
+// Block <-> label rows fused with the block-diagonal basis transform (see labels.cu).
+// data-side tensors (gather input / scatter output) are flat; rows are [rows, d].
+void basis_rows(at::Tensor in, at::Tensor out, c10::optional<at::Tensor> ptr, c10::optional<at::Tensor> pt,
+                c10::optional<at::Tensor> pos, at::Tensor meta, at::Tensor coef, int64_t d_in, int64_t rows,
+                bool gather, bool scatter) {
+  const auto dt = in.scalar_type();
+  TORCH_CHECK(dt == at::kFloat || dt == at::kDouble, "basis_rows: fp32 or fp64");
+  chk(in, dt, "in");
+  chk(out, dt, "out");
+  chk(coef, dt, "coef");
+  chk(meta, at::kInt, "meta");
+  TORCH_CHECK(meta.dim() == 2 && meta.size(1) == 4, "basis_rows: meta [d_out, 4]");
+  maloq::BasisRowsArgs a{};
+  a.in = in.data_ptr();
+  a.out = out.data_ptr();
+  a.d_in = (int)d_in;
+  a.d_out = (int)meta.size(0);
+  a.ld_in = d_in;
+  a.ld_out = a.d_out;
+  a.rows = rows;
+  a.gather = gather;
+  a.scatter = scatter;
+  a.dtype = dt == at::kDouble ? 1 : 0;
+  a.meta = reinterpret_cast<const int4*>(meta.data_ptr<int>());
+  a.coef = coef.data_ptr();
+  if (gather || scatter) {
+    TORCH_CHECK(ptr && pt && pos, "basis_rows: gather/scatter needs ptr, pt, pos");
+    chk(*ptr, at::kLong, "ptr");
+    chk(*pt, at::kLong, "pt");
+    chk(*pos, at::kInt, "pos");
+    TORCH_CHECK(ptr->numel() >= rows && pt->numel() >= rows, "basis_rows: ptr/pt cover the rows");
+    a.ptr = ll(*ptr);
+    a.pt = ll(*pt);
+    a.pos = pos->data_ptr<int>();
+    a.d_pos = (int)pos->size(1);
+    TORCH_CHECK(a.d_pos == (gather ? a.d_in : a.d_out), "basis_rows: position table width");
+  }
+  if (!gather) TORCH_CHECK(in.numel() >= rows * d_in, "basis_rows: input rows");
+  if (!scatter) TORCH_CHECK(out.numel() >= rows * a.d_out, "basis_rows: output rows");
+  const at::cuda::CUDAGuard guard(in.device());
+  check(maloq::basis_rows(a, stream()));
+}
+
 int64_t fock_loss_grid(int64_t n) { return maloq::fock_loss_grid(n); }
 
 void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, at::Tensor part) {
@@ -331,6 +375,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("edge_rotation", &edge_rotation);
   m.def("fock_loss_grid", &fock_loss_grid);
   m.def("fock_loss_stats", &fock_loss_stats);
+  m.def("basis_rows", &basis_rows);
   m.def("fock_loss_grad", &fock_loss_grad);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
 }

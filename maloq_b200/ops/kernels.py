@@ -112,7 +112,7 @@ def linear(x, weight, bias=None, act=None):
 # ------------------------------------------------------------------ ops still on PyTorch glue
 # These run PyTorch on the CUDA tensors until their fused kernels land; each is listed so the
 # set of non-kernel ops is explicit.
-TORCH_GLUE = ("fock_head_process", "gather_scale", "matrix_to_labels", "labels_to_matrix", "basis_transform")
+TORCH_GLUE = ("fock_head_process", "gather_scale")
 
 
 @register("layernorm_silu")
@@ -138,7 +138,10 @@ def rms_norm_sh(x, aw, ab, eps, residual=None):
 
 register("gather_scale")(_ref.gather_scale)
 register("fock_head_process")(lambda x, ws, bs, lp, act, sc, ab: _head_process(x, ws, bs, lp, act, sc, ab))
-register("basis_transform")(lambda x, W: torch.matmul(x, W))
+from . import labels_native  # noqa: E402
+
+for _name in ("basis_transform", "matrix_to_labels", "labels_to_matrix", "blocks_to_coupled", "coupled_to_blocks"):
+    register(_name)(getattr(labels_native, _name))
 
 
 @register("so3_linear")
@@ -224,18 +227,3 @@ def edge_rotation(vec_yzx, lmax, mmax, Js, mapping):
 
     return misc_native.edge_rotation(vec_yzx, lmax, mmax, Js, mapping)
 
-
-def _m2l(data, block_ptr, pair_type, pos_table):
-    from .labels import _ref_m2l
-
-    return _ref_m2l(data, block_ptr, pair_type, pos_table)
-
-
-def _l2m(labels, block_ptr, pair_type, pos_table, n_data):
-    from .labels import _ref_l2m
-
-    return _ref_l2m(labels, block_ptr, pair_type, pos_table, n_data)
-
-
-register("matrix_to_labels")(_m2l)
-register("labels_to_matrix")(_l2m)

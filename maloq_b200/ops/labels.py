@@ -38,3 +38,19 @@ def labels_to_matrix(labels, block_ptr, pair_type, pos_table, n_data):
     if _cuda(labels):
         return _native.labels_to_matrix(labels, block_ptr, pair_type, pos_table, n_data)
     return _ref_l2m(labels, block_ptr, pair_type, pos_table, n_data)
+
+
+def blocks_to_coupled(data, block_ptr, pair_type, pos_table, transform):
+    """Coupled label rows of block-sparse data: ``get_net_out(matrix_to_labels(...))`` in one
+    pass on CUDA (gather + block-diagonal transform, ``ops/csrc/labels.cu``)."""
+    if _cuda(data):
+        return _native.blocks_to_coupled(data, block_ptr, pair_type, pos_table, transform)
+    return transform.get_net_out(_ref_m2l(data, block_ptr, pair_type, pos_table))
+
+
+def coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data):
+    """Block-sparse data of coupled label rows: ``labels_to_matrix(get_H(...))`` in one pass on
+    CUDA (block-diagonal transform + scatter)."""
+    if _cuda(coupled):
+        return _native.coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data)
+    return _ref_l2m(transform.get_H(coupled), block_ptr, pair_type, pos_table, n_data)

@@ -2,6 +2,7 @@
 
     python -m maloq_b200.ops.microbench gemm [--bn 128] [--edges 43408]
     python -m maloq_b200.ops.microbench edge [--edges 43408]
+    python -m maloq_b200.ops.microbench labels [--rows 236000] [--kind large]
 
 ``gemm`` runs the first SO(2) convolution of one drug-like-config layer as one grouped
 launch: M = edges, (N, K) = (1152, 1280), (1024, 1024), (768, 768), bf16 in/out.
@@ -84,9 +85,38 @@ def bench_edge(edges):
           f"error_status={kernels.error_status()}")
 
 
+def bench_labels(rows, kind):
+    """Fused block gather + coupled transform (``blocks_to_coupled``) and its inverse on ``rows``
+    random atom pairs of the ``kind`` basis; bytes = block data + label rows (+ tables)."""
+    from ..data import datasets
+    from . import labels as lab
+
+    dev = torch.device("cuda", 0)
+    labeler = datasets.labeler_for(kind, dev)
+    tbl = labeler.table
+    g = torch.Generator().manual_seed(0)
+    pt = torch.randint(0, tbl.n_types * tbl.n_types, (rows,), generator=g)
+    na = torch.as_tensor(tbl.norb)[pt // tbl.n_types]
+    nb = torch.as_tensor(tbl.norb)[pt % tbl.n_types]
+    ptr = torch.cat([torch.zeros(1, dtype=torch.long), torch.cumsum(na * nb, 0)])
+    n = int(ptr[-1])
+    data = torch.randn(n, device=dev)
+    ptr, pt = ptr.to(dev), pt.to(dev)
+    D = labeler.target_len
+    T = labeler.transform
+    out = lab.blocks_to_coupled(data, ptr, pt, labeler.pos_t, T)
+    ms1 = _timeit(lambda: lab.blocks_to_coupled(data, ptr, pt, labeler.pos_t, T))
+    ms2 = _timeit(lambda: lab.coupled_to_blocks(out, ptr, pt, labeler.pos_t, T, n))
+    byts = 4 * (n + rows * D)
+    print(f"labels {kind} rows={rows} D={D}: blocks->coupled {ms1 * 1e3:.1f} us ({byts / ms1 / 1e6:.0f} GB/s), "
+          f"coupled->blocks {ms2 * 1e3:.1f} us ({byts / ms2 / 1e6:.0f} GB/s)")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "edge", "shape"])
+    ap.add_argument("what", choices=["gemm", "edge", "shape", "labels"])
+    ap.add_argument("--rows", type=int, default=236000)
+    ap.add_argument("--kind", default="large")
     ap.add_argument("--M", type=int, default=32768)
     ap.add_argument("--N", type=int, default=1024)
     ap.add_argument("--K", type=int, default=1024)
@@ -96,6 +126,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.what == "shape":
         bench_gemm_shape(a.M, a.N, a.K, a.bn, a.fp32_out)
+    elif a.what == "labels":
+        bench_labels(a.rows, a.kind)
     elif a.what == "gemm":
         bench_gemm(a.edges, a.bn)
     else:

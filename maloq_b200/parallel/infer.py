@@ -53,10 +53,10 @@ def write_partition_hamiltonian(folder, batch, node_out, edge_out, labeler, part
     nr, nc = tbl.norb[tbl.z_to_type[zr]], tbl.norb[tbl.z_to_type[zc]]
     ptr = np.concatenate([[0], np.cumsum(nr * nc)]).astype(np.int64)
     coupled = torch.cat([edge_out, node_out], 0).to(labeler.device, labeler.dtype)
-    unc = labeler.transform.get_H(coupled)
     from ..ops import labels as lab
 
-    data = lab.labels_to_matrix(unc, torch.as_tensor(ptr, device=labeler.device), pt, labeler.pos_t, int(ptr[-1]))
+    data = lab.coupled_to_blocks(coupled, torch.as_tensor(ptr, device=labeler.device), pt, labeler.pos_t,
+                                 labeler.transform, int(ptr[-1]))
     path = os.path.join(folder, f"hamiltonian_rank{rank}.npz")
     np.savez(path, rows=rows, cols=cols, block_ptr=ptr, data=data.detach().float().cpu().numpy(),
              atom_ids=own, atom_z=z_own)
