@@ -26,6 +26,10 @@ import time
 HERE = os.path.dirname(os.path.abspath(__file__))
 BASELINE_VALUE = None  # BASELINE.json publishes no number for this metric
 METRIC = "train graphs/s (drug-like DP, device-timed, max over ranks)"
+PARTITIONED = {
+    # name: (dataset kind, default atoms, mmax, layers, what)
+    "sio2": ("sio2", 20000, 2, 6, "train"),
+}
 CONFIGS = {
     # name: (dataset kind, mmax, default layers, molecules per batch or None, atoms per batch cap)
     "druglike": ("druglike", 2, 6, 32, None),
@@ -44,7 +48,10 @@ def parse():
     ap.add_argument("--channels", type=int, default=128)
     ap.add_argument("--n-batches", type=int, default=4, help="distinct batches cycled per rank")
     ap.add_argument("--grad-sync", default=None)
-    ap.add_argument("--config", default="druglike", choices=list(CONFIGS),
+    ap.add_argument("--atoms", type=int, default=None, help="atoms of the partitioned structure")
+    ap.add_argument("--edge-chunk", type=int, default=131072,
+                    help="partitioned configs: edges per chunk of the chunked (recomputed) block execution")
+    ap.add_argument("--config", default="druglike", choices=list(CONFIGS) + list(PARTITIONED),
                     help="druglike (headline) or large (10-150 atoms, lmax 6, 8 layers, <=4096 atoms/GPU)")
     return ap.parse_args()
 
@@ -107,6 +114,143 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def timed_steps(args, device, world, step_resident, step_e2e):
+    """Warm-up, then ``args.steps`` device-timed steps on resident inputs (L2 flushed before each
+    step, outside its events), then ``args.steps`` end-to-end steps whose inputs are copied from
+    pinned host memory and whose loss is read back each step.  Returns (device ms summed over
+    steps, e2e ms, kernel launches in the device-timed region, clock record, losses) with both
+    times the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from maloq_b200 import ops
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+    for i in range(args.warmup):
+        step_resident(i)
+    barrier()
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    launches0 = ops.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        flush.zero_()
+        ev[i][0].record()
+        step_resident(i)
+        ev[i][1].record()
+    barrier()
+    launches = ops.launch_count() - launches0
+    ms = sum(a.elapsed_time(b) for a, b in ev)
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e2e_start.record()
+    loss_vals = []
+    for i in range(args.steps):
+        _, _, loss = step_e2e(i)
+        loss_vals.append(loss.item())
+    e2e_end.record()
+    barrier()
+    clk = clocks.stop()
+    t = torch.tensor([ms, e2e_start.elapsed_time(e2e_end)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    return ms, e2e_ms, launches, clk, loss_vals
+
+
+def run_partitioned(args, device, world, rank):
+    """One periodic structure split over the ranks by spatial slabs (graph parallel): each rank
+    trains on its owned atoms and the edges into them; halo (ghost) rows are read from the
+    owners' memory inside the edge kernels (NVLink peer halo) and their gradients are pushed
+    back to the owners; model gradients are summed by the fused all-reduce.  Metric: global
+    edges per second.  Every rank builds the same structure from the same seed."""
+    import torch
+    import torch.distributed as dist
+
+    from maloq_b200.data import datasets
+    from maloq_b200.data.targets import Teacher
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.parallel import dist as pdist
+    from maloq_b200.parallel import partition as P
+    from maloq_b200.parallel.dp import GradSync
+    from maloq_b200.parallel.halo import partition_batch
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    kind, def_atoms, mmax, def_layers, _ = PARTITIONED[args.config]
+    n_atoms = args.atoms or def_atoms
+    layers = def_layers if args.layers == 6 else args.layers
+    t0 = time.time()
+    labeler = datasets.labeler_for(kind, device)
+    lmax = labeler.layout.lmax
+    cutoff = datasets.SPECS[kind]["cutoff"]
+    sample = datasets.build_samples(kind, 1, seed=0, n_atoms=n_atoms)[0]
+    part = P.partition("slab", sample.num_nodes, world, src=sample.src, dst=sample.dst, pos=sample.pos,
+                       cell=sample.cell)
+    dom = P.decompose(part, sample.src, sample.dst, world)[rank]
+    transport = "peer" if world > 1 else "collective"
+    batch = partition_batch(sample, dom, labeler.table, device=device, transport=transport)
+    kw = dict(sphere_channels=args.channels, hidden_channels=args.channels, lmax=lmax, mmax=mmax, cutoff=cutoff,
+              edge_channels=args.channels, num_layers=layers, num_distance_basis=128, edge_chunk=args.edge_chunk)
+    teacher = Teacher(kw, labeler, device=device)
+    with torch.no_grad():
+        no, eo = teacher.head(teacher.backbone(batch), batch)
+    batch.node_y, batch.y = no.detach().clone(), eo.detach().clone()
+    del teacher, no, eo
+    torch.cuda.empty_cache()
+    host = batch.to("cpu").pin_memory()
+    t_data = time.time() - t0
+
+    torch.manual_seed(1)
+    backbone = eSEN_Backbone(labeler.irreps, include_edges=True, **kw).to(device)
+    head = Fock_Irreps_Head(None, labeler.irreps, lmax=lmax, sphere_channels=args.channels,
+                            ls_list=labeler.layout.ls_list, reduce_node=True, reduce_node_intra=True).to(device)
+    params = list(backbone.parameters()) + list(head.parameters())
+    opt = torch.optim.Adam(params, lr=1e-4, fused=True)
+    sync = GradSync(params, mode=args.grad_sync or "fused") if world > 1 else None
+    trainer = SplitTrainer(backbone, head, labeler.irreps, mask_table=torch.as_tensor(labeler.table.mask),
+                           grad_sync=sync)
+    loss_fn = L.rmse_mse_padded_loss
+    ms, e2e_ms, launches, clk, loss_vals = timed_steps(
+        args, device, world, lambda i: trainer.train_step(batch, loss_fn, opt),
+        lambda i: trainer.train_step(host.to(device, non_blocking=True), loss_fn, opt))
+    ms_step = ms / args.steps
+    edges = sample.num_edges
+    h2d = host.nbytes()
+    if rank == 0:
+        out = {
+            "metric": "train edges/s (Si/O partitioned, device-timed, max over ranks)",
+            "value": round(edges / (ms_step / 1e3), 1), "unit": "edges/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random amorphous Si/O supercell, frozen random-init teacher targets; random-init "
+                    "weights)",
+            "config": {"model": f"eSEN lmax={lmax} mmax={mmax} C={args.channels} layers={layers} + Fock head "
+                                f"(DZVP-like, D={labeler.target_len})",
+                       "atoms": sample.num_nodes, "edges": edges, "cutoff_A": cutoff,
+                       "edges_per_atom": round(edges / sample.num_nodes, 1), "parallelism": f"graph{world}",
+                       "partition": "slab", "halo_transport": transport,
+                       "halo_rows_rank0": int(len(dom.halo)), "edges_rank0": int(len(dom.edges)),
+                       "l2": "256 MiB buffer written between timed steps, outside the step events",
+                       "edge_chunk": args.edge_chunk, "edge_stream": "bf16 storage, fp32 compute"},
+            "e2e": {"value": round(edges / (e2e_ms / args.steps / 1e3), 1), "unit": "edges/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 4},
+            "gpu_launches": int(launches), "clocks": clk, "final_loss": loss_vals[-1],
+            "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 2**30, 2),
+            "setup_s": round(t_data, 1),
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        pdist.cleanup_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -137,6 +281,8 @@ def main():
     if args.impl == "torch":
         ops.use_torch_ops(True)
     torch.manual_seed(0)
+    if args.config in PARTITIONED:
+        return run_partitioned(args, device, world, rank)
 
     kind, mmax, def_layers, per_batch, atom_cap = CONFIGS[args.config]
     if args.config != "druglike" and args.layers == 6:
@@ -176,53 +322,13 @@ def main():
     trainer = SplitTrainer(backbone, head, labeler.irreps, mask_table=torch.as_tensor(labeler.table.mask),
                            grad_sync=sync)
     loss_fn = L.rmse_mse_padded_loss
-    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for i in range(args.warmup):
-        trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt)
-    barrier()
-
-    # ---------------- device-timed steps (inputs resident, L2 flushed between steps)
-    clocks = ClockSampler(device.index)
-    clocks.start()
-    launches0 = ops.launch_count()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    barrier()
-    for i in range(args.steps):
-        flush.zero_()
-        ev[i][0].record()
-        trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt)
-        ev[i][1].record()
-    barrier()
-    launches = ops.launch_count() - launches0
-    ms = sum(a.elapsed_time(b) for a, b in ev)
-
-    # ---------------- end to end through the public API: H2D from pinned memory + loss D2H
-    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    e2e_start.record()
-    loss_vals = []
-    for i in range(args.steps):
-        hb = host_batches[i % len(host_batches)]
-        db = hb.to(device, non_blocking=True)
-        _, _, loss = trainer.train_step(db, loss_fn, opt)
-        loss_vals.append(loss.item())
-    e2e_end.record()
-    barrier()
-    clk = clocks.stop()
-    e2e_ms = e2e_start.elapsed_time(e2e_end)
+    ms, e2e_ms, launches, clk, loss_vals = timed_steps(
+        args, device, world, lambda i: trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt),
+        lambda i: trainer.train_step(host_batches[i % len(host_batches)].to(device, non_blocking=True), loss_fn,
+                                     opt))
     nbytes = [sum(v.numel() * v.element_size() for v in hb.tensors().values()) for hb in host_batches]
     h2d = sum(nbytes[i % len(nbytes)] for i in range(args.steps)) / args.steps
 
-    t = torch.tensor([ms, e2e_ms], device=device, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = t.tolist()
     ms_step = ms / args.steps
     # graphs per step on this rank, averaged over the timed steps (batches cycle); weak scaling
     graphs = world * sum(graphs_per_batch[i % len(graphs_per_batch)] for i in range(args.steps)) / args.steps

@@ -97,6 +97,8 @@ class eSEN_Block(nn.Module):
         self.atom_wise = SpectralAtomwise(sphere_channels, hidden_channels, lmax, mmax)
 
     def forward(self, x_node, x_edge_emb, x_edge, graph):
+        if graph.chunks is not None:
+            return self._forward_chunked(x_node, x_edge_emb, x_edge, graph)
         if self.node_or_edge == "node":
             h = self.norm_1(x_node)
             h = self.edge_wise(h, x_edge_emb, x_edge, graph, "node")
@@ -106,6 +108,48 @@ class eSEN_Block(nn.Module):
         h = self.norm_1(h)
         h, res = self.norm_2(h, residual=x_edge_emb)
         return self.atom_wise(h) + res
+
+    # ------------------------------------------------------------------ edge-chunked execution
+    def _forward_chunked(self, x_node, x_edge_emb, x_edge, graph):
+        """The same block over dst-contiguous edge chunks.  With gradients each chunk is
+        recomputed in backward (only its inputs, views of the layer inputs, are kept), so the
+        per-edge working set is bounded by the chunk size.  Halo rows are exchanged once per
+        block (``HaloPlan.materialize``) and shared by the chunks.  The edge stream keeps the
+        dtype it arrives in (bf16 storage by default; every chunk computes in the node stream's
+        dtype)."""
+        run = _checkpointed if torch.is_grad_enabled() else (lambda f, *a: f(*a))
+        subs = graph.subgraphs()
+        if self.node_or_edge == "node":
+            h = self.norm_1(x_node)
+            hx = graph.halo.materialize(h) if graph.halo is not None else h
+            outs = [run(self._node_rows, hx, _rows(x_edge_emb, e0, e1), x_edge[e0:e1], sub)
+                    for (e0, e1, _, _), sub in zip(graph.chunks, subs)]
+            h, res = self.norm_2(torch.cat(outs, 0), residual=x_node)
+            return self.atom_wise(h) + res
+        xn = graph.halo.materialize(x_node) if graph.halo is not None else x_node
+        outs = [run(self._edge_rows, xn, x_edge_emb[e0:e1], x_edge[e0:e1], sub)
+                for (e0, e1, _, _), sub in zip(graph.chunks, subs)]
+        return torch.cat(outs, 0)
+
+    def _node_rows(self, hx, xm, xe, sub):
+        return self.edge_wise(hx, None if xm is None else xm.to(hx.dtype), xe, sub, "node")
+
+    def _edge_rows(self, xn, xee, xe, sub):
+        x_in = xee.to(xn.dtype)  # compute dtype of the node stream
+        h = self.edge_wise(xn, x_in, xe, sub, "edge")
+        h = self.norm_1(h)
+        h, res = self.norm_2(h, residual=x_in)
+        return (self.atom_wise(h) + res).to(xee.dtype)
+
+
+def _rows(x, e0, e1):
+    return None if x is None else x[e0:e1]
+
+
+def _checkpointed(fn, *args):
+    from torch.utils.checkpoint import checkpoint
+
+    return checkpoint(fn, *args, use_reentrant=False)
 
 
 class EdgeDegreeEmbedding(nn.Module):
@@ -140,6 +184,45 @@ class Graph:
         self.src, self.dst, self.rot, self.dst_ptr = src, dst, rot, dst_ptr
         self.num_nodes, self.lmax, self.mmax, self.halo = num_nodes, lmax, mmax, halo
         self.cache = {}
+        # node-path output rows: the scatter writes rows [0, num_out) through out_ptr / dst_out
+        # (all nodes here; one chunk's destination range in a sub-graph)
+        self.out_ptr, self.dst_out, self.num_out = dst_ptr, dst, num_nodes
+        self.chunks = None  # [(e0, e1, n0, n1)] for edge-chunked execution
+
+    def subgraphs(self):
+        """Sub-graphs of ``chunks`` (built once per forward, shared by every layer so their
+        cached source CSRs are reused)."""
+        if "subgraphs" not in self.cache:
+            self.cache["subgraphs"] = [self.sub(*c) for c in self.chunks]
+        return self.cache["subgraphs"]
+
+    def sub(self, e0, e1, n0, n1):
+        """Edges [e0, e1) = every edge into nodes [n0, n1) (edges are dst-sorted).  Gathers
+        still index all (extended) node rows; the node-path output covers rows [n0, n1)."""
+        E = e1 - e0
+        g = Graph(self.src[e0:e1], self.dst[e0:e1], self.rot[e0:e1], (self.dst_ptr - e0).clamp(0, E),
+                  self.num_nodes, self.lmax, self.mmax, None)
+        g.num_nodes_ext = getattr(self, "num_nodes_ext", None) or self.num_nodes
+        g.out_ptr = (self.dst_ptr[n0:n1 + 1] - e0).contiguous()
+        g.dst_out = g.dst - n0
+        g.num_out = n1 - n0
+        return g
+
+
+def chunk_bounds(dst_ptr, max_edges):
+    """Split dst-sorted edges into chunks of whole destination nodes with at most ~max_edges
+    edges (a node with more edges gets a chunk of its own): [(e0, e1, n0, n1)]."""
+    import numpy as np
+
+    ptr = np.asarray(dst_ptr)
+    n = len(ptr) - 1
+    out, n0 = [], 0
+    while n0 < n:
+        n1 = int(np.searchsorted(ptr, ptr[n0] + max_edges, side="right")) - 1
+        n1 = min(max(n1, n0 + 1), n)
+        out.append((int(ptr[n0]), int(ptr[n1]), n0, n1))
+        n0 = n1
+    return out
 
 
 class eSEN_Backbone(nn.Module):
@@ -154,11 +237,15 @@ class eSEN_Backbone(nn.Module):
                  hidden_channels=128, norm_type="rms_norm_sh", act_type="gate", mlp_type="spectral",
                  gaussian_width=1.0, include_edges=True, open_shell=False, wigner_backend="cuda",
                  distributed_graph_training=False, message_type="source-target", activation_checkpointing=False,
-                 **unused):
+                 edge_chunk=None, edge_stream_dtype=torch.bfloat16, **unused):
         super().__init__()
         # recompute each block's forward during backward (saves only the block inputs); needed
         # for graphs whose per-layer edge activations exceed device memory
         self.activation_checkpointing = bool(activation_checkpointing)
+        # graphs with more than edge_chunk edges run every block over chunks of whole
+        # destination nodes (recomputed per chunk in backward) and keep the edge stream in bf16
+        self.edge_chunk = int(edge_chunk) if edge_chunk else None
+        self.edge_stream_dtype = edge_stream_dtype
         if act_type != "gate" or mlp_type != "spectral":
             raise ValueError("only act_type='gate' and mlp_type='spectral' are implemented (as in the reference)")
         self.max_num_elements, self.lmax, self.mmax = max_num_elements, lmax, mmax
@@ -210,6 +297,8 @@ class eSEN_Backbone(nn.Module):
         g = Graph(batch.edge_index[0], batch.edge_index[1], rot, batch.dst_ptr, batch.num_nodes,
                   self.lmax, self.mmax, getattr(batch, "halo", None))
         g.num_nodes_ext = getattr(batch, "num_nodes_ext", None) or batch.num_nodes
+        if self.edge_chunk and batch.num_edges > self.edge_chunk:
+            g.chunks = chunk_bounds(batch.dst_ptr.cpu().numpy(), self.edge_chunk)
         return g
 
     def forward(self, batch):
@@ -228,7 +317,9 @@ class eSEN_Backbone(nn.Module):
         x_edge = torch.cat([self.source_embedding(batch.src_z), gauss, self.target_embedding(batch.dst_z)], dim=1)
         x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
         x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
-        ckpt = self.activation_checkpointing and torch.is_grad_enabled()
+        if graph.chunks is not None and x_edge_emb is not None:
+            x_edge_emb = x_edge_emb.to(self.edge_stream_dtype)  # edge stream storage between blocks
+        ckpt = self.activation_checkpointing and torch.is_grad_enabled() and graph.chunks is None
         for i in range(self.num_layers):
             x_node = self._run_block(self.node_blocks[i], ckpt, x_node, x_edge_emb, x_edge, graph)
             if self.include_edges:
@@ -236,11 +327,20 @@ class eSEN_Backbone(nn.Module):
         x_node = self.norm(x_node)
         out = {"node_embeddings": x_node, "edge_index": batch.edge_index, "edge_distance": dist,
                "edge_distance_vec": batch.edge_attr[:, [2, 3, 1]], "partition": getattr(batch, "halo", None)}
-        if self.include_edges:
+        if self.include_edges and graph.chunks is not None:
+            run = _checkpointed if torch.is_grad_enabled() else (lambda f, *a: f(*a))
+            cd = x_node.dtype
+            out["edge_embeddings"] = torch.cat(
+                [run(self._norm_rows, x_edge_emb[e0:e1], cd) for e0, e1, _, _ in graph.chunks], 0)
+            out["edge_chunks"] = [(e0, e1) for e0, e1, _, _ in graph.chunks]
+        elif self.include_edges:
             out["edge_embeddings"] = self.norm(x_edge_emb)
         else:
             out.update({"x_edge": x_edge, "graph": graph})
         return out
+
+    def _norm_rows(self, x, compute_dtype):
+        return self.norm(x.to(compute_dtype)).to(x.dtype)
 
     @staticmethod
     def _run_block(block, ckpt, x_node, x_edge_emb, x_edge, graph):

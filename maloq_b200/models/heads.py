@@ -170,7 +170,7 @@ class Fock_Irreps_Head(nn.Module):
         edge_index = emb["edge_index"]
         node_outs, edge_outs = [], []
         if self.reduce_edge:
-            alpha, beta, half_mask, rev = self.half_antisym_edge_pairs(edge_emb, edge_index)
+            alpha, beta, half_mask, rev = self.half_antisym_edge_pairs(edge_emb.to(node_emb.dtype), edge_index)
         for spin in range(self.num_spins):
             n_sorted = self.process(node_emb, "node", spin)
             if self.reduce_node:
@@ -192,6 +192,18 @@ class Fock_Irreps_Head(nn.Module):
                 flips = torch.as_tensor(self.parity_flip_indices, device=eo.device, dtype=torch.long)
                 sign = torch.ones(eo.shape[1], device=eo.device, dtype=eo.dtype).index_fill(0, flips, -1.0)
                 edge_out = eo * sign
+            elif emb.get("edge_chunks"):
+                # row-wise over edges: one chunk at a time (recomputed in backward)
+                def rows(x, spin=spin):
+                    return ops.gather_scale(self.process(x.to(node_emb.dtype), "edge", spin), self._edge_gather, None)
+
+                if torch.is_grad_enabled():
+                    from torch.utils.checkpoint import checkpoint
+
+                    parts = [checkpoint(rows, edge_emb[e0:e1], use_reentrant=False) for e0, e1 in emb["edge_chunks"]]
+                else:
+                    parts = [rows(edge_emb[e0:e1]) for e0, e1 in emb["edge_chunks"]]
+                edge_out = torch.cat(parts, 0)
             else:
                 edge_out = ops.gather_scale(self.process(edge_emb, "edge", spin), self._edge_gather, None)
             node_outs.append(node_out)

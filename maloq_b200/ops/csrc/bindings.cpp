@@ -130,6 +130,18 @@ void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
 }
 
 // DX[n] = sum over dst-CSR of DDST + sum over src-CSR of DSRC (either may be absent)
+// OUT[h] = row halo_row[h] of rank halo_owner[h]'s staging slot (peers = device table of slot bases)
+void halo_fetch(int64_t peers, at::Tensor halo_owner, at::Tensor halo_row, at::Tensor OUT) {
+  chk(OUT, at::kFloat, "halo_fetch out");
+  chk(halo_owner, at::kInt, "halo_owner");
+  chk(halo_row, at::kLong, "halo_row");
+  TORCH_CHECK(OUT.size(0) == halo_owner.numel() && halo_row.numel() == halo_owner.numel(), "halo_fetch: rows");
+  const at::cuda::CUDAGuard guard(OUT.device());
+  check(maloq::edge_halo_fetch(reinterpret_cast<const float* const*>(peers), halo_owner.data_ptr<int>(), ll(halo_row),
+                               OUT.data_ptr<float>(), OUT.size(0), (int)(OUT.numel() / std::max<int64_t>(1, OUT.size(0))),
+                               stream()));
+}
+
 void halo_push(at::Tensor G, int64_t recv, at::Tensor halo_owner, at::Tensor recv_slot) {
   chk(G, at::kFloat, "G");
   const int SC = (int)(G.numel() / std::max<int64_t>(1, G.size(0)));
@@ -362,6 +374,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gate_bwd", &gate_bwd);
   m.def("node_reduce", &node_reduce);
   m.def("halo_push", &halo_push);
+  m.def("halo_fetch", &halo_fetch);
   m.def("rms_norm_fwd", &rms_norm_fwd);
   m.def("rms_norm_bwd", &rms_norm_bwd);
   m.def("norm_grid", &norm_grid);

@@ -155,6 +155,18 @@ __global__ void halo_push_kernel(const float* __restrict__ G, float* const* __re
   for (int i = threadIdx.x; i < SC / 4; i += blockDim.x) dst[i] = src[i];
 }
 
+// Halo rows copied out of their owners' staging slots (peer loads over NVLink):
+// OUT[h, :] = peers[halo_owner[h]][halo_row[h] * SC + :]
+__global__ void halo_fetch_kernel(const float* const* __restrict__ peers, const int* __restrict__ halo_owner,
+                                  const long long* __restrict__ halo_row, float* __restrict__ OUT, long long n_halo,
+                                  int SC) {
+  const long long h = blockIdx.x;
+  if (h >= n_halo) return;
+  const float4* src = reinterpret_cast<const float4*>(peers[halo_owner[h]] + halo_row[h] * SC);
+  float4* dst = reinterpret_cast<float4*>(OUT + h * SC);
+  for (int i = threadIdx.x; i < SC / 4; i += blockDim.x) dst[i] = src[i];
+}
+
 // ---------------------------------------------------------------- rotate back
 // Node path: OUT[n, j, c] = scale * sum_{e: dst=n} sum_{k<Rk} rot[e,k,j] Y[e, koff + k*C + c] (+ BASE)
 template <int L, int MM>
@@ -356,6 +368,14 @@ const char* edge_halo_push(const float* G, float* const* recv, const int* halo_o
   if (n_halo == 0) return nullptr;
   if (SC % 4) return "halo push: row size must be a multiple of 4 floats";
   halo_push_kernel<<<(unsigned)n_halo, 128, 0, st>>>(G, recv, halo_owner, recv_slot, n_halo, SC);
+  return last_error();
+}
+
+const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, const long long* halo_row, float* out,
+                            long long n_halo, int SC, cudaStream_t st) {
+  if (n_halo == 0) return nullptr;
+  if (SC % 4) return "halo fetch: row size must be a multiple of 4 floats";
+  halo_fetch_kernel<<<(unsigned)n_halo, 128, 0, st>>>(peers, halo_owner, halo_row, out, n_halo, SC);
   return last_error();
 }
 

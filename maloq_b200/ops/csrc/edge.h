@@ -16,6 +16,8 @@ const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* X
                                    float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
                                    const float* const* peers, const int* halo_owner, const long long* halo_row,
                                    long long n_own, cudaStream_t st);
+const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, const long long* halo_row, float* out,
+                            long long n_halo, int SC, cudaStream_t st);
 const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,
                            long long n_halo, int SC, cudaStream_t st);
 const char* edge_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,

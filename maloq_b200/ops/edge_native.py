@@ -124,8 +124,9 @@ class EdgewiseFn(torch.autograd.Function):
         _gemm([H1[:, a0:a1] for a0, a1 in hb], w2b, [Y2[:, y0:y1] for y0, y1 in cb],
               [b2.float().contiguous()] + [None] * (nw - 1))
         if meta["node"]:
-            out = torch.empty(graph.num_nodes, S, C, device=dev, dtype=torch.float32)
-            lib.rotate_back_scatter(*LM, Y2, 0, R, graph.rot, graph.dst_ptr, None, out, 1.0)
+            # rows of the destination range (all nodes, or one chunk's nodes)
+            out = torch.empty(graph.num_out, S, C, device=dev, dtype=torch.float32)
+            lib.rotate_back_scatter(*LM, Y2, 0, R, graph.rot, graph.out_ptr, None, out, 1.0)
         else:
             out = torch.empty(E, S, C, device=dev, dtype=torch.float32)
             lib.rotate_back_edge(*LM, Y2, 0, R, graph.rot, out)
@@ -148,7 +149,7 @@ class EdgewiseFn(torch.autograd.Function):
         dev = g.device
         g = g.contiguous().float()
         dY2 = torch.empty(E, R * C, device=dev, dtype=torch.bfloat16)
-        lib.rotate_grad(*LM, g, graph.dst if meta["node"] else None, graph.rot, dY2, None, R, 1.0)
+        lib.rotate_grad(*LM, g, graph.dst_out if meta["node"] else None, graph.rot, dY2, None, R, 1.0)
         hb = _blocks(meta["m_size"], H)
         cb = _blocks(meta["m_size"], C)
         ab = _blocks(meta["m_size"], Cin)

@@ -131,7 +131,7 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge, src_feats=Non
     y, _ = so2_conv(h, None, c2.gemm_weights(), c2.fc_m0.bias, c2.m_size, 0, c2.m_output_channels)
     y = rotate_back(y, graph.rot)
     if node_or_edge == "node":
-        return scatter_sum(y, graph.dst, graph.num_nodes)
+        return scatter_sum(y, graph.dst_out, graph.num_out)
     return y
 
 

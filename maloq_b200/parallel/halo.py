@@ -71,9 +71,19 @@ class HaloPlan:
     def extend(self, x_node, graph=None):
         """[owned | halo] rows, differentiable (collective transport; the peer transport is used
         inside the fused edge kernels instead)."""
-        if self.n_halo == 0:
+        if self.world == 1:
             return x_node
+        # every rank joins the exchange: a rank without halo rows may still send rows
         return torch.cat([x_node, self.gather_halo(x_node)], dim=0)
+
+    def materialize(self, x_node):
+        """[owned | halo] rows as one differentiable local tensor with either transport (used
+        by chunked execution, where the chunks share one exchange per layer)."""
+        if self.world == 1:
+            return x_node
+        if self.transport == "peer":
+            return self.peer_for(tuple(x_node.shape[1:])).fetch(x_node.contiguous().float())
+        return self.extend(x_node)
 
     def peer_for(self, row_shape, n_slots=32):
         """The NVLink halo (created on first use - a collective step on every rank)."""

@@ -27,6 +27,26 @@ from ..ops.native import count_launches
 SPIN_LIMIT = 1 << 28
 
 
+class _PeerFetch(torch.autograd.Function):
+    """[owned | halo] rows as one local tensor: publish, then copy every halo row out of its
+    owner's staging slot (peer loads); backward returns the halo gradients to their owners."""
+
+    @staticmethod
+    def forward(ctx, x_node, peer):
+        ctx.peer = peer
+        slot = peer.publish(x_node)
+        ext = x_node.new_empty((peer.n_own + peer.n_halo,) + peer.row_shape)
+        ext[: peer.n_own] = x_node
+        if peer.n_halo:
+            peer.lib.halo_fetch(peer.table_ptr(slot), peer.halo_owner, peer.halo_row, ext[peer.n_own:])
+            count_launches(1)
+        return ext
+
+    @staticmethod
+    def backward(ctx, g):
+        return ctx.peer.reduce_grads(g), None
+
+
 class PeerHalo:
     def __init__(self, domain, device, row_shape, n_slots=16, group=None):
         import torch.distributed._symmetric_memory as symm_mem
@@ -103,6 +123,10 @@ class PeerHalo:
         view.view(self.n_own, *self.row_shape).copy_(x_node.detach())
         self._barrier()
         return slot
+
+    def fetch(self, x_node):
+        """Differentiable [owned | halo] rows (one publish, one peer copy per call)."""
+        return _PeerFetch.apply(x_node, self)
 
     def reduce_grads(self, dx_ext):
         """Gradient of the extended rows -> gradient of the owned rows (halo rows summed on

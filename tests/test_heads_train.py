@@ -144,3 +144,38 @@ def test_activation_checkpointing_matches_plain_backward():
         grads.append([p.grad.clone() for p in bb.parameters()])
     for g0, g1 in zip(*grads):
         assert torch.allclose(g0, g1, rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("chunk,stream", [(7, "fp64"), (25, "fp64"), (7, "bf16")])
+def test_edge_chunked_execution_matches_unchunked(chunk, stream):
+    """Chunked blocks (whole destination nodes per chunk, recomputed in backward) give the
+    unchunked forward and gradients: exactly with a full-precision edge stream, and up to the
+    bf16 rounding of the stored edge stream otherwise."""
+    dtype = torch.float64 if stream == "fp64" else torch.float32
+    b, lab = _batches(np.eye(3), dtype=dtype)
+    sd = torch.float64 if stream == "fp64" else torch.bfloat16
+    res = []
+    for ec in (None, chunk):
+        torch.manual_seed(0)
+        bb = eSEN_Backbone(lab.irreps, edge_chunk=ec, edge_stream_dtype=sd, **KW).to(dtype)
+        hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list,
+                              reduce_node=True, reduce_node_intra=True).to(dtype)
+        emb = bb(b)
+        if ec is not None:
+            assert emb.get("edge_chunks") and len(emb["edge_chunks"]) > 1
+        n, e = hd(emb, b)
+        (n.pow(2).sum() + e.pow(2).sum()).backward()
+        params = list(bb.parameters()) + list(hd.parameters())
+        res.append((n.detach(), e.detach(), [torch.zeros_like(p) if p.grad is None else p.grad.clone() for p in params]))
+    (n0, e0, g0), (n1, e1, g1) = res
+    if stream == "fp64":
+        assert torch.allclose(n0, n1, rtol=1e-10, atol=1e-12)
+        assert torch.allclose(e0, e1, rtol=1e-10, atol=1e-12)
+        for a, c in zip(g0, g1):
+            assert torch.allclose(a, c, rtol=1e-9, atol=1e-11)
+        return
+    for x, y in ((n0, n1), (e0, e1)):
+        assert (x - y).abs().max() <= 2e-2 * x.abs().max()
+    for a, c in zip(g0, g1):
+        if a.numel():
+            assert (a - c).abs().max() <= 5e-2 * max(1e-6, a.abs().max().item())

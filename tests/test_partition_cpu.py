@@ -39,20 +39,20 @@ def test_partitioners_and_decomposition(name, world):
             assert np.array_equal(doms[p].owned[doms[p].send[d.rank]], mine)
 
 
-def _model(lab):
+def _model(lab, edge_chunk=None):
     from maloq_b200.models.backbone import eSEN_Backbone
     from maloq_b200.models.heads import Fock_Irreps_Head
 
     torch.manual_seed(0)
     kw = dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2, cutoff=5.0, num_layers=2, num_distance_basis=8,
               edge_channels=8, message_type="source-target-message")
-    bb = eSEN_Backbone(lab.irreps, **kw)
+    bb = eSEN_Backbone(lab.irreps, edge_chunk=edge_chunk, edge_stream_dtype=torch.float32, **kw)
     hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list, reduce_node=True,
                           reduce_node_intra=True)
     return bb, hd
 
 
-def _partitioned_worker(rank, world, pname):
+def _partitioned_worker(rank, world, pname, edge_chunk=None):
     import torch.distributed as dist
 
     from maloq_b200.data import basis_sets
@@ -64,7 +64,7 @@ def _partitioned_worker(rank, world, pname):
     part = P.partition(pname, g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
     dom = P.decompose(part, g.src, g.dst, world)[rank]
     b = partition_batch(g, dom, lab.table)
-    bb, hd = _model(lab)
+    bb, hd = _model(lab, edge_chunk)
     no, eo = hd(bb(b), b)
     torch.manual_seed(7)
     wn = torch.randn(g.num_nodes, no.shape[-1])
@@ -96,10 +96,12 @@ def _single():
                                             for p in list(bb.parameters()) + list(hd.parameters())]
 
 
-@pytest.mark.parametrize("pname", ["linear-edgewise", "rcb"])
-def test_partitioned_forward_backward_matches_single_process(pname):
+@pytest.mark.parametrize("pname,edge_chunk", [("linear-edgewise", None), ("rcb", None), ("rcb", 40)])
+def test_partitioned_forward_backward_matches_single_process(pname, edge_chunk):
+    """Graph-partitioned (2 gloo ranks, collective halo) = one process; with ``edge_chunk`` the
+    blocks also run over edge chunks sharing one halo exchange per block."""
     ref_n, ref_e, ref_g = _single()
-    out = _dist_util.run(_partitioned_worker, world=2, args=(pname,))
+    out = _dist_util.run(_partitioned_worker, world=2, args=(pname, edge_chunk))
     for r, (own, edges, no, eo, grads) in out.items():
         assert np.allclose(no, ref_n[own].numpy(), atol=1e-5, rtol=1e-4)
         assert np.allclose(eo, ref_e[edges].numpy(), atol=1e-5, rtol=1e-4)
