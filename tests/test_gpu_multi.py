@@ -90,7 +90,7 @@ def test_fused_grad_sync_matches_nccl_in_training():
     assert max(out.values()) < 1e-5, out
 
 
-def _partition_worker(rank, world, transport):
+def _partition_worker(rank, world, transport, edge_chunk=None):
     import numpy as np
     import torch
 
@@ -111,15 +111,15 @@ def _partition_worker(rank, world, transport):
     kw = dict(sphere_channels=32, hidden_channels=32, lmax=4, mmax=2, cutoff=5.0, num_layers=2, num_distance_basis=16,
               edge_channels=32)
 
-    def model():
+    def model(chunk=None):
         torch.manual_seed(0)
-        bb = eSEN_Backbone(lab.irreps, **kw).to(dev)
+        bb = eSEN_Backbone(lab.irreps, edge_chunk=chunk, edge_stream_dtype=torch.float32, **kw).to(dev)
         hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=32, ls_list=lab.layout.ls_list,
                               reduce_node=True, reduce_node_intra=True).to(dev)
         return bb, hd
 
-    def run(batch, own, edges):
-        bb, hd = model()
+    def run(batch, own, edges, chunk=None):
+        bb, hd = model(chunk)
         no, eo = hd(bb(batch), batch)
         torch.manual_seed(7)
         wn = torch.randn(g.num_nodes, no.shape[-1], device=dev)
@@ -135,7 +135,7 @@ def _partition_worker(rank, world, transport):
     part = P.partition("rcb", g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
     dom = P.decompose(part, g.src, g.dst, world)[rank]
     b = partition_batch(g, dom, lab.table, device=dev, transport=transport)
-    no, eo, named = run(b, torch.as_tensor(dom.owned, device=dev), torch.as_tensor(dom.edges, device=dev))
+    no, eo, named = run(b, torch.as_tensor(dom.owned, device=dev), torch.as_tensor(dom.edges, device=dev), edge_chunk)
     errs = {}
     for (n, p), (_, rp) in zip(named, ref_named):
         if p.numel() == 0:
@@ -148,10 +148,13 @@ def _partition_worker(rank, world, transport):
     return no.cpu(), eo.cpu(), errs, kernels.error_status()
 
 
-@pytest.mark.parametrize("transport", ["collective", "peer"])
-def test_partitioned_gpu_matches_unpartitioned(transport):
+@pytest.mark.parametrize("transport,edge_chunk", [("collective", None), ("peer", None), ("peer", 1500),
+                                                  ("collective", 1500)])
+def test_partitioned_gpu_matches_unpartitioned(transport, edge_chunk):
+    """2 GPUs, graph-partitioned = unpartitioned; the in-kernel peer halo, and with
+    ``edge_chunk`` the chunked blocks sharing one halo exchange (peer fetch) per block."""
     _need(2)
-    out = _dist_util.run(_partition_worker, world=2, backend="nccl", args=(transport,))
+    out = _dist_util.run(_partition_worker, world=2, backend="nccl", args=(transport, edge_chunk))
     for r in range(2):
         _, _, errs, status = out[r]
         assert status == 0
