@@ -10,7 +10,8 @@ Conventions kept from the reference:
 * no self edges; both directions present.
 
 Edges are returned sorted by ``dst`` (then ``src``), the order the segmented-reduction
-kernels need.  The native C++ builder (``maloq_b200/native``) is used when it is built.
+kernels need.  Structures too large for this builder use the device builder
+(:mod:`maloq_b200.data.graph_gpu`), which gives the same edges in the same order.
 """
 
 from __future__ import annotations
@@ -18,26 +19,12 @@ from __future__ import annotations
 import numpy as np
 
 
-def _native():
-    try:
-        from ..native import _graph  # type: ignore
-
-        return _graph
-    except Exception:  # noqa: BLE001 - the numpy path below is the portable builder
-        return None
-
-
-def radius_graph(pos, cutoff, cell=None, chunk=65536, use_native=True):
+def radius_graph(pos, cutoff, cell=None, chunk=65536):
     """Return (src, dst, vec) with vec = pos[src] - pos[dst] (minimum image if ``cell``)."""
     pos = np.ascontiguousarray(pos, dtype=np.float64)
     n = len(pos)
     if n == 0:
         return np.zeros(0, np.int64), np.zeros(0, np.int64), np.zeros((0, 3))
-    nat = _native() if use_native else None
-    if nat is not None:
-        c = None if cell is None else np.ascontiguousarray(cell, dtype=np.float64)
-        src, dst, vec = nat.radius_graph(pos, float(cutoff), c)
-        return src, dst, vec
     if cell is not None:
         cell = np.asarray(cell, dtype=np.float64)
         if np.any(cell < 2 * cutoff):

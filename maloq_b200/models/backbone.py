@@ -113,33 +113,55 @@ class eSEN_Block(nn.Module):
     def _forward_chunked(self, x_node, x_edge_emb, x_edge, graph):
         """The same block over dst-contiguous edge chunks.  With gradients each chunk is
         recomputed in backward (only its inputs, views of the layer inputs, are kept), so the
-        per-edge working set is bounded by the chunk size.  Halo rows are exchanged once per
-        block (``HaloPlan.materialize``) and shared by the chunks.  The edge stream keeps the
-        dtype it arrives in (bf16 storage by default; every chunk computes in the node stream's
-        dtype)."""
-        run = _checkpointed if torch.is_grad_enabled() else (lambda f, *a: f(*a))
-        subs = graph.subgraphs()
+        per-edge working set is bounded by the chunk size; without gradients the edge block
+        overwrites the edge stream chunk by chunk.  Halo rows are exchanged once per block
+        (``HaloPlan.materialize``) and shared by the chunks.  ``x_edge`` may be an
+        :class:`EdgeInputs` (rows computed per chunk).  The edge stream keeps the dtype it
+        arrives in (bf16 storage by default; every chunk computes in the node stream's dtype)."""
+        grad = torch.is_grad_enabled()
+        run = _checkpointed if grad else (lambda f, *a: f(*a))
         if self.node_or_edge == "node":
             h = self.norm_1(x_node)
             hx = graph.halo.materialize(h) if graph.halo is not None else h
-            outs = [run(self._node_rows, hx, _rows(x_edge_emb, e0, e1), x_edge[e0:e1], sub)
-                    for (e0, e1, _, _), sub in zip(graph.chunks, subs)]
+            outs = [run(self._node_rows, hx, _rows(x_edge_emb, e0, e1), x_edge, e0, e1, graph.chunk_graph(i))
+                    for i, (e0, e1, _, _) in enumerate(graph.chunks)]
             h, res = self.norm_2(torch.cat(outs, 0), residual=x_node)
             return self.atom_wise(h) + res
         xn = graph.halo.materialize(x_node) if graph.halo is not None else x_node
-        outs = [run(self._edge_rows, xn, x_edge_emb[e0:e1], x_edge[e0:e1], sub)
-                for (e0, e1, _, _), sub in zip(graph.chunks, subs)]
+        if not grad:
+            for i, (e0, e1, _, _) in enumerate(graph.chunks):
+                x_edge_emb[e0:e1] = self._edge_rows(xn, x_edge_emb[e0:e1], x_edge, e0, e1, graph.chunk_graph(i))
+            return x_edge_emb
+        outs = [run(self._edge_rows, xn, x_edge_emb[e0:e1], x_edge, e0, e1, graph.chunk_graph(i))
+                for i, (e0, e1, _, _) in enumerate(graph.chunks)]
         return torch.cat(outs, 0)
 
-    def _node_rows(self, hx, xm, xe, sub):
-        return self.edge_wise(hx, None if xm is None else xm.to(hx.dtype), xe, sub, "node")
+    def _node_rows(self, hx, xm, x_edge, e0, e1, sub):
+        return self.edge_wise(hx, None if xm is None else xm.to(hx.dtype), x_edge[e0:e1], sub, "node")
 
-    def _edge_rows(self, xn, xee, xe, sub):
+    def _edge_rows(self, xn, xee, x_edge, e0, e1, sub):
         x_in = xee.to(xn.dtype)  # compute dtype of the node stream
-        h = self.edge_wise(xn, x_in, xe, sub, "edge")
+        h = self.edge_wise(xn, x_in, x_edge[e0:e1], sub, "edge")
         h = self.norm_1(h)
         h, res = self.norm_2(h, residual=x_in)
         return (self.atom_wise(h) + res).to(xee.dtype)
+
+
+class EdgeInputs:
+    """Edge features ``[src embedding | Gaussian(d) | dst embedding]`` computed for a row range
+    on use (``x_edge[e0:e1]``), so chunked execution never holds them for every edge."""
+
+    def __init__(self, backbone, batch, dist):
+        self.bb, self.batch, self.dist = backbone, batch, dist
+
+    def __getitem__(self, sl):
+        e0, e1 = sl.start or 0, sl.stop
+        b, bb = self.batch, self.bb
+        return torch.cat([bb.source_embedding(b.src_z[e0:e1]), bb.distance_expansion(self.dist[e0:e1]),
+                          bb.target_embedding(b.dst_z[e0:e1])], dim=1)
+
+    def full(self):
+        return self[0:self.dist.shape[0]]
 
 
 def _rows(x, e0, e1):
@@ -188,19 +210,26 @@ class Graph:
         # (all nodes here; one chunk's destination range in a sub-graph)
         self.out_ptr, self.dst_out, self.num_out = dst_ptr, dst, num_nodes
         self.chunks = None  # [(e0, e1, n0, n1)] for edge-chunked execution
+        self.rot_fn = None  # (e0, e1) -> rotations of those edges, when rot is not stored
 
-    def subgraphs(self):
-        """Sub-graphs of ``chunks`` (built once per forward, shared by every layer so their
-        cached source CSRs are reused)."""
-        if "subgraphs" not in self.cache:
-            self.cache["subgraphs"] = [self.sub(*c) for c in self.chunks]
-        return self.cache["subgraphs"]
+    def chunk_graph(self, i):
+        """Sub-graph of chunk ``i``.  With gradients the sub-graphs are built once per forward
+        and shared by every layer (their cached source CSRs are reused in backward); without
+        gradients they are built on use, and with ``rot_fn`` set the chunk's rotations are
+        computed then instead of being held for every edge."""
+        if torch.is_grad_enabled() or self.rot_fn is None:
+            subs = self.cache.setdefault("subgraphs", {})
+            if i not in subs:
+                subs[i] = self.sub(*self.chunks[i])
+            return subs[i]
+        return self.sub(*self.chunks[i])
 
     def sub(self, e0, e1, n0, n1):
         """Edges [e0, e1) = every edge into nodes [n0, n1) (edges are dst-sorted).  Gathers
         still index all (extended) node rows; the node-path output covers rows [n0, n1)."""
         E = e1 - e0
-        g = Graph(self.src[e0:e1], self.dst[e0:e1], self.rot[e0:e1], (self.dst_ptr - e0).clamp(0, E),
+        rot = self.rot[e0:e1] if self.rot is not None else self.rot_fn(e0, e1)
+        g = Graph(self.src[e0:e1], self.dst[e0:e1], rot, (self.dst_ptr - e0).clamp(0, E),
                   self.num_nodes, self.lmax, self.mmax, None)
         g.num_nodes_ext = getattr(self, "num_nodes_ext", None) or self.num_nodes
         g.out_ptr = (self.dst_ptr[n0:n1 + 1] - e0).contiguous()
@@ -289,16 +318,23 @@ class eSEN_Backbone(nn.Module):
         self.norm = get_normalization_layer(norm_type, lmax, sphere_channels)
 
     # ---------------------------------------------------------------------------------
-    def build_graph(self, batch) -> Graph:
-        edge_attr = batch.edge_attr
+    def _rotations(self, edge_attr):
         vec = edge_attr[:, [2, 3, 1]]  # (x, y, z) -> model frame (y, z, x): polar axis = input z
-        rot = ops.edge_rotation(vec, self.lmax, self.mmax, [getattr(self, f"Jd_{l}") for l in range(self.lmax + 1)],
-                                self.mappingReduced)
+        return ops.edge_rotation(vec, self.lmax, self.mmax, [getattr(self, f"Jd_{l}") for l in range(self.lmax + 1)],
+                                 self.mappingReduced)
+
+    def build_graph(self, batch) -> Graph:
+        chunked = bool(self.edge_chunk and batch.num_edges > self.edge_chunk)
+        # chunked inference computes each chunk's rotations on use instead of holding them all
+        lazy_rot = chunked and not torch.is_grad_enabled()
+        rot = None if lazy_rot else self._rotations(batch.edge_attr)
         g = Graph(batch.edge_index[0], batch.edge_index[1], rot, batch.dst_ptr, batch.num_nodes,
                   self.lmax, self.mmax, getattr(batch, "halo", None))
         g.num_nodes_ext = getattr(batch, "num_nodes_ext", None) or batch.num_nodes
-        if self.edge_chunk and batch.num_edges > self.edge_chunk:
+        if chunked:
             g.chunks = chunk_bounds(batch.dst_ptr.cpu().numpy(), self.edge_chunk)
+            if lazy_rot:
+                g.rot_fn = lambda e0, e1: self._rotations(batch.edge_attr[e0:e1])
         return g
 
     def forward(self, batch):
@@ -313,12 +349,14 @@ class eSEN_Backbone(nn.Module):
         l0 = ops.linear(emb, self.scalar_node_embedding.weight, self.scalar_node_embedding.bias)
         x_node = l0.new_zeros(n_local, self.sph_feature_size, self.sphere_channels)
         x_node[:, 0] = l0
-        gauss = self.distance_expansion(dist)
-        x_edge = torch.cat([self.source_embedding(batch.src_z), gauss, self.target_embedding(batch.dst_z)], dim=1)
-        x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
-        x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
-        if graph.chunks is not None and x_edge_emb is not None:
-            x_edge_emb = x_edge_emb.to(self.edge_stream_dtype)  # edge stream storage between blocks
+        if graph.chunks is None:
+            gauss = self.distance_expansion(dist)
+            x_edge = torch.cat([self.source_embedding(batch.src_z), gauss, self.target_embedding(batch.dst_z)], dim=1)
+            x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
+            x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
+        else:
+            x_edge = EdgeInputs(self, batch, dist)
+            x_node, x_edge_emb = self._degree_embedding_chunked(x_node, x_edge, graph)
         ckpt = self.activation_checkpointing and torch.is_grad_enabled() and graph.chunks is None
         for i in range(self.num_layers):
             x_node = self._run_block(self.node_blocks[i], ckpt, x_node, x_edge_emb, x_edge, graph)
@@ -328,16 +366,49 @@ class eSEN_Backbone(nn.Module):
         out = {"node_embeddings": x_node, "edge_index": batch.edge_index, "edge_distance": dist,
                "edge_distance_vec": batch.edge_attr[:, [2, 3, 1]], "partition": getattr(batch, "halo", None)}
         if self.include_edges and graph.chunks is not None:
-            run = _checkpointed if torch.is_grad_enabled() else (lambda f, *a: f(*a))
             cd = x_node.dtype
-            out["edge_embeddings"] = torch.cat(
-                [run(self._norm_rows, x_edge_emb[e0:e1], cd) for e0, e1, _, _ in graph.chunks], 0)
+            if torch.is_grad_enabled():
+                out["edge_embeddings"] = torch.cat(
+                    [_checkpointed(self._norm_rows, x_edge_emb[e0:e1], cd) for e0, e1, _, _ in graph.chunks], 0)
+            else:  # in place on the edge stream
+                for e0, e1, _, _ in graph.chunks:
+                    x_edge_emb[e0:e1] = self._norm_rows(x_edge_emb[e0:e1], cd)
+                out["edge_embeddings"] = x_edge_emb
             out["edge_chunks"] = [(e0, e1) for e0, e1, _, _ in graph.chunks]
         elif self.include_edges:
             out["edge_embeddings"] = self.norm(x_edge_emb)
         else:
             out.update({"x_edge": x_edge, "graph": graph})
         return out
+
+    def _degree_embedding_chunked(self, x_node, x_edge, graph):
+        """Edge-degree embedding over the edge chunks: node rows of each chunk's destination
+        range (base + scaled sum), and the edge stream (stored as ``edge_stream_dtype``)."""
+        grad = torch.is_grad_enabled()
+        run = _checkpointed if grad else (lambda f, *a: f(*a))
+        ede = self.edge_degree_embedding
+
+        def node_rows(base, e0, e1, sub):
+            return ede(base, x_edge[e0:e1], sub, "node")
+
+        def edge_rows(e0, e1, sub):
+            return ede(None, x_edge[e0:e1], sub, "edge").to(self.edge_stream_dtype)
+
+        parts = [run(node_rows, x_node[n0:n1], e0, e1, graph.chunk_graph(i))
+                 for i, (e0, e1, n0, n1) in enumerate(graph.chunks)]
+        x_node = torch.cat(parts, 0)
+        if not self.include_edges:
+            return x_node, None
+        E = graph.src.shape[0]
+        if grad:
+            x_edge_emb = torch.cat([run(edge_rows, e0, e1, graph.chunk_graph(i))
+                                    for i, (e0, e1, _, _) in enumerate(graph.chunks)], 0)
+        else:
+            x_edge_emb = torch.empty(E, self.sph_feature_size, self.sphere_channels, device=x_node.device,
+                                     dtype=self.edge_stream_dtype)
+            for i, (e0, e1, _, _) in enumerate(graph.chunks):
+                x_edge_emb[e0:e1] = edge_rows(e0, e1, graph.chunk_graph(i))
+        return x_node, x_edge_emb
 
     def _norm_rows(self, x, compute_dtype):
         return self.norm(x.to(compute_dtype)).to(x.dtype)

@@ -165,6 +165,18 @@ class Fock_Irreps_Head(nn.Module):
                                        lay.bias if lay.bias.numel() else None) for lay in layers],
                                      self.gate[spin].act, self.gate[spin].scale, self.reduce_edge and kind != "node")
 
+    def node_labels(self, node_emb, spin=0):
+        """Node label rows of one spin channel (the node part of ``forward``)."""
+        n_sorted = self.process(node_emb, "node", spin)
+        return ops.gather_scale(n_sorted, self._node_gather, self.parity_multiplier if self.reduce_node else None)
+
+    def edge_labels(self, edge_emb, spin=0):
+        """Edge label rows of one spin channel for any subset of edge rows (row-wise; the
+        ``reduce_edge`` head pairs edges and is not row-wise)."""
+        if self.reduce_edge:
+            raise ValueError("edge_labels is row-wise; the reduce_edge head needs all edges")
+        return ops.gather_scale(self.process(edge_emb, "edge", spin), self._edge_gather, None)
+
     def forward(self, emb, batch=None):
         node_emb, edge_emb = emb["node_embeddings"], emb["edge_embeddings"]
         edge_index = emb["edge_index"]

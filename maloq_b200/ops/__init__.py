@@ -91,7 +91,7 @@ def rotate_back_m0_scatter(e, graph, x_node, scale):
     if _cuda(e):
         return _native.rotate_back_m0_scatter(e, graph, x_node, scale)
     y = _ref.rotate_back_m0(e, graph.rot)
-    return x_node + _ref.scatter_sum(y * scale, graph.dst, graph.num_nodes).to(x_node.dtype)
+    return x_node + _ref.scatter_sum(y * scale, graph.dst_out, graph.num_out).to(x_node.dtype)
 
 
 def rotate_back_m0(e, graph):

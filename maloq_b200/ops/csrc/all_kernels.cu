@@ -9,3 +9,4 @@
 #include "comm.cu"
 #include "misc.cu"
 #include "labels.cu"
+#include "graph.cu"

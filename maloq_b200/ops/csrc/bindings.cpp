@@ -7,6 +7,7 @@
 #include "comm.h"
 #include "edge.h"
 #include "gemm.h"
+#include "graph.h"
 #include "labels.h"
 #include "misc.h"
 #include "norm.h"
@@ -188,6 +189,18 @@ void rotate_grad(int64_t L, int64_t MM, at::Tensor G, c10::optional<at::Tensor> 
                                 (int)G.size(2), (int)Rk, (float)scale, stream()));
 }
 
+// Node path of rotate_grad with the destinations' edge ranges (out_ptr [N+1]); G [N, S, C].
+void rotate_grad_nodes(int64_t L, int64_t MM, at::Tensor G, at::Tensor out_ptr, at::Tensor rot,
+                       c10::optional<at::Tensor> DY, c10::optional<at::Tensor> DYf, int64_t Rk, double scale) {
+  chk(G, at::kFloat, "G");
+  chk(out_ptr, at::kLong, "out_ptr");
+  TORCH_CHECK(out_ptr.numel() == G.size(0) + 1, "rotate_grad_nodes: out_ptr has N + 1 entries");
+  const at::cuda::CUDAGuard guard(G.device());
+  check(maloq::edge_rotate_grad_nodes((int)L, (int)MM, G.data_ptr<float>(), ll(out_ptr), rot.data_ptr<float>(),
+                                      DY.has_value() ? bf(*DY) : nullptr, ptr<float>(DYf), (int)G.size(0),
+                                      (int)G.size(2), (int)Rk, (float)scale, stream()));
+}
+
 void gate_fwd(int64_t L, int64_t MM, at::Tensor Y1, at::Tensor H1, int64_t H) {
   chk(Y1, at::kBFloat16, "Y1");
   chk(H1, at::kBFloat16, "H1");
@@ -337,6 +350,67 @@ void basis_rows(at::Tensor in, at::Tensor out, c10::optional<at::Tensor> ptr, c1
   check(maloq::basis_rows(a, stream()));
 }
 
+// Device radius graph (see graph.cu).  grid = [lo0, lo1, lo2, ext0, ext1, ext2, cutoff] (fp64 host
+// list), ncell / periodic 3 ints.  mode 0: cell ids of all atoms -> out_cell; 1: per-target counts;
+// 2: fill src/vec from ptr.
+maloq::RadiusGraphArgs rg_args(const at::Tensor& pos, const std::vector<double>& grid, const std::vector<int64_t>& ncell,
+                               const std::vector<int64_t>& periodic) {
+  chk(pos, at::kDouble, "pos");
+  TORCH_CHECK(pos.dim() == 2 && pos.size(1) == 3, "radius_graph: pos [N, 3]");
+  TORCH_CHECK(grid.size() == 7 && ncell.size() == 3 && periodic.size() == 3, "radius_graph: grid description");
+  maloq::RadiusGraphArgs a{};
+  a.pos = pos.data_ptr<double>();
+  for (int d = 0; d < 3; ++d) {
+    a.lo[d] = grid[d];
+    a.ext[d] = grid[3 + d];
+    a.ncell[d] = (int)ncell[d];
+    a.periodic[d] = (int)periodic[d];
+    TORCH_CHECK(a.ncell[d] >= 1, "radius_graph: ncell >= 1");
+  }
+  a.cutoff = grid[6];
+  return a;
+}
+
+void radius_graph_cells(at::Tensor pos, std::vector<double> grid, std::vector<int64_t> ncell,
+                        std::vector<int64_t> periodic, at::Tensor cell) {
+  auto a = rg_args(pos, grid, ncell, periodic);
+  chk(cell, at::kLong, "cell");
+  TORCH_CHECK(cell.numel() == pos.size(0), "radius_graph_cells: one id per atom");
+  const at::cuda::CUDAGuard guard(pos.device());
+  check(maloq::radius_graph_cells(a, pos.size(0), reinterpret_cast<long long*>(cell.data_ptr<int64_t>()), stream()));
+}
+
+void radius_graph_pass(at::Tensor pos, std::vector<double> grid, std::vector<int64_t> ncell,
+                       std::vector<int64_t> periodic, at::Tensor targets, at::Tensor sorted_atoms,
+                       at::Tensor cell_start, c10::optional<at::Tensor> counts, c10::optional<at::Tensor> ptr_,
+                       c10::optional<at::Tensor> src, c10::optional<at::Tensor> vec) {
+  auto a = rg_args(pos, grid, ncell, periodic);
+  chk(targets, at::kLong, "targets");
+  chk(sorted_atoms, at::kLong, "sorted_atoms");
+  chk(cell_start, at::kLong, "cell_start");
+  TORCH_CHECK(cell_start.numel() == ncell[0] * ncell[1] * ncell[2] + 1, "radius_graph: cell_start [n_cells + 1]");
+  a.targets = ll(targets);
+  a.n_targets = (int)targets.numel();
+  a.sorted_atoms = ll(sorted_atoms);
+  a.cell_start = ll(cell_start);
+  const bool fill = ptr_.has_value();
+  if (fill) {
+    TORCH_CHECK(src && vec, "radius_graph fill: src and vec outputs");
+    chk(*ptr_, at::kLong, "ptr");
+    chk(*src, at::kLong, "src");
+    chk(*vec, at::kDouble, "vec");
+    a.ptr = ll(*ptr_);
+    a.src = reinterpret_cast<long long*>(src->data_ptr<int64_t>());
+    a.vec = vec->data_ptr<double>();
+  } else {
+    TORCH_CHECK(counts.has_value(), "radius_graph count: counts output");
+    chk(*counts, at::kLong, "counts");
+    a.counts = reinterpret_cast<long long*>(counts->data_ptr<int64_t>());
+  }
+  const at::cuda::CUDAGuard guard(pos.device());
+  check(maloq::radius_graph_pass(a, fill, stream()));
+}
+
 int64_t fock_loss_grid(int64_t n) { return maloq::fock_loss_grid(n); }
 
 void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, at::Tensor part) {
@@ -375,6 +449,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("node_reduce", &node_reduce);
   m.def("halo_push", &halo_push);
   m.def("halo_fetch", &halo_fetch);
+  m.def("rotate_grad_nodes", &rotate_grad_nodes);
   m.def("rms_norm_fwd", &rms_norm_fwd);
   m.def("rms_norm_bwd", &rms_norm_bwd);
   m.def("norm_grid", &norm_grid);
@@ -389,6 +464,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fock_loss_grid", &fock_loss_grid);
   m.def("fock_loss_stats", &fock_loss_stats);
   m.def("basis_rows", &basis_rows);
+  m.def("radius_graph_cells", &radius_graph_cells);
+  m.def("radius_graph_pass", &radius_graph_pass);
   m.def("fock_loss_grad", &fock_loss_grad);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
 }

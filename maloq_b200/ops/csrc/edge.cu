@@ -259,6 +259,159 @@ __global__ void __launch_bounds__(128) rotate_grad_kernel(const float* __restric
   }
 }
 
+// ---------------------------------------------------------------- rotate back, channel pairs
+// The same three maps with two adjacent channels per thread (bf16x2 / float2 accesses, two FMAs
+// per rotation entry) and Q edges in flight per CTA (Q "edge lanes" of 64 channel pairs).  Used
+// when C, ldy and koff are even.  Node paths walk a destination's edges through its CSR range;
+// the lanes' partial sums are combined in shared memory in a fixed order (deterministic).
+template <int S>
+struct EdgeLanes {
+  static constexpr int Q = S <= 25 ? 4 : 2;
+};
+
+template <int L, int MM>
+__global__ void __launch_bounds__(256) rotate_back_scatter2_kernel(
+    const __nv_bfloat16* __restrict__ Y, int ldy, int koff, const float* __restrict__ rot,
+    const long long* __restrict__ dst_ptr, const float* __restrict__ base, float* __restrict__ out, int N, int C,
+    int Rk, float scale) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R, Q = EdgeLanes<S>::Q;
+  extern __shared__ float2 red2[];  // [Q-1][S][64]
+  const int n = blockIdx.x;
+  const int cp = threadIdx.x % 64, q = threadIdx.x / 64;
+  const int c = 2 * (blockIdx.y * 64 + cp);
+  const bool active = c < C;
+  float2 acc[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) acc[j] = make_float2(0.f, 0.f);
+  if (active) {
+#pragma unroll 1
+    for (long long e = dst_ptr[n] + q; e < dst_ptr[n + 1]; e += Q) {
+      const float* re = rot + (size_t)e * R * S;
+      const __nv_bfloat16* ye = Y + (size_t)e * ldy + koff + c;
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        if (k >= Rk) break;
+        const int l = F::row_l(k);
+        const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ye + (size_t)k * C));
+#pragma unroll
+        for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
+          const float r = __ldg(re + k * S + j);
+          acc[j].x += r * y.x;
+          acc[j].y += r * y.y;
+        }
+      }
+    }
+  }
+  if (q > 0) {
+#pragma unroll
+    for (int j = 0; j < S; ++j) red2[((q - 1) * S + j) * 64 + cp] = acc[j];
+  }
+  __syncthreads();
+  if (q > 0 || !active) return;
+#pragma unroll
+  for (int p = 0; p < Q - 1; ++p)
+#pragma unroll
+    for (int j = 0; j < S; ++j) {
+      const float2 v = red2[(p * S + j) * 64 + cp];
+      acc[j].x += v.x;
+      acc[j].y += v.y;
+    }
+  float* o = out + (size_t)n * S * C + c;
+  const float* b = base ? base + (size_t)n * S * C + c : nullptr;
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    float2 v = make_float2(acc[j].x * scale, acc[j].y * scale);
+    if (b) {
+      const float2 bv = *reinterpret_cast<const float2*>(b + (size_t)j * C);
+      v.x += bv.x;
+      v.y += bv.y;
+    }
+    *reinterpret_cast<float2*>(o + (size_t)j * C) = v;
+  }
+}
+
+template <int L, int MM>
+__global__ void __launch_bounds__(256) rotate_back_edge2_kernel(const __nv_bfloat16* __restrict__ Y, int ldy,
+                                                                int koff, const float* __restrict__ rot,
+                                                                float* __restrict__ out, int E, int C, int Rk) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R, Q = EdgeLanes<S>::Q;
+  const int cp = threadIdx.x % 64, q = threadIdx.x / 64;
+  const long long e = (long long)blockIdx.x * Q + q;
+  const int c = 2 * (blockIdx.y * 64 + cp);
+  if (e >= E || c >= C) return;
+  float2 acc[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) acc[j] = make_float2(0.f, 0.f);
+  const float* re = rot + (size_t)e * R * S;
+  const __nv_bfloat16* ye = Y + (size_t)e * ldy + koff + c;
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    if (k >= Rk) break;
+    const int l = F::row_l(k);
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(ye + (size_t)k * C));
+#pragma unroll
+    for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
+      const float r = __ldg(re + k * S + j);
+      acc[j].x += r * y.x;
+      acc[j].y += r * y.y;
+    }
+  }
+  float* o = out + (size_t)e * S * C + c;
+#pragma unroll
+  for (int j = 0; j < S; ++j) *reinterpret_cast<float2*>(o + (size_t)j * C) = acc[j];
+}
+
+// DY[e, k*C + c] = scale * sum_j rot[e,k,j] G[row, j, c]: node path (row = destination n, its
+// edges out_ptr[n] .. out_ptr[n+1]: G[n] is loaded once per edge lane) or edge path (row = e).
+template <int L, int MM, bool NODE>
+__global__ void __launch_bounds__(256) rotate_grad2_kernel(const float* __restrict__ G,
+                                                           const long long* __restrict__ out_ptr,
+                                                           const float* __restrict__ rot,
+                                                           __nv_bfloat16* __restrict__ DY, float* __restrict__ DYf,
+                                                           int rows, int C, int Rk, float scale) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R, Q = EdgeLanes<S>::Q;
+  const int cp = threadIdx.x % 64, q = threadIdx.x / 64;
+  const int c = 2 * (blockIdx.y * 64 + cp);
+  long long r, e0, e1;
+  if (NODE) {
+    r = blockIdx.x;
+    e0 = out_ptr[r] + q;
+    e1 = out_ptr[r + 1];
+  } else {
+    r = (long long)blockIdx.x * Q + q;
+    e0 = r;
+    e1 = r + 1;
+  }
+  if (r >= rows || c >= C) return;
+  float2 g[S];
+#pragma unroll
+  for (int j = 0; j < S; ++j) g[j] = __ldg(reinterpret_cast<const float2*>(G + ((size_t)r * S + j) * C + c));
+#pragma unroll 1
+  for (long long e = e0; e < e1; e += (NODE ? Q : 1)) {
+    const float* re = rot + (size_t)e * R * S;
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (k >= Rk) break;
+      const int l = F::row_l(k);
+      float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
+        const float rv = __ldg(re + k * S + j);
+        acc.x += rv * g[j].x;
+        acc.y += rv * g[j].y;
+      }
+      acc.x *= scale;
+      acc.y *= scale;
+      const size_t o = ((size_t)e * Rk + k) * C + c;
+      if (DY) *reinterpret_cast<__nv_bfloat162*>(DY + o) = __floats2bfloat162_rn(acc.x, acc.y);
+      if (DYf) *reinterpret_cast<float2*>(DYf + o) = acc;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- gate (m-major)
 // Y1 [E, G + R*H] with G = L*H gate pre-activations; H1 [E, R*H]:
 // H1[e,0,h] = silu(Y1[e, G+h]); H1[e,k,h] = Y1[e, G+k*H+h] * tanh(Y1[e, (l_k-1)*H + h])
@@ -392,6 +545,14 @@ const char* edge_rotate_back_scatter(int L, int MM, const __nv_bfloat16* Y, int 
                                      float scale, cudaStream_t st) {
   MM = clampm(L, MM);
   if (N == 0) return nullptr;
+  if (C % 2 == 0 && ldy % 2 == 0 && koff % 2 == 0) {
+    dim3 grid(N, (C / 2 + 63) / 64);
+    MALOQ_DISPATCH_FRAME(({
+      constexpr int S_ = (FL + 1) * (FL + 1), Q_ = EdgeLanes<S_>::Q;
+      rotate_back_scatter2_kernel<FL, FM><<<grid, 64 * Q_, (Q_ - 1) * S_ * 64 * sizeof(float2), st>>>(
+          Y, ldy, koff, rot, dst_ptr, base, out, N, C, Rk, scale);
+    }))
+  }
   dim3 grid(N, (C + 127) / 128);
   MALOQ_DISPATCH_FRAME((rotate_back_scatter_kernel<FL, FM><<<grid, 128, 0, st>>>(Y, ldy, koff, rot, dst_ptr, base,
                                                                                   out, N, C, Rk, scale)))
@@ -401,6 +562,13 @@ const char* edge_rotate_back(int L, int MM, const __nv_bfloat16* Y, int ldy, int
                              int E, int C, int Rk, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
+  if (C % 2 == 0 && ldy % 2 == 0 && koff % 2 == 0) {
+    MALOQ_DISPATCH_FRAME(({
+      constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
+      dim3 grid((E + Q_ - 1) / Q_, (C / 2 + 63) / 64);
+      rotate_back_edge2_kernel<FL, FM><<<grid, 64 * Q_, 0, st>>>(Y, ldy, koff, rot, out, E, C, Rk);
+    }))
+  }
   dim3 grid(E, (C + 127) / 128);
   MALOQ_DISPATCH_FRAME((rotate_back_edge_kernel<FL, FM><<<grid, 128, 0, st>>>(Y, ldy, koff, rot, out, E, C, Rk)))
 }
@@ -409,8 +577,27 @@ const char* edge_rotate_grad(int L, int MM, const float* G, const long long* row
                              __nv_bfloat16* DY, float* DYf, int E, int C, int Rk, float scale, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
+  if (rows == nullptr && C % 2 == 0) {
+    MALOQ_DISPATCH_FRAME(({
+      constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
+      dim3 grid((E + Q_ - 1) / Q_, (C / 2 + 63) / 64);
+      rotate_grad2_kernel<FL, FM, false><<<grid, 64 * Q_, 0, st>>>(G, nullptr, rot, DY, DYf, E, C, Rk, scale);
+    }))
+  }
   dim3 grid(E, (C + 127) / 128);
   MALOQ_DISPATCH_FRAME((rotate_grad_kernel<FL, FM><<<grid, 128, 0, st>>>(G, rows, rot, DY, DYf, E, C, Rk, scale)))
+}
+
+const char* edge_rotate_grad_nodes(int L, int MM, const float* G, const long long* out_ptr, const float* rot,
+                                   __nv_bfloat16* DY, float* DYf, int N, int C, int Rk, float scale, cudaStream_t st) {
+  MM = clampm(L, MM);
+  if (N == 0) return nullptr;
+  if (C % 2) return "rotate_grad_nodes: even channel count required";
+  dim3 grid(N, (C / 2 + 63) / 64);
+  MALOQ_DISPATCH_FRAME(({
+    constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
+    rotate_grad2_kernel<FL, FM, true><<<grid, 64 * Q_, 0, st>>>(G, out_ptr, rot, DY, DYf, N, C, Rk, scale);
+  }))
 }
 
 const char* edge_gate_fwd(int L, int MM, const __nv_bfloat16* Y1, __nv_bfloat16* H1, int E, int H, cudaStream_t st) {

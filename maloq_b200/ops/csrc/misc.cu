@@ -42,12 +42,29 @@ __global__ void edge_rotation_kernel(const float* __restrict__ vec, long long ld
   const float* Jl = J + T.joff[l];
   float* out = ROT + (e * T.R + k) * T.S;
   for (int j = 0; j < T.S; ++j) out[j] = 0.f;
-  // cos/sin of f * angle for f = l - a, a = 0..2l
+  // cos/sin of f * angle for f = l - a, a = 0..2l: one sincosf per angle, multiples by the
+  // recurrence cos(f t) = 2 cos t cos((f-1) t) - cos((f-2) t) (same for sin), f <= 6
   float cb[13], sb[13], ca[13], sa[13];
-  for (int a = 0; a < d; ++a) {
-    const float f = (float)(l - a);
-    sincosf(-f * beta, &sb[a], &cb[a]);
-    sincosf(-f * alpha, &sa[a], &ca[a]);
+  {
+    float cbf[7], sbf[7], caf[7], saf[7];
+    cbf[0] = caf[0] = 1.f;
+    sbf[0] = saf[0] = 0.f;
+    sincosf(-beta, &sbf[1], &cbf[1]);
+    sincosf(-alpha, &saf[1], &caf[1]);
+    for (int f = 2; f <= l; ++f) {
+      cbf[f] = 2.f * cbf[1] * cbf[f - 1] - cbf[f - 2];
+      sbf[f] = 2.f * cbf[1] * sbf[f - 1] - sbf[f - 2];
+      caf[f] = 2.f * caf[1] * caf[f - 1] - caf[f - 2];
+      saf[f] = 2.f * caf[1] * saf[f - 1] - saf[f - 2];
+    }
+    for (int a = 0; a < d; ++a) {
+      const int f = l - a;  // cos is even, sin odd in f
+      const int af = f < 0 ? -f : f;
+      cb[a] = cbf[af];
+      ca[a] = caf[af];
+      sb[a] = f < 0 ? -sbf[af] : sbf[af];
+      sa[a] = f < 0 ? -saf[af] : saf[af];
+    }
   }
   // D[i][b] = sum_a J[i][a] * M[a][b],  M = X(-beta) J X(-alpha)
   for (int b = 0; b < d; ++b) {

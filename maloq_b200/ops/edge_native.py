@@ -149,7 +149,7 @@ class EdgewiseFn(torch.autograd.Function):
         dev = g.device
         g = g.contiguous().float()
         dY2 = torch.empty(E, R * C, device=dev, dtype=torch.bfloat16)
-        lib.rotate_grad(*LM, g, graph.dst_out if meta["node"] else None, graph.rot, dY2, None, R, 1.0)
+        _rotate_grad(LM, g, graph, meta["node"], dY2, None, R, 1.0)
         hb = _blocks(meta["m_size"], H)
         cb = _blocks(meta["m_size"], C)
         ab = _blocks(meta["m_size"], Cin)
@@ -210,6 +210,16 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
     return EdgewiseFn.apply(x_src_space, x_msg_edge, rad, c1.fc_m0.bias, c2.fc_m0.bias, graph, meta, halo, *weights)
 
 
+def _rotate_grad(LM, g, graph, node, DY, DYf, Rk, scale):
+    """Backward of rotate-back: node path walks each output row's edge range (``out_ptr``),
+    the edge path maps edge to edge."""
+    lib = _lib()
+    if node and g.shape[2] % 2 == 0:
+        lib.rotate_grad_nodes(*LM, g, graph.out_ptr, graph.rot, DY, DYf, Rk, scale)
+    else:
+        lib.rotate_grad(*LM, g, graph.dst_out if node else None, graph.rot, DY, DYf, Rk, scale)
+
+
 def _halo_args(halo):
     """(peer pointer table, halo owner, halo row, n_own) for the gather kernels."""
     if halo is None:
@@ -229,8 +239,9 @@ class RotateBackM0Fn(torch.autograd.Function):
         S = (graph.lmax + 1) ** 2
         Y = e.reshape(E, n0 * C).to(torch.bfloat16).contiguous()
         if base is not None:
-            out = torch.empty(graph.num_nodes, S, C, device=e.device, dtype=torch.float32)
-            lib.rotate_back_scatter(graph.lmax, graph.mmax, Y, 0, n0, graph.rot, graph.dst_ptr, base.contiguous().float(), out, scale)
+            out = torch.empty(graph.num_out, S, C, device=e.device, dtype=torch.float32)
+            lib.rotate_back_scatter(graph.lmax, graph.mmax, Y, 0, n0, graph.rot, graph.out_ptr,
+                                    base.contiguous().float(), out, scale)
         else:
             out = torch.empty(E, S, C, device=e.device, dtype=torch.float32)
             lib.rotate_back_edge(graph.lmax, graph.mmax, Y, 0, n0, graph.rot, out)
@@ -245,8 +256,7 @@ class RotateBackM0Fn(torch.autograd.Function):
         E = graph.src.shape[0]
         C = g.shape[2]
         de = torch.empty(E, ctx.n0 * C, device=g.device, dtype=torch.float32)
-        _lib().rotate_grad(graph.lmax, graph.mmax, g, graph.dst if ctx.node else None, graph.rot, None, de, ctx.n0,
-                           ctx.scale if ctx.node else 1.0)
+        _rotate_grad((graph.lmax, graph.mmax), g, graph, ctx.node, None, de, ctx.n0, ctx.scale if ctx.node else 1.0)
         count_launches(1)
         return de.view(E, ctx.n0, C), (g if ctx.node else None), None, None
 

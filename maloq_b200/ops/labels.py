@@ -48,9 +48,17 @@ def blocks_to_coupled(data, block_ptr, pair_type, pos_table, transform):
     return transform.get_net_out(_ref_m2l(data, block_ptr, pair_type, pos_table))
 
 
-def coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data):
+def coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data, out=None):
     """Block-sparse data of coupled label rows: ``labels_to_matrix(get_H(...))`` in one pass on
-    CUDA (block-diagonal transform + scatter)."""
+    CUDA (block-diagonal transform + scatter).  ``block_ptr[r]`` is row r's data offset; with
+    ``out`` the rows' blocks are written into that buffer (other entries untouched)."""
     if _cuda(coupled):
-        return _native.coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data)
-    return _ref_l2m(transform.get_H(coupled), block_ptr, pair_type, pos_table, n_data)
+        return _native.coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data, out)
+    unc = transform.get_H(coupled)
+    if out is None:
+        return _ref_l2m(unc, block_ptr, pair_type, pos_table, n_data)
+    pos = pos_table.index_select(0, pair_type)
+    valid = pos >= 0
+    flat = (block_ptr[: pos.shape[0]].unsqueeze(1) + pos.clamp(min=0))[valid]
+    out[flat] = unc[valid].to(out.dtype)
+    return out

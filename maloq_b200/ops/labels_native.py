@@ -107,11 +107,18 @@ def blocks_to_coupled(data, block_ptr, pair_type, pos_table, transform):
     return out.to(data.dtype)
 
 
-def coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data):
+def coupled_to_blocks(coupled, block_ptr, pair_type, pos_table, transform, n_data, out=None):
     dt = _dtype(coupled)
     meta, coef = _tables(transform, False, coupled.device, dt)
     ptr, pt = _rows(block_ptr, pair_type)
     rows = pt.numel()
+    if out is not None:
+        if out.dtype != dt or not out.is_contiguous():
+            raise ValueError("coupled_to_blocks: out must be a contiguous buffer of the label dtype")
+        _lib().basis_rows(coupled.to(dt).contiguous(), out, ptr, pt, _pos32(pos_table), meta, coef,
+                          coupled.shape[1], rows, False, True)
+        count_launches(1)
+        return out
     out = torch.zeros(int(n_data), device=coupled.device, dtype=dt)
     _lib().basis_rows(coupled.to(dt).contiguous(), out, ptr, pt, _pos32(pos_table), meta, coef, coupled.shape[1], rows,
                       False, True)

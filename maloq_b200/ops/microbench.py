@@ -3,6 +3,7 @@
     python -m maloq_b200.ops.microbench gemm [--bn 128] [--edges 43408]
     python -m maloq_b200.ops.microbench edge [--edges 43408]
     python -m maloq_b200.ops.microbench labels [--rows 236000] [--kind large]
+    python -m maloq_b200.ops.microbench suite [--edges 43408] [--passes 2]
 
 ``gemm`` runs the first SO(2) convolution of one drug-like-config layer as one grouped
 launch: M = edges, (N, K) = (1152, 1280), (1024, 1024), (768, 768), bf16 in/out.
@@ -73,13 +74,14 @@ def bench_edge(edges):
     rot = torch.randn(edges, R, S, device=dev)
     rad = torch.randn(edges, 12 * Cin, device=dev)
     A = torch.empty(edges, R * Cin, device=dev, dtype=torch.bfloat16)
-    ms = _timeit(lambda: lib.gather_rotate_fwd(4, 2, x, None, src, dst, rot, rad, A, Cin))
+    ms = _timeit(lambda: lib.gather_rotate_fwd(4, 2, x, None, src, dst, rot, rad, A, Cin, 0, None, None, 0))
     byt = edges * (S * Cin * 4 + R * S * 4 + 12 * Cin * 4 + R * Cin * 2)
     print(f"gather_rotate_fwd: {ms * 1e3:.1f} us, {byt / ms / 1e9:.2f} TB/s algorithmic")
     DS = torch.empty(edges, S, C, device=dev)
     DD = torch.empty(edges, S, C, device=dev)
     DR = torch.empty_like(rad)
-    ms = _timeit(lambda: lib.gather_rotate_bwd(4, 2, x, None, src, dst, rot, rad, A, DS, DD, None, DR, Cin))
+    ms = _timeit(lambda: lib.gather_rotate_bwd(4, 2, x, None, src, dst, rot, rad, A, DS, DD, None, DR, Cin, 0, None,
+                                               None, 0))
     byt = edges * (S * Cin * 4 * 2 + R * S * 4 + 12 * Cin * 4 * 2 + R * Cin * 2)
     print(f"gather_rotate_bwd: {ms * 1e3:.1f} us, {byt / ms / 1e9:.2f} TB/s algorithmic, "
           f"error_status={kernels.error_status()}")
@@ -112,9 +114,142 @@ def bench_labels(rows, kind):
           f"coupled->blocks {ms2 * 1e3:.1f} us ({byts / ms2 / 1e6:.0f} GB/s)")
 
 
+def suite_calls(edges=43408, device="cuda"):
+    """One launch of every single-GPU kernel of the library at drug-like-config shapes (L=4,
+    m=2, C=128, ``edges`` edges, 36 edges per node): a list of (name, zero-argument call that
+    launches exactly one kernel).  Used to profile each kernel once (``suite``)."""
+    from . import kernels
+    from ..data import datasets
+    from ..core.sph import J_matrices
+    from ..models.so3 import CoefficientMapping
+    from . import labels_native
+
+    lib = kernels.lib()
+    dev = torch.device(device, 0) if device == "cuda" else torch.device(device)
+    torch.manual_seed(0)
+    E, C, S, R, H, L, MM = edges, 128, 25, 19, 128, 4, 2
+    Cin = 2 * C
+    N = max(2, E // 36)
+    x = torch.randn(N, S, C, device=dev)
+    src = torch.randint(0, N, (E,), device=dev)
+    dst = torch.sort(torch.randint(0, N, (E,), device=dev)).values
+    dst_ptr = torch.zeros(N + 1, dtype=torch.long, device=dev)
+    dst_ptr[1:] = torch.cumsum(torch.bincount(dst, minlength=N), 0)
+    perm = torch.argsort(src, stable=True)
+    sptr = torch.zeros(N + 1, dtype=torch.long, device=dev)
+    sptr[1:] = torch.cumsum(torch.bincount(src, minlength=N), 0)
+    vec = torch.randn(E, 3, device=dev)
+    mapping = CoefficientMapping(L, MM)
+    Js = J_matrices(L)
+    flat = torch.cat([J.reshape(-1).float() for J in Js]).to(dev)
+    joff = [sum((2 * k + 1) ** 2 for k in range(l)) for l in range(L + 1)]
+    rot = torch.empty(E, R, S, device=dev)
+    rad = torch.randn(E, 12 * Cin, device=dev)
+    A = torch.empty(E, R * Cin, device=dev, dtype=torch.bfloat16)
+    DS, DD, DR = torch.empty(E, S, C, device=dev), torch.empty(E, S, C, device=dev), torch.empty_like(rad)
+    DX = torch.empty(N, S, C, device=dev)
+    G = 4 * H  # gate scalars of the m = 0 block
+    Y1 = torch.randn(E, G + R * H, device=dev).bfloat16()
+    H1 = torch.empty(E, R * H, device=dev, dtype=torch.bfloat16)
+    dY1 = torch.empty_like(Y1)
+    Y2 = torch.randn(E, R * C, device=dev).bfloat16()
+    out_n = torch.empty(N, S, C, device=dev)
+    out_e = torch.empty(E, S, C, device=dev)
+    g_n = torch.randn(N, S, C, device=dev)
+    dY2 = torch.empty(E, R * C, device=dev, dtype=torch.bfloat16)
+    shapes = [(1152, 1280), (1024, 1024), (768, 768)]
+    Aop = torch.randn(E, 19 * 256, device=dev).bfloat16()
+    offs = [0, 1280, 1280 + 2048]
+    As = [Aop[:, o:o + k] for o, (n, k) in zip(offs, shapes)]
+    Ws = [torch.randn(n, k, device=dev).bfloat16() for n, k in shapes]
+    Cs = [torch.empty(E, n, device=dev, dtype=torch.bfloat16) for n, k in shapes]
+    gy = torch.randn(E, 1152, device=dev).bfloat16()
+    part = torch.empty(8, 1152, 1280, device=dev)
+    wout = torch.empty(1152, 1280, device=dev)
+    aw, ab = torch.rand(L + 1, C, device=dev), torch.rand(C, device=dev)
+    ssum = torch.empty_like(x)
+    rpart = torch.empty(148 * 4, L + 2, C, device=dev)
+    xl = torch.randn(E, 128, device=dev)
+    wl, bl = torch.rand(128, device=dev), torch.rand(128, device=dev)
+    yl = torch.empty(E, 128, device=dev, dtype=torch.bfloat16)
+    dxl = torch.empty_like(xl)
+    lpart = torch.empty(148 * 4 * 8, 2, 128, device=dev)
+    gates = torch.rand(N, L * C, device=dev)
+    xg = torch.randn(N, S, C, device=dev)
+    og, dxg, dg = torch.empty_like(xg), torch.empty_like(xg), torch.empty_like(gates)
+    labeler = datasets.labeler_for("druglike", dev)
+    D = labeler.target_len
+    tbl = labeler.table
+    pt = torch.randint(0, tbl.n_types * tbl.n_types, (E,), device=dev)
+    sizes = torch.as_tensor(tbl.norb, device=dev)[pt // tbl.n_types] * torch.as_tensor(tbl.norb, device=dev)[
+        pt % tbl.n_types]
+    bptr = torch.zeros(E + 1, dtype=torch.long, device=dev)
+    bptr[1:] = torch.cumsum(sizes, 0)
+    data = torch.randn(int(bptr[-1]), device=dev)
+    meta, coef = labels_native._tables(labeler.transform, True, dev, torch.float32)
+    pos32 = labels_native._pos32(labeler.pos_t)
+    coupled = torch.empty(E, D, device=dev)
+    tgt = torch.randn(E, D, device=dev)
+    mask = torch.as_tensor(tbl.mask, device=dev, dtype=torch.uint8).contiguous()
+    lgrid = lib.fock_loss_grid(E * D)
+    lstat = torch.empty(lgrid, 3, device=dev)
+    lgrad = torch.empty_like(tgt)
+    ls, ms = mapping.l_harmonic.tolist(), mapping.m_complex.tolist()
+    return [
+        ("edge_rotation", lambda: lib.edge_rotation(vec, flat, joff, L, ls, ms, rot)),
+        ("gemm_tc2 (conv1 grouped, 2-SM)", lambda: lib.gemm(As, Ws, Cs, [None] * 3, False, 0, 1.0, 1, 128)),
+        ("gemm_tc (weight grad, split-K)", lambda: lib.gemm([gy], [Aop[:, :1280]], [part], [None], True, 0, 1.0, 8,
+                                                            128)),
+        ("splitk_reduce", lambda: lib.splitk_reduce(part, wout, 0.0)),
+        ("gather_rotate_fwd", lambda: lib.gather_rotate_fwd(L, MM, x, None, src, dst, rot, rad, A, Cin, 0, None, None,
+                                                            0)),
+        ("gather_rotate_bwd", lambda: lib.gather_rotate_bwd(L, MM, x, None, src, dst, rot, rad, A, DS, DD, None, DR,
+                                                            Cin, 0, None, None, 0)),
+        ("node_reduce", lambda: lib.node_reduce(DD, dst_ptr, DS, perm, sptr, DX)),
+        ("gate_fwd", lambda: lib.gate_fwd(L, MM, Y1, H1, H)),
+        ("gate_bwd", lambda: lib.gate_bwd(L, MM, Y1, H1, dY1, H)),
+        ("rotate_back_scatter", lambda: lib.rotate_back_scatter(L, MM, Y2, 0, R, rot, dst_ptr, None, out_n, 1.0)),
+        ("rotate_back_edge", lambda: lib.rotate_back_edge(L, MM, Y2, 0, R, rot, out_e)),
+        ("rotate_grad", lambda: lib.rotate_grad(L, MM, g_n, dst, rot, dY2, None, R, 1.0)),
+        ("rms_norm_fwd", lambda: lib.rms_norm_fwd(L, x, x, aw, ab, out_n, ssum, 1e-5)),
+        ("rms_norm_bwd", lambda: lib.rms_norm_bwd(L, ssum, g_n, g_n, aw, DX, rpart, 1e-5)),
+        ("ln_silu_fwd", lambda: lib.ln_silu_fwd(xl, wl, bl, yl, 1e-5)),
+        ("ln_silu_bwd", lambda: lib.ln_silu_bwd(xl, wl, bl, yl, dxl, lpart, 1e-5)),
+        ("gate_l_fwd", lambda: lib.gate_l_fwd(L, xg, gates, og)),
+        ("gate_l_bwd", lambda: lib.gate_l_bwd(L, xg, gates, og, dxg, dg)),
+        ("basis_rows (blocks -> coupled)", lambda: lib.basis_rows(data, coupled, bptr, pt, pos32, meta, coef, D, E,
+                                                                 True, False)),
+        ("fock_loss_stats", lambda: lib.fock_loss_stats(coupled, tgt, pt, mask, lstat)),
+        ("fock_loss_grad", lambda: lib.fock_loss_grad(coupled, tgt, pt, mask, 1.0, 0.5, lgrad)),
+    ]
+
+
+def bench_suite(edges, passes):
+    """``passes`` passes over :func:`suite_calls` (one launch each), timing every kernel with
+    CUDA events on the last pass."""
+    from . import kernels
+
+    calls = suite_calls(edges)
+    print(f"suite: {len(calls)} kernels per pass, {passes} passes")
+    for p in range(passes):
+        for name, fn in calls:
+            if p + 1 < passes:
+                fn()
+                continue
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            print(f"  {name:34s} {s.elapsed_time(e) * 1e3:9.1f} us")
+    torch.cuda.synchronize()
+    print(f"error_status={kernels.error_status()}")
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "edge", "shape", "labels"])
+    ap.add_argument("what", choices=["gemm", "edge", "shape", "labels", "suite"])
+    ap.add_argument("--passes", type=int, default=2)
     ap.add_argument("--rows", type=int, default=236000)
     ap.add_argument("--kind", default="large")
     ap.add_argument("--M", type=int, default=32768)
@@ -126,6 +261,8 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.what == "shape":
         bench_gemm_shape(a.M, a.N, a.K, a.bn, a.fp32_out)
+    elif a.what == "suite":
+        bench_suite(a.edges, a.passes)
     elif a.what == "labels":
         bench_labels(a.rows, a.kind)
     elif a.what == "gemm":

@@ -135,3 +135,38 @@ def partition_batch(sample, domain, pair_table=None, device="cpu", transport="co
     b.halo = HaloPlan(domain, device, group=group, transport=transport)
     b.num_nodes_ext = domain.n_ext
     return b
+
+
+def local_batch(z, pos, dom, src_local, dst_local, vec, dst_ptr, pair_table=None, device="cuda",
+                transport="peer", group=None, charge=0, spin=1):
+    """The GraphBatch of one rank from its own edges (device tensors from the device radius
+    graph: ``src_local`` in the [owned | halo] numbering of ``dom``, ``dst_local`` owned rows,
+    ``vec = pos[src] - pos[dst]``, ``dst_ptr``), without any global edge list."""
+    from ..data.batch import GraphBatch
+
+    dev = torch.device(device)
+    own_t = torch.as_tensor(dom.owned, device=dev)
+    ext_t = torch.as_tensor(np.concatenate([dom.owned, dom.halo]), device=dev)
+    z_t = torch.as_tensor(np.asarray(z), device=dev)
+    n_own = dom.n_own
+    src_g = ext_t[src_local]
+    vec = vec.to(dev)
+    edge_attr = torch.cat([vec.norm(dim=1, keepdim=True), vec], 1).float()
+    z_own = z_t[own_t]
+    b = GraphBatch(
+        atomic_numbers=z_own, pos=torch.as_tensor(np.asarray(pos)[dom.owned], dtype=torch.float32, device=dev),
+        atom_charge=torch.full((n_own,), charge, dtype=torch.long, device=dev),
+        atom_spin=torch.full((n_own,), spin, dtype=torch.long, device=dev),
+        batch=torch.zeros(n_own, dtype=torch.long, device=dev),
+        edge_index=torch.stack([src_local.to(dev), dst_local.to(dev)]), edge_attr=edge_attr,
+        dst_ptr=dst_ptr.to(dev), src_z=z_t[src_g], dst_z=z_own[dst_local.to(dev)],
+        num_atoms_in_molecule=torch.tensor([n_own], device=dev), global_node_ids=own_t,
+    )
+    if pair_table is not None:
+        zt = torch.as_tensor(pair_table.z_to_type, device=dev)
+        nt = pair_table.n_types
+        b.node_pair_type = zt[z_own] * nt + zt[z_own]
+        b.edge_pair_type = zt[b.src_z] * nt + zt[b.dst_z]
+    b.halo = HaloPlan(dom, dev, group=group, transport=transport)
+    b.num_nodes_ext = dom.n_ext
+    return b

@@ -95,3 +95,38 @@ def load_partitioned_hamiltonian(folder, labeler, symmetrize=True) -> BlockSpars
         blocks = sym
     ptr = np.concatenate([[0], np.cumsum([len(b) for b in blocks])]).astype(np.int64)
     return BlockSparseMatrix(rows, cols, ptr, np.concatenate(blocks) if blocks else np.zeros(0), orb_ptr)
+
+
+@torch.no_grad()
+def hamiltonian_shard(head, emb, batch, labeler, spin=0, out=None):
+    """This rank's block-sparse Hamiltonian on the device, streamed: the edge blocks are made
+    chunk by chunk (head -> coupled labels -> fused CG transform + scatter into the block data,
+    ``coupled_to_blocks``), then the owned atoms' diagonal blocks, so no [E, D] label tensor is
+    formed.  Block order: local edges (dst-sorted), then owned atoms.  Returns
+    (data [n_data] fp32, block_ptr [n_blocks + 1] int64) on the device; ``out`` reuses a data
+    buffer of the right size."""
+    from ..ops import labels as lab
+
+    dev = batch.atomic_numbers.device
+    tbl = labeler.table
+    zt = torch.as_tensor(tbl.z_to_type, device=dev)
+    norb = torch.as_tensor(tbl.norb, device=dev)
+    n_src = norb[zt[batch.src_z]]
+    n_dst = norb[zt[batch.dst_z]]
+    n_at = norb[zt[batch.atomic_numbers]]
+    sizes = torch.cat([n_src * n_dst, n_at * n_at])
+    ptr = torch.zeros(sizes.numel() + 1, dtype=torch.long, device=dev)
+    ptr[1:] = torch.cumsum(sizes, 0)
+    n_data = int(ptr[-1])
+    data = out if out is not None and out.numel() == n_data else torch.empty(n_data, device=dev)
+    E = batch.num_edges
+    pos_t, T = labeler.pos_t.to(dev), labeler.transform
+    chunks = emb.get("edge_chunks") or [(0, E)]
+    edge_emb = emb["edge_embeddings"]
+    node_dtype = emb["node_embeddings"].dtype
+    for e0, e1 in chunks:
+        lbl = head.edge_labels(edge_emb[e0:e1].to(node_dtype), spin)
+        lab.coupled_to_blocks(lbl, ptr[e0:e1 + 1], batch.edge_pair_type[e0:e1], pos_t, T, n_data, out=data)
+    nl = head.node_labels(emb["node_embeddings"], spin)
+    lab.coupled_to_blocks(nl, ptr[E:], batch.node_pair_type, pos_t, T, n_data, out=data)
+    return data, ptr

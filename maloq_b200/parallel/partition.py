@@ -50,7 +50,8 @@ def partition_slab(n, world, pos=None, dst=None, cell=None, **_):
     ext = np.ptp(pos, axis=0) if cell is None else np.asarray(cell)
     ax = int(np.argmax(ext))
     order = np.argsort(pos[:, ax], kind="stable")
-    deg = np.bincount(dst, minlength=n) + 1
+    # balance in-degree + 1 per rank (equal atom counts when no edge list exists yet)
+    deg = np.bincount(dst, minlength=n) + 1 if dst is not None else np.ones(n, dtype=np.int64)
     cuts = _balanced_cuts(deg[order], world)
     part = np.zeros(n, dtype=np.int64)
     bounds = [0] + list(cuts) + [n]
@@ -188,3 +189,42 @@ def decompose(part, src, dst, world):
         d.recv_counts = [int((d.halo_owner == p).sum()) for p in range(world)]
         d.send = [doms[p].halo_row[doms[p].halo_owner == r] for p in range(world)]
     return doms
+
+
+def local_domain(part, rank, world, src_global, group=None):
+    """This rank's :class:`Domain` from its own edges only (edges into the owned atoms, sorted
+    by (owned row, source); ``src_global`` their global source ids), for graphs built per rank (the device radius
+    graph over the owned atoms): no global edge list is formed.  Halo rows are ordered by
+    (owner, owner row); the send lists come from one all-gather of the halo ids.  Returns the
+    domain and the edges' sources in the extended [owned | halo] numbering (a tensor on the
+    edges' device).  ``Domain.edges`` holds local edge ids (there are no global ones)."""
+    import torch
+    import torch.distributed as dist
+
+    part = np.asarray(part)
+    n = len(part)
+    order = np.argsort(part, kind="stable")
+    local_row = np.empty(n, dtype=np.int64)
+    counts = np.bincount(part, minlength=world)
+    starts = np.concatenate([[0], np.cumsum(counts)])
+    for r in range(world):
+        local_row[order[starts[r]:starts[r + 1]]] = np.arange(counts[r])
+    owned = order[starts[rank]:starts[rank + 1]]  # sorted global ids (stable argsort)
+    dev = src_global.device
+    part_t = torch.as_tensor(part, device=dev)
+    remote = part_t[src_global] != rank
+    halo = torch.unique(src_global[remote]).cpu().numpy()
+    halo = halo[np.lexsort((local_row[halo], part[halo]))]
+    ext_map = torch.full((n,), -1, dtype=torch.long, device=dev)
+    ext_map[torch.as_tensor(owned, device=dev)] = torch.arange(len(owned), device=dev)
+    ext_map[torch.as_tensor(halo, device=dev)] = len(owned) + torch.arange(len(halo), device=dev)
+    src_local = ext_map[src_global]
+    halos = [halo]
+    if world > 1:
+        halos = [None] * world
+        dist.all_gather_object(halos, halo, group=group)
+    dom = Domain(rank, world, owned, np.arange(int(src_global.numel())), halo, part[halo], local_row[halo],
+                 np.zeros(0, np.int64), np.zeros(0, np.int64))
+    dom.recv_counts = [int((dom.halo_owner == p).sum()) for p in range(world)]
+    dom.send = [local_row[h[part[h] == rank]] for h in halos]
+    return dom, src_local

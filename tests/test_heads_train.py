@@ -179,3 +179,53 @@ def test_edge_chunked_execution_matches_unchunked(chunk, stream):
     for a, c in zip(g0, g1):
         if a.numel():
             assert (a - c).abs().max() <= 5e-2 * max(1e-6, a.abs().max().item())
+
+
+def test_chunked_inference_streams_in_place_and_matches():
+    """Without gradients the chunked forward overwrites the edge stream in place and computes
+    each chunk's rotations on use; it equals the unchunked forward."""
+    b, lab = _batches(np.eye(3), dtype=torch.float64)
+    outs = []
+    for ec in (None, 9):
+        torch.manual_seed(0)
+        bb = eSEN_Backbone(lab.irreps, edge_chunk=ec, edge_stream_dtype=torch.float64, **KW).double()
+        hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list,
+                              reduce_node=True, reduce_node_intra=True).double()
+        with torch.no_grad():
+            g = bb.build_graph(b)
+            if ec is not None:
+                assert g.rot is None and g.rot_fn is not None and len(g.chunks) > 1
+            emb = bb(b)
+            outs.append(hd(emb, b))
+    (n0, e0), (n1, e1) = outs
+    assert torch.allclose(n0, n1, rtol=1e-10, atol=1e-12)
+    assert torch.allclose(e0, e1, rtol=1e-10, atol=1e-12)
+
+
+def test_streamed_hamiltonian_shard_matches_full_conversion():
+    from maloq_b200.ops import labels as lab_ops
+    from maloq_b200.parallel.infer import hamiltonian_shard
+
+    b, lab = _batches(np.eye(3), dtype=torch.float64)
+    tbl = lab.table
+    b.edge_pair_type = torch.as_tensor(tbl.pair_type(b.src_z.numpy(), b.dst_z.numpy()))
+    b.node_pair_type = torch.as_tensor(tbl.pair_type(b.atomic_numbers.numpy(), b.atomic_numbers.numpy()))
+    res = []
+    for ec in (None, 9):
+        torch.manual_seed(0)
+        bb = eSEN_Backbone(lab.irreps, edge_chunk=ec, edge_stream_dtype=torch.float64, **KW).double()
+        hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list,
+                              reduce_node=True, reduce_node_intra=True).double()
+        with torch.no_grad():
+            emb = bb(b)
+            if ec is None:
+                no, eo = hd(emb, b)
+                data, ptr = hamiltonian_shard(hd, emb, b, lab)
+                full = lab_ops.coupled_to_blocks(torch.cat([eo[0], no[0]]), ptr,
+                                                 torch.cat([b.edge_pair_type, b.node_pair_type]), lab.pos_t,
+                                                 lab.transform, int(ptr[-1]))
+                assert torch.allclose(data.double(), full.double(), atol=1e-10)
+            else:
+                data, ptr = hamiltonian_shard(hd, emb, b, lab)
+        res.append(data)
+    assert torch.allclose(res[0].double(), res[1].double(), atol=1e-10)

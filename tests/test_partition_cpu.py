@@ -131,3 +131,29 @@ def test_partitioned_workflow_train_and_infer(tmp_path):
     dense = H.to_dense()
     assert dense.shape[0] == 150 * 13
     assert np.allclose(dense, dense.T, atol=1e-5)
+
+
+def _local_domain_worker(rank, world):
+    import torch
+
+    g = _toy_graph(seed=3, n=80)
+    part = P.partition("slab", g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+    ref = P.decompose(part, g.src, g.dst, world)[rank]
+    # this rank's edges as a per-rank builder produces them: into owned atoms, (dst row, src) order
+    sel = ref.edges
+    dom, src_local = P.local_domain(part, rank, world, torch.as_tensor(g.src[sel]))
+    return (ref.owned, dom.owned, ref.halo, dom.halo, ref.halo_owner, dom.halo_owner, ref.halo_row, dom.halo_row,
+            ref.src_local, src_local.numpy(), ref.recv_counts, dom.recv_counts,
+            [np.asarray(x) for x in ref.send], [np.asarray(x) for x in dom.send])
+
+
+def test_local_domain_matches_global_decomposition():
+    """A domain built from one rank's own edges (no global edge list) equals the one cut from
+    the global graph: owned rows, halo order, owners, rows, edge sources and send lists."""
+    out = _dist_util.run(_local_domain_worker, world=2)
+    for r, v in out.items():
+        for a, b in zip(v[0:10:2], v[1:10:2]):
+            assert np.array_equal(np.asarray(a), np.asarray(b)), r
+        assert list(v[10]) == list(v[11])
+        for a, b in zip(v[12], v[13]):
+            assert np.array_equal(a, b)
