@@ -109,7 +109,7 @@ void gather_rotate_fwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
                                       rot.data_ptr<float>(), ptr<float>(rad), bf(A), (int)src.size(0),
                                       (int)X.size(2), (int)Cin, reinterpret_cast<const float* const*>(peers),
                                       halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
-                                      n_own, stream()));
+                                      n_own, X.size(0), halo_owner.has_value() ? halo_owner->numel() : 0, stream()));
 }
 
 void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
@@ -127,7 +127,7 @@ void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
                                       DDST.data_ptr<float>(), ptr<float>(DXE), ptr<float>(DRAD), (int)src.size(0),
                                       (int)X.size(2), (int)Cin, reinterpret_cast<const float* const*>(peers),
                                       halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
-                                      n_own, stream()));
+                                      n_own, X.size(0), halo_owner.has_value() ? halo_owner->numel() : 0, stream()));
 }
 
 // DX[n] = sum over dst-CSR of DDST + sum over src-CSR of DSRC (either may be absent)
@@ -158,7 +158,8 @@ void node_reduce(c10::optional<at::Tensor> DDST, at::Tensor dst_ptr, c10::option
   const int SC = (int)(DX.numel() / std::max<int64_t>(1, N));
   const at::cuda::CUDAGuard guard(DX.device());
   check(maloq::edge_node_reduce(ptr<float>(DDST), ll(dst_ptr), ptr<float>(DSRC), ll(src_perm), ll(src_ptr),
-                                DX.data_ptr<float>(), N, SC, stream()));
+                                DX.data_ptr<float>(), N, SC, DDST.has_value() ? DDST->size(0) : 0,
+                                DSRC.has_value() ? DSRC->size(0) : 0, stream()));
 }
 
 void rotate_back_scatter(int64_t L, int64_t MM, at::Tensor Y, int64_t koff, int64_t Rk, at::Tensor rot,
@@ -342,6 +343,8 @@ void basis_rows(at::Tensor in, at::Tensor out, c10::optional<at::Tensor> ptr, c1
     a.pt = ll(*pt);
     a.pos = pos->data_ptr<int>();
     a.d_pos = (int)pos->size(1);
+    a.n_pt = pos->size(0);
+    a.n_data = gather ? in.numel() : out.numel();
     TORCH_CHECK(a.d_pos == (gather ? a.d_in : a.d_out), "basis_rows: position table width");
   }
   if (!gather) TORCH_CHECK(in.numel() >= rows * d_in, "basis_rows: input rows");
@@ -420,7 +423,8 @@ void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask,
   chk(part, at::kFloat, "part");
   const at::cuda::CUDAGuard guard(O.device());
   check(maloq::fock_loss_stats(O.data_ptr<float>(), T.data_ptr<float>(), ll(pt), mask.data_ptr<uint8_t>(),
-                               (int)O.size(1), O.size(0), part.data_ptr<float>(), (int)part.size(0), stream()));
+                               (int)O.size(1), O.size(0), part.data_ptr<float>(), (int)part.size(0), mask.size(0),
+                               stream()));
 }
 
 void fock_loss_grad(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, double g_sse, double g_sae,
@@ -429,10 +433,12 @@ void fock_loss_grad(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, 
   chk(G, at::kFloat, "grad");
   const at::cuda::CUDAGuard guard(O.device());
   check(maloq::fock_loss_grad(O.data_ptr<float>(), T.data_ptr<float>(), ll(pt), mask.data_ptr<uint8_t>(),
-                              (int)O.size(1), O.size(0), (float)g_sse, (float)g_sae, G.data_ptr<float>(), stream()));
+                              (int)O.size(1), O.size(0), (float)g_sse, (float)g_sae, G.data_ptr<float>(), mask.size(0),
+                              stream()));
 }
 
 int64_t error_status(bool clear) { return maloq::error_status(clear); }
+bool bounds_checked() { return maloq::bounds_checked(); }
 
 }  // namespace
 
@@ -468,4 +474,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("radius_graph_pass", &radius_graph_pass);
   m.def("fock_loss_grad", &fock_loss_grad);
   m.def("error_status", &error_status, "read/clear the device error word", py::arg("clear") = true);
+  m.def("bounds_checked", &bounds_checked, "true for a library built with device index checks");
 }

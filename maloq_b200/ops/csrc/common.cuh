@@ -33,6 +33,16 @@ __device__ int g_maloq_error = 0;
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_maloq_error, 0, code); }
 
+// Index checks of checked builds (-DMALOQ_BOUNDS_CHECK): a failed check records ERR_BOUNDS and
+// the caller skips the access; other builds compile them away.
+#ifdef MALOQ_BOUNDS_CHECK
+#define MALOQ_IN_BOUNDS(cond) ((cond) ? true : (::maloq::record_error(::maloq::ERR_BOUNDS), false))
+#define MALOQ_BOUNDS_CHECKED 1
+#else
+#define MALOQ_IN_BOUNDS(cond) true
+#define MALOQ_BOUNDS_CHECKED 0
+#endif
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

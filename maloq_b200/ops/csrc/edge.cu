@@ -25,6 +25,7 @@ struct HaloRef {
   const int* halo_owner;
   const long long* halo_row;
   long long n_own;
+  long long n_src, n_dst;  // valid source / destination rows (bounds checks)
 };
 
 __device__ __forceinline__ const float* src_row(const float* X, long long s, int S, int C, const HaloRef& H) {
@@ -46,6 +47,7 @@ __global__ void __launch_bounds__(128) gather_rotate_fwd_kernel(
   const int e = blockIdx.x;
   const int cp = blockIdx.y * blockDim.x + threadIdx.x;
   if (e >= E || cp >= Cin) return;
+  if (!MALOQ_IN_BOUNDS(src[e] >= 0 && src[e] < H.n_src && dst[e] >= 0 && dst[e] < H.n_dst)) return;
   const float* base;
   if (cp < C) base = src_row(X, src[e], S, C, H) + cp;
   else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
@@ -81,6 +83,7 @@ __global__ void __launch_bounds__(128) gather_rotate_bwd_kernel(
   const int e = blockIdx.x;
   const int cp = blockIdx.y * blockDim.x + threadIdx.x;
   if (e >= E || cp >= Cin) return;
+  if (!MALOQ_IN_BOUNDS(src[e] >= 0 && src[e] < H.n_src && dst[e] >= 0 && dst[e] < H.n_dst)) return;
   float in[S];
   if (rad) {
     const float* base;
@@ -131,15 +134,21 @@ __global__ void __launch_bounds__(128) gather_rotate_bwd_kernel(
 // DX[n] = sum_{e: dst=n} DDST[e] + sum_{e: src=n} DSRC[e], both in fixed (CSR) order.
 __global__ void node_reduce_kernel(const float* __restrict__ DDST, const long long* __restrict__ dst_ptr,
                                    const float* __restrict__ DSRC, const long long* __restrict__ src_perm,
-                                   const long long* __restrict__ src_ptr, float* __restrict__ DX, int N, int SC) {
+                                   const long long* __restrict__ src_ptr, float* __restrict__ DX, int N, int SC,
+                                   long long n_dst_rows, long long n_src_rows) {
   const int n = blockIdx.x;
   const int i = blockIdx.y * blockDim.x + threadIdx.x;
   if (n >= N || i >= SC) return;
   float s = 0.f;
-  if (DDST)
+  if (DDST) {
+    if (!MALOQ_IN_BOUNDS(dst_ptr[n] >= 0 && dst_ptr[n + 1] <= n_dst_rows)) return;
     for (long long e = dst_ptr[n]; e < dst_ptr[n + 1]; ++e) s += DDST[(size_t)e * SC + i];
+  }
   if (DSRC)
-    for (long long q = src_ptr[n]; q < src_ptr[n + 1]; ++q) s += DSRC[(size_t)src_perm[q] * SC + i];
+    for (long long q = src_ptr[n]; q < src_ptr[n + 1]; ++q) {
+      if (!MALOQ_IN_BOUNDS(src_perm[q] >= 0 && src_perm[q] < n_src_rows)) return;
+      s += DSRC[(size_t)src_perm[q] * SC + i];
+    }
   DX[(size_t)n * SC + i] = s;
 }
 
@@ -494,10 +503,11 @@ static inline int clampm(int L, int MM) { return MM > L ? L : MM; }
 const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
                                    const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
                                    int C, int Cin, const float* const* peers, const int* halo_owner,
-                                   const long long* halo_row, long long n_own, cudaStream_t st) {
+                                   const long long* halo_row, long long n_own, long long n_x_rows, long long n_halo,
+                                   cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
-  const HaloRef H{peers, halo_owner, halo_row, n_own};
+  const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows};
   dim3 grid(E, (Cin + 127) / 128);
   MALOQ_DISPATCH_FRAME(
       (gather_rotate_fwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, A, E, C, Cin, H)))
@@ -507,10 +517,10 @@ const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* X
                                    const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
                                    float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
                                    const float* const* peers, const int* halo_owner, const long long* halo_row,
-                                   long long n_own, cudaStream_t st) {
+                                   long long n_own, long long n_x_rows, long long n_halo, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
-  const HaloRef H{peers, halo_owner, halo_row, n_own};
+  const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows};
   dim3 grid(E, (Cin + 127) / 128);
   MALOQ_DISPATCH_FRAME((gather_rotate_bwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, dA, DSRC,
                                                                                 DDST, DXE, DRAD, E, C, Cin, H)))
@@ -533,10 +543,11 @@ const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, co
 }
 
 const char* edge_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,
-                             const long long* src_ptr, float* DX, int N, int SC, cudaStream_t st) {
+                             const long long* src_ptr, float* DX, int N, int SC, long long n_dst_rows,
+                             long long n_src_rows, cudaStream_t st) {
   if (N == 0) return nullptr;
   dim3 grid(N, (SC + 255) / 256);
-  node_reduce_kernel<<<grid, 256, 0, st>>>(DDST, dst_ptr, DSRC, src_perm, src_ptr, DX, N, SC);
+  node_reduce_kernel<<<grid, 256, 0, st>>>(DDST, dst_ptr, DSRC, src_perm, src_ptr, DX, N, SC, n_dst_rows, n_src_rows);
   return last_error();
 }
 

@@ -10,12 +10,13 @@ namespace maloq {
 const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
                                    const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
                                    int C, int Cin, const float* const* peers, const int* halo_owner,
-                                   const long long* halo_row, long long n_own, cudaStream_t st);
+                                   const long long* halo_row, long long n_own, long long n_x_rows, long long n_halo,
+                                   cudaStream_t st);
 const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const long long* src,
                                    const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
                                    float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
                                    const float* const* peers, const int* halo_owner, const long long* halo_row,
-                                   long long n_own, cudaStream_t st);
+                                   long long n_own, long long n_x_rows, long long n_halo, cudaStream_t st);
 const char* edge_rotate_grad_nodes(int L, int MM, const float* G, const long long* out_ptr, const float* rot,
                                    __nv_bfloat16* DY, float* DYf, int N, int C, int Rk, float scale, cudaStream_t st);
 const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, const long long* halo_row, float* out,
@@ -23,7 +24,8 @@ const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, co
 const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,
                            long long n_halo, int SC, cudaStream_t st);
 const char* edge_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,
-                             const long long* src_ptr, float* DX, int N, int SC, cudaStream_t st);
+                             const long long* src_ptr, float* DX, int N, int SC, long long n_dst_rows,
+                             long long n_src_rows, cudaStream_t st);
 const char* edge_rotate_back_scatter(int L, int MM, const __nv_bfloat16* Y, int ldy, int koff, const float* rot,
                                      const long long* dst_ptr, const float* base, float* out, int N, int C, int Rk,
                                      float scale, cudaStream_t st);

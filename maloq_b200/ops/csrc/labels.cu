@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(BT_THREADS) basis_rows_kernel(const T* __restr
                                                                 const int* __restrict__ pos, int d_pos,
                                                                 const int4* __restrict__ meta,
                                                                 const T* __restrict__ coef, int d_in, int d_out,
-                                                                long long rows) {
+                                                                long long rows, long long n_pt, long long n_data) {
   extern __shared__ __align__(16) unsigned char bt_smem[];
   T* xs = reinterpret_cast<T*>(bt_smem);  // [BT_ROWS][d_in]
   const long long n_tiles = (rows + BT_ROWS - 1) / BT_ROWS;
@@ -46,8 +46,12 @@ __global__ void __launch_bounds__(BT_THREADS) basis_rows_kernel(const T* __restr
       T v = T(0);
       if (row < rows) {
         if (GATHER) {
-          const int p = __ldg(pos + __ldg(pt + row) * d_pos + k);
-          if (p >= 0) v = in[__ldg(ptr + row) + p];
+          // a failed check skips the access only: every thread still reaches the barriers below
+          const long long t = __ldg(pt + row);
+          if (MALOQ_IN_BOUNDS(t >= 0 && t < n_pt)) {
+            const int p = __ldg(pos + t * d_pos + k);
+            if (p >= 0 && MALOQ_IN_BOUNDS(__ldg(ptr + row) + p < n_data)) v = in[__ldg(ptr + row) + p];
+          }
         } else {
           v = in[row * ld_in + k];
         }
@@ -70,8 +74,11 @@ __global__ void __launch_bounds__(BT_THREADS) basis_rows_kernel(const T* __restr
         const long long row = r0 + r;
         if (row >= rows) break;
         if (SCATTER) {
-          const int p = __ldg(pos + __ldg(pt + row) * d_pos + u);
-          if (p >= 0) out[__ldg(ptr + row) + p] = acc[r];
+          const long long t = __ldg(pt + row);
+          if (MALOQ_IN_BOUNDS(t >= 0 && t < n_pt)) {
+            const int p = __ldg(pos + t * d_pos + u);
+            if (p >= 0 && MALOQ_IN_BOUNDS(__ldg(ptr + row) + p < n_data)) out[__ldg(ptr + row) + p] = acc[r];
+          }
         } else {
           out[row * ld_out + u] = acc[r];
         }
@@ -90,7 +97,7 @@ static void launch_bt(const BasisRowsArgs& a, cudaStream_t st) {
   const int grid = (int)std::min<long long>(tiles, 148LL * 8);
   k<<<grid, BT_THREADS, smem, st>>>(static_cast<const T*>(a.in), a.ld_in, static_cast<T*>(a.out), a.ld_out, a.ptr,
                                     a.pt, a.pos, a.d_pos, a.meta, static_cast<const T*>(a.coef), a.d_in, a.d_out,
-                                    a.rows);
+                                    a.rows, a.n_pt, a.n_data);
 }
 
 template <typename T>

@@ -22,6 +22,8 @@ struct BasisRowsArgs {
   const void* coef;
   int d_in, d_out;
   long long rows;
+  long long n_pt;    // rows of the position table (bounds checks)
+  long long n_data;  // entries of the block data (bounds checks)
   bool gather, scatter;
   int dtype;
 };

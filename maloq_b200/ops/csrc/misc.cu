@@ -98,13 +98,13 @@ __global__ void edge_rotation_kernel(const float* __restrict__ vec, long long ld
 // stats per CTA: [sse, sae, cnt] over rows of one output kind (node or edge)
 __global__ void fock_loss_stats_kernel(const float* __restrict__ O, const float* __restrict__ Tt,
                                        const long long* __restrict__ pt, const uint8_t* __restrict__ mask, int D,
-                                       long long rows, float* __restrict__ part) {
+                                       long long rows, float* __restrict__ part, long long n_pt) {
   float sse = 0.f, sae = 0.f, cnt = 0.f;
   const long long total = rows * D;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / D;
     const int c = (int)(i - r * D);
-    if (mask[pt[r] * D + c]) {
+    if (MALOQ_IN_BOUNDS(pt[r] >= 0 && pt[r] < n_pt) && mask[pt[r] * D + c]) {
       const float d = O[i] - Tt[i];
       sse += d * d;
       sae += fabsf(d);
@@ -135,13 +135,14 @@ __global__ void fock_loss_stats_kernel(const float* __restrict__ O, const float*
 // G[i] = mask * (g_sse * 2 (o - t) + g_sae * sign(o - t))
 __global__ void fock_loss_grad_kernel(const float* __restrict__ O, const float* __restrict__ Tt,
                                       const long long* __restrict__ pt, const uint8_t* __restrict__ mask, int D,
-                                      long long rows, float g_sse, float g_sae, float* __restrict__ G) {
+                                      long long rows, float g_sse, float g_sae, float* __restrict__ G,
+                                      long long n_pt) {
   const long long total = rows * D;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / D;
     const int c = (int)(i - r * D);
     float g = 0.f;
-    if (mask[pt[r] * D + c]) {
+    if (MALOQ_IN_BOUNDS(pt[r] >= 0 && pt[r] < n_pt) && mask[pt[r] * D + c]) {
       const float d = O[i] - Tt[i];
       g = g_sse * 2.f * d + g_sae * (d > 0.f ? 1.f : (d < 0.f ? -1.f : 0.f));
     }
@@ -175,15 +176,15 @@ const char* edge_rotation(const float* vec, long long ldv, const float* J, const
 int fock_loss_grid(long long n) { return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, 148 * 8)); }
 
 const char* fock_loss_stats(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
-                            long long rows, float* part, int grid, cudaStream_t st) {
-  fock_loss_stats_kernel<<<grid, 256, 0, st>>>(O, Tt, pt, mask, D, rows, part);
+                            long long rows, float* part, int grid, long long n_pt, cudaStream_t st) {
+  fock_loss_stats_kernel<<<grid, 256, 0, st>>>(O, Tt, pt, mask, D, rows, part, n_pt);
   return misc_err();
 }
 
 const char* fock_loss_grad(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
-                           long long rows, float g_sse, float g_sae, float* G, cudaStream_t st) {
+                           long long rows, float g_sse, float g_sae, float* G, long long n_pt, cudaStream_t st) {
   if (rows == 0) return nullptr;
-  fock_loss_grad_kernel<<<fock_loss_grid(rows * D), 256, 0, st>>>(O, Tt, pt, mask, D, rows, g_sse, g_sae, G);
+  fock_loss_grad_kernel<<<fock_loss_grid(rows * D), 256, 0, st>>>(O, Tt, pt, mask, D, rows, g_sse, g_sae, G, n_pt);
   return misc_err();
 }
 

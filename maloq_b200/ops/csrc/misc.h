@@ -10,8 +10,8 @@ const char* edge_rotation(const float* vec, long long ldv, const float* J, const
 int fock_loss_grid(long long n);
 // part: [grid, 3] = (sum of squared error, sum of absolute error, count) per CTA
 const char* fock_loss_stats(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
-                            long long rows, float* part, int grid, cudaStream_t st);
+                            long long rows, float* part, int grid, long long n_pt, cudaStream_t st);
 const char* fock_loss_grad(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
-                           long long rows, float g_sse, float g_sae, float* G, cudaStream_t st);
+                           long long rows, float g_sse, float g_sae, float* G, long long n_pt, cudaStream_t st);
 
 }  // namespace maloq

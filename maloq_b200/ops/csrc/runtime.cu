@@ -14,4 +14,6 @@ int error_status(bool clear) {
   return v;
 }
 
+bool bounds_checked() { return MALOQ_BOUNDS_CHECKED != 0; }
+
 }  // namespace maloq

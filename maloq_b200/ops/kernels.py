@@ -27,6 +27,39 @@ def error_status(clear=True) -> int:
     return int(lib().error_status(clear))
 
 
+class DeviceError(RuntimeError):
+    """A kernel of this library recorded an error code in the device error word."""
+
+
+class CommTimeoutError(DeviceError):
+    """A bounded device wait ran out: a peer GPU did not raise its flag (peer barrier, halo,
+    fused all-reduce), or a GEMM pipeline stage never arrived."""
+
+
+class BoundsError(DeviceError):
+    """An index-checked build (``MALOQ_BOUNDS_CHECK=1``) found an out-of-range index and
+    skipped the access."""
+
+
+ERROR_CODES = {1: ("GEMM producer waited for a free stage", CommTimeoutError),
+               2: ("GEMM MMA warp waited for operand tiles", CommTimeoutError),
+               3: ("GEMM epilogue waited for the accumulator", CommTimeoutError),
+               4: ("a peer GPU did not arrive at a peer barrier", CommTimeoutError),
+               5: ("an index was out of range", BoundsError)}
+
+
+def check_device_status(where="") -> None:
+    """Read and clear the device error word; raise the matching :class:`DeviceError` if a
+    kernel recorded one (the read synchronises the device)."""
+    code = error_status(clear=True)
+    if code == 0:
+        return
+    if code < 0:
+        raise DeviceError(f"could not read the device error word{' after ' + where if where else ''}")
+    msg, cls = ERROR_CODES.get(code, (f"unknown error code {code}", DeviceError))
+    raise cls(f"device error {code}: {msg}{' (after ' + where + ')' if where else ''}")
+
+
 # ------------------------------------------------------------------ GEMM helpers
 def _pad_cols(t, mult=8):
     k = t.shape[-1]

@@ -1,5 +1,9 @@
-"""CUDA implementations (sm_100a kernels) behind the op layer; filled in by ops/cuda_*.py."""
+"""CUDA implementations (sm_100a kernels) behind the op layer (registered by ``ops/kernels.py``).
+
+``MALOQ_NVTX=1`` puts every kernel-backed op call in an NVTX range ``maloq::<op>``."""
 from __future__ import annotations
+
+import os
 
 _IMPL = {}
 
@@ -11,6 +15,23 @@ def register(name):
     return deco
 
 
+def _nvtx_wrap(name, fn):
+    """``fn`` inside an NVTX range ``maloq::<op>`` (visible in Nsight timelines)."""
+    import functools
+
+    import torch
+
+    @functools.wraps(fn)
+    def wrapped(*args, **kwargs):
+        torch.cuda.nvtx.range_push(f"maloq::{name}")
+        try:
+            return fn(*args, **kwargs)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
+    return wrapped
+
+
 def _get(name):
     fn = _IMPL.get(name)
     if fn is None:
@@ -18,6 +39,8 @@ def _get(name):
         fn = _IMPL.get(name)
     if fn is None:
         raise RuntimeError(f"maloq_b200: no CUDA kernel registered for op {name!r}")
+    if os.environ.get("MALOQ_NVTX", "0") not in ("", "0"):
+        fn = _nvtx_wrap(name, fn)
     return fn
 
 

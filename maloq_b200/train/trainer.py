@@ -72,15 +72,28 @@ class Prefetcher:
 
 class SplitTrainer:
     def __init__(self, backbone, head, head_irreps, save_frequency=10, run_id=None, run_name="noname",
-                 mask_table=None, grad_sync=None, nan_guard=False):
+                 mask_table=None, grad_sync=None, nan_guard=False, status_every=0):
         self.backbone, self.head, self.head_irreps = backbone, head, head_irreps
         self.save_frequency, self.run_name = save_frequency, run_name
         self.mask_table = mask_table
         self.grad_sync = grad_sync
         self.nan_guard = nan_guard
+        # every ``status_every`` steps (0: only at the end of each epoch) the device error word
+        # is read and a recorded timeout / bounds error raised on the host (CommTimeoutError,
+        # BoundsError); reading it synchronises the device
+        self.status_every = int(status_every)
+        self._steps = 0
         self.open_shell = getattr(head, "num_spins", 1) > 1
         self.history = {"train_node": [], "train_edge": [], "val_node": [], "val_edge": []}
         self.start_epoch = 0
+
+    @staticmethod
+    def check_status(where=""):
+        """Raise the device error recorded by a kernel, if any (CUDA runs only)."""
+        if torch.cuda.is_available() and torch.cuda.is_initialized():
+            from ..ops import kernels
+
+            kernels.check_device_status(where)
 
     # ------------------------------------------------------------------ one step
     def masks(self, batch):
@@ -112,6 +125,9 @@ class SplitTrainer:
             self.grad_sync.finish()
         optimizer.step()
         optimizer.zero_grad(set_to_none=True)
+        self._steps += 1
+        if self.status_every and self._steps % self.status_every == 0:
+            self.check_status(f"train step {self._steps}")
         if scheduler is not None and not hasattr(scheduler, "patience"):
             scheduler.step()
         return ln.detach(), le.detach(), loss.detach()
@@ -137,6 +153,7 @@ class SplitTrainer:
                 if rank == 0 and log_every and bi % log_every == 0:
                     print(f"--> Rank {rank} epoch {epoch + 1} batch {bi} loss: {loss.item():.6g}", flush=True)
             nb = max(1, len(train_loader))
+            self.check_status(f"epoch {epoch + 1}")
             self.history["train_node"].append(sn.item() / nb)
             self.history["train_edge"].append(se.item() / nb)
             vn, ve, vt = self.validate(val_loader, loss_fxn, device)

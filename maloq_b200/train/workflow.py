@@ -86,6 +86,8 @@ class TrainingWorkflow:
             c["hidden_dim"] = c["l_embedding_dim"]
         c.setdefault("message_type", "source-target")
         c.setdefault("activation_checkpointing", False)
+        # device error word read every N steps (multi-GPU runs default to 50); 0: per epoch only
+        c.setdefault("device_status_every", 50 if self.world_size > 1 else 0)
         c.setdefault("basis_transform_backend", "cuda")
         if c["distribute_graphs"] and c["partition_type"] is None:
             c["partition_type"] = "slab"
@@ -250,7 +252,8 @@ class TrainingWorkflow:
             mask_table = torch.as_tensor(labeler.table.mask)
             trainer = SplitTrainer(backbone, head, labeler.irreps, save_frequency=c["save_frequency"],
                                    run_name=c["run_name"], mask_table=mask_table,
-                                   grad_sync=self.grad_sync(backbone, head))
+                                   grad_sync=self.grad_sync(backbone, head),
+                                   status_every=c["device_status_every"])
             if c["train_or_eval"] == "train":
                 if c["restart_backbone"] or c["restart_head"]:
                     st = ckpt.load_resume(c["output_folder"], sched)

@@ -61,3 +61,21 @@ def test_peer_barrier_timeout_reports_error_and_context_survives(cuda_device):
     assert pads[1, 0].item() == 1  # rank 0 did signal its peer slot
     assert torch.ones(3, device=cuda_device).sum().item() == 3
     assert kernels.error_status() == 0
+
+
+def test_peer_timeout_raises_comm_timeout_on_the_host(cuda_device):
+    """The host-side status check turns the recorded peer timeout into CommTimeoutError (what
+    the trainer raises after a step) and clears the word."""
+    import pytest
+
+    from maloq_b200.ops import kernels
+    from maloq_b200.train.trainer import SplitTrainer
+
+    lib = kernels.lib()
+    kernels.error_status(True)
+    pads = torch.zeros(2, 8, dtype=torch.int32, device=cuda_device)
+    ptrs = torch.tensor([pads[0].data_ptr(), pads[1].data_ptr()], dtype=torch.int64, device=cuda_device)
+    lib.peer_barrier(ptrs.data_ptr(), 0, 2, 1, 0, 2000)
+    with pytest.raises(kernels.CommTimeoutError):
+        SplitTrainer.check_status("test step")
+    kernels.check_device_status()  # cleared: no raise
