@@ -9,11 +9,16 @@
   tables list each code's published ordering of p and d functions (kept identical to the
   reference's ``convention_dict`` because they describe the external programs' outputs).
 * :func:`load_nabladft` - database rows -> graph samples with coupled-basis targets.
+* CP2K periodic data: :func:`read_cp2k_csr` (binary or ASCII sparse dumps, symmetrised),
+  :func:`read_periodic_xyz` (``Lattice=``/``Cell:`` headers), :func:`fermi_energy` and
+  :func:`fermi_shift`, :func:`blocks_from_sparse` (atom-pair blocks without densifying) and
+  :func:`load_cp2k`.
 """
 
 from __future__ import annotations
 
 import math
+import os
 import sqlite3
 
 import numpy as np
@@ -128,3 +133,156 @@ def load_nabladft(path, config, device="cpu", convention="psi4", indices=None):
         s.overlap = S
         samples.append(s)
     return samples, labeler
+
+
+# ------------------------------------------------------------------ CP2K (periodic materials)
+HARTREE_EV = 27.211386245988
+_SYMBOLS = ("X H He Li Be B C N O F Ne Na Mg Al Si P S Cl Ar K Ca Sc Ti V Cr Mn Fe Co Ni Cu Zn Ga Ge As Se Br "
+            "Kr Rb Sr Y Zr Nb Mo Tc Ru Rh Pd Ag Cd In Sn Sb Te I Xe Cs Ba La Ce Pr Nd Pm Sm Eu Gd Tb Dy Ho Er Tm "
+            "Yb Lu Hf Ta W Re Os Ir Pt Au Hg Tl Pb Bi Po At Rn").split()
+SYMBOL_TO_Z = {s: i for i, s in enumerate(_SYMBOLS) if i}
+
+# a Fortran unformatted record of (row int32, col int32, value float64): 4-byte length markers
+# of 16 around the 16-byte payload
+_CP2K_RECORD = np.dtype([("m0", "<i4"), ("row", "<u4"), ("col", "<u4"), ("val", "<f8"), ("m1", "<i4")])
+
+
+def read_cp2k_csr(path, dtype=np.float64):
+    """A CP2K sparse matrix dump (binary Fortran records or ASCII ``row col value`` lines,
+    1-based, usually the upper triangle) as a full symmetric ``scipy.sparse`` CSR matrix:
+    ``H + H^T - diag(H)``.  Reference ``dataset_utils/get_loader.py:556-622``."""
+    import scipy.sparse as sp
+
+    size = os.path.getsize(path)
+    rec = None
+    if size and size % _CP2K_RECORD.itemsize == 0:
+        head = np.fromfile(path, dtype=_CP2K_RECORD, count=min(16, size // _CP2K_RECORD.itemsize))
+        if np.all(head["m0"] == 16) and np.all(head["m1"] == 16):
+            rec = np.fromfile(path, dtype=_CP2K_RECORD)
+    if rec is not None:
+        r, c, v = rec["row"].astype(np.int64), rec["col"].astype(np.int64), rec["val"]
+    else:
+        a = np.loadtxt(path, ndmin=2)
+        r, c, v = a[:, 0].astype(np.int64), a[:, 1].astype(np.int64), a[:, 2]
+    n = int(max(r.max(), c.max())) if len(r) else 0
+    H = sp.coo_matrix((v.astype(dtype), (r - 1, c - 1)), shape=(n, n)).tocsr()
+    return (H + H.T - sp.diags(H.diagonal(), format="csr")).tocsr()
+
+
+def write_cp2k_csr(path, M, binary=True):
+    """Write the upper triangle of a (dense or sparse) matrix in CP2K's dump format (tests and
+    data export)."""
+    import scipy.sparse as sp
+
+    U = sp.triu(sp.coo_matrix(M)).tocoo()
+    if binary:
+        rec = np.zeros(U.nnz, dtype=_CP2K_RECORD)
+        rec["m0"] = rec["m1"] = 16
+        rec["row"], rec["col"], rec["val"] = U.row + 1, U.col + 1, U.data
+        rec.tofile(path)
+    else:
+        np.savetxt(path, np.stack([U.row + 1, U.col + 1, U.data], 1), fmt=["%d", "%d", "%.17g"])
+
+
+def read_periodic_xyz(path):
+    """Structure of an XYZ file whose comment line gives the orthorhombic cell as
+    ``Lattice="ax ay az bx by bz cx cy cz"`` (diagonal used) / ``Lattice="a b c"`` or as
+    ``Cell: a b c`` (CP2K).  Reference ``get_loader.py:644-708``."""
+    import re
+
+    from .structures import Structure
+
+    with open(path) as f:
+        lines = f.read().splitlines()
+    n = int(lines[0].split()[0])
+    z, pos = [], []
+    for ln in lines[2:2 + n]:
+        p = ln.split()
+        z.append(SYMBOL_TO_Z[p[0]])
+        pos.append([float(x) for x in p[1:4]])
+    cell = None
+    m = re.search(r'Lattice="([^"]+)"', lines[1])
+    if m:
+        vals = [float(x) for x in m.group(1).split()]
+        cell = [vals[0], vals[4], vals[8]] if len(vals) == 9 else (vals if len(vals) == 3 else None)
+    else:
+        p = lines[1].split()
+        if p and p[0].lower() in ("cell", "cell:"):
+            cell = [float(x) for x in p[1:4]]
+    return Structure(np.asarray(z, np.int64), np.asarray(pos, np.float64),
+                     None if cell is None else np.asarray(cell, np.float64))
+
+
+def fermi_energy(out_path):
+    """Fermi level (Hartree) from a CP2K output file (``Fermi Energy [eV] :`` is converted;
+    ``Fermi energy:`` / ``Fermi level:`` are taken as Hartree).  Reference
+    ``get_loader.py:710-726``."""
+    import re
+
+    pats = [(re.compile(r"Fermi Energy \[eV\] :\s*([-+]?\d*\.?\d+(?:[eE][-+]?\d+)?)"), 1.0 / HARTREE_EV),
+            (re.compile(r"Fermi energy:\s*([-+]?\d*\.?\d+(?:[eE][-+]?\d+)?)"), 1.0),
+            (re.compile(r"Fermi level:\s*([-+]?\d*\.?\d+(?:[eE][-+]?\d+)?)"), 1.0)]
+    with open(out_path) as f:
+        for line in f:
+            for pat, scale in pats:
+                m = pat.search(line)
+                if m:
+                    return float(m.group(1)) * scale
+    raise ValueError(f"no Fermi energy in {out_path}")
+
+
+def fermi_shift(H, S, mu):
+    """H - mu S (the Hamiltonian referenced to the Fermi level)."""
+    return H - mu * S
+
+
+def blocks_from_sparse(M, rows, cols, orb_ptr):
+    """:class:`BlockSparseMatrix` of the atom-pair blocks (rows[b], cols[b]) of a sparse
+    matrix, without densifying it: each stored entry is mapped to its atom pair and its
+    position inside that pair's block (entries of pairs not listed are dropped)."""
+    import scipy.sparse as sp
+
+    from .labels import BlockSparseMatrix
+
+    C = sp.coo_matrix(M)
+    orb_ptr = np.asarray(orb_ptr, np.int64)
+    n_at = len(orb_ptr) - 1
+    atom_of = np.repeat(np.arange(n_at), np.diff(orb_ptr))
+    rows, cols = np.asarray(rows, np.int64), np.asarray(cols, np.int64)
+    norb = np.diff(orb_ptr)
+    sizes = norb[rows] * norb[cols]
+    ptr = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    data = np.zeros(int(ptr[-1]), dtype=C.dtype)
+    key = rows * n_at + cols
+    order = np.argsort(key)
+    ai, aj = atom_of[C.row], atom_of[C.col]
+    k = ai * n_at + aj
+    at = np.searchsorted(key[order], k)
+    at = np.minimum(at, len(order) - 1)
+    hit = key[order][at] == k
+    b = order[at[hit]]
+    r, c = C.row[hit] - orb_ptr[ai[hit]], C.col[hit] - orb_ptr[aj[hit]]
+    data[ptr[b] + r * norb[cols[b]] + c] = C.data[hit]
+    return BlockSparseMatrix(rows, cols, ptr, data, orb_ptr)
+
+
+def load_cp2k(xyz_path, h_path, config, basis_name="dzvp_like", s_path=None, out_path=None, device="cpu"):
+    """One periodic CP2K structure with coupled-basis targets: structure from the XYZ, the
+    Hamiltonian from the CSR dump (Fermi-shifted, H - mu S, when the overlap and the output
+    file are given), graph within 2 * rcut_orbitals, blocks of every graph pair."""
+    from .basis_sets import get_basis
+    from .batch import make_sample
+    from .labels import orbital_offsets
+    from .targets import FockLabeler
+
+    st = read_periodic_xyz(xyz_path)
+    H = read_cp2k_csr(h_path)
+    if s_path is not None and out_path is not None:
+        H = fermi_shift(H, read_cp2k_csr(s_path), fermi_energy(out_path))
+    labeler = FockLabeler(get_basis(basis_name), device=device)
+    s = make_sample(st, 2 * config.get("rcut_orbitals", 4.0))
+    rows, cols = labeler.pairs(s)
+    bsm = blocks_from_sparse(H, rows, cols, orbital_offsets(st.z, labeler.table))
+    ny, y = labeler.labels_from_blocks(s, bsm)
+    s.node_y, s.y = ny.unsqueeze(0).cpu(), y.unsqueeze(0).cpu()
+    return s, labeler

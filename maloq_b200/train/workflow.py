@@ -156,6 +156,27 @@ class TrainingWorkflow:
         self.partition_sample = sample
         return [batch], [batch], labeler
 
+    def _load_cp2k_folder(self, c):
+        """``dbpath``: a folder of structure directories, each with ``structure.xyz`` and
+        ``hamiltonian.csr`` (CP2K dump), optionally ``overlap.csr`` + ``cp2k.out`` for the
+        Fermi-level shift.  Basis: ``basis_name`` (default the DZVP-like Si/O/Hf basis)."""
+        from ..data.readers import load_cp2k
+
+        root = c["dbpath"]
+        dirs = sorted(d for d in os.listdir(root) if os.path.isfile(os.path.join(root, d, "structure.xyz")))
+        samples, labeler = [], None
+        for d in dirs[: c.get("num_structures") or len(dirs)]:
+            p = os.path.join(root, d)
+            s_path, o_path = os.path.join(p, "overlap.csr"), os.path.join(p, "cp2k.out")
+            s, labeler = load_cp2k(os.path.join(p, "structure.xyz"), os.path.join(p, "hamiltonian.csr"), c,
+                                   basis_name=c.get("basis_name", "dzvp_like"),
+                                   s_path=s_path if os.path.exists(s_path) else None,
+                                   out_path=o_path if os.path.exists(o_path) else None, device=self.device)
+            samples.append(s)
+        if not samples:
+            raise ValueError(f"no CP2K structure directories under {root}")
+        return samples, labeler
+
     def prepare_data(self):
         c = self.config
         if c["distribute_graphs"]:
@@ -172,6 +193,8 @@ class TrainingWorkflow:
             from ..data.readers import load_nabladft
 
             samples, labeler = load_nabladft(c["dbpath"], c, self.device)
+        elif name == "cp2k":
+            samples, labeler = self._load_cp2k_folder(c)
         else:
             raise ValueError(f"Unknown dataset name: {name}")
         n_val = c["num_val"] or max(1, len(samples) // 8)
