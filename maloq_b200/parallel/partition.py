@@ -15,7 +15,11 @@ all returning ``part[node] -> rank``:
   reference's low_nn / longest_dim family);
 * ``greedy`` - breadth-first region growing to equal edge counts (a dependency-free stand-in
   for METIS, which is not installed);
-* ``worst-case`` - round-robin assignment (maximal cut), for stress tests.
+* ``worst-case`` - round-robin assignment (maximal cut), for stress tests;
+* ``surface_volume`` / ``approx_neighbors`` - bisection choosing each cut axis from a
+  geometric estimate (halo shell volume / neighbouring-domain count);
+* ``local_optimal`` / ``bruteforce`` - bisection choosing cut axes by the real halo on the
+  graph (greedily per cut / over every per-level axis sequence).
 """
 
 from __future__ import annotations
@@ -80,6 +84,160 @@ def partition_rcb(n, world, pos=None, dst=None, **_):
     return part
 
 
+# ------------------------------------------------------------------ axis-policy bisections
+def halo_volume(part, src, dst):
+    """Halo rows summed over ranks: distinct (source, destination rank) pairs whose source is
+    owned elsewhere - the rows that cross between GPUs in every exchange."""
+    part = np.asarray(part)
+    cut = part[src] != part[dst]
+    if not cut.any():
+        return 0
+    return int(len(np.unique(np.asarray(src)[cut] * (part.max() + 1) + part[np.asarray(dst)[cut]])))
+
+
+def _bisect(n, world, pos, deg, choose_axis, periodic):
+    """Recursive bisection: each split picks its axis with ``choose_axis(idx, periodic, k)``
+    and cuts at equal cumulative degree (world need not be a power of two)."""
+    part = np.zeros(n, dtype=np.int64)
+
+    def rec(idx, lo, k, per):
+        if k == 1 or len(idx) == 0:
+            part[idx] = lo
+            return
+        ax = choose_axis(idx, per, k)
+        order = idx[np.argsort(pos[idx, ax], kind="stable")]
+        k1 = k // 2
+        c = np.cumsum(deg[order])
+        cut = int(np.searchsorted(c, c[-1] * k1 / k)) + 1
+        per2 = list(per)
+        per2[ax] = False  # a cut axis is no longer wrapped onto itself
+        rec(order[:cut], lo, k1, per2)
+        rec(order[cut:], lo + k1, k - k1, per2)
+
+    rec(np.arange(n), 0, world, list(periodic))
+    return part
+
+
+def _box(pos, idx):
+    return np.ptp(pos[idx], axis=0) + 1e-9
+
+
+def _shell_volume(size, periodic, rcut):
+    """Volume of the rcut shell around a box (faces, edges as quarter cylinders, corners as
+    eighth spheres) counting only non-wrapped directions - the halo a sub-domain imports."""
+    v = 0.0
+    for a in range(3):
+        b, c = [x for x in range(3) if x != a]
+        if not periodic[a]:
+            v += 2 * rcut * size[b] * size[c]
+        if not (periodic[b] and periodic[c]):
+            v += np.pi * rcut ** 2 * size[a]
+    if not all(periodic):
+        v += 4.0 / 3.0 * np.pi * rcut ** 3
+    return v
+
+
+def _neighbour_domains(size, periodic, rcut):
+    """Estimated number of neighbouring sub-domains of a box within rcut."""
+    n = 0.0
+    for a in range(3):
+        if not periodic[a]:
+            n += 2 * np.ceil(rcut / size[a])
+    for a in range(3):
+        for b in range(a + 1, 3):
+            if not (periodic[a] or periodic[b]):
+                n += 4 * np.ceil(rcut / np.hypot(size[a], size[b]))
+    if not any(periodic):
+        n += 8 * np.ceil(rcut / np.linalg.norm(size))
+    return n
+
+
+def _estimate_policy(pos, rcut, cost):
+    def choose(idx, per, k):
+        size = _box(pos, idx)
+        best, best_ax = None, 0
+        for ax in range(3):
+            s2 = size.copy()
+            s2[ax] /= 2
+            p2 = list(per)
+            p2[ax] = False
+            v = cost(s2, p2, rcut)
+            if best is None or v < best - 1e-12:
+                best, best_ax = v, ax
+        return best_ax
+
+    return choose
+
+
+def partition_surface_volume(n, world, pos=None, dst=None, cell=None, rcut=None, **_):
+    """Bisection whose every cut takes the axis leaving the smallest halo shell volume
+    (reference ``fock_utils/reorder.py:190-336``)."""
+    deg = np.bincount(dst, minlength=n) + 1 if dst is not None else np.ones(n, np.int64)
+    rcut = rcut or 0.1 * float(np.ptp(pos, axis=0).max())
+    return _bisect(n, world, pos, deg, _estimate_policy(pos, rcut, _shell_volume), [cell is not None] * 3)
+
+
+def partition_approx_neighbors(n, world, pos=None, dst=None, cell=None, rcut=None, **_):
+    """Bisection whose every cut takes the axis giving the fewest estimated neighbouring
+    domains (the longest axis while everything is still periodic; reference
+    ``reorder.py:338-472``)."""
+    deg = np.bincount(dst, minlength=n) + 1 if dst is not None else np.ones(n, np.int64)
+    rcut = rcut or 0.1 * float(np.ptp(pos, axis=0).max())
+    est = _estimate_policy(pos, rcut, _neighbour_domains)
+
+    def choose(idx, per, k):
+        return int(np.argmax(_box(pos, idx))) if all(per) else est(idx, per, k)
+
+    return _bisect(n, world, pos, deg, choose, [cell is not None] * 3)
+
+
+def partition_local_optimal(n, world, pos=None, src=None, dst=None, **_):
+    """Bisection whose every cut tries all three axes on the graph itself and keeps the one
+    that cuts the fewest edges inside the sub-domain (reference ``reorder.py:889-1003``)."""
+    deg = np.bincount(dst, minlength=n) + 1
+    src, dst = np.asarray(src), np.asarray(dst)
+
+    def choose(idx, per, k):
+        inside = np.zeros(n, bool)
+        inside[idx] = True
+        m = inside[src] & inside[dst]
+        s, d = src[m], dst[m]
+        best, best_ax = None, 0
+        for ax in range(3):
+            order = idx[np.argsort(pos[idx, ax], kind="stable")]
+            c = np.cumsum(deg[order])
+            cut = int(np.searchsorted(c, c[-1] * (k // 2) / k)) + 1
+            left = np.zeros(n, bool)
+            left[order[:cut]] = True
+            cost = int((left[s] != left[d]).sum())
+            if best is None or cost < best:
+                best, best_ax = cost, ax
+        return best_ax
+
+    return _bisect(n, world, pos, deg, choose, [False] * 3)
+
+
+def partition_bruteforce(n, world, pos=None, src=None, dst=None, **_):
+    """Every sequence of cut axes (one axis per tree level, 3^levels candidates) is tried and
+    the partition with the smallest halo volume on the graph is kept (reference
+    ``reorder.py:784-887``)."""
+    import itertools
+
+    deg = np.bincount(dst, minlength=n) + 1
+    levels = int(np.ceil(np.log2(max(world, 1))))
+    best, best_part = None, None
+    for axes in itertools.product(range(3), repeat=max(levels, 1)):
+        def choose(idx, per, k, axes=axes):
+            lvl = levels - int(np.ceil(np.log2(k)))
+            return axes[min(max(lvl, 0), len(axes) - 1)]
+
+        part = _bisect(n, world, pos, deg, choose, [False] * 3)
+        v = halo_volume(part, src, dst)
+        if best is None or v < best:
+            best, best_part = v, part
+    return best_part
+
+
 def partition_greedy(n, world, src=None, dst=None, **_):
     deg = np.bincount(dst, minlength=n) + 1
     target = deg.sum() / world
@@ -115,6 +273,8 @@ PARTITIONERS = {
     "linear-atomwise": partition_linear_atomwise, "linear-edgewise": partition_linear_edgewise,
     "slab": partition_slab, "rcb": partition_rcb, "low_nn": partition_rcb, "longest_dim": partition_rcb,
     "greedy": partition_greedy, "metis": partition_greedy, "worst-case": partition_worst_case,
+    "surface_volume": partition_surface_volume, "approx_neighbors": partition_approx_neighbors,
+    "local_optimal": partition_local_optimal, "bruteforce": partition_bruteforce,
 }
 
 

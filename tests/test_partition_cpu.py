@@ -157,3 +157,16 @@ def test_local_domain_matches_global_decomposition():
         assert list(v[10]) == list(v[11])
         for a, b in zip(v[12], v[13]):
             assert np.array_equal(a, b)
+
+
+def test_graph_aware_bisections_keep_halo_small():
+    g = _toy_graph(seed=5, n=200)
+    hv = {name: P.halo_volume(P.partition(name, g.num_nodes, 4, src=g.src, dst=g.dst, pos=g.pos), g.src, g.dst)
+          for name in ["rcb", "surface_volume", "approx_neighbors", "local_optimal", "bruteforce", "worst-case"]}
+    # the exhaustive search over per-level axis sequences beats each single-axis bisection
+    deg = np.bincount(g.dst, minlength=g.num_nodes) + 1
+    for ax in range(3):
+        fixed = P._bisect(g.num_nodes, 4, g.pos, deg, lambda idx, per, k, ax=ax: ax, [False] * 3)
+        assert hv["bruteforce"] <= P.halo_volume(fixed, g.src, g.dst)
+    assert hv["bruteforce"] <= 1.1 * min(hv["rcb"], hv["surface_volume"], hv["approx_neighbors"])
+    assert hv["local_optimal"] < hv["worst-case"] and hv["bruteforce"] < 0.7 * hv["worst-case"]
