@@ -373,7 +373,8 @@ __global__ void __launch_bounds__(256) rotate_back_edge2_kernel(const __nv_bfloa
 }
 
 // DY[e, k*C + c] = scale * sum_j rot[e,k,j] G[row, j, c]: node path (row = destination n, its
-// edges out_ptr[n] .. out_ptr[n+1]: G[n] is loaded once per edge lane) or edge path (row = e).
+// edges out_ptr[n] .. out_ptr[n+1]: G[n] is loaded once per edge lane) or edge path (row = e, or
+// out_ptr[e] when given: the edge-parallel form of the node path).
 template <int L, int MM, bool NODE>
 __global__ void __launch_bounds__(256) rotate_grad2_kernel(const float* __restrict__ G,
                                                            const long long* __restrict__ out_ptr,
@@ -390,11 +391,12 @@ __global__ void __launch_bounds__(256) rotate_grad2_kernel(const float* __restri
     e0 = out_ptr[r] + q;
     e1 = out_ptr[r + 1];
   } else {
-    r = (long long)blockIdx.x * Q + q;
-    e0 = r;
-    e1 = r + 1;
+    e0 = (long long)blockIdx.x * Q + q;
+    e1 = e0 + 1;
+    if (e0 >= rows || c >= C) return;
+    r = out_ptr ? out_ptr[e0] : e0;  // edge path: out_ptr (if given) is the edge's gradient row
   }
-  if (r >= rows || c >= C) return;
+  if ((NODE && r >= rows) || c >= C) return;
   float2 g[S];
 #pragma unroll
   for (int j = 0; j < S; ++j) g[j] = __ldg(reinterpret_cast<const float2*>(G + ((size_t)r * S + j) * C + c));
@@ -588,11 +590,12 @@ const char* edge_rotate_grad(int L, int MM, const float* G, const long long* row
                              __nv_bfloat16* DY, float* DYf, int E, int C, int Rk, float scale, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
-  if (rows == nullptr && C % 2 == 0) {
+  if (C % 2 == 0) {
+    // edge-parallel, two channels per thread; rows (if given) selects each edge's gradient row
     MALOQ_DISPATCH_FRAME(({
       constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
       dim3 grid((E + Q_ - 1) / Q_, (C / 2 + 63) / 64);
-      rotate_grad2_kernel<FL, FM, false><<<grid, 64 * Q_, 0, st>>>(G, nullptr, rot, DY, DYf, E, C, Rk, scale);
+      rotate_grad2_kernel<FL, FM, false><<<grid, 64 * Q_, 0, st>>>(G, rows, rot, DY, DYf, E, C, Rk, scale);
     }))
   }
   dim3 grid(E, (C + 127) / 128);

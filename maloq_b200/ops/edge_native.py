@@ -159,7 +159,7 @@ class EdgewiseFn(torch.autograd.Function):
         _gemm([dY2[:, a0:a1] for a0, a1 in cb], [w.t().contiguous() for w in w2b], [dH1[:, h0:h1] for h0, h1 in hb],
               [None] * nw)
         dw2 = _weight_grads([dY2[:, a0:a1] for a0, a1 in cb], [H1[:, h0:h1] for h0, h1 in hb])
-        db2 = dY2[:, cb[0][0]:cb[0][1]].float().sum(0)
+        db2 = dY2[:, cb[0][0]:cb[0][1]].sum(0, dtype=torch.float32)
         # gate
         dY1 = torch.empty_like(Y1)
         lib.gate_bwd(*LM, Y1, dH1, dY1, H)
@@ -168,7 +168,7 @@ class EdgewiseFn(torch.autograd.Function):
         _gemm([dY1[:, y0:y1] for y0, y1 in yb], [w.t().contiguous() for w in w1b], [dA[:, a0:a1] for a0, a1 in ab],
               [None] * nw)
         dw1 = _weight_grads([dY1[:, y0:y1] for y0, y1 in yb], [A[:, a0:a1] for a0, a1 in ab])
-        db1 = dY1[:, yb[0][0]:yb[0][1]].float().sum(0)
+        db1 = dY1[:, yb[0][0]:yb[0][1]].sum(0, dtype=torch.float32)
         # gather
         perm, sptr = src_csr(graph)
         DSRC = torch.empty(E, S, C, device=dev, dtype=torch.float32)
@@ -211,13 +211,10 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
 
 
 def _rotate_grad(LM, g, graph, node, DY, DYf, Rk, scale):
-    """Backward of rotate-back: node path walks each output row's edge range (``out_ptr``),
-    the edge path maps edge to edge."""
-    lib = _lib()
-    if node and g.shape[2] % 2 == 0:
-        lib.rotate_grad_nodes(*LM, g, graph.out_ptr, graph.rot, DY, DYf, Rk, scale)
-    else:
-        lib.rotate_grad(*LM, g, graph.dst_out if node else None, graph.rot, DY, DYf, Rk, scale)
+    """Backward of rotate-back, edge-parallel: node path reads each edge's destination row of
+    the gradient (``dst_out``), the edge path its own row.  (Walking each destination's edge
+    range instead - ``rotate_grad_nodes`` - leaves too few CTAs at molecular node counts.)"""
+    _lib().rotate_grad(*LM, g, graph.dst_out if node else None, graph.rot, DY, DYf, Rk, scale)
 
 
 def _halo_args(halo):

@@ -130,7 +130,7 @@ class _Linear(torch.autograd.Function):
         if ctx.needs_input_grad[1]:
             gw = gemm_tn_weight_grad(g2, x2)[: weight.shape[0], : weight.shape[1]]
         if ctx.has_bias and ctx.needs_input_grad[2]:
-            gb = gy.reshape(-1, gy.shape[-1]).float().sum(0)
+            gb = gy.reshape(-1, gy.shape[-1]).sum(0, dtype=torch.float32)
         return gx, gw, gb
 
 

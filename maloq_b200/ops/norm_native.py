@@ -176,7 +176,7 @@ class _SO3Linear(torch.autograd.Function):
                       [part[j] for j in range(S)], [None] * S, mn=True, splits=splits)
         part = part.sum(1)
         dw = torch.stack([part[l * l:(l + 1) * (l + 1)].sum(0) for l in range(L + 1)])
-        db = g[:, 0].float().sum(0)
+        db = g[:, 0].sum(0, dtype=torch.float32)
         return dx.view(B, S, C).to(ctx.in_dtype), dw, db
 
 
