@@ -207,12 +207,12 @@ class SplitTrainer:
     @torch.no_grad()
     def evaluate(self, loss_fxn, device, loader, labeler, output_folder="outputs", samples=None, scale_shift=None,
                  **unused):
-        """Per structure: label MAE, Hamiltonian MAE and eigenvalue MAE (generalised with S
-        when an overlap is given), written to ``model_fock_eval_{rank}.txt``
-        (reference ``splittrainer.py:378-822``)."""
-        import scipy.linalg
-
+        """Per structure: Hamiltonian MAE, orbital-energy MAE (generalised with the overlap
+        when the sample carries one, canonical orthogonalisation), HOMO-LUMO gap and band
+        energy errors (closed shell, all-electron count), written to
+        ``model_fock_eval_{rank}.txt`` (reference ``splittrainer.py:378-822``)."""
         from ..data.batch import collate
+        from ..eval import electronic
 
         self.backbone.eval()
         self.head.eval()
@@ -232,12 +232,19 @@ class SplitTrainer:
             bt = labeler.blocks_from_labels(s, ty, b.y[0])
             Hp, Ht = bp.to_dense(), bt.to_dense()
             Hp = 0.5 * (Hp + Hp.T)
-            ep = scipy.linalg.eigvalsh(Hp)
-            et = scipy.linalg.eigvalsh(Ht)
-            rows.append((k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), s.num_nodes))
+            S = getattr(s, "overlap", None)
+            ne = electronic.n_electrons(s.z, getattr(s, "charge", 0))
+            sp_, st_ = electronic.summary(Hp, S, ne), electronic.summary(Ht, S, ne)
+            ep, et = sp_["eigenvalues"], st_["eigenvalues"]
+
+            def err(key):
+                return float("nan") if sp_[key] is None else abs(sp_[key] - st_[key])
+
+            rows.append((k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), err("gap"),
+                         err("band_energy"), s.num_nodes))
         os.makedirs(output_folder, exist_ok=True)
         with open(os.path.join(output_folder, f"model_fock_eval_{rank}.txt"), "w") as f:
-            f.write("Index\tTotal_MAE\tEigenvalue_MAE\tNum_Atoms\n")
+            f.write("Index\tTotal_MAE\tEigenvalue_MAE\tGap_Error\tBand_Energy_Error\tNum_Atoms\n")
             for r in rows:
                 f.write("\t".join(str(x) for x in r) + "\n")
         return rows
