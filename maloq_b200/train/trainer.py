@@ -206,7 +206,7 @@ class SplitTrainer:
     # ------------------------------------------------------------------ eval / infer
     @torch.no_grad()
     def evaluate(self, loss_fxn, device, loader, labeler, output_folder="outputs", samples=None, scale_shift=None,
-                 **unused):
+                 dump_embeddings=False, **unused):
         """Per structure: Hamiltonian MAE, orbital-energy MAE (generalised with the overlap
         when the sample carries one, canonical orthogonalisation), HOMO-LUMO gap and band
         energy errors (closed shell, all-electron count), written to
@@ -221,6 +221,10 @@ class SplitTrainer:
         for k, s in enumerate(samples):
             b = collate([s], labeler.table).to(device)
             emb = self.backbone(b)
+            if dump_embeddings:
+                from ..analysis.embeddings import dump
+
+                dump(os.path.join(output_folder, "embeddings"), k, emb, b)
             no, eo = self.head(emb, b)
             no, eo = no[0], eo[0]
             if scale_shift is not None:

@@ -289,7 +289,8 @@ class TrainingWorkflow:
                                      log_every=c.get("log_every", 1))
             if c["train_or_eval"] == "eval":
                 return trainer.evaluate(c["test_loss_fxn"], self.device, val, labeler,
-                                        output_folder=c["output_folder"], samples=self.val_samples)
+                                        output_folder=c["output_folder"], samples=self.val_samples,
+                                        dump_embeddings=c.get("dump_embeddings", False))
             if c["distribute_graphs"]:
                 b = val[0]
                 s = self.partition_sample

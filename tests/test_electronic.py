@@ -48,3 +48,38 @@ def test_workflow_eval_writes_orbital_metrics(tmp_path):
                                     "Num_Atoms"]
     vals = [float(x) for x in lines[1].split("\t")]
     assert np.isfinite(vals[1]) and np.isfinite(vals[2])
+
+
+def test_embedding_dumps_projection_and_clusters(tmp_path):
+    from maloq.train_utils import training_workflow
+    from maloq_b200.analysis import embeddings
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=16, batch_size=4, num_epochs=1, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               output_folder=str(tmp_path), device="cpu", log_every=0)
+    training_workflow.TrainingWorkflow(cfg).run()
+    training_workflow.TrainingWorkflow(dict(cfg, train_or_eval="eval", restart_backbone=True, restart_head=True,
+                                            dump_embeddings=True)).run()
+    folder = tmp_path / "embeddings"
+    x, z = embeddings.load(folder)
+    assert x.ndim == 3 and x.shape[1] == 25 and len(z) == len(x)
+    f = embeddings.invariant_features(x)
+    assert f.shape == (len(x), 5 * x.shape[2])
+    out = embeddings.main([str(folder), "--method", "pca", "--clusters", "3"])
+    rows = np.loadtxt(out, delimiter=",", skiprows=1)
+    assert rows.shape == (len(x), 4) and set(np.unique(rows[:, 3])) <= {0, 1, 2}
+    assert len(embeddings.project(f, "tsne")) == len(f)
+
+
+def test_invariant_features_are_rotation_invariant():
+    import torch
+
+    from maloq_b200.analysis.embeddings import invariant_features
+    from maloq_b200.core import sph
+
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((5, 25, 3))
+    R = sph.euler_matrix(0.4, 1.1, -0.7)
+    D = torch.block_diag(*[torch.tensor(sph.wigner_D_from_matrix(l, R)) for l in range(5)]).numpy()
+    xr = np.einsum("ij,njc->nic", D, x)
+    assert np.allclose(invariant_features(x), invariant_features(xr), atol=1e-10)
