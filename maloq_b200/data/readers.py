@@ -13,6 +13,8 @@
   :func:`read_periodic_xyz` (``Lattice=``/``Cell:`` headers), :func:`fermi_energy` and
   :func:`fermi_shift`, :func:`blocks_from_sparse` (atom-pair blocks without densifying) and
   :func:`load_cp2k`.
+* ORCA output: :func:`read_orca_output` (coordinates, contracted basis, printed Fock
+  matrices, total energy).
 """
 
 from __future__ import annotations
@@ -286,3 +288,83 @@ def load_cp2k(xyz_path, h_path, config, basis_name="dzvp_like", s_path=None, out
     ny, y = labeler.labels_from_blocks(s, bsm)
     s.node_y, s.y = ny.unsqueeze(0).cpu(), y.unsqueeze(0).cpu()
     return s, labeler
+
+
+# ------------------------------------------------------------------ ORCA output
+_L_OF = {"s": 0, "p": 1, "d": 2, "f": 3, "g": 4}
+
+
+def _read_printed_matrix(lines, start, n):
+    """An n x n matrix printed in ORCA's column blocks (a header line of column indices, then
+    ``row v v v ...`` lines) from ``lines[start]`` (the first header) to the next blank line;
+    returns (matrix, index of the blank line)."""
+    M = np.zeros((n, n))
+    cols = None
+    i = start
+    while i < len(lines) and lines[i].split():
+        parts = lines[i].split()
+        if cols is not None and len(parts) == len(cols) + 1 and "." in parts[-1]:
+            M[int(parts[0]), cols] = [float(x) for x in parts[1:]]
+        else:
+            cols = [int(x) for x in parts]
+        i += 1
+    return M, i
+
+
+def read_orca_output(path, unrestricted=False):
+    """Structure, contracted basis, Fock matrix and total energy from an ORCA output file.
+
+    Returns ``dict(z, pos, basis, fock, energy)``: ``basis`` maps atomic number -> shell l list
+    (in ORCA's contracted order, e.g. ``3s2p1d`` -> [0, 0, 0, 1, 1, 2]); ``fock`` is the
+    printed ``FOCK`` matrix in ORCA's orbital order (``reorder_orbitals(..., "orca")`` converts
+    it), or ``{"alpha", "beta"}`` when ``unrestricted``; ``energy`` is the total SCF energy in
+    Hartree (None if absent).  Reference ``fock_utils/utils_orca_out.py:30-50, 282-400``."""
+    import re
+
+    with open(path) as f:
+        lines = f.read().splitlines()
+    z, pos, basis, focks, energy = [], [], {}, [], None
+    group = re.compile(r"Group\s+\d+\s+Type\s+(\w+)\s*:\s*\S+\s+contracted to\s+(\S+)")
+    i = 0
+    while i < len(lines):
+        ln = lines[i]
+        if "CARTESIAN COORDINATES (ANGSTROEM)" in ln and not z:
+            j = i + 2
+            while j < len(lines) and lines[j].split():
+                p = lines[j].split()
+                z.append(SYMBOL_TO_Z[p[0]])
+                pos.append([float(x) for x in p[1:4]])
+                j += 1
+            i = j
+            continue
+        m = group.search(ln)
+        if m:
+            shells = []
+            for cnt, l in re.findall(r"(\d+)([spdfg])", m.group(2)):
+                shells += [_L_OF[l]] * int(cnt)
+            basis[SYMBOL_TO_Z[m.group(1)]] = shells
+        if "TOTAL SCF ENERGY" in ln:
+            for k in range(i + 1, min(i + 10, len(lines))):
+                p = lines[k].split()
+                if "Total Energy" in lines[k] and "Eh" in p:
+                    energy = float(p[p.index("Eh") - 1])
+                    break
+        if ln.strip() == "FOCK" and not focks:
+            n = sum(sum(2 * l + 1 for l in basis[a]) for a in z)
+            j = i + 1
+            while not lines[j].split() or set(lines[j].strip()) <= {"-"}:
+                j += 1
+            M, j = _read_printed_matrix(lines, j, n)
+            focks.append(M)
+            if unrestricted:
+                while j < len(lines) and not lines[j].split():
+                    j += 1
+                M, j = _read_printed_matrix(lines, j, n)
+                focks.append(M)
+            i = j
+            continue
+        i += 1
+    fock = None
+    if focks:
+        fock = {"alpha": focks[0], "beta": focks[1]} if unrestricted else focks[0]
+    return {"z": np.asarray(z, np.int64), "pos": np.asarray(pos), "basis": basis, "fock": fock, "energy": energy}

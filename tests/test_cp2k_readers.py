@@ -95,3 +95,40 @@ def test_workflow_trains_on_a_cp2k_folder(tmp_path):
                output_folder=str(tmp_path / "out"), device="cpu", log_every=0)
     h = training_workflow.TrainingWorkflow(cfg).run()
     assert len(h["train_node"]) == 2 and np.isfinite(h["train_node"][-1])
+
+
+def _orca_block(M, width=6):
+    out = []
+    n = len(M)
+    for c0 in range(0, n, width):
+        cols = list(range(c0, min(n, c0 + width)))
+        out.append("                  " + "    ".join(f"{c:6d}" for c in cols))
+        for r in range(n):
+            out.append(f"{r:6d}  " + "  ".join(f"{M[r, c]:10.6f}" for c in cols))
+    return out
+
+
+@pytest.mark.parametrize("unrestricted", [False, True])
+def test_orca_output_reader(tmp_path, unrestricted):
+    rng = np.random.default_rng(5)
+    n = 5 + 14  # H (2s1p) + O (3s2p1d)
+    Fa = np.round(rng.standard_normal((n, n)), 6)
+    Fb = np.round(rng.standard_normal((n, n)), 6)
+    lines = ["junk", "---------------------------------", "CARTESIAN COORDINATES (ANGSTROEM)",
+             "---------------------------------", "  H      0.000000    0.000000    0.740000",
+             "  O      0.100000   -0.200000    0.000000", "", " BASIS SET INFORMATION",
+             "Group   1 Type H   : 4s1p contracted to 2s1p pattern {31/1}",
+             "Group   2 Type O   : 7s4p1d contracted to 3s2p1d pattern {511/31/1}", "",
+             "TOTAL SCF ENERGY", "----------------", "",
+             "Total Energy       :        -76.40123456789 Eh           -2078.97 eV", "", "FOCK", ""]
+    lines += _orca_block(Fa) + ([""] + _orca_block(Fb) if unrestricted else []) + ["", "end"]
+    p = tmp_path / "orca.out"
+    p.write_text("\n".join(lines) + "\n")
+    d = readers.read_orca_output(p, unrestricted=unrestricted)
+    assert list(d["z"]) == [1, 8] and np.allclose(d["pos"][1], [0.1, -0.2, 0.0])
+    assert d["basis"] == {1: [0, 0, 1], 8: [0, 0, 0, 1, 1, 2]}
+    assert abs(d["energy"] + 76.40123456789) < 1e-12
+    if unrestricted:
+        assert np.allclose(d["fock"]["alpha"], Fa) and np.allclose(d["fock"]["beta"], Fb)
+    else:
+        assert np.allclose(d["fock"], Fa)
