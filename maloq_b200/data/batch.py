@@ -24,6 +24,8 @@ class GraphSample:
         self.charge, self.spin = int(charge), int(spin)
         self.node_y, self.y = node_y, y
         self.cell = cell
+        self.energy = None  # total energy (scalar) for energy targets
+        self.forces = None  # [N, 3] for force targets
 
     @property
     def num_nodes(self):
@@ -130,6 +132,10 @@ def collate(samples, pair_table=None, target_dtype=torch.float32, float_dtype=to
     if nys:
         b.node_y = torch.cat([torch.as_tensor(y) for y in nys], dim=1).to(target_dtype)
         b.y = torch.cat([torch.as_tensor(y) for y in ys], dim=1).to(target_dtype)
+    if all(getattr(s, "energy", None) is not None for s in samples):
+        b.energy = torch.as_tensor([float(s.energy) for s in samples], dtype=target_dtype)
+    if all(getattr(s, "forces", None) is not None for s in samples):
+        b.forces = torch.as_tensor(np.concatenate([np.asarray(s.forces) for s in samples]), dtype=target_dtype)
     return b
 
 

@@ -47,14 +47,21 @@ def build_samples(name, n, seed=0, cutoff=None, **kw):
     return [make_sample(spec["gen"](rng), cutoff) for _ in range(n)]
 
 
-def build_dataset(name, n, model_kwargs, seed=0, device="cpu", teacher_seed=1234, cutoff=None, labeler=None, **kw):
+def build_dataset(name, n, model_kwargs, seed=0, device="cpu", teacher_seed=1234, cutoff=None, labeler=None,
+                  target="fock_matrix", **kw):
     """Samples with targets.  ``model_kwargs`` size the teacher (same architecture as the
-    trained model: lmax/mmax/channels/layers/basis count)."""
+    trained model: lmax/mmax/channels/layers/basis count).  ``target``: Fock labels
+    (``fock_matrix`` / ``density_matrix``), or teacher ``energies`` / ``forces``."""
     labeler = labeler or labeler_for(name, device)
     samples = build_samples(name, n, seed, cutoff, **kw)
     teacher = Teacher(model_kwargs, labeler, seed=teacher_seed, device=device)
-    hs = teacher.hamiltonians(samples)
-    attach_targets(samples, hs, labeler)
+    if target in ("energies", "forces"):
+        from .targets import attach_scalar_targets
+
+        attach_scalar_targets(samples, teacher, target)
+    else:
+        hs = teacher.hamiltonians(samples)
+        attach_targets(samples, hs, labeler)
     del teacher
     if torch.cuda.is_available():
         torch.cuda.empty_cache()

@@ -133,6 +133,8 @@ def load_nabladft(path, config, device="cpu", convention="psi4", indices=None):
         ny, y = labeler.labels_from_blocks(s, bsm)
         s.node_y, s.y = ny.unsqueeze(0).cpu(), y.unsqueeze(0).cpu()
         s.overlap = S
+        s.energy = float(E[0])  # energy and forces as stored in the database
+        s.forces = F.astype(np.float64)
         samples.append(s)
     return samples, labeler
 

@@ -125,6 +125,33 @@ class Teacher:
         return out
 
 
+def attach_scalar_targets(samples, teacher: Teacher, kind, seed=4321, chunk=16):
+    """Energy or force targets of a frozen random-init energy/force head on the teacher's
+    backbone (``kind``: "energies" or "forces"); sets ``sample.energy`` / ``sample.forces``.
+    Energies are invariant and forces equivariant by construction, so they are learnable."""
+    from ..models.heads import HELM_Energy_Head, HELM_Force_Head
+
+    g = torch.random.get_rng_state()
+    torch.manual_seed(seed)
+    head = (HELM_Energy_Head if kind == "energies" else HELM_Force_Head)(teacher.backbone).to(teacher.device).eval()
+    torch.random.set_rng_state(g)
+    with torch.no_grad():
+        for i in range(0, len(samples), chunk):
+            part = samples[i:i + chunk]
+            b = collate(part, teacher.labeler.table).to(teacher.device)
+            out = head(teacher.backbone(b), b)
+            if kind == "energies":
+                for s, e in zip(part, out["energies"].double().cpu().numpy()):
+                    s.energy = float(e)
+            else:
+                f = out["forces"].double().cpu().numpy()
+                o = 0
+                for s in part:
+                    s.forces = f[o:o + s.num_nodes].copy()
+                    o += s.num_nodes
+    return samples
+
+
 def attach_targets(samples, hamiltonians, labeler: FockLabeler, scale_shift=None):
     """Fill ``node_y``/``y`` ([1, rows, D] float32, CPU) of every sample."""
     for s, h in zip(samples, hamiltonians):

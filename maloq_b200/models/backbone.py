@@ -212,6 +212,15 @@ class Graph:
         self.chunks = None  # [(e0, e1, n0, n1)] for edge-chunked execution
         self.rot_fn = None  # (e0, e1) -> rotations of those edges, when rot is not stored
 
+    def whole(self):
+        """The unchunked graph (rotations computed if they are not stored)."""
+        if self.chunks is None:
+            return self
+        g = Graph(self.src, self.dst, self.rot if self.rot is not None else self.rot_fn(0, self.src.shape[0]),
+                  self.dst_ptr, self.num_nodes, self.lmax, self.mmax, self.halo)
+        g.num_nodes_ext = getattr(self, "num_nodes_ext", None) or self.num_nodes
+        return g
+
     def chunk_graph(self, i):
         """Sub-graph of chunk ``i``.  With gradients the sub-graphs are built once per forward
         and shared by every layer (their cached source CSRs are reused in backward); without
@@ -377,8 +386,8 @@ class eSEN_Backbone(nn.Module):
             out["edge_chunks"] = [(e0, e1) for e0, e1, _, _ in graph.chunks]
         elif self.include_edges:
             out["edge_embeddings"] = self.norm(x_edge_emb)
-        else:
-            out.update({"x_edge": x_edge, "graph": graph})
+        # edge features and graph for heads that run their own message pass (energy / force)
+        out.update({"x_edge": x_edge, "graph": graph})
         return out
 
     def _degree_embedding_chunked(self, x_node, x_edge, graph):

@@ -267,7 +267,13 @@ class _ConvHeadBase(nn.Module):
                                           self.mappingReduced, internal_weights=True)
 
     def conv(self, emb):
-        return ops.edgewise(self, emb["node_embeddings"], None, emb["x_edge"], emb["graph"], "node")
+        xe = emb["x_edge"]
+        if hasattr(xe, "full"):  # chunked backbones hand over the lazy edge features
+            xe = xe.full()
+        graph = emb["graph"]
+        if graph.chunks is not None:  # one pass over all edges (the head is small)
+            graph = graph.whole()
+        return ops.edgewise(self, emb["node_embeddings"], None, xe, graph, "node")
 
 
 class HELM_Energy_Head(_ConvHeadBase):

@@ -102,7 +102,14 @@ class SplitTrainer:
 
     def forward_loss(self, batch, loss_fxn):
         emb = self.backbone(batch)
-        node_out, edge_out = self.head(emb, batch)
+        out = self.head(emb, batch)
+        if isinstance(out, dict):  # energy / force heads: one loss on the predicted quantity
+            key, target = ("energies", batch.energy) if "energies" in out else ("forces", batch.forces)
+            if target is None:
+                raise ValueError(f"the batch carries no {key} targets")
+            loss = loss_fxn(out[key], target.to(out[key].dtype))
+            return loss, torch.zeros_like(loss), loss
+        node_out, edge_out = out
         mt, npt, ept = self.masks(batch)
         spins = node_out.shape[0]
         lns, les, lts = [], [], []

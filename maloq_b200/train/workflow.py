@@ -188,7 +188,8 @@ class TrainingWorkflow:
             kw = self.model_kwargs(labeler.layout.lmax)
             n = c["num_structures"]
             samples, labeler = datasets.build_dataset(kind, n, kw, seed=c["seed"], device=self.device,
-                                                      cutoff=2 * c["rcut_orbitals"], labeler=labeler)
+                                                      cutoff=2 * c["rcut_orbitals"], labeler=labeler,
+                                                      target=c["loss_target"])
         elif name == "nablaDFT":
             from ..data.readers import load_nabladft
 

@@ -229,3 +229,16 @@ def test_streamed_hamiltonian_shard_matches_full_conversion():
                 data, ptr = hamiltonian_shard(hd, emb, b, lab)
         res.append(data)
     assert torch.allclose(res[0].double(), res[1].double(), atol=1e-10)
+
+
+@pytest.mark.parametrize("target", ["energies", "forces"])
+def test_workflow_trains_energy_and_force_targets(tmp_path, target):
+    """loss_target energies / forces: teacher targets on the samples, the HELM energy / force
+    head, and a loss that goes down."""
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=12, batch_size=4, num_epochs=5, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2, lr_init=3e-3,
+               loss_target=target, output_folder=str(tmp_path), device="cpu", log_every=0)
+    h = training_workflow.TrainingWorkflow(cfg).run()
+    assert np.isfinite(h["train_node"][-1]) and h["train_node"][-1] < h["train_node"][0]
