@@ -116,16 +116,19 @@ class BasisTransform:
         self.W_global_inv = self.W_global_inv.to(device=device, dtype=dtype)
         return self
 
-    def column_tables(self, inverse: bool):
-        """Per output column u of the transform (``inverse`` = uncoupled -> coupled):
+    def column_tables(self, inverse: bool, transpose: bool = False):
+        """Per output column u of the transform (``inverse`` = uncoupled -> coupled;
+        ``transpose`` = multiply by the transposed matrix, the backward of the transform):
         ``meta[u] = (s, n, c, 0)`` and ``coef`` such that
         ``out[:, u] = sum_{j<n} in[:, s + j] * coef[c + j * n]`` (one square CG block per orbital
         shell pair; coefficients of adjacent columns of a block are adjacent)."""
-        key = "_tables_inv" if inverse else "_tables_fwd"
+        key = f"_tables_{'inv' if inverse else 'fwd'}{'_t' if transpose else ''}"
         if getattr(self, key, None) is None:
             W = (self.W_global_inv if inverse else self.W_global).detach().cpu().double().numpy()
             src = self.H_slices if inverse else self.in_slices
             dst = self.in_slices if inverse else self.H_slices
+            if transpose:
+                W, src, dst = W.T, dst, src
             meta = np.zeros((self.dim, 4), dtype=np.int32)
             coef = []
             base = 0

@@ -25,11 +25,11 @@ _IDENTITY = {}
 _POS32 = {}
 
 
-def _tables(transform, inverse, device, dtype):
+def _tables(transform, inverse, device, dtype, transpose=False):
     cache = transform.__dict__.setdefault("_device_tables", {})
-    key = (bool(inverse), str(device), dtype)
+    key = (bool(inverse), bool(transpose), str(device), dtype)
     if key not in cache:
-        meta, coef = transform.column_tables(inverse)
+        meta, coef = transform.column_tables(inverse, transpose)
         cache[key] = (torch.as_tensor(meta, device=device), torch.as_tensor(coef, device=device, dtype=dtype))
     return cache[key]
 
@@ -56,15 +56,34 @@ def _dtype(x):
     return torch.float64 if x.dtype == torch.float64 else torch.float32
 
 
-def basis_transform(x, transform, inverse=False):
+def _rows_transform(x, transform, inverse, transpose):
     dt = _dtype(x)
     shape = x.shape
     x2 = x.reshape(-1, shape[-1]).to(dt).contiguous()
-    meta, coef = _tables(transform, inverse, x.device, dt)
+    meta, coef = _tables(transform, inverse, x.device, dt, transpose)
     out = torch.empty(x2.shape[0], meta.shape[0], device=x.device, dtype=dt)
     _lib().basis_rows(x2, out, None, None, None, meta, coef, x2.shape[1], x2.shape[0], False, False)
     count_launches(1)
     return out.reshape(*shape[:-1], meta.shape[0]).to(x.dtype)
+
+
+class _BasisTransformFn(torch.autograd.Function):
+    """x @ W (block diagonal); backward g @ W^T with the transposed tables."""
+
+    @staticmethod
+    def forward(ctx, x, transform, inverse):
+        ctx.transform, ctx.inverse = transform, inverse
+        return _rows_transform(x, transform, inverse, False)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _rows_transform(g.contiguous(), ctx.transform, ctx.inverse, True), None, None
+
+
+def basis_transform(x, transform, inverse=False):
+    if torch.is_grad_enabled() and x.requires_grad:
+        return _BasisTransformFn.apply(x, transform, inverse)
+    return _rows_transform(x, transform, inverse, False)
 
 
 def _rows(ptr, pt):

@@ -72,7 +72,7 @@ class Prefetcher:
 
 class SplitTrainer:
     def __init__(self, backbone, head, head_irreps, save_frequency=10, run_id=None, run_name="noname",
-                 mask_table=None, grad_sync=None, nan_guard=False, status_every=0):
+                 mask_table=None, grad_sync=None, nan_guard=False, status_every=0, uncoupled_loss_transform=None):
         self.backbone, self.head, self.head_irreps = backbone, head, head_irreps
         self.save_frequency, self.run_name = save_frequency, run_name
         self.mask_table = mask_table
@@ -82,6 +82,10 @@ class SplitTrainer:
         # is read and a recorded timeout / bounds error raised on the host (CommTimeoutError,
         # BoundsError); reading it synchronises the device
         self.status_every = int(status_every)
+        # compute_uncoupled_loss: outputs and targets go through get_H (matrix-element basis)
+        # before the loss; the padding masks are the same in both bases (each CG block keeps
+        # its index range)
+        self.uncoupled = uncoupled_loss_transform
         self._steps = 0
         self.open_shell = getattr(head, "num_spins", 1) > 1
         self.history = {"train_node": [], "train_edge": [], "val_node": [], "val_edge": []}
@@ -114,8 +118,13 @@ class SplitTrainer:
         spins = node_out.shape[0]
         lns, les, lts = [], [], []
         for s in range(spins):
-            ln, le, lt = loss_ops.fock_loss(node_out[s], edge_out[s], batch.node_y[s], batch.y[s], mt, npt, ept,
-                                            loss_fxn)
+            no, eo, nt, et = node_out[s], edge_out[s], batch.node_y[s], batch.y[s]
+            if self.uncoupled is not None:
+                T = self.uncoupled
+                no, eo = T.get_H(no), T.get_H(eo)
+                with torch.no_grad():
+                    nt, et = T.get_H(nt.to(no.dtype)), T.get_H(et.to(eo.dtype))
+            ln, le, lt = loss_ops.fock_loss(no, eo, nt, et, mt, npt, ept, loss_fxn)
             lns.append(ln)
             les.append(le)
             lts.append(lt)

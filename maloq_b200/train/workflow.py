@@ -177,6 +177,51 @@ class TrainingWorkflow:
             raise ValueError(f"no CP2K structure directories under {root}")
         return samples, labeler
 
+    def _apply_scale_shift(self, train, samples, labeler, name):
+        """``scale_and_shift``: Fock targets get the per-element mean of their l=0 on-site
+        entries subtracted (tables ``element_scale_shifts_{dataset}.pt`` in the output folder,
+        loaded if present, else computed from the training set and saved); energy targets get
+        per-element linear references (least squares of E on element counts, saved as
+        ``lin_ref_coeffs_{dataset}.npz`` with ``coeff[Z]``) subtracted.  Reference
+        ``training_workflow.py:150-228``."""
+        import numpy as np
+
+        from ..data.targets import ScaleShift
+
+        c = self.config
+        os.makedirs(c["output_folder"], exist_ok=True)
+        if c["loss_target"] in ("fock_matrix", "density_matrix"):
+            path = os.path.join(c["output_folder"], f"element_scale_shifts_{name}.pt")
+            if os.path.exists(path):
+                d = torch.load(path, weights_only=False)
+                ss = ScaleShift(labeler, means={int(z): torch.as_tensor(v) for z, v in
+                                                d["element_scalar_means"].items()})
+            else:
+                ss = ScaleShift(labeler, train)
+                stds = {}
+                for z in ss.means:
+                    rows = torch.cat([s.node_y[0][torch.as_tensor(s.z == z)][:, ss.scalar_idx] for s in train])
+                    stds[z] = rows.float().std(0, unbiased=False)
+                if self.rank == 0:
+                    torch.save({"element_scalar_means": ss.means, "element_scalar_stds": stds,
+                                "scalar_irrep_indices": ss.scalar_idx.tolist()}, path)
+            for s in samples:
+                s.node_y = ss.shift(s.node_y[0], s.z).unsqueeze(0)
+            self.scale_shift = ss
+        elif c["loss_target"] == "energies":
+            path = os.path.join(c["output_folder"], f"lin_ref_coeffs_{name}.npz")
+            if os.path.exists(path):
+                coeff = np.load(path)["coeff"]
+            else:
+                zmax = max(int(s.z.max()) for s in samples)
+                A = np.stack([np.bincount(s.z, minlength=zmax + 1) for s in train]).astype(np.float64)
+                coeff = np.linalg.lstsq(A, np.array([s.energy for s in train]), rcond=None)[0]
+                if self.rank == 0:
+                    np.savez(path, coeff=coeff)
+            for s in samples:
+                s.energy = s.energy - float(np.bincount(s.z, minlength=len(coeff))[: len(coeff)] @ coeff)
+            self.energy_refs = coeff
+
     def prepare_data(self):
         c = self.config
         if c["distribute_graphs"]:
@@ -201,6 +246,14 @@ class TrainingWorkflow:
         n_val = c["num_val"] or max(1, len(samples) // 8)
         n_train = c["num_train"] or (len(samples) - n_val)
         train, val = samples[:n_train], samples[n_train:n_train + n_val]
+        if name == "nablaDFT" and c.get("dbpath_val"):  # a separate validation database
+            from ..data.readers import load_nabladft
+
+            val, _ = load_nabladft(c["dbpath_val"], c, self.device)
+            samples = train + val
+        self.scale_shift, self.energy_refs = None, None
+        if c.get("scale_and_shift"):
+            self._apply_scale_shift(train, samples, labeler, name)
         if self.world_size > 1 and not c["distribute_graphs"]:
             train = [train[i] for i in pdist.split_indices(len(train), self.rank, self.world_size)]
             val = [val[i] for i in pdist.split_indices(len(val), self.rank, self.world_size, drop_remainder=False)] or val[:1]
@@ -277,7 +330,9 @@ class TrainingWorkflow:
             trainer = SplitTrainer(backbone, head, labeler.irreps, save_frequency=c["save_frequency"],
                                    run_name=c["run_name"], mask_table=mask_table,
                                    grad_sync=self.grad_sync(backbone, head),
-                                   status_every=c["device_status_every"])
+                                   status_every=c["device_status_every"],
+                                   uncoupled_loss_transform=labeler.transform if c.get("compute_uncoupled_loss")
+                                   else None)
             if c["train_or_eval"] == "train":
                 if c["restart_backbone"] or c["restart_head"]:
                     st = ckpt.load_resume(c["output_folder"], sched)
@@ -291,6 +346,7 @@ class TrainingWorkflow:
             if c["train_or_eval"] == "eval":
                 return trainer.evaluate(c["test_loss_fxn"], self.device, val, labeler,
                                         output_folder=c["output_folder"], samples=self.val_samples,
+                                        scale_shift=getattr(self, "scale_shift", None),
                                         dump_embeddings=c.get("dump_embeddings", False))
             if c["distribute_graphs"]:
                 b = val[0]

@@ -97,3 +97,23 @@ def test_irreps_sort_permutation():
     orig = sorted_vals[perm]
     # sorted: 0e(#1) 0e(#3) 1e(#2) 2e(#0) -> original order 2e, 0e, 1e, 0e
     assert orig.tolist() == [5, 6, 7, 8, 9, 0, 2, 3, 4, 1]
+
+
+def test_basis_transform_column_tables_and_transposes():
+    """The per-column tables the row kernel uses reproduce x @ W, x @ W_inv and (for the
+    backward) x @ W^T, x @ W_inv^T."""
+    import numpy as np
+
+    from maloq_b200.data import datasets
+
+    T = datasets.labeler_for("druglike").transform
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((7, T.dim))
+    for inverse in (False, True):
+        W = (T.W_global_inv if inverse else T.W_global).double().numpy()
+        for transpose, ref in ((False, x @ W), (True, x @ W.T)):
+            meta, coef = T.column_tables(inverse, transpose)
+            out = np.zeros_like(x)
+            for u, (s, n, c, _) in enumerate(meta):
+                out[:, u] = x[:, s:s + n] @ coef[c + np.arange(n) * n]
+            assert np.allclose(out, ref, atol=1e-6)

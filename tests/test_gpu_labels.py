@@ -81,3 +81,13 @@ def test_labeler_targets_match_cpu_path():
     assert torch.allclose(e_g.cpu(), e_c, atol=1e-5, rtol=1e-5)
     back = labeler_gpu.blocks_from_labels(s, n_g, e_g)
     assert np.allclose(back.data, bsm.data, atol=1e-4)
+
+
+def test_basis_transform_gradient_matches_matmul():
+    labeler = datasets.labeler_for("druglike", "cuda")
+    T = labeler.transform
+    x = torch.randn(50, T.dim, device="cuda", requires_grad=True)
+    w = torch.randn(50, T.dim, device="cuda")
+    (bt.apply_transform(x, T, inverse=False) * w).sum().backward()
+    ref = w @ T.W_global.to("cuda").float().t()
+    assert (x.grad - ref).abs().max() <= 1e-5 * max(1.0, ref.abs().max().item())

@@ -242,3 +242,35 @@ def test_workflow_trains_energy_and_force_targets(tmp_path, target):
                loss_target=target, output_folder=str(tmp_path), device="cpu", log_every=0)
     h = training_workflow.TrainingWorkflow(cfg).run()
     assert np.isfinite(h["train_node"][-1]) and h["train_node"][-1] < h["train_node"][0]
+
+
+def test_scale_shift_and_uncoupled_loss_in_workflow(tmp_path):
+    """scale_and_shift writes the per-element l=0 table (reference key names) and the
+    shifted targets have zero per-element mean; compute_uncoupled_loss trains through the
+    differentiable basis transform; evaluation un-shifts."""
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=12, batch_size=4, num_epochs=3, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2, lr_init=3e-3,
+               scale_and_shift=True, compute_uncoupled_loss=True, output_folder=str(tmp_path), device="cpu",
+               log_every=0)
+    wf = training_workflow.TrainingWorkflow(cfg)
+    h = wf.run()
+    assert h["train_node"][-1] < h["train_node"][0]
+    d = torch.load(tmp_path / "element_scale_shifts_synthetic_small.pt", weights_only=False)
+    assert set(d) == {"element_scalar_means", "element_scalar_stds", "scalar_irrep_indices"}
+    ev = training_workflow.TrainingWorkflow(dict(cfg, train_or_eval="eval", restart_backbone=True,
+                                                 restart_head=True)).run()
+    assert np.isfinite(ev[0][1])
+
+
+def test_energy_linear_references(tmp_path):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=12, batch_size=4, num_epochs=2, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               loss_target="energies", scale_and_shift=True, output_folder=str(tmp_path), device="cpu", log_every=0)
+    wf = training_workflow.TrainingWorkflow(cfg)
+    wf.run()
+    coeff = np.load(tmp_path / "lin_ref_coeffs_synthetic_small.npz")["coeff"]
+    assert coeff.ndim == 1 and np.isfinite(coeff).all() and wf.energy_refs is not None
