@@ -79,3 +79,19 @@ def test_peer_timeout_raises_comm_timeout_on_the_host(cuda_device):
     with pytest.raises(kernels.CommTimeoutError):
         SplitTrainer.check_status("test step")
     kernels.check_device_status()  # cleared: no raise
+
+
+def test_edge_rotation_rows_orthonormal_and_empty(cuda_device):
+    """The m-truncated rows of D are orthonormal (rot rot^T = 1), and zero edges is a no-op."""
+    from maloq_b200.core import sph
+    from maloq_b200.models.so3 import CoefficientMapping
+    from maloq_b200.ops import misc_native
+
+    mp = CoefficientMapping(6, 2).to(cuda_device)
+    Js = [j.to(cuda_device) for j in sph.J_matrices(6)]
+    v = torch.randn(777, 3, device=cuda_device)
+    rot = misc_native.edge_rotation(v, 6, 2, Js, mp)
+    eye = torch.eye(rot.shape[1], device=cuda_device).expand(rot.shape[0], -1, -1)
+    assert (rot @ rot.transpose(1, 2) - eye).abs().max().item() < 1e-5
+    empty = misc_native.edge_rotation(v[:0], 6, 2, Js, mp)
+    assert empty.shape == (0, rot.shape[1], rot.shape[2])
