@@ -117,12 +117,14 @@ class TrainingWorkflow:
                     mmax=min(mmax, lmax), cutoff=c["rcut_gaussian"], edge_channels=c["l_embedding_dim"],
                     num_layers=c["num_mp_layers"], num_distance_basis=c["num_distance_basis"],
                     gaussian_width=c["gaussian_width"], message_type=c["message_type"], open_shell=c["open_shell"],
-                    activation_checkpointing=c["activation_checkpointing"])
+                    activation_checkpointing=c["activation_checkpointing"], edge_chunk=c.get("edge_chunk"))
 
     def prepare_partitioned(self):
-        """One structure split over the ranks (graph parallel): rank 0 generates it, every rank
-        builds the same partition, keeps its domain, and labels its nodes/edges with the
-        partitioned teacher (reference ``fock_targets_batched.py:231-333``)."""
+        """One structure split over the ranks (graph parallel): rank 0 generates it (or every
+        rank reads the same CP2K structure, ``dataset_name: cp2k``), every rank builds the same
+        partition, keeps its domain, and takes its nodes'/edges' targets (read ones, or the
+        partitioned teacher's for synthetic structures; reference
+        ``fock_targets_batched.py:231-333``)."""
         import torch.distributed as dist
 
         from ..data.targets import Teacher
@@ -132,21 +134,25 @@ class TrainingWorkflow:
         c = self.config
         name = c["dataset_name"]
         kind = name[len("synthetic_"):] if name.startswith("synthetic_") else name
-        labeler = datasets.labeler_for(kind, self.device)
-        obj = [None]
-        if self.rank == 0:
-            obj[0] = datasets.build_samples(kind, 1, seed=c["seed"], cutoff=2 * c["rcut_orbitals"],
-                                            n_atoms=c.get("num_atoms", 20000))[0]
-        if dist.is_initialized():
-            dist.broadcast_object_list(obj, src=0)
-        sample = obj[0]
+        if name == "cp2k":
+            samples, labeler = self._load_cp2k_folder(dict(c, num_structures=c.get("structure_index", 0) + 1))
+            sample = samples[c.get("structure_index", 0)]
+        else:
+            labeler = datasets.labeler_for(kind, self.device)
+            obj = [None]
+            if self.rank == 0:
+                obj[0] = datasets.build_samples(kind, 1, seed=c["seed"], cutoff=2 * c["rcut_orbitals"],
+                                                n_atoms=c.get("num_atoms", 20000))[0]
+            if dist.is_initialized():
+                dist.broadcast_object_list(obj, src=0)
+            sample = obj[0]
         world = self.world_size if dist.is_initialized() else 1
         part = P.partition(c["partition_type"], sample.num_nodes, world, src=sample.src, dst=sample.dst,
                            pos=sample.pos, cell=sample.cell)
         dom = P.decompose(part, sample.src, sample.dst, world)[self.rank if dist.is_initialized() else 0]
         transport = c.get("halo_transport") or ("peer" if self.device.type == "cuda" and world > 1 else "collective")
         batch = partition_batch(sample, dom, labeler.table, device=self.device, transport=transport)
-        if c["train_or_eval"] != "infer":
+        if c["train_or_eval"] != "infer" and sample.node_y is None:
             teacher = Teacher(self.model_kwargs(labeler.layout.lmax), labeler, device=self.device)
             with torch.no_grad():
                 no, eo = teacher.head(teacher.backbone(batch), batch)

@@ -170,3 +170,34 @@ def test_graph_aware_bisections_keep_halo_small():
         assert hv["bruteforce"] <= P.halo_volume(fixed, g.src, g.dst)
     assert hv["bruteforce"] <= 1.1 * min(hv["rcb"], hv["surface_volume"], hv["approx_neighbors"])
     assert hv["local_optimal"] < hv["worst-case"] and hv["bruteforce"] < 0.7 * hv["worst-case"]
+
+
+def _cp2k_worker(rank, world, data, folder):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="cp2k", dbpath=data, distribute_graphs=True, partition_type="linear-edgewise",
+               l_embedding_dim=8, num_mp_layers=1, num_distance_basis=8, rcut_orbitals=3.0, rcut_gaussian=6.0,
+               mmax=2, num_epochs=2, lr_init=1e-3, device="cpu", output_folder=folder, log_every=0, edge_chunk=500)
+    return training_workflow.TrainingWorkflow(cfg).run()
+
+
+def test_partitioned_workflow_on_a_cp2k_structure(tmp_path):
+    """dataset cp2k + distribute_graphs: every rank reads the structure and the dumped
+    Hamiltonian, keeps its domain's targets, and trains (chunked blocks, 2 gloo ranks)."""
+    import scipy.sparse as sp
+
+    from maloq_b200.data import readers, structures
+
+    rng = np.random.default_rng(7)
+    st = structures.amorphous_sio2(rng, 90)
+    d = tmp_path / "data" / "s0"
+    d.mkdir(parents=True)
+    sym = {14: "Si", 8: "O"}
+    lines = [str(len(st.z)), "Cell: 13 13 13"] + [f"{sym[int(z)]} {p[0]:.6f} {p[1]:.6f} {p[2]:.6f}"
+                                                 for z, p in zip(st.z, np.mod(st.pos * 13.0 / st.cell, 13.0))]
+    (d / "structure.xyz").write_text("\n".join(lines) + "\n")
+    n = 13 * len(st.z)
+    A = sp.random(n, n, density=0.02, random_state=0)
+    readers.write_cp2k_csr(d / "hamiltonian.csr", (A + A.T).tocsr())
+    out = _dist_util.run(_cp2k_worker, world=2, args=(str(tmp_path / "data"), str(tmp_path / "out")))
+    assert len(out[0]["train_node"]) == 2 and np.isfinite(out[0]["train_node"]).all()
