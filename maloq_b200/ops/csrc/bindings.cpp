@@ -427,13 +427,15 @@ void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask,
                                stream()));
 }
 
-void fock_loss_grad(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, double g_sse, double g_sae,
-                    at::Tensor G) {
+// G = d(loss)/d(O) from gstat[0] = d/d(sse), gstat[1] = d/d(sae) (device tensor, any offset)
+void fock_loss_grad(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, at::Tensor gstat, at::Tensor G) {
   chk(O, at::kFloat, "output");
   chk(G, at::kFloat, "grad");
+  TORCH_CHECK(gstat.is_cuda() && gstat.scalar_type() == at::kFloat && gstat.numel() >= 2 && gstat.stride(0) == 1,
+              "fock_loss_grad: gstat needs 2 contiguous fp32 values on the device");
   const at::cuda::CUDAGuard guard(O.device());
   check(maloq::fock_loss_grad(O.data_ptr<float>(), T.data_ptr<float>(), ll(pt), mask.data_ptr<uint8_t>(),
-                              (int)O.size(1), O.size(0), (float)g_sse, (float)g_sae, G.data_ptr<float>(), mask.size(0),
+                              (int)O.size(1), O.size(0), gstat.data_ptr<float>(), G.data_ptr<float>(), mask.size(0),
                               stream()));
 }
 

@@ -8,7 +8,8 @@
 //   (gamma = 0).  Output ROT [E, R, S] fp32, zero outside the row's degree block.
 // * fock_loss_stats / fock_loss_grad: masked squared / absolute error sums of the node and
 //   edge label rows (mask = mask_table[pair_type[row]]), reduced per CTA then summed in fixed
-//   order; the gradient kernel writes d(loss)/d(output) from the six scalar gradients.
+//   order; the gradient kernel writes d(loss)/d(output) from the scalar gradients of the
+//   statistics, read from device memory (no host round trip between forward and backward).
 #include "common.cuh"
 #include "misc.h"
 
@@ -135,8 +136,9 @@ __global__ void fock_loss_stats_kernel(const float* __restrict__ O, const float*
 // G[i] = mask * (g_sse * 2 (o - t) + g_sae * sign(o - t))
 __global__ void fock_loss_grad_kernel(const float* __restrict__ O, const float* __restrict__ Tt,
                                       const long long* __restrict__ pt, const uint8_t* __restrict__ mask, int D,
-                                      long long rows, float g_sse, float g_sae, float* __restrict__ G,
+                                      long long rows, const float* __restrict__ gstat, float* __restrict__ G,
                                       long long n_pt) {
+  const float g_sse = gstat[0], g_sae = gstat[1];
   const long long total = rows * D;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / D;
@@ -182,9 +184,9 @@ const char* fock_loss_stats(const float* O, const float* Tt, const long long* pt
 }
 
 const char* fock_loss_grad(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
-                           long long rows, float g_sse, float g_sae, float* G, long long n_pt, cudaStream_t st) {
+                           long long rows, const float* gstat, float* G, long long n_pt, cudaStream_t st) {
   if (rows == 0) return nullptr;
-  fock_loss_grad_kernel<<<fock_loss_grid(rows * D), 256, 0, st>>>(O, Tt, pt, mask, D, rows, g_sse, g_sae, G, n_pt);
+  fock_loss_grad_kernel<<<fock_loss_grid(rows * D), 256, 0, st>>>(O, Tt, pt, mask, D, rows, gstat, G, n_pt);
   return misc_err();
 }
 

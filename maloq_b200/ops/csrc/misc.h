@@ -12,6 +12,6 @@ int fock_loss_grid(long long n);
 const char* fock_loss_stats(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
                             long long rows, float* part, int grid, long long n_pt, cudaStream_t st);
 const char* fock_loss_grad(const float* O, const float* Tt, const long long* pt, const uint8_t* mask, int D,
-                           long long rows, float g_sse, float g_sae, float* G, long long n_pt, cudaStream_t st);
+                           long long rows, const float* gstat, float* G, long long n_pt, cudaStream_t st);
 
 }  // namespace maloq

@@ -17,6 +17,7 @@ import argparse
 import os
 import sys
 
+import numpy as np
 import torch
 
 
@@ -194,7 +195,30 @@ def suite_calls(edges=43408, device="cuda"):
     lgrid = lib.fock_loss_grid(E * D)
     lstat = torch.empty(lgrid, 3, device=dev)
     lgrad = torch.empty_like(tgt)
+    gstat = torch.tensor([1.0, 0.5], device=dev)
     ls, ms = mapping.l_harmonic.tolist(), mapping.m_complex.tolist()
+    meta_h, coef_h = labels_native._tables(labeler.transform, False, dev, torch.float32)
+    blocks_out = torch.empty_like(data)
+    # device radius graph on a periodic Si/O cell of about E / 140 atoms (8 A cutoff)
+    from ..data import structures
+    from ..data.graph_gpu import grid_for
+
+    st = structures.amorphous_sio2(np.random.default_rng(0), max(200, E // 140))
+    lo, ext, ncell, periodic = grid_for(st.pos, 8.0, st.cell)
+    grid = [float(v) for v in lo] + [float(v) for v in ext] + [8.0]
+    nc = [int(v) for v in ncell]
+    pos_t = torch.as_tensor(st.pos, device=dev).contiguous()
+    cell_id = torch.empty(len(st.z), dtype=torch.long, device=dev)
+    lib.radius_graph_cells(pos_t, grid, nc, periodic, cell_id)
+    order = torch.argsort(cell_id, stable=True)
+    cstart = torch.zeros(nc[0] * nc[1] * nc[2] + 1, dtype=torch.long, device=dev)
+    cstart[1:] = torch.cumsum(torch.bincount(cell_id, minlength=nc[0] * nc[1] * nc[2]), 0)
+    tg = torch.arange(len(st.z), device=dev)
+    cnt = torch.empty(len(st.z), dtype=torch.long, device=dev)
+    lib.radius_graph_pass(pos_t, grid, nc, periodic, tg, order, cstart, cnt, None, None, None)
+    gptr = torch.cumsum(cnt, 0) - cnt
+    g_src = torch.empty(int(cnt.sum()), dtype=torch.long, device=dev)
+    g_vec = torch.empty(int(cnt.sum()), 3, dtype=torch.float64, device=dev)
     return [
         ("edge_rotation", lambda: lib.edge_rotation(vec, flat, joff, L, ls, ms, rot)),
         ("gemm_tc2 (conv1 grouped, 2-SM)", lambda: lib.gemm(As, Ws, Cs, [None] * 3, False, 0, 1.0, 1, 128)),
@@ -220,7 +244,14 @@ def suite_calls(edges=43408, device="cuda"):
         ("basis_rows (blocks -> coupled)", lambda: lib.basis_rows(data, coupled, bptr, pt, pos32, meta, coef, D, E,
                                                                  True, False)),
         ("fock_loss_stats", lambda: lib.fock_loss_stats(coupled, tgt, pt, mask, lstat)),
-        ("fock_loss_grad", lambda: lib.fock_loss_grad(coupled, tgt, pt, mask, 1.0, 0.5, lgrad)),
+        ("fock_loss_grad", lambda: lib.fock_loss_grad(coupled, tgt, pt, mask, gstat, lgrad)),
+        ("basis_rows (coupled -> blocks)", lambda: lib.basis_rows(coupled, blocks_out, bptr, pt, pos32, meta_h,
+                                                                 coef_h, D, E, False, True)),
+        ("radius_graph cells", lambda: lib.radius_graph_cells(pos_t, grid, nc, periodic, cell_id)),
+        ("radius_graph count", lambda: lib.radius_graph_pass(pos_t, grid, nc, periodic, tg, order, cstart, cnt,
+                                                              None, None, None)),
+        ("radius_graph fill", lambda: lib.radius_graph_pass(pos_t, grid, nc, periodic, tg, order, cstart, None,
+                                                             gptr, g_src, g_vec)),
     ]
 
 

@@ -58,11 +58,11 @@ class _LossStats(torch.autograd.Function):
     def backward(ctx, g):
         lib = _lib()
         no, eo, nt, et, mask, npt, ept = ctx.saved_tensors
-        g = g.tolist()
+        g = g.float().contiguous()  # stays on the device: no host sync in the backward
         gn = torch.empty_like(no)
         ge = torch.empty_like(eo)
-        lib.fock_loss_grad(no, nt, npt, mask, g[0], g[1], gn)
-        lib.fock_loss_grad(eo, et, ept, mask, g[3], g[4], ge)
+        lib.fock_loss_grad(no, nt, npt, mask, g[0:2], gn)
+        lib.fock_loss_grad(eo, et, ept, mask, g[3:5], ge)
         count_launches(2)
         return gn, ge, None, None, None, None, None
 
