@@ -203,7 +203,7 @@ def suite_calls(edges=43408, device="cuda"):
     from ..data import structures
     from ..data.graph_gpu import grid_for
 
-    st = structures.amorphous_sio2(np.random.default_rng(0), max(200, E // 140))
+    st = structures.amorphous_sio2(np.random.default_rng(0), max(2000, E // 140))
     lo, ext, ncell, periodic = grid_for(st.pos, 8.0, st.cell)
     grid = [float(v) for v in lo] + [float(v) for v in ext] + [8.0]
     nc = [int(v) for v in ncell]
