@@ -190,18 +190,6 @@ void rotate_grad(int64_t L, int64_t MM, at::Tensor G, c10::optional<at::Tensor> 
                                 (int)G.size(2), (int)Rk, (float)scale, stream()));
 }
 
-// Node path of rotate_grad with the destinations' edge ranges (out_ptr [N+1]); G [N, S, C].
-void rotate_grad_nodes(int64_t L, int64_t MM, at::Tensor G, at::Tensor out_ptr, at::Tensor rot,
-                       c10::optional<at::Tensor> DY, c10::optional<at::Tensor> DYf, int64_t Rk, double scale) {
-  chk(G, at::kFloat, "G");
-  chk(out_ptr, at::kLong, "out_ptr");
-  TORCH_CHECK(out_ptr.numel() == G.size(0) + 1, "rotate_grad_nodes: out_ptr has N + 1 entries");
-  const at::cuda::CUDAGuard guard(G.device());
-  check(maloq::edge_rotate_grad_nodes((int)L, (int)MM, G.data_ptr<float>(), ll(out_ptr), rot.data_ptr<float>(),
-                                      DY.has_value() ? bf(*DY) : nullptr, ptr<float>(DYf), (int)G.size(0),
-                                      (int)G.size(2), (int)Rk, (float)scale, stream()));
-}
-
 void gate_fwd(int64_t L, int64_t MM, at::Tensor Y1, at::Tensor H1, int64_t H) {
   chk(Y1, at::kBFloat16, "Y1");
   chk(H1, at::kBFloat16, "H1");
@@ -457,7 +445,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("node_reduce", &node_reduce);
   m.def("halo_push", &halo_push);
   m.def("halo_fetch", &halo_fetch);
-  m.def("rotate_grad_nodes", &rotate_grad_nodes);
   m.def("rms_norm_fwd", &rms_norm_fwd);
   m.def("rms_norm_bwd", &rms_norm_bwd);
   m.def("norm_grid", &norm_grid);

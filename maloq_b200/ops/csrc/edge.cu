@@ -372,9 +372,10 @@ __global__ void __launch_bounds__(256) rotate_back_edge2_kernel(const __nv_bfloa
   for (int j = 0; j < S; ++j) *reinterpret_cast<float2*>(o + (size_t)j * C) = acc[j];
 }
 
-// DY[e, k*C + c] = scale * sum_j rot[e,k,j] G[row, j, c]: node path (row = destination n, its
-// edges out_ptr[n] .. out_ptr[n+1]: G[n] is loaded once per edge lane) or edge path (row = e, or
-// out_ptr[e] when given: the edge-parallel form of the node path).
+// DY[e, k*C + c] = scale * sum_j rot[e,k,j] G[row, j, c], edge-parallel (NODE = false): row = e,
+// or out_ptr[e] when given (the node path: each edge's destination row).  NODE = true walks a
+// destination's edge range instead (G[n] loaded once per lane); it leaves too few CTAs at
+// molecular node counts and is not launched.
 template <int L, int MM, bool NODE>
 __global__ void __launch_bounds__(256) rotate_grad2_kernel(const float* __restrict__ G,
                                                            const long long* __restrict__ out_ptr,
@@ -602,17 +603,6 @@ const char* edge_rotate_grad(int L, int MM, const float* G, const long long* row
   MALOQ_DISPATCH_FRAME((rotate_grad_kernel<FL, FM><<<grid, 128, 0, st>>>(G, rows, rot, DY, DYf, E, C, Rk, scale)))
 }
 
-const char* edge_rotate_grad_nodes(int L, int MM, const float* G, const long long* out_ptr, const float* rot,
-                                   __nv_bfloat16* DY, float* DYf, int N, int C, int Rk, float scale, cudaStream_t st) {
-  MM = clampm(L, MM);
-  if (N == 0) return nullptr;
-  if (C % 2) return "rotate_grad_nodes: even channel count required";
-  dim3 grid(N, (C / 2 + 63) / 64);
-  MALOQ_DISPATCH_FRAME(({
-    constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
-    rotate_grad2_kernel<FL, FM, true><<<grid, 64 * Q_, 0, st>>>(G, out_ptr, rot, DY, DYf, N, C, Rk, scale);
-  }))
-}
 
 const char* edge_gate_fwd(int L, int MM, const __nv_bfloat16* Y1, __nv_bfloat16* H1, int E, int H, cudaStream_t st) {
   MM = clampm(L, MM);

@@ -17,8 +17,6 @@ const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* X
                                    float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
                                    const float* const* peers, const int* halo_owner, const long long* halo_row,
                                    long long n_own, long long n_x_rows, long long n_halo, cudaStream_t st);
-const char* edge_rotate_grad_nodes(int L, int MM, const float* G, const long long* out_ptr, const float* rot,
-                                   __nv_bfloat16* DY, float* DYf, int N, int C, int Rk, float scale, cudaStream_t st);
 const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, const long long* halo_row, float* out,
                             long long n_halo, int SC, cudaStream_t st);
 const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,

@@ -213,7 +213,7 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
 def _rotate_grad(LM, g, graph, node, DY, DYf, Rk, scale):
     """Backward of rotate-back, edge-parallel: node path reads each edge's destination row of
     the gradient (``dst_out``), the edge path its own row.  (Walking each destination's edge
-    range instead - ``rotate_grad_nodes`` - leaves too few CTAs at molecular node counts.)"""
+    range instead leaves too few CTAs at molecular node counts.)"""
     _lib().rotate_grad(*LM, g, graph.dst_out if node else None, graph.rot, DY, DYf, Rk, scale)
 
 
