@@ -1,6 +1,6 @@
 """Headline benchmark: training graphs/s on the drug-like data-parallel config.
 
-Config (BASELINE "Drug-like molecules, data-parallel bf16 on 1/2/4/8 B200"): 30-50 atom
+Config (drug-like molecules, data-parallel bf16 on 1/2/4/8 B200): 30-50 atom
 molecules from {H,C,N,O,F,S,Cl}, def2-SVP-like basis (H 5, 2nd row 14, S/Cl 18 orbitals,
 labels of 324 entries, lmax 4), eSEN backbone lmax=4, mmax=2, 128 channels, 6 layers,
 6 A graph cutoff, 32 molecules per GPU, Fock head with node reductions, rmse+mse loss,
@@ -24,7 +24,7 @@ import sys
 import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-BASELINE_VALUE = None  # BASELINE.json publishes no number for this metric
+BASELINE_VALUE = None  # the reference publishes no number for this metric
 METRIC = "train graphs/s (drug-like DP, device-timed, max over ranks)"
 PARTITIONED = {
     # name: (dataset kind, default atoms, mmax, layers, what)

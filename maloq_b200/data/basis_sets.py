@@ -2,7 +2,7 @@
 
 The def2-SVP tables list the standard def2-SVP shell structure of each element (a
 chemistry fact, identical to the reference's ``fock_utils/basis_sets.py:3-26``).  The
-synthetic sets size the BASELINE benchmark configurations:
+synthetic sets size the benchmark configurations:
 
 * ``split_valence_small``: H 2s1p (5 orbitals), C/N/O 3s2p1d (14);
 * ``def2_svp_like``: H 5, second-row 14, S/Cl 18 orbitals;
