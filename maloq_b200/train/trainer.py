@@ -14,7 +14,6 @@
 
 from __future__ import annotations
 
-import json
 import os
 import time
 
@@ -22,7 +21,6 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from .. import ops
 from ..ops import loss as loss_ops
 from . import checkpoint as ckpt
 

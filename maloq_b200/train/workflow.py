@@ -22,7 +22,6 @@ import random
 import numpy as np
 import torch
 
-from ..core.irreps import Irreps
 from ..data import batch as B
 from ..data import datasets
 from ..models.backbone import eSEN_Backbone

@@ -1,7 +1,6 @@
 """Failure detection on the host (gloo ranks): a rank that raises, a rank that never joins,
 mismatched batch counts, a non-finite loss.  No GPU is faulted, trapped or hung."""
 import datetime
-import os
 
 import pytest
 import torch

@@ -1,7 +1,6 @@
 """Device radius graph (ops/csrc/graph.cu) against the host cell list: same edges, same order."""
 import numpy as np
 import pytest
-import torch
 
 from maloq_b200.data import structures
 from maloq_b200.data.graph import radius_graph

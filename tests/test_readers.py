@@ -1,6 +1,5 @@
 """nablaDFT reader (generated mini database), orbital reordering, label round trip."""
 import numpy as np
-import torch
 
 from maloq_b200.data import readers
 from maloq_b200.data.basis_sets import get_basis
