@@ -98,7 +98,8 @@ class Teacher:
         kw = dict(model_kwargs)
         self.backbone = eSEN_Backbone(labeler.irreps, include_edges=True, **kw).to(device).eval()
         self.head = Fock_Irreps_Head(None, labeler.irreps, lmax=kw["lmax"], sphere_channels=kw["sphere_channels"],
-                                     ls_list=labeler.layout.ls_list, reduce_node=False).to(device).eval()
+                                     ls_list=labeler.layout.ls_list, reduce_node=False,
+                                     open_shell=bool(kw.get("open_shell", False))).to(device).eval()
         torch.random.set_rng_state(g)
         for p in list(self.backbone.parameters()) + list(self.head.parameters()):
             p.requires_grad_(False)
@@ -106,22 +107,24 @@ class Teacher:
 
     @torch.no_grad()
     def hamiltonians(self, samples, chunk=16):
-        """Symmetrised block-sparse Hamiltonians for ``samples``."""
+        """Symmetrised block-sparse Hamiltonians for ``samples`` (open shell: a list of the
+        alpha and beta matrices per sample)."""
         out = []
         for i in range(0, len(samples), chunk):
             part = samples[i:i + chunk]
             b = collate(part, self.labeler.table).to(self.device)
             emb = self.backbone(b)
-            n_out, e_out = self.head(emb, b)
-            n_out, e_out = n_out[0], e_out[0]
+            n_all, e_all = self.head(emb, b)
             no, eo = 0, 0
             for s in part:
-                nl = n_out[no:no + s.num_nodes]
-                el = e_out[eo:eo + s.num_edges]
+                per_spin = []
+                for sp in range(n_all.shape[0]):
+                    nl = n_all[sp, no:no + s.num_nodes]
+                    el = e_all[sp, eo:eo + s.num_edges]
+                    per_spin.append(self.labeler.symmetrize(s, self.labeler.blocks_from_labels(s, nl, el)))
                 no += s.num_nodes
                 eo += s.num_edges
-                bsm = self.labeler.blocks_from_labels(s, nl, el)
-                out.append(self.labeler.symmetrize(s, bsm))
+                out.append(per_spin if len(per_spin) > 1 else per_spin[0])
         return out
 
 
@@ -153,13 +156,18 @@ def attach_scalar_targets(samples, teacher: Teacher, kind, seed=4321, chunk=16):
 
 
 def attach_targets(samples, hamiltonians, labeler: FockLabeler, scale_shift=None):
-    """Fill ``node_y``/``y`` ([1, rows, D] float32, CPU) of every sample."""
+    """Fill ``node_y``/``y`` ([spins, rows, D] float32, CPU) of every sample; a sample's
+    Hamiltonian is one matrix, or a list of spin-channel matrices (open shell)."""
     for s, h in zip(samples, hamiltonians):
-        ny, y = labeler.labels_from_blocks(s, h)
-        if scale_shift is not None:
-            ny = scale_shift.shift(ny, s.z)
-        s.node_y = ny.unsqueeze(0).cpu()
-        s.y = y.unsqueeze(0).cpu()
+        nys, ys = [], []
+        for hs in (h if isinstance(h, list) else [h]):
+            ny, y = labeler.labels_from_blocks(s, hs)
+            if scale_shift is not None:
+                ny = scale_shift.shift(ny, s.z)
+            nys.append(ny.cpu())
+            ys.append(y.cpu())
+        s.node_y = torch.stack(nys)
+        s.y = torch.stack(ys)
     return samples
 
 

@@ -274,3 +274,16 @@ def test_energy_linear_references(tmp_path):
     wf.run()
     coeff = np.load(tmp_path / "lin_ref_coeffs_synthetic_small.npz")["coeff"]
     assert coeff.ndim == 1 and np.isfinite(coeff).all() and wf.energy_refs is not None
+
+
+@pytest.mark.parametrize("extra", [dict(open_shell=True), dict(reduce_edge=True),
+                                   dict(message_type="source-target-message")])
+def test_workflow_variants_train(tmp_path, extra):
+    """Open shell (alpha/beta teacher targets), reduce_edge and the 3-way message all train."""
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=8, batch_size=4, num_epochs=2, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               output_folder=str(tmp_path), device="cpu", log_every=0, **extra)
+    h = training_workflow.TrainingWorkflow(cfg).run()
+    assert len(h["train_node"]) == 2 and np.isfinite(h["train_node"]).all()
