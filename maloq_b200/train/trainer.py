@@ -239,7 +239,18 @@ class SplitTrainer:
                 from ..analysis.embeddings import dump
 
                 dump(os.path.join(output_folder, "embeddings"), k, emb, b)
-            no, eo = self.head(emb, b)
+            out = self.head(emb, b)
+            if isinstance(out, dict):  # energy / force heads
+                if "energies" in out:
+                    err = abs(float(out["energies"][0]) - float(b.energy[0])) if b.energy is not None else float("nan")
+                    rows.append((k, err, float("nan"), s.num_nodes))
+                else:
+                    f = out["forces"].double().cpu().numpy()
+                    err = float(np.abs(f - b.forces.double().cpu().numpy()).mean()) if b.forces is not None \
+                        else float("nan")
+                    rows.append((k, float("nan"), err, s.num_nodes))
+                continue
+            no, eo = out
             no, eo = no[0], eo[0]
             if scale_shift is not None:
                 no = scale_shift.unshift(no, s.z)
@@ -261,6 +272,12 @@ class SplitTrainer:
             rows.append((k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), err("gap"),
                          err("band_energy"), s.num_nodes))
         os.makedirs(output_folder, exist_ok=True)
+        if rows and len(rows[0]) == 4:
+            with open(os.path.join(output_folder, f"model_energy_eval_{rank}.txt"), "w") as f:
+                f.write("Index\tEnergy_Error\tForce_MAE\tNum_Atoms\n")
+                for r in rows:
+                    f.write("\t".join(str(x) for x in r) + "\n")
+            return rows
         with open(os.path.join(output_folder, f"model_fock_eval_{rank}.txt"), "w") as f:
             f.write("Index\tTotal_MAE\tEigenvalue_MAE\tGap_Error\tBand_Energy_Error\tNum_Atoms\n")
             for r in rows:

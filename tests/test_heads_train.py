@@ -287,3 +287,18 @@ def test_workflow_variants_train(tmp_path, extra):
                output_folder=str(tmp_path), device="cpu", log_every=0, **extra)
     h = training_workflow.TrainingWorkflow(cfg).run()
     assert len(h["train_node"]) == 2 and np.isfinite(h["train_node"]).all()
+
+
+@pytest.mark.parametrize("target", ["energies", "forces"])
+def test_workflow_eval_energy_and_force_heads(tmp_path, target):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=8, batch_size=4, num_epochs=1, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               loss_target=target, output_folder=str(tmp_path), device="cpu", log_every=0)
+    training_workflow.TrainingWorkflow(cfg).run()
+    rows = training_workflow.TrainingWorkflow(dict(cfg, train_or_eval="eval", restart_backbone=True,
+                                                   restart_head=True)).run()
+    col = 1 if target == "energies" else 2
+    assert all(np.isfinite(r[col]) for r in rows)
+    assert (tmp_path / "model_energy_eval_0.txt").exists()
