@@ -31,8 +31,38 @@ class _Exchange(torch.autograd.Function):
         return ctx.plan.return_grads(g_halo), None
 
 
+class HaloPlanError(RuntimeError):
+    """The ranks' halo plans disagree (a rank expects rows that its owner will not send)."""
+
+
+def validate_halo_plan(domain, group=None):
+    """Check on the host, with one all-gather of the plan sizes, that every rank's receive
+    count from each owner equals the number of rows that owner sends it, and that halo rows
+    point inside their owner's rows.  Raises :class:`HaloPlanError` on every rank otherwise
+    (a corrupted or stale plan would make the exchange read or write the wrong rows)."""
+    world = domain.world
+    if world == 1:
+        return
+    mine = {"recv": [int(c) for c in domain.recv_counts], "send": [int(len(s)) for s in domain.send],
+            "n_own": int(domain.n_own), "max_row": {int(p): int(domain.halo_row[domain.halo_owner == p].max())
+                                                    for p in set(domain.halo_owner.tolist())}}
+    allp = [None] * world
+    dist.all_gather_object(allp, mine, group=group)
+    bad = []
+    for q in range(world):
+        for p in range(world):
+            if allp[q]["recv"][p] != allp[p]["send"][q]:
+                bad.append(f"rank {q} expects {allp[q]['recv'][p]} rows from rank {p}, which sends "
+                           f"{allp[p]['send'][q]}")
+        for p, mr in allp[q]["max_row"].items():
+            if mr >= allp[p]["n_own"]:
+                bad.append(f"rank {q} reads row {mr} of rank {p}, which owns {allp[p]['n_own']} rows")
+    if bad:
+        raise HaloPlanError("inconsistent halo plans: " + "; ".join(bad[:4]))
+
+
 class HaloPlan:
-    def __init__(self, domain, device, group=None, transport="collective"):
+    def __init__(self, domain, device, group=None, transport="collective", validate=True):
         self.domain = domain
         self.device = torch.device(device)
         self.group = group
@@ -45,6 +75,8 @@ class HaloPlan:
         cat = np.concatenate(domain.send) if sum(self.send_counts) else np.zeros(0, dtype=np.int64)
         self.send_idx = torch.as_tensor(cat, dtype=torch.long, device=self.device)
         self.peer = None
+        if validate and dist.is_initialized():
+            validate_halo_plan(domain, group)
 
     # ------------------------------------------------------------------ collective transport
     def fetch(self, x):

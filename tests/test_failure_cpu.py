@@ -1,5 +1,6 @@
-"""Failure detection on the host (gloo ranks): a rank that raises, a rank that never joins,
-mismatched batch counts, a non-finite loss.  No GPU is faulted, trapped or hung."""
+"""Failure detection on the host (gloo ranks): a rank that raises, a rank that never joins, a
+delayed rank, a corrupted halo plan, mismatched batch counts, a non-finite loss.  No GPU is
+faulted, trapped or hung."""
 import datetime
 
 import pytest
@@ -78,3 +79,46 @@ def test_nan_guard_stops_step():
     with pytest.raises(FloatingPointError):
         tr.train_step(b, L.mse_padded_loss, opt)
     assert all(torch.equal(a, p) for a, p in zip(before, bb.parameters()))
+
+
+def _plan_worker(rank, world, corrupt):
+    from maloq_b200.parallel import partition as P
+    from maloq_b200.parallel.halo import HaloPlan, HaloPlanError
+    from tests.test_partition_cpu import _toy_graph
+
+    g = _toy_graph()
+    part = P.partition("slab", g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+    dom = P.decompose(part, g.src, g.dst, world)[rank]
+    if corrupt and rank == 1:  # a stale plan: one row fewer sent to rank 0
+        dom.send[0] = dom.send[0][:-1]
+    try:
+        HaloPlan(dom, "cpu")
+    except HaloPlanError as e:
+        return str(e)
+    return "ok"
+
+
+@pytest.mark.parametrize("corrupt", [False, True])
+def test_corrupted_halo_plan_is_detected_on_every_rank(corrupt):
+    out = _dist_util.run(_plan_worker, world=2, args=(corrupt,))
+    if corrupt:
+        assert all("inconsistent halo plans" in v and "rank 0 expects" in v for v in out.values())
+    else:
+        assert all(v == "ok" for v in out.values())
+
+
+def _slow_worker(rank, world):
+    import time
+
+    import torch.distributed as dist
+
+    if rank == 1:
+        time.sleep(3.0)  # a straggler: late, but within the process-group timeout
+    t = torch.ones(4) * (rank + 1)
+    dist.all_reduce(t)
+    return float(t[0])
+
+
+def test_delayed_rank_completes_within_timeout():
+    out = _dist_util.run(_slow_worker, world=2)
+    assert all(v == 3.0 for v in out.values())
