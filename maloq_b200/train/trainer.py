@@ -220,13 +220,25 @@ class SplitTrainer:
     # ------------------------------------------------------------------ eval / infer
     @torch.no_grad()
     def evaluate(self, loss_fxn, device, loader, labeler, output_folder="outputs", samples=None, scale_shift=None,
-                 dump_embeddings=False, **unused):
+                 dump_embeddings=False, compute_total_energy=False, basis_name=None, xc="b3lyp", **unused):
         """Per structure: Hamiltonian MAE, orbital-energy MAE (generalised with the overlap
         when the sample carries one, canonical orthogonalisation), HOMO-LUMO gap and band
         energy errors (closed shell, all-electron count), written to
         ``model_fock_eval_{rank}.txt`` (reference ``splittrainer.py:378-822``)."""
         from ..data.batch import collate
         from ..eval import electronic
+
+        mol_of = None
+        if compute_total_energy:
+            try:
+                from pyscf import gto
+
+                def mol_of(s):
+                    return gto.M(atom=[(int(z), tuple(p)) for z, p in zip(s.z, s.pos)], basis=basis_name or "def2-svp",
+                                 charge=int(getattr(s, "charge", 0)), unit="Angstrom")
+            except ImportError:
+                print("compute_total_energy: PySCF is not installed; Total_Energy_Error is reported as nan",
+                      flush=True)
 
         self.backbone.eval()
         self.head.eval()
@@ -269,8 +281,14 @@ class SplitTrainer:
             def err(key):
                 return float("nan") if sp_[key] is None else abs(sp_[key] - st_[key])
 
-            rows.append((k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), err("gap"),
-                         err("band_energy"), s.num_nodes))
+            row = [k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), err("gap"), err("band_energy")]
+            if compute_total_energy:
+                te = float("nan")
+                if mol_of is not None:
+                    mol = mol_of(s)
+                    te = abs(electronic.total_energy(mol, Hp, S, xc) - electronic.total_energy(mol, Ht, S, xc))
+                row.append(te)
+            rows.append(tuple(row + [s.num_nodes]))
         os.makedirs(output_folder, exist_ok=True)
         if rows and len(rows[0]) == 4:
             with open(os.path.join(output_folder, f"model_energy_eval_{rank}.txt"), "w") as f:
@@ -279,7 +297,8 @@ class SplitTrainer:
                     f.write("\t".join(str(x) for x in r) + "\n")
             return rows
         with open(os.path.join(output_folder, f"model_fock_eval_{rank}.txt"), "w") as f:
-            f.write("Index\tTotal_MAE\tEigenvalue_MAE\tGap_Error\tBand_Energy_Error\tNum_Atoms\n")
+            f.write("Index\tTotal_MAE\tEigenvalue_MAE\tGap_Error\tBand_Energy_Error\t"
+                    + ("Total_Energy_Error\t" if compute_total_energy else "") + "Num_Atoms\n")
             for r in rows:
                 f.write("\t".join(str(x) for x in r) + "\n")
         return rows

@@ -352,7 +352,9 @@ class TrainingWorkflow:
                 return trainer.evaluate(c["test_loss_fxn"], self.device, val, labeler,
                                         output_folder=c["output_folder"], samples=self.val_samples,
                                         scale_shift=getattr(self, "scale_shift", None),
-                                        dump_embeddings=c.get("dump_embeddings", False))
+                                        dump_embeddings=c.get("dump_embeddings", False),
+                                        compute_total_energy=c.get("compute_total_energy", False),
+                                        basis_name=c.get("pyscf_basis"), xc=c.get("functional", "b3lyp"))
             if c["distribute_graphs"]:
                 b = val[0]
                 s = self.partition_sample

@@ -83,3 +83,16 @@ def test_invariant_features_are_rotation_invariant():
     D = torch.block_diag(*[torch.tensor(sph.wigner_D_from_matrix(l, R)) for l in range(5)]).numpy()
     xr = np.einsum("ij,njc->nic", D, x)
     assert np.allclose(invariant_features(x), invariant_features(xr), atol=1e-10)
+
+
+def test_eval_total_energy_column_without_pyscf(tmp_path):
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=6, batch_size=3, num_epochs=1, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               output_folder=str(tmp_path), device="cpu", log_every=0)
+    training_workflow.TrainingWorkflow(cfg).run()
+    rows = training_workflow.TrainingWorkflow(dict(cfg, train_or_eval="eval", restart_backbone=True, restart_head=True,
+                                                   compute_total_energy=True)).run()
+    header = (tmp_path / "model_fock_eval_0.txt").read_text().splitlines()[0].split("\t")
+    assert "Total_Energy_Error" in header and len(rows[0]) == len(header)
