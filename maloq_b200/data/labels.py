@@ -93,6 +93,14 @@ class BlockSparseMatrix:
         n = self.n_orb
         return sp.coo_matrix((np.concatenate(vv), (np.concatenate(rr), np.concatenate(cc))), shape=(n, n)).tocsr()
 
+    def save_npz(self, path):
+        """The matrix as a scipy CSR ``.npz`` (``scipy.sparse.load_npz`` reads it back; the
+        reference's inference output format)."""
+        import scipy.sparse as sp
+
+        sp.save_npz(path, self.to_scipy_csr())
+        return path
+
     @staticmethod
     def from_dense(M, rows, cols, orb_ptr):
         sizes = (orb_ptr[rows + 1] - orb_ptr[rows]) * (orb_ptr[cols + 1] - orb_ptr[cols])

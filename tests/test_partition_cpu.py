@@ -131,6 +131,10 @@ def test_partitioned_workflow_train_and_infer(tmp_path):
     dense = H.to_dense()
     assert dense.shape[0] == 150 * 13
     assert np.allclose(dense, dense.T, atol=1e-5)
+    import scipy.sparse as sp
+
+    path = H.save_npz(str(tmp_path / "H.npz"))
+    assert np.allclose(sp.load_npz(path).toarray(), dense)
 
 
 def _local_domain_worker(rank, world):
