@@ -205,3 +205,82 @@ def test_partitioned_workflow_on_a_cp2k_structure(tmp_path):
     readers.write_cp2k_csr(d / "hamiltonian.csr", (A + A.T).tocsr())
     out = _dist_util.run(_cp2k_worker, world=2, args=(str(tmp_path / "data"), str(tmp_path / "out")))
     assert len(out[0]["train_node"]) == 2 and np.isfinite(out[0]["train_node"]).all()
+
+
+def _stream_infer_worker(rank, world):
+    import torch
+
+    from maloq_b200.data import datasets, structures
+    from maloq_b200.data.graph import radius_graph
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.parallel import partition as P
+    from maloq_b200.parallel.halo import local_batch
+    from maloq_b200.parallel.infer import hamiltonian_shard
+
+    rng = np.random.default_rng(3)
+    st = structures.si_slab_with_oxide(rng, 700)
+    lab = datasets.labeler_for("slab")
+    part = P.partition("slab", len(st.z), world, pos=st.pos, cell=st.cell)
+    owned = np.flatnonzero(part == rank)
+    src, dst, vec = radius_graph(st.pos, 6.0, st.cell)
+    keep = np.isin(dst, owned)  # the edges into my atoms, (owned row, src) order
+    row = np.full(len(st.z), -1)
+    row[owned] = np.arange(len(owned))
+    s, d, v = src[keep], row[dst[keep]], vec[keep]
+    o = np.lexsort((s, d))
+    s, d, v = torch.as_tensor(s[o]), torch.as_tensor(d[o]), torch.as_tensor(v[o])
+    ptr = torch.zeros(len(owned) + 1, dtype=torch.long)
+    ptr[1:] = torch.cumsum(torch.bincount(d, minlength=len(owned)), 0)
+    dom, src_local = P.local_domain(part, rank, world, s)
+    b = local_batch(st.z, st.pos, dom, src_local, d, v, ptr, lab.table, device="cpu", transport="collective")
+    kw = dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2, cutoff=6.0, edge_channels=8, num_layers=2,
+              num_distance_basis=8, edge_stream_dtype=torch.float32)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, edge_chunk=300, **kw).eval()
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list,
+                          reduce_node=True, reduce_node_intra=True).eval()
+    with torch.no_grad():
+        data, bptr = hamiltonian_shard(hd, bb(b), b, lab)
+    gsrc = np.concatenate([dom.owned, dom.halo])[src_local.numpy()]
+    return owned, gsrc, dom.owned[d.numpy()], data.numpy(), bptr.numpy()
+
+
+def test_streamed_partitioned_inference_matches_single_process():
+    """Per-rank edges -> local_domain -> local_batch -> chunked streaming inference (collective
+    halo) -> Hamiltonian shard: every block equals the unpartitioned model's block."""
+    import torch
+
+    from maloq_b200.data import datasets, structures
+    from maloq_b200.data.batch import collate, make_sample
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.parallel.infer import hamiltonian_shard
+
+    out = _dist_util.run(_stream_infer_worker, world=2)
+    rng = np.random.default_rng(3)
+    st = structures.si_slab_with_oxide(rng, 700)
+    lab = datasets.labeler_for("slab")
+    smp = make_sample(st, 6.0)
+    b = collate([smp], lab.table)
+    kw = dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2, cutoff=6.0, edge_channels=8, num_layers=2,
+              num_distance_basis=8)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, **kw).eval()
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=8, ls_list=lab.layout.ls_list,
+                          reduce_node=True, reduce_node_intra=True).eval()
+    with torch.no_grad():
+        ref, rptr = hamiltonian_shard(hd, bb(b), b, lab)
+    ref, rptr = ref.numpy(), rptr.numpy()
+    E = len(smp.src)
+    key = {(int(a), int(c)): i for i, (a, c) in enumerate(zip(smp.src, smp.dst))}
+    n_checked = 0
+    for owned, gsrc, gdst, data, bptr in out.values():
+        for j, (a, c) in enumerate(zip(gsrc, gdst)):
+            i = key[(int(a), int(c))]
+            assert np.allclose(data[bptr[j]:bptr[j + 1]], ref[rptr[i]:rptr[i + 1]], atol=2e-4), (a, c)
+            n_checked += 1
+        ne = len(gsrc)
+        for j, a in enumerate(owned):  # on-site blocks follow the edge blocks
+            assert np.allclose(data[bptr[ne + j]:bptr[ne + j + 1]], ref[rptr[E + a]:rptr[E + a + 1]], atol=2e-4)
+    assert n_checked == E
