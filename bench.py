@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--atoms", type=int, default=None, help="atoms of the partitioned structure")
     ap.add_argument("--edge-chunk", type=int, default=131072,
                     help="partitioned configs: edges per chunk of the chunked (recomputed) block execution")
-    ap.add_argument("--config", default="druglike", choices=list(CONFIGS) + list(PARTITIONED),
+    ap.add_argument("--config", default="druglike", choices=list(CONFIGS) + list(PARTITIONED) + ["cpu"],
                     help="druglike (headline) or large (10-150 atoms, lmax 6, 8 layers, <=4096 atoms/GPU)")
     return ap.parse_args()
 
@@ -351,8 +351,69 @@ def run_partitioned(args, device, world, rank):
         pdist.cleanup_process_group()
 
 
+def run_cpu_plumbing(args):
+    """The CPU configuration (no GPU): 8 random molecules of 3-9 atoms from {H,C,N,O}, 5 A graph,
+    split-valence basis, lmax 4, mmax 2, 64 channels, 4 layers, 32 Gaussians, MSE loss, 100 Adam
+    steps, fixed seeds.  Reports the wall time of the 100 steps, the loss drop and the fp32
+    equivariance error of the node and edge outputs under a random rotation (max |D y(x) -
+    y(R x)| / max |y|)."""
+    import numpy as np
+    import torch
+
+    from maloq_b200.core import sph
+    from maloq_b200.data import datasets, structures
+    from maloq_b200.data.batch import collate, make_sample
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    torch.manual_seed(0)
+    steps = 100
+    kw = dict(sphere_channels=64, hidden_channels=64, lmax=4, mmax=2, cutoff=5.0, edge_channels=64, num_layers=4,
+              num_distance_basis=32)
+    labeler = datasets.labeler_for("small", "cpu")
+    samples, _ = datasets.build_dataset("small", 8, kw, seed=0, device="cpu", labeler=labeler)
+    batch = collate(samples, labeler.table)
+    torch.manual_seed(1)
+    bb = eSEN_Backbone(labeler.irreps, include_edges=True, **kw)
+    hd = Fock_Irreps_Head(None, labeler.irreps, lmax=4, sphere_channels=64, ls_list=labeler.layout.ls_list,
+                          reduce_node=True, reduce_node_intra=True)
+    opt = torch.optim.Adam(list(bb.parameters()) + list(hd.parameters()), lr=1e-3)
+    tr = SplitTrainer(bb, hd, labeler.irreps, mask_table=torch.as_tensor(labeler.table.mask))
+    t0 = time.time()
+    losses = [float(tr.train_step(batch, L.mse_padded_loss, opt)[2]) for _ in range(steps)]
+    wall = time.time() - t0
+    # equivariance: rotate the input structures (x, y, z); the model frame is (y, z, x)
+    rng = np.random.default_rng(9)
+    q = rng.normal(size=4)
+    q /= np.linalg.norm(q)
+    a, b_, c, d = q
+    R = np.array([[a * a + b_ * b_ - c * c - d * d, 2 * (b_ * c - a * d), 2 * (b_ * d + a * c)],
+                  [2 * (b_ * c + a * d), a * a - b_ * b_ + c * c - d * d, 2 * (c * d - a * b_)],
+                  [2 * (b_ * d - a * c), 2 * (c * d + a * b_), a * a - b_ * b_ - c * c + d * d]])
+    P = np.array([[0.0, 1.0, 0.0], [0.0, 0.0, 1.0], [1.0, 0.0, 0.0]])
+    rot = [make_sample(structures.Structure(s.z, s.pos @ R.T), 5.0) for s in samples]
+    b1 = collate(rot, labeler.table)
+    with torch.no_grad():
+        n0, e0 = hd(bb(batch), batch)
+        n1, e1 = hd(bb(b1), b1)
+    Dl = torch.block_diag(*[torch.tensor(sph.wigner_D_from_matrix(it.l, P @ R @ P.T), dtype=torch.float32)
+                            for it in labeler.irreps])
+    scale = max(n0.abs().max().item(), e0.abs().max().item(), 1e-12)
+    eq = max((n0[0] @ Dl.T - n1[0]).abs().max().item(), (e0[0] @ Dl.T - e1[0]).abs().max().item()) / scale
+    print(json.dumps({
+        "metric": "CPU plumbing: wall time of 100 Adam steps", "value": round(wall, 3), "unit": "s", "n_gpus": 0,
+        "steps": steps, "warmup": 0, "higher_is_better": False, "dtype": "fp32", "data": "synthetic",
+        "config": {"model": "eSEN lmax=4 mmax=2 C=64 layers=4, 32 Gaussians + Fock head", "global_batch": 8,
+                   "molecules": "3-9 atoms {H,C,N,O}", "loss": "mse"},
+        "loss_first": losses[0], "loss_last": losses[-1], "equivariance_rel_err_fp32": eq}), flush=True)
+
+
 def main():
     args = parse()
+    if args.config == "cpu":
+        return run_cpu_plumbing(args)
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps(reference_arm(args)))
