@@ -39,3 +39,9 @@ def test_nabladft_roundtrip(tmp_path):
     dense = bsm.to_dense()
     ref = readers.reorder_orbitals(mols[0][4], mols[0][0], basis, "psi4")
     assert np.allclose(dense, ref, atol=1e-4)
+    # energy and forces travel with the sample and collate into batch.energy / batch.forces
+    from maloq_b200.data.batch import collate
+
+    assert abs(s.energy - float(np.float32(mols[0][2]))) < 1e-6 and s.forces.shape == (s.num_nodes, 3)
+    b = collate(samples, lab.table)
+    assert b.energy.shape == (3,) and b.forces.shape == (sum(x.num_nodes for x in samples), 3)
