@@ -30,13 +30,15 @@ BOHR_TO_ANGSTROM = 0.52917721092
 # code -> shell letter -> (index permutation into e3nn order, signs)
 CONVENTIONS = {
     "psi4": {"s": ([0], [1]), "p": ([2, 0, 1], [1, 1, 1]), "d": ([4, 2, 0, 1, 3], [1, 1, 1, 1, 1])},
-    "orca": {"s": ([0], [1]), "p": ([2, 0, 1], [1, 1, 1]), "d": ([4, 2, 0, 1, 3], [1, 1, 1, 1, 1])},
+    "orca": {"s": ([0], [1]), "p": ([2, 0, 1], [1, 1, 1]), "d": ([4, 2, 0, 1, 3], [1, 1, 1, 1, 1]),
+             "f": ([6, 4, 2, 0, 1, 3, 5], [-1, 1, 1, 1, 1, 1, -1]),
+             "g": ([8, 6, 4, 2, 0, 1, 3, 5, 7], [-1, -1, 1, 1, 1, 1, 1, -1, -1])},
     "pyscf": {"s": ([0], [1]), "p": ([1, 2, 0], [1, 1, 1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, 1, 1])},
     "aims": {"s": ([0], [1]), "p": ([0, 1, 2], [1, 1, -1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, -1, 1])},
     "e3nn": {"s": ([0], [1]), "p": ([0, 1, 2], [1, 1, 1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, 1, 1]),
              "f": ([0, 1, 2, 3, 4, 5, 6], [1] * 7)},
 }
-_L_LETTER = {0: "s", 1: "p", 2: "d", 3: "f"}
+_L_LETTER = {0: "s", 1: "p", 2: "d", 3: "f", 4: "g"}
 
 
 def reorder_indices(z, basis, convention="psi4"):
@@ -56,6 +58,14 @@ def reorder_indices(z, basis, convention="psi4"):
 def reorder_orbitals(H, z, basis, convention="psi4"):
     idx, sgn = reorder_indices(z, basis, convention)
     return H[..., idx, :][..., :, idx] * sgn[:, None] * sgn[None, :]
+
+
+def reorder_orbitals_inverse(H, z, basis, convention="psi4"):
+    """Inverse of :func:`reorder_orbitals`: an e3nn-ordered matrix back to the code's order."""
+    idx, sgn = reorder_indices(z, basis, convention)
+    out = np.empty_like(H)
+    out[..., idx[:, None], idx[None, :]] = H * sgn[:, None] * sgn[None, :]
+    return out
 
 
 class NablaDFTDatabase:
@@ -111,30 +121,124 @@ def write_nabladft(path, molecules):
 
 def load_nabladft(path, config, device="cpu", convention="psi4", indices=None):
     """Samples with coupled-basis targets from a nablaDFT database (def2-SVP basis)."""
+    db = NablaDFTDatabase(path)
+    n = len(db) if indices is None else None
+    idx = list(range(min(n, config.get("num_structures", n)))) if indices is None else list(indices)
+
+    def mols():
+        for i in idx:
+            Z, R, E, F, H, S, C = db[i]
+            yield {"z": Z, "pos": R * BOHR_TO_ANGSTROM, "H": H.astype(np.float64), "S": S, "energy": float(E[0]),
+                   "forces": F.astype(np.float64)}
+
+    return molecules_to_samples(mols(), "def2_svp_nabla", config, device, convention=convention)
+
+
+def load_qm7(path, config, device="cpu", indices=None):
+    """The QM7 Hamiltonian ASE database (schnetpack rows: ``hamiltonian``, ``overlap``,
+    ``energy``, ``forces`` in ORCA orbital order, def2-SVP; reference
+    ``dataset_utils/get_loader.py:48-79``)."""
+    from .asedb import ASEAtomsData
+
+    db = ASEAtomsData(path)
+    idx = list(range(min(len(db), config.get("num_structures") or len(db)))) if indices is None else list(indices)
+
+    def mols():
+        for i in idx:
+            r = db[i]
+            yield {"z": r["_atomic_numbers"], "pos": r["_positions"], "H": r["hamiltonian"],
+                   "S": r.get("overlap"), "energy": r.get("energy"), "forces": r.get("forces")}
+
+    return molecules_to_samples(mols(), "def2_svp_qm7", config, device, convention="orca")
+
+
+def load_ase_entries(entries, config, device="cpu", basis="def2_tzvpd"):
+    """Molecules of ASE databases given as ``{"db_file", "start_idx", "end_idx"}`` segments
+    (one rank's share from :func:`maloq_b200.data.asedb.distribute_data`, or a whole file);
+    Fock matrices in ``data['fock_matrix']`` are already in e3nn order."""
+    from .asedb import ASEDataset
+
+    open_shell = bool(config.get("open_shell", False))
+
+    def mols():
+        for e in entries:
+            ds = ASEDataset(e["db_file"], open_shell=open_shell, start_idx=e["start_idx"], end_idx=e["end_idx"])
+            for i in range(len(ds)):
+                r = ds[i]
+                yield {"z": r["atomic_numbers"], "pos": r["pos"], "H": r["fock_matrix"], "energy": r["energies"],
+                       "charge": r["charge"], "spin": r["spin_multiplicity"]}
+
+    return molecules_to_samples(mols(), _basis_for(basis), config, device, open_shell=open_shell)
+
+
+def load_omol_csh(path, config, device="cpu", indices=None, opener=None):
+    """OMol-CSH-58k HDF5 molecules (def2-TZVPD, order-corrected Fock matrices)."""
+    from .omol import OMolCSH58kDatabase
+
+    db = OMolCSH58kDatabase(path, indices=indices, opener=opener)
+
+    def mols():
+        for i in range(len(db)):
+            r = db[i]
+            yield {"z": r["z"], "pos": r["pos"], "H": r["fock"], "charge": r["charge"], "spin": r["spin"] or 1}
+
+    return molecules_to_samples(mols(), _basis_for("def2_tzvpd"), config, device,
+                                open_shell=bool(config.get("open_shell", False)))
+
+
+def _basis_for(name):
+    if name == "def2_tzvpd":
+        from .omol import def2_tzvpd_by_z
+
+        return def2_tzvpd_by_z()
+    return name
+
+
+def molecules_to_samples(mols, basis, config, device="cpu", convention=None, open_shell=False):
+    """Graph samples with coupled-basis Fock targets from molecule dicts with ``z``, ``pos``
+    (Angstrom), ``H`` ([n, n], or [2, n, n] alpha/beta) and optionally ``S``, ``energy``,
+    ``forces``, ``charge``, ``spin``.  ``convention`` names the code whose orbital order ``H``
+    is in (None: already e3nn order).  Closed-shell training keeps the first spin of an
+    open-shell matrix; open-shell training repeats a closed-shell matrix for both spins."""
+    import torch
+
     from .basis_sets import get_basis
     from .batch import make_sample
     from .labels import BlockSparseMatrix, orbital_offsets
     from .structures import Structure
     from .targets import FockLabeler
 
-    basis = get_basis("def2_svp_nabla")
+    basis = get_basis(basis)
     labeler = FockLabeler(basis, device=device)
-    db = NablaDFTDatabase(path)
-    n = len(db) if indices is None else None
-    idx = list(range(min(n, config.get("num_structures", n)))) if indices is None else list(indices)
     cutoff = 2 * config.get("rcut_orbitals", 3.0)
     samples = []
-    for i in idx:
-        Z, R, E, F, H, S, C = db[i]
-        s = make_sample(Structure(Z, R * BOHR_TO_ANGSTROM), cutoff)
-        Hs = reorder_orbitals(H.astype(np.float64), Z, basis, convention)
+    for m in mols:
+        Z = np.asarray(m["z"], dtype=np.int64)
+        s = make_sample(Structure(Z, np.asarray(m["pos"], dtype=np.float64)), cutoff)
+        H = np.asarray(m["H"], dtype=np.float64)
+        Hs = H[None] if H.ndim == 2 else H
+        if open_shell and Hs.shape[0] == 1:
+            Hs = np.concatenate([Hs, Hs])
+        elif not open_shell:
+            Hs = Hs[:1]
         rows, cols = labeler.pairs(s)
-        bsm = BlockSparseMatrix.from_dense(Hs, rows, cols, orbital_offsets(Z, labeler.table))
-        ny, y = labeler.labels_from_blocks(s, bsm)
-        s.node_y, s.y = ny.unsqueeze(0).cpu(), y.unsqueeze(0).cpu()
-        s.overlap = S
-        s.energy = float(E[0])  # energy and forces as stored in the database
-        s.forces = F.astype(np.float64)
+        offs = orbital_offsets(Z, labeler.table)
+        nys, ys = [], []
+        for Hk in Hs:
+            if convention is not None:
+                Hk = reorder_orbitals(Hk, Z, basis, convention)
+            bsm = BlockSparseMatrix.from_dense(Hk, rows, cols, offs)
+            ny, y = labeler.labels_from_blocks(s, bsm)
+            nys.append(ny)
+            ys.append(y)
+        s.node_y, s.y = torch.stack(nys).cpu(), torch.stack(ys).cpu()
+        s.overlap = m.get("S")
+        if m.get("energy") is not None:
+            s.energy = float(np.asarray(m["energy"]).reshape(-1)[0])
+        if m.get("forces") is not None:
+            s.forces = np.asarray(m["forces"], dtype=np.float64)
+        s.charge = int(m.get("charge", 0))
+        s.spin = int(m.get("spin", 1)) or 1
         samples.append(s)
     return samples, labeler
 

@@ -246,6 +246,34 @@ class TrainingWorkflow:
             samples, labeler = load_nabladft(c["dbpath"], c, self.device)
         elif name == "cp2k":
             samples, labeler = self._load_cp2k_folder(c)
+        elif name == "QM7":
+            from ..data.readers import load_qm7
+
+            samples, labeler = load_qm7(c["dbpath"], c, self.device)
+        elif name == "omol_csh_58k":
+            from ..data.readers import load_omol_csh
+
+            n_tr, n_va = c["num_train"], c["num_val"]
+            if not n_tr:
+                raise ValueError("omol_csh_58k needs num_train (and num_val) to pick rows of the manifest")
+            tr = pdist.split_indices(n_tr, self.rank, self.world_size, drop_remainder=False)
+            va = [n_tr + i for i in pdist.split_indices(n_va, self.rank, self.world_size, drop_remainder=False)]
+            local, labeler = load_omol_csh(c["dbpath"], c, self.device, indices=list(tr) + va)
+            return self._finish_data(local[:len(tr)], local[len(tr):], local, labeler, name, rank_local=True)
+        elif os.path.isdir(str(c.get("dbpath", ""))) or str(c.get("dbpath", "")).endswith(".db"):
+            # ASE databases (e.g. OMol folders of .db files): each rank reads only its segments
+            from ..data.asedb import distribute_data
+            from ..data.readers import load_ase_entries
+
+            src = c["dbpath"]
+            if os.path.isdir(str(src)):
+                tr_e, va_e = distribute_data(src, self.world_size, self.rank, c["num_train"], c["num_val"])
+                train, labeler = load_ase_entries(tr_e, c, self.device, basis=c.get("basis_name", "def2_tzvpd"))
+                val = load_ase_entries(va_e, c, self.device, basis=c.get("basis_name", "def2_tzvpd"))[0] \
+                    if va_e else []
+                return self._finish_data(train, val, train + val, labeler, name, rank_local=True)
+            samples, labeler = load_ase_entries([{"db_file": src, "start_idx": 0, "end_idx": None}], c,
+                                                self.device, basis=c.get("basis_name", "def2_tzvpd"))
         else:
             raise ValueError(f"Unknown dataset name: {name}")
         n_val = c["num_val"] or max(1, len(samples) // 8)
@@ -256,10 +284,16 @@ class TrainingWorkflow:
 
             val, _ = load_nabladft(c["dbpath_val"], c, self.device)
             samples = train + val
+        return self._finish_data(train, val, samples, labeler, name)
+
+    def _finish_data(self, train, val, samples, labeler, name, rank_local=False):
+        """Scale/shift, the data-parallel split (unless each rank read only its own rows) and
+        batching."""
+        c = self.config
         self.scale_shift, self.energy_refs = None, None
         if c.get("scale_and_shift"):
             self._apply_scale_shift(train, samples, labeler, name)
-        if self.world_size > 1 and not c["distribute_graphs"]:
+        if self.world_size > 1 and not c["distribute_graphs"] and not rank_local:
             train = [train[i] for i in pdist.split_indices(len(train), self.rank, self.world_size)]
             val = [val[i] for i in pdist.split_indices(len(val), self.rank, self.world_size, drop_remainder=False)] or val[:1]
         bs = c["batch_size"]
