@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--atoms", type=int, default=None, help="atoms of the partitioned structure")
     ap.add_argument("--edge-chunk", type=int, default=131072,
                     help="partitioned configs: edges per chunk of the chunked (recomputed) block execution")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="instead of the bench line: per-kernel-class device time of the training step "
+                         "(torch profiler / CUPTI over --steps steps; shares, not a bench number)")
     ap.add_argument("--config", default="druglike", choices=list(CONFIGS) + list(PARTITIONED) + ["cpu"],
                     help="druglike (headline) or large (10-150 atoms, lmax 6, 8 layers, <=4096 atoms/GPU)")
     return ap.parse_args()
@@ -62,18 +65,19 @@ def labeler_name(kind):
 
 
 def reference_arm(args):
-    """Run the unmodified reference through its public API, if it imports."""
-    ref = os.path.join(HERE, "baseline", "_ref")
-    if not os.path.isdir(ref):
-        return {"impl": "reference", "unavailable": "baseline/_ref not installed"}
-    code = ("import sys; sys.path.insert(0, %r); import maloq.helm.esen_osh, maloq.train_utils.training_workflow" % ref)
-    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd="/tmp")
-    if r.returncode != 0:
-        last = (r.stderr.strip().splitlines() or ["import failed"])[-1]
-        return {"impl": "reference",
-                "unavailable": f"reference package cannot import offline (its dependencies e3nn, cupy, mpi4py, "
-                               f"fairchem, torch_geometric, ase are not installable here): {last}"}
-    return {"impl": "reference", "unavailable": "reference imports but its data pipeline needs cupy/mpi4py at run time"}
+    """Run the unmodified reference through its public modules (``bench_reference.py``, which
+    imports nothing from this framework).  Its JSON line (or ``unavailable`` line naming the
+    missing modules) is printed as is."""
+    env = dict(os.environ, BENCH_STEPS=str(args.steps), BENCH_WARMUP=str(args.warmup))
+    r = subprocess.run([sys.executable, os.path.join(HERE, "bench_reference.py")], env=env, capture_output=True,
+                       text=True)
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if lines:
+        return json.loads(lines[-1])
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    last = (r.stderr.strip().splitlines() or ["no output"])[-1]
+    return {"impl": "reference", "unavailable": f"reference run failed (rc {r.returncode}): {last}"}
 
 
 class ClockSampler:
@@ -163,6 +167,81 @@ def timed_steps(args, device, world, step_resident, step_e2e):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms = t.tolist()
     return ms, e2e_ms, launches, clk, loss_vals
+
+
+KERNEL_CLASSES = [
+    # (class, substrings of the kernel name)
+    ("GEMM (tcgen05)", ("gemm_tc",)),
+    ("split-K reduce", ("splitk_reduce",)),
+    ("gather+rotate fwd/bwd", ("gather_rotate",)),
+    ("rotate-back / rotate-grad", ("rotate_back", "rotate_grad")),
+    ("node reduce", ("node_reduce",)),
+    ("SO(2) gate", ("gate_fwd", "gate_bwd")),
+    ("norms / atomwise gate / LN+SiLU", ("rms_norm", "ln_silu", "gate_l", "layernorm")),
+    ("edge rotation", ("edge_rotation",)),
+    ("loss", ("fock_loss",)),
+    ("labels / head", ("basis_rows", "head_")),
+    ("optimizer (Adam)", ("adam", "Adam")),
+    ("copies / casts", ("copy", "Copy", "cat", "Cat", "memcpy", "Memcpy", "memset", "Memset")),
+]
+
+
+def step_breakdown(args, step, n_edges, n_nodes):
+    """Device time of the training step split by kernel class, from the CUDA activity trace of
+    ``args.steps`` steps (after ``args.warmup``).  The step's own CUDA-event time is taken in a
+    separate, unprofiled pass, so 'idle' = event time - summed kernel time (the step runs on one
+    stream).  Prints a markdown table and one JSON line."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        step(i)
+    e.record()
+    torch.cuda.synchronize()
+    ev_ms = s.elapsed_time(e) / args.steps
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for i in range(args.steps):
+            step(i)
+        torch.cuda.synchronize()
+    per_kernel = {}
+    for evt in prof.events():
+        if evt.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        name = evt.name
+        t = evt.device_time_total if hasattr(evt, "device_time_total") else evt.cuda_time_total
+        k = per_kernel.setdefault(name, [0.0, 0])
+        k[0] += t / 1e3 / args.steps
+        k[1] += 1
+    classes = {c: [0.0, 0] for c, _ in KERNEL_CLASSES}
+    classes["other ATen / elementwise"] = [0.0, 0]
+    for name, (ms, n) in per_kernel.items():
+        for c, keys in KERNEL_CLASSES:
+            if any(k in name for k in keys):
+                break
+        else:
+            c = "other ATen / elementwise"
+        classes[c][0] += ms
+        classes[c][1] += n / args.steps
+    busy = sum(v[0] for v in classes.values())
+    print(f"step: {ev_ms:.2f} ms (CUDA events, unprofiled), kernels {busy:.2f} ms, idle {ev_ms - busy:.2f} ms; "
+          f"{n_edges:.0f} edges, {n_nodes:.0f} atoms per step")
+    print("| class | ms/step | share of step | launches/step |")
+    print("|---|---|---|---|")
+    for c, (ms, n) in sorted(classes.items(), key=lambda kv: -kv[1][0]):
+        print(f"| {c} | {ms:.2f} | {ms / ev_ms:.3f} | {n:.0f} |")
+    print(f"| idle (launch gaps, host sync) | {ev_ms - busy:.2f} | {(ev_ms - busy) / ev_ms:.3f} | |")
+    print("\ntop kernels:")
+    print("| kernel | ms/step | launches/step |")
+    print("|---|---|---|")
+    for name, (ms, n) in sorted(per_kernel.items(), key=lambda kv: -kv[1][0])[:30]:
+        print(f"| `{name[:110]}` | {ms:.3f} | {n / args.steps:.0f} |")
+    print(json.dumps({"breakdown_ms_per_step": ev_ms, "kernel_ms": busy,
+                      "classes": {c: round(v[0], 3) for c, v in classes.items()}}), flush=True)
 
 
 def run_partitioned_inference(args, device, world, rank):
@@ -415,8 +494,9 @@ def main():
     if args.config == "cpu":
         return run_cpu_plumbing(args)
     if args.impl == "reference":
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps(reference_arm(args)))
+        out = reference_arm(args)
+        if int(os.environ.get("RANK", "0")) == 0 and out is not None:
+            print(json.dumps(out))
         return
     sys.path.insert(0, HERE)
     import torch
@@ -485,6 +565,9 @@ def main():
     trainer = SplitTrainer(backbone, head, labeler.irreps, mask_table=torch.as_tensor(labeler.table.mask),
                            grad_sync=sync)
     loss_fn = L.rmse_mse_padded_loss
+    if args.breakdown:
+        return step_breakdown(args, lambda i: trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt),
+                              n_edges, n_nodes)
     ms, e2e_ms, launches, clk, loss_vals = timed_steps(
         args, device, world, lambda i: trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt),
         lambda i: trainer.train_step(host_batches[i % len(host_batches)].to(device, non_blocking=True), loss_fn,

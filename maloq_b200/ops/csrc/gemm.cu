@@ -47,7 +47,6 @@ struct alignas(64) GemmProblemDev {
 struct GemmParamsDev {
   GemmProblemDev p[8];
   int nprob;
-  int skip_store;  // diagnostics: epilogue reads TMEM but stores nothing
   int out_fp32;
   int act;
   float alpha;
@@ -223,7 +222,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   } else {
     // ---------------- epilogue warps 2..5
     const int quarter = warp & 3;
-    const bool out32 = P.out_fp32 != 0, skip = P.skip_store != 0;
+    const bool out32 = P.out_fp32 != 0;
     int it = 0, sbuf = 0;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++it) {
       const TileCoord tc = decode_tile(P, w, tiles_per_split, BN);
@@ -245,8 +244,13 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
         const int col0 = tc.n0 + c0;
-        if (col0 >= ep.N || skip) continue;  // warp-uniform
-        epilogue_math(v, have_k ? ep.alpha : 0.f, ep, col0, lane);
+        if (col0 >= ep.N) continue;  // warp-uniform
+        if (!have_k) {
+          // a split with no k-tiles: no MMA wrote this accumulator, so its TMEM holds stale bits
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        epilogue_math(v, ep.alpha, ep, col0, lane);
         // stage the warp's 32 x 32 chunk (row-major, 32*esz bytes per row) and TMA-store it
         // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
         const int ring = out32 ? 4 : 8;
@@ -406,7 +410,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
   } else {
     // ---------------- epilogue warps 2..5 (both CTAs; rows 128 * crank + ...)
     const int quarter = warp & 3;
-    const bool out32 = P.out_fp32 != 0, skip = P.skip_store != 0;
+    const bool out32 = P.out_fp32 != 0;
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
     int it = 0, sbuf = 0;
     for (int w = cluster; w < total_work; w += nclusters, ++it) {
@@ -427,7 +431,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
           if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8);
         }
         const int col0 = tc.n0 + c0;
-        if (col0 >= ep.N || skip) continue;
+        if (col0 >= ep.N) continue;
         epilogue_math(v, ep.alpha, ep, col0, lane);
         // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
         const int ring = out32 ? 4 : 8;
@@ -604,8 +608,6 @@ static const char* launch_2sm(const GemmParamsDev& P, int total, cudaStream_t st
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
 
-static int g_use_2sm = -1;  // -1: read MALOQ_GEMM_2SM once (default on)
-
 const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_mn, bool out_fp32, int act,
                         float alpha, int splits, int bn, cudaStream_t stream) {
   if (nprob < 1 || nprob > 8) return "gemm: 1..8 problems per launch";
@@ -615,7 +617,6 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
   GemmParamsDev P;
   memset(&P, 0, sizeof(P));
   P.nprob = nprob;
-  P.skip_store = getenv("MALOQ_GEMM_SKIP_STORE") != nullptr;
   P.act = act;
   P.alpha = alpha;
   P.out_fp32 = out_fp32 ? 1 : 0;
@@ -642,11 +643,7 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
     tiles += ((g.M + BM - 1) / BM) * d.tiles_n;
   }
   if (tiles == 0) return nullptr;
-  if (g_use_2sm < 0) {
-    const char* env = getenv("MALOQ_GEMM_2SM");
-    g_use_2sm = (env && env[0] == '0') ? 0 : 1;
-  }
-  if (!a_mn && splits == 1 && g_use_2sm && (bn == 256 || bn == 128)) {
+  if (!a_mn && splits == 1 && (bn == 256 || bn == 128)) {
     // re-tile with 256-row pair tiles; the B box is BN/2 rows per CTA
     int total = 0;
     for (int i = 0; i < nprob; ++i) {
