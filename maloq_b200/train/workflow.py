@@ -116,7 +116,8 @@ class TrainingWorkflow:
                     mmax=min(mmax, lmax), cutoff=c["rcut_gaussian"], edge_channels=c["l_embedding_dim"],
                     num_layers=c["num_mp_layers"], num_distance_basis=c["num_distance_basis"],
                     gaussian_width=c["gaussian_width"], message_type=c["message_type"], open_shell=c["open_shell"],
-                    activation_checkpointing=c["activation_checkpointing"], edge_chunk=c.get("edge_chunk"))
+                    activation_checkpointing=c["activation_checkpointing"], edge_chunk=c.get("edge_chunk"),
+                    norm_type=c.get("norm_type", "rms_norm_sh"))
 
     def prepare_partitioned(self):
         """One structure split over the ranks (graph parallel): rank 0 generates it (or every
