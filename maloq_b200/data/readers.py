@@ -377,10 +377,16 @@ def blocks_from_sparse(M, rows, cols, orb_ptr):
 def load_cp2k(xyz_path, h_path, config, basis_name="dzvp_like", s_path=None, out_path=None, device="cpu"):
     """One periodic CP2K structure with coupled-basis targets: structure from the XYZ, the
     Hamiltonian from the CSR dump (Fermi-shifted, H - mu S, when the overlap and the output
-    file are given), graph within 2 * rcut_orbitals, blocks of every graph pair."""
+    file are given), graph within 2 * rcut_orbitals, blocks of every graph pair.
+
+    ``config['tiling_dims']`` = (n_a, n_b, n_c) replicates the cell into a supercell (weak
+    scaling; reference ``fock_targets_batched.py:71-77``): every pair (i, j) of the supercell
+    takes the block of the unit-cell pair (i mod n, j mod n), so each copy carries the unit
+    cell's targets."""
     from .basis_sets import get_basis
     from .batch import make_sample
-    from .labels import orbital_offsets
+    from .labels import BlockSparseMatrix, orbital_offsets
+    from .structures import tile_structure
     from .targets import FockLabeler
 
     st = read_periodic_xyz(xyz_path)
@@ -388,9 +394,23 @@ def load_cp2k(xyz_path, h_path, config, basis_name="dzvp_like", s_path=None, out
     if s_path is not None and out_path is not None:
         H = fermi_shift(H, read_cp2k_csr(s_path), fermi_energy(out_path))
     labeler = FockLabeler(get_basis(basis_name), device=device)
+    tiling = config.get("tiling_dims")
+    n0, z0 = len(st.z), st.z
+    if tiling is not None and any(int(d) != 1 for d in tiling):
+        st = tile_structure(st, tiling)
     s = make_sample(st, 2 * config.get("rcut_orbitals", 4.0))
     rows, cols = labeler.pairs(s)
-    bsm = blocks_from_sparse(H, rows, cols, orbital_offsets(st.z, labeler.table))
+    if len(st.z) == n0:
+        bsm = blocks_from_sparse(H, rows, cols, orbital_offsets(st.z, labeler.table))
+    else:
+        key = (np.asarray(rows) % n0) * n0 + np.asarray(cols) % n0
+        uk, inv = np.unique(key, return_inverse=True)
+        ob = blocks_from_sparse(H, uk // n0, uk % n0, orbital_offsets(z0, labeler.table))
+        lens = np.diff(ob.block_ptr)[inv]
+        ptr = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+        src = np.arange(int(ptr[-1])) - np.repeat(ptr[:-1], lens) + np.repeat(ob.block_ptr[inv], lens)
+        bsm = BlockSparseMatrix(np.asarray(rows, np.int64), np.asarray(cols, np.int64), ptr, ob.data[src],
+                                orbital_offsets(st.z, labeler.table))
     ny, y = labeler.labels_from_blocks(s, bsm)
     s.node_y, s.y = ny.unsqueeze(0).cpu(), y.unsqueeze(0).cpu()
     return s, labeler

@@ -192,3 +192,20 @@ def si_slab_with_oxide(rng, n_atoms=1_000_000, a=5.43, oxide_nm=3.0, sub_frac=0.
     pos = pos + rng.normal(scale=sigma, size=pos.shape)
     cell = np.array([ncell * a, ncell * a, nz * a + 20.0])  # vacuum along z
     return Structure(z, pos, cell)
+
+
+def tile_structure(st: Structure, tiling_dims) -> Structure:
+    """Supercell of a periodic structure: ``tiling_dims`` = (n_a, n_b, n_c) copies along the
+    (orthorhombic) cell axes.  Copies are ordered with the last axis fastest and each copy
+    holds all atoms in their original order, so tiled atom t is original atom t % n (the
+    order of ASE's ``atoms * dims``, which the reference uses, ``fock_targets_batched.py:1196``)."""
+    if st.cell is None:
+        raise ValueError("tiling needs a periodic structure (a cell)")
+    dims = [int(d) for d in tiling_dims]
+    if len(dims) != 3 or min(dims) < 1:
+        raise ValueError(f"tiling_dims must be three positive integers, got {tiling_dims}")
+    cell = np.asarray(st.cell, dtype=np.float64)
+    shifts = np.array([(a, b, c) for a in range(dims[0]) for b in range(dims[1]) for c in range(dims[2])],
+                      dtype=np.float64) * cell
+    pos = (st.pos[None] + shifts[:, None]).reshape(-1, 3)
+    return Structure(np.tile(st.z, len(shifts)), pos, cell * np.asarray(dims, dtype=np.float64), st.charge, st.spin)

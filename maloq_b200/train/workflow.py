@@ -165,7 +165,8 @@ class TrainingWorkflow:
     def _load_cp2k_folder(self, c):
         """``dbpath``: a folder of structure directories, each with ``structure.xyz`` and
         ``hamiltonian.csr`` (CP2K dump), optionally ``overlap.csr`` + ``cp2k.out`` for the
-        Fermi-level shift.  Basis: ``basis_name`` (default the DZVP-like Si/O/Hf basis)."""
+        Fermi-level shift.  Basis: ``basis_name`` (default the DZVP-like Si/O/Hf basis).
+        ``tiling_dims`` replicates each cell into a supercell with the cell's targets."""
         from ..data.readers import load_cp2k
 
         root = c["dbpath"]

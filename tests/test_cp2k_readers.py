@@ -132,3 +132,32 @@ def test_orca_output_reader(tmp_path, unrestricted):
         assert np.allclose(d["fock"]["alpha"], Fa) and np.allclose(d["fock"]["beta"], Fb)
     else:
         assert np.allclose(d["fock"], Fa)
+
+
+def test_tiled_cell_matches_the_unit_cell_per_copy(tmp_path):
+    """tiling_dims: every copy of the supercell carries the unit cell's node labels, and every
+    supercell edge the labels of its unit-cell pair (cutoff below half the cell, so each
+    pair has one image)."""
+    rng = np.random.default_rng(4)
+    st = structures.amorphous_sio2(rng, 90)
+    L = 17.0
+    sym = {14: "Si", 8: "O"}
+    lines = [str(len(st.z)), f"Cell: {L} {L} {L}"] + [f"{sym[int(z)]} {p[0]:.6f} {p[1]:.6f} {p[2]:.6f}"
+                                                     for z, p in zip(st.z, np.mod(st.pos, L))]
+    (tmp_path / "s.xyz").write_text("\n".join(lines) + "\n")
+    n_orb = 13 * len(st.z)
+    A = sp.random(n_orb, n_orb, density=0.02, random_state=5)
+    A = (A + A.T).tocsr()
+    readers.write_cp2k_csr(tmp_path / "h.csr", A)
+    cfg = {"rcut_orbitals": 3.0}
+    s1, lab = readers.load_cp2k(tmp_path / "s.xyz", tmp_path / "h.csr", cfg)
+    s2, _ = readers.load_cp2k(tmp_path / "s.xyz", tmp_path / "h.csr", dict(cfg, tiling_dims=[2, 1, 3]))
+    n = s1.num_nodes
+    assert s2.num_nodes == 6 * n and s2.num_edges == 6 * s1.num_edges
+    for c in range(6):
+        assert np.allclose(s2.node_y[0][c * n:(c + 1) * n].numpy(), s1.node_y[0].numpy())
+    ref = {(int(i), int(j)): k for k, (i, j) in enumerate(zip(s1.src, s1.dst))}
+    idx = np.array([ref[(int(i) % n, int(j) % n)] for i, j in zip(s2.src, s2.dst)])
+    assert np.allclose(s2.y[0].numpy(), s1.y[0].numpy()[idx], atol=1e-6)
+    t = structures.tile_structure(structures.Structure(st.z, np.mod(st.pos, L), np.full(3, L)), [2, 1, 3])
+    assert np.allclose(t.cell, [2 * L, L, 3 * L]) and np.allclose(t.pos[n * 1:n * 2], np.mod(st.pos, L) + [0, 0, L])
