@@ -13,8 +13,9 @@ all returning ``part[node] -> rank``:
   counts (spatial; periodic slabs touch their neighbours only);
 * ``rcb`` - recursive coordinate bisection along the longest extent, edge-balanced (the
   reference's low_nn / longest_dim family);
-* ``greedy`` - breadth-first region growing to equal edge counts (a dependency-free stand-in
-  for METIS, which is not installed);
+* ``metis`` - multilevel k-way partitioning (heavy-edge coarsening, greedy growing, batched
+  boundary refinement; :mod:`maloq_b200.parallel.multilevel`), edge-balanced;
+* ``greedy`` - breadth-first region growing to equal edge counts;
 * ``worst-case`` - round-robin assignment (maximal cut), for stress tests;
 * ``surface_volume`` / ``approx_neighbors`` - bisection choosing each cut axis from a
   geometric estimate (halo shell volume / neighbouring-domain count);
@@ -27,6 +28,8 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 
 import numpy as np
+
+from .multilevel import partition_multilevel
 
 
 def _balanced_cuts(weights, parts):
@@ -272,7 +275,7 @@ def partition_worst_case(n, world, **_):
 PARTITIONERS = {
     "linear-atomwise": partition_linear_atomwise, "linear-edgewise": partition_linear_edgewise,
     "slab": partition_slab, "rcb": partition_rcb, "low_nn": partition_rcb, "longest_dim": partition_rcb,
-    "greedy": partition_greedy, "metis": partition_greedy, "worst-case": partition_worst_case,
+    "greedy": partition_greedy, "metis": partition_multilevel, "worst-case": partition_worst_case,
     "surface_volume": partition_surface_volume, "approx_neighbors": partition_approx_neighbors,
     "local_optimal": partition_local_optimal, "bruteforce": partition_bruteforce,
 }
