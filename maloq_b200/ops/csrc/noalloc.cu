@@ -1,32 +1,19 @@
-// Allocation-free weight-gradient GEMM: a C entry point for callers that cannot allocate.
-//
-// This entry point has no counterpart in the reference.  It exists for callers that must
-// not call cudaMalloc (or any allocator) from the code that launches the work: a host
-// application that hands this library fixed buffers it allocated up front, a runtime that
-// forbids allocation inside its step function, or code running while a memory pool is
-// frozen.  Such callers pass the inputs and the output; the split-K partial sums that the
-// regular path (gemm_tn_weight_grad in ops/kernels.py) keeps in a freshly allocated
-// workspace live here in a fixed-size device array instead.
+// Allocation-free weight-gradient GEMM (declared in noalloc.h, which states the callers it
+// serves and its limits; no counterpart in the reference).
 //
 //   dW[N,K] = gy[M,N]^T @ x[M,K]      (bf16 inputs, fp32 output and accumulation)
 //
-// Limits and behaviour:
-// * The scratch array holds MALOQ_NOALLOC_SCRATCH_FLOATS fp32 values (64 MiB).  Every GPU
-//   that loads this library reserves it until the process exits.  The call uses
-//   s = min(desired splits, scratch / (N*K)) partial slices and is rejected with an error
-//   when even two slices (2*N*K floats) do not fit.
-// * The first call on each device looks up the array's device address with
-//   cudaGetSymbolAddress (with that device current) and caches it; make that first call
-//   before any stream capture.
-// * All calls share the one array and each call overwrites the slices it uses (every
-//   partial element is written before it is read, so nothing needs clearing).  Calls whose
-//   GPU work overlaps - on two streams at once, for example - race on the array; issue them
-//   in order on one stream or synchronise between them.
-// * No cudaMalloc, cudaFree or allocating library routine is called.
+// The number of split-K slices follows the allocating path (gemm_tn_weight_grad in
+// ops/kernels.py): min(ceil(296 / output tiles), M / 1024, 64).  When that is below two the
+// GEMM writes dW directly and the scratch array is not touched.  Otherwise the partials go to
+// the scratch array (as many slices as fit) and a fixed-order reduction writes dW; every
+// partial element a reduction reads is written by the GEMM of the same call first, so nothing
+// needs clearing between calls.  No cudaMalloc, cudaFree or allocating library routine is
+// called.
 #include "common.cuh"
 #include "gemm.h"
+#include "noalloc.h"
 
-#define MALOQ_NOALLOC_SCRATCH_FLOATS (16ll * 1024 * 1024)
 #define MALOQ_NOALLOC_MAX_DEVICES 64
 
 namespace {
@@ -45,15 +32,10 @@ int fail(const char* msg) {
 
 extern "C" {
 
-// Text of the last error returned by maloq_weight_grad_noalloc (nullptr if none).
-const char* maloq_noalloc_last_error() { return g_noalloc_error; }
+const char* maloq_noalloc_last_error(void) { return g_noalloc_error; }
 
-// Scratch capacity in fp32 elements.
-long long maloq_noalloc_scratch_floats() { return MALOQ_NOALLOC_SCRATCH_FLOATS; }
+long long maloq_noalloc_scratch_floats(void) { return MALOQ_NOALLOC_SCRATCH_FLOATS; }
 
-// dW[N,K] = gy[M,N]^T x[M,K] on `stream` without allocating.  gy and x are row-major bf16
-// (16-byte aligned, N and K multiples of 8); dW is row-major fp32 [N,K].  Returns 0 on
-// success, 1 on a rejected call (see maloq_noalloc_last_error).
 int maloq_weight_grad_noalloc(const void* gy, const void* x, float* dw, int M, int N, int K, cudaStream_t stream) {
   g_noalloc_error = nullptr;
   if (M < 0 || N <= 0 || K <= 0) return fail("maloq_weight_grad_noalloc: bad sizes");
@@ -79,8 +61,24 @@ int maloq_weight_grad_noalloc(const void* gy, const void* x, float* dw, int M, i
   long long splits = (296 + tiles - 1) / tiles;
   if (splits > M / 1024) splits = M / 1024;
   if (splits > 64) splits = 64;
-  if (splits < 2) splits = 2;
   if (splits * slice > MALOQ_NOALLOC_SCRATCH_FLOATS) splits = MALOQ_NOALLOC_SCRATCH_FLOATS / slice;
+  if (splits < 2) {
+    // one slice: the GEMM writes dW itself
+    maloq::GemmProblem p;
+    p.a = gy;
+    p.lda = N;
+    p.b = x;
+    p.ldb = K;
+    p.c = dw;
+    p.ldc = K;
+    p.split_stride = slice;
+    p.bias = nullptr;
+    p.M = N;
+    p.N = K;
+    p.K = M;
+    const char* err = maloq::gemm_launch(&p, 1, true, true, true, 0, 1.f, 1, 128, stream);
+    return err ? fail(err) : 0;
+  }
   maloq::GemmProblem p;
   p.a = gy;
   p.lda = N;
