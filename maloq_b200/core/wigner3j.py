@@ -2,11 +2,13 @@
 
 ``wigner_3j(l1, l2, l3)`` is the unit-Frobenius-norm tensor ``C[i, j, k]`` that is invariant
 under simultaneous rotation, ``C = (D1 (x) D2 (x) D3) C`` for every rotation, with the D
-matrices of :mod:`maloq_b200.core.sph`.  Because ``l3`` appears at most once in
-``l1 (x) l2``, the invariant subspace is one-dimensional; for the sorted triple it is computed as the null space
-of ``sum_R (D1(R) (x) D2(R) (x) D3(R) - I)`` over two generic rotations, in float64.  The
-overall sign of the sorted triple is fixed by making its first non-zero entry (C order)
-positive; other orders follow from the permutation symmetry of 3j symbols.
+matrices of :mod:`maloq_b200.core.sph`.  It is built the way e3nn defines its ``wigner_3j``
+(the convention of the reference's labels): the complex Clebsch-Gordan coefficients
+<l1 m1 l2 m2 | l3 m3> (Racah's formula), carried into the real harmonic basis by the
+change-of-basis matrices Q_l (with the (-i)^l factor that makes the result real),
+``C = einsum(Q1, Q2, conj(Q3)^T, CG)``, divided by its Frobenius norm - in float64.  This fixes
+the sign of every triple (the invariant subspace of l1 (x) l2 (x) l3 is one-dimensional, so
+the tensors differ from any other construction by at most a sign).
 
 The coupled<->uncoupled transform follows the reference's ``e3TensorDecomp``
 (``fock_utils/utils_tensor_decomp.py:51-169``): an orbital block ``H[l1, l2]`` of shape
@@ -16,6 +18,7 @@ The coupled<->uncoupled transform follows the reference's ``e3TensorDecomp``
 
 from __future__ import annotations
 
+import math
 from functools import lru_cache
 
 import numpy as np
@@ -24,44 +27,54 @@ import torch
 from . import sph
 
 
+def _clebsch_gordan(j1: int, m1: int, j2: int, m2: int, J: int, M: int) -> float:
+    """<j1 m1 j2 m2 | J M> by Racah's formula (Condon-Shortley phases)."""
+    if M != m1 + m2 or not abs(j1 - j2) <= J <= j1 + j2 or abs(m1) > j1 or abs(m2) > j2 or abs(M) > J:
+        return 0.0
+    f = math.factorial
+    pre = math.sqrt((2 * J + 1) * f(J + j1 - j2) * f(J - j1 + j2) * f(j1 + j2 - J) / f(j1 + j2 + J + 1))
+    pre *= math.sqrt(f(J + M) * f(J - M) * f(j1 - m1) * f(j1 + m1) * f(j2 - m2) * f(j2 + m2))
+    s = 0.0
+    for k in range(j1 + j2 - J + 1):
+        a = (k, j1 + j2 - J - k, j1 - m1 - k, j2 + m2 - k, J - j2 + m1 + k, J - j1 - m2 + k)
+        if min(a) < 0:
+            continue
+        s += (-1) ** k / math.prod(f(x) for x in a)
+    return pre * s
+
+
+def _real_to_complex(l: int) -> np.ndarray:
+    """Q_l with (complex harmonic index, real harmonic index): real harmonics m < 0 / m > 0
+    are the (sin, cos) combinations of the complex pair +-|m|, times (-i)^l so that the real
+    3j tensors below are real."""
+    q = np.zeros((2 * l + 1, 2 * l + 1), dtype=np.complex128)
+    r = 1 / math.sqrt(2)
+    for m in range(-l, 0):
+        q[l + m, l + abs(m)] = r
+        q[l + m, l - abs(m)] = -1j * r
+    q[l, l] = 1.0
+    for m in range(1, l + 1):
+        q[l + m, l + m] = (-1) ** m * r
+        q[l + m, l - m] = 1j * (-1) ** m * r
+    return (-1j) ** l * q
+
+
 @lru_cache(maxsize=None)
 def _wigner_3j_np(l1: int, l2: int, l3: int) -> np.ndarray:
-    """Tensor for any order of (l1, l2, l3), derived from the sorted triple so that the
-    permutation symmetry of 3j symbols holds: cyclic permutations leave it unchanged, odd
-    permutations multiply it by (-1)^(l1+l2+l3)."""
-    ls = (l1, l2, l3)
-    order = sorted(range(3), key=lambda i: (ls[i], i))
-    base = _wigner_3j_sorted(*(ls[i] for i in order))
-    # base axes correspond to ls[order[0]], ls[order[1]], ls[order[2]]; move them back
-    inv = [order.index(i) for i in range(3)]
-    out = np.transpose(base, inv)
-    odd = sum(1 for a in range(3) for b in range(a + 1, 3) if order[a] > order[b]) % 2
-    if odd and (l1 + l2 + l3) % 2:
-        out = -out
-    return np.ascontiguousarray(out)
-
-
-@lru_cache(maxsize=None)
-def _wigner_3j_sorted(l1: int, l2: int, l3: int) -> np.ndarray:
     if not (abs(l1 - l2) <= l3 <= l1 + l2):
         raise ValueError(f"l3={l3} not in |l1-l2|..l1+l2 for l1={l1}, l2={l2}")
-    d1, d2, d3 = 2 * l1 + 1, 2 * l2 + 1, 2 * l3 + 1
-    rots = [sph.euler_matrix(0.7, 1.3, -0.4), sph.euler_matrix(-1.9, 0.5, 2.2)]
-    A = []
-    for R in rots:
-        D = np.kron(np.kron(sph.wigner_D_from_matrix(l1, R), sph.wigner_D_from_matrix(l2, R)),
-                    sph.wigner_D_from_matrix(l3, R))
-        A.append(D - np.eye(d1 * d2 * d3))
-    A = np.concatenate(A, axis=0)
-    _, s, vt = np.linalg.svd(A)
-    v = vt[-1]
-    assert s[-1] < 1e-8 and (len(s) < 2 or s[-2] > 1e-4), "invariant subspace must be 1-D"
-    v = v / np.linalg.norm(v)
-    v[np.abs(v) < 1e-13] = 0.0
-    nz = np.flatnonzero(np.abs(v) > 1e-10)
-    if v[nz[0]] < 0:
-        v = -v
-    return v.reshape(d1, d2, d3)
+    C = np.zeros((2 * l1 + 1, 2 * l2 + 1, 2 * l3 + 1))
+    for m1 in range(-l1, l1 + 1):
+        for m2 in range(-l2, l2 + 1):
+            if abs(m1 + m2) <= l3:
+                C[l1 + m1, l2 + m2, l3 + m1 + m2] = _clebsch_gordan(l1, m1, l2, m2, l3, m1 + m2)
+    Cr = np.einsum("ij,kl,mn,ikn->jlm", _real_to_complex(l1), _real_to_complex(l2),
+                   np.conj(_real_to_complex(l3).T), C.astype(np.complex128))
+    assert np.abs(Cr.imag).max() < 1e-10
+    Cr = Cr.real
+    Cr = Cr / np.linalg.norm(Cr)
+    Cr[np.abs(Cr) < 1e-14] = 0.0
+    return np.ascontiguousarray(Cr)
 
 
 def wigner_3j(l1: int, l2: int, l3: int, dtype=torch.float32, device=None) -> torch.Tensor:

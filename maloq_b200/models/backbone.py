@@ -75,12 +75,15 @@ class SpectralAtomwise(nn.Module):
         self.act = GateActivation(lmax, lmax, hidden_channels, outer_dim="l")
         self.so3_linear_2 = SO3_Linear(hidden_channels, sphere_channels, lmax)
 
-    def forward(self, x):
+    def forward(self, x, residual=None):
+        """``residual`` is added to the output (in the second SO3 linear's GEMM epilogue on the
+        kernel path).  The hidden activations between the two SO3 linears are bf16 on the kernel
+        path (they only feed the next GEMM)."""
         lin = self.scalar_mlp[0]
         g = ops.linear(x[:, 0], lin.weight, lin.bias, act="silu")
-        h = self.so3_linear_1(x)
+        h = self.so3_linear_1(x, out_dtype=torch.bfloat16)
         h = self.act(g, h)
-        return self.so3_linear_2(h)
+        return self.so3_linear_2(h, residual=residual)
 
 
 class eSEN_Block(nn.Module):
@@ -102,12 +105,12 @@ class eSEN_Block(nn.Module):
         if self.node_or_edge == "node":
             h = self.norm_1(x_node)
             h = self.edge_wise(h, x_edge_emb, x_edge, graph, "node")
-            h, res = self.norm_2(h, residual=x_node)  # res = h + x_node
-            return self.atom_wise(h) + res
+            h, res = self.norm_2(h, residual=x_node, out_dtype=torch.bfloat16)  # res = h + x_node
+            return self.atom_wise(h, residual=res)
         h = self.edge_wise(x_node, x_edge_emb, x_edge, graph, "edge")
         h = self.norm_1(h)
-        h, res = self.norm_2(h, residual=x_edge_emb)
-        return self.atom_wise(h) + res
+        h, res = self.norm_2(h, residual=x_edge_emb, out_dtype=torch.bfloat16)
+        return self.atom_wise(h, residual=res)
 
     # ------------------------------------------------------------------ edge-chunked execution
     def _forward_chunked(self, x_node, x_edge_emb, x_edge, graph):
@@ -125,8 +128,8 @@ class eSEN_Block(nn.Module):
             hx = graph.halo.materialize(h) if graph.halo is not None else h
             outs = [run(self._node_rows, hx, _rows(x_edge_emb, e0, e1), x_edge, e0, e1, graph.chunk_graph(i))
                     for i, (e0, e1, _, _) in enumerate(graph.chunks)]
-            h, res = self.norm_2(torch.cat(outs, 0), residual=x_node)
-            return self.atom_wise(h) + res
+            h, res = self.norm_2(torch.cat(outs, 0), residual=x_node, out_dtype=torch.bfloat16)
+            return self.atom_wise(h, residual=res)
         xn = graph.halo.materialize(x_node) if graph.halo is not None else x_node
         if not grad:
             for i, (e0, e1, _, _) in enumerate(graph.chunks):
@@ -143,8 +146,8 @@ class eSEN_Block(nn.Module):
         x_in = xee.to(xn.dtype)  # compute dtype of the node stream
         h = self.edge_wise(xn, x_in, x_edge[e0:e1], sub, "edge")
         h = self.norm_1(h)
-        h, res = self.norm_2(h, residual=x_in)
-        return (self.atom_wise(h) + res).to(xee.dtype)
+        h, res = self.norm_2(h, residual=x_in, out_dtype=torch.bfloat16)
+        return self.atom_wise(h, residual=res).to(xee.dtype)
 
 
 class EdgeInputs:

@@ -91,12 +91,15 @@ class RadialMLP(nn.Module):
             mods.append(nn.SiLU())
         self.net = nn.Sequential(*mods)
 
-    def forward(self, x):
+    def forward(self, x, out_dtype=None):
+        """``out_dtype``: dtype of the last layer's output on the kernel path (the edge kernels
+        read the radial modulation as bf16)."""
         mods = list(self.net)
         i = 0
         while i < len(mods):
             lin = mods[i]
-            x = ops.linear(x, lin.weight, lin.bias)
+            last = i == len(mods) - 1
+            x = ops.linear(x, lin.weight, lin.bias, out_dtype=out_dtype if last else None)
             if i + 1 < len(mods) and isinstance(mods[i + 1], nn.LayerNorm):
                 ln = mods[i + 1]
                 x = ops.layernorm_silu(x, ln.weight, ln.bias, ln.eps)
@@ -118,8 +121,10 @@ class SO3_Linear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(out_features))
         self.register_buffer("expand_index", l_expand_index(lmax))
 
-    def forward(self, x):
-        return ops.so3_linear(x, self.weight, self.bias, self.lmax)
+    def forward(self, x, out_dtype=None, residual=None):
+        """``residual`` is added to the output (fused on the kernel path); ``out_dtype``: bf16
+        output on the kernel path when the consumer is another GEMM."""
+        return ops.so3_linear(x, self.weight, self.bias, self.lmax, out_dtype, residual)
 
 
 class GateActivation(nn.Module):
@@ -165,16 +170,18 @@ class EquivariantRMSNorm(nn.Module):
             bw[l * l : l * l + 2 * l + 1] = 1.0 / (2 * l + 1)
         self.register_buffer("balance_degree_weight", bw / (lmax + 1))
 
-    def forward(self, x, residual=None):
-        """norm(x), or (norm(x + residual), x + residual) when ``residual`` is given."""
-        return ops.rms_norm_sh(x, self.affine_weight, self.affine_bias, self.balance_degree_weight, self.eps, residual)
+    def forward(self, x, residual=None, out_dtype=None):
+        """norm(x), or (norm(x + residual), x + residual) when ``residual`` is given.  On the
+        kernel path ``out_dtype`` = bf16 stores norm(.) as bf16 (the sum stays fp32)."""
+        return ops.rms_norm_sh(x, self.affine_weight, self.affine_bias, self.balance_degree_weight, self.eps, residual,
+                               out_dtype)
 
 
 class _ResidualNorm(nn.Module):
     """``forward(x, residual=None)`` convention of the norms: with a residual, returns
     (norm(x + residual), x + residual)."""
 
-    def forward(self, x, residual=None):
+    def forward(self, x, residual=None, out_dtype=None):
         if residual is None:
             return self.normalize(x)
         s = x + residual

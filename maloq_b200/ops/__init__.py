@@ -39,9 +39,11 @@ def _cuda(*tensors) -> bool:
     return False
 
 
-def linear(x, weight, bias=None, act=None):
+def linear(x, weight, bias=None, act=None, out_dtype=None):
+    """x @ weight^T + bias (optional SiLU).  ``out_dtype`` (CUDA path): dtype of the result,
+    e.g. bf16 when the next consumer reads bf16 (fp32 by default)."""
     if _cuda(x):
-        return _native.linear(x, weight, bias, act)
+        return _native.linear(x, weight, bias, act, out_dtype)
     return _ref.linear(x, weight, bias, act)
 
 
@@ -51,10 +53,14 @@ def layernorm_silu(x, weight, bias, eps=1e-5):
     return _ref.layernorm_silu(x, weight, bias, eps)
 
 
-def so3_linear(x, weight, bias, lmax):
+def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
+    """Per-degree linear; ``residual`` (same shape as the output, fp32) is added to the result
+    (fused into the GEMM epilogue on the kernel path); ``out_dtype`` selects a bf16 output on
+    the kernel path."""
     if _cuda(x):
-        return _native.so3_linear(x, weight, bias, lmax)
-    return _ref.so3_linear(x, weight, bias, lmax)
+        return _native.so3_linear(x, weight, bias, lmax, out_dtype, residual)
+    out = _ref.so3_linear(x.to(weight.dtype), weight, bias, lmax)
+    return out if residual is None else out + residual
 
 
 def gate(gating_scalars, x, expand_index, lmax):
@@ -63,9 +69,11 @@ def gate(gating_scalars, x, expand_index, lmax):
     return _ref.gate(gating_scalars, x, expand_index, lmax)
 
 
-def rms_norm_sh(x, affine_weight, affine_bias, balance_degree_weight, eps, residual=None):
+def rms_norm_sh(x, affine_weight, affine_bias, balance_degree_weight, eps, residual=None, out_dtype=None):
+    """``out_dtype``: dtype of the normalised output on the kernel path (bf16 when it only
+    feeds a GEMM); the residual sum stays fp32."""
     if _cuda(x):
-        return _native.rms_norm_sh(x, affine_weight, affine_bias, eps, residual)
+        return _native.rms_norm_sh(x, affine_weight, affine_bias, eps, residual, out_dtype)
     return _ref.rms_norm_sh(x, affine_weight, affine_bias, balance_degree_weight, eps, residual)
 
 

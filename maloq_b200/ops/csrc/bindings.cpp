@@ -22,9 +22,10 @@ cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 // outs[i] = alpha * A[i] @ B[i]^T (+bias) (act); A/B bf16 row-major.
 // a_mn=false: A [M,K], B [N,K].  a_mn=true: A [K,M], B [K,N] (weight-gradient form).
 // splits > 1: outs[i] is fp32 [splits, M, N] holding partial sums.
+// resids (optional, fp32 output only): Rs[i] [M,N] (row stride free) added in the epilogue.
 void gemm(std::vector<at::Tensor> As, std::vector<at::Tensor> Bs, std::vector<at::Tensor> Cs,
           std::vector<c10::optional<at::Tensor>> biases, bool mn_major, int64_t act, double alpha, int64_t splits,
-          int64_t bn) {
+          int64_t bn, std::vector<c10::optional<at::Tensor>> resids) {
   const size_t np = As.size();
   TORCH_CHECK(np >= 1 && np <= 8 && Bs.size() == np && Cs.size() == np, "gemm: 1..8 problems");
   std::vector<maloq::GemmProblem> P(np);
@@ -56,6 +57,14 @@ void gemm(std::vector<at::Tensor> As, std::vector<at::Tensor> Bs, std::vector<at
       TORCH_CHECK(C.dim() == 2 && C.size(0) == g.M && C.size(1) == g.N, "gemm: output shape");
       g.ldc = C.stride(0);
       g.split_stride = 0;
+    }
+    if (i < resids.size() && resids[i].has_value()) {
+      const auto& R = *resids[i];
+      TORCH_CHECK(R.scalar_type() == at::kFloat && out_fp32 && R.dim() == 2 && R.size(0) == g.M &&
+                      R.size(1) == g.N && R.stride(1) == 1,
+                  "gemm: residual must be fp32 [M, N] with contiguous rows (fp32 output)");
+      g.resid = R.data_ptr<float>();
+      g.ldr = R.stride(0);
     }
     g.bias = nullptr;
     if (i < biases.size() && biases[i].has_value()) {
@@ -92,7 +101,7 @@ __nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>
 const long long* ll(const at::Tensor& t) { return reinterpret_cast<const long long*>(t.data_ptr<int64_t>()); }
 const long long* ll(const c10::optional<at::Tensor>& t) { return t.has_value() ? ll(*t) : nullptr; }
 
-// A [E, R*Cin] = rad * rot . [X[src] | X[dst] | XE]
+// A [E, R*Cin] = rad * rot . [X[src] | X[dst] | XE]; rad bf16 [E, NS*Cin]
 void gather_rotate_fwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
                        at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor A, int64_t Cin,
                        int64_t peers, c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row,
@@ -103,29 +112,43 @@ void gather_rotate_fwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
   chk(src, at::kLong, "src");
   chk(dst, at::kLong, "dst");
   if (XE.has_value()) chk(*XE, at::kFloat, "XE");
-  if (rad.has_value()) chk(*rad, at::kFloat, "rad");
+  if (rad.has_value()) chk(*rad, at::kBFloat16, "rad");
+  TORCH_CHECK(A.numel() == src.numel() * rot.size(1) * Cin, "gather_rotate_fwd: A must be [E, R*Cin]");
   const at::cuda::CUDAGuard guard(X.device());
   check(maloq::edge_gather_rotate_fwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), ll(src), ll(dst),
-                                      rot.data_ptr<float>(), ptr<float>(rad), bf(A), (int)src.size(0),
-                                      (int)X.size(2), (int)Cin, reinterpret_cast<const float* const*>(peers),
+                                      rot.data_ptr<float>(), rad.has_value() ? bf(*rad) : nullptr, bf(A),
+                                      (int)src.size(0), (int)X.size(2), (int)Cin,
+                                      reinterpret_cast<const float* const*>(peers),
                                       halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
                                       n_own, X.size(0), halo_owner.has_value() ? halo_owner->numel() : 0, stream()));
 }
 
-void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor src,
-                       at::Tensor dst, at::Tensor rot, c10::optional<at::Tensor> rad, at::Tensor dA, at::Tensor DSRC,
-                       at::Tensor DDST, c10::optional<at::Tensor> DXE, c10::optional<at::Tensor> DRAD, int64_t Cin,
-                       int64_t peers, c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row,
-                       int64_t n_own) {
+// Backward of gather_rotate: node gradients DX [N, S, C] (dst CSR + src CSR walks, no per-edge
+// rows), DXE (edge embedding part), DRAD (bf16)
+void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Tensor> XE, at::Tensor rot,
+                       c10::optional<at::Tensor> rad, at::Tensor dA, at::Tensor dst_ptr, at::Tensor src_perm,
+                       at::Tensor src_ptr, at::Tensor DX, c10::optional<at::Tensor> DXE,
+                       c10::optional<at::Tensor> DRAD, int64_t Cin, int64_t peers,
+                       c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row, int64_t n_own) {
   chk(X, at::kFloat, "X");
+  chk(rot, at::kFloat, "rot");
   chk(dA, at::kBFloat16, "dA");
-  chk(DSRC, at::kFloat, "DSRC");
-  chk(DDST, at::kFloat, "DDST");
+  chk(DX, at::kFloat, "DX");
+  chk(dst_ptr, at::kLong, "dst_ptr");
+  chk(src_perm, at::kLong, "src_perm");
+  chk(src_ptr, at::kLong, "src_ptr");
+  if (rad.has_value()) chk(*rad, at::kBFloat16, "rad");
+  if (DRAD.has_value()) chk(*DRAD, at::kBFloat16, "DRAD");
+  if (XE.has_value()) chk(*XE, at::kFloat, "XE");
+  if (DXE.has_value()) chk(*DXE, at::kFloat, "DXE");
+  const int N = (int)DX.size(0);
+  TORCH_CHECK(dst_ptr.numel() == N + 1 && src_ptr.numel() == N + 1, "gather_rotate_bwd: CSR offsets need N+1 rows");
   const at::cuda::CUDAGuard guard(X.device());
-  check(maloq::edge_gather_rotate_bwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), ll(src), ll(dst),
-                                      rot.data_ptr<float>(), ptr<float>(rad), bf(dA), DSRC.data_ptr<float>(),
-                                      DDST.data_ptr<float>(), ptr<float>(DXE), ptr<float>(DRAD), (int)src.size(0),
-                                      (int)X.size(2), (int)Cin, reinterpret_cast<const float* const*>(peers),
+  check(maloq::edge_gather_rotate_bwd((int)L, (int)MM, X.data_ptr<float>(), ptr<float>(XE), rot.data_ptr<float>(),
+                                      rad.has_value() ? bf(*rad) : nullptr, bf(dA), ll(dst_ptr), ll(src_perm),
+                                      ll(src_ptr), DX.data_ptr<float>(), ptr<float>(DXE),
+                                      DRAD.has_value() ? bf(*DRAD) : nullptr, N, (int)rot.size(0), (int)X.size(2),
+                                      (int)Cin, reinterpret_cast<const float* const*>(peers),
                                       halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
                                       n_own, X.size(0), halo_owner.has_value() ? halo_owner->numel() : 0, stream()));
 }
@@ -206,26 +229,33 @@ void gate_bwd(int64_t L, int64_t MM, at::Tensor Y1, at::Tensor dH1, at::Tensor d
 }
 
 
+// OUT fp32 or bf16 (the dtype of the tensor passed)
 void rms_norm_fwd(int64_t L, at::Tensor X, c10::optional<at::Tensor> RES, at::Tensor aw, at::Tensor ab,
                   at::Tensor OUT, c10::optional<at::Tensor> SUM, double eps) {
   chk(X, at::kFloat, "X");
-  chk(OUT, at::kFloat, "OUT");
+  const bool ob = OUT.scalar_type() == at::kBFloat16;
+  chk(OUT, ob ? at::kBFloat16 : at::kFloat, "OUT");
   chk(aw, at::kFloat, "affine_weight");
   chk(ab, at::kFloat, "affine_bias");
+  if (RES.has_value()) chk(*RES, at::kFloat, "RES");
+  if (SUM.has_value()) chk(*SUM, at::kFloat, "SUM");
   const at::cuda::CUDAGuard guard(X.device());
   check(maloq::rms_norm_fwd((int)L, X.data_ptr<float>(), ptr<float>(RES), aw.data_ptr<float>(), ab.data_ptr<float>(),
-                            OUT.data_ptr<float>(), ptr<float>(SUM), (int)X.size(0), (int)X.size(2), (float)eps,
+                            OUT.data_ptr(), ob, ptr<float>(SUM), (int)X.size(0), (int)X.size(2), (float)eps,
                             stream()));
 }
 
+// G fp32 or bf16
 void rms_norm_bwd(int64_t L, at::Tensor Sx, at::Tensor G, c10::optional<at::Tensor> GS, at::Tensor aw, at::Tensor DX,
                   at::Tensor PART, double eps) {
   chk(Sx, at::kFloat, "S");
-  chk(G, at::kFloat, "G");
+  const bool gb = G.scalar_type() == at::kBFloat16;
+  chk(G, gb ? at::kBFloat16 : at::kFloat, "G");
   chk(DX, at::kFloat, "DX");
   chk(PART, at::kFloat, "PART");
+  if (GS.has_value()) chk(*GS, at::kFloat, "GS");
   const at::cuda::CUDAGuard guard(Sx.device());
-  check(maloq::rms_norm_bwd((int)L, Sx.data_ptr<float>(), G.data_ptr<float>(), ptr<float>(GS), aw.data_ptr<float>(),
+  check(maloq::rms_norm_bwd((int)L, Sx.data_ptr<float>(), G.data_ptr(), gb, ptr<float>(GS), aw.data_ptr<float>(),
                             DX.data_ptr<float>(), PART.data_ptr<float>(), (int)Sx.size(0), (int)Sx.size(2), (float)eps,
                             (int)PART.size(0), stream()));
 }
@@ -250,21 +280,27 @@ void ln_silu_bwd(at::Tensor X, at::Tensor w, at::Tensor b, at::Tensor G, at::Ten
                            (int)(PART.size(0) / 8), stream()));
 }
 
+// X / OUT (and DO / DX) share a dtype, fp32 or bf16; gates fp32
 void gate_l_fwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor OUT) {
-  chk(X, at::kFloat, "X");
+  const bool b16 = X.scalar_type() == at::kBFloat16;
+  chk(X, b16 ? at::kBFloat16 : at::kFloat, "X");
   chk(Gt, at::kFloat, "gates");
-  chk(OUT, at::kFloat, "OUT");
+  chk(OUT, b16 ? at::kBFloat16 : at::kFloat, "OUT");
   const at::cuda::CUDAGuard guard(X.device());
-  check(maloq::gate_l_fwd((int)L, X.data_ptr<float>(), Gt.data_ptr<float>(), OUT.data_ptr<float>(), (int)X.size(0),
+  check(maloq::gate_l_fwd((int)L, X.data_ptr(), Gt.data_ptr<float>(), OUT.data_ptr(), b16, (int)X.size(0),
                           (int)X.size(2), stream()));
 }
 
 void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tensor DX, at::Tensor DG) {
-  chk(X, at::kFloat, "X");
-  chk(DO, at::kFloat, "DO");
+  const bool b16 = X.scalar_type() == at::kBFloat16;
+  chk(X, b16 ? at::kBFloat16 : at::kFloat, "X");
+  chk(DO, b16 ? at::kBFloat16 : at::kFloat, "DO");
+  chk(DX, b16 ? at::kBFloat16 : at::kFloat, "DX");
+  chk(Gt, at::kFloat, "gates");
+  chk(DG, at::kFloat, "DG");
   const at::cuda::CUDAGuard guard(X.device());
-  check(maloq::gate_l_bwd((int)L, X.data_ptr<float>(), Gt.data_ptr<float>(), DO.data_ptr<float>(), DX.data_ptr<float>(),
-                          DG.data_ptr<float>(), (int)X.size(0), (int)X.size(2), stream()));
+  check(maloq::gate_l_bwd((int)L, X.data_ptr(), Gt.data_ptr<float>(), DO.data_ptr(), DX.data_ptr(),
+                          DG.data_ptr<float>(), b16, (int)X.size(0), (int)X.size(2), stream()));
 }
 
 
@@ -433,7 +469,9 @@ bool bounds_checked() { return maloq::bounds_checked(); }
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
-  m.def("gemm", &gemm, "grouped tcgen05 bf16 GEMM");
+  m.def("gemm", &gemm, "grouped tcgen05 bf16 GEMM", py::arg("As"), py::arg("Bs"), py::arg("Cs"), py::arg("biases"),
+        py::arg("mn_major"), py::arg("act"), py::arg("alpha"), py::arg("splits"), py::arg("bn"),
+        py::arg("resids") = std::vector<c10::optional<at::Tensor>>());
   m.def("splitk_reduce", &splitk_reduce, "sum split-K partials");
   m.def("gather_rotate_fwd", &gather_rotate_fwd);
   m.def("gather_rotate_bwd", &gather_rotate_bwd);

@@ -10,7 +10,9 @@
 //   moving 2 (w-1)/w of the bucket over NVLink.
 // * allreduce_multimem: the same with NVLink SHARP: one multimem.ld_reduce per vector returns
 //   the sum over all ranks (reduced in the switch) and one multimem.st writes it to all ranks.
-// Usage per bucket: barrier(epoch) -> allreduce -> barrier(epoch + 1), all on one stream.
+// Both keep AR_UNROLL vectors per thread in flight.  Usage per bucket, as it becomes ready:
+// peer_barrier(epoch) (every rank finished writing the bucket) -> allreduce; one more
+// peer_barrier after the step's last bucket, before any rank reads or reuses the buffers.
 #include "common.cuh"
 #include "comm.h"
 
@@ -45,62 +47,88 @@ __global__ void peer_barrier_kernel(uint32_t* const* __restrict__ pads, int rank
   __syncthreads();
 }
 
-__global__ void allreduce_p2p_kernel(float* const* __restrict__ bufs, int rank, int world, long long off, long long n,
-                                     float scale) {
+constexpr int AR_UNROLL = 4;  // float4 vectors per thread in flight
+
+__global__ void __launch_bounds__(256) allreduce_p2p_kernel(float* const* __restrict__ bufs, int rank, int world,
+                                                            long long off, long long n, float scale) {
   const long long chunk = ((n + world - 1) / world + 3) / 4 * 4;
   const long long c0 = off + rank * chunk;
   const long long c1 = off + (rank + 1) * chunk < off + n ? off + (rank + 1) * chunk : off + n;
   const long long nvec = (c1 - c0) / 4;
-  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < nvec; v += (long long)gridDim.x * blockDim.x) {
-    const long long i = c0 + 4 * v;
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long v0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; v0 < nvec; v0 += stride * AR_UNROLL) {
+    float4 s[AR_UNROLL];
+#pragma unroll
+    for (int u = 0; u < AR_UNROLL; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int p = 0; p < world; ++p) {
-      const float4 x = *reinterpret_cast<const float4*>(bufs[p] + i);
-      s.x += x.x;
-      s.y += x.y;
-      s.z += x.z;
-      s.w += x.w;
+      float4 x[AR_UNROLL];
+#pragma unroll
+      for (int u = 0; u < AR_UNROLL; ++u) {
+        const long long v = v0 + u * stride;
+        x[u] = v < nvec ? *reinterpret_cast<const float4*>(bufs[p] + c0 + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < AR_UNROLL; ++u) {
+        s[u].x += x[u].x;
+        s[u].y += x[u].y;
+        s[u].z += x[u].z;
+        s[u].w += x[u].w;
+      }
     }
-    s.x *= scale;
-    s.y *= scale;
-    s.z *= scale;
-    s.w *= scale;
-    for (int p = 0; p < world; ++p) *reinterpret_cast<float4*>(bufs[p] + i) = s;
+#pragma unroll
+    for (int u = 0; u < AR_UNROLL; ++u) {
+      s[u].x *= scale;
+      s[u].y *= scale;
+      s[u].z *= scale;
+      s[u].w *= scale;
+    }
+    for (int p = 0; p < world; ++p)
+#pragma unroll
+      for (int u = 0; u < AR_UNROLL; ++u) {
+        const long long v = v0 + u * stride;
+        if (v < nvec) *reinterpret_cast<float4*>(bufs[p] + c0 + 4 * v) = s[u];
+      }
   }
   // scalar tail of the chunk
   const long long tail0 = c0 + 4 * nvec;
-  for (long long i = tail0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < c1;
-       i += (long long)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int p = 0; p < world; ++p) s += bufs[p][i];
-    s *= scale;
-    for (int p = 0; p < world; ++p) bufs[p][i] = s;
+  for (long long i = tail0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < c1; i += stride) {
+    float sum = 0.f;
+    for (int p = 0; p < world; ++p) sum += bufs[p][i];
+    sum *= scale;
+    for (int p = 0; p < world; ++p) bufs[p][i] = sum;
   }
 }
 
-__global__ void allreduce_multimem_kernel(float* mc, int rank, int world, long long off, long long n, float scale) {
+__global__ void __launch_bounds__(256) allreduce_multimem_kernel(float* mc, int rank, int world, long long off,
+                                                                 long long n, float scale) {
   const long long chunk = ((n + world - 1) / world + 3) / 4 * 4;
   const long long c0 = off + rank * chunk;
   const long long c1 = off + (rank + 1) * chunk < off + n ? off + (rank + 1) * chunk : off + n;
   const long long nvec = (c1 - c0) / 4;
-  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < nvec; v += (long long)gridDim.x * blockDim.x) {
-    float* p = mc + c0 + 4 * v;
-    float a, b, c, d;
-    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(a), "=f"(b), "=f"(c), "=f"(d)
-                 : "l"(p)
-                 : "memory");
-    a *= scale;
-    b *= scale;
-    c *= scale;
-    d *= scale;
-    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-                 "f"(d)
-                 : "memory");
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long v0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; v0 < nvec; v0 += stride * AR_UNROLL) {
+    float r[AR_UNROLL][4];
+#pragma unroll
+    for (int u = 0; u < AR_UNROLL; ++u) {
+      const long long v = v0 + u * stride;
+      if (v < nvec) {
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(r[u][0]), "=f"(r[u][1]), "=f"(r[u][2]), "=f"(r[u][3])
+                     : "l"(mc + c0 + 4 * v)
+                     : "memory");
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < AR_UNROLL; ++u) {
+      const long long v = v0 + u * stride;
+      if (v < nvec)
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc + c0 + 4 * v),
+                     "f"(r[u][0] * scale), "f"(r[u][1] * scale), "f"(r[u][2] * scale), "f"(r[u][3] * scale)
+                     : "memory");
+    }
   }
   const long long tail0 = c0 + 4 * nvec;
-  for (long long i = tail0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < c1;
-       i += (long long)gridDim.x * blockDim.x) {
+  for (long long i = tail0 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < c1; i += stride) {
     float a;
     asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(a) : "l"(mc + i) : "memory");
     a *= scale;
@@ -120,25 +148,24 @@ const char* peer_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_
   return comm_err();
 }
 
+static int ar_blocks(long long n, int world) {
+  const long long per = (n + world - 1) / world / 4 + 1;
+  long long blocks = (per + 256 * AR_UNROLL - 1) / (256 * AR_UNROLL);
+  if (blocks > 148 * 2) blocks = 148 * 2;
+  return blocks < 1 ? 1 : (int)blocks;
+}
+
 const char* allreduce_p2p(float* const* bufs_dev, int rank, int world, long long off, long long n, float scale,
                           cudaStream_t st) {
   if (n == 0) return nullptr;
-  const long long per = (n + world - 1) / world / 4 + 1;
-  int blocks = (int)((per + 255) / 256);
-  if (blocks > 148 * 2) blocks = 148 * 2;
-  if (blocks < 1) blocks = 1;
-  allreduce_p2p_kernel<<<blocks, 256, 0, st>>>(bufs_dev, rank, world, off, n, scale);
+  allreduce_p2p_kernel<<<ar_blocks(n, world), 256, 0, st>>>(bufs_dev, rank, world, off, n, scale);
   return comm_err();
 }
 
 const char* allreduce_multimem(float* mc, int rank, int world, long long off, long long n, float scale,
                                cudaStream_t st) {
   if (n == 0) return nullptr;
-  const long long per = (n + world - 1) / world / 4 + 1;
-  int blocks = (int)((per + 255) / 256);
-  if (blocks > 148 * 2) blocks = 148 * 2;
-  if (blocks < 1) blocks = 1;
-  allreduce_multimem_kernel<<<blocks, 256, 0, st>>>(mc, rank, world, off, n, scale);
+  allreduce_multimem_kernel<<<ar_blocks(n, world), 256, 0, st>>>(mc, rank, world, off, n, scale);
   return comm_err();
 }
 

@@ -7,6 +7,7 @@ namespace maloq {
 
 const char* peer_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t epoch, int slot_base,
                          long long spin_limit, cudaStream_t st);
+// Bucket all-reduce: sum * scale of elements [off, off + n) over ranks, in place.
 const char* allreduce_p2p(float* const* bufs_dev, int rank, int world, long long off, long long n, float scale,
                           cudaStream_t st);
 const char* allreduce_multimem(float* mc, int rank, int world, long long off, long long n, float scale,

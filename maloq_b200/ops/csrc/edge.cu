@@ -36,99 +36,235 @@ __device__ __forceinline__ const float* src_row(const float* X, long long s, int
 
 // ---------------------------------------------------------------- gather + rotate + modulate
 // A[e, k, c'] = rad[e, slot(k)*Cin + c'] * sum_{j in degree l_k} rot[e,k,j] * in[e, j, c']
-// in = [X[src] | X[dst] | XE[e]] along channels (Cin = 2C or 3C).
+// in = [X[src] | X[dst] | XE[e]] along channels (Cin = 2C or 3C); rad is bf16.
+// Edge-parallel: Q edge lanes per CTA, two adjacent channels per thread (C even).
+template <int S>
+struct EdgeLanes {
+  static constexpr int Q = S <= 25 ? 4 : 2;
+};
+
 template <int L, int MM>
-__global__ void __launch_bounds__(128) gather_rotate_fwd_kernel(
+__global__ void __launch_bounds__(256) gather_rotate_fwd_kernel(
     const float* __restrict__ X, const float* __restrict__ XE, const long long* __restrict__ src,
-    const long long* __restrict__ dst, const float* __restrict__ rot, const float* __restrict__ rad,
+    const long long* __restrict__ dst, const float* __restrict__ rot, const __nv_bfloat16* __restrict__ rad,
     __nv_bfloat16* __restrict__ A, int E, int C, int Cin, const HaloRef H) {
   using F = Frame<L, MM>;
-  constexpr int S = F::S, R = F::R;
-  const int e = blockIdx.x;
-  const int cp = blockIdx.y * blockDim.x + threadIdx.x;
+  constexpr int S = F::S, R = F::R, Q = EdgeLanes<S>::Q;
+  const int cpair = threadIdx.x % 64, q = threadIdx.x / 64;
+  const long long e = (long long)blockIdx.x * Q + q;
+  const int cp = 2 * (blockIdx.y * 64 + cpair);
   if (e >= E || cp >= Cin) return;
   if (!MALOQ_IN_BOUNDS(src[e] >= 0 && src[e] < H.n_src && dst[e] >= 0 && dst[e] < H.n_dst)) return;
   const float* base;
   if (cp < C) base = src_row(X, src[e], S, C, H) + cp;
   else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
   else base = XE + (size_t)e * S * C + (cp - 2 * C);
-  float in[S];
+  float2 in[S];
 #pragma unroll
-  for (int j = 0; j < S; ++j) in[j] = __ldg(base + (size_t)j * C);
+  for (int j = 0; j < S; ++j) in[j] = __ldg(reinterpret_cast<const float2*>(base + (size_t)j * C));
   const float* re = rot + (size_t)e * R * S;
-  const float* rd = rad ? rad + (size_t)e * F::NS * Cin + cp : nullptr;
+  const __nv_bfloat16* rd = rad ? rad + (size_t)e * F::NS * Cin + cp : nullptr;
   __nv_bfloat16* out = A + (size_t)e * R * Cin + cp;
 #pragma unroll
   for (int k = 0; k < R; ++k) {
     const int l = F::row_l(k);
-    float acc = 0.f;
+    float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int j = l * l; j < (l + 1) * (l + 1); ++j) acc += __ldg(re + k * S + j) * in[j];
-    if (rd) acc *= __ldg(rd + (size_t)F::slot(k) * Cin);
-    out[(size_t)k * Cin] = __float2bfloat16_rn(acc);
+    for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
+      const float r = __ldg(re + k * S + j);
+      acc.x += r * in[j].x;
+      acc.y += r * in[j].y;
+    }
+    if (rd) {
+      const float2 m = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(rd + (size_t)F::slot(k) * Cin));
+      acc.x *= m.x;
+      acc.y *= m.y;
+    }
+    *reinterpret_cast<__nv_bfloat162*>(out + (size_t)k * Cin) = __floats2bfloat162_rn(acc.x, acc.y);
   }
 }
 
-// Backward of gather_rotate, one thread per (edge, channel): u = rot . in (recomputed),
-// dU = dA * rad, dRAD[slot] = sum over the slot's rows of dA * u, d_in = rot^T dU.
-// d_in goes to DSRC[e] (channels of x[src]), DDST[e] (x[dst]) or DXE[e] (edge embedding).
-template <int L, int MM>
-__global__ void __launch_bounds__(128) gather_rotate_bwd_kernel(
-    const float* __restrict__ X, const float* __restrict__ XE, const long long* __restrict__ src,
-    const long long* __restrict__ dst, const float* __restrict__ rot, const float* __restrict__ rad,
-    const __nv_bfloat16* __restrict__ dA, float* __restrict__ DSRC, float* __restrict__ DDST,
-    float* __restrict__ DXE, float* __restrict__ DRAD, int E, int C, int Cin, const HaloRef H) {
+// V adjacent channels (V = 1 or 2) loaded to / stored from fp32 registers v[0..V).
+template <int V>
+__device__ __forceinline__ void ldv(float* v, const float* p) {
+  if constexpr (V == 2) {
+    const float2 t = __ldg(reinterpret_cast<const float2*>(p));
+    v[0] = t.x;
+    v[1] = t.y;
+  } else {
+    v[0] = __ldg(p);
+  }
+}
+template <int V>
+__device__ __forceinline__ void ldv(float* v, const __nv_bfloat16* p) {
+  if constexpr (V == 2) {
+    const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+    v[0] = t.x;
+    v[1] = t.y;
+  } else {
+    v[0] = __bfloat162float(*p);
+  }
+}
+template <int V>
+__device__ __forceinline__ void stv(float* p, const float* v) {
+  if constexpr (V == 2) *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  else *p = v[0];
+}
+template <int V>
+__device__ __forceinline__ void stv(__nv_bfloat16* p, const float* v) {
+  if constexpr (V == 2) *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v[0], v[1]);
+  else *p = __float2bfloat16_rn(v[0]);
+}
+
+// One m-major row K (and its -m partner) of the backward of gather_rotate, with the frame's
+// row structure folded at compile time (template recursion over K).
+template <int L, int MM, int V, int K>
+__device__ __forceinline__ void gather_rotate_bwd_rows(const float* __restrict__ re, const float* g, const float* r,
+                                                       bool has_rad, __nv_bfloat16* __restrict__ drd, int Cin,
+                                                       const float* in, float* din) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S;
+  if constexpr (K < F::R) {
+    if constexpr (F::leads(K)) {
+      constexpr int KP = F::pair(K), l = F::row_l(K), SL = F::slot(K);
+      constexpr int NQ = KP < 0 ? 1 : 2;
+      float dr[V];
+#pragma unroll
+      for (int i = 0; i < V; ++i) dr[i] = 0.f;
+#pragma unroll
+      for (int qq = 0; qq < NQ; ++qq) {
+        const int kk = qq == 0 ? K : KP;
+#pragma unroll
+        for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
+          const float rv = __ldg(re + kk * S + j);
+#pragma unroll
+          for (int i = 0; i < V; ++i) {
+            const float gk = g[kk * V + i];
+            dr[i] += gk * rv * in[j * V + i];
+            din[j * V + i] += rv * (gk * r[SL * V + i]);
+          }
+        }
+      }
+      if (has_rad) stv<V>(drd + (size_t)SL * Cin, dr);
+    }
+    gather_rotate_bwd_rows<L, MM, V, K + 1>(re, g, r, has_rad, drd, Cin, in, din);
+  }
+}
+
+// One edge's contribution to the backward of gather_rotate for V channels at offset `off` of
+// the Cin channels (in/din: [S][V] registers): u = rot . in (recomputed), dU = dA * rad,
+// dRAD[slot] = sum over the slot's rows of dA * u (written), din += rot^T dU.
+template <int L, int MM, int V>
+__device__ __forceinline__ void gather_rotate_bwd_edge(const float* __restrict__ re, const __nv_bfloat16* __restrict__ ga,
+                                                       const __nv_bfloat16* __restrict__ rd,
+                                                       __nv_bfloat16* __restrict__ drd, int Cin, const float* in,
+                                                       float* din) {
+  using F = Frame<L, MM>;
+  constexpr int R = F::R;
+  float g[R * V], r[F::NS * V];
+#pragma unroll
+  for (int k = 0; k < R; ++k) ldv<V>(g + k * V, ga + (size_t)k * Cin);
+#pragma unroll
+  for (int sl = 0; sl < F::NS; ++sl) {
+    if (rd) ldv<V>(r + sl * V, rd + (size_t)sl * Cin);
+    else
+#pragma unroll
+      for (int i = 0; i < V; ++i) r[sl * V + i] = 1.f;
+  }
+  gather_rotate_bwd_rows<L, MM, V, 0>(re, g, r, rd != nullptr, drd, Cin, in, din);
+}
+
+// Node gradients of gather_rotate, one CTA per (node n of the source space, 64*V channels):
+// DX[n] = sum over n's incoming edges of the x[dst] part (channels C..2C) + sum over n's
+// outgoing edges (src CSR) of the x[src] part (channels 0..C), both recomputed from dA in a
+// fixed order (Q edge lanes of 64 threads, lane sums combined in shared memory) - no per-edge
+// gradient rows are stored.  Both parts use the node's own row X[n] (a peer row for halo
+// nodes).  The radial gradient DRAD of those channels is written per edge on the way.
+template <int L, int MM, int V, int Q>
+__global__ void __launch_bounds__(64 * Q) gather_rotate_bwd_nodes_kernel(
+    const float* __restrict__ X, const float* __restrict__ rot, const __nv_bfloat16* __restrict__ rad,
+    const __nv_bfloat16* __restrict__ dA, const long long* __restrict__ dst_ptr,
+    const long long* __restrict__ src_perm, const long long* __restrict__ src_ptr, float* __restrict__ DX,
+    __nv_bfloat16* __restrict__ DRAD, int N, int C, int Cin, long long E, const HaloRef H) {
   using F = Frame<L, MM>;
   constexpr int S = F::S, R = F::R;
-  const int e = blockIdx.x;
-  const int cp = blockIdx.y * blockDim.x + threadIdx.x;
-  if (e >= E || cp >= Cin) return;
-  if (!MALOQ_IN_BOUNDS(src[e] >= 0 && src[e] < H.n_src && dst[e] >= 0 && dst[e] < H.n_dst)) return;
-  float in[S];
-  if (rad) {
-    const float* base;
-    if (cp < C) base = src_row(X, src[e], S, C, H) + cp;
-    else if (cp < 2 * C) base = X + (size_t)dst[e] * S * C + (cp - C);
-    else base = XE + (size_t)e * S * C + (cp - 2 * C);
+  constexpr int LIST = 256;  // edge ids staged in shared memory per CTA
+  extern __shared__ float red_s[];  // [Q-1][S][64*V]
+  __shared__ long long elist[LIST];
+  const int n = blockIdx.x;
+  const int t = threadIdx.x % 64, q = threadIdx.x / 64;
+  const int c = V * (blockIdx.y * 64 + t);
+  const bool active = c < C;
+  const long long d0 = dst_ptr[n], nd = dst_ptr[n + 1] - d0;
+  const long long s0 = src_ptr[n], ns = src_ptr[n + 1] - s0;
+  const long long total = nd + ns;
+  // the node's edges: incoming (x[dst] part) then outgoing (x[src] part, through src_perm)
+  for (long long i = threadIdx.x; i < total && i < LIST; i += blockDim.x)
+    elist[i] = i < nd ? d0 + i : src_perm[s0 + i - nd];
+  __syncthreads();
+  float din[S * V];
 #pragma unroll
-    for (int j = 0; j < S; ++j) in[j] = __ldg(base + (size_t)j * C);
-  }
-  const float* re = rot + (size_t)e * R * S;
-  const float* rd = rad ? rad + (size_t)e * F::NS * Cin + cp : nullptr;
-  const __nv_bfloat16* ga = dA + (size_t)e * R * Cin + cp;
-  float din[S];
+  for (int j = 0; j < S * V; ++j) din[j] = 0.f;
+  if (active) {
+    float in[S * V];
+    const float* xr = src_row(X, n, S, C, H) + c;
 #pragma unroll
-  for (int j = 0; j < S; ++j) din[j] = 0.f;
-#pragma unroll
-  for (int k = 0; k < R; ++k) {
-    if (!F::leads(k)) continue;
-    const int kp = F::pair(k);
-    const int l = F::row_l(k);
-    const float r = rd ? __ldg(rd + (size_t)F::slot(k) * Cin) : 1.f;
-    float dr = 0.f;
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      if (q == 1 && kp < 0) continue;
-      const int kk = q == 0 ? k : kp;
-      const float g = bf2f(ga[(size_t)kk * Cin]);
-      if (rd) {
-        float u = 0.f;
-#pragma unroll
-        for (int j = l * l; j < (l + 1) * (l + 1); ++j) u += __ldg(re + kk * S + j) * in[j];
-        dr += g * u;
-      }
-      const float du = g * r;
-#pragma unroll
-      for (int j = l * l; j < (l + 1) * (l + 1); ++j) din[j] += __ldg(re + kk * S + j) * du;
+    for (int j = 0; j < S; ++j) ldv<V>(in + j * V, xr + (size_t)j * C);
+#pragma unroll 1
+    for (long long i = q; i < total; i += Q) {
+      const long long e = i < LIST ? elist[i] : (i < nd ? d0 + i : src_perm[s0 + i - nd]);
+      const int off = i < nd ? C : 0;
+      if (!MALOQ_IN_BOUNDS(e >= 0 && e < E)) continue;
+      const size_t eo = (size_t)e * F::NS * Cin + off + c;
+      gather_rotate_bwd_edge<L, MM, V>(rot + (size_t)e * R * S, dA + (size_t)e * R * Cin + off + c,
+                                       rad ? rad + eo : nullptr, DRAD ? DRAD + eo : nullptr, Cin, in, din);
     }
-    if (rd) DRAD[(size_t)e * F::NS * Cin + (size_t)F::slot(k) * Cin + cp] = dr;
   }
-  float* o;
-  if (cp < C) o = DSRC + (size_t)e * S * C + cp;
-  else if (cp < 2 * C) o = DDST + (size_t)e * S * C + (cp - C);
-  else o = DXE + (size_t)e * S * C + (cp - 2 * C);
+  if (q > 0) {
 #pragma unroll
-  for (int j = 0; j < S; ++j) o[(size_t)j * C] = din[j];
+    for (int j = 0; j < S; ++j)
+#pragma unroll
+      for (int i = 0; i < V; ++i) red_s[((q - 1) * S + j) * 64 * V + i * 64 + t] = din[j * V + i];
+  }
+  __syncthreads();
+  if (q > 0 || !active) return;
+#pragma unroll
+  for (int p = 0; p < Q - 1; ++p)
+#pragma unroll
+    for (int j = 0; j < S; ++j)
+#pragma unroll
+      for (int i = 0; i < V; ++i) din[j * V + i] += red_s[(p * S + j) * 64 * V + i * 64 + t];
+  float* o = DX + (size_t)n * S * C + c;
+#pragma unroll
+  for (int j = 0; j < S; ++j) stv<V>(o + (size_t)j * C, din + j * V);
+}
+
+// Edge-embedding part of the gather_rotate backward (Cin = 3C): DXE[e] (channels 2C..3C) and
+// those channels of DRAD, edge-parallel.
+template <int L, int MM>
+__global__ void __launch_bounds__(256) gather_rotate_bwd_edges_kernel(
+    const float* __restrict__ XE, const float* __restrict__ rot, const __nv_bfloat16* __restrict__ rad,
+    const __nv_bfloat16* __restrict__ dA, float* __restrict__ DXE, __nv_bfloat16* __restrict__ DRAD, int E, int C,
+    int Cin) {
+  using F = Frame<L, MM>;
+  constexpr int S = F::S, R = F::R, Q = EdgeLanes<S>::Q;
+  const int cpair = threadIdx.x % 64, q = threadIdx.x / 64;
+  const long long e = (long long)blockIdx.x * Q + q;
+  const int c = 2 * (blockIdx.y * 64 + cpair);
+  if (e >= E || c >= C) return;
+  float in[S * 2], din[S * 2];
+  const float* xr = XE + (size_t)e * S * C + c;
+#pragma unroll
+  for (int j = 0; j < S; ++j) {
+    ldv<2>(in + 2 * j, xr + (size_t)j * C);
+    din[2 * j] = din[2 * j + 1] = 0.f;
+  }
+  const size_t eo = (size_t)e * F::NS * Cin + 2 * C + c;
+  gather_rotate_bwd_edge<L, MM, 2>(rot + (size_t)e * R * S, dA + (size_t)e * R * Cin + 2 * C + c,
+                                   rad ? rad + eo : nullptr, DRAD ? DRAD + eo : nullptr, Cin, in, din);
+  float* o = DXE + (size_t)e * S * C + c;
+#pragma unroll
+  for (int j = 0; j < S; ++j) stv<2>(o + (size_t)j * C, din + 2 * j);
 }
 
 // DX[n] = sum_{e: dst=n} DDST[e] + sum_{e: src=n} DSRC[e], both in fixed (CSR) order.
@@ -273,11 +409,6 @@ __global__ void __launch_bounds__(128) rotate_grad_kernel(const float* __restric
 // per rotation entry) and Q edges in flight per CTA (Q "edge lanes" of 64 channel pairs).  Used
 // when C, ldy and koff are even.  Node paths walk a destination's edges through its CSR range;
 // the lanes' partial sums are combined in shared memory in a fixed order (deterministic).
-template <int S>
-struct EdgeLanes {
-  static constexpr int Q = S <= 25 ? 4 : 2;
-};
-
 template <int L, int MM>
 __global__ void __launch_bounds__(256) rotate_back_scatter2_kernel(
     const __nv_bfloat16* __restrict__ Y, int ldy, int koff, const float* __restrict__ rot,
@@ -504,29 +635,62 @@ static const char* last_error() {
 static inline int clampm(int L, int MM) { return MM > L ? L : MM; }
 
 const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
-                                   const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
-                                   int C, int Cin, const float* const* peers, const int* halo_owner,
-                                   const long long* halo_row, long long n_own, long long n_x_rows, long long n_halo,
-                                   cudaStream_t st) {
+                                   const long long* dst, const float* rot, const __nv_bfloat16* rad,
+                                   __nv_bfloat16* A, int E, int C, int Cin, const float* const* peers,
+                                   const int* halo_owner, const long long* halo_row, long long n_own,
+                                   long long n_x_rows, long long n_halo, cudaStream_t st) {
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
+  if (C % 2 != 0) return "gather_rotate: channel count must be even";
   const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows};
-  dim3 grid(E, (Cin + 127) / 128);
-  MALOQ_DISPATCH_FRAME(
-      (gather_rotate_fwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, A, E, C, Cin, H)))
+  MALOQ_DISPATCH_FRAME(({
+    constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
+    dim3 grid((E + Q_ - 1) / Q_, (Cin / 2 + 63) / 64);
+    gather_rotate_fwd_kernel<FL, FM><<<grid, 64 * Q_, 0, st>>>(X, XE, src, dst, rot, rad, A, E, C, Cin, H);
+  }))
 }
 
-const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const long long* src,
-                                   const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
-                                   float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
-                                   const float* const* peers, const int* halo_owner, const long long* halo_row,
-                                   long long n_own, long long n_x_rows, long long n_halo, cudaStream_t st) {
+static const char* gather_rotate_bwd_nodes(int L, int MM, const float* X, const float* rot,
+                                           const __nv_bfloat16* rad, const __nv_bfloat16* dA,
+                                           const long long* dst_ptr, const long long* src_perm,
+                                           const long long* src_ptr, float* DX, __nv_bfloat16* DRAD, int N, int E,
+                                           int C, int Cin, const HaloRef& H, cudaStream_t st) {
+  constexpr int V = 1, Q = 4;
+  MALOQ_DISPATCH_FRAME(({
+    constexpr int S_ = (FL + 1) * (FL + 1);
+    dim3 grid(N, (C / V + 63) / 64);
+    gather_rotate_bwd_nodes_kernel<FL, FM, V, Q><<<grid, 64 * Q, (Q - 1) * S_ * 64 * V * sizeof(float), st>>>(
+        X, rot, rad, dA, dst_ptr, src_perm, src_ptr, DX, DRAD, N, C, Cin, E, H);
+  }))
+}
+
+static const char* gather_rotate_bwd_edges(int L, int MM, const float* XE, const float* rot,
+                                           const __nv_bfloat16* rad, const __nv_bfloat16* dA, float* DXE,
+                                           __nv_bfloat16* DRAD, int E, int C, int Cin, cudaStream_t st) {
+  MALOQ_DISPATCH_FRAME(({
+    constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
+    dim3 grid((E + Q_ - 1) / Q_, (C / 2 + 63) / 64);
+    gather_rotate_bwd_edges_kernel<FL, FM><<<grid, 64 * Q_, 0, st>>>(XE, rot, rad, dA, DXE, DRAD, E, C, Cin);
+  }))
+}
+
+const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const float* rot,
+                                   const __nv_bfloat16* rad, const __nv_bfloat16* dA, const long long* dst_ptr,
+                                   const long long* src_perm, const long long* src_ptr, float* DX, float* DXE,
+                                   __nv_bfloat16* DRAD, int N, int E, int C, int Cin, const float* const* peers,
+                                   const int* halo_owner, const long long* halo_row, long long n_own,
+                                   long long n_x_rows, long long n_halo, cudaStream_t st) {
   MM = clampm(L, MM);
-  if (E == 0) return nullptr;
+  if (C % 2 != 0) return "gather_rotate: channel count must be even";
+  if (Cin == 3 * C && (XE == nullptr || DXE == nullptr)) return "gather_rotate_bwd: edge part needs XE and DXE";
   const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows};
-  dim3 grid(E, (Cin + 127) / 128);
-  MALOQ_DISPATCH_FRAME((gather_rotate_bwd_kernel<FL, FM><<<grid, 128, 0, st>>>(X, XE, src, dst, rot, rad, dA, DSRC,
-                                                                                DDST, DXE, DRAD, E, C, Cin, H)))
+  if (N > 0) {
+    const char* err = gather_rotate_bwd_nodes(L, MM, X, rot, rad, dA, dst_ptr, src_perm, src_ptr, DX, DRAD, N, E, C,
+                                              Cin, H, st);
+    if (err) return err;
+  }
+  if (E > 0 && Cin == 3 * C) return gather_rotate_bwd_edges(L, MM, XE, rot, rad, dA, DXE, DRAD, E, C, Cin, st);
+  return nullptr;
 }
 
 const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,

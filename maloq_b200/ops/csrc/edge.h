@@ -7,16 +7,20 @@ namespace maloq {
 
 // peers/halo_owner/halo_row/n_own: optional halo (source rows >= n_own read from peers'
 // staging buffers); pass peers = nullptr when every source row is local.
+// rad / DRAD: radial modulation [E, NS*Cin] bf16 (nullptr: no modulation).
 const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* XE, const long long* src,
-                                   const long long* dst, const float* rot, const float* rad, __nv_bfloat16* A, int E,
-                                   int C, int Cin, const float* const* peers, const int* halo_owner,
-                                   const long long* halo_row, long long n_own, long long n_x_rows, long long n_halo,
-                                   cudaStream_t st);
-const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const long long* src,
-                                   const long long* dst, const float* rot, const float* rad, const __nv_bfloat16* dA,
-                                   float* DSRC, float* DDST, float* DXE, float* DRAD, int E, int C, int Cin,
-                                   const float* const* peers, const int* halo_owner, const long long* halo_row,
-                                   long long n_own, long long n_x_rows, long long n_halo, cudaStream_t st);
+                                   const long long* dst, const float* rot, const __nv_bfloat16* rad,
+                                   __nv_bfloat16* A, int E, int C, int Cin, const float* const* peers,
+                                   const int* halo_owner, const long long* halo_row, long long n_own,
+                                   long long n_x_rows, long long n_halo, cudaStream_t st);
+// Backward: DX [N, S, C] (N rows of the source space, written completely), DXE (Cin = 3C),
+// DRAD.  dst_ptr has N+1 entries (rows without incoming edges have empty ranges).
+const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const float* rot,
+                                   const __nv_bfloat16* rad, const __nv_bfloat16* dA, const long long* dst_ptr,
+                                   const long long* src_perm, const long long* src_ptr, float* DX, float* DXE,
+                                   __nv_bfloat16* DRAD, int N, int E, int C, int Cin, const float* const* peers,
+                                   const int* halo_owner, const long long* halo_row, long long n_own,
+                                   long long n_x_rows, long long n_halo, cudaStream_t st);
 const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, const long long* halo_row, float* out,
                             long long n_halo, int SC, cudaStream_t st);
 const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,

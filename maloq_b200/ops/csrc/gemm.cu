@@ -1,6 +1,9 @@
 // Grouped bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
-//   C[p] (M x N) = alpha * A[p] (M x K) * B[p]^T (K x N) (+ bias[N]) (act)
+//   C[p] (M x N) = alpha * A[p] (M x K) * B[p]^T (K x N) (+ bias[N]) (act) (+ R[p])
+//
+// R (optional, fp32 output only, no split-K) is a residual read in the epilogue: a row-major
+// [M, N] view with its own row stride, added after the activation.
 //
 // A and B are bf16 and either K-major (row-major [M,K] / [N,K]) or MN-major (row-major
 // [K,M] / [K,N], used for weight gradients where K is the edge dimension).  Up to eight
@@ -36,7 +39,9 @@ struct alignas(64) GemmProblemDev {
   CUtensorMap tc;  // output, 3-D {N, M, splits}, box {32, 32, 1}, swizzled
   void* c;
   const float* bias;
+  const float* resid;
   long long ldc;
+  long long ldr;
   long long split_stride;
   int M, N, K;
   int tiles_n;
@@ -64,7 +69,29 @@ struct EpiScalars {
   const float* bias;
   float alpha;
   int act, N, M;
+  const float* resid;
+  long long ldr;
 };
+
+// v[j] += R[row, col0 + j] (the residual of the lane's row; 32 consecutive floats)
+__device__ __forceinline__ void epilogue_residual(float* v, const EpiScalars& ep, int row, int col0) {
+  if (ep.resid == nullptr || row >= ep.M) return;
+  const float* r = ep.resid + (size_t)row * ep.ldr + col0;
+  if (col0 + 32 <= ep.N && (reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(r) + j);
+      v[4 * j] += t.x;
+      v[4 * j + 1] += t.y;
+      v[4 * j + 2] += t.z;
+      v[4 * j + 3] += t.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < ep.N) v[j] += __ldg(r + j);
+  }
+}
 
 // v[j] (column col0 + j of this lane's row) = act(alpha * v[j] + bias[col0 + j]); lane j loads
 // bias[col0 + j] and the row's 32 values are broadcast by shuffles.
@@ -227,7 +254,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++it) {
       const TileCoord tc = decode_tile(P, w, tiles_per_split, BN);
       const GemmProblemDev& pr = P.p[tc.pi];
-      const EpiScalars ep{pr.bias, P.alpha, P.act, pr.N, pr.M};
+      const EpiScalars ep{pr.bias, P.alpha, P.act, pr.N, pr.M, pr.resid, pr.ldr};
       const int k_begin = tc.split * pr.k_per_split;
       const bool have_k = min(pr.K, k_begin + pr.k_per_split) > k_begin;
       const int buf = it & 1;
@@ -251,6 +278,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
         epilogue_math(v, ep.alpha, ep, col0, lane);
+        epilogue_residual(v, ep, tc.m0 + quarter * 32 + lane, col0);
         // stage the warp's 32 x 32 chunk (row-major, 32*esz bytes per row) and TMA-store it
         // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
         const int ring = out32 ? 4 : 8;
@@ -416,7 +444,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
     for (int w = cluster; w < total_work; w += nclusters, ++it) {
       const TileCoord tc = decode_tile(P, w, total_work, BN, 256);
       const GemmProblemDev& pr = P.p[tc.pi];
-      const EpiScalars ep{pr.bias, P.alpha, P.act, pr.N, pr.M};
+      const EpiScalars ep{pr.bias, P.alpha, P.act, pr.N, pr.M, pr.resid, pr.ldr};
       const int buf = it & 1;
       if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, ERR_EPI_WAIT)) break;
       tc_fence_after();
@@ -433,6 +461,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
         const int col0 = tc.n0 + c0;
         if (col0 >= ep.N) continue;
         epilogue_math(v, ep.alpha, ep, col0, lane);
+        epilogue_residual(v, ep, row0 + lane, col0);
         // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
         const int ring = out32 ? 4 : 8;
         uint8_t* stg = stage_out + quarter * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
@@ -630,8 +659,11 @@ const char* gemm_launch(const GemmProblem* probs, int nprob, bool a_mn, bool b_m
     if (err) return err;
     err = make_out_map(&d.tc, g.c, g.M, g.N, g.ldc, g.split_stride, splits, out_fp32);
     if (err) return err;
+    if (g.resid != nullptr && (!out_fp32 || splits > 1)) return "gemm: a residual needs fp32 output and no split-K";
     d.c = g.c;
     d.bias = g.bias;
+    d.resid = g.resid;
+    d.ldr = g.ldr;
     d.ldc = g.ldc;
     d.split_stride = g.split_stride;
     d.M = g.M;

@@ -13,6 +13,8 @@ struct GemmProblem {
   long long ldc;
   long long split_stride;  // elements between split-K outputs
   const float* bias;   // [N] or nullptr
+  const float* resid = nullptr;  // fp32 [M, N] rows added in the epilogue (row stride ldr), or nullptr
+  long long ldr = 0;
   int M, N, K;
 };
 

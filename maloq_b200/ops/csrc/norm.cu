@@ -13,6 +13,12 @@
 
 namespace maloq {
 
+// fp32 / bf16 element access (activations that feed a bf16 GEMM are stored as bf16)
+__device__ __forceinline__ float ldf(const float* p) { return *p; }
+__device__ __forceinline__ float ldf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void stf(float* p, float v) { *p = v; }
+__device__ __forceinline__ void stf(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
 template <int NW>
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -35,11 +41,11 @@ __device__ __forceinline__ float degree_weight(int j) {
 }
 
 // ------------------------------------------------------------------ rms_norm_sh
-template <int L, int NW>
+template <int L, int NW, typename TO>
 __global__ void __launch_bounds__(NW * 32) rms_norm_fwd_kernel(const float* __restrict__ X,
                                                                const float* __restrict__ RES,
                                                                const float* __restrict__ aw,
-                                                               const float* __restrict__ ab, float* __restrict__ OUT,
+                                                               const float* __restrict__ ab, TO* __restrict__ OUT,
                                                                float* __restrict__ SUM, int B, int C, float eps) {
   constexpr int S = (L + 1) * (L + 1);
   __shared__ float red[NW];
@@ -71,7 +77,7 @@ __global__ void __launch_bounds__(NW * 32) rms_norm_fwd_kernel(const float* __re
         while ((l + 1) * (l + 1) <= j) ++l;
         float o = v[j] * r * __ldg(aw + l * C + c);
         if (j == 0) o += __ldg(ab + c);
-        OUT[base + (size_t)j * C] = o;
+        stf(OUT + base + (size_t)j * C, o);
       }
     }
   }
@@ -79,9 +85,9 @@ __global__ void __launch_bounds__(NW * 32) rms_norm_fwd_kernel(const float* __re
 
 // G: grad of OUT; GS (optional): grad flowing into the residual sum itself.
 // DX = d(sum); PART[blockIdx.x] += (d_aw [L+1, C], d_ab [C]).
-template <int L, int NW>
+template <int L, int NW, typename TG>
 __global__ void __launch_bounds__(NW * 32) rms_norm_bwd_kernel(const float* __restrict__ Sx,
-                                                               const float* __restrict__ G,
+                                                               const TG* __restrict__ G,
                                                                const float* __restrict__ GS,
                                                                const float* __restrict__ aw, float* __restrict__ DX,
                                                                float* __restrict__ PART, int B, int C, float eps) {
@@ -101,7 +107,7 @@ __global__ void __launch_bounds__(NW * 32) rms_norm_bwd_kernel(const float* __re
 #pragma unroll
     for (int j = 0; j < S; ++j) {
       f[j] = act ? Sx[base + (size_t)j * C] : 0.f;
-      g[j] = act ? G[base + (size_t)j * C] : 0.f;
+      g[j] = act ? ldf(G + base + (size_t)j * C) : 0.f;
     }
     const float mean0 = block_sum<NW>(f[0], red) / C;
     if (act) f[0] -= mean0;
@@ -257,47 +263,47 @@ __global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* __r
 
 // ------------------------------------------------------------------ gate (l-outer)
 // OUT[b,0,h] = silu(X[b,0,h]); OUT[b,j,h] = X[b,j,h] * tanh(Gt[b,(l_j-1)*H + h])
-template <int L>
-__global__ void gate_l_fwd_kernel(const float* __restrict__ X, const float* __restrict__ Gt, float* __restrict__ OUT,
-                                  int B, int H) {
-  constexpr int S = (L + 1) * (L + 1);
-  const long long total = (long long)B * H;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int h = (int)(i % H);
-    const long long b = i / H;
-    const float* x = X + b * S * H + h;
-    float* o = OUT + b * S * H + h;
-    o[0] = silu(x[0]);
-#pragma unroll
-    for (int l = 1; l <= L; ++l) {
-      const float t = tanhf(Gt[b * L * H + (l - 1) * H + h]);
-#pragma unroll
-      for (int j = l * l; j < (l + 1) * (l + 1); ++j) o[(size_t)j * H] = x[(size_t)j * H] * t;
-    }
-  }
-}
-
-template <int L>
-__global__ void gate_l_bwd_kernel(const float* __restrict__ X, const float* __restrict__ Gt,
-                                  const float* __restrict__ DO, float* __restrict__ DX, float* __restrict__ DG, int B,
+template <int L, typename T>
+__global__ void gate_l_fwd_kernel(const T* __restrict__ X, const float* __restrict__ Gt, T* __restrict__ OUT, int B,
                                   int H) {
   constexpr int S = (L + 1) * (L + 1);
   const long long total = (long long)B * H;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
     const int h = (int)(i % H);
     const long long b = i / H;
-    const float* x = X + b * S * H + h;
-    const float* d = DO + b * S * H + h;
-    float* dx = DX + b * S * H + h;
-    dx[0] = d[0] * dsilu(x[0]);
+    const T* x = X + b * S * H + h;
+    T* o = OUT + b * S * H + h;
+    stf(o, silu(ldf(x)));
+#pragma unroll
+    for (int l = 1; l <= L; ++l) {
+      const float t = tanhf(Gt[b * L * H + (l - 1) * H + h]);
+#pragma unroll
+      for (int j = l * l; j < (l + 1) * (l + 1); ++j) stf(o + (size_t)j * H, ldf(x + (size_t)j * H) * t);
+    }
+  }
+}
+
+template <int L, typename T>
+__global__ void gate_l_bwd_kernel(const T* __restrict__ X, const float* __restrict__ Gt, const T* __restrict__ DO,
+                                  T* __restrict__ DX, float* __restrict__ DG, int B, int H) {
+  constexpr int S = (L + 1) * (L + 1);
+  const long long total = (long long)B * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int h = (int)(i % H);
+    const long long b = i / H;
+    const T* x = X + b * S * H + h;
+    const T* d = DO + b * S * H + h;
+    T* dx = DX + b * S * H + h;
+    stf(dx, ldf(d) * dsilu(ldf(x)));
 #pragma unroll
     for (int l = 1; l <= L; ++l) {
       const float t = tanhf(Gt[b * L * H + (l - 1) * H + h]);
       float acc = 0.f;
 #pragma unroll
       for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
-        dx[(size_t)j * H] = d[(size_t)j * H] * t;
-        acc += d[(size_t)j * H] * x[(size_t)j * H];
+        const float dv = ldf(d + (size_t)j * H);
+        stf(dx + (size_t)j * H, dv * t);
+        acc += dv * ldf(x + (size_t)j * H);
       }
       DG[b * L * H + (l - 1) * H + h] = acc * (1.f - t * t);
     }
@@ -334,19 +340,31 @@ int norm_grid(long long rows) { return (int)std::min<long long>(rows, 148 * 16);
   else if (C <= 256) { constexpr int NWW = 8; __VA_ARGS__; }   \
   else return "norm kernels: channels must be <= 256";
 
-const char* rms_norm_fwd(int L, const float* X, const float* RES, const float* aw, const float* ab, float* OUT,
-                         float* SUM, int B, int C, float eps, cudaStream_t st) {
+const char* rms_norm_fwd(int L, const float* X, const float* RES, const float* aw, const float* ab, void* OUT,
+                         bool out_bf16, float* SUM, int B, int C, float eps, cudaStream_t st) {
   if (B == 0) return nullptr;
   const int grid = norm_grid(B);
-  MALOQ_NW_CASES(C, MALOQ_DISPATCH_L((rms_norm_fwd_kernel<LL, NWW><<<grid, NWW * 32, 0, st>>>(X, RES, aw, ab, OUT, SUM,
-                                                                                               B, C, eps))))
+  if (out_bf16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(OUT);
+    MALOQ_NW_CASES(C, MALOQ_DISPATCH_L((rms_norm_fwd_kernel<LL, NWW, __nv_bfloat16><<<grid, NWW * 32, 0, st>>>(
+                          X, RES, aw, ab, o, SUM, B, C, eps))))
+  }
+  float* o = static_cast<float*>(OUT);
+  MALOQ_NW_CASES(C, MALOQ_DISPATCH_L((rms_norm_fwd_kernel<LL, NWW, float><<<grid, NWW * 32, 0, st>>>(X, RES, aw, ab, o,
+                                                                                                      SUM, B, C, eps))))
 }
 
-const char* rms_norm_bwd(int L, const float* Sx, const float* G, const float* GS, const float* aw, float* DX,
-                         float* PART, int B, int C, float eps, int grid, cudaStream_t st) {
+const char* rms_norm_bwd(int L, const float* Sx, const void* G, bool g_bf16, const float* GS, const float* aw,
+                         float* DX, float* PART, int B, int C, float eps, int grid, cudaStream_t st) {
   if (B == 0) return nullptr;
-  MALOQ_NW_CASES(C, MALOQ_DISPATCH_L((rms_norm_bwd_kernel<LL, NWW><<<grid, NWW * 32, 0, st>>>(Sx, G, GS, aw, DX, PART,
-                                                                                               B, C, eps))))
+  if (g_bf16) {
+    const __nv_bfloat16* g = static_cast<const __nv_bfloat16*>(G);
+    MALOQ_NW_CASES(C, MALOQ_DISPATCH_L((rms_norm_bwd_kernel<LL, NWW, __nv_bfloat16><<<grid, NWW * 32, 0, st>>>(
+                          Sx, g, GS, aw, DX, PART, B, C, eps))))
+  }
+  const float* g = static_cast<const float*>(G);
+  MALOQ_NW_CASES(C, MALOQ_DISPATCH_L((rms_norm_bwd_kernel<LL, NWW, float><<<grid, NWW * 32, 0, st>>>(Sx, g, GS, aw, DX,
+                                                                                                      PART, B, C, eps))))
 }
 
 #define MALOQ_VPT_CASES(W, ...)                                  \
@@ -373,17 +391,29 @@ const char* ln_silu_bwd(const float* X, const float* w, const float* b, const __
   return norm_err();
 }
 
-const char* gate_l_fwd(int L, const float* X, const float* Gt, float* OUT, int B, int H, cudaStream_t st) {
+const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st) {
   if (B == 0) return nullptr;
   const int grid = (int)std::min<long long>(((long long)B * H + 255) / 256, 148 * 32);
-  MALOQ_DISPATCH_L((gate_l_fwd_kernel<LL><<<grid, 256, 0, st>>>(X, Gt, OUT, B, H)))
+  if (bf16) {
+    MALOQ_DISPATCH_L((gate_l_fwd_kernel<LL, __nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(X), Gt, static_cast<__nv_bfloat16*>(OUT), B, H)))
+  }
+  MALOQ_DISPATCH_L((gate_l_fwd_kernel<LL, float><<<grid, 256, 0, st>>>(static_cast<const float*>(X), Gt,
+                                                                      static_cast<float*>(OUT), B, H)))
 }
 
-const char* gate_l_bwd(int L, const float* X, const float* Gt, const float* DO, float* DX, float* DG, int B, int H,
-                       cudaStream_t st) {
+const char* gate_l_bwd(int L, const void* X, const float* Gt, const void* DO, void* DX, float* DG, bool bf16, int B,
+                       int H, cudaStream_t st) {
   if (B == 0) return nullptr;
   const int grid = (int)std::min<long long>(((long long)B * H + 255) / 256, 148 * 32);
-  MALOQ_DISPATCH_L((gate_l_bwd_kernel<LL><<<grid, 256, 0, st>>>(X, Gt, DO, DX, DG, B, H)))
+  if (bf16) {
+    MALOQ_DISPATCH_L((gate_l_bwd_kernel<LL, __nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(X), Gt, static_cast<const __nv_bfloat16*>(DO),
+        static_cast<__nv_bfloat16*>(DX), DG, B, H)))
+  }
+  MALOQ_DISPATCH_L((gate_l_bwd_kernel<LL, float><<<grid, 256, 0, st>>>(static_cast<const float*>(X), Gt,
+                                                                      static_cast<const float*>(DO),
+                                                                      static_cast<float*>(DX), DG, B, H)))
 }
 
 }  // namespace maloq

@@ -6,18 +6,21 @@
 namespace maloq {
 
 int norm_grid(long long rows);
-const char* rms_norm_fwd(int L, const float* X, const float* RES, const float* aw, const float* ab, float* OUT,
-                         float* SUM, int B, int C, float eps, cudaStream_t st);
-// PART: [grid, L+2, C] partial (d_affine_weight, d_affine_bias) per CTA
-const char* rms_norm_bwd(int L, const float* Sx, const float* G, const float* GS, const float* aw, float* DX,
-                         float* PART, int B, int C, float eps, int grid, cudaStream_t st);
+// OUT: fp32, or bf16 when out_bf16 (an output that only feeds a bf16 GEMM)
+const char* rms_norm_fwd(int L, const float* X, const float* RES, const float* aw, const float* ab, void* OUT,
+                         bool out_bf16, float* SUM, int B, int C, float eps, cudaStream_t st);
+// G: gradient of OUT (fp32, or bf16 when g_bf16).  PART: [grid, L+2, C] partial
+// (d_affine_weight, d_affine_bias) per CTA
+const char* rms_norm_bwd(int L, const float* Sx, const void* G, bool g_bf16, const float* GS, const float* aw,
+                         float* DX, float* PART, int B, int C, float eps, int grid, cudaStream_t st);
 const char* ln_silu_fwd(const float* X, const float* w, const float* b, __nv_bfloat16* OUT, int M, int W, float eps,
                         cudaStream_t st);
 // PART: [grid * 8, 2, W] partial (d_weight, d_bias) per warp (256-thread CTAs)
 const char* ln_silu_bwd(const float* X, const float* w, const float* b, const __nv_bfloat16* G, float* DX, float* PART,
                         int M, int W, float eps, int grid, cudaStream_t st);
-const char* gate_l_fwd(int L, const float* X, const float* Gt, float* OUT, int B, int H, cudaStream_t st);
-const char* gate_l_bwd(int L, const float* X, const float* Gt, const float* DO, float* DX, float* DG, int B, int H,
-                       cudaStream_t st);
+// X / OUT / DO / DX: fp32, or bf16 when bf16; gates Gt and their gradient DG fp32
+const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st);
+const char* gate_l_bwd(int L, const void* X, const float* Gt, const void* DO, void* DX, float* DG, bool bf16, int B,
+                       int H, cudaStream_t st);
 
 }  // namespace maloq

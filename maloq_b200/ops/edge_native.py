@@ -3,6 +3,7 @@
 Forward (per layer, node or edge path):
 
 1. ``gather_rotate_fwd``: A = rad * rot . [x[src] | x[dst] (| x_edge)] -> bf16 [E, R*Cin]
+   (rad: the radial MLP's output, bf16 [E, NS*Cin])
 2. grouped tcgen05 GEMM, one problem per |m| (pair weights for m > 0) -> Y1 = [gates | m-major]
 3. ``gate_fwd`` -> H1 [E, R*H]
 4. grouped tcgen05 GEMM (second SO(2) conv) -> Y2 [E, R*C]
@@ -10,7 +11,9 @@ Forward (per layer, node or edge path):
    ``rotate_back_edge`` (edge path).
 
 Backward runs the transposed chain; weight gradients are deterministic split-K GEMMs over
-the edges, node gradients are fixed-order segmented sums (dst CSR, then src CSR).
+the edges; node gradients come out of one kernel that walks each node's incoming and
+outgoing edges in a fixed order and recomputes their contributions from dA (no per-edge
+gradient rows).
 Reference: ``helm/esen_block.py:146-258`` and ``helm/nn/so2_layers.py:139-214``.
 """
 
@@ -18,6 +21,7 @@ from __future__ import annotations
 
 import torch
 
+from . import weights as W
 from .native import count_launches
 
 
@@ -96,6 +100,8 @@ def _weight_grads(gys, xs):
 class EdgewiseFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_node, x_edge_emb, rad, b1, b2, graph, meta, halo, *weights):
+        """``weights``: fc_m0.weight and the SO2_m_Conv fc.weight of each |m| > 0 (the pair
+        matrices are built from them in the bf16 weight cache) for both convolutions."""
         lib = _lib()
         nw = len(weights) // 2
         w1, w2 = weights[:nw], weights[nw:]
@@ -106,11 +112,11 @@ class EdgewiseFn(torch.autograd.Function):
         dev = x_node.device
         x_node = x_node.contiguous()
         xe = x_edge_emb.contiguous() if x_edge_emb is not None else None
-        rad = rad.contiguous().float()
+        rad = rad.to(torch.bfloat16).contiguous()
         A = torch.empty(E, R * Cin, device=dev, dtype=torch.bfloat16)
         lib.gather_rotate_fwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, A, Cin, *_halo_args(halo))
-        w1b = [w.to(torch.bfloat16).contiguous() for w in w1]
-        w2b = [w.to(torch.bfloat16).contiguous() for w in w2]
+        w1b = [W.bf16(w1[0])] + [W.pair_bf16(w) for w in w1[1:]]
+        w2b = [W.bf16(w2[0])] + [W.pair_bf16(w) for w in w2[1:]]
         Y1 = torch.empty(E, G + R * H, device=dev, dtype=torch.bfloat16)
         ab = _blocks(meta["m_size"], Cin)
         yb = _blocks(meta["m_size"], H, G)
@@ -131,7 +137,7 @@ class EdgewiseFn(torch.autograd.Function):
             out = torch.empty(E, S, C, device=dev, dtype=torch.float32)
             lib.rotate_back_edge(*LM, Y2, 0, R, graph.rot, out)
         count_launches(4)
-        ctx.save_for_backward(x_node, xe, rad, A, Y1, H1, *w1b, *w2b)
+        ctx.save_for_backward(x_node, xe, rad, A, Y1, H1, *weights)
         ctx.graph, ctx.meta, ctx.nw, ctx.halo = graph, meta, nw, halo
         return out
 
@@ -141,7 +147,9 @@ class EdgewiseFn(torch.autograd.Function):
         graph, meta, nw = ctx.graph, ctx.meta, ctx.nw
         saved = ctx.saved_tensors
         x_node, xe, rad, A, Y1, H1 = saved[:6]
-        w1b, w2b = saved[6:6 + nw], saved[6 + nw:]
+        w1, w2 = saved[6:6 + nw], saved[6 + nw:]
+        w1t = [W.bf16_t(w1[0])] + [W.pair_bf16_t(w) for w in w1[1:]]
+        w2t = [W.bf16_t(w2[0])] + [W.pair_bf16_t(w) for w in w2[1:]]
         S, C = x_node.shape[1], x_node.shape[2]
         R, H, L, Cin, G = meta["R"], meta["H"], meta["L"], meta["Cin"], meta["G"]
         LM = (meta["L"], meta["MM"])
@@ -156,8 +164,7 @@ class EdgewiseFn(torch.autograd.Function):
         yb = _blocks(meta["m_size"], H, G)
         # conv2
         dH1 = torch.empty(E, R * H, device=dev, dtype=torch.bfloat16)
-        _gemm([dY2[:, a0:a1] for a0, a1 in cb], [w.t().contiguous() for w in w2b], [dH1[:, h0:h1] for h0, h1 in hb],
-              [None] * nw)
+        _gemm([dY2[:, a0:a1] for a0, a1 in cb], w2t, [dH1[:, h0:h1] for h0, h1 in hb], [None] * nw)
         dw2 = _weight_grads([dY2[:, a0:a1] for a0, a1 in cb], [H1[:, h0:h1] for h0, h1 in hb])
         db2 = dY2[:, cb[0][0]:cb[0][1]].sum(0, dtype=torch.float32)
         # gate
@@ -165,24 +172,23 @@ class EdgewiseFn(torch.autograd.Function):
         lib.gate_bwd(*LM, Y1, dH1, dY1, H)
         # conv1
         dA = torch.empty(E, R * Cin, device=dev, dtype=torch.bfloat16)
-        _gemm([dY1[:, y0:y1] for y0, y1 in yb], [w.t().contiguous() for w in w1b], [dA[:, a0:a1] for a0, a1 in ab],
-              [None] * nw)
+        _gemm([dY1[:, y0:y1] for y0, y1 in yb], w1t, [dA[:, a0:a1] for a0, a1 in ab], [None] * nw)
         dw1 = _weight_grads([dY1[:, y0:y1] for y0, y1 in yb], [A[:, a0:a1] for a0, a1 in ab])
         db1 = dY1[:, yb[0][0]:yb[0][1]].sum(0, dtype=torch.float32)
-        # gather
+        # gather: node gradients straight from dA (fixed-order walks over each node's incoming
+        # and outgoing edges), the edge-embedding part per edge, the radial gradient per edge
         perm, sptr = src_csr(graph)
-        DSRC = torch.empty(E, S, C, device=dev, dtype=torch.float32)
-        DDST = torch.empty(E, S, C, device=dev, dtype=torch.float32)
-        DXE = torch.empty_like(xe) if xe is not None else None
-        DRAD = torch.empty_like(rad)
-        lib.gather_rotate_bwd(*LM, x_node, xe, graph.src, graph.dst, graph.rot, rad, dA, DSRC, DDST, DXE, DRAD, Cin,
-                              *_halo_args(ctx.halo))
         n_ext = graph.num_nodes_ext if ctx.halo is not None else x_node.shape[0]
         DX = torch.empty((n_ext,) + tuple(x_node.shape[1:]), device=dev, dtype=torch.float32)
-        lib.node_reduce(DDST, dst_ptr_ext(graph, n_ext), DSRC, perm, sptr, DX)
+        DXE = torch.empty_like(xe) if xe is not None else None
+        DRAD = torch.empty_like(rad)
+        lib.gather_rotate_bwd(*LM, x_node, xe, graph.rot, rad, dA, dst_ptr_ext(graph, n_ext), perm, sptr, DX, DXE,
+                              DRAD, Cin, *_halo_args(ctx.halo))
         if ctx.halo is not None:
             DX = ctx.halo[0].reduce_grads(DX)
-        count_launches(6)
+        count_launches(5 + (xe is not None))
+        dw1 = dw1[:1] + [W.pair_grad(d) for d in dw1[1:]]
+        dw2 = dw2[:1] + [W.pair_grad(d) for d in dw2[1:]]
         return (DX, DXE, DRAD, db1, db2, None, None, None, *dw1, *dw2)
 
 
@@ -197,7 +203,7 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
         meta = dict(R=mapping.res_size, H=c1.m_output_channels, L=mod.lmax, MM=mod.mmax, Cin=Cin,
                     G=c1.extra_m0_output_channels, m_size=list(mapping.m_size), node=node_or_edge == "node")
         graph.cache[key] = meta
-    rad = c1.rad_func(x_edge)
+    rad = c1.rad_func(x_edge, out_dtype=torch.bfloat16)
     halo = None
     x_src_space = x_node
     if graph.halo is not None:
@@ -206,7 +212,8 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
             halo = (peer, peer.publish(x_node))  # rows readable by every rank; slot id
         else:
             x_src_space = graph.halo.extend(x_node, graph)
-    weights = list(c1.gemm_weights()) + list(c2.gemm_weights())
+    weights = [c1.fc_m0.weight] + [c.fc.weight for c in c1.so2_m_conv] + \
+        [c2.fc_m0.weight] + [c.fc.weight for c in c2.so2_m_conv]
     return EdgewiseFn.apply(x_src_space, x_msg_edge, rad, c1.fc_m0.bias, c2.fc_m0.bias, graph, meta, halo, *weights)
 
 

@@ -11,6 +11,7 @@ import torch
 
 from . import _ext
 from . import reference as _ref
+from . import weights as W
 from .native import count_launches, register
 
 _lib = None
@@ -68,10 +69,11 @@ def _pad_cols(t, mult=8):
     return torch.nn.functional.pad(t, (0, mult - k % mult))
 
 
-def gemm_nt(a, w, bias=None, out_dtype=torch.float32, act=0, alpha=1.0, bn=None):
-    """out[M,N] = alpha * a[M,K] @ w[N,K]^T (+bias) (silu if act); bf16 operands."""
+def gemm_nt(a, w, bias=None, out_dtype=torch.float32, act=0, alpha=1.0, bn=None, w_bf16=None):
+    """out[M,N] = alpha * a[M,K] @ w[N,K]^T (+bias) (silu if act); bf16 operands.  ``w_bf16``:
+    a ready bf16 copy of ``w`` (the weight cache)."""
     a = _pad_cols(a.to(torch.bfloat16)).contiguous()
-    w = _pad_cols(w.to(torch.bfloat16))
+    w = _pad_cols(w_bf16 if w_bf16 is not None else w.to(torch.bfloat16))
     N = w.shape[0]
     if N % 8:
         w = torch.nn.functional.pad(w, (0, 0, 0, 8 - N % 8))
@@ -111,10 +113,10 @@ def gemm_tn_weight_grad(gy, x):
 
 class _Linear(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, bias):
+    def forward(ctx, x, weight, bias, out_dtype):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
-        y = gemm_nt(x2, weight, bias)
+        y = gemm_nt(x2, weight, bias, out_dtype=out_dtype, w_bf16=W.bf16(weight))
         ctx.save_for_backward(x2, weight)
         ctx.has_bias = bias is not None
         ctx.in_shape, ctx.in_dtype = shape, x.dtype
@@ -126,17 +128,17 @@ class _Linear(torch.autograd.Function):
         g2 = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16).contiguous()
         gx = gw = gb = None
         if ctx.needs_input_grad[0]:
-            gx = gemm_nt(g2, weight.t().contiguous()).to(ctx.in_dtype).reshape(ctx.in_shape)
+            gx = gemm_nt(g2, weight, w_bf16=W.bf16_t(weight)).to(ctx.in_dtype).reshape(ctx.in_shape)
         if ctx.needs_input_grad[1]:
             gw = gemm_tn_weight_grad(g2, x2)[: weight.shape[0], : weight.shape[1]]
         if ctx.has_bias and ctx.needs_input_grad[2]:
             gb = gy.reshape(-1, gy.shape[-1]).sum(0, dtype=torch.float32)
-        return gx, gw, gb
+        return gx, gw, gb, None
 
 
 @register("linear")
-def linear(x, weight, bias=None, act=None):
-    y = _Linear.apply(x, weight, bias)
+def linear(x, weight, bias=None, act=None, out_dtype=None):
+    y = _Linear.apply(x, weight, bias, out_dtype or torch.float32)
     if act == "silu":
         y = torch.nn.functional.silu(y)
     return y
@@ -163,10 +165,10 @@ def gate(gating_scalars, x, expand_index, lmax):
 
 
 @register("rms_norm_sh")
-def rms_norm_sh(x, aw, ab, eps, residual=None):
+def rms_norm_sh(x, aw, ab, eps, residual=None, out_dtype=None):
     from . import norm_native
 
-    return norm_native.rms_norm_sh(x, aw, ab, eps, residual)
+    return norm_native.rms_norm_sh(x, aw, ab, eps, residual, out_dtype)
 
 
 register("gather_scale")(_ref.gather_scale)
@@ -178,10 +180,10 @@ for _name in ("basis_transform", "matrix_to_labels", "labels_to_matrix", "blocks
 
 
 @register("so3_linear")
-def so3_linear(x, weight, bias, lmax):
+def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
     from . import norm_native
 
-    return norm_native.so3_linear(x, weight, bias, lmax)
+    return norm_native.so3_linear(x, weight, bias, lmax, out_dtype, residual)
 
 
 def _head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):

@@ -73,17 +73,23 @@ def bench_edge(edges):
     src = torch.randint(0, N, (edges,), device=dev)
     dst = torch.sort(torch.randint(0, N, (edges,), device=dev)).values
     rot = torch.randn(edges, R, S, device=dev)
-    rad = torch.randn(edges, 12 * Cin, device=dev)
+    rad = torch.randn(edges, 12 * Cin, device=dev).bfloat16()
     A = torch.empty(edges, R * Cin, device=dev, dtype=torch.bfloat16)
     ms = _timeit(lambda: lib.gather_rotate_fwd(4, 2, x, None, src, dst, rot, rad, A, Cin, 0, None, None, 0))
-    byt = edges * (S * Cin * 4 + R * S * 4 + 12 * Cin * 4 + R * Cin * 2)
+    # node rows come from L2 (N*S*C*4 bytes once); per edge: rotation, radial row, A row
+    byt = N * S * C * 4 + edges * (R * S * 4 + 12 * Cin * 2 + R * Cin * 2)
     print(f"gather_rotate_fwd: {ms * 1e3:.1f} us, {byt / ms / 1e9:.2f} TB/s algorithmic")
-    DS = torch.empty(edges, S, C, device=dev)
-    DD = torch.empty(edges, S, C, device=dev)
+    dptr = torch.zeros(N + 1, dtype=torch.long, device=dev)
+    dptr[1:] = torch.cumsum(torch.bincount(dst, minlength=N), 0)
+    perm = torch.argsort(src, stable=True)
+    sptr = torch.zeros(N + 1, dtype=torch.long, device=dev)
+    sptr[1:] = torch.cumsum(torch.bincount(src, minlength=N), 0)
+    DX = torch.empty(N, S, C, device=dev)
     DR = torch.empty_like(rad)
-    ms = _timeit(lambda: lib.gather_rotate_bwd(4, 2, x, None, src, dst, rot, rad, A, DS, DD, None, DR, Cin, 0, None,
-                                               None, 0))
-    byt = edges * (S * Cin * 4 * 2 + R * S * 4 + 12 * Cin * 4 * 2 + R * Cin * 2)
+    ms = _timeit(lambda: lib.gather_rotate_bwd(4, 2, x, None, rot, rad, A, dptr, perm, sptr, DX, None, DR, Cin, 0,
+                                               None, None, 0))
+    # per edge: rotation twice (both walks), radial row, dA row, radial gradient row
+    byt = N * S * C * 4 * 2 + edges * (2 * R * S * 4 + 12 * Cin * 2 * 2 + R * Cin * 2)
     print(f"gather_rotate_bwd: {ms * 1e3:.1f} us, {byt / ms / 1e9:.2f} TB/s algorithmic, "
           f"error_status={kernels.error_status()}")
 
@@ -145,9 +151,9 @@ def suite_calls(edges=43408, device="cuda"):
     flat = torch.cat([J.reshape(-1).float() for J in Js]).to(dev)
     joff = [sum((2 * k + 1) ** 2 for k in range(l)) for l in range(L + 1)]
     rot = torch.empty(E, R, S, device=dev)
-    rad = torch.randn(E, 12 * Cin, device=dev)
+    rad = torch.randn(E, 12 * Cin, device=dev).bfloat16()
     A = torch.empty(E, R * Cin, device=dev, dtype=torch.bfloat16)
-    DS, DD, DR = torch.empty(E, S, C, device=dev), torch.empty(E, S, C, device=dev), torch.empty_like(rad)
+    DR = torch.empty_like(rad)
     DX = torch.empty(N, S, C, device=dev)
     G = 4 * H  # gate scalars of the m = 0 block
     Y1 = torch.randn(E, G + R * H, device=dev).bfloat16()
@@ -227,9 +233,8 @@ def suite_calls(edges=43408, device="cuda"):
         ("splitk_reduce", lambda: lib.splitk_reduce(part, wout, 0.0)),
         ("gather_rotate_fwd", lambda: lib.gather_rotate_fwd(L, MM, x, None, src, dst, rot, rad, A, Cin, 0, None, None,
                                                             0)),
-        ("gather_rotate_bwd", lambda: lib.gather_rotate_bwd(L, MM, x, None, src, dst, rot, rad, A, DS, DD, None, DR,
-                                                            Cin, 0, None, None, 0)),
-        ("node_reduce", lambda: lib.node_reduce(DD, dst_ptr, DS, perm, sptr, DX)),
+        ("gather_rotate_bwd", lambda: lib.gather_rotate_bwd(L, MM, x, None, rot, rad, A, dst_ptr, perm, sptr, DX, None,
+                                                            DR, Cin, 0, None, None, 0)),
         ("gate_fwd", lambda: lib.gate_fwd(L, MM, Y1, H1, H)),
         ("gate_bwd", lambda: lib.gate_bwd(L, MM, Y1, H1, dY1, H)),
         ("rotate_back_scatter", lambda: lib.rotate_back_scatter(L, MM, Y2, 0, R, rot, dst_ptr, None, out_n, 1.0)),

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import torch
 
+from . import weights as W
 from .native import count_launches
 
 
@@ -27,12 +28,12 @@ def _partial_grid(rows):
 
 class _RmsNorm(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, res, aw, ab, eps):
+    def forward(ctx, x, res, aw, ab, eps, out_dtype):
         lib = _lib()
         L = aw.shape[0] - 1
         x = x.contiguous().float()
         res_c = res.contiguous().float() if res is not None else None
-        out = torch.empty_like(x)
+        out = torch.empty(x.shape, device=x.device, dtype=out_dtype)
         s = torch.empty_like(x) if res is not None else None
         lib.rms_norm_fwd(L, x, res_c, aw.contiguous(), ab.contiguous(), out, s, eps)
         count_launches(1)
@@ -54,19 +55,20 @@ class _RmsNorm(torch.autograd.Function):
         gs = g_s.contiguous().float() if (ctx.has_res and g_s is not None) else None
         if g_out is None:
             g_out = torch.zeros_like(s)
-        lib.rms_norm_bwd(L, s, g_out.contiguous().float(), gs, aw.contiguous(), dx, part, ctx.eps)
+        g_out = g_out.contiguous()
+        if g_out.dtype not in (torch.float32, torch.bfloat16):
+            g_out = g_out.float()
+        lib.rms_norm_bwd(L, s, g_out, gs, aw.contiguous(), dx, part, ctx.eps)
         count_launches(1)
         p = part.sum(0)
         daw, dab = p[: L + 1], p[L + 1]
         if ctx.has_res:
-            return dx, dx, daw, dab, None
-        return dx, None, daw, dab, None
+            return dx, dx, daw, dab, None, None
+        return dx, None, daw, dab, None, None
 
 
-def rms_norm_sh(x, aw, ab, eps, residual=None):
-    if residual is None:
-        return _RmsNorm.apply(x, None, aw, ab, eps)
-    return _RmsNorm.apply(x, residual, aw, ab, eps)
+def rms_norm_sh(x, aw, ab, eps, residual=None, out_dtype=None):
+    return _RmsNorm.apply(x, residual, aw, ab, eps, out_dtype or torch.float32)
 
 
 class _LnSilu(torch.autograd.Function):
@@ -100,9 +102,13 @@ def layernorm_silu(x, w, b, eps=1e-5):
 
 
 class _GateL(torch.autograd.Function):
+    """fp32 or bf16 activations (output in the input's dtype); gates fp32."""
+
     @staticmethod
     def forward(ctx, gates, x, lmax):
-        x = x.contiguous().float()
+        x = x.contiguous()
+        if x.dtype != torch.bfloat16:
+            x = x.float()
         gates = gates.contiguous().float()
         out = torch.empty_like(x)
         _lib().gate_l_fwd(lmax, x, gates, out)
@@ -116,7 +122,7 @@ class _GateL(torch.autograd.Function):
         x, gates = ctx.saved_tensors
         dx = torch.empty_like(x)
         dg = torch.empty_like(gates)
-        _lib().gate_l_bwd(ctx.lmax, x, gates, g.contiguous().float(), dx, dg)
+        _lib().gate_l_bwd(ctx.lmax, x, gates, g.to(x.dtype).contiguous(), dx, dg)
         count_launches(1)
         return dg, dx, None
 
@@ -135,39 +141,50 @@ def _coef_l(S):
     return out
 
 
-def _run_problems(As, Ws, Cs, biases, mn=False, splits=1):
+def _run_problems(As, Ws, Cs, biases, mn=False, splits=1, resids=None):
     lib = _lib()
     for i in range(0, len(As), 8):
-        lib.gemm(As[i:i + 8], Ws[i:i + 8], Cs[i:i + 8], biases[i:i + 8], mn, 0, 1.0, splits, 128)
+        lib.gemm(As[i:i + 8], Ws[i:i + 8], Cs[i:i + 8], biases[i:i + 8], mn, 0, 1.0, splits, 128,
+                 resids[i:i + 8] if resids is not None else [])
         count_launches(1)
 
 
 class _SO3Linear(torch.autograd.Function):
+    """out[:, j] = x[:, j] @ W[l_j]^T (+ bias on j = 0) (+ residual), one GEMM problem per
+    coefficient j.  x fp32 or bf16 (cast once to bf16); output fp32 (with the residual added in
+    the GEMM epilogue) or bf16; the input gradient comes back in the input's dtype."""
+
     @staticmethod
-    def forward(ctx, x, weight, bias):
+    def forward(ctx, x, weight, bias, out_dtype, residual):
         B, S, C = x.shape
         Co = weight.shape[1]
         xb = x.to(torch.bfloat16).contiguous().view(B, S * C)
-        wb = weight.to(torch.bfloat16).contiguous()
-        out = torch.empty(B, S * Co, device=x.device, dtype=torch.float32)
+        wb = W.bf16(weight)
+        out = torch.empty(B, S * Co, device=x.device, dtype=out_dtype)
         ls = _coef_l(S)
+        res = None
+        if residual is not None:
+            res = residual.contiguous().float().view(B, S * Co)
         _run_problems([xb[:, j * C:(j + 1) * C] for j in range(S)], [wb[ls[j]] for j in range(S)],
                       [out[:, j * Co:(j + 1) * Co] for j in range(S)],
-                      [bias.float().contiguous()] + [None] * (S - 1))
-        ctx.save_for_backward(xb, wb)
+                      [bias.float().contiguous()] + [None] * (S - 1),
+                      resids=None if res is None else [res[:, j * Co:(j + 1) * Co] for j in range(S)])
+        ctx.save_for_backward(xb, weight)
         ctx.dims = (B, S, C, Co)
         ctx.in_dtype = x.dtype
+        ctx.has_res = residual is not None
         return out.view(B, S, Co)
 
     @staticmethod
     def backward(ctx, g):
-        xb, wb = ctx.saved_tensors
+        xb, weight = ctx.saved_tensors
         B, S, C, Co = ctx.dims
         ls = _coef_l(S)
         L = ls[-1]
         gb = g.to(torch.bfloat16).contiguous().view(B, S * Co)
-        dx = torch.empty(B, S * C, device=g.device, dtype=torch.float32)
-        wt = [wb[l].t().contiguous() for l in range(L + 1)]
+        dx_dtype = torch.bfloat16 if ctx.in_dtype == torch.bfloat16 else torch.float32
+        dx = torch.empty(B, S * C, device=g.device, dtype=dx_dtype)
+        wt = W.bf16_t(weight)
         _run_problems([gb[:, j * Co:(j + 1) * Co] for j in range(S)], [wt[ls[j]] for j in range(S)],
                       [dx[:, j * C:(j + 1) * C] for j in range(S)], [None] * S)
         splits = max(1, min(-(-296 // S), B // 2048, 16))
@@ -177,8 +194,9 @@ class _SO3Linear(torch.autograd.Function):
         part = part.sum(1)
         dw = torch.stack([part[l * l:(l + 1) * (l + 1)].sum(0) for l in range(L + 1)])
         db = g[:, 0].sum(0, dtype=torch.float32)
-        return dx.view(B, S, C).to(ctx.in_dtype), dw, db
+        dres = g if ctx.has_res else None
+        return dx.view(B, S, C).to(ctx.in_dtype), dw, db, None, dres
 
 
-def so3_linear(x, weight, bias, lmax):
-    return _SO3Linear.apply(x, weight, bias)
+def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
+    return _SO3Linear.apply(x, weight, bias, out_dtype or torch.float32, residual)

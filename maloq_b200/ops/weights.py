@@ -1,0 +1,81 @@
+"""bf16 operand copies of fp32 master weights, made once per optimizer step.
+
+The tcgen05 GEMMs read bf16 operands; the parameters stay fp32.  Instead of casting (and, in
+backward, transposing) every weight at every call, :func:`bf16` / :func:`bf16_t` /
+:func:`pair_bf16` return a cached copy that is rebuilt only when the parameter may have
+changed.  A cached copy is keyed by
+
+* a global epoch, advanced after every ``torch.optim`` optimizer step (a process-wide
+  step post-hook; fused optimizers update parameters without bumping their version
+  counters, so the epoch is what catches their updates),
+* the parameter's version counter (in-place edits such as ``load_state_dict``),
+* its storage address.
+
+Code that changes weights some other way (through ``.data``) calls :func:`invalidate`.
+"""
+
+from __future__ import annotations
+
+import torch
+
+_EPOCH = [0]
+_CACHE: dict[int, tuple] = {}
+
+
+def _bump(*_args, **_kwargs):
+    _EPOCH[0] += 1
+    _CACHE.clear()
+
+
+from torch.optim.optimizer import register_optimizer_step_post_hook  # noqa: E402
+
+register_optimizer_step_post_hook(_bump)
+
+
+def invalidate() -> None:
+    """Drop every cached copy (call after changing weights through ``.data``)."""
+    _bump()
+
+
+def _get(p, kind, make):
+    if not isinstance(p, torch.nn.Parameter):  # only parameters live long enough to cache
+        return make(p.detach())
+    key = (_EPOCH[0], p._version, p.data_ptr(), kind)
+    ent = _CACHE.get((id(p), kind))
+    if ent is not None and ent[0] == key:
+        return ent[1]
+    t = make(p.detach())
+    _CACHE[(id(p), kind)] = (key, t)
+    return t
+
+
+def bf16(p):
+    """Contiguous bf16 copy of ``p``."""
+    return _get(p, "bf16", lambda w: w.to(torch.bfloat16).contiguous())
+
+
+def bf16_t(p):
+    """Contiguous bf16 copy of the transpose of a 2-D ``p`` (or of each matrix of a 3-D one)."""
+    return _get(p, "bf16_t", lambda w: w.transpose(-1, -2).to(torch.bfloat16).contiguous())
+
+
+def _pair(w):
+    h = w.shape[0] // 2
+    wr, wi = w[:h], w[h:]
+    return torch.cat([torch.cat([wr, -wi], 1), torch.cat([wi, wr], 1)], 0)
+
+
+def pair_bf16(p):
+    """bf16 [[W_r, -W_i], [W_i, W_r]] of an SO(2) m > 0 weight ``p`` = [W_r; W_i]."""
+    return _get(p, "pair", lambda w: _pair(w).to(torch.bfloat16).contiguous())
+
+
+def pair_bf16_t(p):
+    return _get(p, "pair_t", lambda w: _pair(w).t().to(torch.bfloat16).contiguous())
+
+
+def pair_grad(dP):
+    """Gradient of ``p`` = [W_r; W_i] from the gradient of its pair matrix."""
+    h2, k2 = dP.shape
+    d = dP.view(2, h2 // 2, 2, k2 // 2)
+    return torch.cat([d[0, :, 0] + d[1, :, 1], d[1, :, 0] - d[0, :, 1]], 0)

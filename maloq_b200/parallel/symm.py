@@ -2,13 +2,14 @@
 
 The data-parallel gradient buckets live in one symmetric-memory allocation
 (``torch.distributed._symmetric_memory``), so every rank can address every peer's buckets.
-Reducing a bucket is three kernels on the reduction stream:
-
-1. ``peer_barrier(epoch)`` - all ranks have finished writing this bucket's gradients;
-2. ``allreduce_multimem`` (NVLink SHARP through NVSwitch, when the group supports multicast)
-   or ``allreduce_p2p`` (peer loads/stores) - rank r reduces chunk r over all ranks, scales
-   by 1/world and writes the result into chunk r of every rank's bucket;
-3. ``peer_barrier(epoch + 1)`` - every chunk has been written everywhere.
+Reducing a bucket is two kernels on the reduction stream: ``peer_barrier(epoch)`` (one
+CTA: every rank raises its epoch flag in every peer's signal pad and waits until all peers
+raised theirs - the bucket is complete everywhere), then ``allreduce_multimem`` (NVLink SHARP
+through NVSwitch, when the group supports multicast) or ``allreduce_p2p`` (peer
+loads/stores): rank r reduces chunk r over all ranks, scales by 1/world and writes the result
+into chunk r of every rank's bucket.  One more ``peer_barrier`` after the step's last bucket
+(:meth:`PeerAllReduce.wait`) guarantees every chunk has been written everywhere before any
+rank reads its gradients or reuses the buffer.
 
 The reference reduces every parameter with its own synchronous NCCL all-reduce after
 backward (``train_utils/splittrainer.py:204-218``).  Waits are bounded (see comm.cu); a
@@ -52,7 +53,7 @@ class PeerAllReduce:
             use_multimem = os.environ.get("MALOQ_NO_MULTIMEM", "0") != "1"
         self.mc = mc if use_multimem else 0
         self.epoch = 0
-        self.events = []
+        self.pending = None
         self.hdl.barrier()
 
     @property
@@ -66,6 +67,7 @@ class PeerAllReduce:
         self.epoch += 1
         self.lib.peer_barrier(self.pads_dev.data_ptr(), self.rank, self.world,
                               self.epoch, 0, SPIN_LIMIT)
+        count_launches(1)
 
     def all_reduce_(self, flat, side_stream=None, scale=1.0):
         """Reduce ``flat`` (a view of this object's buffer) in place: sum over ranks * scale."""
@@ -82,13 +84,18 @@ class PeerAllReduce:
                 self.lib.allreduce_multimem(self.mc, self.rank, self.world, off, n, scale)
             else:
                 self.lib.allreduce_p2p(self.bufs_dev.data_ptr(), self.rank, self.world, off, n, scale)
-            self._barrier()
-            ev = torch.cuda.Event()
-            ev.record(stream)
-            self.events.append(ev)
-        count_launches(3)
+            self.pending = stream
+        count_launches(1)
 
     def wait(self, stream):
-        for ev in self.events:
-            stream.wait_event(ev)
-        self.events = []
+        """Close the step: one peer barrier after the last bucket (on the reduction stream),
+        then ``stream`` waits for it."""
+        side = getattr(self, "pending", None)
+        if side is None:
+            return
+        with torch.cuda.stream(side):
+            self._barrier()
+            ev = torch.cuda.Event()
+            ev.record(side)
+        stream.wait_event(ev)
+        self.pending = None

@@ -117,3 +117,25 @@ def test_basis_transform_column_tables_and_transposes():
             for u, (s, n, c, _) in enumerate(meta):
                 out[:, u] = x[:, s:s + n] @ coef[c + np.arange(n) * n]
             assert np.allclose(out, ref, atol=1e-6)
+
+
+# largest entry of wigner_3j(l1, l2, l3) for every triple of an s/p/d basis (def2-SVP-like
+# layouts): the e3nn construction (Racah Clebsch-Gordan + real change of basis with the
+# (-i)^l factor, unit norm) fixes each triple's sign; these values pin it
+_W3J_PINS = {(0, 0, 0): ((0, 0, 0), 1.0), (0, 1, 1): ((0, 1, 1), 0.57735), (0, 2, 2): ((0, 2, 2), 0.447214),
+             (1, 0, 1): ((1, 0, 1), 0.57735), (1, 1, 0): ((1, 1, 0), 0.57735), (1, 1, 1): ((0, 1, 2), 0.408248),
+             (1, 1, 2): ((1, 1, 2), 0.365148), (1, 2, 1): ((1, 2, 1), 0.365148), (1, 2, 2): ((1, 0, 4), -0.365148),
+             (1, 2, 3): ((1, 2, 3), 0.29277), (2, 0, 2): ((2, 0, 2), 0.447214), (2, 1, 1): ((2, 1, 1), 0.365148),
+             (2, 1, 2): ((0, 1, 4), 0.365148), (2, 1, 3): ((2, 1, 3), 0.29277), (2, 2, 0): ((2, 2, 0), 0.447214),
+             (2, 2, 1): ((0, 4, 1), -0.365148), (2, 2, 2): ((2, 2, 2), 0.239046), (2, 2, 3): ((0, 2, 5), 0.267261),
+             (2, 2, 4): ((2, 2, 4), 0.239046)}
+
+
+def test_wigner3j_signs_pinned_to_e3nn_construction():
+    from maloq_b200.core import wigner3j
+
+    for (l1, l2, l3), (idx, val) in _W3J_PINS.items():
+        C = wigner3j.wigner_3j(l1, l2, l3, dtype=torch.float64)
+        assert abs(C[idx].item() - val) < 1e-6, ((l1, l2, l3), C[idx].item(), val)
+        # the pinned entry is the largest in magnitude (so the sign is unambiguous)
+        assert abs(val) >= C.abs().max().item() - 1e-6

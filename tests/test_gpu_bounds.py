@@ -25,7 +25,7 @@ CASE = textwrap.dedent("""
     src = torch.randint(0, N, (E,), device=dev)
     dst = torch.sort(torch.randint(0, N, (E,), device=dev)).values
     rot = torch.randn(E, R, S, device=dev)
-    rad = torch.randn(E, 12 * Cin, device=dev)
+    rad = torch.randn(E, 12 * Cin, device=dev).bfloat16()
     A0 = torch.zeros(E, R * Cin, device=dev, dtype=torch.bfloat16)
     lib.gather_rotate_fwd(4, 2, X, None, src, dst, rot, rad, A0, Cin, 0, None, None, 0)
     torch.cuda.synchronize()

@@ -302,3 +302,57 @@ def test_workflow_eval_energy_and_force_heads(tmp_path, target):
     col = 1 if target == "energies" else 2
     assert all(np.isfinite(r[col]) for r in rows)
     assert (tmp_path / "model_energy_eval_0.txt").exists()
+
+
+def test_state_dict_shapes_follow_reference_modules():
+    """Every parameter/buffer shape of the backbone and Fock head equals the shape the
+    reference's module definitions give (``esen_osh.py:140-200, 522-703``, ``esen_block.py:60-105,
+    261-298``, ``so2_layers.py:19-214``, ``layer_norm.py:230-338``, e3nn ``o3.Linear`` flat
+    weights), for the reference's own setting mmax = lmax and the source-target message."""
+    _, lab = _batches(np.eye(3), torch.float32)
+    L, C, Hd, Ce, G = 4, 8, 8, 8, 8
+    kw = dict(KW, mmax=L)
+    bb = eSEN_Backbone(lab.irreps, **kw)
+    sd = {k: tuple(v.shape) for k, v in bb.state_dict().items()}
+    Cin = 2 * C  # source-target message
+    n_rad = (L + 1) * Cin + sum((L - m + 1) * Cin for m in range(1, L + 1))
+    exp = {f"Jd_{l}": (2 * l + 1, 2 * l + 1) for l in range(L + 1)}
+    exp.update({"distance_expansion.offset": (G,), "sphere_embedding.weight": (100, C),
+                "charge_embedding.weight": (21, C), "spin_embedding.weight": (11, C),
+                "scalar_node_embedding.weight": (C, 3 * C), "scalar_node_embedding.bias": (C,),
+                "source_embedding.weight": (100, Ce), "target_embedding.weight": (100, Ce),
+                "edge_degree_embedding.rad_func.net.0.weight": (Ce, G + 2 * Ce),
+                "edge_degree_embedding.rad_func.net.1.weight": (Ce,),
+                "edge_degree_embedding.rad_func.net.3.weight": (Ce, Ce),
+                "edge_degree_embedding.rad_func.net.6.weight": ((L + 1) * C, Ce),
+                "norm.affine_weight": (L + 1, C), "norm.affine_bias": (C,)})
+    for kind in ("node_blocks", "edge_blocks"):
+        for i in range(2):
+            p = f"{kind}.{i}."
+            exp.update({p + "norm_1.affine_weight": (L + 1, C), p + "norm_2.affine_bias": (C,),
+                        p + "norm_1.balance_degree_weight": ((L + 1) ** 2, 1),
+                        p + "edge_wise.so2_conv_1.fc_m0.weight": ((L + 1) * Hd + L * Hd, (L + 1) * Cin),
+                        p + "edge_wise.so2_conv_1.fc_m0.bias": ((L + 1) * Hd + L * Hd,),
+                        p + "edge_wise.so2_conv_1.rad_func.net.0.weight": (Ce, G + 2 * Ce),
+                        p + "edge_wise.so2_conv_1.rad_func.net.6.weight": (n_rad, Ce),
+                        p + "edge_wise.so2_conv_2.fc_m0.weight": ((L + 1) * C, (L + 1) * Hd),
+                        p + "atom_wise.scalar_mlp.0.weight": (L * Hd, C),
+                        p + "atom_wise.so3_linear_1.weight": (L + 1, Hd, C),
+                        p + "atom_wise.so3_linear_2.weight": (L + 1, C, Hd),
+                        p + "atom_wise.so3_linear_1.expand_index": ((L + 1) ** 2,)})
+            for m in range(1, L + 1):
+                exp[p + f"edge_wise.so2_conv_1.so2_m_conv.{m - 1}.fc.weight"] = (2 * Hd * (L - m + 1), (L - m + 1) * Cin)
+                exp[p + f"edge_wise.so2_conv_2.so2_m_conv.{m - 1}.fc.weight"] = (2 * C * (L - m + 1), (L - m + 1) * Hd)
+    for k, shape in exp.items():
+        assert k in sd, k
+        assert sd[k] == shape, (k, sd[k], shape)
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=L, sphere_channels=C, ls_list=lab.layout.ls_list, reduce_node=True,
+                          reduce_node_intra=True)
+    hsd = {k: tuple(v.shape) for k, v in hd.state_dict().items()}
+    # scalars C x 0e -> (C + L*C) x 0e (C scalars + one gate per gated irrep C x 1e .. C x Le)
+    assert hsd["lin_scalars_learnable.0.weight"] == (C * (C + L * C),)  # e3nn flat [mul_in * mul_out]
+    for l in range(L + 1):
+        k = f"node_lin_out_layers.0.{l}.weight"
+        if k in hsd:
+            mul_out = hd.node_lin_out_layers[0][l].mul_out
+            assert hsd[k] == (C * mul_out,), (k, hsd[k])
