@@ -572,6 +572,16 @@ def main():
         args, device, world, lambda i: trainer.train_step(dev_batches[i % len(dev_batches)], loss_fn, opt),
         lambda i: trainer.train_step(host_batches[i % len(host_batches)].to(device, non_blocking=True), loss_fn,
                                      opt))
+    # equivariance of the timed model on the product path (bf16 GEMM operands), outside the timing
+    import numpy as np
+
+    from maloq_b200.data import structures as S_
+    from maloq_b200.eval.equivariance import model_equivariance_error, random_rotation
+
+    rng_eq = np.random.default_rng(7)
+    mols_eq = [S_.random_druglike_molecule(rng_eq, 30, 50) for _ in range(4)] if kind == "druglike" else []
+    eq_err = (model_equivariance_error(backbone, head, mols_eq, labeler, 6.0, random_rotation(rng_eq), device)
+              if mols_eq and args.impl == "native" else None)
     nbytes = [sum(v.numel() * v.element_size() for v in hb.tensors().values()) for hb in host_batches]
     h2d = sum(nbytes[i % len(nbytes)] for i in range(args.steps)) / args.steps
 
@@ -601,6 +611,7 @@ def main():
             "gpu_launches": int(launches),
             "clocks": clk,
             "final_loss": loss_vals[-1],
+            "equivariance_rel_err_bf16": None if eq_err is None else float(f"{eq_err:.3g}"),
             "peak_mem_gb": round(torch.cuda.max_memory_allocated(device) / 2**30, 2),
             "activation_checkpointing": backbone.activation_checkpointing,
             "setup_s": round(t_data, 1),

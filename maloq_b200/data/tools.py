@@ -1,0 +1,148 @@
+"""Dataset tools: database builders and target statistics, as standalone commands.
+
+    python -m maloq_b200.data.tools orca-to-db OUT.db RUN_DIR [RUN_DIR ...] [--unrestricted]
+    python -m maloq_b200.data.tools lin-ref DATASET OUT.npz [--dataset-name nablaDFT|QM7|ase]
+    python -m maloq_b200.data.tools scale-shift DATASET OUT.pt [--dataset-name ...] [--num N]
+
+* ``orca-to-db``: every directory holding an ORCA output (``*.out``) becomes one row of an ASE
+  database (the format the OMol folders use): positions and atomic numbers, and in ``data``
+  the Fock matrix converted to e3nn orbital order (``fock_matrix``; [2, n, n] for
+  unrestricted runs), ``total_energy [Eh]``, ``is_open_shell``, ``charge``,
+  ``spin_multiplicity`` and ``folder_name`` (reference
+  ``dataset_utils/make_omol_database_raw.py``).  The basis shell order is the one ORCA prints.
+* ``lin-ref``: per-element linear energy references - the least-squares fit of the total
+  energies on the element counts, ``E ~ sum_Z n_Z(molecule) coeff[Z]`` - saved as
+  ``coeff[Z]`` (the table the workflow subtracts from energy targets; reference
+  ``dataset_utils/compute_lin_ref_nabla.py``).
+* ``scale-shift``: per-element means and standard deviations of the l = 0 on-site (node)
+  label entries over a dataset, saved with the key names the workflow loads
+  (``element_scalar_means``, ``element_scalar_stds``, ``scalar_irrep_indices``; reference
+  ``dataset_utils/get_scale_shift.py``).
+"""
+
+from __future__ import annotations
+
+import argparse
+import glob
+import os
+
+import numpy as np
+import torch
+
+
+# ------------------------------------------------------------------ ORCA runs -> ASE database
+def orca_runs_to_db(out_path, run_dirs, unrestricted=False, charge=0, spin_multiplicity=None):
+    """One ASE-database row per ORCA run directory; returns the number of rows written."""
+    from .asedb import write_asedb
+    from .readers import read_orca_output, reorder_orbitals
+
+    rows = []
+    for d in run_dirs:
+        outs = sorted(glob.glob(os.path.join(d, "*.out")))
+        if not outs:
+            continue
+        r = read_orca_output(outs[0], unrestricted=unrestricted)
+        z = np.asarray(r["z"], dtype=np.int64)
+        basis = r["basis"]
+        if unrestricted:
+            fock = np.stack([reorder_orbitals(r["fock"][k], z, basis, "orca") for k in ("alpha", "beta")])
+        else:
+            fock = reorder_orbitals(r["fock"], z, basis, "orca")
+        mult = spin_multiplicity if spin_multiplicity is not None else (2 if unrestricted else 1)
+        rows.append({"numbers": z, "positions": np.asarray(r["pos"]),
+                     "energy": r["energy"],
+                     "data": {"fock_matrix": fock.astype(np.float32),
+                              "total_energy [Eh]": r["energy"] if r["energy"] is not None else 0.0,
+                              "is_open_shell": bool(unrestricted), "charge": int(charge),
+                              "spin_multiplicity": int(mult), "folder_name": os.path.basename(os.path.normpath(d))}})
+    if rows:
+        write_asedb(out_path, rows)
+    return len(rows)
+
+
+# ------------------------------------------------------------------ statistics
+def linear_energy_references(numbers_list, energies):
+    """coeff[Z] minimising ||E - counts @ coeff||^2 over molecules (least squares)."""
+    zmax = max(int(np.max(z)) for z in numbers_list)
+    A = np.stack([np.bincount(np.asarray(z, dtype=np.int64), minlength=zmax + 1) for z in numbers_list])
+    return np.linalg.lstsq(A.astype(np.float64), np.asarray(energies, dtype=np.float64), rcond=None)[0]
+
+
+def scale_shift_table(samples, labeler):
+    """Per-element means / stds of the l = 0 node label entries of ``samples`` (targets in
+    ``node_y``), in the workflow's file layout."""
+    from .targets import ScaleShift
+
+    ss = ScaleShift(labeler, samples)
+    stds = {}
+    for z in ss.means:
+        rows = torch.cat([s.node_y[0][torch.as_tensor(s.z == z)][:, ss.scalar_idx] for s in samples])
+        stds[z] = rows.float().std(0, unbiased=False)
+    return {"element_scalar_means": ss.means, "element_scalar_stds": stds,
+            "scalar_irrep_indices": ss.scalar_idx.tolist()}
+
+
+def _load(path, name, num=None):
+    from . import readers
+
+    cfg = {"rcut_orbitals": 3.0, "num_structures": num}
+    if name == "nablaDFT":
+        return readers.load_nabladft(path, {k: v for k, v in cfg.items() if v is not None})
+    if name == "QM7":
+        return readers.load_qm7(path, cfg)
+    return readers.load_ase_entries([{"db_file": path, "start_idx": 0, "end_idx": num}], cfg)
+
+
+def _energies(path, name, num=None):
+    if name == "nablaDFT":
+        from .readers import NablaDFTDatabase
+
+        db = NablaDFTDatabase(path)
+        n = len(db) if num is None else min(num, len(db))
+        rows = [db[i] for i in range(n)]
+        return [r[0] for r in rows], [float(r[2][0]) for r in rows]
+    from .asedb import AseDb
+
+    db = AseDb(path)
+    rows = db.rows(0, num)
+    zs = [r["numbers"] for r in rows]
+    es = [r["data"].get("total_energy [Eh]", r["energy"]) if name != "QM7" else
+          float(np.asarray(r["data"].get("energy", r["energy"])).reshape(-1)[0]) for r in rows]
+    return zs, es
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    a = sub.add_parser("orca-to-db")
+    a.add_argument("out")
+    a.add_argument("runs", nargs="+")
+    a.add_argument("--unrestricted", action="store_true")
+    a.add_argument("--charge", type=int, default=0)
+    b = sub.add_parser("lin-ref")
+    b.add_argument("dataset")
+    b.add_argument("out")
+    b.add_argument("--dataset-name", default="nablaDFT")
+    b.add_argument("--num", type=int, default=None)
+    c = sub.add_parser("scale-shift")
+    c.add_argument("dataset")
+    c.add_argument("out")
+    c.add_argument("--dataset-name", default="nablaDFT")
+    c.add_argument("--num", type=int, default=None)
+    args = ap.parse_args(argv)
+    if args.cmd == "orca-to-db":
+        n = orca_runs_to_db(args.out, args.runs, args.unrestricted, args.charge)
+        print(f"wrote {n} rows to {args.out}")
+    elif args.cmd == "lin-ref":
+        zs, es = _energies(args.dataset, args.dataset_name, args.num)
+        coeff = linear_energy_references(zs, es)
+        np.savez(args.out, coeff=coeff)
+        print(f"linear references for {len(es)} molecules -> {args.out}")
+    else:
+        samples, lab = _load(args.dataset, args.dataset_name, args.num)
+        torch.save(scale_shift_table(samples, lab), args.out)
+        print(f"scale/shift of {len(samples)} molecules -> {args.out}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,74 @@
+"""Dataset tools (CPU): ORCA runs -> ASE database, linear energy references, scale/shift."""
+import numpy as np
+import torch
+
+from maloq_b200.data import asedb, readers, tools
+from maloq_b200.data.basis_sets import get_basis
+
+
+def _orca_text(F, energy):
+    from tests.test_cp2k_readers import _orca_block
+
+    lines = ["junk", "---------------------------------", "CARTESIAN COORDINATES (ANGSTROEM)",
+             "---------------------------------", "  H      0.000000    0.000000    0.740000",
+             "  O      0.100000   -0.200000    0.000000", "", " BASIS SET INFORMATION",
+             "Group   1 Type H   : 4s1p contracted to 2s1p pattern {31/1}",
+             "Group   2 Type O   : 7s4p1d contracted to 3s2p1d pattern {511/31/1}", "",
+             "TOTAL SCF ENERGY", "----------------", "",
+             f"Total Energy       :        {energy:.11f} Eh           -2078.97 eV", "", "FOCK", ""]
+    return "\n".join(lines + _orca_block(F) + ["", "end"]) + "\n"
+
+
+def test_orca_runs_to_ase_database(tmp_path):
+    rng = np.random.default_rng(0)
+    Fs = []
+    for k in range(3):
+        F = np.round(rng.standard_normal((19, 19)), 6)
+        F = F + F.T
+        Fs.append(F)
+        d = tmp_path / f"run{k}"
+        d.mkdir()
+        (d / "orca.out").write_text(_orca_text(F, -76.0 - k))
+    out = str(tmp_path / "mols.db")
+    assert tools.main(["orca-to-db", out] + [str(tmp_path / f"run{k}") for k in range(3)]) is None
+    ds = asedb.ASEDataset(out)
+    assert len(ds) == 3
+    r = ds[1]
+    assert list(r["atomic_numbers"]) == [1, 8] and r["folder_name"] == "run1"
+    assert abs(r["energies"] + 77.0) < 1e-9
+    ref = readers.reorder_orbitals(Fs[1], [1, 8], {1: [0, 0, 1], 8: [0, 0, 0, 1, 1, 2]}, "orca")
+    assert np.allclose(r["fock_matrix"], ref, atol=1e-5)
+
+
+def test_linear_references_recover_coefficients(tmp_path):
+    rng = np.random.default_rng(1)
+    coeff = {1: -0.5, 6: -37.8, 8: -75.0}
+    basis = get_basis("def2_svp_nabla")
+    mols = []
+    for _ in range(20):
+        z = rng.choice([1, 6, 8], size=int(rng.integers(3, 8))).astype(np.int32)
+        E = sum(coeff[int(a)] for a in z) + rng.normal() * 1e-6
+        n = sum(sum(2 * l + 1 for l in basis[int(a)]) for a in z)
+        mols.append((z, rng.uniform(0, 6, (len(z), 3)), E, np.zeros((len(z), 3)), np.eye(n), np.eye(n), np.eye(n)))
+    path = str(tmp_path / "nabla.db")
+    readers.write_nabladft(path, mols)
+    out = str(tmp_path / "lin.npz")
+    tools.main(["lin-ref", path, out, "--dataset-name", "nablaDFT"])
+    c = np.load(out)["coeff"]
+    for z, v in coeff.items():
+        assert abs(c[z] - v) < 1e-4, (z, c[z])
+
+
+def test_scale_shift_table_matches_workflow_layout(tmp_path):
+    from maloq_b200.data import datasets
+
+    lab = datasets.labeler_for("small")
+    samples, _ = datasets.build_dataset("small", 4, dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2,
+                                                          cutoff=5.0, num_layers=1, num_distance_basis=8,
+                                                          edge_channels=8), labeler=lab)
+    t = tools.scale_shift_table(samples, lab)
+    assert set(t) == {"element_scalar_means", "element_scalar_stds", "scalar_irrep_indices"}
+    z = int(samples[0].z[0])
+    rows = torch.cat([s.node_y[0][torch.as_tensor(s.z == z)] for s in samples])
+    idx = torch.tensor(t["scalar_irrep_indices"])
+    assert torch.allclose(t["element_scalar_means"][z], rows[:, idx].float().mean(0), atol=1e-6)

@@ -26,6 +26,11 @@ def _rel(a, b):
     return ((a - b).abs().max() / (b.abs().max() + 1e-12)).item()
 
 
+def _relf(a, b):
+    """Relative Frobenius error (the typical, rather than worst, element error)."""
+    return ((a - b).float().norm() / (b.float().norm() + 1e-12)).item()
+
+
 @pytest.mark.parametrize("path", ["node", "edge"])
 @pytest.mark.parametrize("message_type,mmax", [("source-target", 2), ("source-target-message", 2),
                                                ("source-target", 4)])
@@ -49,12 +54,16 @@ def test_edgewise_matches_reference(cuda_device, path, message_type, mmax):
     rgrads = torch.autograd.grad((ref * gout).sum(), [x, x_edge] + ([xe] if xe is not None else []) +
                                  list(mod.parameters()), allow_unused=True)
     assert _rel(out, ref) < 2e-2
+    assert _relf(out, ref) < 1e-2, _relf(out, ref)
+    print(path, message_type, mmax, "out", _rel(out, ref), _relf(out, ref))
     names = ["x", "x_edge"] + (["xe"] if xe is not None else []) + [n for n, _ in mod.named_parameters()]
     for n, g, rg in zip(names, grads, rgrads):
         if rg is None:
             continue
         assert g is not None, n
         assert _rel(g, rg) < 3e-2, (n, _rel(g, rg))
+        assert _relf(g, rg) < 1e-2, (n, _relf(g, rg))
+        print("  grad", n, _rel(g, rg), _relf(g, rg))
     from maloq_b200.ops import kernels
 
     assert kernels.error_status() == 0
