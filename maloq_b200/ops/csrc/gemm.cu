@@ -15,7 +15,8 @@
 // 64 through a STAGES-deep TMA ring:
 //   warp 0 (one elected lane): TMA producer        - waits "empty", loads the A/B tiles
 //   warp 1 (one elected lane): tcgen05.mma issuer  - waits "full", 4 MMAs (K=16), commits "empty"
-//   warps 2-5: epilogue - tcgen05.ld of TMEM lanes 32*(w%4).., bias/activation, store.
+//   warps 2-9: epilogue - tcgen05.ld of TMEM lanes 32*(w%4).. (two warps per lane quarter, each
+//   half of the columns), bias/activation/residual, store.
 // Two TMEM accumulators (2 x BN fp32 columns) let a tile's epilogue overlap the next tile's
 // MMAs.  TMA loads use no multicast.
 #include <cstdio>
@@ -31,7 +32,9 @@ namespace maloq {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int STAGE_WARP_BYTES = 16384;  // epilogue staging per epilogue warp
+constexpr int EPI_WARPS = 8;             // two warps per TMEM lane quarter, each half of the columns
+constexpr int GEMM_THREADS = 64 + 32 * EPI_WARPS;
+constexpr int STAGE_WARP_BYTES = 8192;   // epilogue staging per epilogue warp
 
 struct alignas(64) GemmProblemDev {
   CUtensorMap ta;
@@ -122,12 +125,12 @@ __device__ __forceinline__ TileCoord decode_tile(const GemmParamsDev& P, int w, 
   return tc;
 }
 
-// Persistent warp-specialised kernel: 6 warps.
+// Persistent warp-specialised kernel: 10 warps.
 //   warp 0: TMA producer (one lane); warp 1: MMA issuer (one lane);
-//   warps 2-5: epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+//   warps 2-9: epilogue (warp w reads TMEM lanes 32*(w%4) .. +31, columns of its half).
 // Two TMEM accumulators (2*BN columns): the epilogue of work item i overlaps the MMAs of i+1.
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ GemmParamsDev P, int total_work,
+__global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc_kernel(const __grid_constant__ GemmParamsDev P, int total_work,
                                                          int tiles_per_split) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -139,9 +142,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;  // [2] MMA -> epilogue
-  uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (4 arrivals: one per epilogue warp)
+  uint64_t* acc_empty = acc_full + 2;   // [2] epilogue -> MMA (one arrival per epilogue warp)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  // epilogue staging: 4 warps x STAGE_WARP_BYTES, 1024-aligned
+  // epilogue staging: EPI_WARPS x STAGE_WARP_BYTES, 1024-aligned
   uint8_t* stage_out = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 1023) & ~uintptr_t(1023));
 
@@ -153,7 +156,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], EPI_WARPS);
     }
     fence_barrier_init();
   }
@@ -247,8 +250,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5
-    const int quarter = warp & 3;
+    // ---------------- epilogue warps 2..9: warp w reads TMEM lanes 32*(w%4).. and half (w-2)/4 of
+    // the accumulator's columns
+    const int ew = warp - 2, quarter = warp & 3;
+    const int cbeg = (ew / 4) * (BN / 2), cend = cbeg + BN / 2;
     const bool out32 = P.out_fp32 != 0;
     int it = 0, sbuf = 0;
     for (int w = blockIdx.x; w < total_work; w += gridDim.x, ++it) {
@@ -261,11 +266,11 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       if (!mbar_wait(&acc_full[buf], (it >> 1) & 1, ERR_EPI_WAIT)) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c0), v);
-        if (c0 + 32 >= BN) {
-          // accumulator fully read: hand the buffer back to the MMA warp
+        if (c0 + 32 >= cend) {
+          // this warp's part of the accumulator is read: hand it back to the MMA warp
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -280,12 +285,12 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         epilogue_math(v, ep.alpha, ep, col0, lane);
         epilogue_residual(v, ep, tc.m0 + quarter * 32 + lane, col0);
         // stage the warp's 32 x 32 chunk (row-major, 32*esz bytes per row) and TMA-store it
-        // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
-        const int ring = out32 ? 4 : 8;
-        uint8_t* stg = stage_out + quarter * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
+        // per-warp ring of staging chunks (8 KB): 4 bf16 or 2 fp32 chunks of 32 x 32
+        const int ring = out32 ? 2 : 4;
+        uint8_t* stg = stage_out + ew * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
         if (lane == 0) {
-          if (out32) bulk_wait_read<3>();  // the chunk stored `ring` chunks ago has been read
-          else bulk_wait_read<7>();
+          if (out32) bulk_wait_read<1>();  // the chunk stored `ring` chunks ago has been read
+          else bulk_wait_read<3>();
         }
         __syncwarp();
         if (out32) {
@@ -329,9 +334,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 // FLOP relative to the 1-SM kernel.  K-major operands only; no split-K.
 // Barriers: full[s] lives in the leader (both CTAs' TMA loads complete on it); empty[s] and
 // acc_full[b] exist in both CTAs and are signalled by two commits from the leader; acc_empty[b]
-// lives in the leader and collects 8 arrivals (4 epilogue warps per CTA).
+// lives in the leader and collects 2 * EPI_WARPS arrivals (the epilogue warps of both CTAs).
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant__ GemmParamsDev P, int total_work) {
+__global__ void __launch_bounds__(GEMM_THREADS, 1) gemm_tc2_kernel(const __grid_constant__ GemmParamsDev P, int total_work) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int A_BYTES = 128 * BK * 2;
@@ -357,7 +362,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);
+      mbar_init(&acc_empty[b], 2 * EPI_WARPS);
     }
     fence_barrier_init();
   }
@@ -436,8 +441,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
       }
     }
   } else {
-    // ---------------- epilogue warps 2..5 (both CTAs; rows 128 * crank + ...)
-    const int quarter = warp & 3;
+    // ---------------- epilogue warps 2..9 (both CTAs; rows 128 * crank + ...); warp w reads TMEM
+    // lanes 32*(w%4).. and half (w-2)/4 of the columns
+    const int ew = warp - 2, quarter = warp & 3;
+    const int cbeg = (ew / 4) * (BN / 2), cend = cbeg + BN / 2;
     const bool out32 = P.out_fp32 != 0;
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
     int it = 0, sbuf = 0;
@@ -450,10 +457,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
       tc_fence_after();
       const int row0 = tc.m0 + 128 * (int)crank + quarter * 32;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c0), v);
-        if (c0 + 32 >= BN) {
+        if (c0 + 32 >= cend) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(acc_empty_leader + buf * 8);
@@ -462,12 +469,12 @@ __global__ void __launch_bounds__(192, 1) gemm_tc2_kernel(const __grid_constant_
         if (col0 >= ep.N) continue;
         epilogue_math(v, ep.alpha, ep, col0, lane);
         epilogue_residual(v, ep, row0 + lane, col0);
-        // per-warp ring of staging chunks (16 KB): 8 bf16 or 4 fp32 chunks of 32 x 32
-        const int ring = out32 ? 4 : 8;
-        uint8_t* stg = stage_out + quarter * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
+        // per-warp ring of staging chunks (8 KB): 4 bf16 or 2 fp32 chunks of 32 x 32
+        const int ring = out32 ? 2 : 4;
+        uint8_t* stg = stage_out + ew * STAGE_WARP_BYTES + (sbuf % ring) * (out32 ? 4096 : 2048);
         if (lane == 0) {
-          if (out32) bulk_wait_read<3>();  // the chunk stored `ring` chunks ago has been read
-          else bulk_wait_read<7>();
+          if (out32) bulk_wait_read<1>();  // the chunk stored `ring` chunks ago has been read
+          else bulk_wait_read<3>();
         }
         __syncwarp();
         if (out32) {
@@ -577,7 +584,7 @@ static const char* make_out_map(CUtensorMap* m, void* base, long long M, long lo
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaStream_t st) {
-  constexpr int smem = STAGES * (BM * BK + BN * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 + 4 * STAGE_WARP_BYTES;
+  constexpr int smem = STAGES * (BM * BK + BN * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 + EPI_WARPS * STAGE_WARP_BYTES;
   auto k = gemm_tc_kernel<BN, STAGES, A_MN, B_MN>;
   static bool init = false;  // per process; the attribute applies to every device
   if (!init) {
@@ -594,7 +601,7 @@ static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaS
   }
   const int total = tiles * splits;
   const int grid = total < num_sms ? total : num_sms;
-  k<<<grid, 192, smem, st>>>(P, total, tiles);
+  k<<<grid, GEMM_THREADS, smem, st>>>(P, total, tiles);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
@@ -602,7 +609,7 @@ static const char* launch_t(const GemmParamsDev& P, int tiles, int splits, cudaS
 template <int BN, int STAGES>
 static const char* launch_2sm(const GemmParamsDev& P, int total, cudaStream_t st) {
   constexpr int smem = STAGES * (128 * BK + (BN / 2) * BK) * 2 + 1024 + (2 * STAGES + 4) * 8 + 16 + 1024 +
-                       4 * STAGE_WARP_BYTES;
+                       EPI_WARPS * STAGE_WARP_BYTES;
   auto k = gemm_tc2_kernel<BN, STAGES>;
   static bool init = false;
   if (!init) {
@@ -621,7 +628,7 @@ static const char* launch_2sm(const GemmParamsDev& P, int total, cudaStream_t st
   if (total < clusters) clusters = total;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

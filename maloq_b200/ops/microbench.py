@@ -88,6 +88,21 @@ def bench_edge(edges):
     DR = torch.empty_like(rad)
     ms = _timeit(lambda: lib.gather_rotate_bwd(4, 2, x, None, rot, rad, A, dptr, perm, sptr, DX, None, DR, Cin, 0,
                                                None, None, 0))
+    Y2 = torch.randn(edges, R * C, device=dev).bfloat16()
+    out_n = torch.empty(N, S, C, device=dev)
+    out_e = torch.empty(edges, S, C, device=dev)
+    gn = torch.randn(N, S, C, device=dev)
+    dY = torch.empty(edges, R * C, device=dev, dtype=torch.bfloat16)
+    for name, fn, byt2 in [
+            ("rotate_back_scatter (node path)",
+             lambda: lib.rotate_back_scatter(4, 2, Y2, 0, R, rot, dptr, None, out_n, 1.0),
+             edges * (R * C * 2 + R * S * 4)),
+            ("rotate_back_edge (edge path)", lambda: lib.rotate_back_edge(4, 2, Y2, 0, R, rot, out_e),
+             edges * (R * C * 2 + R * S * 4 + S * C * 4)),
+            ("rotate_grad (node path)", lambda: lib.rotate_grad(4, 2, gn, dst, rot, dY, None, R, 1.0),
+             edges * (R * C * 2 + R * S * 4))]:
+        t = _timeit(fn)
+        print(f"{name}: {t * 1e3:.1f} us, {byt2 / t / 1e9:.2f} TB/s algorithmic")
     # per edge: rotation twice (both walks), radial row, dA row, radial gradient row
     byt = N * S * C * 4 * 2 + edges * (2 * R * S * 4 + 12 * Cin * 2 * 2 + R * Cin * 2)
     print(f"gather_rotate_bwd: {ms * 1e3:.1f} us, {byt / ms / 1e9:.2f} TB/s algorithmic, "

@@ -43,7 +43,7 @@ def _timed(fn, iters, warm=3):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--mib", type=int, default=256, help="all-reduce buffer size (MiB, fp32)")
+    ap.add_argument("--mib", type=int, nargs="+", default=[16, 256], help="all-reduce buffer sizes (MiB, fp32)")
     ap.add_argument("--halo-rows", type=int, default=20000)
     ap.add_argument("--own-rows", type=int, default=20000)
     ap.add_argument("--iters", type=int, default=20)
@@ -59,22 +59,35 @@ def main(argv=None):
     rank, world = dist.get_rank(), dist.get_world_size()
     out = []
 
-    # ---- all-reduce
-    n = a.mib * 2**20 // 4
-    par = PeerAllReduce(n, dev)
-    buf = par.view(0, n)
-    buf.fill_(1.0)
-    ms = _timed(lambda: par.all_reduce_(buf), a.iters)
-    nbytes = n * 4
-    bus = nbytes * 2 * (world - 1) / world / (ms * 1e-3) / 1e9
-    out.append({"path": f"fused all-reduce ({par.transport})", "bytes": nbytes, "ms": round(ms, 4),
-                "bus_gbs": round(bus, 1), "frac_of_link": round(bus / a.link_gbs, 3)})
-    t = torch.ones(n, device=dev)
-    ms = _timed(lambda: dist.all_reduce(t), a.iters)
-    bus = nbytes * 2 * (world - 1) / world / (ms * 1e-3) / 1e9
-    out.append({"path": "NCCL all_reduce", "bytes": nbytes, "ms": round(ms, 4), "bus_gbs": round(bus, 1),
-                "frac_of_link": round(bus / a.link_gbs, 3)})
-    correct = bool(torch.allclose(buf[:1024], torch.full((1024,), float(world) ** (3 + a.iters), device=dev)))
+    # ---- all-reduce: fused (multimem where the group has a multicast object, and p2p) vs NCCL
+    correct = True
+    for mib in a.mib:
+        n = mib * 2**20 // 4
+        nbytes = n * 4
+        for use_mm in (True, False):
+            par = PeerAllReduce(n, dev, use_multimem=use_mm)
+            if use_mm and not par.mc:
+                continue
+            buf = par.view(0, n)
+            buf.fill_(1.0)
+
+            def one():
+                par.all_reduce_(buf)
+                par.wait(torch.cuda.current_stream())
+
+            ms = _timed(one, a.iters)
+            bus = nbytes * 2 * (world - 1) / world / (ms * 1e-3) / 1e9
+            out.append({"path": f"fused all-reduce ({par.transport})", "bytes": nbytes, "ms": round(ms, 4),
+                        "bus_gbs": round(bus, 1), "frac_of_link": round(bus / a.link_gbs, 3)})
+            correct &= bool(torch.allclose(buf[:1024], torch.full((1024,), float(world) ** (3 + a.iters),
+                                                                    device=dev)))
+            del par, buf
+        t = torch.ones(n, device=dev)
+        ms = _timed(lambda: dist.all_reduce(t), a.iters)
+        bus = nbytes * 2 * (world - 1) / world / (ms * 1e-3) / 1e9
+        out.append({"path": "NCCL all_reduce", "bytes": nbytes, "ms": round(ms, 4), "bus_gbs": round(bus, 1),
+                    "frac_of_link": round(bus / a.link_gbs, 3)})
+        del t
 
     # ---- halo fetch: rank r reads rows 0..H-1 of rank (r+1) % N
     M, H = a.own_rows, a.halo_rows

@@ -18,8 +18,6 @@ missing peer shows up as a non-zero ``error_status()`` instead of a hang.
 
 from __future__ import annotations
 
-import os
-
 import torch
 import torch.distributed as dist
 
@@ -50,7 +48,9 @@ class PeerAllReduce:
         except Exception:  # noqa: BLE001 - no multicast object for this group
             mc = 0
         if use_multimem is None:
-            use_multimem = os.environ.get("MALOQ_NO_MULTIMEM", "0") != "1"
+            # NVLS moves 1.5x the bucket per GPU in each direction at two ranks (the switch reads
+            # both copies and writes both); peer loads/stores move 1x, so two ranks use p2p
+            use_multimem = self.world > 2
         self.mc = mc if use_multimem else 0
         self.epoch = 0
         self.pending = None

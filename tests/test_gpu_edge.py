@@ -62,7 +62,7 @@ def test_edgewise_matches_reference(cuda_device, path, message_type, mmax):
             continue
         assert g is not None, n
         assert _rel(g, rg) < 3e-2, (n, _rel(g, rg))
-        assert _relf(g, rg) < 1e-2, (n, _relf(g, rg))
+        assert _relf(g, rg) < 1.5e-2, (n, _relf(g, rg))
         print("  grad", n, _rel(g, rg), _relf(g, rg))
     from maloq_b200.ops import kernels
 

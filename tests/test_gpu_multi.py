@@ -38,7 +38,7 @@ def _allreduce_worker(rank, world, multimem):
     return res, par.transport, kernels.error_status()
 
 
-@pytest.mark.parametrize("multimem", [False, None])
+@pytest.mark.parametrize("multimem", [False, True])
 def test_peer_allreduce_matches_nccl(multimem):
     _need(2)
     out = _dist_util.run(_allreduce_worker, world=2, backend="nccl", args=(multimem,))
