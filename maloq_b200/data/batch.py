@@ -92,6 +92,31 @@ class GraphBatch:
         return getattr(self, key, None) is not None
 
 
+def merge_samples(samples) -> GraphSample:
+    """Disjoint union of molecule samples as one graph (a "supergraph"), for partitioning a
+    batch of molecules over ranks: nodes and edges concatenated with offset indices, targets
+    concatenated along the node / edge axis.  Per-atom charge, spin and molecule id are kept
+    in ``atom_charge`` / ``atom_spin`` / ``atom_mol_id`` (reference: the batched targets of
+    ``fock_utils/fock_targets_batched.py``, ``atom_mol_id``)."""
+    off = 0
+    src, dst, mol, ch, sp = [], [], [], [], []
+    for g, s in enumerate(samples):
+        src.append(s.src + off)
+        dst.append(s.dst + off)
+        mol.append(np.full(s.num_nodes, g, dtype=np.int64))
+        ch.append(np.full(s.num_nodes, s.charge, dtype=np.int64))
+        sp.append(np.full(s.num_nodes, s.spin, dtype=np.int64))
+        off += s.num_nodes
+    m = GraphSample(np.concatenate([s.z for s in samples]), np.concatenate([s.pos for s in samples]),
+                    np.concatenate(src), np.concatenate(dst), np.concatenate([s.edge_attr for s in samples]),
+                    samples[0].charge, samples[0].spin)
+    m.atom_charge, m.atom_spin, m.atom_mol_id = np.concatenate(ch), np.concatenate(sp), np.concatenate(mol)
+    if all(s.node_y is not None for s in samples):
+        m.node_y = torch.cat([torch.as_tensor(s.node_y) for s in samples], dim=1)
+        m.y = torch.cat([torch.as_tensor(s.y) for s in samples], dim=1)
+    return m
+
+
 def collate(samples, pair_table=None, target_dtype=torch.float32, float_dtype=torch.float32) -> GraphBatch:
     zs, pos, ch, sp, bt, srcs, dsts, eattr, nys, ys = [], [], [], [], [], [], [], [], [], []
     off = 0

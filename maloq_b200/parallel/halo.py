@@ -144,8 +144,10 @@ def partition_batch(sample, domain, pair_table=None, device="cpu", transport="co
     kw = dict(
         atomic_numbers=torch.as_tensor(z[own]),
         pos=torch.as_tensor(sample.pos[own], dtype=torch.float32),
-        atom_charge=torch.full((len(own),), sample.charge, dtype=torch.long),
-        atom_spin=torch.full((len(own),), sample.spin, dtype=torch.long),
+        atom_charge=torch.as_tensor(sample.atom_charge[own]) if getattr(sample, "atom_charge", None) is not None
+        else torch.full((len(own),), sample.charge, dtype=torch.long),
+        atom_spin=torch.as_tensor(sample.atom_spin[own]) if getattr(sample, "atom_spin", None) is not None
+        else torch.full((len(own),), sample.spin, dtype=torch.long),
         batch=torch.zeros(len(own), dtype=torch.long),
         edge_index=torch.as_tensor(np.stack([domain.src_local, domain.dst_local])),
         edge_attr=torch.as_tensor(sample.edge_attr[e], dtype=torch.float32),
@@ -157,6 +159,8 @@ def partition_batch(sample, domain, pair_table=None, device="cpu", transport="co
         global_edge_ids=torch.as_tensor(e),
     )
     b = GraphBatch(**kw)
+    if getattr(sample, "atom_mol_id", None) is not None:  # molecule of each owned atom (supergraphs)
+        b.atom_mol_id = torch.as_tensor(sample.atom_mol_id[own])
     if pair_table is not None:
         b.node_pair_type = torch.as_tensor(pair_table.pair_type(z[own], z[own]))
         b.edge_pair_type = torch.as_tensor(pair_table.pair_type(z[src_g], z[dst_g]))

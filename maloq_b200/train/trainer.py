@@ -183,7 +183,8 @@ class SplitTrainer:
                       f"[edge] {self.history['train_edge'][-1]:.6g}  Val: [node] {vn:.6g} [edge] {ve:.6g}  "
                       f"lr {lr:.3g}  time {time.perf_counter() - t0:.2f}s", flush=True)
             done = lr <= min_lr
-            if rank == 0 and ((epoch + 1) % self.save_frequency == 0 or done or epoch + 1 == num_epochs):
+            periodic = self.save_frequency and (epoch + 1) % self.save_frequency == 0  # 0: only at the end
+            if rank == 0 and (periodic or done or epoch + 1 == num_epochs):
                 self.save_training_state(epoch, optimizer, scheduler, output_folder)
             if done:
                 print("Reached minimum learning rate, finished training.", flush=True)

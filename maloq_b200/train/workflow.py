@@ -134,6 +134,8 @@ class TrainingWorkflow:
         c = self.config
         name = c["dataset_name"]
         kind = name[len("synthetic_"):] if name.startswith("synthetic_") else name
+        if name != "cp2k" and kind not in ("sio2", "slab"):
+            return self.prepare_partitioned_molecules()
         if name == "cp2k":
             samples, labeler = self._load_cp2k_folder(dict(c, num_structures=c.get("structure_index", 0) + 1))
             sample = samples[c.get("structure_index", 0)]
@@ -161,6 +163,79 @@ class TrainingWorkflow:
         self.val_samples = []
         self.partition_sample = sample
         return [batch], [batch], labeler
+
+    def prepare_partitioned_molecules(self):
+        """``distribute_graphs`` on a molecule dataset: every batch of ``batch_size`` molecules
+        becomes one graph (their disjoint union) split over all ranks.  Each rank takes its
+        share of the molecules; the ranks then take turns as the source, broadcasting their
+        molecules batch by batch, so that every rank sees every batch and keeps its domain of it
+        (reference ``dataset_utils/get_loader.py:320-400``).  All ranks end with the same number
+        of batches, in the same order."""
+        import torch.distributed as dist
+
+        from ..parallel import partition as P
+        from ..parallel.halo import partition_batch
+
+        c = self.config
+        samples, labeler = self._load_global_samples(c)
+        n_val = c["num_val"] or max(1, len(samples) // 8)
+        n_train = c["num_train"] or (len(samples) - n_val)
+        train, val = samples[:n_train], samples[n_train:n_train + n_val]
+        if c.get("scale_and_shift"):
+            self.scale_shift, self.energy_refs = None, None
+            self._apply_scale_shift(train, samples, labeler, c["dataset_name"])
+        on = dist.is_initialized()
+        world, rank = (self.world_size, self.rank) if on else (1, 0)
+        # GPUs: the halos of molecule batches are small; the collective transport needs no
+        # per-batch symmetric-memory buffers
+        transport = c.get("halo_transport") or "collective"
+
+        def batches(pool):
+            mine = [pool[i] for i in pdist.split_indices(len(pool), rank, world, drop_remainder=False)]
+            counts = [len(mine)]
+            if on and world > 1:
+                counts = [None] * world
+                dist.all_gather_object(counts, len(mine))
+            out = []
+            for src_rank in range(world):
+                for i in range(0, counts[src_rank], c["batch_size"]):
+                    obj = [mine[i:i + c["batch_size"]] if src_rank == rank else None]
+                    if on and world > 1:
+                        dist.broadcast_object_list(obj, src=src_rank)
+                    g = B.merge_samples(obj[0])
+                    part = P.partition(c["partition_type"], g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+                    dom = P.decompose(part, g.src, g.dst, world)[rank]
+                    out.append(partition_batch(g, dom, labeler.table, device=self.device, transport=transport))
+            return out
+
+        self.labeler = labeler
+        self.val_samples = []
+        return batches(train), batches(val), labeler
+
+    def _load_global_samples(self, c):
+        """All molecules of a dataset that every rank reads whole (synthetic, nablaDFT, QM7, one
+        ASE database file)."""
+        name = c["dataset_name"]
+        if name.startswith("synthetic_"):
+            kind = name[len("synthetic_"):]
+            labeler = datasets.labeler_for(kind, self.device)
+            return datasets.build_dataset(kind, c["num_structures"], self.model_kwargs(labeler.layout.lmax),
+                                          seed=c["seed"], device=self.device, cutoff=2 * c["rcut_orbitals"],
+                                          labeler=labeler, target=c["loss_target"])
+        if name == "nablaDFT":
+            from ..data.readers import load_nabladft
+
+            return load_nabladft(c["dbpath"], c, self.device)
+        if name == "QM7":
+            from ..data.readers import load_qm7
+
+            return load_qm7(c["dbpath"], c, self.device)
+        if str(c.get("dbpath", "")).endswith(".db"):
+            from ..data.readers import load_ase_entries
+
+            return load_ase_entries([{"db_file": c["dbpath"], "start_idx": 0, "end_idx": None}], c, self.device,
+                                    basis=c.get("basis_name", "def2_tzvpd"))
+        raise ValueError(f"distribute_graphs: dataset {name!r} is not a molecule dataset read whole by every rank")
 
     def _load_cp2k_folder(self, c):
         """``dbpath``: a folder of structure directories, each with ``structure.xyz`` and
@@ -234,24 +309,10 @@ class TrainingWorkflow:
         if c["distribute_graphs"]:
             return self.prepare_partitioned()
         name = c["dataset_name"]
-        if name.startswith("synthetic_"):
-            kind = name[len("synthetic_"):]
-            labeler = datasets.labeler_for(kind, self.device)
-            kw = self.model_kwargs(labeler.layout.lmax)
-            n = c["num_structures"]
-            samples, labeler = datasets.build_dataset(kind, n, kw, seed=c["seed"], device=self.device,
-                                                      cutoff=2 * c["rcut_orbitals"], labeler=labeler,
-                                                      target=c["loss_target"])
-        elif name == "nablaDFT":
-            from ..data.readers import load_nabladft
-
-            samples, labeler = load_nabladft(c["dbpath"], c, self.device)
+        if name.startswith("synthetic_") or name in ("nablaDFT", "QM7"):
+            samples, labeler = self._load_global_samples(c)
         elif name == "cp2k":
             samples, labeler = self._load_cp2k_folder(c)
-        elif name == "QM7":
-            from ..data.readers import load_qm7
-
-            samples, labeler = load_qm7(c["dbpath"], c, self.device)
         elif name == "omol_csh_58k":
             from ..data.readers import load_omol_csh
 
@@ -391,6 +452,17 @@ class TrainingWorkflow:
                                         dump_embeddings=c.get("dump_embeddings", False),
                                         compute_total_energy=c.get("compute_total_energy", False),
                                         basis_name=c.get("pyscf_basis"), xc=c.get("functional", "b3lyp"))
+            if c["distribute_graphs"] and getattr(self, "partition_sample", None) is None:
+                # molecule batches split over ranks: one block-sparse shard folder per batch
+                from ..parallel.infer import write_partition_hamiltonian
+
+                paths = []
+                with torch.no_grad():
+                    for i, b in enumerate(val):
+                        no, eo = head(backbone(b), b)
+                        paths.append(write_partition_hamiltonian(os.path.join(c["output_folder"], f"batch_{i:04d}"),
+                                                                 b, no[0], eo[0], labeler))
+                return paths
             if c["distribute_graphs"]:
                 b = val[0]
                 s = self.partition_sample
@@ -402,8 +474,13 @@ class TrainingWorkflow:
                 return write_partition_hamiltonian(c["output_folder"], b, no[0], eo[0], labeler,
                                                    global_src=s.src[e], global_dst=s.dst[e])
             return trainer.infer(self.device, val[0].to(self.device), labeler, output_folder=c["output_folder"])
+        except BaseException:
+            # the other ranks may be inside a collective this rank will never join: leave
+            # without the closing barrier (their process-group timeout ends their wait)
+            self.close(sync=False)
+            raise
         finally:
             self.close()
 
-    def close(self):
-        pdist.cleanup_process_group(sync_barrier=self.world_size > 1)
+    def close(self, sync=True):
+        pdist.cleanup_process_group(sync_barrier=sync and self.world_size > 1)
