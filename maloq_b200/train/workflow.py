@@ -165,12 +165,17 @@ class TrainingWorkflow:
         return [batch], [batch], labeler
 
     def prepare_partitioned_molecules(self):
-        """``distribute_graphs`` on a molecule dataset: every batch of ``batch_size`` molecules
-        becomes one graph (their disjoint union) split over all ranks.  Each rank takes its
-        share of the molecules; the ranks then take turns as the source, broadcasting their
-        molecules batch by batch, so that every rank sees every batch and keeps its domain of it
-        (reference ``dataset_utils/get_loader.py:320-400``).  All ranks end with the same number
-        of batches, in the same order."""
+        """``distribute_graphs`` on a molecule dataset: batches of molecules become single graphs
+        (disjoint unions, "supergraphs") split over all ranks; every rank keeps its domain of
+        every supergraph, so all ranks hold the same number of batches in the same order.
+        Each rank first takes its share of the molecules.  Two ways to form the supergraphs
+        (reference ``dataset_utils/get_loader.py:237-413``):
+
+        * training (``all_ranks_contribute``): supergraph i is the union of molecules
+          [i·batch_size, (i+1)·batch_size) of every rank's share, in rank order (all-gathered);
+        * evaluation (``one_rank_contributes``): the ranks take turns as the source,
+          broadcasting their share ``batch_size`` molecules at a time.
+        """
         import torch.distributed as dist
 
         from ..parallel import partition as P
@@ -184,32 +189,45 @@ class TrainingWorkflow:
         if c.get("scale_and_shift"):
             self.scale_shift, self.energy_refs = None, None
             self._apply_scale_shift(train, samples, labeler, c["dataset_name"])
-        on = dist.is_initialized()
+        on = dist.is_initialized() and self.world_size > 1
         world, rank = (self.world_size, self.rank) if on else (1, 0)
+        bs = c["batch_size"]
+        mode = "one_rank_contributes" if c["train_or_eval"] == "eval" else "all_ranks_contribute"
         # GPUs: the halos of molecule batches are small; the collective transport needs no
         # per-batch symmetric-memory buffers
         transport = c.get("halo_transport") or "collective"
 
+        def split(g):
+            part = P.partition(c["partition_type"], g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+            dom = P.decompose(part, g.src, g.dst, world)[rank]
+            return partition_batch(g, dom, labeler.table, device=self.device, transport=transport)
+
         def batches(pool):
             mine = [pool[i] for i in pdist.split_indices(len(pool), rank, world, drop_remainder=False)]
             counts = [len(mine)]
-            if on and world > 1:
+            if on:
                 counts = [None] * world
                 dist.all_gather_object(counts, len(mine))
-            out = []
-            for src_rank in range(world):
-                for i in range(0, counts[src_rank], c["batch_size"]):
-                    obj = [mine[i:i + c["batch_size"]] if src_rank == rank else None]
-                    if on and world > 1:
-                        dist.broadcast_object_list(obj, src=src_rank)
-                    g = B.merge_samples(obj[0])
-                    part = P.partition(c["partition_type"], g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
-                    dom = P.decompose(part, g.src, g.dst, world)[rank]
-                    out.append(partition_batch(g, dom, labeler.table, device=self.device, transport=transport))
-            return out
+            groups = []
+            if mode == "all_ranks_contribute":
+                for i in range(0, max(counts), bs):
+                    parts = [mine[i:i + bs]]
+                    if on:
+                        parts = [None] * world
+                        dist.all_gather_object(parts, mine[i:i + bs])
+                    groups.append([m for p in parts for m in p])
+            else:
+                for src_rank in range(world):
+                    for i in range(0, counts[src_rank], bs):
+                        obj = [mine[i:i + bs] if src_rank == rank else None]
+                        if on:
+                            dist.broadcast_object_list(obj, src=src_rank)
+                        groups.append(obj[0])
+            return [split(B.merge_samples(g)) for g in groups]
 
         self.labeler = labeler
         self.val_samples = []
+        self.supergraph_mode = mode
         return batches(train), batches(val), labeler
 
     def _load_global_samples(self, c):

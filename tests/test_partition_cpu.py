@@ -312,40 +312,42 @@ def test_multilevel_partitioner_beats_greedy_and_balances():
     assert cut_pairs <= 14, cut_pairs
 
 
-def _molecule_batches_worker(rank, world, folder):
+def _molecule_batches_worker(rank, world, folder, mode):
     from maloq_b200.train.workflow import TrainingWorkflow
 
     cfg = dict(dataset_name="synthetic_small", num_structures=10, num_train=7, num_val=3, batch_size=2,
                distribute_graphs=True, partition_type="rcb", l_embedding_dim=8, num_mp_layers=1,
                num_distance_basis=8, mmax=2, num_epochs=2, lr_init=1e-3, device="cpu", output_folder=folder,
-               log_every=0, save_frequency=0)
+               log_every=0, save_frequency=0, train_or_eval=mode)
     wf = TrainingWorkflow(cfg)
     train, val, _ = wf.prepare_data()
     cover = [(b.global_node_ids.numpy(), b.atom_mol_id.numpy(), b.node_y.numpy()) for b in train]
-    hist = wf.run()
-    return len(train), len(val), cover, hist["train_node"]
+    hist = wf.run() if mode == "train" else None
+    return len(train), len(val), cover, hist["train_node"] if hist else None
 
 
-def test_distribute_graphs_over_molecule_batches(tmp_path):
-    """distribute_graphs on a molecule dataset: the ranks' molecules are broadcast batch by batch,
-    each batch's disjoint union is split over both ranks; together the ranks own every atom of
-    every batch exactly once, with its targets, and training runs."""
+@pytest.mark.parametrize("mode", ["train", "eval"])
+def test_distribute_graphs_over_molecule_batches(tmp_path, mode):
+    """distribute_graphs on a molecule dataset: batches of molecules become one disjoint-union
+    graph each, split over both ranks.  Training: supergraph i joins molecules
+    [2i, 2i+2) of every rank's share; evaluation: the ranks take turns broadcasting their share.
+    Together the ranks own every atom of every supergraph exactly once, with its targets, and
+    training runs."""
     from maloq_b200.data import batch as B
-    from maloq_b200.data import datasets
     from maloq_b200.train.workflow import TrainingWorkflow
 
-    out = _dist_util.run(_molecule_batches_worker, world=2, args=(str(tmp_path),))
-    n_tr = {r: o[0] for r, o in out.items()}
-    assert n_tr[0] == n_tr[1] == 4  # 7 molecules: 4 on rank 0, 3 on rank 1 -> 2 + 2 batches of <= 2
-    assert out[0][1] == out[1][1] == 2
-    # the same molecules, read on one process, in the same batch order
+    out = _dist_util.run(_molecule_batches_worker, world=2, args=(str(tmp_path), mode))
     wf = TrainingWorkflow(dict(dataset_name="synthetic_small", num_structures=10, l_embedding_dim=8,
                                num_mp_layers=1, num_distance_basis=8, mmax=2, device="cpu",
                                output_folder=str(tmp_path)))
     samples, _ = wf._load_global_samples(wf.config)
-    train = samples[:7]
-    order = [train[i] for i in [0, 1, 2, 3]] + [train[i] for i in [4, 5, 6]]
-    groups = [order[0:2], order[2:4], order[4:6], order[6:7]]
+    share = [samples[0:4], samples[4:7]]  # 7 training molecules: 4 on rank 0, 3 on rank 1
+    if mode == "train":
+        groups = [share[0][0:2] + share[1][0:2], share[0][2:4] + share[1][2:3]]
+    else:
+        groups = [share[0][0:2], share[0][2:4], share[1][0:2], share[1][2:3]]
+    assert out[0][0] == out[1][0] == len(groups)
+    assert out[0][1] == out[1][1] == (1 if mode == "train" else 2)  # 3 val molecules: 2 + 1
     for k, grp in enumerate(groups):
         g = B.merge_samples(grp)
         ids = np.concatenate([out[r][2][k][0] for r in (0, 1)])
@@ -354,5 +356,6 @@ def test_distribute_graphs_over_molecule_batches(tmp_path):
             own, mol, ny = out[r][2][k]
             assert np.array_equal(mol, g.atom_mol_id[own])
             assert np.allclose(ny, g.node_y[:, own].numpy())
-    for r in (0, 1):
-        assert len(out[r][3]) == 2 and np.isfinite(out[r][3]).all()
+    if mode == "train":
+        for r in (0, 1):
+            assert len(out[r][3]) == 2 and np.isfinite(out[r][3]).all()
