@@ -303,6 +303,43 @@ void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tenso
                           DG.data_ptr<float>(), b16, (int)X.size(0), (int)X.size(2), stream()));
 }
 
+// Fock-head gate: X [B, S, C] fp32, SV [B, (L+1) C] fp32, A [B, S, C] bf16 (act 0 sigmoid, 1 tanh)
+static void head_gate_shapes(int64_t L, const at::Tensor& X, const at::Tensor& SV) {
+  const int64_t S = (L + 1) * (L + 1);
+  TORCH_CHECK(X.dim() == 3 && X.size(1) == S, "head_gate: X must be [B, (L+1)^2, C]");
+  TORCH_CHECK(SV.dim() == 2 && SV.size(0) == X.size(0) && SV.size(1) == (L + 1) * X.size(2),
+              "head_gate: SV must be [B, (L+1) C]");
+}
+
+void head_gate_fwd(int64_t L, at::Tensor X, at::Tensor SV, at::Tensor A, int64_t act, double scale, bool absg) {
+  chk(X, at::kFloat, "X");
+  chk(SV, at::kFloat, "SV");
+  chk(A, at::kBFloat16, "A");
+  head_gate_shapes(L, X, SV);
+  TORCH_CHECK(A.sizes() == X.sizes(), "head_gate_fwd: A must have X's shape");
+  TORCH_CHECK(act == 0 || act == 1, "head_gate: act must be 0 (sigmoid) or 1 (tanh)");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::head_gate_fwd((int)L, X.data_ptr<float>(), SV.data_ptr<float>(), bf(A), (int)act, (float)scale, absg,
+                             (int)X.size(0), (int)X.size(2), stream()));
+}
+
+void head_gate_bwd(int64_t L, at::Tensor X, at::Tensor SV, at::Tensor DA, at::Tensor DX, at::Tensor DSV, int64_t act,
+                   double scale, bool absg) {
+  chk(X, at::kFloat, "X");
+  chk(SV, at::kFloat, "SV");
+  chk(DA, at::kFloat, "DA");
+  chk(DX, at::kFloat, "DX");
+  chk(DSV, at::kFloat, "DSV");
+  head_gate_shapes(L, X, SV);
+  TORCH_CHECK(DA.sizes() == X.sizes() && DX.sizes() == X.sizes() && DSV.sizes() == SV.sizes(),
+              "head_gate_bwd: DA / DX must have X's shape, DSV SV's");
+  TORCH_CHECK(act == 0 || act == 1, "head_gate: act must be 0 (sigmoid) or 1 (tanh)");
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::head_gate_bwd((int)L, X.data_ptr<float>(), SV.data_ptr<float>(), DA.data_ptr<float>(),
+                             DX.data_ptr<float>(), DSV.data_ptr<float>(), (int)act, (float)scale, absg, (int)X.size(0),
+                             (int)X.size(2), stream()));
+}
+
 
 // ---- NVLink peer-memory collectives (pointers come from torch symmetric memory handles)
 void peer_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch, int64_t slot_base, int64_t spin_limit) {
@@ -490,6 +527,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ln_silu_bwd", &ln_silu_bwd);
   m.def("gate_l_fwd", &gate_l_fwd);
   m.def("gate_l_bwd", &gate_l_bwd);
+  m.def("head_gate_fwd", &head_gate_fwd);
+  m.def("head_gate_bwd", &head_gate_bwd);
   m.def("peer_barrier", &peer_barrier);
   m.def("allreduce_p2p", &allreduce_p2p);
   m.def("allreduce_multimem", &allreduce_multimem);

@@ -6,10 +6,14 @@
 //   Reference math: helm/nn/layer_norm.py:290-338.
 // * layernorm_silu: silu(LayerNorm(x)) on rows of width W (<= 1024), one warp per row.
 // * gate_l: the l-outer gate of the atomwise block (helm/nn/activation.py:57-77).
+// * head_gate: the gated operand of the Fock head's per-degree projections
+//   (helm/esen_osh.py:986-1052): row 0 the transformed scalars, every l >= 1 coefficient times
+//   its activated gate (sigmoid or tanh of the raw, optionally absolute, gate, times a scale).
 // Parameter gradients are written as per-CTA partial sums (grid-stride over rows) and summed
 // by the caller in a fixed order, so they are deterministic.
 #include "common.cuh"
 #include "norm.h"
+#include "head_gate.cuh"
 
 namespace maloq {
 
@@ -414,6 +418,26 @@ const char* gate_l_bwd(int L, const void* X, const float* Gt, const void* DO, vo
   MALOQ_DISPATCH_L((gate_l_bwd_kernel<LL, float><<<grid, 256, 0, st>>>(static_cast<const float*>(X), Gt,
                                                                       static_cast<const float*>(DO),
                                                                       static_cast<float*>(DX), DG, B, H)))
+}
+
+const char* head_gate_fwd(int L, const float* X, const float* SV, __nv_bfloat16* A, int act, float scale, bool absg,
+                          int B, int C, cudaStream_t st) {
+  if (B == 0) return nullptr;
+  const int grid = (int)std::min<long long>(((long long)B * C + 255) / 256, 148 * 32);
+  if (act == 0) {
+    MALOQ_DISPATCH_L((head_gate_fwd_kernel<LL, 0><<<grid, 256, 0, st>>>(X, SV, A, B, C, scale, absg)))
+  }
+  MALOQ_DISPATCH_L((head_gate_fwd_kernel<LL, 1><<<grid, 256, 0, st>>>(X, SV, A, B, C, scale, absg)))
+}
+
+const char* head_gate_bwd(int L, const float* X, const float* SV, const float* DA, float* DX, float* DSV, int act,
+                          float scale, bool absg, int B, int C, cudaStream_t st) {
+  if (B == 0) return nullptr;
+  const int grid = (int)std::min<long long>(((long long)B * C + 255) / 256, 148 * 32);
+  if (act == 0) {
+    MALOQ_DISPATCH_L((head_gate_bwd_kernel<LL, 0><<<grid, 256, 0, st>>>(X, SV, DA, DX, DSV, B, C, scale, absg)))
+  }
+  MALOQ_DISPATCH_L((head_gate_bwd_kernel<LL, 1><<<grid, 256, 0, st>>>(X, SV, DA, DX, DSV, B, C, scale, absg)))
 }
 
 }  // namespace maloq

@@ -22,5 +22,12 @@ const char* ln_silu_bwd(const float* X, const float* w, const float* b, const __
 const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st);
 const char* gate_l_bwd(int L, const void* X, const float* Gt, const void* DO, void* DX, float* DG, bool bf16, int B,
                        int H, cudaStream_t st);
+// Fock-head gate: X [B, (L+1)^2, C] fp32, SV [B, (L+1) C] fp32 (transformed scalars | raw
+// gates), A [B, (L+1)^2, C] bf16; act 0 sigmoid, 1 tanh; gates = scale * act(|u| if absg else u).
+// Backward: DA fp32 -> DX (row 0 zero), DSV.
+const char* head_gate_fwd(int L, const float* X, const float* SV, __nv_bfloat16* A, int act, float scale, bool absg,
+                          int B, int C, cudaStream_t st);
+const char* head_gate_bwd(int L, const float* X, const float* SV, const float* DA, float* DX, float* DSV, int act,
+                          float scale, bool absg, int B, int C, cudaStream_t st);
 
 }  // namespace maloq

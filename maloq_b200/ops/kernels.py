@@ -147,7 +147,7 @@ def linear(x, weight, bias=None, act=None, out_dtype=None):
 # ------------------------------------------------------------------ ops still on PyTorch glue
 # These run PyTorch on the CUDA tensors until their fused kernels land; each is listed so the
 # set of non-kernel ops is explicit.
-TORCH_GLUE = ("fock_head_process", "gather_scale")
+TORCH_GLUE = ("gather_scale",)
 
 
 @register("layernorm_silu")
@@ -186,24 +186,123 @@ def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
     return norm_native.so3_linear(x, weight, bias, lmax, out_dtype, residual)
 
 
+def _pad8(n):
+    return (n + 7) // 8 * 8
+
+
+_HEAD_COLS = {}
+
+
+class _FockHeadFn(torch.autograd.Function):
+    """Gated per-degree projections of the Fock head (reference ``esen_osh.py:986-1052``).
+
+    ``head_gate`` writes the bf16 GEMM operand A [N, S, C] in one pass (row 0 the transformed
+    scalars, every l >= 1 coefficient times its activated gate).  One grouped-GEMM problem per
+    coefficient j projects A[:, j] with its degree's weight into column block j of one fp32
+    buffer Y (blocks padded to 8 columns); one gather puts Y's columns into the head's sorted
+    order (per degree, e3nn's (channel, m) flattening).  Backward: the gather's transpose, one
+    grouped input-gradient GEMM, split-K weight gradients summed per degree in a fixed order, and
+    ``head_gate_bwd`` for the gradients of x and of the scalar linear's output."""
+
+    @staticmethod
+    def forward(ctx, x, sv, act, scale, absg, present, *wb):
+        from .norm_native import _run_problems
+
+        N, S, C = x.shape
+        L = int(round(S ** 0.5)) - 1
+        ls = [l for l in range(L + 1) if present[l]]
+        ws = dict(zip(ls, wb[0::2]))
+        bs = dict(zip(ls, wb[1::2]))
+        mul = {l: ws[l].shape[0] for l in ls}
+        x = x.contiguous().float()
+        sv = sv.contiguous().float()
+        A = torch.empty(N, S, C, device=x.device, dtype=torch.bfloat16)
+        lib().head_gate_fwd(L, x, sv, A, 0 if act == "sigmoid" else 1, float(scale), bool(absg))
+        js = [j for j in range(S) if int(j ** 0.5) in mul]
+        lj = {j: int(j ** 0.5) for j in js}
+        off, o = {}, 0
+        for j in js:
+            off[j] = o
+            o += _pad8(mul[lj[j]])
+        key = (x.device, L, tuple(sorted(mul.items())))
+        if key not in _HEAD_COLS:
+            cols = [off[l * l + m] + oo for l in ls for oo in range(mul[l]) for m in range(2 * l + 1)]
+            _HEAD_COLS[key] = torch.tensor(cols, dtype=torch.long, device=x.device)
+        cols = _HEAD_COLS[key]
+        wpad, bpad = {}, {}
+        for l in ls:
+            w = ws[l].to(torch.bfloat16)
+            wpad[l] = torch.nn.functional.pad(w, (0, 0, 0, _pad8(mul[l]) - mul[l])).contiguous()
+            bpad[l] = None if bs[l] is None else \
+                torch.nn.functional.pad(bs[l].float(), (0, _pad8(mul[l]) - mul[l])).contiguous()
+        Y = torch.empty(N, o, device=x.device, dtype=torch.float32)
+        A2 = A.view(N, S * C)
+        if N > 0:
+            _run_problems([A2[:, j * C:(j + 1) * C] for j in js], [wpad[lj[j]] for j in js],
+                          [Y[:, off[j]:off[j] + _pad8(mul[lj[j]])] for j in js], [bpad[lj[j]] for j in js])
+        count_launches(2)
+        ctx.save_for_backward(x, sv, A, *[ws[l] for l in ls])
+        ctx.meta = (L, ls, mul, js, lj, off, o, act, float(scale), bool(absg), cols, [bs[l] is not None for l in ls])
+        return Y.index_select(1, cols)
+
+    @staticmethod
+    def backward(ctx, g):
+        from .norm_native import _run_problems
+
+        x, sv, A = ctx.saved_tensors[:3]
+        wlist = ctx.saved_tensors[3:]
+        L, ls, mul, js, lj, off, width, act, scale, absg, cols, has_b = ctx.meta
+        N, S, C = x.shape
+        dY = torch.zeros(N, width, device=g.device, dtype=torch.float32)
+        dY.index_copy_(1, cols, g.float().contiguous())
+        dYb = dY.to(torch.bfloat16)
+        dA = torch.empty(N, S, C, device=g.device, dtype=torch.float32)
+        dA2 = dA.view(N, S * C)
+        for j in range(S):  # coefficients of degrees without outputs: no gradient reaches them
+            if j not in lj:
+                dA2[:, j * C:(j + 1) * C].zero_()
+        wt = {l: torch.nn.functional.pad(w.to(torch.bfloat16), (0, 0, 0, _pad8(mul[l]) - mul[l])).t().contiguous()
+              for l, w in zip(ls, wlist)}
+        splits = max(1, min(-(-296 // max(1, len(js))), N // 2048, 16))
+        parts = {j: torch.empty(splits, _pad8(mul[lj[j]]), C, device=g.device, dtype=torch.float32) for j in js}
+        A2 = A.view(N, S * C)
+        if N > 0:
+            _run_problems([dYb[:, off[j]:off[j] + _pad8(mul[lj[j]])] for j in js], [wt[lj[j]] for j in js],
+                          [dA2[:, j * C:(j + 1) * C] for j in js], [None] * len(js))
+            _run_problems([dYb[:, off[j]:off[j] + _pad8(mul[lj[j]])] for j in js],
+                          [A2[:, j * C:(j + 1) * C] for j in js], [parts[j] for j in js], [None] * len(js),
+                          mn=True, splits=splits)
+        grads = []
+        for l, hb in zip(ls, has_b):
+            jl = [j for j in js if lj[j] == l]
+            if N > 0:
+                dw = parts[jl[0]].sum(0)
+                for j in jl[1:]:
+                    dw = dw + parts[j].sum(0)
+            else:
+                dw = torch.zeros(_pad8(mul[l]), C, device=g.device)
+            grads.append(dw[:mul[l]])
+            db = None
+            if hb:
+                db = dY[:, off[jl[0]]:off[jl[0]] + mul[l]].sum(0)
+                for j in jl[1:]:
+                    db = db + dY[:, off[j]:off[j] + mul[l]].sum(0)
+            grads.append(db)
+        dx = torch.empty_like(x)
+        dsv = torch.empty_like(sv)
+        lib().head_gate_bwd(L, x, sv, dA, dx, dsv, 0 if act == "sigmoid" else 1, scale, absg)
+        count_launches(4)
+        return (dx, dsv, None, None, None, None, *grads)
+
+
 def _head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):
-    N, S, C = x.shape
-    L = int(round(S ** 0.5)) - 1
-    s = linear(x[:, 0], ws, bs)
-    t0, g = s[:, :C], s[:, C:]
-    if abs_gates:
-        g = g.abs()
-    g = (torch.sigmoid(g) if act == "sigmoid" else torch.tanh(g)) * act_scale
-    g = g.view(N, L, C)
-    outs = []
-    for l in range(L + 1):
-        w, b = layer_params[l]
-        if w is None:
-            continue
-        xl = t0.unsqueeze(1) if l == 0 else x[:, l * l:(l + 1) ** 2] * g[:, l - 1].unsqueeze(1)
-        yl = linear(xl, w, b)
-        outs.append(yl.transpose(1, 2).reshape(N, -1))
-    return torch.cat(outs, dim=1)
+    sv = linear(x[:, 0], ws, bs)
+    present = tuple(w is not None for w, _ in layer_params)
+    wb = []
+    for w, b in layer_params:
+        if w is not None:
+            wb += [w, b]
+    return _FockHeadFn.apply(x, sv, act, act_scale, abs_gates, present, *wb)
 
 
 @register("edgewise")

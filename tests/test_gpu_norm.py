@@ -90,3 +90,40 @@ def test_so3_linear(cuda_device):
     gr = torch.autograd.grad((R.so3_linear(x, W, b, 4) * g).sum(), [x, W, b])
     for a, bb in zip(ga, gr):
         assert _rel(a, bb) < 2e-2
+
+
+@pytest.mark.parametrize("act,absg,muls,N", [("sigmoid", False, [14, 0, 9, 3, 1], 700),
+                                             ("tanh", True, [14, 10, 9, 3, 1], 5000)])
+def test_fock_head_process_kernel(cuda_device, act, absg, muls, N):
+    """Fock head process step on the kernel path (head_gate + per-coefficient grouped GEMMs +
+    sorted-order gather) vs its fp32 PyTorch definition, forward and gradients."""
+    from maloq_b200.ops import kernels
+    from maloq_b200.ops import reference as R
+
+    torch.manual_seed(5)
+    L, C = 4, 128
+    S = (L + 1) ** 2
+    dev = cuda_device
+    x = torch.randn(N, S, C, device=dev, requires_grad=True)
+    ws = torch.nn.Parameter(torch.randn((L + 1) * C, C, device=dev) / C ** 0.5)
+    bs = torch.nn.Parameter(torch.randn((L + 1) * C, device=dev) * 0.1)
+    layers = []
+    for l, m in enumerate(muls):
+        if m == 0:
+            layers.append((None, None))
+            continue
+        w = torch.nn.Parameter(torch.randn(m, C, device=dev) / C ** 0.5)
+        b = torch.nn.Parameter(torch.randn(m, device=dev) * 0.1) if l == 0 else None
+        layers.append((w, b))
+    params = [x, ws, bs] + [t for wb in layers for t in wb if t is not None]
+    out = kernels._head_process(x, ws, bs, layers, act, 1.3, absg)
+    ref = R.fock_head_process(x, ws, bs, layers, act, 1.3, absg)
+    relf = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()
+    assert out.shape == ref.shape
+    assert relf(out, ref) < 1e-2, relf(out, ref)
+    g = torch.randn_like(ref)
+    got = torch.autograd.grad((out * g).sum(), params)
+    want = torch.autograd.grad((ref * g).sum(), params)
+    for a, b in zip(got, want):
+        assert relf(a, b) < 1.5e-2, relf(a, b)
+    assert kernels.error_status() == 0

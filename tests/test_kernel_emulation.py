@@ -1,0 +1,170 @@
+"""CUDA kernels whose source also builds as host C++ (no shared memory, warp intrinsics or
+synchronisation), run over an emulated grid on the CPU and compared with PyTorch.  This checks
+the kernels' own index arithmetic and math without a GPU; the GPU tests check the same kernels on
+the device."""
+import ctypes
+import os
+import shutil
+import subprocess
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "..", "maloq_b200", "ops", "csrc")
+CUDA_INC = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+
+
+@pytest.fixture(scope="module")
+def emu(tmp_path_factory):
+    cxx = shutil.which("g++")
+    if cxx is None or not os.path.isfile(os.path.join(CUDA_INC, "cuda_bf16.h")):
+        pytest.skip("needs g++ and the CUDA headers")
+    so = str(tmp_path_factory.mktemp("emu") / "head_gate_emu.so")
+    subprocess.run([cxx, "-O1", "-std=c++17", "-shared", "-fPIC", "-I", CSRC, "-I", CUDA_INC,
+                    os.path.join(HERE, "csrc", "head_gate_emu.cpp"), "-o", so], check=True)
+    return ctypes.CDLL(so)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _gate_ref(x, sv, act, scale, absg):
+    """The Fock head's gated operand (ops/reference.py fock_head_process, before the per-degree
+    linears): row 0 the transformed scalars, every l >= 1 coefficient times its gate."""
+    N, S, C = x.shape
+    L = int(round(S ** 0.5)) - 1
+    t0, g = sv[:, :C], sv[:, C:]
+    if absg:
+        g = g.abs()
+    g = (torch.sigmoid(g) if act == 0 else torch.tanh(g)) * scale
+    g = g.view(N, L, C)
+    rows = [t0.unsqueeze(1)]
+    for l in range(1, L + 1):
+        rows.append(x[:, l * l:(l + 1) ** 2] * g[:, l - 1].unsqueeze(1))
+    return torch.cat(rows, dim=1)
+
+
+@pytest.mark.parametrize("L,C,act,absg", [(0, 8, 0, False), (1, 5, 1, True), (2, 128, 0, True), (4, 128, 1, False),
+                                          (4, 33, 0, False), (6, 16, 1, True)])
+@pytest.mark.parametrize("grid", [1, 3, 64])
+def test_head_gate_kernels_on_emulated_grid(emu, L, C, act, absg, grid):
+    torch.manual_seed(L * 100 + C + grid)
+    N, S = 7, (L + 1) ** 2
+    scale = 1.7
+    x = torch.randn(N, S, C, dtype=torch.float32, requires_grad=True)
+    sv = torch.randn(N, (L + 1) * C, dtype=torch.float32, requires_grad=True)
+    with torch.no_grad():
+        sv[0, C:C + 3] = 0.0  # |u| at u = 0: zero gradient, as PyTorch's abs
+    A = torch.empty(N, S, C, dtype=torch.bfloat16)
+    assert emu.emu_head_gate_fwd(L, _p(x), _p(sv), _p(A), act, ctypes.c_float(scale), int(absg), N, C, grid, 32) == 0
+    ref = _gate_ref(x, sv, act, scale, absg)
+    # bf16 rounding of the same fp32 value; the host's tanhf / expf may differ from PyTorch's by
+    # an ulp, which can move a value across a bf16 rounding boundary (one bf16 ulp: 2^-8 relative)
+    r = ref.detach()
+    np.testing.assert_allclose(A.float().numpy(), r.numpy(), rtol=2 ** -8, atol=1e-30)
+    assert (A != r.to(torch.bfloat16)).float().mean().item() < 0.01
+    dA = torch.randn(N, S, C)
+    dx, dsv = torch.full_like(x, float("nan")), torch.full_like(sv, float("nan"))
+    assert emu.emu_head_gate_bwd(L, _p(x), _p(sv), _p(dA), _p(dx), _p(dsv), act, ctypes.c_float(scale), int(absg),
+                                 N, C, grid, 32) == 0
+    rdx, rdsv = torch.autograd.grad(ref, [x, sv], dA, allow_unused=True)
+    rdx = torch.zeros_like(x) if rdx is None else rdx
+    np.testing.assert_allclose(dx.numpy(), rdx.numpy(), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(dsv.numpy(), rdsv.numpy(), rtol=1e-5, atol=1e-6)
+
+
+class _CpuExtension:
+    """Stand-in for the compiled extension on CPU tensors: GEMMs as PyTorch matmuls with the
+    extension's operand conventions (bf16 operands, fp32 accumulation; ``mn`` = weight-gradient
+    form C = A^T B, split-K slices over the rows), the head gate through the emulated kernels.
+    It lets the Python side of a kernel path (views, strides, padding, ordering, autograd) run
+    on the CPU."""
+
+    def __init__(self, emu):
+        self.emu = emu
+
+    def gemm(self, As, Bs, Cs, biases, mn, act, alpha, splits, bn, resids=()):
+        assert 1 <= len(As) <= 8 and len(Bs) == len(Cs) == len(As)
+        for i, (a, b, c) in enumerate(zip(As, Bs, Cs)):
+            # the extension's argument checks, and the 16-byte rule of its TMA descriptors
+            assert a.dtype == b.dtype == torch.bfloat16 and a.dim() == b.dim() == 2
+            assert a.stride(1) == 1 and b.stride(1) == 1 and c.stride(-1) == 1
+            M, K, N = (a.shape[1], a.shape[0], b.shape[1]) if mn else (a.shape[0], a.shape[1], b.shape[0])
+            assert (b.shape[0] if mn else b.shape[1]) == K
+            if splits > 1 or c.dim() == 3:
+                assert c.dim() == 3 and c.dtype == torch.float32 and tuple(c.shape) == (splits, M, N)
+            else:
+                assert tuple(c.shape) == (M, N)
+            for t in (a, b, c):
+                assert t.data_ptr() % 16 == 0 and all((st * t.element_size()) % 16 == 0 for st in t.stride()[:-1])
+            a, b = a.float(), b.float()
+            if mn:
+                if c.dim() == 3:
+                    rows = torch.arange(a.shape[0])
+                    for s in range(c.shape[0]):
+                        sel = rows[s::c.shape[0]]
+                        c[s] = a[sel].T @ b[sel]
+                    continue
+                y = a.T @ b
+            else:
+                y = alpha * (a @ b.T)
+            if biases[i] is not None:
+                y = y + biases[i]
+            if act == 1:
+                y = torch.nn.functional.silu(y)
+            if i < len(resids) and resids[i] is not None:
+                y = y + resids[i]
+            c.copy_(y.to(c.dtype))
+
+    def splitk_reduce(self, part, out, beta):
+        out.copy_(part.sum(0).view_as(out) + beta * out)
+
+    def head_gate_fwd(self, L, x, sv, A, act, scale, absg):
+        N, S, C = x.shape
+        assert self.emu.emu_head_gate_fwd(L, _p(x), _p(sv), _p(A), act, ctypes.c_float(scale), int(absg), N, C,
+                                          max(1, min((N * C + 255) // 256, 148 * 32)), 256) == 0
+
+    def head_gate_bwd(self, L, x, sv, dA, dx, dsv, act, scale, absg):
+        N, S, C = x.shape
+        assert self.emu.emu_head_gate_bwd(L, _p(x), _p(sv), _p(dA), _p(dx), _p(dsv), act, ctypes.c_float(scale),
+                                          int(absg), N, C, max(1, min((N * C + 255) // 256, 148 * 32)), 256) == 0
+
+
+@pytest.mark.parametrize("act,absg,muls", [("sigmoid", False, [3, 0, 5, 2, 1]), ("tanh", True, [9, 4, 0, 11, 6])])
+def test_fock_head_kernel_path_on_cpu(emu, monkeypatch, act, absg, muls):
+    """The kernel path of the Fock head's process step (head_gate + per-coefficient grouped GEMMs
+    + sorted-order gather, and its backward) against the PyTorch definition, with bf16 GEMM
+    operands emulated on the CPU."""
+    from maloq_b200.ops import kernels
+    from maloq_b200.ops import reference as R
+
+    monkeypatch.setattr(kernels, "_lib", _CpuExtension(emu))
+    torch.manual_seed(3)
+    L, C, N = 4, 16, 37
+    S = (L + 1) ** 2
+    x = torch.randn(N, S, C, requires_grad=True)
+    ws = torch.nn.Parameter(torch.randn((L + 1) * C, C) / C ** 0.5)
+    bs = torch.nn.Parameter(torch.randn((L + 1) * C) * 0.1)
+    layers = []
+    for l, m in enumerate(muls):
+        if m == 0:
+            layers.append((None, None))
+            continue
+        w = torch.nn.Parameter(torch.randn(m, C) / C ** 0.5)
+        b = torch.nn.Parameter(torch.randn(m) * 0.1) if l == 0 else None
+        layers.append((w, b))
+    params = [x, ws, bs] + [t for wb in layers for t in wb if t is not None]
+    out = kernels._head_process(x, ws, bs, layers, act, 1.3, absg)
+    ref = R.fock_head_process(x, ws, bs, layers, act, 1.3, absg)
+    assert out.shape == ref.shape == (N, sum(m * (2 * l + 1) for l, m in enumerate(muls)))
+    rel = lambda a, b: ((a - b).norm() / b.norm()).item()
+    assert rel(out, ref) < 1e-2  # bf16 GEMM operands
+    g = torch.randn_like(ref)
+    got = torch.autograd.grad((out * g).sum(), params)
+    want = torch.autograd.grad((ref * g).sum(), params)
+    for a, b in zip(got, want):
+        assert a.shape == b.shape
+        assert rel(a, b) < 2e-2, rel(a, b)
