@@ -122,3 +122,49 @@ def _slow_worker(rank, world):
 def test_delayed_rank_completes_within_timeout():
     out = _dist_util.run(_slow_worker, world=2)
     assert all(v == 3.0 for v in out.values())
+
+
+def _crash_resume_worker(rank, world, folder, phase):
+    """phase "full": 3 epochs uninterrupted; "crash": rank 1 raises in its first step of epoch 3
+    (after the epoch-2 checkpoint); "resume": restart from the checkpoint and finish epoch 3."""
+    from maloq_b200.train import trainer as T
+    from maloq.train_utils import training_workflow
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=12, num_val=2, batch_size=3, num_epochs=3,
+               l_embedding_dim=8, num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0,
+               mmax=2, output_folder=folder, device="cpu", save_frequency=1, log_every=0, lr_init=3e-3)
+    if phase == "resume":
+        cfg.update(restart_backbone=True, restart_head=True, restart_optimizer=True)
+    if phase == "crash" and rank == 1:
+        step = T.SplitTrainer.train_step
+        calls = [0]
+
+        def failing_step(self, *a, **k):
+            calls[0] += 1
+            if calls[0] == 2 * 2 + 1:  # two batches per epoch on each rank
+                raise RuntimeError("injected crash on rank 1")
+            return step(self, *a, **k)
+
+        T.SplitTrainer.train_step = failing_step
+    try:
+        hist = training_workflow.TrainingWorkflow(cfg).run()
+    except Exception as e:  # noqa: BLE001 - the failure is the result of this phase
+        return "crashed: " + type(e).__name__ + ": " + str(e)[:200]
+    sd = torch.load(f"{folder}/backbone.pt", weights_only=False)["model_state_dict"]
+    return hist["train_node"], {k: v for k, v in sd.items() if v.is_floating_point()}
+
+
+def test_crashed_rank_ends_the_job_and_resume_matches_uninterrupted_run(tmp_path):
+    """A rank that raises mid-training ends the job on every rank (the other rank's collective
+    fails instead of hanging); restarting from the last checkpoint (weights, optimizer,
+    scheduler, epoch, RNG) reproduces the uninterrupted run bit for bit."""
+    full = _dist_util.run(_crash_resume_worker, world=2, args=(str(tmp_path / "full"), "full"))
+    crash = _dist_util.run(_crash_resume_worker, world=2, args=(str(tmp_path / "run"), "crash"), timeout=300)
+    assert "injected crash" in crash[1]
+    assert crash[0].startswith("crashed")
+    res = _dist_util.run(_crash_resume_worker, world=2, args=(str(tmp_path / "run"), "resume"))
+    h_full, sd_full = full[0]
+    h_res, sd_res = res[0]
+    assert len(h_res) == 3 and h_res == h_full
+    for k in sd_full:
+        assert (sd_full[k] == sd_res[k]).all(), k
