@@ -264,32 +264,8 @@ class SplitTrainer:
                     rows.append((k, float("nan"), err, s.num_nodes))
                 continue
             no, eo = out
-            no, eo = no[0], eo[0]
-            if scale_shift is not None:
-                no = scale_shift.unshift(no, s.z)
-                ty = scale_shift.unshift(b.node_y[0], s.z)
-            else:
-                ty = b.node_y[0]
-            bp = labeler.blocks_from_labels(s, no, eo)
-            bt = labeler.blocks_from_labels(s, ty, b.y[0])
-            Hp, Ht = bp.to_dense(), bt.to_dense()
-            Hp = 0.5 * (Hp + Hp.T)
-            S = getattr(s, "overlap", None)
-            ne = electronic.n_electrons(s.z, getattr(s, "charge", 0))
-            sp_, st_ = electronic.summary(Hp, S, ne), electronic.summary(Ht, S, ne)
-            ep, et = sp_["eigenvalues"], st_["eigenvalues"]
-
-            def err(key):
-                return float("nan") if sp_[key] is None else abs(sp_[key] - st_[key])
-
-            row = [k, float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), err("gap"), err("band_energy")]
-            if compute_total_energy:
-                te = float("nan")
-                if mol_of is not None:
-                    mol = mol_of(s)
-                    te = abs(electronic.total_energy(mol, Hp, S, xc) - electronic.total_energy(mol, Ht, S, xc))
-                row.append(te)
-            rows.append(tuple(row + [s.num_nodes]))
+            rows.append((k,) + self._fock_metrics(s, no[0], eo[0], b.node_y[0], b.y[0], labeler, scale_shift,
+                                                   compute_total_energy, mol_of, xc))
         os.makedirs(output_folder, exist_ok=True)
         if rows and len(rows[0]) == 4:
             with open(os.path.join(output_folder, f"model_energy_eval_{rank}.txt"), "w") as f:
@@ -302,6 +278,82 @@ class SplitTrainer:
                     + ("Total_Energy_Error\t" if compute_total_energy else "") + "Num_Atoms\n")
             for r in rows:
                 f.write("\t".join(str(x) for x in r) + "\n")
+        return rows
+
+    @staticmethod
+    def _fock_metrics(s, no, eo, ty, y, labeler, scale_shift, compute_total_energy, mol_of, xc):
+        """Errors of one structure's predicted labels (no, eo) against its targets (ty, y):
+        Hamiltonian MAE, orbital-energy MAE, gap and band-energy errors (and total energy)."""
+        from ..eval import electronic
+
+        if scale_shift is not None:
+            no = scale_shift.unshift(no, s.z)
+            ty = scale_shift.unshift(ty, s.z)
+        bp = labeler.blocks_from_labels(s, no, eo)
+        bt = labeler.blocks_from_labels(s, ty, y)
+        Hp, Ht = bp.to_dense(), bt.to_dense()
+        Hp = 0.5 * (Hp + Hp.T)
+        S = getattr(s, "overlap", None)
+        ne = electronic.n_electrons(s.z, getattr(s, "charge", 0))
+        sp_, st_ = electronic.summary(Hp, S, ne), electronic.summary(Ht, S, ne)
+        ep, et = sp_["eigenvalues"], st_["eigenvalues"]
+
+        def err(key):
+            return float("nan") if sp_[key] is None else abs(sp_[key] - st_[key])
+
+        row = [float(np.abs(Hp - Ht).mean()), float(np.abs(ep - et).mean()), err("gap"), err("band_energy")]
+        if compute_total_energy:
+            te = float("nan")
+            if mol_of is not None:
+                mol = mol_of(s)
+                te = abs(electronic.total_energy(mol, Hp, S, xc) - electronic.total_energy(mol, Ht, S, xc))
+            row.append(te)
+        return tuple(row + [s.num_nodes])
+
+    @torch.no_grad()
+    def evaluate_partitioned(self, device, batches, groups, labeler, output_folder="outputs", scale_shift=None,
+                             **unused):
+        """Evaluation of molecule supergraphs split over the ranks: every rank runs its domain of
+        each supergraph; the owned node rows and local edge rows are gathered to rank 0 (uneven,
+        as objects), put back in the supergraph's order and cut into molecules, whose metrics
+        rank 0 writes to ``model_fock_eval_0.txt`` (reference ``splittrainer.py:1270-1404``).
+        ``groups[i]`` are the molecules of ``batches[i]`` in the order they were merged."""
+        self.backbone.eval()
+        self.head.eval()
+        rank, world = _rank(), _world()
+        rows = []
+        k = 0
+        for b, group in zip(batches, groups):
+            no, eo = self.head(self.backbone(b), b)
+            mine = (b.global_node_ids.cpu(), no[0].float().cpu(), b.global_edge_ids.cpu(), eo[0].float().cpu())
+            parts = [mine]
+            if world > 1:
+                parts = [None] * world
+                dist.all_gather_object(parts, mine)
+            if rank != 0:
+                k += len(group)
+                continue
+            n_all = sum(len(m.z) for m in group)
+            e_all = sum(len(m.src) for m in group)
+            node = torch.zeros(n_all, no.shape[-1])
+            edge = torch.zeros(e_all, eo.shape[-1])
+            for ids, nv, eids, ev in parts:
+                node[ids] = nv
+                edge[eids] = ev
+            n0 = e0 = 0
+            for m in group:
+                n1, e1 = n0 + len(m.z), e0 + len(m.src)
+                rows.append((k,) + self._fock_metrics(m, node[n0:n1].to(device), edge[e0:e1].to(device),
+                                                      torch.as_tensor(m.node_y[0]).to(device),
+                                                      torch.as_tensor(m.y[0]).to(device), labeler, scale_shift,
+                                                      False, None, None))
+                n0, e0, k = n1, e1, k + 1
+        if rank == 0:
+            os.makedirs(output_folder, exist_ok=True)
+            with open(os.path.join(output_folder, "model_fock_eval_0.txt"), "w") as f:
+                f.write("Index\tTotal_MAE\tEigenvalue_MAE\tGap_Error\tBand_Energy_Error\tNum_Atoms\n")
+                for r in rows:
+                    f.write("\t".join(str(x) for x in r) + "\n")
         return rows
 
     @torch.no_grad()

@@ -223,12 +223,14 @@ class TrainingWorkflow:
                         if on:
                             dist.broadcast_object_list(obj, src=src_rank)
                         groups.append(obj[0])
-            return [split(B.merge_samples(g)) for g in groups]
+            return [split(B.merge_samples(g)) for g in groups], groups
 
         self.labeler = labeler
         self.val_samples = []
         self.supergraph_mode = mode
-        return batches(train), batches(val), labeler
+        tr, _ = batches(train)
+        va, self.val_groups = batches(val)
+        return tr, va, labeler
 
     def _load_global_samples(self, c):
         """All molecules of a dataset that every rank reads whole (synthetic, nablaDFT, QM7, one
@@ -463,6 +465,10 @@ class TrainingWorkflow:
                                      val_loader=val, output_folder=c["output_folder"],
                                      step_every_epoch=c["step_every_epoch"] if "step_every_epoch" in c else False,
                                      log_every=c.get("log_every", 1))
+            if c["train_or_eval"] == "eval" and getattr(self, "val_groups", None) is not None:
+                return trainer.evaluate_partitioned(self.device, val, self.val_groups, labeler,
+                                                    output_folder=c["output_folder"],
+                                                    scale_shift=getattr(self, "scale_shift", None))
             if c["train_or_eval"] == "eval":
                 return trainer.evaluate(c["test_loss_fxn"], self.device, val, labeler,
                                         output_folder=c["output_folder"], samples=self.val_samples,
