@@ -50,9 +50,9 @@ def src_csr(graph):
         src = graph.src
         n = graph.num_nodes_ext if hasattr(graph, "num_nodes_ext") else graph.num_nodes
         perm = torch.argsort(src, stable=True)
-        cnt = torch.bincount(src, minlength=n)
-        ptr = torch.zeros(n + 1, dtype=torch.long, device=src.device)
-        ptr[1:] = torch.cumsum(cnt, 0)
+        # ptr[i] = number of edges with source < i: a search in the sorted sources, which (unlike
+        # a bincount) needs no device-to-host read of the largest index
+        ptr = torch.searchsorted(src[perm], torch.arange(n + 1, device=src.device, dtype=src.dtype))
         graph.cache[key] = (perm, ptr)
     return graph.cache[key]
 

@@ -392,3 +392,25 @@ def test_partitioned_molecule_evaluation_matches_single_process(tmp_path):
         assert a[0] == b[0] and a[-1] == b[-1]
         np.testing.assert_allclose(np.array(a[1:-1], dtype=float), np.array(b[1:-1], dtype=float),
                                    rtol=1e-4, atol=1e-6)
+
+
+def test_source_csr_offsets():
+    """The source-grouped CSR of the edge kernels' backward (perm, ptr) from a sorted search:
+    ptr[i] counts edges with source < i, including sources with no edges and halo rows."""
+    import torch
+
+    from maloq_b200.ops.edge_native import src_csr
+
+    class G:
+        pass
+
+    rng = np.random.default_rng(0)
+    g = G()
+    g.src = torch.as_tensor(rng.integers(0, 40, size=500))
+    g.src[g.src == 7] = 8  # a node without outgoing edges
+    g.num_nodes, g.num_nodes_ext, g.cache = 38, 45, {}
+    perm, ptr = src_csr(g)
+    assert ptr.shape == (46,) and ptr.dtype == torch.long
+    ref = np.concatenate([[0], np.cumsum(np.bincount(g.src.numpy(), minlength=45))])
+    assert np.array_equal(ptr.numpy(), ref)
+    assert np.array_equal(g.src[perm].numpy(), np.sort(g.src.numpy(), kind="stable"))
