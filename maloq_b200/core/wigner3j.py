@@ -24,8 +24,6 @@ from functools import lru_cache
 import numpy as np
 import torch
 
-from . import sph
-
 
 def _clebsch_gordan(j1: int, m1: int, j2: int, m2: int, J: int, M: int) -> float:
     """<j1 m1 j2 m2 | J M> by Racah's formula (Condon-Shortley phases)."""

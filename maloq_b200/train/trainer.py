@@ -227,7 +227,6 @@ class SplitTrainer:
         energy errors (closed shell, all-electron count), written to
         ``model_fock_eval_{rank}.txt`` (reference ``splittrainer.py:378-822``)."""
         from ..data.batch import collate
-        from ..eval import electronic
 
         mol_of = None
         if compute_total_energy:
