@@ -72,3 +72,47 @@ def test_scale_shift_table_matches_workflow_layout(tmp_path):
     rows = torch.cat([s.node_y[0][torch.as_tensor(s.z == z)] for s in samples])
     idx = torch.tensor(t["scalar_irrep_indices"])
     assert torch.allclose(t["element_scalar_means"][z], rows[:, idx].float().mean(0), atol=1e-6)
+
+
+def test_pooled_linear_references_and_statistics(tmp_path):
+    """lin-ref over several ASE databases with random subsampling, then dataset statistics of
+    the reference-subtracted energies and the forces."""
+    import pickle
+
+    rng = np.random.default_rng(2)
+    coeff = {1: -0.5, 6: -37.8, 8: -75.0}
+    paths, all_e, all_f = [], [], []
+    for k in range(2):
+        rows = []
+        for _ in range(15):
+            z = rng.choice([1, 6, 8], size=int(rng.integers(3, 8)))
+            noise = rng.normal() * 1e-3
+            f = rng.normal(size=(len(z), 3))
+            rows.append({"numbers": z, "positions": rng.uniform(0, 5, (len(z), 3)), "forces": f,
+                         "data": {"total_energy [Eh]": sum(coeff[int(a)] for a in z) + noise}})
+            all_e.append(noise)
+            all_f.append(f)
+        p = str(tmp_path / f"part{k}.db")
+        asedb.write_asedb(p, rows)
+        paths.append(p)
+    out = str(tmp_path / "lin.npz")
+    tools.main(["lin-ref"] + paths + [out, "--dataset-name", "ase", "--subsample", "24", "--seed", "3"])
+    c = np.load(out)["coeff"]
+    for z, v in coeff.items():
+        assert abs(c[z] - v) < 5e-3, (z, c[z])
+    mols = tools.pooled_molecules(paths, "ase", subsample=24, seed=3)
+    assert len(mols) == 24
+    assert len({round(m[1], 12) for m in mols}) == 24  # drawn without replacement
+    assert len(tools.pooled_molecules(paths, "ase", subsample=None)) == 30
+    # statistics of one database with the exact references
+    np.savez(str(tmp_path / "exact.npz"), coeff=np.array([0, -0.5, 0, 0, 0, 0, -37.8, 0, -75.0]))
+    tools.main(["stats", paths[0], str(tmp_path / "st"), "--dataset-name", "ase", "--lin-ref",
+                str(tmp_path / "exact.npz")])
+    st = pickle.load(open(tmp_path / "st" / "stats.pkl", "rb"))
+    e, f = np.array(all_e[:15]), np.concatenate(all_f[:15])
+    assert abs(st["energy_mean"] - e.mean()) < 1e-9 and abs(st["energy_std"] - e.std()) < 1e-9
+    assert abs(st["force_rms"] - np.sqrt(np.mean(f ** 2))) < 1e-12
+    assert abs(st["force_md"] - np.linalg.norm(f, axis=1).mean()) < 1e-12
+    h = np.load(tmp_path / "st" / "energy_histogram.npz")
+    assert h["hist"].sum() == 15 and len(h["bins"]) == 101
+    assert (tmp_path / "st" / "force_norm_histogram.npz").exists()
