@@ -78,16 +78,25 @@ def linear_energy_references(numbers_list, energies):
 
 def scale_shift_table(samples, labeler):
     """Per-element means / stds of the l = 0 node label entries of ``samples`` (targets in
-    ``node_y``), in the workflow's file layout."""
+    ``node_y`` [spins, N, D]), in the workflow's file layout.  Open-shell targets (two spin
+    channels) give one table per channel, keys suffixed ``_alpha`` / ``_beta`` (reference
+    ``get_scale_shift.py:256-268``)."""
     from .targets import ScaleShift
 
     ss = ScaleShift(labeler, samples)
-    stds = {}
-    for z in ss.means:
-        rows = torch.cat([s.node_y[0][torch.as_tensor(s.z == z)][:, ss.scalar_idx] for s in samples])
-        stds[z] = rows.float().std(0, unbiased=False)
-    return {"element_scalar_means": ss.means, "element_scalar_stds": stds,
-            "scalar_irrep_indices": ss.scalar_idx.tolist()}
+    idx = ss.scalar_idx
+    spins = int(samples[0].node_y.shape[0]) if samples else 1
+    out = {"scalar_irrep_indices": idx.tolist()}
+    for k in range(spins):
+        means, stds = {}, {}
+        for z in ss.means:
+            rows = torch.cat([s.node_y[k][torch.as_tensor(s.z == z)][:, idx] for s in samples]).float()
+            means[z] = rows.mean(0)
+            stds[z] = rows.std(0, unbiased=False)
+        suffix = "" if spins == 1 else ("_alpha", "_beta")[k]
+        out["element_scalar_means" + suffix] = means if spins > 1 else ss.means
+        out["element_scalar_stds" + suffix] = stds
+    return out
 
 
 def _load(path, name, num=None):

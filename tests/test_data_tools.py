@@ -116,3 +116,20 @@ def test_pooled_linear_references_and_statistics(tmp_path):
     h = np.load(tmp_path / "st" / "energy_histogram.npz")
     assert h["hist"].sum() == 15 and len(h["bins"]) == 101
     assert (tmp_path / "st" / "force_norm_histogram.npz").exists()
+
+
+def test_open_shell_scale_shift_has_one_table_per_spin():
+    from maloq_b200.data import datasets
+
+    lab = datasets.labeler_for("small")
+    samples, _ = datasets.build_dataset("small", 3, dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2,
+                                                          cutoff=5.0, num_layers=1, num_distance_basis=8,
+                                                          edge_channels=8), labeler=lab)
+    for s in samples:  # a second spin channel: alpha + 1
+        s.node_y = torch.cat([s.node_y, s.node_y + 1.0])
+    t = tools.scale_shift_table(samples, lab)
+    assert {"element_scalar_means_alpha", "element_scalar_means_beta", "element_scalar_stds_alpha",
+            "element_scalar_stds_beta", "scalar_irrep_indices"} == set(t)
+    z = int(samples[0].z[0])
+    assert torch.allclose(t["element_scalar_means_beta"][z], t["element_scalar_means_alpha"][z] + 1.0, atol=1e-5)
+    assert torch.allclose(t["element_scalar_stds_beta"][z], t["element_scalar_stds_alpha"][z], atol=1e-5)
