@@ -293,23 +293,25 @@ class TrainingWorkflow:
         c = self.config
         os.makedirs(c["output_folder"], exist_ok=True)
         if c["loss_target"] in ("fock_matrix", "density_matrix"):
+            from ..data.tools import scale_shift_table
+
             path = os.path.join(c["output_folder"], f"element_scale_shifts_{name}.pt")
+            spins = int(train[0].node_y.shape[0]) if train else 1
+            suffixes = [""] if spins == 1 else ["_alpha", "_beta"]
             if os.path.exists(path):
                 d = torch.load(path, weights_only=False)
-                ss = ScaleShift(labeler, means={int(z): torch.as_tensor(v) for z, v in
-                                                d["element_scalar_means"].items()})
             else:
-                ss = ScaleShift(labeler, train)
-                stds = {}
-                for z in ss.means:
-                    rows = torch.cat([s.node_y[0][torch.as_tensor(s.z == z)][:, ss.scalar_idx] for s in train])
-                    stds[z] = rows.float().std(0, unbiased=False)
+                d = scale_shift_table(train, labeler)
                 if self.rank == 0:
-                    torch.save({"element_scalar_means": ss.means, "element_scalar_stds": stds,
-                                "scalar_irrep_indices": ss.scalar_idx.tolist()}, path)
+                    torch.save(d, path)
+            # one table per spin channel (open shell: keys suffixed _alpha / _beta)
+            per_spin = [ScaleShift(labeler, means={int(z): torch.as_tensor(v) for z, v in
+                                                   d["element_scalar_means" + sf].items()}) for sf in suffixes]
             for s in samples:
-                s.node_y = ss.shift(s.node_y[0], s.z).unsqueeze(0)
+                s.node_y = torch.stack([ss.shift(s.node_y[k], s.z) for k, ss in enumerate(per_spin)])
+            ss = per_spin[0]
             self.scale_shift = ss
+            self.scale_shifts = per_spin
         elif c["loss_target"] == "energies":
             path = os.path.join(c["output_folder"], f"lin_ref_coeffs_{name}.npz")
             if os.path.exists(path):

@@ -133,3 +133,34 @@ def test_open_shell_scale_shift_has_one_table_per_spin():
     z = int(samples[0].z[0])
     assert torch.allclose(t["element_scalar_means_beta"][z], t["element_scalar_means_alpha"][z] + 1.0, atol=1e-5)
     assert torch.allclose(t["element_scalar_stds_beta"][z], t["element_scalar_stds_alpha"][z], atol=1e-5)
+
+
+def test_workflow_scale_shift_shifts_each_spin_channel(tmp_path):
+    """Open-shell targets keep both spin channels, each shifted by its own table; the saved
+    file has the per-spin keys and is read back on the next run."""
+    from maloq_b200.data import datasets
+    from maloq_b200.train.workflow import TrainingWorkflow
+
+    lab = datasets.labeler_for("small")
+    kw = dict(sphere_channels=8, hidden_channels=8, lmax=4, mmax=2, cutoff=5.0, num_layers=1, num_distance_basis=8,
+              edge_channels=8)
+    samples, _ = datasets.build_dataset("small", 3, kw, labeler=lab)
+    for s in samples:
+        s.node_y = torch.cat([s.node_y, s.node_y + 1.0])
+    orig = [s.node_y.clone() for s in samples]
+    wf = TrainingWorkflow(dict(dataset_name="synthetic_small", output_folder=str(tmp_path), device="cpu",
+                               scale_and_shift=True))
+    wf._apply_scale_shift(samples, samples, lab, "osh")
+    d = torch.load(tmp_path / "element_scale_shifts_osh.pt", weights_only=False)
+    assert "element_scalar_means_beta" in d
+    for s, o in zip(samples, orig):
+        assert s.node_y.shape == o.shape
+        # beta = alpha + 1 and beta's means = alpha's + 1: the shifted scalar entries agree
+        assert torch.allclose(s.node_y[0][:, wf.scale_shift.scalar_idx], s.node_y[1][:, wf.scale_shift.scalar_idx],
+                              atol=1e-5)
+    again = [s.node_y.clone() for s in samples]
+    for s, o in zip(samples, orig):
+        s.node_y = o.clone()
+    wf._apply_scale_shift(samples, samples, lab, "osh")  # loads the saved tables
+    for s, a in zip(samples, again):
+        assert torch.allclose(s.node_y, a, atol=1e-6)
