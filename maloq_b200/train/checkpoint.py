@@ -5,6 +5,7 @@ Files written to ``output_folder`` (reference ``splittrainer.py:1828-1872``):
 * ``backbone.pt`` / ``head.pt``: ``{'model_state_dict', 'optimizer_state_dict'}``;
 * ``backbone_state_dic.pt`` / ``head_state_dic.pt``: the raw state dicts;
 * ``{backbone|head}_training_loss.txt`` / ``_validation_loss.txt``: ``edge\\tnode`` per epoch;
+* ``loss.png``: the four loss curves on a log scale (``maloq_b200.utils.lossplot``);
 * ``resume.pt`` (new): epoch, scheduler state, loss history and RNG states, so a restart
   continues at the next epoch instead of epoch 0.
 
@@ -45,6 +46,9 @@ def save_training_state(folder, backbone, head, optimizer, scheduler, epoch, his
         with open(os.path.join(folder, f"{name}_validation_loss.txt"), "w") as f:
             for e, n in zip(history["val_edge"], history["val_node"]):
                 f.write(f"{e:.10f}\t{n:.10f}\n")
+    from ..utils.lossplot import save_loss_png
+
+    save_loss_png(os.path.join(folder, "loss.png"), history)
     state = {"epoch": epoch, "history": history,
              "scheduler": scheduler.state_dict() if scheduler is not None else None,
              "rng": {"torch": torch.get_rng_state(), "numpy": np.random.get_state(), "python": random.getstate(),

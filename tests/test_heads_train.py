@@ -356,3 +356,21 @@ def test_state_dict_shapes_follow_reference_modules():
         if k in hsd:
             mul_out = hd.node_lin_out_layers[0][l].mul_out
             assert hsd[k] == (C * mul_out,), (k, hsd[k])
+
+
+def test_loss_png_is_a_valid_image(tmp_path):
+    import struct
+    import zlib
+
+    from maloq_b200.utils.lossplot import save_loss_png
+
+    h = {"train_node": [1.0, 0.3, 0.05], "train_edge": [2.0, 0.5, 0.2], "val_node": [1.2, 0.4, 0.1],
+         "val_edge": [float("nan"), 0.6, 0.3]}
+    data = open(save_loss_png(str(tmp_path / "loss.png"), h), "rb").read()
+    assert data[:8] == b"\x89PNG\r\n\x1a\n"
+    w, hgt = struct.unpack(">II", data[16:24])
+    n = struct.unpack(">I", data[33:37])[0]
+    assert data[37:41] == b"IDAT"
+    raw = zlib.decompress(data[41:41 + n])
+    img = np.frombuffer(raw, dtype=np.uint8).reshape(hgt, w * 3 + 1)[:, 1:].reshape(hgt, w, 3)
+    assert (img == np.array([31, 119, 180], dtype=np.uint8)).all(-1).sum() > 50  # the train_node curve
