@@ -18,3 +18,15 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("CUDA not available")
     return torch.device("cuda:0")
+
+
+def pytest_collection_modifyitems(config, items):
+    """GPU-marked tests are skipped on a machine without a CUDA device (they all need one)."""
+    import torch
+
+    if torch.cuda.is_available():
+        return
+    skip = pytest.mark.skip(reason="CUDA not available")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)

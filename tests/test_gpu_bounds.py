@@ -45,7 +45,7 @@ CASE = textwrap.dedent("""
 """)
 
 
-def test_checked_build_reports_and_skips_out_of_range_gather_source():
+def test_checked_build_reports_and_skips_out_of_range_gather_source(cuda_device):
     env = dict(os.environ, MALOQ_BOUNDS_CHECK="1")
     r = subprocess.run([sys.executable, "-c", CASE.format(root=ROOT)], capture_output=True, text=True, env=env,
                        timeout=900)
