@@ -249,8 +249,9 @@ class _FockHeadFn(torch.autograd.Function):
     def backward(ctx, g):
         from .norm_native import _run_problems
 
-        x, sv, A = ctx.saved_tensors[:3]
-        wlist = ctx.saved_tensors[3:]
+        saved = ctx.saved_tensors  # read once (a second read fails under non-reentrant checkpointing)
+        x, sv, A = saved[:3]
+        wlist = saved[3:]
         L, ls, mul, js, lj, off, width, act, scale, absg, cols, has_b = ctx.meta
         N, S, C = x.shape
         dY = torch.zeros(N, width, device=g.device, dtype=torch.float32)

@@ -1,0 +1,332 @@
+"""A CPU stand-in for the compiled extension (``maloq_b200_C``), for tests.
+
+Each function takes the same arguments as the extension's binding and writes the same outputs,
+computed with PyTorch on CPU tensors from the contract stated in the kernel sources' comments
+(``ops/csrc/*.cu``): GEMMs with bf16 operands and fp32 accumulation, the edge-frame gather /
+rotate / rotate-back maps, the m-major gate, the norms, the fused loss.  Backward kernels are
+the autograd gradients of the same definitions.  Per-CTA partial-sum outputs get the whole sum
+in slice 0 and zeros elsewhere (the callers sum the slices).
+
+With ``use_cpu_extension(monkeypatch)`` the op layer sends CPU tensors down the kernel path, so
+the Python side of that path (views, strides, padding, buffer layouts, autograd functions,
+weight caches) runs on a machine without a GPU and can be compared with the PyTorch path.  The
+argument checks mirror the extension's (dtypes, shapes, contiguity, the 16-byte rule of the TMA
+descriptors).  Kernels that need peer memory (halo, fused all-reduce) are not provided.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+def frame_rows(L, MM):
+    """(degree, slot) of each m-major row of the (L, MM) edge frame: m = 0 rows l = 0..L (slot
+    l), then for m = 1..min(MM, L) the +m rows and the -m rows of l = m..L, which share the
+    slots base_m + l - m."""
+    M = min(MM, L)
+    ls, slots = list(range(L + 1)), list(range(L + 1))
+    base = L + 1
+    for m in range(1, M + 1):
+        n = L - m + 1
+        for _ in range(2):
+            ls += list(range(m, L + 1))
+            slots += list(range(base, base + n))
+        base += n
+    return ls, slots, base
+
+
+def _bf(t):
+    assert t.dtype == torch.bfloat16, t.dtype
+    return t.float()
+
+
+def _contig(*ts):
+    for t in ts:
+        assert t is None or t.is_contiguous(), "expected a contiguous tensor"
+
+
+def _grad(fn, inputs, grad_out):
+    """Gradients of fn(*inputs) w.r.t. the inputs that are not None (None for the others)."""
+    leaves = [None if x is None else x.detach().float().requires_grad_(True) for x in inputs]
+    with torch.enable_grad():  # called from inside autograd backward functions
+        out = fn(*leaves)
+        used = [x for x in leaves if x is not None]
+        gs = torch.autograd.grad(out, used, grad_out, allow_unused=True)
+    it = iter(gs)
+    res = []
+    for x in leaves:
+        if x is None:
+            res.append(None)
+        else:
+            g = next(it)
+            res.append(torch.zeros_like(x) if g is None else g)
+    return res
+
+
+def _dst_of(dst_ptr, E):
+    counts = dst_ptr[1:] - dst_ptr[:-1]
+    dst = torch.repeat_interleave(torch.arange(len(counts)), counts)
+    assert dst.numel() == E, "dst_ptr does not cover the edges"
+    return dst
+
+
+class CpuExtension:
+    """The extension's bindings on CPU tensors (see the module docstring)."""
+
+    # ------------------------------------------------------------------ GEMM
+    def gemm(self, As, Bs, Cs, biases, mn, act, alpha, splits, bn, resids=()):
+        assert 1 <= len(As) <= 8 and len(Bs) == len(Cs) == len(As)
+        for i, (a, b, c) in enumerate(zip(As, Bs, Cs)):
+            # the binding's checks, and the 16-byte rule of the TMA descriptors
+            assert a.dtype == b.dtype == torch.bfloat16 and a.dim() == b.dim() == 2
+            assert a.stride(1) == 1 and b.stride(1) == 1 and c.stride(-1) == 1
+            assert c.dtype == Cs[0].dtype and c.dtype in (torch.float32, torch.bfloat16)
+            M, K, N = (a.shape[1], a.shape[0], b.shape[1]) if mn else (a.shape[0], a.shape[1], b.shape[0])
+            assert (b.shape[0] if mn else b.shape[1]) == K, "gemm: K mismatch"
+            if splits > 1 or c.dim() == 3:
+                assert c.dim() == 3 and c.dtype == torch.float32 and tuple(c.shape) == (splits, M, N)
+            else:
+                assert tuple(c.shape) == (M, N), (tuple(c.shape), M, N)
+            for t in (a, b, c):
+                assert t.data_ptr() % 16 == 0 and all((s * t.element_size()) % 16 == 0 for s in t.stride()[:-1])
+            bias = biases[i] if i < len(biases) else None
+            assert bias is None or (bias.dtype == torch.float32 and bias.numel() == N)
+            res = resids[i] if i < len(resids) else None
+            assert res is None or (res.dtype == torch.float32 and tuple(res.shape) == (M, N) and c.dtype == torch.float32)
+            a, b = a.float(), b.float()
+            if mn and c.dim() == 3:  # split-K over the rows: slice s takes rows s, s + splits, ...
+                rows = torch.arange(a.shape[0])
+                for s in range(c.shape[0]):
+                    sel = rows[s::c.shape[0]]
+                    c[s] = a[sel].T @ b[sel]
+                continue
+            y = a.T @ b if mn else alpha * (a @ b.T)
+            if bias is not None:
+                y = y + bias
+            if act == 1:
+                y = F.silu(y)
+            if res is not None:
+                y = y + res
+            c.copy_(y.to(c.dtype))
+
+    def splitk_reduce(self, part, out, beta):
+        assert part.dtype == out.dtype == torch.float32 and out.is_contiguous()
+        out.copy_(part.sum(0).view_as(out) + beta * out)
+
+    # ------------------------------------------------------------------ edge frame
+    @staticmethod
+    def _gather(L, MM, X, XE, src, dst, rot, rad, Cin):
+        """A [E, R, Cin] (fp32) = rad[slot(k)] * rot . [X[src] | X[dst] | XE]."""
+        ls, slots, ns = frame_rows(L, MM)
+        E, R = src.shape[0], len(ls)
+        parts = [X.index_select(0, src), X.index_select(0, dst)] + ([XE] if XE is not None else [])
+        inp = torch.cat(parts, dim=2)[:, :, :Cin]
+        u = torch.bmm(rot, inp)
+        if rad is not None:
+            u = u * rad.view(E, ns, Cin)[:, torch.tensor(slots)]
+        return u
+
+    def gather_rotate_fwd(self, L, MM, X, XE, src, dst, rot, rad, A, Cin, peers, halo_owner, halo_row, n_own):
+        assert peers == 0, "the CPU stand-in has no peer memory"
+        _contig(X, XE, rot, A)
+        assert X.dtype == rot.dtype == torch.float32 and A.dtype == torch.bfloat16
+        E = src.shape[0]
+        assert A.numel() == E * rot.shape[1] * Cin
+        r = None if rad is None else _bf(rad)
+        A.copy_(self._gather(L, MM, X, XE, src, dst, rot, r, Cin).reshape(A.shape).to(torch.bfloat16))
+
+    def gather_rotate_bwd(self, L, MM, X, XE, rot, rad, dA, dst_ptr, src_perm, src_ptr, DX, DXE, DRAD, Cin,
+                          peers=0, halo_owner=None, halo_row=None, n_own=0):
+        assert peers == 0, "the CPU stand-in has no peer memory"
+        E = rot.shape[0]
+        N = DX.shape[0]
+        assert dst_ptr.numel() == N + 1 and src_ptr.numel() == N + 1
+        dst = _dst_of(dst_ptr, E)
+        # the sources from the source CSR: edge src_perm[i] has source n for i in [ptr[n], ptr[n+1])
+        src = torch.empty(E, dtype=torch.long)
+        src[src_perm] = _dst_of(src_ptr, E)
+        R = rot.shape[1]
+        g = _bf(dA).view(E, R, Cin)
+        r = None if rad is None else _bf(rad)
+        gx, gxe, grad_r = _grad(lambda x, xe, rr: self._gather(L, MM, x, xe, src, dst, rot, rr, Cin), [X, XE, r], g)
+        DX.copy_(gx[:N])
+        if DXE is not None:
+            DXE.copy_(gxe)
+        if DRAD is not None:
+            DRAD.copy_(grad_r.to(torch.bfloat16))
+
+    @staticmethod
+    def _rotate_back(Y, koff, Rk, rot, C):
+        E = rot.shape[0]
+        y = _bf(Y)[:, koff:koff + Rk * C].reshape(E, Rk, C)
+        return torch.bmm(rot[:, :Rk].transpose(1, 2), y)
+
+    def rotate_back_scatter(self, L, MM, Y, koff, Rk, rot, dst_ptr, base, out, scale):
+        assert out.dtype == torch.float32 and out.is_contiguous()
+        E = rot.shape[0]
+        msg = self._rotate_back(Y, koff, Rk, rot, out.shape[2])
+        acc = torch.zeros_like(out).index_add_(0, _dst_of(dst_ptr, E), msg) * scale
+        out.copy_(acc + (base if base is not None else 0.0))
+
+    def rotate_back_edge(self, L, MM, Y, koff, Rk, rot, out):
+        assert out.dtype == torch.float32 and out.is_contiguous()
+        out.copy_(self._rotate_back(Y, koff, Rk, rot, out.shape[2]))
+
+    def rotate_grad(self, L, MM, G, rows, rot, DY, DYf, Rk, scale):
+        E, C = rot.shape[0], G.shape[2]
+        g = G.index_select(0, rows) if rows is not None else G
+        d = (scale * torch.bmm(rot[:, :Rk], g)).reshape(E, Rk * C)
+        for t in (DY, DYf):
+            if t is not None:
+                t[:, :Rk * C].copy_(d.to(t.dtype))
+
+    @staticmethod
+    def _gate(L, MM, y1, H):
+        ls, _, _ = frame_rows(L, MM)
+        E, G = y1.shape[0], L * H
+        g = torch.tanh(y1[:, :G].reshape(E, L, H))
+        x = y1[:, G:].reshape(E, len(ls), H)
+        rows = [F.silu(x[:, 0])] + [x[:, k] * g[:, l - 1] for k, l in enumerate(ls) if k > 0]
+        return torch.stack(rows, 1).reshape(E, -1)
+
+    def gate_fwd(self, L, MM, Y1, H1, H):
+        H1.copy_(self._gate(L, MM, _bf(Y1), H).to(torch.bfloat16))
+
+    def gate_bwd(self, L, MM, Y1, dH1, dY1, H):
+        (g,) = _grad(lambda y: self._gate(L, MM, y, H), [_bf(Y1)], _bf(dH1))
+        dY1.copy_(g.to(torch.bfloat16))
+
+    # ------------------------------------------------------------------ norms and gates
+    @staticmethod
+    def _rms(L, s, aw, ab, eps):
+        from maloq_b200.ops import reference as R
+
+        S = (L + 1) ** 2
+        bw = torch.zeros(S, 1)
+        for l in range(L + 1):
+            bw[l * l:(l + 1) ** 2] = 1.0 / ((2 * l + 1) * (L + 1))
+        return R.rms_norm_sh(s, aw, ab, bw, eps)
+
+    def norm_grid(self, rows):
+        return 1
+
+    def rms_norm_fwd(self, L, X, RES, aw, ab, OUT, SUM, eps):
+        _contig(X, RES, OUT, SUM)
+        s = X + RES if RES is not None else X
+        if SUM is not None:
+            SUM.copy_(s)
+        OUT.copy_(self._rms(L, s, aw, ab, eps).to(OUT.dtype))
+
+    def rms_norm_bwd(self, L, Sx, G, GS, aw, DX, PART, eps):
+        ab = torch.zeros(aw.shape[1])
+        gx, gw, gb = _grad(lambda s, w, b: self._rms(L, s, w, b, eps), [Sx, aw, ab], G.float())
+        DX.copy_(gx + (GS if GS is not None else 0.0))
+        PART.zero_()
+        PART[0, :L + 1] = gw
+        PART[0, L + 1] = gb
+
+    def ln_silu_fwd(self, X, w, b, OUT, eps):
+        OUT.copy_(F.silu(F.layer_norm(X, (X.shape[1],), w, b, eps)).to(OUT.dtype))
+
+    def ln_silu_bwd(self, X, w, b, G, DX, PART, eps):
+        gx, gw, gb = _grad(lambda x, ww, bb: F.silu(F.layer_norm(x, (x.shape[1],), ww, bb, eps)), [X, w, b], _bf(G))
+        DX.copy_(gx)
+        PART.zero_()
+        PART[0, 0] = gw
+        PART[0, 1] = gb
+
+    @staticmethod
+    def _gate_l(L, x, gt):
+        B, S, H = x.shape
+        t = torch.tanh(gt.view(B, L, H))
+        rows = [F.silu(x[:, :1])] + [x[:, l * l:(l + 1) ** 2] * t[:, l - 1:l] for l in range(1, L + 1)]
+        return torch.cat(rows, 1)
+
+    def gate_l_fwd(self, L, X, Gt, OUT):
+        OUT.copy_(self._gate_l(L, X.float(), Gt).to(OUT.dtype))
+
+    def gate_l_bwd(self, L, X, Gt, DO, DX, DG):
+        gx, gg = _grad(lambda x, g: self._gate_l(L, x, g), [X.float(), Gt], DO.float())
+        DX.copy_(gx.to(DX.dtype))
+        DG.copy_(gg)
+
+    @staticmethod
+    def _head_gate(L, x, sv, act, scale, absg):
+        B, S, C = x.shape
+        u = sv[:, C:].reshape(B, L, C)
+        u = u.abs() if absg else u
+        g = (torch.sigmoid(u) if act == 0 else torch.tanh(u)) * scale
+        rows = [sv[:, :C].unsqueeze(1)] + [x[:, l * l:(l + 1) ** 2] * g[:, l - 1:l] for l in range(1, L + 1)]
+        return torch.cat(rows, 1)
+
+    def head_gate_fwd(self, L, X, SV, A, act, scale, absg):
+        assert A.dtype == torch.bfloat16 and A.shape == X.shape and SV.shape == (X.shape[0], (L + 1) * X.shape[2])
+        A.copy_(self._head_gate(L, X, SV, act, scale, absg).to(torch.bfloat16))
+
+    def head_gate_bwd(self, L, X, SV, DA, DX, DSV, act, scale, absg):
+        gx, gs = _grad(lambda x, s: self._head_gate(L, x, s, act, scale, absg), [X, SV], DA)
+        DX.copy_(gx)
+        DSV.copy_(gs)
+
+    # ------------------------------------------------------------------ rotation, loss, status
+    def edge_rotation(self, vec, J, joff, L, row_l, row_m, ROT):
+        from maloq_b200.core import sph
+
+        Js = [J[joff[l]:joff[l] + (2 * l + 1) ** 2].view(2 * l + 1, 2 * l + 1) for l in range(L + 1)]
+        alpha, beta = sph.edge_euler_angles(vec.double())
+        D = sph.block_diag_wigner(L, torch.zeros_like(alpha), -beta, -alpha, [j.double() for j in Js])
+        idx = torch.tensor([l * l + l + m for l, m in zip(row_l, row_m)])
+        ROT.copy_(D.index_select(1, idx).float())
+
+    def fock_loss_grid(self, n):
+        return 1
+
+    def fock_loss_stats(self, O, T, pt, mask, part):
+        m = mask[pt].float()
+        d = O - T
+        part.zero_()
+        part[0] = torch.stack([(m * d * d).sum(), (m * d.abs()).sum(), m.sum()])
+
+    def fock_loss_grad(self, O, T, pt, mask, gstat, G):
+        m = mask[pt].float()
+        d = O - T
+        G.copy_(m * (gstat[0] * 2 * d + gstat[1] * torch.sign(d)))
+
+    def error_status(self, clear):
+        return 0
+
+    def bounds_checked(self):
+        return False
+
+
+class _Recorder:
+    """Delegates to the stand-in and records which bindings were called (``calls``)."""
+
+    def __init__(self, ext):
+        self._ext, self.calls = ext, {}
+
+    def __getattr__(self, name):
+        fn = getattr(self._ext, name)
+
+        def call(*a, **k):
+            self.calls[name] = self.calls.get(name, 0) + 1
+            return fn(*a, **k)
+
+        return call
+
+
+def use_cpu_extension(monkeypatch):
+    """Route CPU tensors through the kernel path with :class:`CpuExtension` as the extension."""
+    from maloq_b200 import ops
+    from maloq_b200.ops import kernels
+
+    ext = _Recorder(CpuExtension())
+    monkeypatch.setattr(kernels, "_lib", ext)
+    from maloq_b200.ops import loss as ops_loss
+
+    # the op layer and the loss module decide CPU vs kernel path with _cuda; labels and the basis
+    # transform stay on the PyTorch path (their kernels are not provided here)
+    for mod in (ops, ops_loss):
+        monkeypatch.setattr(mod, "_cuda", lambda *t: True)
+    return ext

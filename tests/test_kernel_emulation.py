@@ -11,6 +11,8 @@ import numpy as np
 import pytest
 import torch
 
+from tests.cpu_extension import CpuExtension
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "..", "maloq_b200", "ops", "csrc")
 CUDA_INC = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
@@ -76,51 +78,12 @@ def test_head_gate_kernels_on_emulated_grid(emu, L, C, act, absg, grid):
     np.testing.assert_allclose(dsv.numpy(), rdsv.numpy(), rtol=1e-5, atol=1e-6)
 
 
-class _CpuExtension:
-    """Stand-in for the compiled extension on CPU tensors: GEMMs as PyTorch matmuls with the
-    extension's operand conventions (bf16 operands, fp32 accumulation; ``mn`` = weight-gradient
-    form C = A^T B, split-K slices over the rows), the head gate through the emulated kernels.
-    It lets the Python side of a kernel path (views, strides, padding, ordering, autograd) run
-    on the CPU."""
+class _CpuExtension(CpuExtension):
+    """The CPU stand-in of the extension with the head-gate calls running the kernel source
+    on the emulated grid."""
 
     def __init__(self, emu):
         self.emu = emu
-
-    def gemm(self, As, Bs, Cs, biases, mn, act, alpha, splits, bn, resids=()):
-        assert 1 <= len(As) <= 8 and len(Bs) == len(Cs) == len(As)
-        for i, (a, b, c) in enumerate(zip(As, Bs, Cs)):
-            # the extension's argument checks, and the 16-byte rule of its TMA descriptors
-            assert a.dtype == b.dtype == torch.bfloat16 and a.dim() == b.dim() == 2
-            assert a.stride(1) == 1 and b.stride(1) == 1 and c.stride(-1) == 1
-            M, K, N = (a.shape[1], a.shape[0], b.shape[1]) if mn else (a.shape[0], a.shape[1], b.shape[0])
-            assert (b.shape[0] if mn else b.shape[1]) == K
-            if splits > 1 or c.dim() == 3:
-                assert c.dim() == 3 and c.dtype == torch.float32 and tuple(c.shape) == (splits, M, N)
-            else:
-                assert tuple(c.shape) == (M, N)
-            for t in (a, b, c):
-                assert t.data_ptr() % 16 == 0 and all((st * t.element_size()) % 16 == 0 for st in t.stride()[:-1])
-            a, b = a.float(), b.float()
-            if mn:
-                if c.dim() == 3:
-                    rows = torch.arange(a.shape[0])
-                    for s in range(c.shape[0]):
-                        sel = rows[s::c.shape[0]]
-                        c[s] = a[sel].T @ b[sel]
-                    continue
-                y = a.T @ b
-            else:
-                y = alpha * (a @ b.T)
-            if biases[i] is not None:
-                y = y + biases[i]
-            if act == 1:
-                y = torch.nn.functional.silu(y)
-            if i < len(resids) and resids[i] is not None:
-                y = y + resids[i]
-            c.copy_(y.to(c.dtype))
-
-    def splitk_reduce(self, part, out, beta):
-        out.copy_(part.sum(0).view_as(out) + beta * out)
 
     def head_gate_fwd(self, L, x, sv, A, act, scale, absg):
         N, S, C = x.shape

@@ -1,0 +1,90 @@
+"""The whole kernel path of the model (every op the training step sends to the extension) run
+on the CPU through a stand-in for the extension (``tests/cpu_extension.py``) and compared with
+the PyTorch path: forward outputs, loss and every parameter gradient.  This checks the Python
+side of the kernel path - buffer layouts, views and strides handed to the kernels, GEMM problem
+grouping, padding, the autograd functions - without a GPU."""
+import numpy as np
+import pytest
+import torch
+
+from tests.cpu_extension import use_cpu_extension
+
+
+def _model(mmax, message_type="source-target", **extra):
+    from maloq_b200.data import basis_sets, structures
+    from maloq_b200.data.batch import collate, make_sample
+    from maloq_b200.data.targets import FockLabeler
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+
+    lab = FockLabeler(basis_sets.get_basis("split_valence_small"))
+    rng = np.random.default_rng(4)
+    samples = [make_sample(structures.random_small_molecule(rng), 5.0) for _ in range(3)]
+    for s in samples:
+        s.node_y = torch.randn(1, s.num_nodes, lab.target_len)
+        s.y = torch.randn(1, s.num_edges, lab.target_len)
+    b = collate(samples, lab.table)
+    torch.manual_seed(0)
+    kw = dict(sphere_channels=16, hidden_channels=16, lmax=4, mmax=mmax, cutoff=5.0, num_layers=2,
+              num_distance_basis=8, edge_channels=16, message_type=message_type, **extra)
+    bb = eSEN_Backbone(lab.irreps, include_edges=True, **kw)
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=16, ls_list=lab.layout.ls_list,
+                          reduce_node=True, reduce_node_intra=True)
+    return bb, hd, b, lab
+
+
+def _step(bb, hd, b, lab):
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    tr = SplitTrainer(bb, hd, lab.irreps, mask_table=torch.as_tensor(lab.table.mask))
+    for p in list(bb.parameters()) + list(hd.parameters()):
+        p.grad = None
+    ln, le, loss = tr.forward_loss(b, L.rmse_mse_padded_loss)
+    loss.backward()
+    grads = {n: p.grad.clone() for n, p in list(bb.named_parameters()) + [("head." + k, v) for k, v in hd.named_parameters()]
+             if p.grad is not None}
+    return float(ln.detach()), float(le.detach()), float(loss.detach()), grads
+
+
+@pytest.mark.parametrize("mmax,message_type", [(2, "source-target"), (2, "source-target-message"),
+                                               (4, "source-target"), (1, "source-target")])
+def test_kernel_path_matches_pytorch_path_on_cpu(monkeypatch, mmax, message_type):
+    bb, hd, b, lab = _model(mmax, message_type)
+    ref = _step(bb, hd, b, lab)
+    ext = use_cpu_extension(monkeypatch)
+    got = _step(bb, hd, b, lab)
+    expected = {"gemm", "edge_rotation", "gather_rotate_fwd", "gather_rotate_bwd", "gate_fwd",
+                "gate_bwd", "rotate_back_scatter", "rotate_back_edge", "rotate_grad", "rms_norm_fwd", "rms_norm_bwd",
+                "ln_silu_fwd", "ln_silu_bwd", "gate_l_fwd", "gate_l_bwd", "head_gate_fwd", "head_gate_bwd",
+                "fock_loss_stats", "fock_loss_grad"}
+    assert expected <= set(ext.calls), expected - set(ext.calls)
+    for a, r in zip(got[:3], ref[:3]):
+        assert abs(a - r) <= 2e-2 * abs(r), (a, r)
+    assert set(got[3]) == set(ref[3])
+    worst = []
+    for n, g in ref[3].items():
+        d = (got[3][n] - g).norm() / (g.norm() + 1e-12)
+        worst.append((float(d), n))
+    worst.sort(reverse=True)
+    assert worst[0][0] < 5e-2, worst[:5]
+
+
+@pytest.mark.parametrize("extra", [dict(edge_chunk=40, edge_stream_dtype=torch.float32), dict(edge_chunk=40),
+                                   dict(activation_checkpointing=True)])
+def test_chunked_and_recomputed_kernel_paths_match_on_cpu(monkeypatch, extra):
+    """Edge-chunked execution (per-chunk recompute, fp32 or bf16 edge stream) and block
+    recompute on the kernel path against the unchunked PyTorch path."""
+    bb, hd, b, lab = _model(2)
+    ref = _step(bb, hd, b, lab)
+    bb2, hd2, _, _ = _model(2, **extra)
+    bb2.load_state_dict(bb.state_dict())
+    hd2.load_state_dict(hd.state_dict())
+    ext = use_cpu_extension(monkeypatch)
+    got = _step(bb2, hd2, b, lab)
+    assert ext.calls.get("gather_rotate_fwd", 0) > 0
+    tol = 2e-2 if extra.get("edge_stream_dtype", torch.bfloat16) == torch.float32 or "edge_chunk" not in extra else 4e-2
+    for a, r in zip(got[:3], ref[:3]):
+        assert abs(a - r) <= tol * abs(r), (a, r)
+    worst = max(float((got[3][n] - g).norm() / (g.norm() + 1e-12)) for n, g in ref[3].items())
+    assert worst < 2.5 * tol, worst
