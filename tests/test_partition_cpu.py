@@ -414,3 +414,33 @@ def test_source_csr_offsets():
     ref = np.concatenate([[0], np.cumsum(np.bincount(g.src.numpy(), minlength=45))])
     assert np.array_equal(ptr.numpy(), ref)
     assert np.array_equal(g.src[perm].numpy(), np.sort(g.src.numpy(), kind="stable"))
+
+
+def _partitioned_kernel_path_worker(rank, world, pname, edge_chunk):
+    """The partitioned worker with the kernel path on the CPU stand-in of the extension."""
+    from maloq_b200 import ops
+    from maloq_b200.ops import kernels
+    from maloq_b200.ops import loss as ops_loss
+    from tests.cpu_extension import CpuExtension
+
+    kernels._lib = CpuExtension()
+    ops._cuda = ops_loss._cuda = lambda *t: True
+    return _partitioned_worker(rank, world, pname, edge_chunk)
+
+
+@pytest.mark.parametrize("pname,edge_chunk", [("rcb", None), ("linear-edgewise", 40)])
+def test_partitioned_kernel_path_matches_single_process(monkeypatch, pname, edge_chunk):
+    """Graph partitioned over 2 gloo ranks (collective halo) on the kernel path = one process on
+    the kernel path (both on the CPU stand-in of the extension: the same bf16 roundings, so the
+    partitioned exchange must reproduce the single-process values closely)."""
+    from tests.cpu_extension import use_cpu_extension
+
+    out = _dist_util.run(_partitioned_kernel_path_worker, world=2, args=(pname, edge_chunk))
+    use_cpu_extension(monkeypatch)
+    ref_n, ref_e, ref_g = _single()
+    rel = lambda a, b: float(np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-12))
+    for r, (own, edges, no, eo, grads) in out.items():
+        assert rel(no, ref_n[own].numpy()) < 2e-3
+        assert rel(eo, ref_e[edges].numpy()) < 2e-3
+        worst = max(rel(a, b.numpy()) for a, b in zip(grads, ref_g) if np.linalg.norm(b.numpy()) > 0)
+        assert worst < 1e-2, worst
