@@ -80,9 +80,9 @@ class SpectralAtomwise(nn.Module):
         kernel path).  The hidden activations between the two SO3 linears are bf16 on the kernel
         path (they only feed the next GEMM)."""
         lin = self.scalar_mlp[0]
-        g = ops.linear(x[:, 0], lin.weight, lin.bias, act="silu")
-        h = self.so3_linear_1(x, out_dtype=torch.bfloat16)
-        h = self.act(g, h)
+        s1 = self.so3_linear_1
+        h, pre = ops.so3_linear_scalar(x, s1.weight, s1.bias, self.lmax, torch.bfloat16, lin.weight, lin.bias)
+        h = self.act(torch.nn.functional.silu(pre), h)
         return self.so3_linear_2(h, residual=residual)
 
 

@@ -10,7 +10,7 @@ from . import reference as _ref
 from . import native as _native
 
 __all__ = [
-    "linear", "layernorm_silu", "so3_linear", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
+    "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
     "rotate_back_m0_scatter", "rotate_back_m0", "fock_loss",
 ]
 
@@ -61,6 +61,16 @@ def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
         return _native.so3_linear(x, weight, bias, lmax, out_dtype, residual)
     out = _ref.so3_linear(x.to(weight.dtype), weight, bias, lmax)
     return out if residual is None else out + residual
+
+
+def so3_linear_scalar(x, weight, bias, lmax, out_dtype, scalar_weight, scalar_bias):
+    """(so3_linear(x), x[:, 0] @ scalar_weight^T + scalar_bias): the atomwise block's SO3 linear
+    and the linear of its gate scalars, which read the same input (one autograd node on the
+    kernel path, so the scalar linear's input gradient is added into row 0 in place)."""
+    if _cuda(x):
+        return _native.so3_linear_scalar(x, weight, bias, lmax, out_dtype, scalar_weight, scalar_bias)
+    return _ref.so3_linear(x.to(weight.dtype), weight, bias, lmax), _ref.linear(x[:, 0].to(weight.dtype),
+                                                                                 scalar_weight, scalar_bias)
 
 
 def gate(gating_scalars, x, expand_index, lmax):

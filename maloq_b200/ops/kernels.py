@@ -186,6 +186,13 @@ def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
     return norm_native.so3_linear(x, weight, bias, lmax, out_dtype, residual)
 
 
+@register("so3_linear_scalar")
+def so3_linear_scalar(x, weight, bias, lmax, out_dtype, sw, sb):
+    from . import norm_native
+
+    return norm_native.so3_linear_scalar(x, weight, bias, lmax, out_dtype, sw, sb)
+
+
 def _pad8(n):
     return (n + 7) // 8 * 8
 
@@ -200,15 +207,20 @@ class _FockHeadFn(torch.autograd.Function):
     scalars, every l >= 1 coefficient times its activated gate).  One grouped-GEMM problem per
     coefficient j projects A[:, j] with its degree's weight into column block j of one fp32
     buffer Y (blocks padded to 8 columns); one gather puts Y's columns into the head's sorted
-    order (per degree, e3nn's (channel, m) flattening).  Backward: the gather's transpose, one
-    grouped input-gradient GEMM, split-K weight gradients summed per degree in a fixed order, and
-    ``head_gate_bwd`` for the gradients of x and of the scalar linear's output."""
+    order (per degree, e3nn's (channel, m) flattening).  The scalar linear (x[:, 0] ->
+    transformed scalars | raw gates) runs inside, so its input gradient lands in row 0 of dx
+    directly (no full-size zero gradient for the row selection).  Backward: the gather's
+    transpose, one grouped input-gradient GEMM, split-K weight gradients summed per degree in a
+    fixed order, ``head_gate_bwd`` for the gradients of x and of the scalar linear's output, and
+    the scalar linear's gradients."""
 
     @staticmethod
-    def forward(ctx, x, sv, act, scale, absg, present, *wb):
+    def forward(ctx, x, ws_s, bs_s, act, scale, absg, present, *wb):
         from .norm_native import _run_problems
 
         N, S, C = x.shape
+        x0 = x[:, 0].to(torch.bfloat16).contiguous()
+        sv = gemm_nt(x0, ws_s, bs_s, out_dtype=torch.float32, w_bf16=W.bf16(ws_s))
         L = int(round(S ** 0.5)) - 1
         ls = [l for l in range(L + 1) if present[l]]
         ws = dict(zip(ls, wb[0::2]))
@@ -241,8 +253,9 @@ class _FockHeadFn(torch.autograd.Function):
             _run_problems([A2[:, j * C:(j + 1) * C] for j in js], [wpad[lj[j]] for j in js],
                           [Y[:, off[j]:off[j] + _pad8(mul[lj[j]])] for j in js], [bpad[lj[j]] for j in js])
         count_launches(2)
-        ctx.save_for_backward(x, sv, A, *[ws[l] for l in ls])
-        ctx.meta = (L, ls, mul, js, lj, off, o, act, float(scale), bool(absg), cols, [bs[l] is not None for l in ls])
+        ctx.save_for_backward(x, sv, A, x0, ws_s, *[ws[l] for l in ls])
+        ctx.meta = (L, ls, mul, js, lj, off, o, act, float(scale), bool(absg), cols, [bs[l] is not None for l in ls],
+                    bs_s is not None)
         return Y.index_select(1, cols)
 
     @staticmethod
@@ -250,9 +263,9 @@ class _FockHeadFn(torch.autograd.Function):
         from .norm_native import _run_problems
 
         saved = ctx.saved_tensors  # read once (a second read fails under non-reentrant checkpointing)
-        x, sv, A = saved[:3]
-        wlist = saved[3:]
-        L, ls, mul, js, lj, off, width, act, scale, absg, cols, has_b = ctx.meta
+        x, sv, A, x0, ws_s = saved[:5]
+        wlist = saved[5:]
+        L, ls, mul, js, lj, off, width, act, scale, absg, cols, has_b, has_bs = ctx.meta
         N, S, C = x.shape
         dY = torch.zeros(N, width, device=g.device, dtype=torch.float32)
         dY.index_copy_(1, cols, g.float().contiguous())
@@ -293,17 +306,21 @@ class _FockHeadFn(torch.autograd.Function):
         dsv = torch.empty_like(sv)
         lib().head_gate_bwd(L, x, sv, dA, dx, dsv, 0 if act == "sigmoid" else 1, scale, absg)
         count_launches(4)
-        return (dx, dsv, None, None, None, None, *grads)
+        # the scalar linear: its input gradient is row 0 of dx (head_gate_bwd left it zero)
+        d2 = dsv.to(torch.bfloat16)
+        dx[:, 0] = gemm_nt(d2, ws_s, w_bf16=W.bf16_t(ws_s))
+        dws = gemm_tn_weight_grad(d2, x0)[: ws_s.shape[0], : ws_s.shape[1]] if ctx.needs_input_grad[1] else None
+        dbs = dsv.sum(0) if has_bs and ctx.needs_input_grad[2] else None
+        return (dx, dws, dbs, None, None, None, None, *grads)
 
 
 def _head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):
-    sv = linear(x[:, 0], ws, bs)
     present = tuple(w is not None for w, _ in layer_params)
     wb = []
     for w, b in layer_params:
         if w is not None:
             wb += [w, b]
-    return _FockHeadFn.apply(x, sv, act, act_scale, abs_gates, present, *wb)
+    return _FockHeadFn.apply(x, ws, bs, act, act_scale, abs_gates, present, *wb)
 
 
 @register("edgewise")

@@ -152,10 +152,15 @@ def _run_problems(As, Ws, Cs, biases, mn=False, splits=1, resids=None):
 class _SO3Linear(torch.autograd.Function):
     """out[:, j] = x[:, j] @ W[l_j]^T (+ bias on j = 0) (+ residual), one GEMM problem per
     coefficient j.  x fp32 or bf16 (cast once to bf16); output fp32 (with the residual added in
-    the GEMM epilogue) or bf16; the input gradient comes back in the input's dtype."""
+    the GEMM epilogue) or bf16; the input gradient comes back in the input's dtype.
+
+    With a side weight ``sw`` [Ns, C] (and bias ``sb``) it also returns the scalar linear
+    ``pre = x[:, 0] @ sw^T + sb`` (fp32) of the same input - the atomwise block's gate scalars -
+    whose input gradient is added to row 0 of dx in place, instead of autograd building a
+    full-size zero gradient for the row selection and adding it."""
 
     @staticmethod
-    def forward(ctx, x, weight, bias, out_dtype, residual):
+    def forward(ctx, x, weight, bias, out_dtype, residual, sw=None, sb=None):
         B, S, C = x.shape
         Co = weight.shape[1]
         xb = x.to(torch.bfloat16).contiguous().view(B, S * C)
@@ -169,15 +174,24 @@ class _SO3Linear(torch.autograd.Function):
                       [out[:, j * Co:(j + 1) * Co] for j in range(S)],
                       [bias.float().contiguous()] + [None] * (S - 1),
                       resids=None if res is None else [res[:, j * Co:(j + 1) * Co] for j in range(S)])
-        ctx.save_for_backward(xb, weight)
         ctx.dims = (B, S, C, Co)
         ctx.in_dtype = x.dtype
         ctx.has_res = residual is not None
-        return out.view(B, S, Co)
+        ctx.side = sw is not None
+        ctx.has_sb = sb is not None
+        if sw is None:
+            ctx.save_for_backward(xb, weight)
+            return out.view(B, S, Co)
+        from .kernels import gemm_nt
+
+        pre = gemm_nt(xb[:, :C], sw, sb, out_dtype=torch.float32, w_bf16=W.bf16(sw))
+        ctx.save_for_backward(xb, weight, sw)
+        return out.view(B, S, Co), pre
 
     @staticmethod
-    def backward(ctx, g):
-        xb, weight = ctx.saved_tensors
+    def backward(ctx, g, g_pre=None):
+        saved = ctx.saved_tensors
+        xb, weight = saved[:2]
         B, S, C, Co = ctx.dims
         ls = _coef_l(S)
         L = ls[-1]
@@ -195,8 +209,22 @@ class _SO3Linear(torch.autograd.Function):
         dw = torch.stack([part[l * l:(l + 1) * (l + 1)].sum(0) for l in range(L + 1)])
         db = g[:, 0].sum(0, dtype=torch.float32)
         dres = g if ctx.has_res else None
-        return dx.view(B, S, C).to(ctx.in_dtype), dw, db, None, dres
+        dsw = dsb = None
+        if ctx.side and g_pre is not None:
+            from .kernels import gemm_nt, gemm_tn_weight_grad
+
+            sw = saved[2]
+            gp = g_pre.to(torch.bfloat16).contiguous()
+            dx[:, :C] += gemm_nt(gp, sw, w_bf16=W.bf16_t(sw)).to(dx.dtype)
+            dsw = gemm_tn_weight_grad(gp, xb[:, :C].contiguous())[: sw.shape[0], : sw.shape[1]]
+            dsb = g_pre.sum(0, dtype=torch.float32) if ctx.has_sb else None
+        return dx.view(B, S, C).to(ctx.in_dtype), dw, db, None, dres, dsw, dsb
 
 
 def so3_linear(x, weight, bias, lmax, out_dtype=None, residual=None):
     return _SO3Linear.apply(x, weight, bias, out_dtype or torch.float32, residual)
+
+
+def so3_linear_scalar(x, weight, bias, lmax, out_dtype, sw, sb):
+    """(so3_linear(x), x[:, 0] @ sw^T + sb) with one autograd node (see ``_SO3Linear``)."""
+    return _SO3Linear.apply(x, weight, bias, out_dtype or torch.float32, None, sw, sb)

@@ -182,9 +182,9 @@ def fock_head_process(x, ws, bs, layer_params, act, act_scale, abs_gates):
 
 
 def gather_scale(x, idx, mult=None):
-    """out[:, k] = x[:, idx[k]] * mult[k] (idx < 0 -> 0)."""
-    valid = (idx >= 0).to(x.dtype)
-    out = x.index_select(1, idx.clamp(min=0)) * valid
+    """out[:, k] = x[:, idx[k]] * mult[k] (idx < 0 -> 0): one gather and one multiply by the
+    combined column weights (validity times ``mult``)."""
+    w = (idx >= 0).to(x.dtype)
     if mult is not None:
-        out = out * mult.to(x.dtype)
-    return out
+        w = w * mult.to(x.dtype)
+    return x.index_select(1, idx.clamp(min=0)) * w

@@ -116,7 +116,10 @@ class SplitTrainer:
         spins = node_out.shape[0]
         lns, les, lts = [], [], []
         for s in range(spins):
-            no, eo, nt, et = node_out[s], edge_out[s], batch.node_y[s], batch.y[s]
+            if spins == 1:  # a view whose backward allocates nothing (indexing [0] would)
+                no, eo, nt, et = node_out.squeeze(0), edge_out.squeeze(0), batch.node_y[0], batch.y[0]
+            else:
+                no, eo, nt, et = node_out[s], edge_out[s], batch.node_y[s], batch.y[s]
             if self.uncoupled is not None:
                 T = self.uncoupled
                 no, eo = T.get_H(no), T.get_H(eo)

@@ -92,6 +92,32 @@ def test_so3_linear(cuda_device):
         assert _rel(a, bb) < 2e-2
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_so3_linear_with_scalar_side_linear(cuda_device, dtype):
+    """The atomwise block's SO3 linear and its gate-scalar linear of x[:, 0] as one autograd node
+    (the scalar linear's input gradient added into row 0 in place) vs the two separate ops."""
+    from maloq_b200.ops import norm_native
+    from maloq_b200.ops import reference as R
+
+    torch.manual_seed(1)
+    x = torch.randn(2000, 25, 128, device=cuda_device).to(dtype).requires_grad_()
+    W = (torch.randn(5, 128, 128, device=cuda_device) / 11).requires_grad_()
+    b = torch.randn(128, device=cuda_device, requires_grad=True)
+    sw = (torch.randn(512, 128, device=cuda_device) / 11).requires_grad_()
+    sb = torch.randn(512, device=cuda_device, requires_grad=True)
+    h, pre = norm_native.so3_linear_scalar(x, W, b, 4, torch.bfloat16, sw, sb)
+    assert h.dtype == torch.bfloat16 and pre.dtype == torch.float32
+    xf = x.float()
+    rh, rp = R.so3_linear(xf, W, b, 4), R.linear(xf[:, 0], sw, sb)
+    assert _rel(h, rh) < 1e-2 and _rel(pre, rp) < 1e-2
+    gh, gp = torch.randn_like(rh), torch.randn_like(rp)
+    got = torch.autograd.grad((h.float() * gh).sum() + (pre * gp).sum(), [x, W, b, sw, sb])
+    want = torch.autograd.grad((rh * gh).sum() + (rp * gp).sum(), [x, W, b, sw, sb])
+    for a, r in zip(got, want):
+        assert a.dtype == r.dtype or a.dtype == dtype
+        assert ((a.float() - r.float()).norm() / r.float().norm()).item() < 1.5e-2
+
+
 @pytest.mark.parametrize("act,absg,muls,N", [("sigmoid", False, [14, 0, 9, 3, 1], 700),
                                              ("tanh", True, [14, 10, 9, 3, 1], 5000)])
 def test_fock_head_process_kernel(cuda_device, act, absg, muls, N):
