@@ -278,7 +278,11 @@ class _FockHeadFn(torch.autograd.Function):
         wt = {l: torch.nn.functional.pad(w.to(torch.bfloat16), (0, 0, 0, _pad8(mul[l]) - mul[l])).t().contiguous()
               for l, w in zip(ls, wlist)}
         splits = max(1, min(-(-296 // max(1, len(js))), N // 2048, 16))
-        parts = {j: torch.empty(splits, _pad8(mul[lj[j]]), C, device=g.device, dtype=torch.float32) for j in js}
+        # split-K partials of the weight gradients, one contiguous block per degree so that each
+        # degree's gradient is a single reduction over (coefficient, split)
+        partsL = {l: torch.empty(2 * l + 1, splits, _pad8(mul[l]), C, device=g.device, dtype=torch.float32)
+                  for l in ls}
+        parts = {j: partsL[lj[j]][j - lj[j] ** 2] for j in js}
         A2 = A.view(N, S * C)
         if N > 0:
             _run_problems([dYb[:, off[j]:off[j] + _pad8(mul[lj[j]])] for j in js], [wt[lj[j]] for j in js],
@@ -288,19 +292,11 @@ class _FockHeadFn(torch.autograd.Function):
                           mn=True, splits=splits)
         grads = []
         for l, hb in zip(ls, has_b):
-            jl = [j for j in js if lj[j] == l]
-            if N > 0:
-                dw = parts[jl[0]].sum(0)
-                for j in jl[1:]:
-                    dw = dw + parts[j].sum(0)
-            else:
-                dw = torch.zeros(_pad8(mul[l]), C, device=g.device)
+            P, o0 = _pad8(mul[l]), off[l * l]
+            dw = partsL[l].sum((0, 1)) if N > 0 else torch.zeros(P, C, device=g.device)
             grads.append(dw[:mul[l]])
-            db = None
-            if hb:
-                db = dY[:, off[jl[0]]:off[jl[0]] + mul[l]].sum(0)
-                for j in jl[1:]:
-                    db = db + dY[:, off[j]:off[j] + mul[l]].sum(0)
+            # the degree's column blocks are adjacent in dY: [N, 2l+1, P]
+            db = dY[:, o0:o0 + (2 * l + 1) * P].view(N, 2 * l + 1, P)[:, :, :mul[l]].sum((0, 1)) if hb else None
             grads.append(db)
         dx = torch.empty_like(x)
         dsv = torch.empty_like(sv)

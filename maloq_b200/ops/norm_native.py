@@ -205,8 +205,9 @@ class _SO3Linear(torch.autograd.Function):
         part = torch.empty(S, splits, Co, C, device=g.device, dtype=torch.float32)
         _run_problems([gb[:, j * Co:(j + 1) * Co] for j in range(S)], [xb[:, j * C:(j + 1) * C] for j in range(S)],
                       [part[j] for j in range(S)], [None] * S, mn=True, splits=splits)
-        part = part.sum(1)
-        dw = torch.stack([part[l * l:(l + 1) * (l + 1)].sum(0) for l in range(L + 1)])
+        dw = torch.empty(L + 1, Co, C, device=g.device, dtype=torch.float32)
+        for l in range(L + 1):  # one reduction per degree over its coefficients and splits
+            torch.sum(part[l * l:(l + 1) * (l + 1)], dim=(0, 1), out=dw[l])
         db = g[:, 0].sum(0, dtype=torch.float32)
         dres = g if ctx.has_res else None
         dsw = dsb = None

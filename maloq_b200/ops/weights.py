@@ -56,13 +56,16 @@ def bf16(p):
 
 def bf16_t(p):
     """Contiguous bf16 copy of the transpose of a 2-D ``p`` (or of each matrix of a 3-D one)."""
-    return _get(p, "bf16_t", lambda w: w.transpose(-1, -2).to(torch.bfloat16).contiguous())
+    return _get(p, "bf16_t", lambda w: bf16(p).transpose(-1, -2).contiguous() if isinstance(p, torch.nn.Parameter)
+                else w.transpose(-1, -2).to(torch.bfloat16).contiguous())
 
 
 def _pair(w):
-    h = w.shape[0] // 2
+    """[[W_r, -W_i], [W_i, W_r]] of w = [W_r; W_i]: rows r of the result interleave the blocks
+    as [W_r[r] | -W_i[r]] and [W_i[r] | W_r[r]]."""
+    h, k = w.shape[0] // 2, w.shape[1]
     wr, wi = w[:h], w[h:]
-    return torch.cat([torch.cat([wr, -wi], 1), torch.cat([wi, wr], 1)], 0)
+    return torch.stack([torch.stack([wr, -wi], 1), torch.stack([wi, wr], 1)], 0).view(2 * h, 2 * k)
 
 
 def pair_bf16(p):
@@ -71,7 +74,9 @@ def pair_bf16(p):
 
 
 def pair_bf16_t(p):
-    return _get(p, "pair_t", lambda w: _pair(w).t().to(torch.bfloat16).contiguous())
+    # the transpose of the cached pair matrix: one copy instead of rebuilding the blocks
+    return _get(p, "pair_t", lambda w: pair_bf16(p).t().contiguous() if isinstance(p, torch.nn.Parameter)
+                else _pair(w).t().to(torch.bfloat16).contiguous())
 
 
 def pair_grad(dP):

@@ -131,3 +131,30 @@ def test_fock_head_kernel_path_on_cpu(emu, monkeypatch, act, absg, muls):
     for a, b in zip(got, want):
         assert a.shape == b.shape
         assert rel(a, b) < 2e-2, rel(a, b)
+
+
+def test_weight_cache_layouts_and_refresh():
+    """bf16 copies of the GEMM weights (plain, transposed, SO(2) pair form and its transpose)
+    match their definitions and are rebuilt after an optimizer step changes the parameter."""
+    from maloq_b200.ops import weights as W
+
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(8, 6))
+    q = torch.nn.Parameter(torch.randn(3, 4, 5))
+    opt = torch.optim.SGD([p, q], lr=0.1)
+    for _ in range(2):
+        wr, wi = p.detach()[:4], p.detach()[4:]
+        pair = torch.cat([torch.cat([wr, -wi], 1), torch.cat([wi, wr], 1)], 0)
+        assert torch.equal(W.pair_bf16(p), pair.bfloat16())
+        assert torch.equal(W.pair_bf16_t(p), pair.t().bfloat16())
+        assert torch.equal(W.bf16(p), p.detach().bfloat16())
+        assert torch.equal(W.bf16_t(q), q.detach().transpose(-1, -2).bfloat16())
+        dP = torch.randn(8, 12)
+        g = W.pair_grad(dP)
+        pr = p.detach().clone().requires_grad_()
+        wr_, wi_ = pr[:4], pr[4:]
+        (torch.cat([torch.cat([wr_, -wi_], 1), torch.cat([wi_, wr_], 1)], 0) * dP).sum().backward()
+        assert torch.allclose(g, pr.grad)
+        (p.sum() + q.sum()).backward()
+        opt.step()
+        opt.zero_grad()
