@@ -347,6 +347,13 @@ void peer_barrier(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch, 
                             (int)slot_base, spin_limit, stream()));
 }
 
+// barrier among this rank's halo neighbours (bit t of mask set for neighbour t; world <= 64)
+void peer_barrier_mask(int64_t pads_dev, int64_t rank, int64_t world, int64_t epoch, int64_t slot_base,
+                       int64_t spin_limit, int64_t mask) {
+  check(maloq::peer_barrier(reinterpret_cast<uint32_t* const*>(pads_dev), (int)rank, (int)world, (uint32_t)epoch,
+                            (int)slot_base, spin_limit, stream(), (unsigned long long)mask));
+}
+
 void allreduce_p2p(int64_t bufs_dev, int64_t rank, int64_t world, int64_t off, int64_t n, double scale) {
   check(maloq::allreduce_p2p(reinterpret_cast<float* const*>(bufs_dev), (int)rank, (int)world, off, n, (float)scale,
                              stream()));
@@ -530,6 +537,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("head_gate_fwd", &head_gate_fwd);
   m.def("head_gate_bwd", &head_gate_bwd);
   m.def("peer_barrier", &peer_barrier);
+  m.def("peer_barrier_mask", &peer_barrier_mask);
   m.def("allreduce_p2p", &allreduce_p2p);
   m.def("allreduce_multimem", &allreduce_multimem);
   m.def("edge_rotation", &edge_rotation);

@@ -27,15 +27,19 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// mask != 0: only the ranks whose bit is set (and this rank) take part - a barrier among a
+// rank's halo neighbours.  The neighbour relation must be symmetric, so every rank that waits
+// on another is also signalled by it.
 __global__ void peer_barrier_kernel(uint32_t* const* __restrict__ pads, int rank, int world, uint32_t epoch,
-                                    int slot_base, long long spin_limit) {
+                                    int slot_base, long long spin_limit, unsigned long long mask) {
   const int t = threadIdx.x;
-  if (t < world) {
+  const bool member = t < world && (mask == 0ull || ((mask >> t) & 1ull) || t == rank);
+  if (member) {
     __threadfence_system();
     st_release_sys(pads[t] + slot_base + rank, epoch);
   }
   __syncthreads();
-  if (t < world) {
+  if (member) {
     const uint32_t* mine = pads[rank] + slot_base + t;
     long long i = 0;
     for (; i < spin_limit; ++i) {
@@ -142,9 +146,11 @@ static const char* comm_err() {
 }
 
 const char* peer_barrier(uint32_t* const* pads_dev, int rank, int world, uint32_t epoch, int slot_base,
-                         long long spin_limit, cudaStream_t st) {
+                         long long spin_limit, cudaStream_t st, unsigned long long mask) {
   if (world > 1024) return "peer_barrier: world too large";
-  peer_barrier_kernel<<<1, world < 32 ? 32 : world, 0, st>>>(pads_dev, rank, world, epoch, slot_base, spin_limit);
+  if (mask != 0ull && world > 64) return "peer_barrier: a member mask needs world <= 64";
+  peer_barrier_kernel<<<1, world < 32 ? 32 : world, 0, st>>>(pads_dev, rank, world, epoch, slot_base, spin_limit,
+                                                                mask);
   return comm_err();
 }
 

@@ -10,7 +10,8 @@ halo rows are stored by ``halo_push`` into the owners' receive buffers (double-b
 a barrier follows, and each owner adds its received rows to its own gradient with the
 fixed-order segmented sum ``node_reduce`` (a reduce-scatter done inside the scatter stage).
 
-All waits are the bounded peer barriers of ``comm.cu``.  Staging slots are kept for
+All waits are the bounded peer barriers of ``comm.cu``, among each rank's halo neighbours only
+(the owners it reads from and the ranks that read from it), not all ranks.  Staging slots are kept for
 ``n_slots`` consecutive layers so the backward pass can re-read the forward rows.
 Reference behaviour: ``helm/nn/communication.py:190-340`` (NCCL P2P with a device
 synchronise and a global barrier per exchange).
@@ -25,6 +26,18 @@ import torch.distributed as dist
 from ..ops.native import count_launches
 
 SPIN_LIMIT = 1 << 28
+
+
+def halo_neighbours(domain):
+    """Ranks this rank exchanges halo rows with: the owners it reads from and the ranks that
+    read from it (symmetric across the ranks' domains)."""
+    return sorted({p for p in range(domain.world) if p != domain.rank and
+                   (domain.recv_counts[p] > 0 or len(domain.send[p]) > 0)})
+
+
+def _signed64(m):
+    """A 64-bit member mask as the signed integer the binding takes."""
+    return m - (1 << 64) if m >= 1 << 63 else m
 
 
 class _PeerFetch(torch.autograd.Function):
@@ -101,6 +114,11 @@ class PeerHalo:
         self.recv_perm = torch.as_tensor(perm.astype(np.int64), device=self.device)
         self.recv_ptr = torch.as_tensor(ptr.astype(np.int64), device=self.device)
         self.zero_ptr = torch.zeros(self.n_own + 1, dtype=torch.int64, device=self.device)
+        # halo neighbours: the owners I read from and the ranks that read from me (a symmetric
+        # relation); the peer barriers include only them (every rank calls them equally often,
+        # so the epochs stay in step)
+        self.neighbours = halo_neighbours(domain)
+        self.mask = sum(1 << p for p in self.neighbours) | (1 << self.rank) if self.world <= 64 else 0
         self.epoch = 0
         self.next_slot = 0
         self.grad_calls = 0
@@ -109,7 +127,11 @@ class PeerHalo:
 
     def _barrier(self):
         self.epoch += 1
-        self.lib.peer_barrier(self.pads.data_ptr(), self.rank, self.world, self.epoch, 0, SPIN_LIMIT)
+        if self.mask:
+            self.lib.peer_barrier_mask(self.pads.data_ptr(), self.rank, self.world, self.epoch, 0, SPIN_LIMIT,
+                                       _signed64(self.mask))
+        else:
+            self.lib.peer_barrier(self.pads.data_ptr(), self.rank, self.world, self.epoch, 0, SPIN_LIMIT)
         count_launches(1)
 
     def table_ptr(self, slot):

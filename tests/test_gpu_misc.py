@@ -63,6 +63,28 @@ def test_peer_barrier_timeout_reports_error_and_context_survives(cuda_device):
     assert kernels.error_status() == 0
 
 
+def test_masked_peer_barrier_waits_only_for_members(cuda_device):
+    """A member mask limits the barrier to halo neighbours: with only this rank in the mask
+    (rank 0 of 3) nothing is waited for and nothing is signalled to the others; with rank 2 in
+    the mask and rank 2 silent, the bounded wait runs out and records ERR_PEER_WAIT.  All three
+    "ranks'" pads are local memory of this GPU."""
+    from maloq_b200.ops import kernels
+
+    lib = kernels.lib()
+    kernels.error_status(True)
+    pads = torch.zeros(3, 8, dtype=torch.int32, device=cuda_device)
+    ptrs = torch.tensor([pads[i].data_ptr() for i in range(3)], dtype=torch.int64, device=cuda_device)
+    lib.peer_barrier_mask(ptrs.data_ptr(), 0, 3, 1, 0, 2000, 0b001)
+    torch.cuda.synchronize()
+    assert kernels.error_status(True) == 0
+    assert pads[1, 0].item() == 0 and pads[2, 0].item() == 0 and pads[0, 0].item() == 1
+    lib.peer_barrier_mask(ptrs.data_ptr(), 0, 3, 2, 0, 2000, 0b101)
+    torch.cuda.synchronize()
+    assert kernels.error_status(True) == 4
+    assert pads[2, 0].item() == 2 and pads[1, 0].item() == 0  # signalled the member only
+    assert kernels.error_status() == 0
+
+
 def test_peer_timeout_raises_comm_timeout_on_the_host(cuda_device):
     """The host-side status check turns the recorded peer timeout into CommTimeoutError (what
     the trainer raises after a step) and clears the word."""

@@ -444,3 +444,21 @@ def test_partitioned_kernel_path_matches_single_process(monkeypatch, pname, edge
         assert rel(eo, ref_e[edges].numpy()) < 2e-3
         worst = max(rel(a, b.numpy()) for a, b in zip(grads, ref_g) if np.linalg.norm(b.numpy()) > 0)
         assert worst < 1e-2, worst
+
+
+@pytest.mark.parametrize("pname,world", [("slab", 4), ("rcb", 8), ("linear-edgewise", 3)])
+def test_halo_neighbour_sets_are_symmetric(pname, world):
+    """The NVLink halo's peer barriers include only halo neighbours; that is safe only if the
+    neighbour relation is symmetric (a rank waits on exactly the ranks that signal it)."""
+    from maloq_b200.parallel.peer_halo import halo_neighbours
+
+    g = _toy_graph(seed=5, n=200)
+    part = P.partition(pname, g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+    doms = P.decompose(part, g.src, g.dst, world)
+    nb = [set(halo_neighbours(d)) for d in doms]
+    for r in range(world):
+        assert r not in nb[r]
+        for p in nb[r]:
+            assert r in nb[p]
+        # every rank whose rows r reads is a neighbour
+        assert {int(o) for o in doms[r].halo_owner} <= nb[r]
