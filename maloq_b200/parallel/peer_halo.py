@@ -7,8 +7,8 @@ message - the halo never exists as a separate exchanged tensor.
 
 Backward: the gather backward produces gradients for the extended [owned | halo] rows; the
 halo rows are stored by ``halo_push`` into the owners' receive buffers (double-buffered),
-a barrier follows, and each owner adds its received rows to its own gradient with the
-fixed-order segmented sum ``node_reduce`` (a reduce-scatter done inside the scatter stage).
+a barrier follows, and each owner sums its own gradient rows and its received rows with one
+fixed-order segmented sum, ``node_reduce`` (a reduce-scatter done inside the scatter stage).
 
 All waits are the bounded peer barriers of ``comm.cu``, among each rank's halo neighbours only
 (the owners it reads from and the ranks that read from it), not all ranks.  Staging slots are kept for
@@ -113,7 +113,9 @@ class PeerHalo:
         ptr = np.concatenate([[0], np.cumsum(np.bincount(send_idx, minlength=self.n_own))])
         self.recv_perm = torch.as_tensor(perm.astype(np.int64), device=self.device)
         self.recv_ptr = torch.as_tensor(ptr.astype(np.int64), device=self.device)
-        self.zero_ptr = torch.zeros(self.n_own + 1, dtype=torch.int64, device=self.device)
+        # each owned row is its own single "edge" in the destination walk of node_reduce, so the
+        # reduction adds the owned gradient and the received halo rows in one pass
+        self.self_ptr = torch.arange(self.n_own + 1, dtype=torch.int64, device=self.device)
         # halo neighbours: the owners I read from and the ranks that read from me (a symmetric
         # relation); the peer barriers include only them (every rank calls them equally often,
         # so the epochs stay in step)
@@ -165,8 +167,8 @@ class PeerHalo:
         if self.n_recv == 0:
             return own.clone()
         recv = self.recvbuf[b * self.max_recv * self.sc:(b * self.max_recv + self.n_recv) * self.sc]
-        extra = torch.empty_like(own)
-        self.lib.node_reduce(None, self.zero_ptr, recv.view(self.n_recv, self.sc), self.recv_perm, self.recv_ptr,
-                             extra.view(self.n_own, self.sc))
+        out = torch.empty_like(own)
+        self.lib.node_reduce(own.reshape(self.n_own, self.sc), self.self_ptr, recv.view(self.n_recv, self.sc),
+                             self.recv_perm, self.recv_ptr, out.view(self.n_own, self.sc))
         count_launches(1)
-        return own + extra
+        return out
