@@ -499,7 +499,13 @@ class TrainingWorkflow:
 
                 return write_partition_hamiltonian(c["output_folder"], b, no[0], eo[0], labeler,
                                                    global_src=s.src[e], global_dst=s.dst[e])
-            return trainer.infer(self.device, val[0].to(self.device), labeler, output_folder=c["output_folder"])
+            if len(val) == 1:
+                return trainer.infer(self.device, val[0].to(self.device), labeler, output_folder=c["output_folder"])
+            # every batch of the evaluation set (reference ``splittrainer.py:825-1148``), one
+            # block-sparse shard folder per batch
+            return [trainer.infer(self.device, bt.to(self.device), labeler,
+                                  output_folder=os.path.join(c["output_folder"], f"batch_{i:04d}"))
+                    for i, bt in enumerate(val)]
         except BaseException:
             # the other ranks may be inside a collective this rank will never join: leave
             # without the closing barrier (their process-group timeout ends their wait)

@@ -374,3 +374,23 @@ def test_loss_png_is_a_valid_image(tmp_path):
     raw = zlib.decompress(data[41:41 + n])
     img = np.frombuffer(raw, dtype=np.uint8).reshape(hgt, w * 3 + 1)[:, 1:].reshape(hgt, w, 3)
     assert (img == np.array([31, 119, 180], dtype=np.uint8)).all(-1).sum() > 50  # the train_node curve
+
+
+def test_workflow_infer_writes_every_batch(tmp_path):
+    """train_or_eval='infer' on a molecule dataset writes a block-sparse Hamiltonian for every
+    batch of the evaluation set; each matches the dense labels -> matrix conversion."""
+    from maloq.train_utils import training_workflow
+    from maloq_b200.data import datasets
+    from maloq_b200.parallel.infer import load_partitioned_hamiltonian
+
+    cfg = dict(dataset_name="synthetic_small", num_structures=10, num_train=6, num_val=4, batch_size=2,
+               num_epochs=1, l_embedding_dim=8, num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5,
+               rcut_gaussian=5.0, mmax=2, output_folder=str(tmp_path), device="cpu", log_every=0)
+    training_workflow.TrainingWorkflow(cfg).run()
+    paths = training_workflow.TrainingWorkflow(dict(cfg, train_or_eval="infer", restart_backbone=True,
+                                                    restart_head=True)).run()
+    assert len(paths) == 2
+    lab = datasets.labeler_for("small")
+    for i in range(2):
+        H = load_partitioned_hamiltonian(str(tmp_path / f"batch_{i:04d}"), lab).to_dense()
+        assert H.shape[0] == H.shape[1] > 0 and np.allclose(H, H.T, atol=1e-5)
