@@ -98,6 +98,47 @@ def zeropower_via_newtonschulz5(G, steps: int = 5):
     return X
 
 
+def _muon_update(p, st, lr, momentum, nesterov, ns_steps, weight_decay):
+    """One Muon step of parameter ``p`` (state ``st``): momentum, the Newton-Schulz orthogonalised
+    update of the [rows, rest] matrix scaled by sqrt(max(1, rows / cols)), decoupled decay."""
+    buf = st.setdefault("momentum_buffer", torch.zeros_like(p))
+    buf.mul_(momentum).add_(p.grad)
+    upd = p.grad.add(buf, alpha=momentum) if nesterov else buf
+    shape = upd.shape
+    u = zeropower_via_newtonschulz5(upd.reshape(shape[0], -1), ns_steps).to(p.dtype)
+    u = u.reshape(shape) * max(1.0, shape[0] / max(1, u[0].numel())) ** 0.5
+    if weight_decay:
+        p.mul_(1 - lr * weight_decay)
+    p.add_(u, alpha=-lr)
+
+
+class Muon(torch.optim.Optimizer):
+    """Muon alone, for parameters of two or more dimensions (reference ``train_utils/loss.py:164-208``;
+    reference default: no Nesterov momentum)."""
+
+    def __init__(self, params, lr=0.02, momentum=0.95, nesterov=False, ns_steps=5, weight_decay=0.0):
+        super().__init__(params, dict(lr=lr, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps,
+                                      weight_decay=weight_decay))
+        for g in self.param_groups:
+            for p in g["params"]:
+                if p.ndim < 2:
+                    raise ValueError(f"Muon updates matrices only; got a parameter of shape {tuple(p.shape)} "
+                                     "(use HybridMuon for mixed parameter sets)")
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for g in self.param_groups:
+            for p in g["params"]:
+                if p.grad is not None:
+                    _muon_update(p, self.state[p], g["lr"], g["momentum"], g["nesterov"], g["ns_steps"],
+                                 g["weight_decay"])
+        return loss
+
+
 class HybridMuon(torch.optim.Optimizer):
     """Muon (momentum + Newton-Schulz orthogonalised update) for >= 2-D parameters and
     AdamW for the rest (reference ``train_utils/loss.py:164-248``)."""
@@ -124,15 +165,7 @@ class HybridMuon(torch.optim.Optimizer):
                     continue
                 st = self.state[p]
                 if g["use_muon"]:
-                    buf = st.setdefault("momentum_buffer", torch.zeros_like(p))
-                    buf.mul_(g["momentum"]).add_(p.grad)
-                    upd = p.grad.add(buf, alpha=g["momentum"]) if g["nesterov"] else buf
-                    shape = upd.shape
-                    u = zeropower_via_newtonschulz5(upd.reshape(shape[0], -1), g["ns_steps"]).to(p.dtype)
-                    u = u.reshape(shape) * max(1.0, shape[0] / max(1, u[0].numel())) ** 0.5
-                    if g["weight_decay"]:
-                        p.mul_(1 - g["lr"] * g["weight_decay"])
-                    p.add_(u, alpha=-g["lr"])
+                    _muon_update(p, st, g["lr"], g["momentum"], g["nesterov"], g["ns_steps"], g["weight_decay"])
                 else:
                     st.setdefault("step", 0)
                     st["step"] += 1

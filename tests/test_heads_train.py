@@ -394,3 +394,29 @@ def test_workflow_infer_writes_every_batch(tmp_path):
     for i in range(2):
         H = load_partitioned_hamiltonian(str(tmp_path / f"batch_{i:04d}"), lab).to_dense()
         assert H.shape[0] == H.shape[1] > 0 and np.allclose(H, H.T, atol=1e-5)
+
+
+def test_standalone_muon_orthogonal_steps():
+    """Muon alone: matrices only; a step moves along an orthogonalised direction (its singular
+    values are all close to one, times the learning rate) and a least-squares fit improves."""
+    import pytest
+
+    from maloq_b200.train.loss import Muon
+
+    with pytest.raises(ValueError):
+        Muon([torch.nn.Parameter(torch.zeros(3))])
+    torch.manual_seed(0)
+    W = torch.nn.Parameter(torch.zeros(16, 32))
+    A, T = torch.randn(64, 16), torch.randn(64, 32)
+    opt = Muon([W], lr=0.05, momentum=0.0)
+    loss0 = ((A @ W - T) ** 2).mean()
+    loss0.backward()
+    before = W.detach().clone()
+    opt.step()
+    sv = torch.linalg.svdvals((W.detach() - before) / 0.05)
+    assert sv.min() > 0.5 and sv.max() < 1.5
+    for _ in range(30):
+        opt.zero_grad()
+        ((A @ W - T) ** 2).mean().backward()
+        opt.step()
+    assert ((A @ W - T) ** 2).mean().item() < loss0.item()
