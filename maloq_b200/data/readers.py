@@ -33,7 +33,9 @@ CONVENTIONS = {
     "orca": {"s": ([0], [1]), "p": ([2, 0, 1], [1, 1, 1]), "d": ([4, 2, 0, 1, 3], [1, 1, 1, 1, 1]),
              "f": ([6, 4, 2, 0, 1, 3, 5], [-1, 1, 1, 1, 1, 1, -1]),
              "g": ([8, 6, 4, 2, 0, 1, 3, 5, 7], [-1, -1, 1, 1, 1, 1, 1, -1, -1])},
-    "pyscf": {"s": ([0], [1]), "p": ([1, 2, 0], [1, 1, 1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, 1, 1])},
+    "pyscf": {"s": ([0], [1]), "p": ([1, 2, 0], [1, 1, 1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, 1, 1]),
+              "f": ([0, 1, 2, 3, 4, 5, 6], [-1, 1, 1, 1, 1, 1, -1]),
+              "g": ([0, 1, 2, 3, 4, 5, 6, 7, 8], [-1, -1, 1, 1, 1, 1, 1, -1, -1])},
     "aims": {"s": ([0], [1]), "p": ([0, 1, 2], [1, 1, -1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, -1, 1])},
     "e3nn": {"s": ([0], [1]), "p": ([0, 1, 2], [1, 1, 1]), "d": ([0, 1, 2, 3, 4], [1, 1, 1, 1, 1]),
              "f": ([0, 1, 2, 3, 4, 5, 6], [1] * 7)},

@@ -45,3 +45,28 @@ def test_nabladft_roundtrip(tmp_path):
     assert abs(s.energy - float(np.float32(mols[0][2]))) < 1e-6 and s.forces.shape == (s.num_nodes, 3)
     b = collate(samples, lab.table)
     assert b.energy.shape == (3,) and b.forces.shape == (sum(x.num_nodes for x in samples), 3)
+
+
+def test_pyscf_orbital_order_up_to_g_shells():
+    """PySCF -> e3nn orbital order for s..g shells: p shells permuted (x, y, z) -> (y, z, x) in
+    e3nn's (m = -1, 0, 1) order; d shells as they are; f and g shells keep their order with the
+    outermost |m| components negated (the reference's PySCF reflections), and the map is the
+    inverse of e3nn -> PySCF."""
+    import numpy as np
+
+    from maloq_b200.data.readers import reorder_orbitals, reorder_orbitals_inverse
+
+    basis = {8: [0, 1, 2, 3, 4]}
+    n = 1 + 3 + 5 + 7 + 9
+    rng = np.random.default_rng(0)
+    H = rng.standard_normal((n, n))
+    H = H + H.T
+    He = reorder_orbitals(H, [8], basis, "pyscf")
+    assert np.allclose(reorder_orbitals_inverse(He, [8], basis, "pyscf"), H)
+    # p block: e3nn row 0 (m=-1) is PySCF row 1, e3nn row 2 (m=+1) is PySCF row 0
+    assert np.allclose(He[1:4, 1:4], H[1:4, 1:4][[1, 2, 0]][:, [1, 2, 0]])
+    assert np.allclose(He[4:9, 4:9], H[4:9, 4:9])
+    sf = np.array([-1, 1, 1, 1, 1, 1, -1.0])
+    assert np.allclose(He[9:16, 9:16], H[9:16, 9:16] * np.outer(sf, sf))
+    sg = np.array([-1, -1, 1, 1, 1, 1, 1, -1, -1.0])
+    assert np.allclose(He[16:, 16:], H[16:, 16:] * np.outer(sg, sg))
