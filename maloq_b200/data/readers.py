@@ -495,4 +495,100 @@ def read_orca_output(path, unrestricted=False):
     fock = None
     if focks:
         fock = {"alpha": focks[0], "beta": focks[1]} if unrestricted else focks[0]
-    return {"z": np.asarray(z, np.int64), "pos": np.asarray(pos), "basis": basis, "fock": fock, "energy": energy}
+    eps, occ = _orbital_energies(lines)
+    return {"z": np.asarray(z, np.int64), "pos": np.asarray(pos), "basis": basis, "fock": fock, "energy": energy,
+            "orbital_energies": eps, "occupations": occ}
+
+
+def _orbital_energies(lines):
+    """Orbital energies [Eh] and occupations of the last ``ORBITAL ENERGIES`` section: one
+    array per spin channel (two after ``SPIN UP`` / ``SPIN DOWN ORBITALS`` headers)."""
+    starts = [i for i, ln in enumerate(lines) if ln.strip() == "ORBITAL ENERGIES"]
+    if not starts:
+        return [], []
+    eps, occ = [], []
+    i = starts[-1] + 1
+    while i < len(lines) and len(eps) < 2:
+        t = lines[i].strip()
+        if t.split()[:2] == ["NO", "OCC"]:
+            e, o = [], []
+            i += 1
+            while i < len(lines):
+                q = lines[i].split()
+                try:
+                    o.append(float(q[1]))
+                    e.append(float(q[2]))
+                except (IndexError, ValueError):
+                    break
+                i += 1
+            eps.append(np.asarray(e))
+            occ.append(np.asarray(o))
+            continue
+        # between the tables only blank lines, dashes and the spin headers
+        if eps and t and not t.startswith("SPIN") and set(t) != {"-"}:
+            break
+        i += 1
+    return eps, occ
+
+
+def homo_lumo_energies(orbital_energies, n_electrons, multiplicity=1):
+    """(HOMO energies, LUMO energies), one per spin channel: n_alpha = (N + M - 1) / 2 and
+    n_beta = (N - M + 1) / 2 occupied orbitals for multiplicity M (reference
+    ``utils_orca_out.py:258-269``); a single channel gives the closed-shell / alpha values."""
+    n_alpha = (n_electrons + multiplicity - 1) // 2
+    homo, lumo = [orbital_energies[0][n_alpha - 1]], [orbital_energies[0][n_alpha]]
+    if len(orbital_energies) > 1:
+        n_beta = (n_electrons - multiplicity + 1) // 2
+        homo.append(orbital_energies[1][n_beta - 1])
+        lumo.append(orbital_energies[1][n_beta])
+    return homo, lumo
+
+
+def charge_and_multiplicity_from_path(path, levels=3):
+    """(charge, multiplicity) from a run folder named ``..._<charge>_<multiplicity>``, looking at
+    the file's folder and up to ``levels - 1`` parents; (0, 1) when none matches (reference
+    ``utils_orca_out.py:82-117``)."""
+    import re
+
+    d = os.path.dirname(os.path.abspath(path))
+    for _ in range(levels):
+        m = re.search(r"_(-?\d+)_(\d+)$", os.path.basename(d))
+        if m:
+            return int(m.group(1)), int(m.group(2))
+        parent = os.path.dirname(d)
+        if parent == d:
+            break
+        d = parent
+    return 0, 1
+
+
+def read_finalms(path):
+    """The ``finalms`` value of an ORCA input file (final spin projection), or None."""
+    import re
+
+    with open(path) as f:
+        for ln in f:
+            m = re.search(r"finalms\s+([-\d.]+)", ln, re.IGNORECASE)
+            if m:
+                return float(m.group(1))
+    return None
+
+
+def orbital_count(z, basis):
+    """Number of orbitals (the Fock matrix size) of atoms ``z`` in ``basis``."""
+    return int(sum(sum(2 * (l % 10) + 1 for l in basis[int(a)]) for a in z))
+
+
+def sort_by_l(H, basis, z):
+    """Reorder each atom's shells by angular momentum (stable within a degree), rows and
+    columns (reference ``utils_orca_out.py:467-495``)."""
+    perm, off = [], 0
+    for a in z:
+        shells = []
+        for l in basis[int(a)]:
+            n = 2 * (l % 10) + 1
+            shells.append((l % 10, off, n))
+            off += n
+        for _, o, n in sorted(shells, key=lambda t: t[0]):
+            perm.extend(range(o, o + n))
+    return H[np.ix_(perm, perm)]

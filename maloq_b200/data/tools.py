@@ -39,30 +39,38 @@ import torch
 
 
 # ------------------------------------------------------------------ ORCA runs -> ASE database
-def orca_runs_to_db(out_path, run_dirs, unrestricted=False, charge=0, spin_multiplicity=None):
-    """One ASE-database row per ORCA run directory; returns the number of rows written."""
+def orca_runs_to_db(out_path, run_dirs, unrestricted=None, charge=None, spin_multiplicity=None):
+    """One ASE-database row per ORCA run directory; returns the number of rows written.  Charge
+    and multiplicity default to the ``..._<charge>_<multiplicity>`` suffix of the run's folder
+    (or a parent's; 0 and 1 without one), and a multiplicity above 1 means an unrestricted run
+    (two Fock matrices) unless ``unrestricted`` says otherwise."""
     from .asedb import write_asedb
-    from .readers import read_orca_output, reorder_orbitals
+    from .readers import charge_and_multiplicity_from_path, read_orca_output, reorder_orbitals
 
     rows = []
     for d in run_dirs:
         outs = sorted(glob.glob(os.path.join(d, "*.out")))
         if not outs:
             continue
-        r = read_orca_output(outs[0], unrestricted=unrestricted)
+        q_path, m_path = charge_and_multiplicity_from_path(outs[0])
+        q = q_path if charge is None else charge
+        mult = m_path if spin_multiplicity is None else spin_multiplicity
+        uhf = (mult > 1) if unrestricted is None else bool(unrestricted)
+        r = read_orca_output(outs[0], unrestricted=uhf)
         z = np.asarray(r["z"], dtype=np.int64)
         basis = r["basis"]
-        if unrestricted:
+        if uhf:
             fock = np.stack([reorder_orbitals(r["fock"][k], z, basis, "orca") for k in ("alpha", "beta")])
         else:
             fock = reorder_orbitals(r["fock"], z, basis, "orca")
-        mult = spin_multiplicity if spin_multiplicity is not None else (2 if unrestricted else 1)
-        rows.append({"numbers": z, "positions": np.asarray(r["pos"]),
-                     "energy": r["energy"],
-                     "data": {"fock_matrix": fock.astype(np.float32),
-                              "total_energy [Eh]": r["energy"] if r["energy"] is not None else 0.0,
-                              "is_open_shell": bool(unrestricted), "charge": int(charge),
-                              "spin_multiplicity": int(mult), "folder_name": os.path.basename(os.path.normpath(d))}})
+        data = {"fock_matrix": fock.astype(np.float32),
+                "total_energy [Eh]": r["energy"] if r["energy"] is not None else 0.0,
+                "is_open_shell": uhf, "charge": int(q), "spin_multiplicity": int(mult),
+                "folder_name": os.path.basename(os.path.normpath(d))}
+        if r["orbital_energies"]:
+            data["orbital_energies [Eh]"] = np.stack(r["orbital_energies"]) if len(
+                {len(e) for e in r["orbital_energies"]}) == 1 else r["orbital_energies"][0]
+        rows.append({"numbers": z, "positions": np.asarray(r["pos"]), "energy": r["energy"], "data": data})
     if rows:
         write_asedb(out_path, rows)
     return len(rows)
@@ -202,8 +210,9 @@ def main(argv=None):
     a = sub.add_parser("orca-to-db")
     a.add_argument("out")
     a.add_argument("runs", nargs="+")
-    a.add_argument("--unrestricted", action="store_true")
-    a.add_argument("--charge", type=int, default=0)
+    a.add_argument("--unrestricted", action="store_true", default=None)
+    a.add_argument("--charge", type=int, default=None)
+    a.add_argument("--multiplicity", type=int, default=None)
     b = sub.add_parser("lin-ref")
     b.add_argument("datasets", nargs="+")
     b.add_argument("out")
@@ -224,7 +233,7 @@ def main(argv=None):
     c.add_argument("--num", type=int, default=None)
     args = ap.parse_args(argv)
     if args.cmd == "orca-to-db":
-        n = orca_runs_to_db(args.out, args.runs, args.unrestricted, args.charge)
+        n = orca_runs_to_db(args.out, args.runs, args.unrestricted, args.charge, args.multiplicity)
         print(f"wrote {n} rows to {args.out}")
     elif args.cmd == "lin-ref":
         if args.subsample is None and len(args.datasets) == 1:

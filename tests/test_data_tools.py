@@ -26,15 +26,16 @@ def test_orca_runs_to_ase_database(tmp_path):
         F = np.round(rng.standard_normal((19, 19)), 6)
         F = F + F.T
         Fs.append(F)
-        d = tmp_path / f"run{k}"
+        d = tmp_path / (f"run{k}_0_1" if k == 1 else f"run{k}")
         d.mkdir()
         (d / "orca.out").write_text(_orca_text(F, -76.0 - k))
     out = str(tmp_path / "mols.db")
-    assert tools.main(["orca-to-db", out] + [str(tmp_path / f"run{k}") for k in range(3)]) is None
+    runs = [str(tmp_path / (f"run{k}_0_1" if k == 1 else f"run{k}")) for k in range(3)]
+    assert tools.main(["orca-to-db", out] + runs) is None
     ds = asedb.ASEDataset(out)
     assert len(ds) == 3
     r = ds[1]
-    assert list(r["atomic_numbers"]) == [1, 8] and r["folder_name"] == "run1"
+    assert list(r["atomic_numbers"]) == [1, 8] and r["folder_name"] == "run1_0_1"
     assert abs(r["energies"] + 77.0) < 1e-9
     ref = readers.reorder_orbitals(Fs[1], [1, 8], {1: [0, 0, 1], 8: [0, 0, 0, 1, 1, 2]}, "orca")
     assert np.allclose(r["fock_matrix"], ref, atol=1e-5)

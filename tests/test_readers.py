@@ -70,3 +70,41 @@ def test_pyscf_orbital_order_up_to_g_shells():
     assert np.allclose(He[9:16, 9:16], H[9:16, 9:16] * np.outer(sf, sf))
     sg = np.array([-1, -1, 1, 1, 1, 1, 1, -1, -1.0])
     assert np.allclose(He[16:, 16:], H[16:, 16:] * np.outer(sg, sg))
+
+
+def _orca_orbital_text(unrestricted):
+    head = ["----------------", "ORBITAL ENERGIES", "----------------", ""]
+    tab = lambda e, o: ["  NO   OCC          E(Eh)            E(eV) "] + \
+        [f"{i:4d}   {oc:.4f}     {en: .6f}    {en * 27.2114: .4f}" for i, (en, oc) in enumerate(zip(e, o))] + [""]
+    if not unrestricted:
+        return head + tab([-20.5, -1.3, -0.6, 0.1, 0.4], [2, 2, 2, 0, 0]) + ["", "MULLIKEN POPULATION ANALYSIS", "1 2 3"]
+    return head + ["SPIN UP ORBITALS"] + tab([-20.0, -1.0, -0.5, 0.2], [1, 1, 1, 0]) + \
+        ["SPIN DOWN ORBITALS"] + tab([-19.9, -0.9, 0.3, 0.5], [1, 1, 0, 0]) + ["", "MULLIKEN POPULATION ANALYSIS"]
+
+
+def test_orca_orbital_energies_homo_lumo_and_path_conventions(tmp_path):
+    import numpy as np
+
+    from maloq_b200.data import readers as R
+
+    eps, occ = R._orbital_energies(_orca_orbital_text(False))
+    assert len(eps) == 1 and np.allclose(eps[0], [-20.5, -1.3, -0.6, 0.1, 0.4]) and occ[0].sum() == 6
+    assert R.homo_lumo_energies(eps, 6) == ([-0.6], [0.1])
+    eps, occ = R._orbital_energies(_orca_orbital_text(True))
+    assert len(eps) == 2 and len(eps[1]) == 4
+    homo, lumo = R.homo_lumo_energies(eps, 5, multiplicity=2)  # 3 alpha, 2 beta electrons
+    assert homo == [-0.5, -0.9] and lumo == [0.2, 0.3]
+    d = tmp_path / "mol_17_-1_2" / "step1"
+    d.mkdir(parents=True)
+    (d / "orca.out").write_text("x")
+    assert R.charge_and_multiplicity_from_path(str(d / "orca.out")) == (-1, 2)
+    assert R.charge_and_multiplicity_from_path(str(tmp_path / "plain" / "orca.out")) == (0, 1)
+    (d / "orca.inp").write_text("%scf\n  FinalMs 0.5\nend\n")
+    assert R.read_finalms(str(d / "orca.inp")) == 0.5
+    basis = {1: [0, 0, 1], 8: [0, 1, 0, 2, 1]}
+    assert R.orbital_count([8, 1, 1], basis) == 1 + 3 + 1 + 5 + 3 + 2 * 5
+    H = np.arange(13 * 13, dtype=float).reshape(13, 13)
+    Hs = R.sort_by_l(H, basis, [8])
+    # O shells s(0) p(1-3) s(4) d(5-9) p(10-12) -> s s p p d
+    perm = [0, 4] + [1, 2, 3] + [10, 11, 12] + [5, 6, 7, 8, 9]
+    assert np.array_equal(Hs, H[np.ix_(perm, perm)])
