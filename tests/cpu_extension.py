@@ -112,7 +112,8 @@ class CpuExtension:
 
     def splitk_reduce(self, part, out, beta):
         assert part.dtype == out.dtype == torch.float32 and out.is_contiguous()
-        out.copy_(part.sum(0).view_as(out) + beta * out)
+        s = part.sum(0).view_as(out)
+        out.copy_(s if beta == 0 else beta * out + s)  # beta = 0: out is not read (may be uninitialised)
 
     # ------------------------------------------------------------------ edge frame
     @staticmethod

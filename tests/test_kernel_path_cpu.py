@@ -88,3 +88,72 @@ def test_chunked_and_recomputed_kernel_paths_match_on_cpu(monkeypatch, extra):
         assert abs(a - r) <= tol * abs(r), (a, r)
     worst = max(float((got[3][n] - g).norm() / (g.norm() + 1e-12)) for n, g in ref[3].items())
     assert worst < 2.5 * tol, worst
+
+
+def _train_mae(steps, kernel_path, monkeypatch):
+    """Train the small model on fixed synthetic Fock targets; Hamiltonian MAE of the result."""
+    from maloq_b200.data import datasets
+    from maloq_b200.data.batch import collate
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    lab = datasets.labeler_for("small")
+    kw = dict(sphere_channels=16, hidden_channels=16, lmax=4, mmax=2, cutoff=5.0, num_layers=2,
+              num_distance_basis=8, edge_channels=16)
+    samples, _ = datasets.build_dataset("small", 6, kw, seed=3, labeler=lab)
+    b = collate(samples, lab.table)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, include_edges=True, **kw)
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=16, ls_list=lab.layout.ls_list,
+                          reduce_node=True, reduce_node_intra=True)
+    if kernel_path:
+        use_cpu_extension(monkeypatch)
+    opt = torch.optim.Adam(list(bb.parameters()) + list(hd.parameters()), lr=3e-3)
+    tr = SplitTrainer(bb, hd, lab.irreps, mask_table=torch.as_tensor(lab.table.mask))
+    for _ in range(steps):
+        tr.train_step(b, L.rmse_mse_padded_loss, opt)
+    with torch.no_grad():
+        no, eo = hd(bb(b), b)
+    maes = []
+    n0 = e0 = 0
+    for s in samples:  # per molecule: predicted vs target Hamiltonian blocks
+        n1, e1 = n0 + s.num_nodes, e0 + s.num_edges
+        Hp = lab.blocks_from_labels(s, no[0][n0:n1], eo[0][e0:e1]).to_dense()
+        Ht = lab.blocks_from_labels(s, s.node_y[0], s.y[0]).to_dense()
+        maes.append(float(np.abs(Hp - Ht).mean()))
+        n0, e0 = n1, e1
+    return float(np.mean(maes))
+
+
+def test_trained_hamiltonian_mae_matches_pytorch_path(monkeypatch):
+    """Hamiltonian MAE after the same training run on the PyTorch path (fp32) and on the kernel
+    path (bf16 GEMM operands, CPU stand-in): the reduced-precision operands do not cost
+    accuracy at this scale (within 10 %), and both improve on the untrained model."""
+    mae0 = _train_mae(0, False, monkeypatch)
+    ref = _train_mae(40, False, monkeypatch)
+    got = _train_mae(40, True, monkeypatch)
+    assert ref < 0.7 * mae0 and got < 0.7 * mae0, (mae0, ref, got)
+    assert abs(got - ref) <= 0.1 * ref, (ref, got)
+
+
+def test_kernel_path_reads_no_uninitialised_memory(monkeypatch):
+    """With PyTorch filling every new uninitialised tensor with NaN, one training step on the
+    kernel path (CPU stand-in) stays finite: no buffer handed to a kernel is read before it is
+    written."""
+    import torch.utils.deterministic as det
+
+    bb, hd, b, lab = _model(2, "source-target-message")
+    old_mode, old_fill = torch.are_deterministic_algorithms_enabled(), det.fill_uninitialized_memory
+    torch.use_deterministic_algorithms(True, warn_only=True)
+    det.fill_uninitialized_memory = True
+    try:
+        use_cpu_extension(monkeypatch)
+        ln, le, loss, grads = _step(bb, hd, b, lab)
+    finally:
+        torch.use_deterministic_algorithms(old_mode)
+        det.fill_uninitialized_memory = old_fill
+    assert np.isfinite([ln, le, loss]).all()
+    bad = [n for n, g in grads.items() if not torch.isfinite(g).all()]
+    assert not bad, bad
