@@ -138,13 +138,15 @@ def test_trained_hamiltonian_mae_matches_pytorch_path(monkeypatch):
     assert abs(got - ref) <= 0.1 * ref, (ref, got)
 
 
-def test_kernel_path_reads_no_uninitialised_memory(monkeypatch):
+@pytest.mark.parametrize("extra", [{}, dict(edge_chunk=40), dict(edge_chunk=40, edge_stream_dtype=torch.float32),
+                                   dict(activation_checkpointing=True)])
+def test_kernel_path_reads_no_uninitialised_memory(monkeypatch, extra):
     """With PyTorch filling every new uninitialised tensor with NaN, one training step on the
     kernel path (CPU stand-in) stays finite: no buffer handed to a kernel is read before it is
     written."""
     import torch.utils.deterministic as det
 
-    bb, hd, b, lab = _model(2, "source-target-message")
+    bb, hd, b, lab = _model(2, "source-target-message", **extra)
     old_mode, old_fill = torch.are_deterministic_algorithms_enabled(), det.fill_uninitialized_memory
     torch.use_deterministic_algorithms(True, warn_only=True)
     det.fill_uninitialized_memory = True
