@@ -363,7 +363,9 @@ class eSEN_Backbone(nn.Module):
         x_node[:, 0] = l0
         if graph.chunks is None:
             gauss = self.distance_expansion(dist)
-            x_edge = torch.cat([self.source_embedding(batch.src_z), gauss, self.target_embedding(batch.dst_z)], dim=1)
+            # the radial MLPs' input: read by every block's radial MLP, only through GEMMs
+            x_edge = ops.gemm_operand(torch.cat([self.source_embedding(batch.src_z), gauss,
+                                                 self.target_embedding(batch.dst_z)], dim=1))
             x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
             x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
         else:

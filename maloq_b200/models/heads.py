@@ -266,6 +266,12 @@ class _ConvHeadBase(nn.Module):
         self.so2_conv_2 = SO2_Convolution(self.hidden_channels, out_channels, self.lmax, self.mmax,
                                           self.mappingReduced, internal_weights=True)
 
+    @property
+    def mapping(self):
+        """The coefficient mapping under the name the Edgewise ops read (``mappingReduced`` is
+        the reference's attribute name)."""
+        return self.mappingReduced
+
     def conv(self, emb):
         xe = emb["x_edge"]
         if hasattr(xe, "full"):  # chunked backbones hand over the lazy edge features

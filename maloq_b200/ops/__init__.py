@@ -10,7 +10,7 @@ from . import reference as _ref
 from . import native as _native
 
 __all__ = [
-    "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
+    "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
     "rotate_back_m0_scatter", "rotate_back_m0", "fock_loss",
 ]
 
@@ -37,6 +37,17 @@ def _cuda(*tensors) -> bool:
         if t is not None and hasattr(t, "is_cuda"):
             return bool(t.is_cuda)
     return False
+
+
+def gemm_operand(x):
+    """``x`` in the dtype the kernel path's GEMMs read (bf16) when it only feeds GEMMs - cast once
+    instead of once per consumer, with its gradient accumulated in that dtype too; unchanged on
+    the PyTorch path."""
+    if _cuda(x):
+        import torch
+
+        return x.to(torch.bfloat16)
+    return x
 
 
 def linear(x, weight, bias=None, act=None, out_dtype=None):

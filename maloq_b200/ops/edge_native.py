@@ -124,17 +124,18 @@ class EdgewiseFn(torch.autograd.Function):
               [b1.float().contiguous()] + [None] * (nw - 1))
         H1 = torch.empty(E, R * H, device=dev, dtype=torch.bfloat16)
         lib.gate_fwd(*LM, Y1, H1, H)
-        Y2 = torch.empty(E, R * C, device=dev, dtype=torch.bfloat16)
+        Co = meta["Co"]  # output channels of the second convolution (C, or a padded head width)
+        Y2 = torch.empty(E, R * Co, device=dev, dtype=torch.bfloat16)
         hb = _blocks(meta["m_size"], H)
-        cb = _blocks(meta["m_size"], C)
+        cb = _blocks(meta["m_size"], Co)
         _gemm([H1[:, a0:a1] for a0, a1 in hb], w2b, [Y2[:, y0:y1] for y0, y1 in cb],
               [b2.float().contiguous()] + [None] * (nw - 1))
         if meta["node"]:
             # rows of the destination range (all nodes, or one chunk's nodes)
-            out = torch.empty(graph.num_out, S, C, device=dev, dtype=torch.float32)
+            out = torch.empty(graph.num_out, S, Co, device=dev, dtype=torch.float32)
             lib.rotate_back_scatter(*LM, Y2, 0, R, graph.rot, graph.out_ptr, None, out, 1.0)
         else:
-            out = torch.empty(E, S, C, device=dev, dtype=torch.float32)
+            out = torch.empty(E, S, Co, device=dev, dtype=torch.float32)
             lib.rotate_back_edge(*LM, Y2, 0, R, graph.rot, out)
         count_launches(4)
         ctx.save_for_backward(x_node, xe, rad, A, Y1, H1, *weights)
@@ -156,10 +157,11 @@ class EdgewiseFn(torch.autograd.Function):
         E = graph.src.shape[0]
         dev = g.device
         g = g.contiguous().float()
-        dY2 = torch.empty(E, R * C, device=dev, dtype=torch.bfloat16)
+        Co = meta["Co"]
+        dY2 = torch.empty(E, R * Co, device=dev, dtype=torch.bfloat16)
         _rotate_grad(LM, g, graph, meta["node"], dY2, None, R, 1.0)
         hb = _blocks(meta["m_size"], H)
-        cb = _blocks(meta["m_size"], C)
+        cb = _blocks(meta["m_size"], Co)
         ab = _blocks(meta["m_size"], Cin)
         yb = _blocks(meta["m_size"], H, G)
         # conv2
@@ -199,9 +201,11 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
     Cin = mod.concat_size * C
     key = ("edge_meta", id(mod), node_or_edge)
     meta = graph.cache.get(key)
+    co = c2.m_output_channels
+    cp = co if co % 8 == 0 else (co + 7) // 8 * 8  # GEMM / rotate-back rows: 16-byte aligned widths
     if meta is None:
         meta = dict(R=mapping.res_size, H=c1.m_output_channels, L=mod.lmax, MM=mod.mmax, Cin=Cin,
-                    G=c1.extra_m0_output_channels, m_size=list(mapping.m_size), node=node_or_edge == "node")
+                    G=c1.extra_m0_output_channels, m_size=list(mapping.m_size), node=node_or_edge == "node", Co=cp)
         graph.cache[key] = meta
     rad = c1.rad_func(x_edge, out_dtype=torch.bfloat16)
     halo = None
@@ -212,9 +216,24 @@ def edgewise(mod, x_node, x_msg_edge, x_edge, graph, node_or_edge):
             halo = (peer, peer.publish(x_node))  # rows readable by every rank; slot id
         else:
             x_src_space = graph.halo.extend(x_node, graph)
-    weights = [c1.fc_m0.weight] + [c.fc.weight for c in c1.so2_m_conv] + \
-        [c2.fc_m0.weight] + [c.fc.weight for c in c2.so2_m_conv]
-    return EdgewiseFn.apply(x_src_space, x_msg_edge, rad, c1.fc_m0.bias, c2.fc_m0.bias, graph, meta, halo, *weights)
+    w2 = [c2.fc_m0.weight] + [c.fc.weight for c in c2.so2_m_conv]
+    b2 = c2.fc_m0.bias
+    if cp != co:
+        # narrow heads (e.g. one force channel): zero output channels up to cp, as differentiable
+        # views of the parameters (their gradients come back unpadded); the caller sees co channels
+        w2 = [_pad_out_channels(w, co, cp) for w in w2]
+        b2 = _pad_out_channels(b2, co, cp)
+    weights = [c1.fc_m0.weight] + [c.fc.weight for c in c1.so2_m_conv] + w2
+    out = EdgewiseFn.apply(x_src_space, x_msg_edge, rad, c1.fc_m0.bias, b2, graph, meta, halo, *weights)
+    return out if cp == co else out[..., :co]
+
+
+def _pad_out_channels(w, co, cp):
+    """Rows of a convolution weight (or bias) grouped as [..., co] output channels -> cp
+    channels, the new ones zero: [n*co, K] -> [n*cp, K] (and [n*co] -> [n*cp])."""
+    if w.dim() == 1:
+        return torch.nn.functional.pad(w.view(-1, co), (0, cp - co)).reshape(-1)
+    return torch.nn.functional.pad(w.view(-1, co, w.shape[1]), (0, 0, 0, cp - co)).reshape(-1, w.shape[1])
 
 
 def _rotate_grad(LM, g, graph, node, DY, DYf, Rk, scale):

@@ -57,3 +57,46 @@ def test_trained_hamiltonian_mae_kernel_path_matches_fp32_pytorch(cuda_device):
     assert ref < 0.8 * mae0
     assert abs(got - ref) <= 0.1 * ref, (ref, got)
     assert kernels.error_status() == 0
+
+
+@pytest.mark.parametrize("kind", ["energies", "forces"])
+def test_energy_and_force_heads_kernel_path(cuda_device, kind):
+    """Energy / force heads on the kernel path (their convolution has C or one output channel,
+    padded to 8 for the kernels) against the fp32 PyTorch ops: loss and head gradients."""
+    from maloq_b200 import ops
+    from maloq_b200.data import datasets
+    from maloq_b200.data.batch import collate
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import HELM_Energy_Head, HELM_Force_Head
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    lab = datasets.labeler_for("small")
+    kw = dict(sphere_channels=32, hidden_channels=32, lmax=4, mmax=2, cutoff=5.0, num_layers=1,
+              num_distance_basis=16, edge_channels=32)
+    samples = datasets.build_samples("small", 6, seed=1)
+    b = collate(samples, lab.table).to(cuda_device)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, include_edges=False, **kw).to(cuda_device)
+    hd = (HELM_Energy_Head if kind == "energies" else HELM_Force_Head)(bb).to(cuda_device)
+    if kind == "energies":
+        b.energy = torch.randn(b.num_graphs, device=cuda_device)
+    else:
+        b.forces = torch.randn(b.num_nodes, 3, device=cuda_device)
+
+    def step(torch_ops):
+        ops.use_torch_ops(torch_ops)
+        try:
+            tr = SplitTrainer(bb, hd, lab.irreps)
+            for p in list(bb.parameters()) + list(hd.parameters()):
+                p.grad = None
+            _, _, loss = tr.forward_loss(b, L.mse_padded_loss)
+            loss.backward()
+        finally:
+            ops.use_torch_ops(False)
+        return float(loss.detach()), {n: p.grad.clone() for n, p in hd.named_parameters() if p.grad is not None}
+
+    ref, got = step(True), step(False)
+    assert abs(got[0] - ref[0]) <= 2e-2 * abs(ref[0])
+    for n, g in ref[1].items():
+        assert ((got[1][n] - g).norm() / (g.norm() + 1e-12)).item() < 5e-2, n

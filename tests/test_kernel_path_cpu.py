@@ -159,3 +159,35 @@ def test_kernel_path_reads_no_uninitialised_memory(monkeypatch, extra):
     assert np.isfinite([ln, le, loss]).all()
     bad = [n for n, g in grads.items() if not torch.isfinite(g).all()]
     assert not bad, bad
+
+
+@pytest.mark.parametrize("kind", ["energies", "forces"])
+def test_energy_and_force_heads_on_the_kernel_path(monkeypatch, kind):
+    """Energy / force heads (an extra Edgewise convolution on the node embeddings) on the kernel
+    path against the PyTorch path: loss and gradients."""
+    from maloq_b200.models.heads import HELM_Energy_Head, HELM_Force_Head
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    bb, _, b, lab = _model(2)
+    torch.manual_seed(2)
+    hd = (HELM_Energy_Head if kind == "energies" else HELM_Force_Head)(bb)
+    if kind == "energies":
+        b.energy = torch.randn(b.num_graphs)
+    else:
+        b.forces = torch.randn(b.num_nodes, 3)
+
+    def step():
+        tr = SplitTrainer(bb, hd, lab.irreps)
+        for p in list(bb.parameters()) + list(hd.parameters()):
+            p.grad = None
+        _, _, loss = tr.forward_loss(b, L.mse_padded_loss)
+        loss.backward()
+        return float(loss.detach()), {n: p.grad.clone() for n, p in hd.named_parameters() if p.grad is not None}
+
+    ref = step()
+    use_cpu_extension(monkeypatch)
+    got = step()
+    assert abs(got[0] - ref[0]) <= 2e-2 * abs(ref[0])
+    for n, g in ref[1].items():
+        assert ((got[1][n] - g).norm() / (g.norm() + 1e-12)).item() < 5e-2, n
