@@ -9,12 +9,16 @@ changed.  A cached copy is keyed by
   step post-hook; fused optimizers update parameters without bumping their version
   counters, so the epoch is what catches their updates),
 * the parameter's version counter (in-place edits such as ``load_state_dict``),
-* its storage address.
+* its storage address,
+
+and holds a weak reference to the parameter itself (an entry is dropped when its parameter dies).
 
 Code that changes weights some other way (through ``.data``) calls :func:`invalidate`.
 """
 
 from __future__ import annotations
+
+import weakref
 
 import torch
 
@@ -42,10 +46,13 @@ def _get(p, kind, make):
         return make(p.detach())
     key = (_EPOCH[0], p._version, p.data_ptr(), kind)
     ent = _CACHE.get((id(p), kind))
-    if ent is not None and ent[0] == key:
+    # the entry must belong to this very parameter: a freed parameter's id and storage address
+    # can be reused by a new one with the same version count (e.g. a model built after another
+    # was deleted), which the key alone would not tell apart
+    if ent is not None and ent[0] == key and ent[2]() is p:
         return ent[1]
     t = make(p.detach())
-    _CACHE[(id(p), kind)] = (key, t)
+    _CACHE[(id(p), kind)] = (key, t, weakref.ref(p, lambda _r, k=(id(p), kind): _CACHE.pop(k, None)))
     return t
 
 

@@ -9,9 +9,10 @@ in slice 0 and zeros elsewhere (the callers sum the slices).
 
 With ``use_cpu_extension(monkeypatch)`` the op layer sends CPU tensors down the kernel path, so
 the Python side of that path (views, strides, padding, buffer layouts, autograd functions,
-weight caches) runs on a machine without a GPU and can be compared with the PyTorch path.  The
-argument checks mirror the extension's (dtypes, shapes, contiguity, the 16-byte rule of the TMA
-descriptors).  Kernels that need peer memory (halo, fused all-reduce) are not provided.
+weight caches, label rows) runs on a machine without a GPU and can be compared with the PyTorch
+path.  The argument checks mirror the extension's (dtypes, shapes, contiguity, the 16-byte rule
+of the TMA descriptors).  Kernels that need peer memory (halo, fused all-reduce) and the device
+radius graph are not provided.
 """
 
 from __future__ import annotations
@@ -270,6 +271,33 @@ class CpuExtension:
         DX.copy_(gx)
         DSV.copy_(gs)
 
+    # ------------------------------------------------------------------ label rows
+    def basis_rows(self, inp, out, ptr, pt, pos, meta, coef, d_in, rows, gather, scatter):
+        """out[r, u] = sum_{j < n_u} in[r, s_u + j] * coef[c_u + j n_u], meta[u] = (s_u, n_u, c_u, 0);
+        gather: in[r, k] = data[ptr[r] + pos[pt[r], k]] (0 where pos < 0); scatter: data[ptr[r] +
+        pos[pt[r], u]] = out[r, u] (skipped where pos < 0); otherwise dense rows."""
+        assert inp.dtype == out.dtype == coef.dtype and inp.dtype in (torch.float32, torch.float64)
+        assert meta.dtype == torch.int32 and meta.shape[1] == 4
+        d_out = meta.shape[0]
+        if gather:
+            p = pos[pt[:rows]].long()  # [rows, d_in]
+            idx = ptr[:rows, None] + p.clamp(min=0)
+            x = torch.where(p >= 0, inp.reshape(-1)[idx], torch.zeros((), dtype=inp.dtype))
+        else:
+            x = inp.reshape(-1)[: rows * d_in].view(rows, d_in)
+        y = torch.empty(rows, d_out, dtype=inp.dtype)
+        for u in range(d_out):
+            su, nu, cu = (int(v) for v in meta[u, :3])
+            c = coef[cu + torch.arange(nu) * nu]
+            y[:, u] = x[:, su:su + nu] @ c
+        if scatter:
+            p = pos[pt[:rows]].long()  # [rows, d_out]
+            ok = p >= 0
+            flat = out.view(-1)
+            flat[(ptr[:rows, None] + p)[ok]] = y[ok]
+        else:
+            out.view(-1)[: rows * d_out].copy_(y.reshape(-1))
+
     # ------------------------------------------------------------------ rotation, loss, status
     def edge_rotation(self, vec, J, joff, L, row_l, row_m, ROT):
         from maloq_b200.core import sph
@@ -324,10 +352,10 @@ def use_cpu_extension(monkeypatch):
 
     ext = _Recorder(CpuExtension())
     monkeypatch.setattr(kernels, "_lib", ext)
+    from maloq_b200.ops import basis_transform, labels
     from maloq_b200.ops import loss as ops_loss
 
-    # the op layer and the loss module decide CPU vs kernel path with _cuda; labels and the basis
-    # transform stay on the PyTorch path (their kernels are not provided here)
-    for mod in (ops, ops_loss):
+    # every module that decides CPU vs kernel path with _cuda
+    for mod in (ops, ops_loss, labels, basis_transform):
         monkeypatch.setattr(mod, "_cuda", lambda *t: True)
     return ext

@@ -79,10 +79,11 @@ def test_energy_and_force_heads_kernel_path(cuda_device, kind):
     torch.manual_seed(0)
     bb = eSEN_Backbone(lab.irreps, include_edges=False, **kw).to(cuda_device)
     hd = (HELM_Energy_Head if kind == "energies" else HELM_Force_Head)(bb).to(cuda_device)
+    # zero targets: the loss's relative error is then the prediction's
     if kind == "energies":
-        b.energy = torch.randn(b.num_graphs, device=cuda_device)
+        b.energy = torch.zeros(b.num_graphs, device=cuda_device)
     else:
-        b.forces = torch.randn(b.num_nodes, 3, device=cuda_device)
+        b.forces = torch.zeros(b.num_nodes, 3, device=cuda_device)
 
     def step(torch_ops):
         ops.use_torch_ops(torch_ops)

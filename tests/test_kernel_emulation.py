@@ -158,3 +158,19 @@ def test_weight_cache_layouts_and_refresh():
         (p.sum() + q.sum()).backward()
         opt.step()
         opt.zero_grad()
+
+
+def test_weight_cache_entries_die_with_their_parameter():
+    """A cached bf16 copy is dropped when its parameter is freed, so a new parameter that reuses
+    the freed one's id and storage address cannot be served the old copy."""
+    import gc
+
+    from maloq_b200.ops import weights as W
+
+    p = torch.nn.Parameter(torch.randn(4, 4))
+    W.bf16(p)
+    key = (id(p), "bf16")
+    assert key in W._CACHE and W._CACHE[key][2]() is p
+    del p
+    gc.collect()
+    assert key not in W._CACHE
