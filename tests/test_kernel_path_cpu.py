@@ -257,3 +257,35 @@ def test_workflow_trains_on_the_kernel_path(monkeypatch, tmp_path, target):
     tr = hist["train_node"] if target == "fock_matrix" else [a + b for a, b in zip(hist["train_node"],
                                                                                    hist["train_edge"])]
     assert np.isfinite(tr).all() and tr[-1] < tr[0], tr
+
+
+def test_lmax6_frame_on_the_kernel_path(monkeypatch):
+    """The lmax 6 / mmax 2 frame of the large-molecule configuration (def2-TZVP-like basis, f
+    shells) on the kernel path against the PyTorch path."""
+    from maloq_b200.data import datasets
+    from maloq_b200.data.batch import collate
+    from maloq_b200.models.backbone import eSEN_Backbone
+    from maloq_b200.models.heads import Fock_Irreps_Head
+
+    lab = datasets.labeler_for("large")
+    assert lab.layout.lmax == 6
+    samples = datasets.build_samples("large", 1, seed=2)
+    samples = [s for s in samples]
+    torch.manual_seed(5)
+    for s in samples:
+        s.node_y = torch.randn(1, s.num_nodes, lab.target_len)
+        s.y = torch.randn(1, s.num_edges, lab.target_len)
+    b = collate(samples, lab.table)
+    kw = dict(sphere_channels=8, hidden_channels=8, lmax=6, mmax=2, cutoff=6.0, num_layers=1, num_distance_basis=8,
+              edge_channels=8)
+    torch.manual_seed(0)
+    bb = eSEN_Backbone(lab.irreps, include_edges=True, **kw)
+    hd = Fock_Irreps_Head(None, lab.irreps, lmax=6, sphere_channels=8, ls_list=lab.layout.ls_list,
+                          reduce_node=True, reduce_node_intra=True)
+    ref = _step(bb, hd, b, lab)
+    use_cpu_extension(monkeypatch)
+    got = _step(bb, hd, b, lab)
+    assert abs(got[2] - ref[2]) <= 3e-2 * abs(ref[2])
+    errs = sorted(float((got[3][n] - g).norm() / (g.norm() + 1e-12)) for n, g in ref[3].items())
+    # 8 channels: bf16 operand noise is larger than at production widths
+    assert errs[-1] < 8e-2 and errs[len(errs) // 2] < 2e-2, errs[-5:]
