@@ -289,3 +289,33 @@ def test_lmax6_frame_on_the_kernel_path(monkeypatch):
     errs = sorted(float((got[3][n] - g).norm() / (g.norm() + 1e-12)) for n, g in ref[3].items())
     # 8 channels: bf16 operand noise is larger than at production widths
     assert errs[-1] < 8e-2 and errs[len(errs) // 2] < 2e-2, errs[-5:]
+
+
+def test_streamed_inference_on_the_kernel_path(monkeypatch):
+    """Chunked, gradient-free inference on the kernel path (edge stream overwritten in place,
+    rotations computed per chunk, bf16 stream) and the streamed block-sparse Hamiltonian shard,
+    against the unchunked PyTorch path."""
+    from maloq_b200.parallel.infer import hamiltonian_shard
+
+    bb, hd, b, lab = _model(2)
+    tbl = lab.table
+    b.edge_pair_type = torch.as_tensor(tbl.pair_type(b.src_z.numpy(), b.dst_z.numpy()))
+    b.node_pair_type = torch.as_tensor(tbl.pair_type(b.atomic_numbers.numpy(), b.atomic_numbers.numpy()))
+    with torch.no_grad():
+        emb = bb(b)
+        no, eo = hd(emb, b)
+        ref_data, ref_ptr = hamiltonian_shard(hd, emb, b, lab)
+    bb2, hd2, _, _ = _model(2, edge_chunk=30)
+    bb2.load_state_dict(bb.state_dict())
+    hd2.load_state_dict(hd.state_dict())
+    ext = use_cpu_extension(monkeypatch)
+    with torch.no_grad():
+        g = bb2.build_graph(b)
+        assert g.rot is None and len(g.chunks) > 1
+        emb2 = bb2(b)
+        no2, eo2 = hd2(emb2, b)
+        data, ptr = hamiltonian_shard(hd2, emb2, b, lab)
+    assert ext.calls.get("gather_rotate_fwd", 0) > 0 and ext.calls.get("basis_rows", 0) > 0
+    rel = lambda a, r: ((a.double() - r.double()).norm() / r.double().norm()).item()
+    assert rel(no2, no) < 2e-2 and rel(eo2, eo) < 3e-2
+    assert torch.equal(ptr, ref_ptr) and rel(data, ref_data) < 3e-2
