@@ -160,8 +160,9 @@ class EdgeInputs:
     def __getitem__(self, sl):
         e0, e1 = sl.start or 0, sl.stop
         b, bb = self.batch, self.bb
-        return torch.cat([bb.source_embedding(b.src_z[e0:e1]), bb.distance_expansion(self.dist[e0:e1]),
-                          bb.target_embedding(b.dst_z[e0:e1])], dim=1)
+        return torch.cat([ops.embedding(b.src_z[e0:e1], bb.source_embedding.weight),
+                          bb.distance_expansion(self.dist[e0:e1]),
+                          ops.embedding(b.dst_z[e0:e1], bb.target_embedding.weight)], dim=1)
 
     def full(self):
         return self[0:self.dist.shape[0]]
@@ -357,15 +358,17 @@ class eSEN_Backbone(nn.Module):
         z_local = z if getattr(batch, "local_node_ids", None) is None else z[batch.local_node_ids]
         charge = batch.atom_charge + self.abs_max_charge
         spin = batch.atom_spin
-        emb = torch.cat([self.sphere_embedding(z_local), self.charge_embedding(charge), self.spin_embedding(spin)], -1)
+        emb = torch.cat([ops.embedding(z_local, self.sphere_embedding.weight),
+                         ops.embedding(charge, self.charge_embedding.weight),
+                         ops.embedding(spin, self.spin_embedding.weight)], -1)
         l0 = ops.linear(emb, self.scalar_node_embedding.weight, self.scalar_node_embedding.bias)
         x_node = l0.new_zeros(n_local, self.sph_feature_size, self.sphere_channels)
         x_node[:, 0] = l0
         if graph.chunks is None:
             gauss = self.distance_expansion(dist)
             # the radial MLPs' input: read by every block's radial MLP, only through GEMMs
-            x_edge = ops.gemm_operand(torch.cat([self.source_embedding(batch.src_z), gauss,
-                                                 self.target_embedding(batch.dst_z)], dim=1))
+            x_edge = ops.gemm_operand(torch.cat([ops.embedding(batch.src_z, self.source_embedding.weight), gauss,
+                                                 ops.embedding(batch.dst_z, self.target_embedding.weight)], dim=1))
             x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
             x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
         else:

@@ -10,7 +10,7 @@ from . import reference as _ref
 from . import native as _native
 
 __all__ = [
-    "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
+    "embedding", "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
     "rotate_back_m0_scatter", "rotate_back_m0", "fock_loss",
 ]
 
@@ -37,6 +37,14 @@ def _cuda(*tensors) -> bool:
         if t is not None and hasattr(t, "is_cuda"):
             return bool(t.is_cuda)
     return False
+
+
+def embedding(idx, weight):
+    """weight[idx] (an ``nn.Embedding`` lookup); on the kernel path its backward needs no
+    host synchronisation."""
+    if _cuda(weight):
+        return _native.embedding(idx, weight)
+    return weight.index_select(0, idx)
 
 
 def gemm_operand(x):

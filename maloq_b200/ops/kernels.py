@@ -136,6 +136,30 @@ class _Linear(torch.autograd.Function):
         return gx, gw, gb, None
 
 
+class _Embedding(torch.autograd.Function):
+    """Embedding rows with a backward that needs no device-to-host read: the weight gradient is
+    one_hot(idx)^T @ g, one dense GEMM (deterministic), instead of the sort-and-segment
+    reduction of the stock backward, which reads a segment count back to the host for large
+    index counts (one synchronisation per call)."""
+
+    @staticmethod
+    def forward(ctx, idx, weight):
+        ctx.save_for_backward(idx)
+        ctx.n_rows = weight.shape[0]
+        return weight.index_select(0, idx)
+
+    @staticmethod
+    def backward(ctx, g):
+        (idx,) = ctx.saved_tensors
+        onehot = (idx.unsqueeze(1) == torch.arange(ctx.n_rows, device=idx.device)).to(g.dtype)
+        return None, onehot.t() @ g
+
+
+@register("embedding")
+def embedding(idx, weight):
+    return _Embedding.apply(idx, weight)
+
+
 @register("linear")
 def linear(x, weight, bias=None, act=None, out_dtype=None):
     y = _Linear.apply(x, weight, bias, out_dtype or torch.float32)
