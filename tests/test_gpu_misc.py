@@ -85,6 +85,25 @@ def test_masked_peer_barrier_waits_only_for_members(cuda_device):
     assert kernels.error_status() == 0
 
 
+def test_peer_barrier_rejects_a_stale_epoch(cuda_device):
+    """A peer whose flag still holds an older epoch has not arrived: the wait for epoch 6 runs
+    out while the peer shows 5; once the peer shows 6 (or a later epoch) the barrier passes."""
+    from maloq_b200.ops import kernels
+
+    lib = kernels.lib()
+    kernels.error_status(True)
+    pads = torch.zeros(2, 8, dtype=torch.int32, device=cuda_device)
+    ptrs = torch.tensor([pads[0].data_ptr(), pads[1].data_ptr()], dtype=torch.int64, device=cuda_device)
+    pads[0, 1] = 5  # rank 1's flag in rank 0's pad: a previous step's epoch
+    lib.peer_barrier(ptrs.data_ptr(), 0, 2, 6, 0, 2000)
+    torch.cuda.synchronize()
+    assert kernels.error_status(True) == 4
+    pads[0, 1] = 7
+    lib.peer_barrier(ptrs.data_ptr(), 0, 2, 6, 0, 2000)
+    torch.cuda.synchronize()
+    assert kernels.error_status(True) == 0
+
+
 def test_peer_timeout_raises_comm_timeout_on_the_host(cuda_device):
     """The host-side status check turns the recorded peer timeout into CommTimeoutError (what
     the trainer raises after a step) and clears the word."""
