@@ -224,12 +224,30 @@ class SplitTrainer:
     # ------------------------------------------------------------------ eval / infer
     @torch.no_grad()
     def evaluate(self, loss_fxn, device, loader, labeler, output_folder="outputs", samples=None, scale_shift=None,
-                 dump_embeddings=False, compute_total_energy=False, basis_name=None, xc="b3lyp", **unused):
+                 dump_embeddings=False, compute_total_energy=False, basis_name=None, xc="b3lyp",
+                 hf_basis_file=None, **unused):
         """Per structure: Hamiltonian MAE, orbital-energy MAE (generalised with the overlap
         when the sample carries one, canonical orthogonalisation), HOMO-LUMO gap and band
         energy errors (closed shell, all-electron count), written to
-        ``model_fock_eval_{rank}.txt`` (reference ``splittrainer.py:378-822``)."""
+        ``model_fock_eval_{rank}.txt`` (reference ``splittrainer.py:378-822``).
+
+        ``hf_basis_file`` (a Gaussian94 basis file whose shells match the labels' basis) adds
+        ``HF_Energy_Error``: the difference of the Hartree-Fock energy functionals
+        E = 1/2 Tr[P (H + F)] + E_nn of the predicted and target Fock matrices, with this
+        package's own one-electron integrals (no PySCF; for Kohn-Sham targets the XC correction
+        is not included)."""
         from ..data.batch import collate
+
+        hf_basis = None
+        if hf_basis_file:
+            from ..eval.integrals import parse_gaussian94
+
+            with open(hf_basis_file) as fh:
+                hf_basis = parse_gaussian94(fh.read())
+            for zz, ls in labeler.orbital_basis.items():
+                got = [l for l, *_ in hf_basis.get(zz, [])]
+                if got != [l % 10 for l in ls]:
+                    raise ValueError(f"hf_basis_file: element {zz} has shells {got}, the labels' basis {ls}")
 
         mol_of = None
         if compute_total_energy:
@@ -267,7 +285,7 @@ class SplitTrainer:
                 continue
             no, eo = out
             rows.append((k,) + self._fock_metrics(s, no[0], eo[0], b.node_y[0], b.y[0], labeler, scale_shift,
-                                                   compute_total_energy, mol_of, xc))
+                                                   compute_total_energy, mol_of, xc, hf_basis))
         os.makedirs(output_folder, exist_ok=True)
         if rows and len(rows[0]) == 4:
             with open(os.path.join(output_folder, f"model_energy_eval_{rank}.txt"), "w") as f:
@@ -277,13 +295,14 @@ class SplitTrainer:
             return rows
         with open(os.path.join(output_folder, f"model_fock_eval_{rank}.txt"), "w") as f:
             f.write("Index\tTotal_MAE\tEigenvalue_MAE\tGap_Error\tBand_Energy_Error\t"
-                    + ("Total_Energy_Error\t" if compute_total_energy else "") + "Num_Atoms\n")
+                    + ("Total_Energy_Error\t" if compute_total_energy else "")
+                    + ("HF_Energy_Error\t" if hf_basis is not None else "") + "Num_Atoms\n")
             for r in rows:
                 f.write("\t".join(str(x) for x in r) + "\n")
         return rows
 
     @staticmethod
-    def _fock_metrics(s, no, eo, ty, y, labeler, scale_shift, compute_total_energy, mol_of, xc):
+    def _fock_metrics(s, no, eo, ty, y, labeler, scale_shift, compute_total_energy, mol_of, xc, hf_basis=None):
         """Errors of one structure's predicted labels (no, eo) against its targets (ty, y):
         Hamiltonian MAE, orbital-energy MAE, gap and band-energy errors (and total energy)."""
         from ..eval import electronic
@@ -310,6 +329,12 @@ class SplitTrainer:
                 mol = mol_of(s)
                 te = abs(electronic.total_energy(mol, Hp, S, xc) - electronic.total_energy(mol, Ht, S, xc))
             row.append(te)
+        if hf_basis is not None:
+            from ..eval.integrals import hf_energy
+
+            ep_ = hf_energy(Hp, s.z, s.pos, hf_basis, n_electrons=ne)["total"]
+            et_ = hf_energy(0.5 * (Ht + Ht.T), s.z, s.pos, hf_basis, n_electrons=ne)["total"]
+            row.append(abs(ep_ - et_))
         return tuple(row + [s.num_nodes])
 
     @torch.no_grad()

@@ -477,7 +477,8 @@ class TrainingWorkflow:
                                         scale_shift=getattr(self, "scale_shift", None),
                                         dump_embeddings=c.get("dump_embeddings", False),
                                         compute_total_energy=c.get("compute_total_energy", False),
-                                        basis_name=c.get("pyscf_basis"), xc=c.get("functional", "b3lyp"))
+                                        basis_name=c.get("pyscf_basis"), xc=c.get("functional", "b3lyp"),
+                                        hf_basis_file=c.get("hf_basis_file"))
             if c["distribute_graphs"] and getattr(self, "partition_sample", None) is None:
                 # molecule batches split over ranks: one block-sparse shard folder per batch
                 from ..parallel.infer import write_partition_hamiltonian

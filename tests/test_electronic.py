@@ -96,3 +96,32 @@ def test_eval_total_energy_column_without_pyscf(tmp_path):
                                                    compute_total_energy=True)).run()
     header = (tmp_path / "model_fock_eval_0.txt").read_text().splitlines()[0].split("\t")
     assert "Total_Energy_Error" in header and len(rows[0]) == len(header)
+
+
+def test_eval_hf_energy_column_with_own_integrals(tmp_path):
+    """hf_basis_file: the evaluation adds the Hartree-Fock energy-functional error of the
+    predicted Fock matrices, with this package's one-electron integrals (no PySCF)."""
+    import numpy as np
+
+    from maloq.train_utils import training_workflow
+
+    def shell(kind, exps):
+        return [f"{kind}   {len(exps)}   1.00"] + [f"  {e:.6f}   {1.0 / len(exps):.6f}" for e in exps]
+
+    lines = []
+    for sym, shells in (("H", ["S", "S", "P"]), ("C", ["S", "S", "S", "P", "P", "D"]), ("N", ["S", "S", "S", "P", "P", "D"]),
+                        ("O", ["S", "S", "S", "P", "P", "D"])):
+        lines.append(f"{sym}     0")
+        for i, k in enumerate(shells):
+            lines += shell(k, [6.0 / (i + 1), 1.2 / (i + 1)])
+        lines.append("****")
+    (tmp_path / "basis.g94").write_text("\n".join(lines) + "\n")
+    cfg = dict(dataset_name="synthetic_small", num_structures=6, batch_size=3, num_epochs=1, l_embedding_dim=8,
+               num_mp_layers=1, num_distance_basis=8, rcut_orbitals=2.5, rcut_gaussian=5.0, mmax=2,
+               output_folder=str(tmp_path), device="cpu", log_every=0)
+    training_workflow.TrainingWorkflow(cfg).run()
+    rows = training_workflow.TrainingWorkflow(dict(cfg, train_or_eval="eval", restart_backbone=True, restart_head=True,
+                                                   hf_basis_file=str(tmp_path / "basis.g94"))).run()
+    header = (tmp_path / "model_fock_eval_0.txt").read_text().splitlines()[0].split("\t")
+    assert header[-2] == "HF_Energy_Error" and len(rows[0]) == len(header)
+    assert all(np.isfinite(r[-2]) and r[-2] >= 0 for r in rows)
