@@ -260,3 +260,75 @@ def hf_energy(F, z, pos, basis, n_electrons=None, units="angstrom", tol=1e-6):
     e_nn = nuclear_repulsion(z, pos, units)
     return {"total": e_el + e_nn, "electronic": e_el, "nuclear_repulsion": e_nn,
             "one_electron": float(np.sum(P * H)), "orbital_energies": e, "density": P, "overlap": S}
+
+
+# ------------------------------------------------------------------ orbitals on a grid, files
+def ao_values(points, z, pos, basis, units="angstrom"):
+    """Values [n_points, n_orb] of the contracted orbitals (normalised as in
+    :func:`one_electron_integrals`) at ``points`` (same units as ``pos``)."""
+    f = BOHR_PER_ANGSTROM if units == "angstrom" else 1.0
+    pts = np.asarray(points, dtype=np.float64) * f
+    shells = _shells(np.asarray(z), np.asarray(pos, dtype=np.float64) * f, basis)
+    cols = []
+    for l, exps, coefs, A in shells:
+        d = pts - A
+        r2 = np.sum(d * d, axis=1)
+        radial = np.exp(-r2[:, None] * exps[None, :]) @ coefs
+        cart = np.stack([d[:, 0] ** a * d[:, 1] ** b * d[:, 2] ** c for a, b, c in _cart_components(l)], axis=1)
+        cols.append((cart @ solid_harmonic_coefficients(l).T) * radial[:, None])
+    vals = np.concatenate(cols, axis=1)
+    # the normalisation of the integrals: divide by the norms of the unnormalised functions
+    return vals / _raw_norms(z, pos, basis, units)[None, :]
+
+
+def _raw_norms(z, pos, basis, units):
+    f = BOHR_PER_ANGSTROM if units == "angstrom" else 1.0
+    shells = _shells(np.asarray(z), np.asarray(pos, dtype=np.float64) * f, basis)
+    out = []
+    for l, e, c, A in shells:
+        s, _, _ = _shell_pair(l, e, c, A, l, e, c, A, A[None, :], np.zeros(1))
+        C = solid_harmonic_coefficients(l)
+        out.append(np.sqrt(np.diag(C @ s @ C.T)))
+    return np.concatenate(out)
+
+
+def write_density_cube(path, z, pos, P, basis, spacing=0.4, margin=3.0):
+    """Electron density rho(r) = sum_ij P_ij phi_i(r) phi_j(r) on a box around the molecule
+    (``spacing`` and ``margin`` in Angstrom) as a Gaussian cube file (bohr units inside)."""
+    pos = np.asarray(pos, dtype=np.float64)
+    lo = pos.min(axis=0) - margin
+    n = np.ceil((pos.max(axis=0) + margin - lo) / spacing).astype(int)
+    axes = [lo[k] + spacing * np.arange(n[k]) for k in range(3)]
+    X, Y, Z = np.meshgrid(*axes, indexing="ij")
+    pts = np.stack([X.ravel(), Y.ravel(), Z.ravel()], axis=1)
+    rho = np.empty(len(pts))
+    for s0 in range(0, len(pts), 20000):
+        a = ao_values(pts[s0:s0 + 20000], z, pos, basis)
+        rho[s0:s0 + 20000] = np.einsum("pi,ij,pj->p", a, P, a)
+    rho = rho.reshape(tuple(n))  # electrons per bohr^3 (the orbitals are functions of bohr coordinates)
+    b = BOHR_PER_ANGSTROM
+    with open(path, "w") as fh:
+        fh.write("electron density\nwritten by maloq_b200\n")
+        fh.write(f"{len(z):5d} {lo[0] * b:12.6f} {lo[1] * b:12.6f} {lo[2] * b:12.6f}\n")
+        for k in range(3):
+            v = [0.0, 0.0, 0.0]
+            v[k] = spacing * b
+            fh.write(f"{n[k]:5d} {v[0]:12.6f} {v[1]:12.6f} {v[2]:12.6f}\n")
+        for zz, p in zip(z, pos):
+            fh.write(f"{int(zz):5d} {float(zz):12.6f} {p[0] * b:12.6f} {p[1] * b:12.6f} {p[2] * b:12.6f}\n")
+        flat = rho.reshape(n[0] * n[1], n[2])
+        for row in flat:
+            for s0 in range(0, len(row), 6):
+                fh.write(" ".join(f"{v:13.5e}" for v in row[s0:s0 + 6]) + "\n")
+    return path
+
+
+def write_xyz(path, z, pos, comment="written by maloq_b200"):
+    from ..data.readers import SYMBOL_TO_Z
+
+    sym = {v: k for k, v in SYMBOL_TO_Z.items()}
+    with open(path, "w") as fh:
+        fh.write(f"{len(z)}\n{comment}\n")
+        for zz, p in zip(z, np.asarray(pos, dtype=np.float64)):
+            fh.write(f"{sym[int(zz)]:2s} {p[0]:20.10f} {p[1]:20.10f} {p[2]:20.10f}\n")
+    return path

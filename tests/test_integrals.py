@@ -181,3 +181,30 @@ SP   2   1.00
     assert [l for l, *_ in b[8]] == [0, 0, 1]
     assert np.isclose(b[8][0][1][0], 130.70932)
     assert np.allclose(b[8][2][2], [0.15591627, 0.60768372])
+
+
+def test_orbitals_on_a_grid_density_cube_and_xyz(tmp_path):
+    """Orbital values reproduce the overlap matrix by quadrature; the density of P integrates to
+    Tr[P S] electrons; the cube and xyz files have the standard layouts."""
+    basis = _toy_basis()
+    z = [8, 1, 1]
+    pos = np.array([[0.0, 0.1, 0.0], [0.76, -0.5, 0.1], [-0.7, -0.45, -0.2]])  # Angstrom
+    S, _, _ = I.one_electron_integrals(z, pos, basis)
+    g = np.linspace(-5.0, 5.0, 81)  # Angstrom
+    h = (g[1] - g[0]) * I.BOHR_PER_ANGSTROM
+    X, Y, Z = np.meshgrid(g, g, g, indexing="ij")
+    a = I.ao_values(np.stack([X.ravel(), Y.ravel(), Z.ravel()], 1), z, pos, basis)
+    Sq = a.T @ a * h ** 3
+    assert np.abs(Sq - S).max() < 2e-3
+    rng = np.random.default_rng(0)
+    C = rng.normal(size=(S.shape[0], 5))
+    P = C @ C.T
+    path = I.write_density_cube(str(tmp_path / "rho.cube"), z, pos, P, basis, spacing=0.15, margin=4.0)
+    lines = open(path).read().splitlines()
+    n = [int(lines[3 + k].split()[0]) for k in range(3)]
+    vals = np.array([float(v) for ln in lines[6 + len(z):] for v in ln.split()])
+    assert vals.size == n[0] * n[1] * n[2]
+    dv = (0.15 * I.BOHR_PER_ANGSTROM) ** 3
+    assert abs(vals.sum() * dv - np.sum(P * S)) < 2e-2 * np.sum(P * S)
+    xyz = open(I.write_xyz(str(tmp_path / "m.xyz"), z, pos)).read().splitlines()
+    assert xyz[0] == "3" and xyz[2].split()[0] == "O" and float(xyz[3].split()[1]) == 0.76
