@@ -319,3 +319,13 @@ def test_streamed_inference_on_the_kernel_path(monkeypatch):
     rel = lambda a, r: ((a.double() - r.double()).norm() / r.double().norm()).item()
     assert rel(no2, no) < 2e-2 and rel(eo2, eo) < 3e-2
     assert torch.equal(ptr, ref_ptr) and rel(data, ref_data) < 3e-2
+
+
+def test_driver_smoke_on_the_cpu_stand_in(monkeypatch):
+    """The driver's smoke() (tiny flagship forward + backward: teacher targets, label rows,
+    model, fused loss) on the kernel path through the CPU stand-in."""
+    import __graft_entry__ as entry
+
+    ext = use_cpu_extension(monkeypatch)
+    entry.smoke("cpu")
+    assert {"gather_rotate_fwd", "head_gate_fwd", "basis_rows", "fock_loss_stats", "gather_rotate_bwd"} <= set(ext.calls)
