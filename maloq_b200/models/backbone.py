@@ -365,10 +365,15 @@ class eSEN_Backbone(nn.Module):
         x_node = l0.new_zeros(n_local, self.sph_feature_size, self.sphere_channels)
         x_node[:, 0] = l0
         if graph.chunks is None:
-            gauss = self.distance_expansion(dist)
             # the radial MLPs' input: read by every block's radial MLP, only through GEMMs
-            x_edge = ops.gemm_operand(torch.cat([ops.embedding(batch.src_z, self.source_embedding.weight), gauss,
-                                                 ops.embedding(batch.dst_z, self.target_embedding.weight)], dim=1))
+            if isinstance(self.distance_expansion, GaussianSmearing):
+                de = self.distance_expansion
+                x_edge = ops.edge_inputs(batch.src_z, batch.dst_z, batch.edge_attr, self.source_embedding.weight,
+                                         self.target_embedding.weight, de.offset, de.coeff)
+            else:
+                gauss = self.distance_expansion(dist)
+                x_edge = ops.gemm_operand(torch.cat([ops.embedding(batch.src_z, self.source_embedding.weight), gauss,
+                                                     ops.embedding(batch.dst_z, self.target_embedding.weight)], dim=1))
             x_node = self.edge_degree_embedding(x_node, x_edge, graph, "node")
             x_edge_emb = self.edge_degree_embedding(x_node, x_edge, graph, "edge") if self.include_edges else None
         else:

@@ -10,7 +10,7 @@ from . import reference as _ref
 from . import native as _native
 
 __all__ = [
-    "embedding", "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
+    "edge_inputs", "embedding", "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
     "rotate_back_m0_scatter", "rotate_back_m0", "fock_loss",
 ]
 
@@ -37,6 +37,17 @@ def _cuda(*tensors) -> bool:
         if t is not None and hasattr(t, "is_cuda"):
             return bool(t.is_cuda)
     return False
+
+
+def edge_inputs(src_z, dst_z, edge_attr, src_weight, dst_weight, offset, coeff):
+    """Radial-MLP input rows [src_weight[src_z] | exp(coeff (d - offset)^2) | dst_weight[dst_z]]
+    with d = edge_attr[:, 0]: one kernel writing the bf16 GEMM operand on the kernel path."""
+    if _cuda(src_weight):
+        return _native.edge_inputs(src_z, dst_z, edge_attr, src_weight, dst_weight, offset, coeff)
+    import torch
+
+    g = torch.exp(coeff * (edge_attr[:, 0].view(-1, 1) - offset.view(1, -1)) ** 2)
+    return torch.cat([src_weight.index_select(0, src_z), g, dst_weight.index_select(0, dst_z)], dim=1)
 
 
 def embedding(idx, weight):

@@ -482,6 +482,27 @@ void radius_graph_pass(at::Tensor pos, std::vector<double> grid, std::vector<int
   check(maloq::radius_graph_pass(a, fill, stream()));
 }
 
+// OUT [E, 2C + NB] bf16: [src_table[src_z] | exp(coeff (d - offset)^2) | dst_table[dst_z]], d = column 0
+// of the edge attributes [E, A]
+void edge_inputs(at::Tensor src_z, at::Tensor dst_z, at::Tensor edge_attr, at::Tensor src_table, at::Tensor dst_table,
+                 at::Tensor offset, double coeff, at::Tensor OUT) {
+  chk(src_z, at::kLong, "src_z");
+  chk(dst_z, at::kLong, "dst_z");
+  chk(edge_attr, at::kFloat, "edge_attr");
+  chk(src_table, at::kFloat, "src_table");
+  chk(dst_table, at::kFloat, "dst_table");
+  chk(offset, at::kFloat, "offset");
+  chk(OUT, at::kBFloat16, "OUT");
+  const int64_t E = src_z.numel(), C = src_table.size(1), NB = offset.numel();
+  TORCH_CHECK(dst_z.numel() == E && edge_attr.dim() == 2 && edge_attr.size(0) == E, "edge_inputs: edge counts");
+  TORCH_CHECK(dst_table.sizes() == src_table.sizes(), "edge_inputs: tables of one shape");
+  TORCH_CHECK(OUT.dim() == 2 && OUT.size(0) == E && OUT.size(1) == 2 * C + NB, "edge_inputs: OUT [E, 2C + NB]");
+  const at::cuda::CUDAGuard guard(OUT.device());
+  check(maloq::edge_inputs(ll(src_z), ll(dst_z), edge_attr.data_ptr<float>(), edge_attr.size(1),
+                           src_table.data_ptr<float>(), dst_table.data_ptr<float>(), src_table.size(0),
+                           offset.data_ptr<float>(), (float)coeff, bf(OUT), E, (int)C, (int)NB, stream()));
+}
+
 int64_t fock_loss_grid(int64_t n) { return maloq::fock_loss_grid(n); }
 
 void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, at::Tensor part) {
@@ -536,6 +557,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gate_l_bwd", &gate_l_bwd);
   m.def("head_gate_fwd", &head_gate_fwd);
   m.def("head_gate_bwd", &head_gate_bwd);
+  m.def("edge_inputs", &edge_inputs);
   m.def("peer_barrier", &peer_barrier);
   m.def("peer_barrier_mask", &peer_barrier_mask);
   m.def("allreduce_p2p", &allreduce_p2p);

@@ -12,6 +12,7 @@
 //   statistics, read from device memory (no host round trip between forward and backward).
 #include "common.cuh"
 #include "misc.h"
+#include "edge_inputs.cuh"
 
 namespace maloq {
 
@@ -188,6 +189,18 @@ const char* fock_loss_grad(const float* O, const float* Tt, const long long* pt,
   if (rows == 0) return nullptr;
   fock_loss_grad_kernel<<<fock_loss_grid(rows * D), 256, 0, st>>>(O, Tt, pt, mask, D, rows, gstat, G, n_pt);
   return misc_err();
+}
+
+const char* edge_inputs(const long long* src_z, const long long* dst_z, const float* D, long long ld_d,
+                        const float* src_table, const float* dst_table, long long n_types, const float* offset,
+                        float coeff, __nv_bfloat16* OUT, long long E, int C, int NB, cudaStream_t st) {
+  if (E == 0) return nullptr;
+  const long long total = E * (2LL * C + NB);
+  const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 32);
+  edge_inputs_kernel<<<grid, 256, 0, st>>>(src_z, dst_z, D, ld_d, src_table, dst_table, n_types, offset, coeff, OUT,
+                                           E, C, NB);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
 }
 
 }  // namespace maloq

@@ -155,6 +155,13 @@ class _Embedding(torch.autograd.Function):
         return None, onehot.t() @ g
 
 
+@register("edge_inputs")
+def edge_inputs(src_z, dst_z, edge_attr, src_w, dst_w, offset, coeff):
+    from . import misc_native
+
+    return misc_native.edge_inputs(src_z, dst_z, edge_attr, src_w, dst_w, offset, coeff)
+
+
 @register("embedding")
 def embedding(idx, weight):
     return _Embedding.apply(idx, weight)

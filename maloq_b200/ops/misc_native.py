@@ -80,3 +80,39 @@ def fock_loss(node_out, edge_out, node_t, edge_t, mask_table, node_pt, edge_pt, 
     ct = cnt_n + cnt_e
     lt = f((sse_n + sse_e) / ct, (sae_n + sae_e) / ct)
     return ln, le, lt
+
+
+class _EdgeInputs(torch.autograd.Function):
+    """Radial-MLP input rows [E, 2C + NB] bf16 in one kernel: source-element embedding,
+    Gaussian expansion of the edge length, target-element embedding.  Backward: the two
+    embedding tables' gradients as one-hot GEMMs (the Gaussian part has no parameters)."""
+
+    @staticmethod
+    def forward(ctx, src_z, dst_z, edge_attr, src_w, dst_w, offset, coeff):
+        E, C, NB = src_z.shape[0], src_w.shape[1], offset.numel()
+        out = torch.empty(E, 2 * C + NB, device=src_w.device, dtype=torch.bfloat16)
+        _lib().edge_inputs(src_z.contiguous(), dst_z.contiguous(), edge_attr.contiguous().float(),
+                           src_w.detach().contiguous().float(), dst_w.detach().contiguous().float(),
+                           offset.contiguous().float(), float(coeff), out)
+        count_launches(1)
+        ctx.save_for_backward(src_z, dst_z)
+        ctx.dims = (C, NB, src_w.shape[0], dst_w.shape[0])
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        src_z, dst_z = ctx.saved_tensors
+        C, NB, ns, nd = ctx.dims
+        g = g.float()
+        gs = gd = None
+        if ctx.needs_input_grad[3]:
+            oh = (src_z.unsqueeze(1) == torch.arange(ns, device=g.device)).to(g.dtype)
+            gs = oh.t() @ g[:, :C]
+        if ctx.needs_input_grad[4]:
+            oh = (dst_z.unsqueeze(1) == torch.arange(nd, device=g.device)).to(g.dtype)
+            gd = oh.t() @ g[:, C + NB:]
+        return None, None, None, gs, gd, None, None
+
+
+def edge_inputs(src_z, dst_z, edge_attr, src_w, dst_w, offset, coeff):
+    return _EdgeInputs.apply(src_z, dst_z, edge_attr, src_w, dst_w, offset, coeff)

@@ -271,6 +271,12 @@ class CpuExtension:
         DX.copy_(gx)
         DSV.copy_(gs)
 
+    def edge_inputs(self, src_z, dst_z, edge_attr, src_table, dst_table, offset, coeff, OUT):
+        C, NB = src_table.shape[1], offset.numel()
+        assert OUT.dtype == torch.bfloat16 and tuple(OUT.shape) == (src_z.numel(), 2 * C + NB)
+        g = torch.exp(coeff * (edge_attr[:, 0:1] - offset.view(1, -1)) ** 2)
+        OUT.copy_(torch.cat([src_table[src_z], g, dst_table[dst_z]], 1).to(torch.bfloat16))
+
     # ------------------------------------------------------------------ label rows
     def basis_rows(self, inp, out, ptr, pt, pos, meta, coef, d_in, rows, gather, scatter):
         """out[r, u] = sum_{j < n_u} in[r, s_u + j] * coef[c_u + j n_u], meta[u] = (s_u, n_u, c_u, 0);

@@ -136,3 +136,31 @@ def test_edge_rotation_rows_orthonormal_and_empty(cuda_device):
     assert (rot @ rot.transpose(1, 2) - eye).abs().max().item() < 1e-5
     empty = misc_native.edge_rotation(v[:0], 6, 2, Js, mp)
     assert empty.shape == (0, rot.shape[1], rot.shape[2])
+
+
+def test_edge_inputs_kernel_and_gradients(cuda_device):
+    """Radial-MLP input rows in one kernel (bf16) vs embedding lookups + Gaussian expansion +
+    concatenation in fp32; the embedding-table gradients (one-hot GEMMs) vs autograd."""
+    from maloq_b200.ops import misc_native
+
+    torch.manual_seed(0)
+    E, V, C, NB = 5000, 100, 128, 128
+    src_z = torch.randint(1, 20, (E,), device=cuda_device)
+    dst_z = torch.randint(1, 20, (E,), device=cuda_device)
+    attr = torch.rand(E, 4, device=cuda_device) * 6
+    sw = torch.randn(V, C, device=cuda_device, requires_grad=True)
+    dw = torch.randn(V, C, device=cuda_device, requires_grad=True)
+    off = torch.linspace(0, 6, NB, device=cuda_device)
+    coeff = -0.5 / float(off[1] - off[0]) ** 2
+    out = misc_native.edge_inputs(src_z, dst_z, attr, sw, dw, off, coeff)
+    ref = torch.cat([sw[src_z], torch.exp(coeff * (attr[:, :1] - off.view(1, -1)) ** 2), dw[dst_z]], 1)
+    assert out.dtype == torch.bfloat16
+    assert ((out.float() - ref).abs() <= 2 ** -8 * ref.abs() + 1e-30).all()
+    g = torch.randn_like(ref)
+    ga = torch.autograd.grad((out.float() * g).sum(), [sw, dw])
+    gr = torch.autograd.grad((ref * g).sum(), [sw, dw])
+    for a, b in zip(ga, gr):
+        assert ((a - b).norm() / b.norm()).item() < 1e-2
+    from maloq_b200.ops import kernels
+
+    assert kernels.error_status() == 0

@@ -174,3 +174,37 @@ def test_weight_cache_entries_die_with_their_parameter():
     del p
     gc.collect()
     assert key not in W._CACHE
+
+
+@pytest.mark.parametrize("E,C,NB,grid", [(37, 16, 8, 1), (200, 128, 128, 7), (5, 8, 3, 64)])
+def test_edge_inputs_kernel_on_emulated_grid(tmp_path, E, C, NB, grid):
+    """The radial-input kernel (embedding rows around the Gaussian expansion of the edge length,
+    bf16) from its own source on an emulated grid against PyTorch; an element index outside the
+    table is zeroed and reported."""
+    cxx = shutil.which("g++")
+    if cxx is None:
+        pytest.skip("needs g++")
+    so = str(tmp_path / "ei.so")
+    subprocess.run([cxx, "-O1", "-std=c++17", "-shared", "-fPIC", "-I", CSRC, "-I", CUDA_INC,
+                    os.path.join(HERE, "csrc", "edge_inputs_emu.cpp"), "-o", so], check=True)
+    lib = ctypes.CDLL(so)
+    torch.manual_seed(E)
+    V = 12
+    src_z, dst_z = torch.randint(0, V, (E,)), torch.randint(0, V, (E,))
+    attr = torch.rand(E, 4) * 6
+    st, dt = torch.randn(V, C), torch.randn(V, C)
+    off = torch.linspace(0, 6, NB)
+    coeff = -0.5 / float(off[1] - off[0]) ** 2 if NB > 1 else -1.0
+    out = torch.empty(E, 2 * C + NB, dtype=torch.bfloat16)
+    err = lib.emu_edge_inputs(_p(src_z), _p(dst_z), _p(attr), ctypes.c_longlong(4), _p(st), _p(dt),
+                              ctypes.c_longlong(V), _p(off), ctypes.c_float(coeff), _p(out), ctypes.c_longlong(E), C, NB,
+                              grid, 64)
+    assert err == 0
+    ref = torch.cat([st[src_z], torch.exp(coeff * (attr[:, :1] - off.view(1, -1)) ** 2), dt[dst_z]], 1)
+    np.testing.assert_allclose(out.float().numpy(), ref.numpy(), rtol=2 ** -8, atol=1e-30)
+    bad = src_z.clone()
+    bad[0] = V
+    err = lib.emu_edge_inputs(_p(bad), _p(dst_z), _p(attr), ctypes.c_longlong(4), _p(st), _p(dt),
+                              ctypes.c_longlong(V), _p(off), ctypes.c_float(coeff), _p(out), ctypes.c_longlong(E), C, NB,
+                              grid, 64)
+    assert err == 5 and torch.all(out[0, :C] == 0)
