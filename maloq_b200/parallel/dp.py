@@ -127,7 +127,7 @@ class GradSync:
             if not b.launched:
                 self._launch(b)
         if self.mode == "fused":
-            self._fused.wait(torch.cuda.current_stream(self.device))
+            self._fused.wait(torch.cuda.current_stream(self.device) if self.is_cuda else None)
             return
         for w, b in self.works:
             w.wait()

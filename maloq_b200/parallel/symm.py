@@ -75,16 +75,23 @@ class PeerAllReduce:
         assert off % 16 == 0 and 0 <= off and flat.is_contiguous(), "bucket must be an aligned view of the buffer"
         off //= 4
         n = flat.numel()
+        if self.device.type != "cuda":  # host memory (tests): in order, no streams
+            self._reduce(off, n, scale)
+            self.pending = "host"
+            return
         stream = side_stream or torch.cuda.current_stream(self.device)
         if side_stream is not None:
             side_stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):
-            self._barrier()
-            if self.mc:
-                self.lib.allreduce_multimem(self.mc, self.rank, self.world, off, n, scale)
-            else:
-                self.lib.allreduce_p2p(self.bufs_dev.data_ptr(), self.rank, self.world, off, n, scale)
+            self._reduce(off, n, scale)
             self.pending = stream
+
+    def _reduce(self, off, n, scale):
+        self._barrier()
+        if self.mc:
+            self.lib.allreduce_multimem(self.mc, self.rank, self.world, off, n, scale)
+        else:
+            self.lib.allreduce_p2p(self.bufs_dev.data_ptr(), self.rank, self.world, off, n, scale)
         count_launches(1)
 
     def wait(self, stream):
@@ -92,6 +99,10 @@ class PeerAllReduce:
         then ``stream`` waits for it."""
         side = getattr(self, "pending", None)
         if side is None:
+            return
+        if side == "host":
+            self._barrier()
+            self.pending = None
             return
         with torch.cuda.stream(side):
             self._barrier()

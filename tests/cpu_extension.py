@@ -11,8 +11,8 @@ With ``use_cpu_extension(monkeypatch)`` the op layer sends CPU tensors down the 
 the Python side of that path (views, strides, padding, buffer layouts, autograd functions,
 weight caches, label rows) runs on a machine without a GPU and can be compared with the PyTorch
 path.  The argument checks mirror the extension's (dtypes, shapes, contiguity, the 16-byte rule
-of the TMA descriptors).  Kernels that need peer memory (halo, fused all-reduce) and the device
-radius graph are not provided.
+of the TMA descriptors).  The peer-memory kernels (halo, barriers, fused all-reduce) work on
+the host shared memory of ``tests/fake_symm.py``; the device radius graph is not provided.
 """
 
 from __future__ import annotations
@@ -75,6 +75,10 @@ def _dst_of(dst_ptr, E):
 class CpuExtension:
     """The extension's bindings on CPU tensors (see the module docstring)."""
 
+    def __init__(self, barrier_timeout=30.0):
+        self._err = 0  # the device error word
+        self.barrier_timeout = barrier_timeout  # seconds, the bounded spin of the device barriers
+
     # ------------------------------------------------------------------ GEMM
     def gemm(self, As, Bs, Cs, biases, mn, act, alpha, splits, bn, resids=()):
         assert 1 <= len(As) <= 8 and len(Bs) == len(Cs) == len(As)
@@ -129,8 +133,16 @@ class CpuExtension:
             u = u * rad.view(E, ns, Cin)[:, torch.tensor(slots)]
         return u
 
+    def _extended(self, X, peers, halo_owner, halo_row, n_own):
+        """[owned rows | halo rows read from their owners' staging slots]."""
+        if peers == 0:
+            return X
+        SC = X[0].numel()
+        halo = self._fetch_rows(peers, halo_owner, halo_row, SC).view(-1, *X.shape[1:])
+        return torch.cat([X[:n_own], halo])
+
     def gather_rotate_fwd(self, L, MM, X, XE, src, dst, rot, rad, A, Cin, peers, halo_owner, halo_row, n_own):
-        assert peers == 0, "the CPU stand-in has no peer memory"
+        X = self._extended(X, peers, halo_owner, halo_row, n_own)
         _contig(X, XE, rot, A)
         assert X.dtype == rot.dtype == torch.float32 and A.dtype == torch.bfloat16
         E = src.shape[0]
@@ -140,7 +152,7 @@ class CpuExtension:
 
     def gather_rotate_bwd(self, L, MM, X, XE, rot, rad, dA, dst_ptr, src_perm, src_ptr, DX, DXE, DRAD, Cin,
                           peers=0, halo_owner=None, halo_row=None, n_own=0):
-        assert peers == 0, "the CPU stand-in has no peer memory"
+        X = self._extended(X, peers, halo_owner, halo_row, n_own)
         E = rot.shape[0]
         N = DX.shape[0]
         assert dst_ptr.numel() == N + 1 and src_ptr.numel() == N + 1
@@ -329,7 +341,86 @@ class CpuExtension:
         G.copy_(m * (gstat[0] * 2 * d + gstat[1] * torch.sign(d)))
 
     def error_status(self, clear):
-        return 0
+        e = self._err
+        if clear:
+            self._err = 0
+        return e
+
+    # ------------------------------------------------------------------ peer memory
+    # (addresses from tests/fake_symm.py: every rank's buffers mapped into this process)
+    @staticmethod
+    def _world():
+        import torch.distributed as dist
+
+        return dist.get_world_size() if dist.is_initialized() else 1
+
+    def _barrier(self, pads_dev, rank, world, epoch, slot_base, mask):
+        import time
+
+        from tests.fake_symm import PAD_WORDS, int32_at, table
+
+        pads = table(pads_dev, world)
+        members = [t for t in range(world) if mask == 0 or (mask >> t) & 1 or t == rank]
+        for t in members:
+            int32_at(pads[t], PAD_WORDS)[slot_base + rank] = epoch
+        mine = int32_at(pads[rank], PAD_WORDS)
+        deadline = time.time() + self.barrier_timeout
+        for t in members:
+            while int(mine[slot_base + t]) - epoch < 0:
+                if time.time() > deadline:
+                    self._err = self._err or 4  # a peer did not arrive
+                    return
+                time.sleep(2e-4)
+
+    def peer_barrier(self, pads_dev, rank, world, epoch, slot_base, spin_limit):
+        self._barrier(pads_dev, rank, world, epoch, slot_base, 0)
+
+    def peer_barrier_mask(self, pads_dev, rank, world, epoch, slot_base, spin_limit, mask):
+        assert mask != 0
+        self._barrier(pads_dev, rank, world, epoch, slot_base, mask & ((1 << 64) - 1))
+
+    def allreduce_p2p(self, bufs_dev, rank, world, off, n, scale):
+        """Rank r reduces chunk r over all ranks' buffers and writes it back into every one."""
+        from tests.fake_symm import floats_at, table
+
+        chunk = ((n + world - 1) // world + 3) // 4 * 4
+        c0, c1 = off + rank * chunk, min(off + (rank + 1) * chunk, off + n)
+        if c1 <= c0:
+            return
+        views = [floats_at(b + 4 * c0, c1 - c0) for b in table(bufs_dev, world)]
+        total = torch.stack([v.clone() for v in views]).sum(0) * scale
+        for v in views:
+            v.copy_(total)
+
+    def _fetch_rows(self, peers, halo_owner, halo_row, SC):
+        from tests.fake_symm import floats_at, table
+
+        bases = table(peers, self._world())
+        rows = [floats_at(bases[int(o)] + 4 * int(r) * SC, SC).clone() for o, r in zip(halo_owner, halo_row)]
+        return torch.stack(rows) if rows else torch.zeros(0, SC)
+
+    def halo_fetch(self, peers, halo_owner, halo_row, OUT):
+        SC = OUT[0].numel() if OUT.shape[0] else 0
+        if OUT.shape[0]:
+            OUT.view(OUT.shape[0], SC).copy_(self._fetch_rows(peers, halo_owner, halo_row, SC))
+
+    def halo_push(self, G, recv, halo_owner, recv_slot):
+        from tests.fake_symm import floats_at, table
+
+        SC = G.shape[1]
+        bases = table(recv, self._world())
+        for h, (o, sl) in enumerate(zip(halo_owner, recv_slot)):
+            floats_at(bases[int(o)] + 4 * int(sl) * SC, SC).copy_(G[h])
+
+    def node_reduce(self, DDST, dst_ptr, DSRC, src_perm, src_ptr, DX):
+        N = DX.shape[0]
+        out = torch.zeros(N, DX[0].numel() if N else 0)
+        if DDST is not None:
+            out.index_add_(0, _dst_of(dst_ptr, DDST.shape[0]), DDST.reshape(DDST.shape[0], -1))
+        if DSRC is not None:
+            rows = _dst_of(src_ptr, src_perm.numel())
+            out.index_add_(0, rows, DSRC.reshape(DSRC.shape[0], -1)[src_perm])
+        DX.view(N, -1).copy_(out)
 
     def bounds_checked(self):
         return False

@@ -57,3 +57,29 @@ def test_grad_sync_per_param_matches_average():
     for got_step, exp_step in zip(res[0], exp):
         for g, e in zip(got_step, exp_step):
             assert torch.allclose(torch.as_tensor(g), e, atol=1e-6)
+
+
+def _fused_worker(rank, world, folder):
+    from maloq_b200.ops import kernels
+    from tests import fake_symm
+    from tests.cpu_extension import CpuExtension
+
+    fake_symm.install(folder)
+    kernels._lib = CpuExtension()
+    out = _grad_sync_worker(rank, world, "fused")
+    return out, kernels._lib.error_status(True)
+
+
+def test_fused_allreduce_on_emulated_peer_memory(tmp_path):
+    """The fused gradient all-reduce (buckets in one symmetric buffer, a peer barrier per bucket,
+    each rank reducing its chunk over every rank's buffer and writing it back, a closing barrier)
+    on symmetric memory emulated in shared memory across gloo processes: every rank's gradients
+    equal the average over ranks, at 2 and 3 ranks (uneven chunks)."""
+    for world in (2, 3):
+        out = _dist_util.run(_fused_worker, world=world, args=(str(tmp_path / f"w{world}"),), timeout=300)
+        exp = _expected(world)
+        for r, (steps, err) in out.items():
+            assert err == 0
+            for got, ref in zip(steps, exp):
+                for a, b in zip(got, ref):
+                    assert torch.allclose(torch.as_tensor(a), b, atol=1e-5, rtol=1e-5)

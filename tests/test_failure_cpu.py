@@ -168,3 +168,34 @@ def test_crashed_rank_ends_the_job_and_resume_matches_uninterrupted_run(tmp_path
     assert len(h_res) == 3 and h_res == h_full
     for k in sd_full:
         assert (sd_full[k] == sd_res[k]).all(), k
+
+
+def _missing_peer_worker(rank, world, folder):
+    import torch.distributed as dist
+
+    from tests import fake_symm
+    from tests.cpu_extension import CpuExtension
+
+    symm = fake_symm.install(folder)
+    lib = CpuExtension(barrier_timeout=1.0)
+    buf = symm.empty(64)
+    hdl = symm.rendezvous(buf)
+    pads = torch.tensor(hdl.signal_pad_ptrs, dtype=torch.int64)
+    lib.peer_barrier(pads.data_ptr(), rank, world, 1, 0, 0)  # everyone arrives
+    first = lib.error_status(True)
+    if rank == 1:  # rank 1 leaves between steps: it never reaches the second barrier
+        dist.barrier()
+        return first, None
+    lib.peer_barrier(pads.data_ptr(), rank, world, 2, 0, 0)
+    second = lib.error_status(True)
+    dist.barrier()
+    return first, second
+
+
+def test_missing_peer_at_a_peer_barrier_is_reported(tmp_path):
+    """A rank that stops before a peer barrier: the other rank's bounded wait gives up and
+    records the peer-wait error (code 4) instead of hanging; the barrier that everyone reached
+    records nothing.  Peer memory is emulated in shared memory across gloo processes."""
+    out = _dist_util.run(_missing_peer_worker, world=2, args=(str(tmp_path),), timeout=120)
+    assert out[0] == (0, 4)
+    assert out[1][0] == 0

@@ -462,3 +462,62 @@ def test_halo_neighbour_sets_are_symmetric(pname, world):
             assert r in nb[p]
         # every rank whose rows r reads is a neighbour
         assert {int(o) for o in doms[r].halo_owner} <= nb[r]
+
+
+def _peer_halo_worker(rank, world, folder, pname, edge_chunk):
+    """The partitioned worker on the NVLink halo transport, with symmetric memory emulated in
+    host shared memory and the kernel path on the CPU stand-in."""
+    import torch.distributed as dist
+
+    from maloq_b200 import ops
+    from maloq_b200.data import basis_sets
+    from maloq_b200.data.targets import FockLabeler
+    from maloq_b200.ops import kernels
+    from maloq_b200.ops import loss as ops_loss
+    from maloq_b200.parallel.halo import partition_batch
+    from tests import fake_symm
+    from tests.cpu_extension import CpuExtension
+
+    fake_symm.install(folder)
+    kernels._lib = CpuExtension()
+    ops._cuda = ops_loss._cuda = lambda *t: True
+    g = _toy_graph()
+    lab = FockLabeler(basis_sets.get_basis("split_valence_small"))
+    part = P.partition(pname, g.num_nodes, world, src=g.src, dst=g.dst, pos=g.pos)
+    dom = P.decompose(part, g.src, g.dst, world)[rank]
+    b = partition_batch(g, dom, lab.table, transport="peer")
+    bb, hd = _model(lab, edge_chunk)
+    no, eo = hd(bb(b), b)
+    torch.manual_seed(7)
+    wn = torch.randn(g.num_nodes, no.shape[-1])
+    we = torch.randn(len(g.src), eo.shape[-1])
+    loss = (no[0] * wn[dom.owned]).sum() + (eo[0] * we[dom.edges]).sum()
+    loss.backward()
+    grads = [p.grad.clone() if p.grad is not None else torch.zeros_like(p) for p in
+             list(bb.parameters()) + list(hd.parameters())]
+    for gr in grads:
+        dist.all_reduce(gr)
+    peer = b.halo.peer
+    return (dom.owned, dom.edges, no[0].detach(), eo[0].detach(), grads, kernels._lib.error_status(True),
+            None if peer is None else (peer.neighbours, peer.epoch))
+
+
+@pytest.mark.parametrize("pname,world,edge_chunk", [("slab", 2, None), ("slab", 3, None), ("rcb", 3, 40)])
+def test_nvlink_halo_path_on_emulated_peer_memory(monkeypatch, tmp_path, pname, world, edge_chunk):
+    """The NVLink halo transport (publish to staging slots, neighbour barriers, halo rows read
+    from the owners' memory inside the gather, halo gradients pushed to the owners and summed
+    there) on symmetric memory emulated in shared memory across gloo processes: equal to the
+    single-process kernel path, no barrier timed out, and each rank's barriers include only its
+    halo neighbours."""
+    from tests.cpu_extension import use_cpu_extension
+
+    out = _dist_util.run(_peer_halo_worker, world=world, args=(str(tmp_path), pname, edge_chunk), timeout=300)
+    use_cpu_extension(monkeypatch)
+    ref_n, ref_e, ref_g = _single()
+    rel = lambda a, b: float(np.linalg.norm(a - b) / (np.linalg.norm(b) + 1e-12))
+    for r, (own, edges, no, eo, grads, err, peer) in out.items():
+        assert err == 0
+        assert rel(no, ref_n[own].numpy()) < 2e-3 and rel(eo, ref_e[edges].numpy()) < 2e-3
+        worst = max(rel(a, b.numpy()) for a, b in zip(grads, ref_g) if np.linalg.norm(b.numpy()) > 0)
+        assert worst < 1e-2, worst
+        assert peer is not None and peer[1] > 0 and r not in peer[0]
