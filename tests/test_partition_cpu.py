@@ -521,3 +521,36 @@ def test_nvlink_halo_path_on_emulated_peer_memory(monkeypatch, tmp_path, pname, 
         worst = max(rel(a, b.numpy()) for a, b in zip(grads, ref_g) if np.linalg.norm(b.numpy()) > 0)
         assert worst < 1e-2, worst
         assert peer is not None and peer[1] > 0 and r not in peer[0]
+
+
+def _peer_workflow_worker(rank, world, folder, transport):
+    from maloq_b200 import ops
+    from maloq_b200.ops import basis_transform, kernels, labels
+    from maloq_b200.ops import loss as ops_loss
+    from maloq_b200.train.workflow import TrainingWorkflow
+    from tests import fake_symm
+    from tests.cpu_extension import CpuExtension
+
+    fake_symm.install(folder + "/symm")
+    kernels._lib = CpuExtension()
+    for m in (ops, ops_loss, labels, basis_transform):
+        m._cuda = lambda *t: True
+    cfg = dict(dataset_name="synthetic_sio2", num_atoms=150, distribute_graphs=True, partition_type="slab",
+               halo_transport=transport, l_embedding_dim=8, num_mp_layers=1, num_distance_basis=8,
+               rcut_orbitals=2.0, rcut_gaussian=4.0, mmax=2, num_epochs=2, lr_init=1e-3, device="cpu",
+               output_folder=folder + "/" + transport, log_every=0, save_frequency=0)
+    hist = TrainingWorkflow(cfg).run()
+    return hist["train_node"], hist["train_edge"], kernels._lib.error_status(True)
+
+
+def test_partitioned_training_on_the_nvlink_halo_transport(tmp_path):
+    """Two epochs of graph-partitioned training (3 ranks, slab partition) on the kernel path:
+    the NVLink halo transport on emulated peer memory (staging slots and receive buffers reused
+    across layers and steps) gives the same losses as the collective transport."""
+    runs = {t: _dist_util.run(_peer_workflow_worker, world=3, args=(str(tmp_path), t), timeout=600)
+            for t in ("peer", "collective")}
+    for r in range(3):
+        pn, pe, err = runs["peer"][r]
+        cn, ce, _ = runs["collective"][r]
+        assert err == 0
+        assert np.allclose(pn, cn, rtol=1e-4) and np.allclose(pe, ce, rtol=1e-4), (pn, cn)
