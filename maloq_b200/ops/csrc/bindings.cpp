@@ -129,7 +129,8 @@ void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
                        c10::optional<at::Tensor> rad, at::Tensor dA, at::Tensor dst_ptr, at::Tensor src_perm,
                        at::Tensor src_ptr, at::Tensor DX, c10::optional<at::Tensor> DXE,
                        c10::optional<at::Tensor> DRAD, int64_t Cin, int64_t peers,
-                       c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row, int64_t n_own) {
+                       c10::optional<at::Tensor> halo_owner, c10::optional<at::Tensor> halo_row, int64_t n_own,
+                       int64_t recv, c10::optional<at::Tensor> recv_slot) {
   chk(X, at::kFloat, "X");
   chk(rot, at::kFloat, "rot");
   chk(dA, at::kBFloat16, "dA");
@@ -150,7 +151,8 @@ void gather_rotate_bwd(int64_t L, int64_t MM, at::Tensor X, c10::optional<at::Te
                                       DRAD.has_value() ? bf(*DRAD) : nullptr, N, (int)rot.size(0), (int)X.size(2),
                                       (int)Cin, reinterpret_cast<const float* const*>(peers),
                                       halo_owner.has_value() ? halo_owner->data_ptr<int>() : nullptr, ll(halo_row),
-                                      n_own, X.size(0), halo_owner.has_value() ? halo_owner->numel() : 0, stream()));
+                                      n_own, X.size(0), halo_owner.has_value() ? halo_owner->numel() : 0, stream(),
+                                      reinterpret_cast<float* const*>(recv), ll(recv_slot)));
 }
 
 // DX[n] = sum over dst-CSR of DDST + sum over src-CSR of DSRC (either may be absent)
@@ -539,7 +541,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("resids") = std::vector<c10::optional<at::Tensor>>());
   m.def("splitk_reduce", &splitk_reduce, "sum split-K partials");
   m.def("gather_rotate_fwd", &gather_rotate_fwd);
-  m.def("gather_rotate_bwd", &gather_rotate_bwd);
+  m.def("gather_rotate_bwd", &gather_rotate_bwd, py::arg("L"), py::arg("MM"), py::arg("X"), py::arg("XE"),
+        py::arg("rot"), py::arg("rad"), py::arg("dA"), py::arg("dst_ptr"), py::arg("src_perm"), py::arg("src_ptr"),
+        py::arg("DX"), py::arg("DXE"), py::arg("DRAD"), py::arg("Cin"), py::arg("peers"), py::arg("halo_owner"),
+        py::arg("halo_row"), py::arg("n_own"), py::arg("recv") = 0, py::arg("recv_slot") = py::none());
   m.def("rotate_back_scatter", &rotate_back_scatter);
   m.def("rotate_back_edge", &rotate_back_edge);
   m.def("rotate_grad", &rotate_grad);

@@ -26,6 +26,11 @@ struct HaloRef {
   const long long* halo_row;
   long long n_own;
   long long n_src, n_dst;  // valid source / destination rows (bounds checks)
+  // backward with recv != nullptr: the gradient row of halo node h (row n_own + h) is stored
+  // straight into slot recv_slot[h] of its owner's receive buffer recv[halo_owner[h]] (a store
+  // over NVLink) instead of into DX
+  float* const* recv;
+  const long long* recv_slot;
 };
 
 __device__ __forceinline__ const float* src_row(const float* X, long long s, int S, int C, const HaloRef& H) {
@@ -235,6 +240,10 @@ __global__ void __launch_bounds__(64 * Q) gather_rotate_bwd_nodes_kernel(
 #pragma unroll
       for (int i = 0; i < V; ++i) din[j * V + i] += red_s[(p * S + j) * 64 * V + i * 64 + t];
   float* o = DX + (size_t)n * S * C + c;
+  if (H.recv != nullptr && n >= H.n_own) {  // a halo node: straight into its owner's receive slot
+    const long long h = n - H.n_own;
+    o = H.recv[H.halo_owner[h]] + (size_t)H.recv_slot[h] * S * C + c;
+  }
 #pragma unroll
   for (int j = 0; j < S; ++j) stv<V>(o + (size_t)j * C, din + j * V);
 }
@@ -642,7 +651,7 @@ const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* X
   MM = clampm(L, MM);
   if (E == 0) return nullptr;
   if (C % 2 != 0) return "gather_rotate: channel count must be even";
-  const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows};
+  const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows, nullptr, nullptr};
   MALOQ_DISPATCH_FRAME(({
     constexpr int Q_ = EdgeLanes<(FL + 1) * (FL + 1)>::Q;
     dim3 grid((E + Q_ - 1) / Q_, (Cin / 2 + 63) / 64);
@@ -679,11 +688,13 @@ const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* X
                                    const long long* src_perm, const long long* src_ptr, float* DX, float* DXE,
                                    __nv_bfloat16* DRAD, int N, int E, int C, int Cin, const float* const* peers,
                                    const int* halo_owner, const long long* halo_row, long long n_own,
-                                   long long n_x_rows, long long n_halo, cudaStream_t st) {
+                                   long long n_x_rows, long long n_halo, cudaStream_t st, float* const* recv,
+                                   const long long* recv_slot) {
   MM = clampm(L, MM);
   if (C % 2 != 0) return "gather_rotate: channel count must be even";
   if (Cin == 3 * C && (XE == nullptr || DXE == nullptr)) return "gather_rotate_bwd: edge part needs XE and DXE";
-  const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows};
+  if (recv != nullptr && (peers == nullptr || recv_slot == nullptr)) return "gather_rotate_bwd: recv needs a halo";
+  const HaloRef H{peers, halo_owner, halo_row, n_own, peers ? n_own + n_halo : n_x_rows, n_x_rows, recv, recv_slot};
   if (N > 0) {
     const char* err = gather_rotate_bwd_nodes(L, MM, X, rot, rad, dA, dst_ptr, src_perm, src_ptr, DX, DRAD, N, E, C,
                                               Cin, H, st);

@@ -13,14 +13,16 @@ const char* edge_gather_rotate_fwd(int L, int MM, const float* X, const float* X
                                    __nv_bfloat16* A, int E, int C, int Cin, const float* const* peers,
                                    const int* halo_owner, const long long* halo_row, long long n_own,
                                    long long n_x_rows, long long n_halo, cudaStream_t st);
-// Backward: DX [N, S, C] (N rows of the source space, written completely), DXE (Cin = 3C),
-// DRAD.  dst_ptr has N+1 entries (rows without incoming edges have empty ranges).
+// Backward: DX [N, S, C] (N rows of the source space, written completely - or, with recv, the
+// halo rows stored into their owners' receive slots instead), DXE (Cin = 3C), DRAD.  dst_ptr
+// has N+1 entries (rows without incoming edges have empty ranges).
 const char* edge_gather_rotate_bwd(int L, int MM, const float* X, const float* XE, const float* rot,
                                    const __nv_bfloat16* rad, const __nv_bfloat16* dA, const long long* dst_ptr,
                                    const long long* src_perm, const long long* src_ptr, float* DX, float* DXE,
                                    __nv_bfloat16* DRAD, int N, int E, int C, int Cin, const float* const* peers,
                                    const int* halo_owner, const long long* halo_row, long long n_own,
-                                   long long n_x_rows, long long n_halo, cudaStream_t st);
+                                   long long n_x_rows, long long n_halo, cudaStream_t st,
+                                   float* const* recv = nullptr, const long long* recv_slot = nullptr);
 const char* edge_halo_fetch(const float* const* peers, const int* halo_owner, const long long* halo_row, float* out,
                             long long n_halo, int SC, cudaStream_t st);
 const char* edge_halo_push(const float* G, float* const* recv, const int* halo_owner, const long long* recv_slot,

@@ -184,10 +184,15 @@ class EdgewiseFn(torch.autograd.Function):
         DX = torch.empty((n_ext,) + tuple(x_node.shape[1:]), device=dev, dtype=torch.float32)
         DXE = torch.empty_like(xe) if xe is not None else None
         DRAD = torch.empty_like(rad)
-        lib.gather_rotate_bwd(*LM, x_node, xe, graph.rot, rad, dA, dst_ptr_ext(graph, n_ext), perm, sptr, DX, DXE,
-                              DRAD, Cin, *_halo_args(ctx.halo))
-        if ctx.halo is not None:
-            DX = ctx.halo[0].reduce_grads(DX)
+        if ctx.halo is not None:  # halo rows' gradients go straight to their owners' receive slots
+            peer = ctx.halo[0]
+            b, recv = peer.begin_grads()
+            lib.gather_rotate_bwd(*LM, x_node, xe, graph.rot, rad, dA, dst_ptr_ext(graph, n_ext), perm, sptr, DX,
+                                  DXE, DRAD, Cin, *_halo_args(ctx.halo), recv, peer.recv_slot)
+            DX = peer.finish_grads(DX[:peer.n_own], b)
+        else:
+            lib.gather_rotate_bwd(*LM, x_node, xe, graph.rot, rad, dA, dst_ptr_ext(graph, n_ext), perm, sptr, DX,
+                                  DXE, DRAD, Cin, *_halo_args(ctx.halo))
         count_launches(5 + (xe is not None))
         dw1 = dw1[:1] + [W.pair_grad(d) for d in dw1[1:]]
         dw2 = dw2[:1] + [W.pair_grad(d) for d in dw2[1:]]

@@ -5,10 +5,12 @@ symmetric-memory buffer and passes a peer barrier; the gather kernel then loads 
 source row directly from the owning rank's slot (``peers[owner] + row``) while it rotates the
 message - the halo never exists as a separate exchanged tensor.
 
-Backward: the gather backward produces gradients for the extended [owned | halo] rows; the
-halo rows are stored by ``halo_push`` into the owners' receive buffers (double-buffered),
-a barrier follows, and each owner sums its own gradient rows and its received rows with one
-fixed-order segmented sum, ``node_reduce`` (a reduce-scatter done inside the scatter stage).
+Backward: the gather-backward kernel stores each halo row's gradient straight into its owner's
+receive buffer (double-buffered; ``begin_grads``), a barrier among the neighbours follows, and
+each owner sums its own gradient rows and its received rows with one fixed-order segmented sum,
+``node_reduce`` (``finish_grads``) - a reduce-scatter done inside the scatter stage.  The
+chunked path, which materialises [owned | halo] rows once per layer, pushes its halo rows with
+``halo_push`` instead (``reduce_grads``).
 
 All waits are the bounded peer barriers of ``comm.cu``, among each rank's halo neighbours only
 (the owners it reads from and the ranks that read from it), not all ranks.  Staging slots are kept for
@@ -151,6 +153,27 @@ class PeerHalo:
     def fetch(self, x_node):
         """Differentiable [owned | halo] rows (one publish, one peer copy per call)."""
         return _PeerFetch.apply(x_node, self)
+
+    def begin_grads(self):
+        """(receive-buffer index, its address table) for a backward kernel that stores the halo
+        rows' gradients straight into their owners' receive slots (``recv_slot``)."""
+        b = self.grad_calls % 2
+        self.grad_calls += 1
+        return b, self.recv_tables[b].data_ptr()
+
+    def finish_grads(self, own, b):
+        """After such a kernel: wait until the neighbours have stored their rows, then sum the
+        owned gradient rows and the received ones (one fixed-order pass)."""
+        self._barrier()
+        own = own.contiguous()
+        if self.n_recv == 0:
+            return own
+        recv = self.recvbuf[b * self.max_recv * self.sc:(b * self.max_recv + self.n_recv) * self.sc]
+        out = torch.empty_like(own)
+        self.lib.node_reduce(own.reshape(self.n_own, self.sc), self.self_ptr, recv.view(self.n_recv, self.sc),
+                             self.recv_perm, self.recv_ptr, out.view(self.n_own, self.sc))
+        count_launches(1)
+        return out
 
     def reduce_grads(self, dx_ext):
         """Gradient of the extended rows -> gradient of the owned rows (halo rows summed on

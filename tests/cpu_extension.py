@@ -151,7 +151,7 @@ class CpuExtension:
         A.copy_(self._gather(L, MM, X, XE, src, dst, rot, r, Cin).reshape(A.shape).to(torch.bfloat16))
 
     def gather_rotate_bwd(self, L, MM, X, XE, rot, rad, dA, dst_ptr, src_perm, src_ptr, DX, DXE, DRAD, Cin,
-                          peers=0, halo_owner=None, halo_row=None, n_own=0):
+                          peers=0, halo_owner=None, halo_row=None, n_own=0, recv=0, recv_slot=None):
         X = self._extended(X, peers, halo_owner, halo_row, n_own)
         E = rot.shape[0]
         N = DX.shape[0]
@@ -164,7 +164,17 @@ class CpuExtension:
         g = _bf(dA).view(E, R, Cin)
         r = None if rad is None else _bf(rad)
         gx, gxe, grad_r = _grad(lambda x, xe, rr: self._gather(L, MM, x, xe, src, dst, rot, rr, Cin), [X, XE, r], g)
-        DX.copy_(gx[:N])
+        if recv:  # halo rows into their owners' receive slots, owned rows into DX
+            from tests.fake_symm import floats_at, table
+
+            assert peers and recv_slot is not None
+            SC = gx[0].numel()
+            bases = table(recv, self._world())
+            for h, (o, sl) in enumerate(zip(halo_owner, recv_slot)):
+                floats_at(bases[int(o)] + 4 * int(sl) * SC, SC).copy_(gx[n_own + h].reshape(-1))
+            DX[:n_own].copy_(gx[:n_own])
+        else:
+            DX.copy_(gx[:N])
         if DXE is not None:
             DXE.copy_(gxe)
         if DRAD is not None:
