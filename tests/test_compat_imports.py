@@ -26,3 +26,15 @@ def test_reference_import_paths():
     assert Fock_Irreps_Head is heads.Fock_Irreps_Head and SO2_Convolution is layers.SO2_Convolution
     assert EquivariantRMSNormArraySphericalHarmonicsV2 is layers.EquivariantRMSNorm
     assert SplitTrainer is ST and callable(decompose) and callable(split_indices) and CoefficientMapping
+
+
+def test_reference_data_tool_import_paths():
+    from maloq.dataset_utils.ASEDataset import ASEDataset, distribute_data
+    from maloq.dataset_utils.compute_lin_ref_nabla import linear_energy_references
+    from maloq.dataset_utils.get_scale_shift import scale_shift_table
+    from maloq.dataset_utils.omol_csh_58k_dataset_utils import OMolCSH58kDatabase
+    from maloq.fock_utils.get_energy_from_fock import hf_energy, write_density_cube
+    from maloq.fock_utils.utils_orca_out import get_fock_size, sort_by_l
+
+    assert all(callable(f) for f in (ASEDataset, distribute_data, linear_energy_references, scale_shift_table,
+                                     OMolCSH58kDatabase, hf_energy, write_density_cube, get_fock_size, sort_by_l))
