@@ -111,7 +111,7 @@ def test_overlap_and_kinetic_energy_against_a_grid():
     basis = {8: [(1, [1.3], [1.0]), (2, [0.9], [1.0]), (3, [0.7], [1.0])]}
     pos = np.array([[0.0, 0.0, 0.0], [0.3, -0.4, 0.5]])  # bohr
     S, T, _ = I.one_electron_integrals([8, 8], pos, basis, units="bohr")
-    g = np.linspace(-7, 7, 141)
+    g = np.linspace(-6.5, 6.5, 105)
     h = g[1] - g[0]
     X, Y, Z = np.meshgrid(g, g, g, indexing="ij")
 

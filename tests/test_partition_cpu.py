@@ -535,7 +535,7 @@ def _peer_workflow_worker(rank, world, folder, transport):
     kernels._lib = CpuExtension()
     for m in (ops, ops_loss, labels, basis_transform):
         m._cuda = lambda *t: True
-    cfg = dict(dataset_name="synthetic_sio2", num_atoms=150, distribute_graphs=True, partition_type="slab",
+    cfg = dict(dataset_name="synthetic_sio2", num_atoms=90, distribute_graphs=True, partition_type="slab",
                halo_transport=transport, l_embedding_dim=8, num_mp_layers=1, num_distance_basis=8,
                rcut_orbitals=2.0, rcut_gaussian=4.0, mmax=2, num_epochs=2, lr_init=1e-3, device="cpu",
                output_folder=folder + "/" + transport, log_every=0, save_frequency=0)
