@@ -182,7 +182,8 @@ class Fock_Irreps_Head(nn.Module):
         edge_index = emb["edge_index"]
         node_outs, edge_outs = [], []
         if self.reduce_edge:
-            alpha, beta, half_mask, rev = self.half_antisym_edge_pairs(edge_emb.to(node_emb.dtype), edge_index)
+            alpha, beta, half_mask, rev = self.half_antisym_edge_pairs(edge_emb.to(node_emb.dtype), edge_index,
+                                                                       node_emb.shape[0])
         for spin in range(self.num_spins):
             n_sorted = self.process(node_emb, "node", spin)
             if self.reduce_node:
@@ -193,17 +194,12 @@ class Fock_Irreps_Head(nn.Module):
                 oa = self.process(alpha, "edge_alpha", spin)
                 ob = self.process(beta, "edge_beta", spin)
                 oa, ob = self.half_edges_to_full(rev, half_mask, oa, ob)
-                oa = oa[:, self.output_permutation["edge_alpha"]]
-                ob = ob[:, self.output_permutation["edge_beta"]]
-                ia = torch.as_tensor(self.off_diag_alpha, device=oa.device, dtype=torch.long)
-                ib = torch.as_tensor(self.off_diag_beta, device=ob.device, dtype=torch.long)
-                va, vb = oa[:, ia].clone(), ob[:, ib].clone()
+                pa, pb, ia, ib, remix, sign = self._reduce_edge_tables(oa.device, oa.dtype, oa.shape[1] + ob.shape[1])
+                oa, ob = oa.index_select(1, pa), ob.index_select(1, pb)
+                va, vb = oa.index_select(1, ia), ob.index_select(1, ib)
                 oa = oa.index_copy(1, ia, va + vb)
                 ob = ob.index_copy(1, ib, va - vb)
-                eo = torch.cat([oa, ob], dim=-1)[:, self.remix]
-                flips = torch.as_tensor(self.parity_flip_indices, device=eo.device, dtype=torch.long)
-                sign = torch.ones(eo.shape[1], device=eo.device, dtype=eo.dtype).index_fill(0, flips, -1.0)
-                edge_out = eo * sign
+                edge_out = torch.cat([oa, ob], dim=-1).index_select(1, remix) * sign
             elif emb.get("edge_chunks"):
                 # row-wise over edges: one chunk at a time (recomputed in backward)
                 def rows(x, spin=spin):
@@ -222,30 +218,50 @@ class Fock_Irreps_Head(nn.Module):
             edge_outs.append(edge_out)
         return torch.stack(node_outs, 0), torch.stack(edge_outs, 0)
 
+    def _reduce_edge_tables(self, device, dtype, width):
+        """Index tables of the reduce_edge remix on ``device``, built once (a per-call copy from
+        host lists would wait for the device)."""
+        key = (str(device), dtype, width)
+        cache = self.__dict__.setdefault("_tables", {})
+        if key not in cache:
+            flips = torch.as_tensor(self.parity_flip_indices, dtype=torch.long)
+            sign = torch.ones(width, dtype=dtype).index_fill(0, flips, -1.0)
+            lt = lambda v: torch.as_tensor(v, dtype=torch.long).to(device)
+            cache[key] = (lt(self.output_permutation["edge_alpha"]), lt(self.output_permutation["edge_beta"]),
+                          lt(self.off_diag_alpha), lt(self.off_diag_beta), lt(self.remix), sign.to(device))
+        return cache[key]
+
     @staticmethod
-    def reverse_edge_indices(edge_index):
-        n = int(edge_index.max()) + 1 if edge_index.numel() else 1
+    def reverse_edge_indices(edge_index, num_nodes=None):
+        """rev[e] = the edge with the endpoints of e swapped (every edge has one).  ``num_nodes``
+        (known on the host) avoids reading the largest index back from the device."""
+        if num_nodes is None:
+            num_nodes = int(edge_index.max()) + 1 if edge_index.numel() else 1
+        n = int(num_nodes)
         _, po = torch.sort(edge_index[0] * n + edge_index[1])
         _, pf = torch.sort(edge_index[1] * n + edge_index[0])
         return pf[torch.argsort(po)]
 
-    def half_antisym_edge_pairs(self, edge_emb, edge_index):
-        """Symmetric/antisymmetric combinations for the canonical half of the edge pairs."""
-        rev = self.reverse_edge_indices(edge_index)
-        half = torch.arange(edge_index.shape[1], device=edge_index.device) < rev
-        a, b = edge_emb[half], edge_emb[rev[half]]
+    def half_antisym_edge_pairs(self, edge_emb, edge_index, num_nodes=None):
+        """Symmetric/antisymmetric combinations for the canonical half of the edge pairs (the
+        edges e with e < rev[e]: exactly half of them, so they are selected by a stable sort
+        rather than a boolean mask - no host synchronisation).  Returns (a + b, a - b, the
+        half's edge ids, rev)."""
+        rev = self.reverse_edge_indices(edge_index, num_nodes)
+        E = edge_index.shape[1]
+        first = torch.arange(E, device=edge_index.device) < rev
+        half = torch.argsort((~first).to(torch.int8), stable=True)[: E // 2]
+        a, b = edge_emb.index_select(0, half), edge_emb.index_select(0, rev.index_select(0, half))
         return a + b, a - b, half, rev
 
     @staticmethod
     def half_edges_to_full(rev, half, oa, ob):
+        """Full edge rows from the half's outputs: the half's rows and, at their reverse edges,
+        the same alpha rows and negated beta rows (``half``: edge ids)."""
         E = rev.shape[0]
-        fa = oa.new_zeros((E,) + oa.shape[1:])
-        fb = ob.new_zeros((E,) + ob.shape[1:])
-        flipped = rev[half]
-        fa[half] = oa
-        fa[flipped] = oa
-        fb[half] = ob
-        fb[flipped] = -ob
+        flipped = rev.index_select(0, half)
+        fa = oa.new_zeros((E,) + oa.shape[1:]).index_copy(0, half, oa).index_copy(0, flipped, oa)
+        fb = ob.new_zeros((E,) + ob.shape[1:]).index_copy(0, half, ob).index_copy(0, flipped, -ob)
         return fa, fb
 
 
