@@ -198,6 +198,12 @@ class EdgeDegreeEmbedding(nn.Module):
         return ops.rotate_back_m0(e, graph)
 
 
+def _model_frame(edge_attr):
+    """Edge vectors in the model frame: columns [d, x, y, z] -> (y, z, x), polar axis = input z
+    (slices, so no index tensor is copied to the device per call)."""
+    return torch.cat([edge_attr[:, 2:4], edge_attr[:, 1:2]], dim=1)
+
+
 class Graph:
     """Per-forward graph data shared by all layers.
 
@@ -332,7 +338,7 @@ class eSEN_Backbone(nn.Module):
 
     # ---------------------------------------------------------------------------------
     def _rotations(self, edge_attr):
-        vec = edge_attr[:, [2, 3, 1]]  # (x, y, z) -> model frame (y, z, x): polar axis = input z
+        vec = _model_frame(edge_attr)
         return ops.edge_rotation(vec, self.lmax, self.mmax, [getattr(self, f"Jd_{l}") for l in range(self.lmax + 1)],
                                  self.mappingReduced)
 
@@ -386,7 +392,7 @@ class eSEN_Backbone(nn.Module):
                 x_edge_emb = self._run_block(self.edge_blocks[i], ckpt, x_node, x_edge_emb, x_edge, graph)
         x_node = self.norm(x_node)
         out = {"node_embeddings": x_node, "edge_index": batch.edge_index, "edge_distance": dist,
-               "edge_distance_vec": batch.edge_attr[:, [2, 3, 1]], "partition": getattr(batch, "halo", None)}
+               "edge_distance_vec": _model_frame(batch.edge_attr), "partition": getattr(batch, "halo", None)}
         if self.include_edges and graph.chunks is not None:
             cd = x_node.dtype
             if torch.is_grad_enabled():

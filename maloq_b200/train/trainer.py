@@ -99,8 +99,10 @@ class SplitTrainer:
 
     # ------------------------------------------------------------------ one step
     def masks(self, batch):
-        mt = self.mask_table.to(batch.node_pair_type.device)
-        return mt, batch.node_pair_type, batch.edge_pair_type
+        dev = batch.node_pair_type.device
+        if getattr(self, "_mask_dev", None) is None or self._mask_dev.device != dev:
+            self._mask_dev = self.mask_table.to(dev)  # copied to the device once, not every step
+        return self._mask_dev, batch.node_pair_type, batch.edge_pair_type
 
     def forward_loss(self, batch, loss_fxn):
         emb = self.backbone(batch)
