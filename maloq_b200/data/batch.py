@@ -151,6 +151,7 @@ def collate(samples, pair_table=None, target_dtype=torch.float32, float_dtype=to
     )
     b = GraphBatch(**kw)
     b.num_graphs = len(samples)
+    b.dst_ptr_host = kw["dst_ptr"].numpy()  # a host copy (not moved with the batch) for chunking
     if pair_table is not None:
         b.node_pair_type = torch.as_tensor(pair_table.pair_type(z, z))
         b.edge_pair_type = torch.as_tensor(pair_table.pair_type(z[src], z[dst]))

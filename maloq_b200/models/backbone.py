@@ -351,7 +351,8 @@ class eSEN_Backbone(nn.Module):
                   self.lmax, self.mmax, getattr(batch, "halo", None))
         g.num_nodes_ext = getattr(batch, "num_nodes_ext", None) or batch.num_nodes
         if chunked:
-            g.chunks = chunk_bounds(batch.dst_ptr.cpu().numpy(), self.edge_chunk)
+            host = getattr(batch, "dst_ptr_host", None)  # avoids reading dst_ptr back from the device
+            g.chunks = chunk_bounds(host if host is not None else batch.dst_ptr.cpu().numpy(), self.edge_chunk)
             if lazy_rot:
                 g.rot_fn = lambda e0, e1: self._rotations(batch.edge_attr[e0:e1])
         return g

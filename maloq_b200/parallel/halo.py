@@ -159,6 +159,7 @@ def partition_batch(sample, domain, pair_table=None, device="cpu", transport="co
         global_edge_ids=torch.as_tensor(e),
     )
     b = GraphBatch(**kw)
+    b.dst_ptr_host = kw["dst_ptr"].numpy()  # a host copy (not moved with the batch) for chunking
     if getattr(sample, "atom_mol_id", None) is not None:  # molecule of each owned atom (supergraphs)
         b.atom_mol_id = torch.as_tensor(sample.atom_mol_id[own])
     if pair_table is not None:

@@ -329,3 +329,65 @@ def test_driver_smoke_on_the_cpu_stand_in(monkeypatch):
     ext = use_cpu_extension(monkeypatch)
     entry.smoke("cpu")
     assert {"gather_rotate_fwd", "head_gate_fwd", "basis_rows", "fock_loss_stats", "gather_rotate_bwd"} <= set(ext.calls)
+
+
+_SYNC_OPS = {"_local_scalar_dense", "nonzero", "masked_select", "lift_fresh", "lift_fresh_copy", "repeat_interleave",
+             "unique", "_unique2", "bincount"}
+
+
+def _sync_census(step):
+    """ATen ops of ``step`` that would make the host wait for the device (reading a value back,
+    data-dependent output sizes) or copy host data to it, excluding ops of the CPU stand-in."""
+    import traceback
+
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    class Census(TorchDispatchMode):
+        def __init__(self):
+            super().__init__()
+            self.hits = []
+
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            name = func.overloadpacket.__name__
+            masked = name in ("index", "index_put", "index_put_") and any(
+                isinstance(t, torch.Tensor) and t.dtype == torch.bool for t in (args[1] if len(args) > 1 else []))
+            if name in _SYNC_OPS or masked:  # boolean-mask indexing has a data-dependent size
+                st = traceback.extract_stack()
+                # the stand-in's own ops, and torch.optim's step counters (host tensors on a GPU too)
+                if not any("cpu_extension.py" in f.filename or "fake_symm.py" in f.filename or
+                           "torch/optim" in f.filename for f in st):
+                    site = [f"{f.filename.split('repo/')[-1]}:{f.lineno}" for f in st if "maloq_b200" in f.filename]
+                    self.hits.append((name, site[-1] if site else "?"))
+            return func(*args, **(kwargs or {}))
+
+    c = Census()
+    with c:
+        step()
+    return c.hits
+
+
+@pytest.mark.parametrize("head_kw,extra", [({}, {}), (dict(reduce_edge=True), {}), ({}, dict(edge_chunk=40))])
+def test_training_step_has_no_host_synchronisation(monkeypatch, head_kw, extra):
+    """A steady-state training step (forward, fused loss, backward, optimizer step with the bf16
+    weight-cache refresh) on the kernel path issues no op that would stall the host on a GPU:
+    no value read back, no data-dependent output size, no host data copied to the device."""
+    from maloq_b200.models.heads import Fock_Irreps_Head
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    bb, hd, b, lab = _model(2, **extra)
+    if head_kw:
+        hd = Fock_Irreps_Head(None, lab.irreps, lmax=4, sphere_channels=16, ls_list=lab.layout.ls_list,
+                              reduce_node=True, **head_kw)
+    use_cpu_extension(monkeypatch)
+    opt = torch.optim.Adam(list(bb.parameters()) + list(hd.parameters()), lr=1e-3)
+    tr = SplitTrainer(bb, hd, lab.irreps, mask_table=torch.as_tensor(lab.table.mask))
+    tr.train_step(b, L.rmse_mse_padded_loss, opt)  # first step: caches and tables are built
+    hits = _sync_census(lambda: tr.train_step(b, L.rmse_mse_padded_loss, opt))
+    assert not hits, hits
+    # the census does see such ops when they come from the package
+    from maloq_b200.ops import reference as R
+
+    assert _sync_census(lambda: R.fock_loss(torch.ones(2, 3), torch.ones(2, 3), torch.zeros(2, 3), torch.zeros(2, 3),
+                                            torch.ones(2, 3, dtype=torch.bool), torch.ones(2, 3, dtype=torch.bool),
+                                            L.mse_padded_loss))
