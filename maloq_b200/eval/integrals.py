@@ -332,3 +332,44 @@ def write_xyz(path, z, pos, comment="written by maloq_b200"):
         for zz, p in zip(z, np.asarray(pos, dtype=np.float64)):
             fh.write(f"{sym[int(zz)]:2s} {p[0]:20.10f} {p[1]:20.10f} {p[2]:20.10f}\n")
     return path
+
+
+# ------------------------------------------------------------------ command line
+def main(argv=None):
+    """``python -m maloq_b200.eval.integrals STRUCTURE.xyz BASIS.g94 FOCK.npy [--cube rho.cube]``:
+    the Hartree-Fock energy functional of a closed-shell Fock matrix (this package's orbital
+    order) and optionally its electron-density cube (reference ``get_energy_from_fock.py``)."""
+    import argparse
+
+    from ..data.readers import SYMBOL_TO_Z
+
+    ap = argparse.ArgumentParser(description="energy functional and density of a Fock matrix")
+    ap.add_argument("xyz")
+    ap.add_argument("basis")
+    ap.add_argument("fock")
+    ap.add_argument("--charge", type=int, default=0)
+    ap.add_argument("--cube", default=None)
+    ap.add_argument("--spacing", type=float, default=0.4)
+    args = ap.parse_args(argv)
+    with open(args.xyz) as fh:
+        lines = fh.read().splitlines()
+    n = int(lines[0].split()[0])
+    z, pos = [], []
+    for ln in lines[2:2 + n]:
+        p = ln.split()
+        z.append(SYMBOL_TO_Z[p[0].capitalize()])
+        pos.append([float(v) for v in p[1:4]])
+    with open(args.basis) as fh:
+        basis = parse_gaussian94(fh.read())
+    F = np.load(args.fock)
+    res = hf_energy(F, z, np.array(pos), basis, n_electrons=int(sum(z)) - args.charge)
+    print(f"E = {res['total']:.10f} Eh  (electronic {res['electronic']:.10f}, nuclear repulsion "
+          f"{res['nuclear_repulsion']:.10f})")
+    if args.cube:
+        write_density_cube(args.cube, z, np.array(pos), res["density"], basis, spacing=args.spacing)
+        print(f"density cube -> {args.cube}")
+    return res
+
+
+if __name__ == "__main__":
+    main()

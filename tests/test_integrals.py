@@ -208,3 +208,21 @@ def test_orbitals_on_a_grid_density_cube_and_xyz(tmp_path):
     assert abs(vals.sum() * dv - np.sum(P * S)) < 2e-2 * np.sum(P * S)
     xyz = open(I.write_xyz(str(tmp_path / "m.xyz"), z, pos)).read().splitlines()
     assert xyz[0] == "3" and xyz[2].split()[0] == "O" and float(xyz[3].split()[1]) == 0.76
+
+
+def test_energy_command_line(tmp_path, capsys):
+    """The energy/cube command on H2 in STO-3G with its SCF Fock matrix."""
+    pos = np.array([[0.0, 0.0, 0.0], [0.0, 0.0, 1.4]]) / I.BOHR_PER_ANGSTROM
+    S, T, V = I.one_electron_integrals([1, 1], pos, H_STO3G)
+    eri = _ss_eri(pos * I.BOHR_PER_ANGSTROM, *H_STO3G[1][0][1:])
+    c = np.array([1.0, 1.0]) / math.sqrt(2 * (1 + S[0, 1]))
+    P = 2 * np.outer(c, c)
+    F = T + V + np.einsum("ls,mnsl->mn", P, eri) - 0.5 * np.einsum("ls,mlsn->mn", P, eri)
+    np.save(tmp_path / "F.npy", F)
+    I.write_xyz(str(tmp_path / "h2.xyz"), [1, 1], pos)
+    (tmp_path / "b.g94").write_text("H 0\nS 3 1.00\n 3.42525091 0.15432897\n 0.62391373 0.53532814\n"
+                                    " 0.16885540 0.44463454\n****\n")
+    res = I.main([str(tmp_path / "h2.xyz"), str(tmp_path / "b.g94"), str(tmp_path / "F.npy"), "--cube",
+                  str(tmp_path / "h2.cube"), "--spacing", "0.3"])
+    assert abs(res["total"] + 1.1167) < 1e-4 and "E = -1.116" in capsys.readouterr().out
+    assert (tmp_path / "h2.cube").exists()
