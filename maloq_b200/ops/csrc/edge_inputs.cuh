@@ -8,10 +8,11 @@
 // A plain grid-stride kernel over (edge, column) without shared memory or synchronisation, so
 // this file also compiles as host C++: a test builds it with the host compiler, runs it over an
 // emulated grid on the CPU and compares it with PyTorch (the host build defines
-// MALOQ_HOST_EMULATION and provides blockIdx / threadIdx / blockDim / gridDim).
+// MALOQ_HOST_EMULATION and provides blockIdx / threadIdx / blockDim / gridDim; a build through the
+// test runtime, which defines MALOQ_EMU_RUNTIME, brings its own error word).
 #pragma once
 #include <cuda_bf16.h>
-#ifdef MALOQ_HOST_EMULATION
+#if defined(MALOQ_HOST_EMULATION) && !defined(MALOQ_EMU_RUNTIME)
 #include <cmath>
 namespace maloq {
 constexpr int ERR_BOUNDS = 5;

@@ -44,4 +44,10 @@ const char* emu_gate_bwd(int L, int MM, const __nv_bfloat16* Y1, const __nv_bflo
                          int H) {
   return maloq::edge_gate_bwd(L, MM, Y1, dH1, dY1, E, H, nullptr);
 }
+
+const char* emu_node_reduce(const float* DDST, const long long* dst_ptr, const float* DSRC, const long long* src_perm,
+                            const long long* src_ptr, float* DX, int N, int SC, long long n_dst_rows,
+                            long long n_src_rows) {
+  return maloq::edge_node_reduce(DDST, dst_ptr, DSRC, src_perm, src_ptr, DX, N, SC, n_dst_rows, n_src_rows, nullptr);
+}
 }

@@ -1,6 +1,6 @@
 // A small CUDA-on-CPU runtime for tests: kernels from ops/csrc, rewritten textually by the test
 // (launch syntax, shared-memory declarations, this header in place of common.cuh), run with one
-// std::thread per CUDA thread of a block, blocks one after another.
+// std::thread per CUDA thread of a block (one team per launch), blocks one after another.
 //
 // * __syncthreads: a barrier over the block's threads (threads that returned are dropped);
 // * warp shuffles: a per-warp exchange buffer between two warp barriers;
@@ -10,6 +10,7 @@
 //   misaligned float2 / float4 load faults on the GPU, so it aborts here);
 // * the device error word: a host atomic.
 #pragma once
+#define MALOQ_EMU_RUNTIME 1
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -90,36 +91,52 @@ inline std::tuple<T...> args(T... t) {
   return std::tuple<T...>(t...);
 }
 
+// One team of nt host threads per launch walks the grid's blocks in order.  Between blocks the
+// team meets at a barrier whose completion step (run by one thread while the others wait) re-arms
+// the block's barriers - threads that returned from the kernel dropped out of them - clears the
+// shared memory and moves to the next block index.
 template <class... A, class... T>
 inline void operator|(Bound<A...> b, std::tuple<T...> t) {
   const unsigned nt = b.cfg.blk.x * b.cfg.blk.y * b.cfg.blk.z;
+  const unsigned long long nb = (unsigned long long)b.cfg.grid.x * b.cfg.grid.y * b.cfg.grid.z;
+  if (nt == 0 || nb == 0) return;
   g_dim = Dim{b.cfg.grid.x, b.cfg.grid.y, b.cfg.grid.z};
   b_dim = Dim{b.cfg.blk.x, b.cfg.blk.y, b.cfg.blk.z};
   std::tuple<A...> a = std::apply([](auto... v) { return std::tuple<A...>(static_cast<A>(v)...); }, t);
-  for (unsigned bz = 0; bz < b.cfg.grid.z; ++bz)
-    for (unsigned by = 0; by < b.cfg.grid.y; ++by)
-      for (unsigned bx = 0; bx < b.cfg.grid.x; ++bx) {
-        Block blk;
-        blk.bar = std::make_unique<std::barrier<>>(nt);
-        const unsigned nw = (nt + 31) / 32;
-        for (unsigned w = 0; w < nw; ++w) blk.warp.push_back(std::make_unique<std::barrier<>>(std::min(32u, nt - 32 * w)));
-        blk.shfl.assign(nw * 32, 0.f);
-        blk.smem.assign(b.cfg.smem + 16, 0);
-        block = &blk;
-        std::vector<std::thread> th;
-        th.reserve(nt);
-        for (unsigned t = 0; t < nt; ++t)
-          th.emplace_back([&, t] {
-            t_lin = (int)t;
-            t_idx = Dim{t % b.cfg.blk.x, (t / b.cfg.blk.x) % b.cfg.blk.y, t / (b.cfg.blk.x * b.cfg.blk.y)};
-            b_idx = Dim{bx, by, bz};
-            std::apply(b.f, a);
-            blk.warp[t / 32]->arrive_and_drop();
-            blk.bar->arrive_and_drop();
-          });
-        for (auto& x : th) x.join();
-        block = nullptr;
+  const unsigned nw = (nt + 31) / 32;
+  Block blk;
+  blk.shfl.assign(nw * 32, 0.f);
+  auto arm = [&] {
+    blk.bar = std::make_unique<std::barrier<>>(nt);
+    blk.warp.clear();
+    for (unsigned w = 0; w < nw; ++w) blk.warp.push_back(std::make_unique<std::barrier<>>(std::min(32u, nt - 32 * w)));
+    blk.smem.assign(b.cfg.smem + 16, 0);
+  };
+  arm();
+  block = &blk;
+  unsigned long long cur = 0;
+  auto next = [&]() noexcept {
+    ++cur;
+    if (cur < nb) arm();
+  };
+  std::barrier<decltype(next)> end(nt, next);
+  std::vector<std::thread> th;
+  th.reserve(nt);
+  for (unsigned t = 0; t < nt; ++t)
+    th.emplace_back([&, t] {
+      t_lin = (int)t;
+      t_idx = Dim{t % b.cfg.blk.x, (t / b.cfg.blk.x) % b.cfg.blk.y, t / (b.cfg.blk.x * b.cfg.blk.y)};
+      for (unsigned long long q = 0; q < nb; ++q) {
+        b_idx = Dim{(unsigned)(q % b.cfg.grid.x), (unsigned)((q / b.cfg.grid.x) % b.cfg.grid.y),
+                    (unsigned)(q / ((unsigned long long)b.cfg.grid.x * b.cfg.grid.y))};
+        std::apply(b.f, a);
+        blk.warp[t / 32]->arrive_and_drop();
+        blk.bar->arrive_and_drop();
+        end.arrive_and_wait();
       }
+    });
+  for (auto& x : th) x.join();
+  block = nullptr;
 }
 
 template <class T>
@@ -145,10 +162,19 @@ inline T ldg(const T* p) {
 #undef cudaGetLastError
 #define cudaGetLastError() cudaSuccess
 #define cudaGetErrorString(e) "emulated launch error"
+#undef __grid_constant__
+#define __grid_constant__
+// launch attributes have no effect on the emulated launch
+#define cudaFuncSetAttribute(...) cudaSuccess
 
 // device math names the kernels call, from their mathematical definitions
 inline float rsqrtf(float x) { return 1.f / std::sqrt(x); }
 inline float __expf(float x) { return std::exp(x); }
+inline void sincosf_emu(float x, float* s, float* c) {
+  *s = std::sin(x);
+  *c = std::cos(x);
+}
+#define sincosf sincosf_emu
 
 namespace maloq {
 

@@ -1,0 +1,32 @@
+// extern "C" entry points to the host launchers of misc.cu (edge rotation, Fock loss, radial
+// inputs) in the emulated build; the test compiles this file after rewriting misc.cu for
+// tests/csrc/host_emu.cuh.
+#include "misc_emu_src.inc"
+
+extern "C" {
+int emu_error_word() { return ::emu::error_word.exchange(0); }
+
+const char* emu_edge_rotation(const float* vec, long long ldv, const float* J, const int* joff, int L,
+                              const int* row_l, const int* row_m, int R, float* ROT, int E) {
+  return maloq::edge_rotation(vec, ldv, J, joff, L, row_l, row_m, R, ROT, E, nullptr);
+}
+
+int emu_fock_loss_grid(long long n) { return maloq::fock_loss_grid(n); }
+
+const char* emu_fock_loss_stats(const float* O, const float* T, const long long* pt, const uint8_t* mask, int D,
+                                long long rows, float* part, int grid, long long n_pt) {
+  return maloq::fock_loss_stats(O, T, pt, mask, D, rows, part, grid, n_pt, nullptr);
+}
+
+const char* emu_fock_loss_grad(const float* O, const float* T, const long long* pt, const uint8_t* mask, int D,
+                               long long rows, const float* gstat, float* G, long long n_pt) {
+  return maloq::fock_loss_grad(O, T, pt, mask, D, rows, gstat, G, n_pt, nullptr);
+}
+
+const char* emu_edge_inputs(const long long* src_z, const long long* dst_z, const float* D, long long ld_d,
+                            const float* src_table, const float* dst_table, long long n_types, const float* offset,
+                            float coeff, __nv_bfloat16* OUT, long long E, int C, int NB) {
+  return maloq::edge_inputs(src_z, dst_z, D, ld_d, src_table, dst_table, n_types, offset, coeff, OUT, E, C, NB,
+                            nullptr);
+}
+}

@@ -34,4 +34,14 @@ const char* emu_gate_l_bwd(int L, const void* X, const float* Gt, const void* DO
                            int H) {
   return maloq::gate_l_bwd(L, X, Gt, DO, DX, DG, bf16 != 0, B, H, nullptr);
 }
+
+const char* emu_head_gate_fwd(int L, const float* X, const float* SV, __nv_bfloat16* A, int act, float scale, int absg,
+                              int B, int C) {
+  return maloq::head_gate_fwd(L, X, SV, A, act, scale, absg != 0, B, C, nullptr);
+}
+
+const char* emu_head_gate_bwd(int L, const float* X, const float* SV, const float* DA, float* DX, float* DSV, int act,
+                              float scale, int absg, int B, int C) {
+  return maloq::head_gate_bwd(L, X, SV, DA, DX, DSV, act, scale, absg != 0, B, C, nullptr);
+}
 }
