@@ -76,3 +76,79 @@ def test_label_gather_with_a_bad_pair_type_records_an_error(monkeypatch, libs):
     out = lab.matrix_to_labels(data, ptr, pt, labeler.pos_t.cpu())
     assert ext.emulated_error_word() == 5  # ERR_BOUNDS
     assert torch.all(out[0] == 0)
+
+
+@pytest.mark.parametrize("periodic", [False, True])
+@pytest.mark.parametrize("subset", [False, True])
+def test_device_radius_graph_on_emulated_kernels(monkeypatch, libs, periodic, subset):
+    from maloq_b200.data.graph import radius_graph
+    from maloq_b200.data.graph_gpu import radius_graph_device
+
+    rng = np.random.default_rng(3)
+    cell = np.array([11.0, 12.5, 10.5]) if periodic else None
+    pos = rng.uniform(0, 10.5, (150, 3))
+    cutoff = 3.2
+    src, dst, vec = radius_graph(pos, cutoff, cell)
+    targets = np.arange(0, 150, 3) if subset else None
+    ext = use_emulated_extension(monkeypatch, libs)
+    s, d, v, ptr = radius_graph_device(pos, cutoff, cell, targets=targets, device="cpu")
+    assert ext.emulated_calls == {"radius_graph_cells": 1, "radius_graph_pass": 2}
+    if subset:  # the host graph restricted to the target rows, dst renumbered
+        keep = np.isin(dst, targets)
+        src, dst, vec = src[keep], np.searchsorted(targets, dst[keep]), vec[keep]
+    assert np.array_equal(s.numpy(), src) and np.array_equal(d.numpy(), dst)
+    assert np.allclose(v.numpy(), vec, atol=1e-12)
+    assert ptr[-1].item() == len(src)
+    assert ext.emulated_error_word() == 0
+
+
+@pytest.mark.parametrize("lmax,mmax", [(2, 2), (4, 2), (6, 2), (6, 6)])
+def test_edge_rotation_kernel_matches_wigner_matrices(libs, lmax, mmax):
+    """The kernel's rows of D(0, -beta, -alpha) against the stand-in's fp64 Wigner matrices, for
+    random directions and the poles (beta = 0 and pi), over a strided vector view."""
+    from maloq_b200.core import sph
+    from maloq_b200.models.so3 import CoefficientMapping
+    from tests.cpu_extension import CpuExtension
+    from tests.emulated_extension import EmulatedExtension
+
+    Js = sph.J_matrices(lmax)
+    flat = torch.cat([J.reshape(-1).float() for J in Js]).contiguous()
+    joff = [sum((2 * q + 1) ** 2 for q in range(l)) for l in range(lmax + 1)]
+    mp = CoefficientMapping(lmax, mmax)
+    ls, ms = mp.l_harmonic.tolist(), mp.m_complex.tolist()
+    g = torch.Generator().manual_seed(lmax + mmax)
+    attr = torch.randn(40, 4, generator=g)
+    attr[0, 1:] = torch.tensor([0.3, 0.0, 0.0])  # along +y in the model frame (the polar axis)
+    attr[1, 1:] = torch.tensor([-2.0, 0.0, 0.0])
+    vec = attr[:, 1:]  # strided view: leading dimension 4
+    R, S = len(ls), (lmax + 1) ** 2
+    got, ref = torch.empty(40, R, S), torch.empty(40, R, S)
+    emu = EmulatedExtension(libs)
+    emu.edge_rotation(vec, flat, joff, lmax, ls, ms, got)
+    CpuExtension().edge_rotation(vec.contiguous(), flat, joff, lmax, ls, ms, ref)
+    assert (got - ref).abs().max() < 2e-5
+    assert emu.emulated_error_word() == 0
+
+
+@pytest.mark.parametrize("extra", [{}, dict(edge_chunk=40)])
+def test_model_training_step_on_emulated_kernels(monkeypatch, libs, extra):
+    """Forward, loss and every parameter gradient of a two-layer Fock model with every plain
+    kernel of the step (edge frame, norms, gates, head gate, rotation, radial inputs, loss) run
+    from its CUDA source on the emulator (GEMMs from the stand-in), against the PyTorch path."""
+    from tests.test_kernel_path_cpu import _model, _step
+
+    bb, hd, b, lab = _model(2, "source-target", **extra)
+    ref = _step(bb, hd, b, lab)
+    ext = use_emulated_extension(monkeypatch, libs)
+    got = _step(bb, hd, b, lab)
+    expected = {"edge_rotation", "gather_rotate_fwd", "gather_rotate_bwd", "gate_fwd", "gate_bwd",
+                "rotate_back_scatter", "rotate_back_edge", "rotate_grad", "rms_norm_fwd", "rms_norm_bwd",
+                "ln_silu_fwd", "ln_silu_bwd", "gate_l_fwd", "gate_l_bwd", "head_gate_fwd", "head_gate_bwd",
+                "fock_loss_stats", "fock_loss_grad"}
+    assert expected <= set(ext.emulated_calls), expected - set(ext.emulated_calls)
+    for a, r in zip(got[:3], ref[:3]):
+        assert abs(a - r) <= 3e-2 * abs(r), (a, r)
+    assert set(got[3]) == set(ref[3])
+    worst = max((float((got[3][n] - g).norm() / (g.norm() + 1e-12)), n) for n, g in ref[3].items())
+    assert worst[0] < 5e-2, worst
+    assert ext.emulated_error_word() == 0

@@ -3,57 +3,29 @@ for the CPU with a small CUDA runtime emulator (tests/csrc/host_emu.cuh: one thr
 thread with real block barriers, emulated warp shuffles, alignment-checked vector loads) and run
 through their own host launchers, against the contracts of the CPU stand-in
 (tests/cpu_extension.py).  Small shapes; several (lmax, mmax) frames."""
-import ctypes
-
 import numpy as np
 import pytest
 import torch
 
 from tests.cpu_extension import CpuExtension
-from tests.kernel_emu_build import build
+from tests.emulated_extension import load_libraries
 
-P, I, LL, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float
-
-EDGE_SIG = {
-    "emu_gather_rotate_fwd": [I, I, P, P, P, P, P, P, P, I, I, I, LL],
-    "emu_gather_rotate_bwd": [I, I, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I],
-    "emu_rotate_back_scatter": [I, I, P, I, I, P, P, P, P, I, I, I, F],
-    "emu_rotate_back_edge": [I, I, P, I, I, P, P, I, I, I],
-    "emu_rotate_grad": [I, I, P, P, P, P, P, I, I, I, F],
-    "emu_gate_fwd": [I, I, P, P, I, I],
-    "emu_gate_bwd": [I, I, P, P, P, I, I],
-}
-NORM_SIG = {
-    "emu_norm_grid": [LL],
-    "emu_rms_norm_fwd": [I, P, P, P, P, P, I, P, I, I, F],
-    "emu_rms_norm_bwd": [I, P, P, I, P, P, P, P, I, I, F, I],
-    "emu_ln_silu_fwd": [P, P, P, P, I, I, F],
-    "emu_ln_silu_bwd": [P, P, P, P, P, P, I, I, F, I],
-    "emu_gate_l_fwd": [I, P, P, P, I, I, I],
-    "emu_gate_l_bwd": [I, P, P, P, P, P, I, I, I],
-}
-
-
-def _load(name, sig, folder):
-    lib = build(name, str(folder))
-    if lib is None:
+@pytest.fixture(scope="module")
+def _libs(tmp_path_factory):
+    libs = load_libraries(tmp_path_factory.mktemp("kernel_emu"), names=("edge", "norm"))
+    if libs is None:
         pytest.skip("needs g++ and the CUDA headers")
-    for fn, args in sig.items():
-        f = getattr(lib, fn)
-        f.argtypes = args
-        f.restype = ctypes.c_int if fn == "emu_norm_grid" else ctypes.c_char_p
-    lib.emu_error_word.restype = ctypes.c_int
-    return lib
+    return libs
 
 
 @pytest.fixture(scope="module")
-def edge(tmp_path_factory):
-    return _load("edge", EDGE_SIG, tmp_path_factory.mktemp("edge_emu"))
+def edge(_libs):
+    return _libs["edge"]
 
 
 @pytest.fixture(scope="module")
-def norm(tmp_path_factory):
-    return _load("norm", NORM_SIG, tmp_path_factory.mktemp("norm_emu"))
+def norm(_libs):
+    return _libs["norm"]
 
 
 def _p(t):
