@@ -505,6 +505,70 @@ void edge_inputs(at::Tensor src_z, at::Tensor dst_z, at::Tensor edge_attr, at::T
                            offset.data_ptr<float>(), (float)coeff, bf(OUT), E, (int)C, (int)NB, stream()));
 }
 
+// out[N] (fp32, contiguous) = column sums of the 2-D X (fp32 or bf16, unit column stride, any
+// row stride) in a fixed order; the partial-sum scratch comes from the caching allocator
+void colsum(at::Tensor X, at::Tensor out) {
+  TORCH_CHECK(X.is_cuda() && X.dim() == 2 && (X.scalar_type() == at::kFloat || X.scalar_type() == at::kBFloat16),
+              "colsum: X must be a 2-D fp32 or bf16 CUDA tensor");
+  TORCH_CHECK(X.size(1) <= 1 || X.stride(1) == 1, "colsum: X needs unit column stride");
+  chk(out, at::kFloat, "colsum out");
+  TORCH_CHECK(out.numel() == X.size(1), "colsum: out has one value per column");
+  const long long M = X.size(0);
+  const int N = (int)X.size(1);
+  const int P = maloq::colsum_chunks(M, N);
+  const at::cuda::CUDAGuard guard(X.device());
+  at::Tensor part;
+  if (P > 1) part = at::empty({P, (long long)N}, X.options().dtype(at::kFloat));
+  check(maloq::colsum(X.data_ptr(), X.scalar_type() == at::kBFloat16, M, N, M > 1 ? X.stride(0) : (long long)N,
+                      P > 1 ? part.data_ptr<float>() : nullptr, P, out.data_ptr<float>(), stream()));
+}
+
+// out[s] = column sums of rows [seg[s], seg[s + 1]) of the fp32 2-D X (unit column stride);
+// out: contiguous fp32 holding len(seg) - 1 rows of X.size(1) values
+void colsum_segments(at::Tensor X, std::vector<int64_t> seg, at::Tensor out) {
+  TORCH_CHECK(X.is_cuda() && X.dim() == 2 && X.scalar_type() == at::kFloat, "colsum_segments: 2-D fp32 CUDA X");
+  TORCH_CHECK(X.size(1) <= 1 || X.stride(1) == 1, "colsum_segments: X needs unit column stride");
+  chk(out, at::kFloat, "colsum_segments out");
+  TORCH_CHECK(seg.size() >= 2 && seg.front() >= 0 && seg.back() <= X.size(0), "colsum_segments: row offsets");
+  TORCH_CHECK(out.numel() == (int64_t)(seg.size() - 1) * X.size(1), "colsum_segments: out size");
+  std::vector<long long> s(seg.begin(), seg.end());
+  const at::cuda::CUDAGuard guard(X.device());
+  check(maloq::colsum_segments(X.data_ptr<float>(), (int)X.size(1), X.size(0) > 1 ? X.stride(0) : X.size(1), s.data(),
+                               (int)s.size() - 1, out.data_ptr<float>(), stream()));
+}
+
+// Weight operand copies and pair-matrix gradients (kinds: maloq::kPack*), all jobs in one or a
+// few launches.  srcs: contiguous fp32 CUDA tensors (1-D, 2-D or a 3-D batch of matrices).
+void weight_pack(std::vector<at::Tensor> srcs, std::vector<at::Tensor> dsts, std::vector<int64_t> kinds) {
+  const size_t n = srcs.size();
+  TORCH_CHECK(dsts.size() == n && kinds.size() == n, "weight_pack: one destination and kind per source");
+  if (n == 0) return;
+  std::vector<const float*> sp(n);
+  std::vector<void*> dp(n);
+  std::vector<int> batch(n), rows(n), cols(n), kind(n);
+  for (size_t g = 0; g < n; ++g) {
+    const at::Tensor& S = srcs[g];
+    const at::Tensor& D = dsts[g];
+    chk(S, at::kFloat, "weight_pack source");
+    TORCH_CHECK(S.device() == srcs[0].device() && D.device() == S.device(), "weight_pack: one device");
+    TORCH_CHECK(S.dim() >= 1 && S.dim() <= 3, "weight_pack: 1-D, 2-D or 3-D sources");
+    batch[g] = S.dim() == 3 ? (int)S.size(0) : 1;
+    rows[g] = S.dim() >= 2 ? (int)S.size(S.dim() - 2) : 1;
+    cols[g] = (int)S.size(S.dim() - 1);
+    kind[g] = (int)kinds[g];
+    const bool grad = kind[g] == maloq::kPackPairGrad;
+    const bool pair = kind[g] == maloq::kPackPair || kind[g] == maloq::kPackPairT;
+    chk(D, grad ? at::kFloat : at::kBFloat16, "weight_pack destination");
+    TORCH_CHECK(D.numel() == (pair ? 2 * S.numel() : (grad ? S.numel() / 2 : S.numel())),
+                "weight_pack: destination size does not match the job");
+    sp[g] = S.data_ptr<float>();
+    dp[g] = D.data_ptr();
+  }
+  const at::cuda::CUDAGuard guard(srcs[0].device());
+  check(maloq::weight_pack((int)n, sp.data(), dp.data(), batch.data(), rows.data(), cols.data(), kind.data(),
+                           stream()));
+}
+
 int64_t fock_loss_grid(int64_t n) { return maloq::fock_loss_grid(n); }
 
 void fock_loss_stats(at::Tensor O, at::Tensor T, at::Tensor pt, at::Tensor mask, at::Tensor part) {
@@ -569,6 +633,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("allreduce_multimem", &allreduce_multimem);
   m.def("edge_rotation", &edge_rotation);
   m.def("fock_loss_grid", &fock_loss_grid);
+  m.def("colsum", &colsum, "fixed-order column sums (fp32 out)");
+  m.def("colsum_segments", &colsum_segments, "fixed-order column sums of row segments");
+  m.def("weight_pack", &weight_pack, "bf16 weight operand copies / pair-matrix gradients in one launch");
   m.def("fock_loss_stats", &fock_loss_stats);
   m.def("basis_rows", &basis_rows);
   m.def("radius_graph_cells", &radius_graph_cells);

@@ -10,6 +10,18 @@
 //   edge label rows (mask = mask_table[pair_type[row]]), reduced per CTA then summed in fixed
 //   order; the gradient kernel writes d(loss)/d(output) from the scalar gradients of the
 //   statistics, read from device memory (no host round trip between forward and backward).
+// * colsum: column sums of a row-strided [M, N] fp32 or bf16 matrix into fp32 [N] (bias
+//   gradients, per-CTA partial sums of the norm kernels) in a fixed order, so that the result
+//   does not depend on scheduling.  Stage 1: a 32 x 8 CTA covers 32 columns of one row chunk;
+//   each thread sums every 8th row of the chunk with four independent accumulators, the 8
+//   partials are added in thread order through shared memory into part[chunk, N].  Stage 2
+//   is the same kernel over part with a single chunk.  One stage when the matrix is short.
+//   colsum_segments: one CTA row per row segment (per-degree sums of split-K partials).
+// * weight_pack: the bf16 GEMM operand copies of fp32 master weights (plain, transposed, and
+//   the SO(2) pair matrix [[W_r, -W_i], [W_i, W_r]] of W = [W_r; W_i] and its transpose), and
+//   the fp32 gradient of W from the gradient of its pair matrix, for up to kPackJobs tensors in
+//   one launch: the job table is a kernel parameter, each thread writes one output element
+//   (coalesced stores) and finds its job by a binary search over the jobs' first elements.
 #include "common.cuh"
 #include "misc.h"
 #include "edge_inputs.cuh"
@@ -153,6 +165,109 @@ __global__ void fock_loss_grad_kernel(const float* __restrict__ O, const float* 
   }
 }
 
+__device__ __forceinline__ float colsum_load(const float* p) { return *p; }
+__device__ __forceinline__ float colsum_load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+// CTA: 32 columns from blockIdx.x, rows [r0, r1); writes the 32 sums to out[n]
+template <class T>
+__device__ __forceinline__ void colsum_block(const T* __restrict__ X, long long r0, long long r1, int N, long long ld,
+                                             float* __restrict__ out) {
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int n = blockIdx.x * 32 + tx;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (n < N) {
+    const T* p = X + n;
+    long long r = r0 + ty;
+    for (; r + 24 < r1; r += 32) {
+      s0 += colsum_load(p + r * ld);
+      s1 += colsum_load(p + (r + 8) * ld);
+      s2 += colsum_load(p + (r + 16) * ld);
+      s3 += colsum_load(p + (r + 24) * ld);
+    }
+    for (; r < r1; r += 8) s0 += colsum_load(p + r * ld);
+  }
+  red[ty][tx] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (ty == 0 && n < N) {
+    float t = 0.f;
+    for (int k = 0; k < 8; ++k) t += red[k][tx];
+    out[n] = t;
+  }
+}
+
+// blockIdx.y: row chunk [y * chunk, (y + 1) * chunk) -> out row y
+template <class T>
+__global__ void __launch_bounds__(256) colsum_kernel(const T* __restrict__ X, long long M, int N, long long ld,
+                                                     long long chunk, float* __restrict__ out) {
+  const long long r0 = blockIdx.y * chunk;
+  colsum_block(X, r0, r0 + chunk < M ? r0 + chunk : M, N, ld, out + blockIdx.y * (long long)N);
+}
+
+struct SegTable {
+  long long ptr[kColsumSegs + 1];
+};
+
+// blockIdx.y: row segment [ptr[y], ptr[y + 1]) -> out row y
+__global__ void __launch_bounds__(256) colsum_seg_kernel(const float* __restrict__ X, int N, long long ld,
+                                                         const __grid_constant__ SegTable T, float* __restrict__ out) {
+  colsum_block(X, T.ptr[blockIdx.y], T.ptr[blockIdx.y + 1], N, ld, out + blockIdx.y * (long long)N);
+}
+
+struct PackTable {
+  int n;
+  long long start[kPackJobs + 1];  // first output element of each job; start[n] = total
+  const float* src[kPackJobs];
+  void* dst[kPackJobs];
+  int batch[kPackJobs], rows[kPackJobs], cols[kPackJobs], kind[kPackJobs];  // shape of src
+};
+
+__global__ void __launch_bounds__(256) weight_pack_kernel(const __grid_constant__ PackTable T) {
+  const long long total = T.start[T.n];
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    int lo = 0, hi = T.n - 1;  // last job with start <= i
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (T.start[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    const int j = lo;
+    const long long t = i - T.start[j];
+    const int rows = T.rows[j], cols = T.cols[j], kind = T.kind[j];
+    const float* S = T.src[j];
+    float v;
+    if (kind == kPackCast) {
+      v = S[t];
+    } else if (kind == kPackTranspose) {  // dst [batch, cols, rows]
+      const long long mat = (long long)rows * cols, b = t / mat, u = t % mat;
+      const int x = (int)(u / rows), y = (int)(u % rows);
+      v = S[b * mat + (long long)y * cols + x];
+    } else if (kind == kPackPairGrad) {  // src dP [2h, 2k] -> dst fp32 [2h, k]
+      const int h = rows / 2, k = cols / 2;
+      const int R = (int)(t / k), c = (int)(t % k), r = R % h;
+      v = R < h ? S[(long long)r * cols + c] + S[(long long)(h + r) * cols + k + c]
+                : S[(long long)(h + r) * cols + c] - S[(long long)r * cols + k + c];
+      static_cast<float*>(T.dst[j])[t] = v;
+      continue;
+    } else {  // pair matrix [2h, 2k] of src [2h, k] (kPackPair), or its transpose [2k, 2h]
+      const int h = rows / 2, k = cols;
+      int R, C;
+      if (kind == kPackPair) {
+        R = (int)(t / (2 * k));
+        C = (int)(t % (2 * k));
+      } else {
+        C = (int)(t / (2 * h));
+        R = (int)(t % (2 * h));
+      }
+      const int a = R / h, r = R % h, q = C / k, c = C % k;
+      // (a, q) = (0, 0): W_r   (0, 1): -W_i   (1, 0): W_i   (1, 1): W_r
+      const float w = S[(long long)((a ^ q) ? h + r : r) * k + c];
+      v = (a == 0 && q == 1) ? -w : w;
+    }
+    static_cast<__nv_bfloat16*>(T.dst[j])[t] = __float2bfloat16(v);
+  }
+}
+
 static const char* misc_err() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? nullptr : cudaGetErrorString(e);
@@ -174,6 +289,85 @@ const char* edge_rotation(const float* vec, long long ldv, const float* J, const
   const long long n = (long long)E * R;
   edge_rotation_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(vec, ldv, J, ROT, E, T);
   return misc_err();
+}
+
+int colsum_chunks(long long M, int N) {
+  if (M <= 4096) return 1;
+  const long long cols = (N + 31) / 32;
+  const long long want = (148 * 4 + cols - 1) / cols;  // about four CTAs per SM in stage 1
+  const long long most = (M + 255) / 256;              // at least 256 rows (32 per thread) a chunk
+  return (int)std::max<long long>(1, std::min<long long>(std::min(want, most), 1024));
+}
+
+const char* colsum(const void* X, bool bf16, long long M, int N, long long ld, float* part, int P, float* out,
+                   cudaStream_t st) {
+  if (N <= 0) return nullptr;
+  const dim3 blk(32, 8);
+  if (P <= 1 || M == 0) {
+    const long long chunk = M > 0 ? M : 1;
+    if (bf16)
+      colsum_kernel<__nv_bfloat16><<<dim3((N + 31) / 32, 1), blk, 0, st>>>(static_cast<const __nv_bfloat16*>(X), M, N, ld, chunk,
+                                                            out);
+    else
+      colsum_kernel<float><<<dim3((N + 31) / 32, 1), blk, 0, st>>>(static_cast<const float*>(X), M, N, ld, chunk, out);
+    return misc_err();
+  }
+  const long long chunk = (M + P - 1) / P;
+  // chunks that hold rows (<= P): stage 2 reads only the rows of part that stage 1 wrote
+  const int used = (int)((M + chunk - 1) / chunk);
+  if (bf16)
+    colsum_kernel<__nv_bfloat16><<<dim3((N + 31) / 32, used), blk, 0, st>>>(static_cast<const __nv_bfloat16*>(X), M, N, ld, chunk,
+                                                             part);
+  else
+    colsum_kernel<float><<<dim3((N + 31) / 32, used), blk, 0, st>>>(static_cast<const float*>(X), M, N, ld, chunk, part);
+  colsum_kernel<float><<<dim3((N + 31) / 32, 1), blk, 0, st>>>(static_cast<const float*>(part), (long long)used, N,
+                                                        (long long)N, (long long)used, out);
+  return misc_err();
+}
+
+const char* colsum_segments(const float* X, int N, long long ld, const long long* seg, int nseg, float* out,
+                            cudaStream_t st) {
+  if (nseg < 1 || nseg > kColsumSegs) return "colsum_segments: 1 to kColsumSegs segments";
+  if (N <= 0) return nullptr;
+  SegTable T;
+  for (int s = 0; s <= nseg; ++s) {
+    T.ptr[s] = seg[s];
+    if (s > 0 && seg[s] < seg[s - 1]) return "colsum_segments: decreasing row offsets";
+  }
+  colsum_seg_kernel<<<dim3((N + 31) / 32, nseg), dim3(32, 8), 0, st>>>(X, N, ld, T, out);
+  return misc_err();
+}
+
+const char* weight_pack(int n, const float* const* src, void* const* dst, const int* batch, const int* rows,
+                        const int* cols, const int* kind, cudaStream_t st) {
+  for (int j0 = 0; j0 < n; j0 += kPackJobs) {
+    PackTable T;
+    T.n = std::min(kPackJobs, n - j0);
+    long long at = 0;
+    for (int j = 0; j < T.n; ++j) {
+      const int g = j0 + j, kd = kind[g];
+      if (kd < kPackCast || kd > kPackPairGrad) return "weight_pack: unknown job kind";
+      if ((kd == kPackPair || kd == kPackPairT || kd == kPackPairGrad) && (rows[g] % 2 || batch[g] != 1))
+        return "weight_pack: a pair job needs one matrix with an even row count";
+      if (kd == kPackPairGrad && cols[g] % 2) return "weight_pack: a pair gradient needs an even column count";
+      T.start[j] = at;
+      T.src[j] = src[g];
+      T.dst[j] = dst[g];
+      T.batch[j] = batch[g];
+      T.rows[j] = rows[g];
+      T.cols[j] = cols[g];
+      T.kind[j] = kd;
+      const long long m = (long long)batch[g] * rows[g] * cols[g];
+      at += (kd == kPackPair || kd == kPackPairT) ? 2 * m : (kd == kPackPairGrad ? m / 2 : m);
+    }
+    T.start[T.n] = at;
+    if (at == 0) continue;
+    const int grid = (int)std::min<long long>((at + 255) / 256, 148 * 8);
+    weight_pack_kernel<<<grid, 256, 0, st>>>(T);
+    const char* e = misc_err();
+    if (e) return e;
+  }
+  return nullptr;
 }
 
 int fock_loss_grid(long long n) { return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, 148 * 8)); }

@@ -31,6 +31,12 @@ def _lib():
     return lib()
 
 
+def _colsum(x):
+    from .kernels import colsum
+
+    return colsum(x)
+
+
 def dst_ptr_ext(graph, n):
     """Destination CSR offsets over ``n`` rows (halo rows, beyond the owned ones, have no
     incoming edges)."""
@@ -168,7 +174,7 @@ class EdgewiseFn(torch.autograd.Function):
         dH1 = torch.empty(E, R * H, device=dev, dtype=torch.bfloat16)
         _gemm([dY2[:, a0:a1] for a0, a1 in cb], w2t, [dH1[:, h0:h1] for h0, h1 in hb], [None] * nw)
         dw2 = _weight_grads([dY2[:, a0:a1] for a0, a1 in cb], [H1[:, h0:h1] for h0, h1 in hb])
-        db2 = dY2[:, cb[0][0]:cb[0][1]].sum(0, dtype=torch.float32)
+        db2 = _colsum(dY2[:, cb[0][0]:cb[0][1]])
         # gate
         dY1 = torch.empty_like(Y1)
         lib.gate_bwd(*LM, Y1, dH1, dY1, H)
@@ -176,7 +182,7 @@ class EdgewiseFn(torch.autograd.Function):
         dA = torch.empty(E, R * Cin, device=dev, dtype=torch.bfloat16)
         _gemm([dY1[:, y0:y1] for y0, y1 in yb], w1t, [dA[:, a0:a1] for a0, a1 in ab], [None] * nw)
         dw1 = _weight_grads([dY1[:, y0:y1] for y0, y1 in yb], [A[:, a0:a1] for a0, a1 in ab])
-        db1 = dY1[:, yb[0][0]:yb[0][1]].sum(0, dtype=torch.float32)
+        db1 = _colsum(dY1[:, yb[0][0]:yb[0][1]])
         # gather: node gradients straight from dA (fixed-order walks over each node's incoming
         # and outgoing edges), the edge-embedding part per edge, the radial gradient per edge
         perm, sptr = src_csr(graph)
@@ -194,8 +200,9 @@ class EdgewiseFn(torch.autograd.Function):
             lib.gather_rotate_bwd(*LM, x_node, xe, graph.rot, rad, dA, dst_ptr_ext(graph, n_ext), perm, sptr, DX,
                                   DXE, DRAD, Cin, *_halo_args(ctx.halo))
         count_launches(5 + (xe is not None))
-        dw1 = dw1[:1] + [W.pair_grad(d) for d in dw1[1:]]
-        dw2 = dw2[:1] + [W.pair_grad(d) for d in dw2[1:]]
+        pg = W.pair_grads(dw1[1:] + dw2[1:])
+        dw1 = dw1[:1] + pg[:nw - 1]
+        dw2 = dw2[:1] + pg[nw - 1:]
         return (DX, DXE, DRAD, db1, db2, None, None, None, *dw1, *dw2)
 
 

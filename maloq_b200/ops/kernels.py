@@ -88,6 +88,17 @@ def gemm_nt(a, w, bias=None, out_dtype=torch.float32, act=0, alpha=1.0, bn=None,
     return out[:, :N] if out.shape[1] != N else out
 
 
+def colsum(x):
+    """fp32 [N] column sums of a 2-D fp32/bf16 tensor in a fixed order (bias gradients and
+    per-CTA partial sums); any row stride, unit column stride."""
+    if x.dim() != 2 or (x.shape[1] > 1 and x.stride(1) != 1) or x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.reshape(-1, x.shape[-1]).float().contiguous()
+    out = torch.empty(x.shape[1], device=x.device, dtype=torch.float32)
+    lib().colsum(x, out)
+    count_launches(1 if x.shape[0] <= 4096 else 2)
+    return out
+
+
 def gemm_tn_weight_grad(gy, x):
     """dW[N,K] = gy[M,N]^T @ x[M,K] with deterministic split-K over M (fp32 result)."""
     gy = _pad_cols(gy.to(torch.bfloat16)).contiguous()
@@ -132,7 +143,7 @@ class _Linear(torch.autograd.Function):
         if ctx.needs_input_grad[1]:
             gw = gemm_tn_weight_grad(g2, x2)[: weight.shape[0], : weight.shape[1]]
         if ctx.has_bias and ctx.needs_input_grad[2]:
-            gb = gy.reshape(-1, gy.shape[-1]).sum(0, dtype=torch.float32)
+            gb = colsum(gy.reshape(-1, gy.shape[-1]))
         return gx, gw, gb, None
 
 
@@ -337,7 +348,7 @@ class _FockHeadFn(torch.autograd.Function):
         d2 = dsv.to(torch.bfloat16)
         dx[:, 0] = gemm_nt(d2, ws_s, w_bf16=W.bf16_t(ws_s))
         dws = gemm_tn_weight_grad(d2, x0)[: ws_s.shape[0], : ws_s.shape[1]] if ctx.needs_input_grad[1] else None
-        dbs = dsv.sum(0) if has_bs and ctx.needs_input_grad[2] else None
+        dbs = colsum(dsv) if has_bs and ctx.needs_input_grad[2] else None
         return (dx, dws, dbs, None, None, None, None, *grads)
 
 

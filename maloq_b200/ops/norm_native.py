@@ -22,6 +22,12 @@ def _lib():
     return lib()
 
 
+def _colsum(x):
+    from .kernels import colsum
+
+    return colsum(x)
+
+
 def _partial_grid(rows):
     return max(1, min(int(rows), 148 * 4))
 
@@ -60,7 +66,7 @@ class _RmsNorm(torch.autograd.Function):
             g_out = g_out.float()
         lib.rms_norm_bwd(L, s, g_out, gs, aw.contiguous(), dx, part, ctx.eps)
         count_launches(1)
-        p = part.sum(0)
+        p = _colsum(part.view(part.shape[0], -1)).view(part.shape[1:])
         daw, dab = p[: L + 1], p[L + 1]
         if ctx.has_res:
             return dx, dx, daw, dab, None, None
@@ -93,7 +99,7 @@ class _LnSilu(torch.autograd.Function):
         _lib().ln_silu_bwd(x2, w.contiguous(), b.contiguous(), g.reshape(M, W).to(torch.bfloat16).contiguous(), dx,
                            part, ctx.eps)
         count_launches(1)
-        p = part.sum(0)
+        p = _colsum(part.view(part.shape[0], -1)).view(part.shape[1:])
         return dx.view(ctx.shape), p[0], p[1], None
 
 
@@ -206,9 +212,10 @@ class _SO3Linear(torch.autograd.Function):
         _run_problems([gb[:, j * Co:(j + 1) * Co] for j in range(S)], [xb[:, j * C:(j + 1) * C] for j in range(S)],
                       [part[j] for j in range(S)], [None] * S, mn=True, splits=splits)
         dw = torch.empty(L + 1, Co, C, device=g.device, dtype=torch.float32)
-        for l in range(L + 1):  # one reduction per degree over its coefficients and splits
-            torch.sum(part[l * l:(l + 1) * (l + 1)], dim=(0, 1), out=dw[l])
-        db = g[:, 0].sum(0, dtype=torch.float32)
+        # each degree's sum over its coefficients and splits: row segments of part, one launch
+        _lib().colsum_segments(part.view(S * splits, Co * C), [l * l * splits for l in range(L + 2)], dw)
+        count_launches(1)
+        db = _colsum(g[:, 0])
         dres = g if ctx.has_res else None
         dsw = dsb = None
         if ctx.side and g_pre is not None:
@@ -218,7 +225,7 @@ class _SO3Linear(torch.autograd.Function):
             gp = g_pre.to(torch.bfloat16).contiguous()
             dx[:, :C] += gemm_nt(gp, sw, w_bf16=W.bf16_t(sw)).to(dx.dtype)
             dsw = gemm_tn_weight_grad(gp, xb[:, :C].contiguous())[: sw.shape[0], : sw.shape[1]]
-            dsb = g_pre.sum(0, dtype=torch.float32) if ctx.has_sb else None
+            dsb = _colsum(g_pre) if ctx.has_sb else None
         return dx.view(B, S, C).to(ctx.in_dtype), dw, db, None, dres, dsw, dsb
 
 

@@ -115,6 +115,36 @@ class CpuExtension:
                 y = y + res
             c.copy_(y.to(c.dtype))
 
+    def weight_pack(self, srcs, dsts, kinds):
+        from maloq_b200.ops import weights as W
+
+        for S, D, k in zip(srcs, dsts, kinds):
+            assert S.dtype == torch.float32 and S.is_contiguous() and D.is_contiguous()
+            if k == 0:
+                v = S
+            elif k == 1:
+                v = S.transpose(-1, -2)
+            elif k == 2:
+                v = W._pair(S)
+            elif k == 3:
+                v = W._pair(S).t()
+            else:
+                assert k == 4 and D.dtype == torch.float32
+                v = W.pair_grad(S)
+            assert D.numel() == v.numel()
+            D.copy_(v.reshape(D.shape))
+
+    def colsum_segments(self, X, seg, out):
+        assert X.dim() == 2 and X.dtype == torch.float32 and out.is_contiguous()
+        o = out.view(len(seg) - 1, X.shape[1])
+        for s in range(len(seg) - 1):
+            o[s] = X[seg[s]:seg[s + 1]].sum(0)
+
+    def colsum(self, X, out):
+        assert X.dim() == 2 and out.dtype == torch.float32 and out.numel() == X.shape[1]
+        assert X.shape[1] <= 1 or X.stride(1) == 1
+        out.copy_(X.float().sum(0))
+
     def splitk_reduce(self, part, out, beta):
         assert part.dtype == out.dtype == torch.float32 and out.is_contiguous()
         s = part.sum(0).view_as(out)

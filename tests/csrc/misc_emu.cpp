@@ -1,5 +1,5 @@
 // extern "C" entry points to the host launchers of misc.cu (edge rotation, Fock loss, radial
-// inputs) in the emulated build; the test compiles this file after rewriting misc.cu for
+// inputs, column sums, weight packing) in the emulated build; the test compiles this file after rewriting misc.cu for
 // tests/csrc/host_emu.cuh.
 #include "misc_emu_src.inc"
 
@@ -28,5 +28,20 @@ const char* emu_edge_inputs(const long long* src_z, const long long* dst_z, cons
                             float coeff, __nv_bfloat16* OUT, long long E, int C, int NB) {
   return maloq::edge_inputs(src_z, dst_z, D, ld_d, src_table, dst_table, n_types, offset, coeff, OUT, E, C, NB,
                             nullptr);
+}
+
+int emu_colsum_chunks(long long M, int N) { return maloq::colsum_chunks(M, N); }
+
+const char* emu_colsum(const void* X, int bf16, long long M, int N, long long ld, float* part, int P, float* out) {
+  return maloq::colsum(X, bf16 != 0, M, N, ld, part, P, out, nullptr);
+}
+
+const char* emu_weight_pack(int n, const float* const* src, void* const* dst, const int* batch, const int* rows,
+                            const int* cols, const int* kind) {
+  return maloq::weight_pack(n, src, dst, batch, rows, cols, kind, nullptr);
+}
+
+const char* emu_colsum_segments(const float* X, int N, long long ld, const long long* seg, int nseg, float* out) {
+  return maloq::colsum_segments(X, N, ld, seg, nseg, out, nullptr);
 }
 }

@@ -51,6 +51,10 @@ SIGNATURES = {
         "emu_edge_rotation": [P, LL, P, P, I, P, P, I, P, I],
         "emu_fock_loss_grid": [LL],
         "emu_fock_loss_stats": [P, P, P, P, I, LL, P, I, LL],
+        "emu_colsum_chunks": [LL, I],
+        "emu_colsum": [P, I, LL, I, LL, P, I, P],
+        "emu_weight_pack": [I, P, P, P, P, P, P],
+        "emu_colsum_segments": [P, I, LL, P, I, P],
         "emu_fock_loss_grad": [P, P, P, P, I, LL, P, P, LL],
         "emu_edge_inputs": [P, P, P, LL, P, P, LL, P, F, P, LL, I, I],
     },
@@ -62,7 +66,7 @@ SIGNATURES = {
         "emu_radius_graph_pass": [P, P, P, P, P, I, P, P, P, P, P, P, I],
     },
 }
-_INT_RESULT = {"emu_norm_grid", "emu_fock_loss_grid"}
+_INT_RESULT = {"emu_norm_grid", "emu_fock_loss_grid", "emu_colsum_chunks"}
 
 
 def load_libraries(folder, names=tuple(SIGNATURES), defines=()):
@@ -221,6 +225,34 @@ class EmulatedExtension(CpuExtension):
         self._count("edge_inputs")
         _check(self.m.emu_edge_inputs(_p(src_z), _p(dst_z), _p(edge_attr), edge_attr.shape[1], _p(src_table),
                                       _p(dst_table), src_table.shape[0], _p(offset), coeff, _p(OUT), E, C, NB))
+
+    def colsum(self, X, out):
+        assert X.dim() == 2 and X.dtype in (torch.float32, torch.bfloat16) and out.dtype == torch.float32
+        assert (X.shape[1] <= 1 or X.stride(1) == 1) and out.is_contiguous() and out.numel() == X.shape[1]
+        self._count("colsum")
+        M, N = X.shape
+        P = self.m.emu_colsum_chunks(M, N)
+        part = torch.empty(P, N, dtype=torch.float32) if P > 1 else None
+        _check(self.m.emu_colsum(_p(X), int(X.dtype == torch.bfloat16), M, N, X.stride(0) if M > 1 else N,
+                                 _p(part), P, _p(out)))
+
+    def colsum_segments(self, X, seg, out):
+        assert X.dim() == 2 and X.dtype == torch.float32 and (X.shape[1] <= 1 or X.stride(1) == 1)
+        assert out.is_contiguous() and out.numel() == (len(seg) - 1) * X.shape[1]
+        self._count("colsum_segments")
+        s = (ctypes.c_longlong * len(seg))(*[int(v) for v in seg])
+        _check(self.m.emu_colsum_segments(_p(X), X.shape[1], X.stride(0) if X.shape[0] > 1 else X.shape[1], s,
+                                          len(seg) - 1, _p(out)))
+
+    def weight_pack(self, srcs, dsts, kinds):
+        n = len(srcs)
+        shp = [(S.shape[0] if S.dim() == 3 else 1, S.shape[-2] if S.dim() >= 2 else 1, S.shape[-1]) for S in srcs]
+        for S, D in zip(srcs, dsts):
+            assert S.dtype == torch.float32 and S.is_contiguous() and D.is_contiguous()
+        self._count("weight_pack")
+        ptrs = lambda ts: (ctypes.c_void_p * n)(*[t.data_ptr() for t in ts])  # noqa: E731
+        _check(self.m.emu_weight_pack(n, ptrs(srcs), ptrs(dsts), _i32([b for b, _, _ in shp]),
+                                      _i32([r for _, r, _ in shp]), _i32([c for _, _, c in shp]), _i32(kinds)))
 
     def fock_loss_grid(self, n):
         return self.m.emu_fock_loss_grid(n)

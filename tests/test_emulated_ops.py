@@ -152,3 +152,125 @@ def test_model_training_step_on_emulated_kernels(monkeypatch, libs, extra):
     worst = max((float((got[3][n] - g).norm() / (g.norm() + 1e-12)), n) for n, g in ref[3].items())
     assert worst[0] < 5e-2, worst
     assert ext.emulated_error_word() == 0
+
+
+@pytest.mark.parametrize("M,N,dtype,col0", [(0, 5, torch.float32, 0), (1, 3, torch.bfloat16, 0),
+                                            (300, 40, torch.bfloat16, 8), (4096, 7, torch.float32, 2),
+                                            (9000, 70, torch.bfloat16, 16), (20000, 33, torch.float32, 1)])
+def test_colsum_kernel(libs, M, N, dtype, col0):
+    """Fixed-order column sums of a row-strided slice (one stage for short matrices, row chunks
+    plus a second pass for long ones) against an fp64 sum, twice with the same bits."""
+    from tests.emulated_extension import EmulatedExtension
+
+    ext = EmulatedExtension(libs)
+    g = torch.Generator().manual_seed(M + N)
+    full = torch.randn(M, N + col0 + 5, generator=g).to(dtype)
+    X = full[:, col0:col0 + N]
+    out = torch.full((N,), float("nan"))
+    ext.colsum(X, out)
+    ref = X.double().sum(0)
+    assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-4 * max(1.0, M ** 0.5))
+    again = torch.empty(N)
+    ext.colsum(X, again)
+    assert torch.equal(out, again)
+    assert ext.emulated_error_word() == 0
+
+
+def test_colsum_chunk_count(libs):
+    """The chunk count and the launch's chunks: rows that do not split evenly leave trailing
+    chunks empty, which the launcher does not launch or read back."""
+    m = libs["misc"]
+    assert m.emu_colsum_chunks(4096, 128) == 1
+    assert m.emu_colsum_chunks(45948, 128) == 148  # four 32-column blocks, ~592 CTAs
+    assert m.emu_colsum_chunks(151553, 8) == 592
+    for M, N in ((151553, 8), (45948, 128), (5000, 3072)):
+        P = m.emu_colsum_chunks(M, N)
+        chunk = -(-M // P)
+        used = -(-M // chunk)
+        assert 1 <= used <= P and (used - 1) * chunk < M <= used * chunk
+
+
+def test_weight_pack_kernel(libs):
+    """The weight operand copies (bf16 cast, transpose of a matrix and of a batch of matrices,
+    SO(2) pair matrix and its transpose) and the pair-matrix gradient, in one call of more jobs
+    than one launch takes, against their PyTorch definitions."""
+    from maloq_b200.ops import weights as W
+    from tests.emulated_extension import EmulatedExtension
+
+    ext = EmulatedExtension(libs)
+    g = torch.Generator().manual_seed(3)
+    srcs, dsts, kinds, refs = [], [], [], []
+    for i in range(60):  # > 48 jobs: two launches
+        kind = i % 5
+        h, k = 1 + i % 7, 1 + (3 * i) % 11
+        if kind == 1 and i % 2:
+            S = torch.randn(3, 2 * h, k, generator=g)
+        elif kind == 4:
+            S = torch.randn(2 * h, 2 * k, generator=g)
+        else:
+            S = torch.randn(2 * h, k, generator=g)
+        ref = [lambda: S, lambda: S.transpose(-1, -2), lambda: W._pair(S), lambda: W._pair(S).t(),
+               lambda: W.pair_grad(S)][kind]()
+        refs.append(ref if kind == 4 else ref.to(torch.bfloat16))
+        dsts.append(torch.full(ref.shape, float("nan"), dtype=torch.float32 if kind == 4 else torch.bfloat16))
+        srcs.append(S)
+        kinds.append(kind)
+    ext.weight_pack(srcs, dsts, kinds)
+    for d, r, kd in zip(dsts, refs, kinds):
+        if kd == 4:
+            assert torch.allclose(d, r, rtol=1e-6, atol=1e-6)
+        else:
+            assert torch.equal(d, r), kd
+    assert ext.emulated_error_word() == 0
+
+
+def test_colsum_segments_kernel(libs):
+    """Row-segment sums (an empty segment included) against fp64 sums."""
+    from tests.emulated_extension import EmulatedExtension
+
+    ext = EmulatedExtension(libs)
+    g = torch.Generator().manual_seed(5)
+    X = torch.randn(140, 75, generator=g)
+    seg = [0, 3, 3, 40, 100, 140]
+    out = torch.full((len(seg) - 1, 75), float("nan"))
+    ext.colsum_segments(X, seg, out)
+    ref = torch.stack([X[a:b].double().sum(0) for a, b in zip(seg[:-1], seg[1:])])
+    assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-4)
+    assert ext.emulated_error_word() == 0
+
+
+def test_weight_cache_refreshed_in_place_by_weight_pack(monkeypatch, libs):
+    """On the kernel path the bf16 weight copies come from the weight-pack kernel; after an
+    optimizer step the hook rewrites every live copy in place (same tensors, new values) in one
+    launch, and the pair-matrix gradients of several weights come from one call."""
+    from maloq_b200.ops import weights as W
+
+    ext = use_emulated_extension(monkeypatch, libs)
+    W.invalidate()
+    torch.manual_seed(0)
+    p = torch.nn.Parameter(torch.randn(8, 6))
+    q = torch.nn.Parameter(torch.randn(3, 4, 5))
+    opt = torch.optim.SGD([p, q], lr=0.1)
+    first = None
+    for step in range(3):
+        wr, wi = p.detach()[:4], p.detach()[4:]
+        pair = torch.cat([torch.cat([wr, -wi], 1), torch.cat([wi, wr], 1)], 0)
+        got = [W.pair_bf16(p), W.pair_bf16_t(p), W.bf16(p), W.bf16_t(q)]
+        for a, b in zip(got, [pair, pair.t(), p.detach(), q.detach().transpose(-1, -2)]):
+            assert torch.equal(a, b.bfloat16())
+        if first is None:
+            first = got
+        else:  # the same tensors, rewritten by the hook
+            assert all(a is b for a, b in zip(got, first))
+        (p.sum() + (q * step).sum()).backward()
+        before = ext.emulated_calls.get("weight_pack", 0)
+        opt.step()
+        assert ext.emulated_calls["weight_pack"] == before + 1
+        opt.zero_grad()
+    dPs = [torch.randn(8, 12), torch.randn(4, 2)]
+    before = ext.emulated_calls["weight_pack"]
+    for g, d in zip(W.pair_grads(dPs), dPs):
+        assert torch.allclose(g, W.pair_grad(d))
+    assert ext.emulated_calls["weight_pack"] == before + 1
+    assert ext.emulated_error_word() == 0
+    W.invalidate()

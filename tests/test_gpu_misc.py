@@ -1,4 +1,4 @@
-"""Edge rotation and fused loss kernels vs their PyTorch definitions."""
+"""Edge rotation, fused loss and column-sum kernels vs their PyTorch definitions."""
 import pytest
 import torch
 
@@ -163,4 +163,52 @@ def test_edge_inputs_kernel_and_gradients(cuda_device):
         assert ((a - b).norm() / b.norm()).item() < 1e-2
     from maloq_b200.ops import kernels
 
+    assert kernels.error_status() == 0
+
+
+@pytest.mark.parametrize("M,N,dtype,col0", [(1, 3, torch.bfloat16, 0), (300, 40, torch.float32, 8),
+                                            (45948, 128, torch.bfloat16, 128), (151553, 8, torch.float32, 0),
+                                            (20000, 3072, torch.bfloat16, 0)])
+def test_colsum_matches_fp32_sum(cuda_device, M, N, dtype, col0):
+    """Column sums of a row-strided slice against a PyTorch fp32 sum; repeated calls give the same bits."""
+    from maloq_b200.ops import kernels
+
+    torch.manual_seed(M)
+    full = torch.randn(M, N + col0 + 8, device=cuda_device).to(dtype)
+    X = full[:, col0:col0 + N]
+    out = kernels.colsum(X)
+    ref = X.double().sum(0)
+    assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-4 * max(1.0, M ** 0.5))
+    assert torch.equal(out, kernels.colsum(X))
+    assert kernels.error_status() == 0
+
+
+def test_weight_pack_and_segment_sums(cuda_device):
+    """bf16 weight operand copies, pair matrices and pair-matrix gradients (one call, more jobs
+    than one launch takes) and row-segment sums against their PyTorch definitions."""
+    from maloq_b200.ops import kernels
+    from maloq_b200.ops import weights as W
+
+    torch.manual_seed(1)
+    srcs, dsts, kinds, refs = [], [], [], []
+    for i in range(60):
+        kind = i % 5
+        h, k = 8 + i % 7, 16 + (3 * i) % 11
+        S = torch.randn(*((3, 2 * h, k) if kind == 1 and i % 2 else (2 * h, 2 * k) if kind == 4 else (2 * h, k)),
+                        device=cuda_device)
+        ref = [lambda: S, lambda: S.transpose(-1, -2), lambda: W._pair(S), lambda: W._pair(S).t(),
+               lambda: W.pair_grad(S)][kind]()
+        refs.append(ref.contiguous() if kind == 4 else ref.to(torch.bfloat16).contiguous())
+        dsts.append(torch.empty_like(refs[-1]))
+        srcs.append(S)
+        kinds.append(kind)
+    kernels.lib().weight_pack(srcs, dsts, kinds)
+    for d, r, kd in zip(dsts, refs, kinds):
+        assert torch.allclose(d, r, rtol=1e-6, atol=1e-6) if kd == 4 else torch.equal(d, r)
+    X = torch.randn(5 * 16 * 25, 128 * 128 // 4, device=cuda_device)
+    seg = [l * l * 16 for l in range(6)]
+    out = torch.empty(5, X.shape[1], device=cuda_device)
+    kernels.lib().colsum_segments(X, seg, out)
+    ref = torch.stack([X[a:b].double().sum(0) for a, b in zip(seg[:-1], seg[1:])])
+    assert torch.allclose(out.double(), ref, rtol=1e-5, atol=1e-3)
     assert kernels.error_status() == 0
