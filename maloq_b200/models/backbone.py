@@ -82,7 +82,7 @@ class SpectralAtomwise(nn.Module):
         lin = self.scalar_mlp[0]
         s1 = self.so3_linear_1
         h, pre = ops.so3_linear_scalar(x, s1.weight, s1.bias, self.lmax, torch.bfloat16, lin.weight, lin.bias)
-        h = self.act(torch.nn.functional.silu(pre), h)
+        h = ops.gate_silu(pre, h, self.act.expand_index, self.lmax)  # = self.act(silu(pre), h)
         return self.so3_linear_2(h, residual=residual)
 
 

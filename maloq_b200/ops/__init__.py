@@ -10,7 +10,7 @@ from . import reference as _ref
 from . import native as _native
 
 __all__ = [
-    "edge_inputs", "embedding", "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "rms_norm_sh", "edge_rotation", "edgewise",
+    "edge_inputs", "embedding", "gemm_operand", "linear", "layernorm_silu", "so3_linear", "so3_linear_scalar", "gate", "gate_silu", "rms_norm_sh", "edge_rotation", "edgewise",
     "rotate_back_m0_scatter", "rotate_back_m0", "fock_loss",
 ]
 
@@ -107,6 +107,16 @@ def gate(gating_scalars, x, expand_index, lmax):
     if _cuda(x):
         return _native.gate(gating_scalars, x, expand_index, lmax)
     return _ref.gate(gating_scalars, x, expand_index, lmax)
+
+
+def gate_silu(pre, x, expand_index, lmax):
+    """``gate(silu(pre), x, ...)`` with the SiLU inside the gate kernels on the kernel path (no
+    separate pass over the gate pre-activations in forward or backward)."""
+    if _cuda(x):
+        return _native.gate_silu(pre, x, expand_index, lmax)
+    import torch
+
+    return _ref.gate(torch.nn.functional.silu(pre), x, expand_index, lmax)
 
 
 def rms_norm_sh(x, affine_weight, affine_bias, balance_degree_weight, eps, residual=None, out_dtype=None):

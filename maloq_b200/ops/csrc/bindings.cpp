@@ -283,17 +283,17 @@ void ln_silu_bwd(at::Tensor X, at::Tensor w, at::Tensor b, at::Tensor G, at::Ten
 }
 
 // X / OUT (and DO / DX) share a dtype, fp32 or bf16; gates fp32
-void gate_l_fwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor OUT) {
+void gate_l_fwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor OUT, bool silu_gates) {
   const bool b16 = X.scalar_type() == at::kBFloat16;
   chk(X, b16 ? at::kBFloat16 : at::kFloat, "X");
   chk(Gt, at::kFloat, "gates");
   chk(OUT, b16 ? at::kBFloat16 : at::kFloat, "OUT");
   const at::cuda::CUDAGuard guard(X.device());
   check(maloq::gate_l_fwd((int)L, X.data_ptr(), Gt.data_ptr<float>(), OUT.data_ptr(), b16, (int)X.size(0),
-                          (int)X.size(2), stream()));
+                          (int)X.size(2), stream(), silu_gates));
 }
 
-void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tensor DX, at::Tensor DG) {
+void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tensor DX, at::Tensor DG, bool silu_gates) {
   const bool b16 = X.scalar_type() == at::kBFloat16;
   chk(X, b16 ? at::kBFloat16 : at::kFloat, "X");
   chk(DO, b16 ? at::kBFloat16 : at::kFloat, "DO");
@@ -302,7 +302,7 @@ void gate_l_bwd(int64_t L, at::Tensor X, at::Tensor Gt, at::Tensor DO, at::Tenso
   chk(DG, at::kFloat, "DG");
   const at::cuda::CUDAGuard guard(X.device());
   check(maloq::gate_l_bwd((int)L, X.data_ptr(), Gt.data_ptr<float>(), DO.data_ptr(), DX.data_ptr(),
-                          DG.data_ptr<float>(), b16, (int)X.size(0), (int)X.size(2), stream()));
+                          DG.data_ptr<float>(), b16, (int)X.size(0), (int)X.size(2), stream(), silu_gates));
 }
 
 // Fock-head gate: X [B, S, C] fp32, SV [B, (L+1) C] fp32, A [B, S, C] bf16 (act 0 sigmoid, 1 tanh)
@@ -622,8 +622,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("norm_grid", &norm_grid);
   m.def("ln_silu_fwd", &ln_silu_fwd);
   m.def("ln_silu_bwd", &ln_silu_bwd);
-  m.def("gate_l_fwd", &gate_l_fwd);
-  m.def("gate_l_bwd", &gate_l_bwd);
+  m.def("gate_l_fwd", &gate_l_fwd, py::arg("L"), py::arg("X"), py::arg("Gt"), py::arg("OUT"),
+        py::arg("silu_gates") = false);
+  m.def("gate_l_bwd", &gate_l_bwd, py::arg("L"), py::arg("X"), py::arg("Gt"), py::arg("DO"), py::arg("DX"),
+        py::arg("DG"), py::arg("silu_gates") = false);
   m.def("head_gate_fwd", &head_gate_fwd);
   m.def("head_gate_bwd", &head_gate_bwd);
   m.def("edge_inputs", &edge_inputs);

@@ -266,10 +266,12 @@ __global__ void ln_silu_bwd_kernel(const float* __restrict__ X, const float* __r
 }
 
 // ------------------------------------------------------------------ gate (l-outer)
-// OUT[b,0,h] = silu(X[b,0,h]); OUT[b,j,h] = X[b,j,h] * tanh(Gt[b,(l_j-1)*H + h])
+// OUT[b,0,h] = silu(X[b,0,h]); OUT[b,j,h] = X[b,j,h] * tanh(g), g = Gt[b,(l_j-1)*H + h], or
+// g = silu(Gt[...]) when silu_gates (Gt then holds the gate pre-activations: the SiLU of the
+// atomwise block's scalar MLP is applied here instead of in a separate pass)
 template <int L, typename T>
 __global__ void gate_l_fwd_kernel(const T* __restrict__ X, const float* __restrict__ Gt, T* __restrict__ OUT, int B,
-                                  int H) {
+                                  int H, bool silu_gates) {
   constexpr int S = (L + 1) * (L + 1);
   const long long total = (long long)B * H;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -280,7 +282,8 @@ __global__ void gate_l_fwd_kernel(const T* __restrict__ X, const float* __restri
     stf(o, silu(ldf(x)));
 #pragma unroll
     for (int l = 1; l <= L; ++l) {
-      const float t = tanhf(Gt[b * L * H + (l - 1) * H + h]);
+      const float g = Gt[b * L * H + (l - 1) * H + h];
+      const float t = tanhf(silu_gates ? silu(g) : g);
 #pragma unroll
       for (int j = l * l; j < (l + 1) * (l + 1); ++j) stf(o + (size_t)j * H, ldf(x + (size_t)j * H) * t);
     }
@@ -289,7 +292,7 @@ __global__ void gate_l_fwd_kernel(const T* __restrict__ X, const float* __restri
 
 template <int L, typename T>
 __global__ void gate_l_bwd_kernel(const T* __restrict__ X, const float* __restrict__ Gt, const T* __restrict__ DO,
-                                  T* __restrict__ DX, float* __restrict__ DG, int B, int H) {
+                                  T* __restrict__ DX, float* __restrict__ DG, int B, int H, bool silu_gates) {
   constexpr int S = (L + 1) * (L + 1);
   const long long total = (long long)B * H;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -301,7 +304,8 @@ __global__ void gate_l_bwd_kernel(const T* __restrict__ X, const float* __restri
     stf(dx, ldf(d) * dsilu(ldf(x)));
 #pragma unroll
     for (int l = 1; l <= L; ++l) {
-      const float t = tanhf(Gt[b * L * H + (l - 1) * H + h]);
+      const float g = Gt[b * L * H + (l - 1) * H + h];
+      const float t = tanhf(silu_gates ? silu(g) : g);
       float acc = 0.f;
 #pragma unroll
       for (int j = l * l; j < (l + 1) * (l + 1); ++j) {
@@ -309,7 +313,7 @@ __global__ void gate_l_bwd_kernel(const T* __restrict__ X, const float* __restri
         stf(dx + (size_t)j * H, dv * t);
         acc += dv * ldf(x + (size_t)j * H);
       }
-      DG[b * L * H + (l - 1) * H + h] = acc * (1.f - t * t);
+      DG[b * L * H + (l - 1) * H + h] = acc * (1.f - t * t) * (silu_gates ? dsilu(g) : 1.f);
     }
   }
 }
@@ -395,29 +399,30 @@ const char* ln_silu_bwd(const float* X, const float* w, const float* b, const __
   return norm_err();
 }
 
-const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st) {
+const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st,
+                       bool silu_gates) {
   if (B == 0) return nullptr;
   const int grid = (int)std::min<long long>(((long long)B * H + 255) / 256, 148 * 32);
   if (bf16) {
     MALOQ_DISPATCH_L((gate_l_fwd_kernel<LL, __nv_bfloat16><<<grid, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(X), Gt, static_cast<__nv_bfloat16*>(OUT), B, H)))
+        static_cast<const __nv_bfloat16*>(X), Gt, static_cast<__nv_bfloat16*>(OUT), B, H, silu_gates)))
   }
   MALOQ_DISPATCH_L((gate_l_fwd_kernel<LL, float><<<grid, 256, 0, st>>>(static_cast<const float*>(X), Gt,
-                                                                      static_cast<float*>(OUT), B, H)))
+                                                                      static_cast<float*>(OUT), B, H, silu_gates)))
 }
 
 const char* gate_l_bwd(int L, const void* X, const float* Gt, const void* DO, void* DX, float* DG, bool bf16, int B,
-                       int H, cudaStream_t st) {
+                       int H, cudaStream_t st, bool silu_gates) {
   if (B == 0) return nullptr;
   const int grid = (int)std::min<long long>(((long long)B * H + 255) / 256, 148 * 32);
   if (bf16) {
     MALOQ_DISPATCH_L((gate_l_bwd_kernel<LL, __nv_bfloat16><<<grid, 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(X), Gt, static_cast<const __nv_bfloat16*>(DO),
-        static_cast<__nv_bfloat16*>(DX), DG, B, H)))
+        static_cast<__nv_bfloat16*>(DX), DG, B, H, silu_gates)))
   }
   MALOQ_DISPATCH_L((gate_l_bwd_kernel<LL, float><<<grid, 256, 0, st>>>(static_cast<const float*>(X), Gt,
                                                                       static_cast<const float*>(DO),
-                                                                      static_cast<float*>(DX), DG, B, H)))
+                                                                      static_cast<float*>(DX), DG, B, H, silu_gates)))
 }
 
 const char* head_gate_fwd(int L, const float* X, const float* SV, __nv_bfloat16* A, int act, float scale, bool absg,

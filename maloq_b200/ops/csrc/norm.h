@@ -19,9 +19,11 @@ const char* ln_silu_fwd(const float* X, const float* w, const float* b, __nv_bfl
 const char* ln_silu_bwd(const float* X, const float* w, const float* b, const __nv_bfloat16* G, float* DX, float* PART,
                         int M, int W, float eps, int grid, cudaStream_t st);
 // X / OUT / DO / DX: fp32, or bf16 when bf16; gates Gt and their gradient DG fp32
-const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st);
+// silu_gates: Gt holds pre-activations g, the gate is tanh(silu(g)) and DG is the gradient wrt g
+const char* gate_l_fwd(int L, const void* X, const float* Gt, void* OUT, bool bf16, int B, int H, cudaStream_t st,
+                       bool silu_gates = false);
 const char* gate_l_bwd(int L, const void* X, const float* Gt, const void* DO, void* DX, float* DG, bool bf16, int B,
-                       int H, cudaStream_t st);
+                       int H, cudaStream_t st, bool silu_gates = false);
 // Fock-head gate: X [B, (L+1)^2, C] fp32, SV [B, (L+1) C] fp32 (transformed scalars | raw
 // gates), A [B, (L+1)^2, C] bf16; act 0 sigmoid, 1 tanh; gates = scale * act(|u| if absg else u).
 // Backward: DA fp32 -> DX (row 0 zero), DSV.

@@ -206,6 +206,13 @@ def gate(gating_scalars, x, expand_index, lmax):
     return norm_native.gate_l(gating_scalars, x, lmax)
 
 
+@register("gate_silu")
+def gate_silu(pre, x, expand_index, lmax):
+    from . import norm_native
+
+    return norm_native.gate_l(pre, x, lmax, silu_gates=True)
+
+
 @register("rms_norm_sh")
 def rms_norm_sh(x, aw, ab, eps, residual=None, out_dtype=None):
     from . import norm_native

@@ -108,19 +108,20 @@ def layernorm_silu(x, w, b, eps=1e-5):
 
 
 class _GateL(torch.autograd.Function):
-    """fp32 or bf16 activations (output in the input's dtype); gates fp32."""
+    """fp32 or bf16 activations (output in the input's dtype); gates fp32.  ``silu_gates``: the
+    gates are pre-activations whose SiLU the kernels apply (and differentiate) themselves."""
 
     @staticmethod
-    def forward(ctx, gates, x, lmax):
+    def forward(ctx, gates, x, lmax, silu_gates):
         x = x.contiguous()
         if x.dtype != torch.bfloat16:
             x = x.float()
         gates = gates.contiguous().float()
         out = torch.empty_like(x)
-        _lib().gate_l_fwd(lmax, x, gates, out)
+        _lib().gate_l_fwd(lmax, x, gates, out, silu_gates)
         count_launches(1)
         ctx.save_for_backward(x, gates)
-        ctx.lmax = lmax
+        ctx.lmax, ctx.silu_gates = lmax, silu_gates
         return out
 
     @staticmethod
@@ -128,13 +129,13 @@ class _GateL(torch.autograd.Function):
         x, gates = ctx.saved_tensors
         dx = torch.empty_like(x)
         dg = torch.empty_like(gates)
-        _lib().gate_l_bwd(ctx.lmax, x, gates, g.to(x.dtype).contiguous(), dx, dg)
+        _lib().gate_l_bwd(ctx.lmax, x, gates, g.to(x.dtype).contiguous(), dx, dg, ctx.silu_gates)
         count_launches(1)
-        return dg, dx, None
+        return dg, dx, None, None
 
 
-def gate_l(gates, x, lmax):
-    return _GateL.apply(gates, x, lmax)
+def gate_l(gates, x, lmax, silu_gates=False):
+    return _GateL.apply(gates, x, lmax, silu_gates)
 
 
 def _coef_l(S):

@@ -297,11 +297,12 @@ class CpuExtension:
         rows = [F.silu(x[:, :1])] + [x[:, l * l:(l + 1) ** 2] * t[:, l - 1:l] for l in range(1, L + 1)]
         return torch.cat(rows, 1)
 
-    def gate_l_fwd(self, L, X, Gt, OUT):
-        OUT.copy_(self._gate_l(L, X.float(), Gt).to(OUT.dtype))
+    def gate_l_fwd(self, L, X, Gt, OUT, silu_gates=False):
+        OUT.copy_(self._gate_l(L, X.float(), F.silu(Gt) if silu_gates else Gt).to(OUT.dtype))
 
-    def gate_l_bwd(self, L, X, Gt, DO, DX, DG):
-        gx, gg = _grad(lambda x, g: self._gate_l(L, x, g), [X.float(), Gt], DO.float())
+    def gate_l_bwd(self, L, X, Gt, DO, DX, DG, silu_gates=False):
+        gx, gg = _grad(lambda x, g: self._gate_l(L, x, F.silu(g) if silu_gates else g), [X.float(), Gt],
+                       DO.float())
         DX.copy_(gx.to(DX.dtype))
         DG.copy_(gg)
 

@@ -35,6 +35,16 @@ const char* emu_gate_l_bwd(int L, const void* X, const float* Gt, const void* DO
   return maloq::gate_l_bwd(L, X, Gt, DO, DX, DG, bf16 != 0, B, H, nullptr);
 }
 
+// the same with the gate pre-activation flag
+const char* emu_gate_l_fwd_s(int L, const void* X, const float* Gt, void* OUT, int bf16, int B, int H, int silu_gates) {
+  return maloq::gate_l_fwd(L, X, Gt, OUT, bf16 != 0, B, H, nullptr, silu_gates != 0);
+}
+
+const char* emu_gate_l_bwd_s(int L, const void* X, const float* Gt, const void* DO, void* DX, float* DG, int bf16,
+                             int B, int H, int silu_gates) {
+  return maloq::gate_l_bwd(L, X, Gt, DO, DX, DG, bf16 != 0, B, H, nullptr, silu_gates != 0);
+}
+
 const char* emu_head_gate_fwd(int L, const float* X, const float* SV, __nv_bfloat16* A, int act, float scale, int absg,
                               int B, int C) {
   return maloq::head_gate_fwd(L, X, SV, A, act, scale, absg != 0, B, C, nullptr);

@@ -44,6 +44,8 @@ SIGNATURES = {
         "emu_ln_silu_bwd": [P, P, P, P, P, P, I, I, F, I],
         "emu_gate_l_fwd": [I, P, P, P, I, I, I],
         "emu_gate_l_bwd": [I, P, P, P, P, P, I, I, I],
+        "emu_gate_l_fwd_s": [I, P, P, P, I, I, I, I],
+        "emu_gate_l_bwd_s": [I, P, P, P, P, P, I, I, I, I],
         "emu_head_gate_fwd": [I, P, P, P, I, F, I, I, I],
         "emu_head_gate_bwd": [I, P, P, P, P, P, I, F, I, I, I],
     },
@@ -190,15 +192,15 @@ class EmulatedExtension(CpuExtension):
         _check(self.n.emu_ln_silu_bwd(_p(X), _p(w), _p(b), _p(G), _p(DX), _p(PART), X.shape[0], X.shape[1], eps,
                                       PART.shape[0] // 8))
 
-    def gate_l_fwd(self, L, X, Gt, OUT):
+    def gate_l_fwd(self, L, X, Gt, OUT, silu_gates=False):
         self._count("gate_l_fwd")
-        _check(self.n.emu_gate_l_fwd(L, _p(X), _p(Gt), _p(OUT), int(X.dtype == torch.bfloat16), X.shape[0],
-                                     X.shape[2]))
+        _check(self.n.emu_gate_l_fwd_s(L, _p(X), _p(Gt), _p(OUT), int(X.dtype == torch.bfloat16), X.shape[0],
+                                       X.shape[2], int(silu_gates)))
 
-    def gate_l_bwd(self, L, X, Gt, DO, DX, DG):
+    def gate_l_bwd(self, L, X, Gt, DO, DX, DG, silu_gates=False):
         self._count("gate_l_bwd")
-        _check(self.n.emu_gate_l_bwd(L, _p(X), _p(Gt), _p(DO), _p(DX), _p(DG), int(X.dtype == torch.bfloat16),
-                                     X.shape[0], X.shape[2]))
+        _check(self.n.emu_gate_l_bwd_s(L, _p(X), _p(Gt), _p(DO), _p(DX), _p(DG), int(X.dtype == torch.bfloat16),
+                                       X.shape[0], X.shape[2], int(silu_gates)))
 
     def head_gate_fwd(self, L, X, SV, A, act, scale, absg):
         assert A.shape == X.shape and SV.shape == (X.shape[0], (L + 1) * X.shape[2])

@@ -274,3 +274,31 @@ def test_weight_cache_refreshed_in_place_by_weight_pack(monkeypatch, libs):
     assert ext.emulated_calls["weight_pack"] == before + 1
     assert ext.emulated_error_word() == 0
     W.invalidate()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gate_with_silu_gates_kernel(libs, dtype):
+    """The l-outer gate fed the gate pre-activations (SiLU inside the kernels) against
+    ``gate(silu(pre), x)`` in PyTorch, forward and both gradients."""
+    from maloq_b200.ops import reference as R
+    from tests.emulated_extension import EmulatedExtension
+
+    ext = EmulatedExtension(libs)
+    L, B, H = 4, 13, 24
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(B, (L + 1) ** 2, H, generator=g).to(dtype)
+    pre = torch.randn(B, L * H, generator=g) * 2
+    dout = torch.randn(B, (L + 1) ** 2, H, generator=g).to(dtype)
+    idx = torch.tensor([l - 1 for l in range(1, L + 1) for _ in range(2 * l + 1)])
+    xr, pr = x.float().requires_grad_(), pre.clone().requires_grad_()
+    ref = R.gate(torch.nn.functional.silu(pr), xr, idx, L)
+    ref.backward(dout.float())
+    out = torch.empty_like(x)
+    ext.gate_l_fwd(L, x, pre, out, True)
+    dx, dpre = torch.empty_like(x), torch.empty_like(pre)
+    ext.gate_l_bwd(L, x, pre, dout, dx, dpre, True)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    assert torch.allclose(out.float(), ref.detach(), rtol=tol, atol=tol)
+    assert torch.allclose(dx.float(), xr.grad, rtol=tol, atol=tol)
+    assert torch.allclose(dpre, pr.grad, rtol=1e-4 if dtype == torch.float32 else 2e-2, atol=1e-4 if dtype == torch.float32 else 2e-2)
+    assert ext.emulated_error_word() == 0

@@ -74,6 +74,23 @@ def test_gate_l(cuda_device):
         assert _rel(a, b) < 1e-5
 
 
+def test_gate_with_silu_gates(cuda_device):
+    """Gate fed the pre-activations (SiLU inside the kernels) vs gate(silu(pre), x) in fp32."""
+    from maloq_b200.ops import norm_native
+    from maloq_b200.ops import reference as R
+
+    L, H = 4, 64
+    x = torch.randn(200, 25, H, device=cuda_device, requires_grad=True)
+    pre = (2 * torch.randn(200, L * H, device=cuda_device)).requires_grad_()
+    idx = torch.cat([torch.full((2 * l + 1,), l - 1) for l in range(1, L + 1)]).to(cuda_device)
+    out = norm_native.gate_l(pre, x, L, silu_gates=True)
+    ref = R.gate(torch.nn.functional.silu(pre), x, idx, L)
+    assert _rel(out, ref) < 1e-6
+    w = torch.randn_like(out)
+    for a, b in zip(torch.autograd.grad((out * w).sum(), [pre, x]), torch.autograd.grad((ref * w).sum(), [pre, x])):
+        assert _rel(a, b) < 1e-5
+
+
 def test_so3_linear(cuda_device):
     from maloq_b200.ops import norm_native
     from maloq_b200.ops import reference as R
