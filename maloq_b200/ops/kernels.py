@@ -342,10 +342,11 @@ class _FockHeadFn(torch.autograd.Function):
         grads = []
         for l, hb in zip(ls, has_b):
             P, o0 = _pad8(mul[l]), off[l * l]
-            dw = partsL[l].sum((0, 1)) if N > 0 else torch.zeros(P, C, device=g.device)
+            pl = partsL[l]
+            dw = colsum(pl.view(-1, P * C)).view(P, C) if N > 0 else torch.zeros(P, C, device=g.device)
             grads.append(dw[:mul[l]])
             # the degree's column blocks are adjacent in dY: [N, 2l+1, P]
-            db = dY[:, o0:o0 + (2 * l + 1) * P].view(N, 2 * l + 1, P)[:, :, :mul[l]].sum((0, 1)) if hb else None
+            db = colsum(colsum(dY[:, o0:o0 + (2 * l + 1) * P]).view(2 * l + 1, P))[:mul[l]] if hb else None
             grads.append(db)
         dx = torch.empty_like(x)
         dsv = torch.empty_like(sv)

@@ -391,3 +391,56 @@ def test_training_step_has_no_host_synchronisation(monkeypatch, head_kw, extra):
     assert _sync_census(lambda: R.fock_loss(torch.ones(2, 3), torch.ones(2, 3), torch.zeros(2, 3), torch.zeros(2, 3),
                                             torch.ones(2, 3, dtype=torch.bool), torch.ones(2, 3, dtype=torch.bool),
                                             L.mse_padded_loss))
+
+
+def _op_census(step):
+    """(op name, last package frame) -> count of the ATen ops of ``step`` outside the CPU stand-in
+    and torch.optim, views and allocations excluded: on a GPU each is a launch of its own."""
+    import collections
+    import traceback
+
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    free = {"view", "_unsafe_view", "slice", "select", "as_strided", "t", "transpose", "detach", "alias", "unsqueeze",
+            "squeeze", "expand", "permute", "reshape", "split", "split_with_sizes", "unbind", "narrow", "empty",
+            "empty_like", "empty_strided", "new_empty", "new_empty_strided", "is_same_size"}
+    cnt = collections.Counter()
+
+    class Census(TorchDispatchMode):
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            name = func.overloadpacket.__name__
+            if name not in free:
+                st = traceback.extract_stack()
+                if not any("cpu_extension.py" in f.filename or "torch/optim" in f.filename for f in st):
+                    site = [f"{f.filename.split('repo/')[-1]}:{f.lineno}" for f in st if "maloq_b200" in f.filename]
+                    cnt[(name, site[-1] if site else "?")] += 1
+            return func(*args, **(kwargs or {}))
+
+    with Census():
+        step()
+    return cnt
+
+
+def test_training_step_launch_budget(monkeypatch):
+    """Glue ops of a steady-state training step stay few: column sums (bias gradients, norm
+    partials, per-degree weight-gradient sums) run in the extension, the optimizer step rewrites
+    the whole bf16 weight cache through the extension, and the total stays within a budget."""
+    from maloq_b200.ops import weights as W
+    from maloq_b200.train import loss as L
+    from maloq_b200.train.trainer import SplitTrainer
+
+    bb, hd, b, lab = _model(2)
+    ext = use_cpu_extension(monkeypatch)
+    W.invalidate()
+    opt = torch.optim.Adam(list(bb.parameters()) + list(hd.parameters()), lr=1e-3)
+    tr = SplitTrainer(bb, hd, lab.irreps, mask_table=torch.as_tensor(lab.table.mask))
+    tr.train_step(b, L.rmse_mse_padded_loss, opt)
+    packs = ext.calls.get("weight_pack", 0)
+    cnt = _op_census(lambda: tr.train_step(b, L.rmse_mse_padded_loss, opt))
+    sums = {k: v for k, v in cnt.items() if k[0] == "sum" and k[1].startswith("maloq_b200/ops/")}
+    assert not sums, sums
+    from_cache = sum(v for k, v in cnt.items() if k[1].startswith("maloq_b200/ops/weights.py"))
+    assert from_cache <= 6, from_cache  # only non-parameter weights (padded head views) are cast per call
+    assert ext.calls["weight_pack"] > packs
+    assert sum(cnt.values()) <= 320, sorted(cnt.items(), key=lambda kv: -kv[1])[:20]
+    W.invalidate()
